@@ -1,0 +1,175 @@
+"""Regenerate the golden vectors in this directory from the reference MemFast.
+
+Run in a container where the reference package is importable (it is not needed
+at test time):
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /path/to/MemFast
+
+Every case stores its operands, its Config keyword arguments (JSON) and the
+reference's outputs, plus the reference's quantised buffers where the case is
+used to pin quantisation.  The CPU test suite checks the oracle against these
+files; the GPU suite checks the CUDA engine against them and the oracle.
+"""
+
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+def _jsonable(kwargs):
+    out = {}
+    for key, value in kwargs.items():
+        if key == "nonidealities":
+            out[key] = dict(value)
+        elif isinstance(value, tuple):
+            out[key] = list(value)
+        else:
+            out[key] = value
+    return out
+
+
+def main(reference_root):
+    sys.path.insert(0, str(reference_root))
+    sys.dont_write_bytecode = True
+    import memfast
+    from memfast import Config, Nonidealities, Simulator
+
+    torch.set_num_threads(8)
+    base = dict(
+        array_size=(128, 128), rows_per_read=32, weight_quant_gran=(32, 1),
+        input_quant_gran=(1, 32), input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2),
+    )
+    matrix = dict(
+        array_size=(256, 256), rows_per_read=64, input_quant_gran=(1, 64), weight_quant_gran=(64, 1),
+    )
+    effects3 = dict(write_variation=0.05, adc_nonlinearity=0.02, stuck_at_low=5e-4,
+                    stuck_at_high=5e-4, drift_coefficient=0.05, drift_time=100.0)
+
+    def make(kwargs):
+        effects = kwargs.get("nonidealities", {})
+        return Config(**{k: v for k, v in kwargs.items() if k != "nonidealities"},
+                      nonidealities=Nonidealities(**effects))
+
+    def save(case, kwargs, arrays, **meta):
+        payload = {k: np.asarray(v) for k, v in arrays.items()}
+        payload["config_json"] = np.array(json.dumps(_jsonable(kwargs)))
+        payload["meta_json"] = np.array(json.dumps(meta))
+        np.savez_compressed(HERE / f"{case}.npz", **payload)
+        size = (HERE / f"{case}.npz").stat().st_size
+        print(f"{case:28s} {size/1024:7.1f} KiB")
+
+    def mm_case(name, kwargs, n, k, o, seed, *, a=None, b=None, calls=1, buffers=False):
+        cfg = make(kwargs)
+        g = torch.Generator().manual_seed(seed)
+        a = torch.randn(n, k, generator=g) if a is None else a
+        b = torch.randn(k, o, generator=g) if b is None else b
+        sim = Simulator(cfg, device="cpu")
+        outs = [sim.mm(a, b) for _ in range(calls)]
+        arrays = {"A": a.numpy(), "B": b.numpy()}
+        for i, out in enumerate(outs):
+            arrays[f"out{i}"] = out.numpy()
+        if buffers:
+            matrix_obj = sim._matrix_for(b)
+            arrays["packed"] = matrix_obj.packed.numpy()
+            arrays["weight_scale"] = matrix_obj.weight_scale.numpy()
+            q, xs = memfast.quantization.input_tiles(a, cfg)
+            arrays["q"] = q.numpy()
+            arrays["xscale"] = xs.numpy()
+        save(name, kwargs, arrays, kind="mm", calls=calls, name="matrix.0")
+
+    ideal = dict(write_variation=0.0)
+    # BASELINE config #1 exactly: CPU Simulator.mm, torch.manual_seed(0), randn(4,128) @ randn(128,32).
+    torch.manual_seed(0)
+    a1, b1 = torch.randn(4, 128), torch.randn(128, 32)
+    mm_case("config1", dict(base, adc_bits=7, nonidealities=dict(write_variation=0.02)),
+            4, 128, 32, 0, a=a1, b=b1, buffers=True)
+    int8 = dict(base, adc_bits=(6, 7, 7, 8, 8))
+    mm_case("int8_ideal", dict(int8, nonidealities=ideal), 64, 256, 192, 1, buffers=True)
+    mm_case("int8_ideal_ragged", dict(int8, nonidealities=ideal), 5, 200, 130, 2, buffers=True)
+    mm_case("int8_ideal_single", dict(int8, nonidealities=ideal), 1, 384, 256, 3)
+    g = torch.Generator().manual_seed(4)
+    a_clip = 1.0 + 0.05 * torch.rand(16, 256, generator=g)
+    b_clip = 1.0 + 0.05 * torch.rand(256, 128, generator=g)
+    b_clip[:, 64:] *= -1
+    mm_case("int8_ideal_clip", dict(int8, nonidealities=ideal), 16, 256, 128, 4,
+            a=a_clip, b=b_clip, buffers=True)
+    mm_case("int8_ideal_rpr48", dict(int8, rows_per_read=48, input_quant_gran=(1, None),
+                                     weight_quant_gran=(None, 1), nonidealities=ideal),
+            6, 300, 140, 5)
+    mm_case("int8_nonideal", dict(int8, nonidealities=dict(write_variation=0.02, read_variation=0.02,
+                                                           voltage_variation=0.02)),
+            16, 256, 256, 6, calls=2)
+    mm_case("int8_write_only", dict(int8, nonidealities=dict(write_variation=0.02)), 32, 256, 256, 7)
+    mm_case("int4_matrix", dict(matrix, activation_bits=4, weight_bits=4, input_slice=(1, 1, 2),
+                                weight_slice=(1, 1, 2), nonidealities=effects3), 8, 512, 256, 8)
+    mm_case("int8_matrix", dict(matrix, input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2),
+                                nonidealities=effects3), 8, 512, 256, 9)
+    mm_case("bfp16_matrix", dict(matrix, activation_bits=16, weight_bits=16, input_slice=(1, 3, 4, 4, 4),
+                                 weight_slice=(1, 3, 4, 4, 4), bw_e=8, adc_bits=8,
+                                 nonidealities=effects3), 4, 512, 256, 10, buffers=True)
+    mm_case("bfp16_ideal", dict(matrix, activation_bits=16, weight_bits=16, input_slice=(1, 3, 4, 4, 4),
+                                weight_slice=(1, 3, 4, 4, 4), bw_e=8, adc_bits=8,
+                                nonidealities=ideal), 4, 512, 256, 11)
+    mm_case("int12_ideal", dict(base, activation_bits=12, weight_bits=12, input_slice=(1, 3, 4, 4),
+                                weight_slice=(1, 3, 4, 4), adc_bits=10, nonidealities=ideal),
+            4, 256, 128, 12)
+    mm_case("default_config", {}, 8, 100, 70, 13)
+    mm_case("default_ideal", dict(nonidealities=ideal), 8, 100, 70, 14)
+    mm_case("slice_pair", dict(int8, nonidealities=dict(write_variation=0.02, read_variation=0.05,
+                                                        read_mode="slice_pair")), 4, 256, 128, 15)
+    mm_case("output_mode", dict(int8, nonidealities=dict(write_variation=0.02, read_variation=0.05,
+                                                         read_mode="output")), 4, 256, 128, 16)
+    mm_case("shared_read_events", dict(int8, nonidealities=dict(write_variation=0.0, read_variation=0.05)),
+            4, 256, 128, 17, calls=3)
+
+    # Unsigned imported weights with zero points (simulator.py:173-185, 587-611).
+    kwargs = dict(int8, weight_signed=False, nonidealities=ideal)
+    cfg = make(kwargs)
+    g = torch.Generator().manual_seed(18)
+    codes = torch.randint(0, 256, (96, 256), generator=g)
+    scales = torch.rand(96, 1, generator=g) * 0.01 + 0.001
+    zeros = torch.randint(100, 156, (96, 1), generator=g).float()
+    x = torch.randn(12, 256, generator=g)
+    sim = Simulator(cfg, device="cpu")
+    layer = sim.map_quantized(codes, scales, zero_points=zeros, name="imported")
+    save("map_quantized", kwargs, dict(codes=codes.numpy(), scales=scales.numpy(), zeros=zeros.numpy(),
+                                       x=x.numpy(), out0=layer(x).numpy()), kind="map_quantized",
+         name="imported")
+
+    # Fixed input scale (simulator.py:432-450).
+    kwargs = dict(int8, nonidealities=ideal)
+    cfg = make(kwargs)
+    g = torch.Generator().manual_seed(19)
+    w = torch.randn(64, 256, generator=g)
+    x = torch.randn(8, 256, generator=g)
+    sim = Simulator(cfg, device="cpu")
+    layer = sim.map(w, name="fixed")
+    layer.set_input_scale(torch.full((1, 256), 0.02))
+    save("fixed_input_scale", kwargs, dict(W=w.numpy(), x=x.numpy(), scale=np.float32(0.02),
+                                           out0=layer(x).numpy()), kind="fixed_scale", name="fixed")
+
+    # convert_model on a small Conv2d + Linear network (nn/conversion.py, nn/convolution.py).
+    kwargs = dict(int8, adc_bits=7, nonidealities=dict(write_variation=0.02))
+    cfg = make(kwargs)
+    torch.manual_seed(20)
+    net = torch.nn.Sequential(
+        torch.nn.Conv2d(4, 6, 3, padding=1, stride=1, groups=2), torch.nn.ReLU(),
+        torch.nn.Conv2d(6, 8, 3, padding=0, stride=2), torch.nn.Flatten(), torch.nn.Linear(8 * 3 * 3, 10),
+    )
+    x = torch.randn(3, 4, 8, 8)
+    analog = memfast.convert_model(net, Simulator(cfg, device="cpu"))
+    out0 = analog(x)
+    out1 = analog(x)
+    state = {k: v.numpy() for k, v in net.state_dict().items()}
+    save("convert_model", kwargs, dict(x=x.numpy(), out0=out0.numpy(), out1=out1.numpy(),
+                                       **{f"param::{k}": v for k, v in state.items()}),
+         kind="convert_model")
+
+
+if __name__ == "__main__":
+    main(Path(sys.argv[1] if len(sys.argv) > 1 else "../MemFast").resolve())

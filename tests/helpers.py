@@ -1,0 +1,69 @@
+"""Shared test helpers: golden-case loading and Config reconstruction."""
+
+import json
+from pathlib import Path
+
+import numpy as np
+
+from memfast_b200.config import Config, Nonidealities
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def config_from_json(text):
+    kwargs = json.loads(str(text))
+    effects = kwargs.pop("nonidealities", {})
+    for key in ("array_size", "weight_quant_gran", "input_quant_gran", "input_slice", "weight_slice"):
+        if key in kwargs and kwargs[key] is not None:
+            kwargs[key] = tuple(kwargs[key])
+    if isinstance(kwargs.get("adc_bits"), list):
+        kwargs["adc_bits"] = tuple(kwargs["adc_bits"])
+    return Config(**kwargs, nonidealities=Nonidealities(**effects))
+
+
+def load_case(name):
+    data = np.load(GOLDEN / f"{name}.npz")
+    arrays = {key: data[key] for key in data.files if key not in ("config_json", "meta_json")}
+    return config_from_json(data["config_json"]), arrays, json.loads(str(data["meta_json"]))
+
+
+def mm_cases():
+    names = []
+    for path in sorted(GOLDEN.glob("*.npz")):
+        meta = json.loads(str(np.load(path)["meta_json"]))
+        if meta.get("kind") == "mm":
+            names.append(path.stem)
+    return names
+
+
+# Nonideal currents are real-valued FP32 dot products.  Summing them in another
+# order than the reference's CPU bmm flips an ADC rounding where a current sits
+# within an ulp of a count boundary.  Tolerance for such cases (stated once, used
+# by every parity test): at most 0.5% of output elements differ, by at most 1% of
+# the output range, and the mean signed error stays below 1e-4 of the range.
+MISMATCH_FRACTION = 5e-3
+MAX_ERROR_OF_RANGE = 1e-2
+MEAN_ERROR_OF_RANGE = 1e-4
+
+
+def assert_close_nonideal(got, want, label=""):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    assert got.shape == want.shape, label
+    scale = max(np.abs(want).max(), 1e-30)
+    diff = got - want
+    assert np.mean(diff != 0) <= MISMATCH_FRACTION, (label, np.mean(diff != 0))
+    assert np.abs(diff).max() <= MAX_ERROR_OF_RANGE * scale, (label, np.abs(diff).max() / scale)
+    assert abs(diff.mean()) <= MEAN_ERROR_OF_RANGE * scale, (label, diff.mean() / scale)
+
+
+def assert_parity(got, want, config, label=""):
+    """Bit-exact for ideal devices; the nonideal tolerance above otherwise."""
+    got = np.asarray(got)
+    want = np.asarray(want)
+    assert got.dtype == want.dtype and got.shape == want.shape, (label, got.dtype, want.dtype)
+    if config.nonidealities.ideal:
+        assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), (
+            label, np.mean(got != want), np.abs(got.astype(np.float64) - want).max())
+    else:
+        assert_close_nonideal(got, want, label)
