@@ -1,0 +1,362 @@
+#!/usr/bin/env python
+"""Benchmark of the sliced analog matrix product (BASELINE metric).
+
+Metric: simulated MAC/s of ``Simulator.mm`` on the 4096x4096x4096 sliced INT8
+workload (array 128x128, rows_per_read 32, groups
+(32,1)/(1,32), slices (1,1,2,2,2), adc_bits (6,7,7,8,8), ideal device) on
+seeded N(0,1) FP32 operands.  One step = one ``Simulator.mm(A, B)`` call
+(quantise A, reprogram B, sliced product with fused epilogue), operands
+resident in HBM.  ``e2e`` repeats it with pinned host operands copied in and the
+result copied out inside the timed region.  With --gpus N the batch rows are
+sharded across ranks (noise addresses stay global through vector_offset) and
+the output rows are all-gathered over NCCL inside each step: a fixed total
+problem, i.e. strong scaling.
+
+``--impl reference`` times the reference algorithm's CPU restatement (the
+oracle: restored conductances, FP32 currents, ADC, signed reconstruction,
+scale epilogue) on the host cores, on a bounded prefix of the same rows.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "simulated MAC/s on 4096^3 sliced INT8 Simulator.mm"
+UNIT = "MAC/s"
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    p.add_argument("--size", type=int, default=4096, help="N = K = O")
+    p.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
+    p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work budget of the baseline sample")
+    return p.parse_args()
+
+
+def bench_config(mf_module):
+    return mf_module.Config(
+        array_size=(128, 128), rows_per_read=32, weight_quant_gran=(32, 1), input_quant_gran=(1, 32),
+        input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2), adc_bits=(6, 7, 7, 8, 8),
+        nonidealities=mf_module.Nonidealities(write_variation=0.0),
+    )
+
+
+def operands(size, seed=2024):
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(size, size, generator=g)
+    b = torch.randn(size, size, generator=g)
+    return a, b
+
+
+def workload(args):
+    n = k = o = args.size
+    return dict(workload=f"Simulator.mm {n}x{k}x{o} INT8 (1,1,2,2,2) ideal", n=n, k=k, o=o,
+                array=[128, 128], rows_per_read=32, adc_bits=[6, 7, 7, 8, 8],
+                input_groups=[1, 32], weight_groups=[32, 1], operands="seeded N(0,1) fp32",
+                l2="inputs 2x64 MiB fp32 exceed the 126 MB L2; L2 also flushed between timed steps")
+
+
+# ------------------------------------------------------------------ CPU leg --
+def cpu_sample(size, budget_s, config):
+    """Time the oracle (reference algorithm restated in C, all host threads) on a row prefix."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    O.lib()
+    a, b = operands(size)
+    a, b = a.numpy(), b.numpy()
+    rows = 1
+    start = time.perf_counter()
+    O.mm(a[:rows], b, config, physical=True)
+    first = time.perf_counter() - start
+    rows = int(max(1, min(size, budget_s / max(first, 1e-3))))
+    start = time.perf_counter()
+    O.mm(a[:rows], b, config, physical=True)
+    elapsed = time.perf_counter() - start
+    value = rows * size * size / elapsed
+    return dict(value=value, unit=UNIT, cores=threads, kind="port",
+                sample=f"oracle C restatement, physical FP32 path, first {rows} of {size} rows "
+                       f"(B programmed once per sample), {elapsed:.1f} s wall",
+                seconds=elapsed, rows=rows)
+
+
+def reference_arm(args):
+    import memfast_b200 as mf
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    config = bench_config(mf)
+    import numpy as np
+
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    size = args.size
+    a, b = operands(size)
+    a, b = a.numpy(), b.numpy()
+    start = time.perf_counter()
+    O.mm(a[:1], b, config, physical=True)
+    one = time.perf_counter() - start
+    budget = max(1.0, 150.0 / max(1, args.steps + args.warmup))
+    rows = int(max(1, min(size, budget / max(one, 1e-3))))
+    times = []
+    for step in range(args.warmup + args.steps):
+        start = time.perf_counter()
+        O.mm(a[:rows], b, config, physical=True)
+        if step >= args.warmup:
+            times.append(time.perf_counter() - start)
+    per_step = statistics.mean(times)
+    value = rows * size * size / per_step
+    line = dict(metric=METRIC, value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
+                ms_per_step=per_step * 1e3, higher_is_better=True, scaling="strong", vs_baseline=None,
+                dtype="f32 currents / int64 totals", data="synthetic", config=workload(args), impl="reference",
+                cpu_baseline=dict(value=value, unit=UNIT, cores=threads, kind="port",
+                                  sample=f"first {rows} of {size} rows per step (oracle C restatement of the "
+                                         f"reference CPU algorithm, physical FP32 path)"),
+                e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ clock sampler --
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.samples = []
+        self.proc = None
+        self.device_index = device_index
+
+    def __enter__(self):
+        try:
+            import torch
+
+            ident = str(torch.cuda.get_device_properties(self.device_index).uuid)
+            ident = ident if ident.startswith("GPU-") else f"GPU-{ident}"
+        except Exception:
+            ident = str(self.device_index)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={ident}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=["no samples"], samples=0)
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[5 + i] == "Active"})
+        return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=max(mx) if mx else None,
+                    reasons=reasons, samples=len(self.samples))
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return data.get("bf16_tflops"), data.get("hbm_gbs"), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch of the sliced-mm kernel from the committed ncu summary, if any."""
+    path = ROOT / "profiles" / "sliced_mm_4096_ideal.md"
+    if path.exists():
+        for line in path.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                try:
+                    return float(line.split(":", 1)[1].split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+# --------------------------------------------------------------- engine arm --
+def engine_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    import memfast_b200 as mf
+    from memfast_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    config = bench_config(mf)
+    size = args.size
+    a_cpu, b_cpu = operands(size)
+    rows = size // world
+    r0 = rank * rows
+    r1 = size if rank == world - 1 else r0 + rows
+    a_host = a_cpu[r0:r1].contiguous().pin_memory()
+    b_host = b_cpu.contiguous().pin_memory()
+    a = a_host.to(device)
+    b = b_host.to(device)
+    sim = mf.Simulator(config, device=device)
+    gathered = torch.empty((size, size), device=device) if world > 1 else None
+    out_host = torch.empty((r1 - r0, size), pin_memory=True)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step(x, y):
+        out = sim.mm(x, y)
+        if world > 1:
+            if r1 - r0 == rows:
+                dist.all_gather_into_tensor(gathered, out)
+            else:
+                raise SystemExit("bench: batch must divide evenly across ranks")
+        return out
+
+    def timed(fn, count):
+        times = []
+        for _ in range(count):
+            flush.zero_()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize(device)
+            start.record(stream)
+            fn()
+            end.record(stream)
+            torch.cuda.synchronize(device)
+            times.append(start.elapsed_time(end) / 1e3)
+        return times
+
+    for _ in range(args.warmup):
+        step(a, b)
+    torch.cuda.synchronize(device)
+    launches0 = _lib.load().mf_launch_count()
+    with ClockSampler(local) as clocks:
+        t_wall = time.perf_counter()
+        times = timed(lambda: step(a, b), args.steps)
+        launches = _lib.load().mf_launch_count() - launches0
+        # Keep the GPU loaded long enough for the clock sampler (not part of the measurement).
+        while time.perf_counter() - t_wall < 1.0:
+            step(a, b)
+            torch.cuda.synchronize(device)
+    per_step = sum(times) / len(times)
+
+    # End to end: pinned host operands in, result out, every step.
+    def e2e_step():
+        x = a_host.to(device, non_blocking=True)
+        y = b_host.to(device, non_blocking=True)
+        out = step(x, y)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    e2e_times = timed(e2e_step, args.steps)
+    e2e_step_s = sum(e2e_times) / len(e2e_times)
+
+    # Dominant kernel alone: the fused sliced product on pre-quantised operands.
+    from memfast_b200.quantization import input_tiles
+    from memfast_b200.simulator import default_schedule
+
+    matrix = sim._matrix_for(b)
+    q, xscale = input_tiles(a, config)
+    kernel_times = timed(lambda: matrix._execute(q, xscale, default_schedule(config), 0), max(3, args.steps))
+    kernel_s = sum(kernel_times) / len(kernel_times)
+
+    def reduce_max(value):
+        if world == 1:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    per_step = reduce_max(per_step)
+    e2e_step_s = reduce_max(e2e_step_s)
+    kernel_s = reduce_max(kernel_s)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    macs = float(size) ** 3
+    pairs = len(config.input_layout) * len(config.weight_layout)
+    bf16, hbm, peak_kind = measured_peaks()
+    int8_peak_tops = 2.0 * bf16
+    kernel_ops = 2.0 * (rows * size * size) * pairs
+    achieved_tops = kernel_ops / kernel_s / 1e12
+    traffic = profiled_traffic()
+    line = dict(
+        metric=METRIC, value=macs / per_step, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+        ms_per_step=per_step * 1e3, higher_is_better=True, scaling="strong", vs_baseline=None,
+        dtype="u8 digits / int32 totals / f32 epilogue", data="synthetic", config=workload(args),
+        slice_pair_macs_per_s=macs * pairs / per_step,
+        roofline=dict(bound="tensor", achieved=achieved_tops, peak=int8_peak_tops, unit="TFLOP/s",
+                      frac=achieved_tops / int8_peak_tops, traffic=traffic,
+                      note=f"sliced-mm kernel alone, {rows}x{size}x{size} per launch, algorithmic "
+                           f"{pairs} slice-pair int8 MAC streams x2 ops; peak = 2 x {peak_kind} "
+                           f"dense bf16 ({bf16} TFLOP/s), the int8 dense rate of B200",
+                      kernel_ms=kernel_s * 1e3),
+        e2e=dict(value=macs / e2e_step_s, unit=UNIT,
+                 h2d_bytes_per_step=int((size * size + size * size * world) * 4),
+                 d2h_bytes_per_step=int(size * size * 4), ms_per_step=e2e_step_s * 1e3),
+        gpu_launches=int(launches),
+        clocks=clocks.summary(),
+    )
+    if world == 1 and not args.skip_cpu:
+        line["cpu_baseline"] = cpu_sample(size, args.cpu_seconds, config)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        engine_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,157 @@
+/*
+ * memfast_b200 -- C ABI of the B200 engine for MemFast's sliced matrix product.
+ *
+ * The reference (HUST-ISMD-Odyssey/MemFast v0.3.0) crosses into device code in
+ * memfast/cuda.py: it JIT-compiles memfast/kernels.cu with NVRTC (cuda.py:130-220)
+ * and launches two kernels through ctypes cuLaunchKernel (cuda.py:275-310) from
+ * ``partial(q, packed, config, schedule, seed, event, begin, end)``
+ * (cuda.py:322-373), after which AnalogMatrix._execute scales and sums the
+ * partials in PyTorch (simulator.py:561-616).  This library replaces that whole
+ * boundary with prebuilt sm_100a kernels: partials never reach HBM, and the
+ * quantisation (memfast/quantization.py:9-137) also runs on the device.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  Every pointer argument is DEVICE memory
+ *     unless its comment says "host"; the caller owns every buffer, including
+ *     workspaces (query their size first).  The library never allocates device
+ *     memory on these paths.
+ *   - All work is enqueued asynchronously on `stream` (a cudaStream_t, passed as
+ *     void*; NULL is the legacy default stream).
+ *   - Return value: MF_OK, or an error code; mf_last_error() gives the message of
+ *     the calling thread's last failure.  No exception crosses the ABI.
+ *   - Thread safety: calls are reentrant; per-device one-time set-up runs under
+ *     a mutex.
+ *   - Slice tables are least-significant-slice first, as in
+ *     memfast/config.py:193-209 (Config.input_layout / weight_layout).
+ */
+#ifndef MEMFAST_B200_H
+#define MEMFAST_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MF_ABI_VERSION 1
+#define MF_MAX_SLICES 32
+
+typedef enum {
+    MF_OK = 0,
+    MF_ERR_INVALID = 1,   /* bad argument or configuration  (reference: ValueError)    */
+    MF_ERR_RESOURCE = 2,  /* workspace/grid/shared-memory limit (reference: ResourceError, cuda.py:15) */
+    MF_ERR_CUDA = 3,      /* CUDA runtime failure          (reference: RuntimeError, cuda.py:19-21) */
+    MF_ERR_UNSUPPORTED = 4
+} mf_status;
+
+typedef enum { MF_F32 = 0, MF_F16 = 1, MF_BF16 = 2, MF_F64 = 3 } mf_dtype;
+
+/* POD mirror of Config + Nonidealities (memfast/config.py:21-224); every
+ * derived quantity is precomputed on the host exactly as the reference derives it
+ * (drift factor as in cuda.py:74). */
+typedef struct {
+    int32_t abi_version;             /* MF_ABI_VERSION */
+    int32_t activation_bits, weight_bits, weight_signed, bw_e;   /* bw_e 0 = INT */
+    int32_t n_in, n_w;               /* physical input / weight slices */
+    int32_t in_shift[MF_MAX_SLICES], in_mask[MF_MAX_SLICES];
+    int64_t in_factor[MF_MAX_SLICES];
+    int32_t w_shift[MF_MAX_SLICES], w_mask[MF_MAX_SLICES];
+    int64_t w_factor[MF_MAX_SLICES];
+    int32_t adc_max[MF_MAX_SLICES];  /* per weight slice */
+    int32_t rows, cols;              /* array_size */
+    int32_t read_rows, reads;        /* rows per ADC read, reads per array */
+    int32_t in_group_rows, in_group_cols;   /* input_quant_gran, 0 = whole extent */
+    int32_t w_group_rows, w_group_cols;     /* weight_quant_gran over [K,O], 0 = whole */
+    int32_t wide;                    /* FP64 scales and reconstruction (Config.wide) */
+    int32_t wide_codes;              /* int64 codes instead of uint8 */
+    int32_t precise_currents;        /* FP64 currents (Config.precise_currents) */
+    int32_t read_mode;               /* 0 shared, 1 slice_pair, 2 output */
+    int32_t ideal;                   /* no effect perturbs a current */
+    double high, low, voltage, unit;
+    double write_var, read_var, volt_var, nonlinear, saf_low, saf_high, drift;
+} mf_config;
+
+/* Execution schedule (the reference's tuned-mode grid, simulator.py:27-45,
+ * re-declared over this engine's tile shapes).  Every schedule gives
+ * bit-identical output. */
+typedef struct {
+    int32_t kernel;     /* 0 auto, 1 generic SIMT, 2 tcgen05 fast path */
+    int32_t tile_n;     /* vectors per CTA (generic: 8,16,32) */
+    int32_t tile_o;     /* output columns per CTA (generic: 32,64,128) */
+    int32_t arrays;     /* tiles restored per group in physical mode (>=1) */
+} mf_schedule;
+
+typedef struct {
+    size_t workspace_bytes;
+    int32_t threads, shared_bytes, registers, local_bytes, blocks_per_sm;
+} mf_resources;
+
+int32_t mf_abi_version(void);
+
+/* Message of this thread's last failure ("" if none).  Returns its length. */
+int32_t mf_last_error(char* buffer, size_t capacity);
+
+/* Kernels this library has launched in this process (all devices, all entry points). */
+uint64_t mf_launch_count(void);
+
+/* Number of visible devices and whether device `index` is an sm_100 part. */
+mf_status mf_device_check(int32_t index, int32_t* is_sm100);
+
+/* Replaces memfast/quantization.py input_tiles (:115-137) with grouped_quantize
+ * (:9-44).  x: [n, k] row stride ldx elements, dtype x_dtype.  fixed_scale:
+ * NULL for dynamic groups, else [k] FP32 (FP64 when cfg->wide) per-column scales
+ * (AnalogMatrix.set_input_scale, simulator.py:432-450).  codes: [n, m*rows]
+ * uint8 (int64 when cfg->wide_codes), m = ceil(k/rows).  xscale: [n, m*reads]
+ * FP32 (FP64 when cfg->wide).  workspace: mf_quantize_workspace() bytes. */
+mf_status mf_quantize_input(const mf_config* cfg, const void* x, int32_t x_dtype, int64_t n,
+                            int64_t k, int64_t ldx, const void* fixed_scale, void* codes,
+                            void* xscale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces quantization.py weight_tiles (:82-91) + pack_weight (:94-112).
+ * w: PyTorch-layout [o, k] weights, row stride ldw.  packed: [m, p, rows, cols]
+ * uint8 (int64 when cfg->wide_codes); wscale: [m*reads, p, cols] FP32/FP64. */
+mf_status mf_program_weights(const mf_config* cfg, const void* w, int32_t w_dtype, int64_t o,
+                             int64_t k, int64_t ldw, void* packed, void* wscale,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of scratch mf_quantize_input (is_weight=0, shape [n,k]) or
+ * mf_program_weights (is_weight=1, shape [o,k]) needs. */
+mf_status mf_quantize_workspace(const mf_config* cfg, int32_t is_weight, int64_t rows,
+                                int64_t cols, size_t* bytes);
+
+/* The analog product for output tiles [tile_begin, tile_end): replaces
+ * cuda.partial (cuda.py:322-373) and the scale/sum epilogue of
+ * AnalogMatrix._execute (simulator.py:561-586), plus the bias add (:612-613).
+ *   codes/xscale: from mf_quantize_input ([n, m*rows], [n, m*reads]).
+ *   packed/wscale: from mf_program_weights ([m, p, rows, cols], [m*reads, p, cols]).
+ *   bias: NULL or [out_features] FP32 (FP64 when wide or stable).
+ *   out: [n, ldo] FP32 (FP64 when cfg->wide or stable); columns
+ *        [tile_begin*cols, min(tile_end*cols, out_features)) are written.
+ *   seed: AnalogMatrix.seed; event: read-event counter (simulator.py:427-429,633).
+ *   vector_offset: global index of row 0 (noise addresses stay global when rows
+ *        are sharded across calls or GPUs).
+ *   stable: 1 = FP64 restore_scales epilogue (simulator.py:57-66, the non-finite
+ *        rerun at :614-615).
+ *   workspace: mf_sliced_mm_workspace() bytes. */
+mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const void* codes,
+                       const void* xscale, const void* packed, const void* wscale,
+                       const void* bias, void* out, int64_t n, int32_t m, int32_t p,
+                       int32_t out_features, int64_t ldo, int32_t tile_begin, int32_t tile_end,
+                       uint32_t seed, uint64_t event, int64_t vector_offset, int32_t stable,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedule, int64_t n,
+                                 int32_t m, int32_t p, int32_t tile_begin, int32_t tile_end,
+                                 size_t* bytes);
+
+/* Resource admission for a schedule (replaces Simulator._admit, simulator.py:216-237,
+ * and Program.resources, cuda.py:239-273).  MF_ERR_RESOURCE if it cannot run. */
+mf_status mf_query(const mf_config* cfg, const mf_schedule* schedule, int64_t n, int32_t m,
+                   int32_t p, mf_resources* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEMFAST_B200_H */

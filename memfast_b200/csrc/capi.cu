@@ -1,0 +1,212 @@
+// C ABI of libmemfast_b200 (declared in include/memfast_b200.h).
+//
+// Validation mirrors the argument checks the reference performs before it
+// launches (cuda.py:322-373, simulator.py:216-237); failures return a status
+// and leave a message for mf_last_error() instead of raising.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mf {
+
+static thread_local std::string g_last_error;
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void set_error(const char* fmt, ...) {
+    char buffer[512];
+    va_list args;
+    va_start(args, fmt);
+    vsnprintf(buffer, sizeof(buffer), fmt, args);
+    va_end(args);
+    g_last_error = buffer;
+}
+
+mf_status cuda_status(cudaError_t err, const char* what) {
+    set_error("%s: %s (%s)", what, cudaGetErrorString(err), cudaGetErrorName(err));
+    return MF_ERR_CUDA;
+}
+
+static mf_status check_config(const mf_config* c) {
+    if (!c) {
+        set_error("config is NULL");
+        return MF_ERR_INVALID;
+    }
+    if (c->abi_version != MF_ABI_VERSION) {
+        set_error("config ABI version %d, library expects %d", c->abi_version, MF_ABI_VERSION);
+        return MF_ERR_INVALID;
+    }
+    if (c->n_in < 1 || c->n_in > MF_MAX_SLICES || c->n_w < 1 || c->n_w > MF_MAX_SLICES) {
+        set_error("slice counts must be in [1, %d]", MF_MAX_SLICES);
+        return MF_ERR_INVALID;
+    }
+    if (c->rows < 1 || c->cols < 4 || c->cols % 4 || c->read_rows < 1 || c->read_rows > c->rows ||
+        c->reads != (c->rows + c->read_rows - 1) / c->read_rows) {
+        set_error("invalid array geometry (rows %d, cols %d, read_rows %d, reads %d)", c->rows, c->cols,
+                  c->read_rows, c->reads);
+        return MF_ERR_INVALID;
+    }
+    for (int i = 0; i < c->n_w; ++i)
+        if (c->adc_max[i] < 1 || c->adc_max[i] > 65535) {
+            set_error("adc maximum %d out of range", c->adc_max[i]);
+            return MF_ERR_INVALID;
+        }
+    if (c->read_mode < 0 || c->read_mode > 2) {
+        set_error("read_mode must be 0 (shared), 1 (slice_pair) or 2 (output)");
+        return MF_ERR_INVALID;
+    }
+    return MF_OK;
+}
+
+}  // namespace mf
+
+using namespace mf;
+
+extern "C" {
+
+int32_t mf_abi_version(void) { return MF_ABI_VERSION; }
+
+uint64_t mf_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int32_t mf_last_error(char* buffer, size_t capacity) {
+    const std::string& e = g_last_error;
+    if (buffer && capacity) {
+        size_t n = e.size() < capacity - 1 ? e.size() : capacity - 1;
+        memcpy(buffer, e.data(), n);
+        buffer[n] = 0;
+    }
+    return (int32_t)e.size();
+}
+
+mf_status mf_device_check(int32_t index, int32_t* is_sm100) {
+    int count = 0;
+    MF_CHECK_CUDA(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (index < 0 || index >= count) {
+        set_error("device %d not present (%d visible)", index, count);
+        return MF_ERR_INVALID;
+    }
+    int major = 0, minor = 0;
+    MF_CHECK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, index), "capability");
+    MF_CHECK_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, index), "capability");
+    if (is_sm100) *is_sm100 = (major == 10 && minor == 0);
+    return MF_OK;
+}
+
+mf_status mf_quantize_workspace(const mf_config* cfg, int32_t is_weight, int64_t rows, int64_t cols,
+                                size_t* bytes) {
+    mf_status st = check_config(cfg);
+    if (st) return st;
+    if (!bytes || rows < 1 || cols < 1) {
+        set_error("quantize workspace query needs positive shape and an output pointer");
+        return MF_ERR_INVALID;
+    }
+    *bytes = quantize_workspace_bytes(*cfg, is_weight != 0, rows, cols);
+    return MF_OK;
+}
+
+mf_status mf_quantize_input(const mf_config* cfg, const void* x, int32_t x_dtype, int64_t n, int64_t k,
+                            int64_t ldx, const void* fixed_scale, void* codes, void* xscale,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+    mf_status st = check_config(cfg);
+    if (st) return st;
+    if (!x || !codes || !xscale || n < 1 || k < 1 || ldx < k || x_dtype < MF_F32 || x_dtype > MF_F64) {
+        set_error("mf_quantize_input: invalid operands (n=%lld k=%lld ldx=%lld dtype=%d)", (long long)n,
+                  (long long)k, (long long)ldx, x_dtype);
+        return MF_ERR_INVALID;
+    }
+    if (!fixed_scale && !workspace) {
+        set_error("mf_quantize_input: dynamic scales need a workspace");
+        return MF_ERR_INVALID;
+    }
+    return quantize_input(*cfg, x, x_dtype, n, k, ldx, fixed_scale, codes, xscale, workspace,
+                          workspace_bytes, (cudaStream_t)stream);
+}
+
+mf_status mf_program_weights(const mf_config* cfg, const void* w, int32_t w_dtype, int64_t o, int64_t k,
+                             int64_t ldw, void* packed, void* wscale, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    mf_status st = check_config(cfg);
+    if (st) return st;
+    if (!w || !packed || !wscale || !workspace || o < 1 || k < 1 || ldw < k || w_dtype < MF_F32 ||
+        w_dtype > MF_F64) {
+        set_error("mf_program_weights: invalid operands (o=%lld k=%lld ldw=%lld dtype=%d)", (long long)o,
+                  (long long)k, (long long)ldw, w_dtype);
+        return MF_ERR_INVALID;
+    }
+    return program_weights(*cfg, w, w_dtype, o, k, ldw, packed, wscale, workspace, workspace_bytes,
+                           (cudaStream_t)stream);
+}
+
+static bool use_ideal(const mf_config& c, const mf_schedule& s) {
+    if (!c.ideal || !exact_integer_counts(c)) return false;
+    if (s.kernel == 1 || s.kernel == 0 || s.kernel == 2) return generic_ideal_fits(c, s);
+    return false;
+}
+
+static mf_schedule schedule_or_default(const mf_schedule* s) {
+    mf_schedule d{0, 32, 64, 2};
+    return s ? *s : d;
+}
+
+mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedule, int64_t n, int32_t m,
+                                 int32_t p, int32_t tile_begin, int32_t tile_end, size_t* bytes) {
+    mf_status st = check_config(cfg);
+    if (st) return st;
+    if (!bytes || n < 0 || m < 1 || p < 1 || tile_begin < 0 || tile_end > p || tile_begin >= tile_end) {
+        set_error("mf_sliced_mm_workspace: invalid shape");
+        return MF_ERR_INVALID;
+    }
+    mf_schedule s = schedule_or_default(schedule);
+    *bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, tile_end - tile_begin);
+    return MF_OK;
+}
+
+mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const void* codes,
+                       const void* xscale, const void* packed, const void* wscale, const void* bias,
+                       void* out, int64_t n, int32_t m, int32_t p, int32_t out_features, int64_t ldo,
+                       int32_t tile_begin, int32_t tile_end, uint32_t seed, uint64_t event,
+                       int64_t vector_offset, int32_t stable, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+    mf_status st = check_config(cfg);
+    if (st) return st;
+    if (!codes || !xscale || !packed || !wscale || !out || n < 0 || m < 1 || p < 1 || out_features < 1 ||
+        out_features > (int64_t)p * cfg->cols || ldo < out_features || tile_begin < 0 || tile_end > p ||
+        tile_begin >= tile_end || vector_offset < 0) {
+        set_error("mf_sliced_mm: invalid operands (n=%lld m=%d p=%d out=%d ldo=%lld tiles=[%d,%d))",
+                  (long long)n, m, p, out_features, (long long)ldo, tile_begin, tile_end);
+        return MF_ERR_INVALID;
+    }
+    if (n == 0) return MF_OK;
+    if ((long long)(n + 31) / 32 > 2147483647LL) {
+        set_error("mf_sliced_mm: too many vectors for one launch");
+        return MF_ERR_RESOURCE;
+    }
+    mf_schedule s = schedule_or_default(schedule);
+    MMArgs a{codes, xscale, packed, wscale, bias, out, n, m, p, out_features, ldo, tile_begin, tile_end,
+             seed, event, vector_offset, stable};
+    if (use_ideal(*cfg, s)) return generic_ideal(*cfg, s, a, (cudaStream_t)stream);
+    return physical(*cfg, s, a, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+mf_status mf_query(const mf_config* cfg, const mf_schedule* schedule, int64_t n, int32_t m, int32_t p,
+                   mf_resources* out) {
+    mf_status st = check_config(cfg);
+    if (st) return st;
+    if (!out || m < 1 || p < 1 || n < 0) {
+        set_error("mf_query: invalid shape");
+        return MF_ERR_INVALID;
+    }
+    mf_schedule s = schedule_or_default(schedule);
+    memset(out, 0, sizeof(*out));
+    out->workspace_bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, p);
+    out->threads = 256;
+    return MF_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,567 @@
+// Generic SIMT engine for the sliced product: every configuration, every mode.
+//
+//   ideal_kernel     ideal devices whose ADC counts are exact integer digit dots
+//                    (reference.py:81-115 with V and G reduced to digits): digit
+//                    planes staged in shared memory 4 rows per word, dp4a dots,
+//                    min(dot, adc_max) counts, signed reconstruction in registers.
+//   restore_kernel   per-cell conductances with write variation, drift, stuck-at
+//                    faults and shared read variation (reference.py:10-51).
+//   physical_kernel  explicit FP32/FP64 currents in ascending row order with
+//                    voltage noise, slice-pair and output read modes and the
+//                    S-shaped ADC (reference.py:63-117).
+// Both product kernels end in the same fused epilogue: per read, the reconstructed
+// total is scaled fl(fl(T*xs)*ws) (or restore_scales in FP64, simulator.py:57-66)
+// and summed over reads in PyTorch's CPU cascade order (simulator.py:585), so
+// partials never leave registers.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mf {
+
+namespace {
+
+constexpr int IDEAL_TV = 32;      // vectors per CTA
+constexpr int IDEAL_TC = 64;      // output columns per CTA
+constexpr int PHYS_TV = 16;
+constexpr int PHYS_TC = 64;
+constexpr int PHYS_RCH = 32;      // rows staged per chunk
+constexpr int THREADS = 256;
+
+template <typename OutT, typename ScaleT, typename TotT>
+__device__ __forceinline__ OutT scaled_partial(TotT total, ScaleT xs, ScaleT ws);
+
+template <>
+__device__ __forceinline__ float scaled_partial<float, float, long long>(long long t, float xs, float ws) {
+    return __fmul_rn(__fmul_rn(__ll2float_rn(t), xs), ws);
+}
+template <>
+__device__ __forceinline__ float scaled_partial<float, float, int>(int t, float xs, float ws) {
+    return __fmul_rn(__fmul_rn(__int2float_rn(t), xs), ws);
+}
+template <>
+__device__ __forceinline__ double scaled_partial<double, double, long long>(long long t, double xs, double ws) {
+    return restore_scales(__ll2double_rn(t), xs, ws);
+}
+template <>
+__device__ __forceinline__ double scaled_partial<double, double, int>(int t, double xs, double ws) {
+    return restore_scales((double)t, xs, ws);
+}
+// Non-finite FP32 rerun of a narrow config: partials were FP32 (reference.py:116-117).
+template <>
+__device__ __forceinline__ double scaled_partial<double, float, long long>(long long t, float xs, float ws) {
+    return restore_scales((double)__ll2float_rn(t), (double)xs, (double)ws);
+}
+template <>
+__device__ __forceinline__ double scaled_partial<double, float, int>(int t, float xs, float ws) {
+    return restore_scales((double)__int2float_rn(t), (double)xs, (double)ws);
+}
+
+template <typename CodeT>
+__device__ __forceinline__ uint32_t digit_of(CodeT code, int shift, int mask) {
+    return (uint32_t)(((long long)code >> shift) & mask);
+}
+
+// ------------------------------------------------------------ ideal kernel --
+template <typename CodeT, typename TotT, typename OutT, typename ScaleT>
+__global__ void __launch_bounds__(THREADS) ideal_kernel(Layout L, MMArgs a, int power, long long full) {
+    extern __shared__ __align__(16) uint32_t smem[];
+    const int R4 = (L.rows + 3) >> 2;
+    uint32_t* sA = smem;                               // [n_in][32][R4]
+    uint32_t* sW = smem + L.n_in * IDEAL_TV * R4;      // [n_w][R4][64]
+    const CodeT* codes = static_cast<const CodeT*>(a.codes);
+    const CodeT* packed = static_cast<const CodeT*>(a.packed);
+    const ScaleT* xscale = static_cast<const ScaleT*>(a.xscale);
+    const ScaleT* wscale = static_cast<const ScaleT*>(a.wscale);
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const long long v0 = (long long)blockIdx.x * IDEAL_TV;
+    const long long col0 = (long long)a.tile_begin * L.C + (long long)blockIdx.y * IDEAL_TC;
+    const long long col_end = (long long)a.tile_end * L.C;
+    const int MR = a.m * L.reads;
+    const long long row_stride = (long long)a.m * L.R;
+
+    Cascade<OutT> acc[2][4];
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[e][j].init();
+
+    for (int i = 0; i < MR; ++i) {
+        const int arr = i / L.reads, g = i % L.reads;
+        const int r0 = g * L.rows;
+        const int len = L.rows < L.R - r0 ? L.rows : L.R - r0;
+        __syncthreads();
+        for (int idx = tid; idx < L.n_in * IDEAL_TV * R4; idx += THREADS) {
+            const int r4 = idx % R4, v = (idx / R4) % IDEAL_TV, s = idx / (R4 * IDEAL_TV);
+            const long long vec = v0 + v;
+            uint32_t word = 0;
+            if (vec < a.n) {
+                const CodeT* row = codes + vec * row_stride + (long long)arr * L.R + r0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int r = 4 * r4 + b;
+                    if (r < len) word |= digit_of(row[r], L.in_shift[s], L.in_mask[s]) << (8 * b);
+                }
+            }
+            sA[(s * IDEAL_TV + v) * R4 + r4] = word;
+        }
+        for (int idx = tid; idx < L.n_w * R4 * IDEAL_TC; idx += THREADS) {
+            const int c = idx % IDEAL_TC, r4 = (idx / IDEAL_TC) % R4, s = idx / (IDEAL_TC * R4);
+            const long long col = col0 + c;
+            uint32_t word = 0;
+            if (col < col_end) {
+                const long long t = col / L.C, cc = col % L.C;
+                const CodeT* base = packed + (((long long)arr * a.p + t) * L.R + r0) * L.C + cc;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int r = 4 * r4 + b;
+                    if (r < len) word |= digit_of(base[(long long)r * L.C], L.w_shift[s], L.w_mask[s]) << (8 * b);
+                }
+            }
+            sW[(s * R4 + r4) * IDEAL_TC + c] = word;
+        }
+        __syncthreads();
+
+        TotT total[2][4];
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) total[e][j] = 0;
+        for (int sa = 0; sa < L.n_in; ++sa) {
+            const uint32_t* pa0 = sA + (sa * IDEAL_TV + ty) * R4;
+            const uint32_t* pa1 = pa0 + 16 * R4;
+            for (int sw = 0; sw < L.n_w; ++sw) {
+                const uint32_t* pw = sW + sw * R4 * IDEAL_TC + 4 * tx;
+                uint32_t dot[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+                for (int r4 = 0; r4 < R4; ++r4) {
+                    const uint32_t x0 = pa0[r4], x1 = pa1[r4];
+                    const uint4 wv = *reinterpret_cast<const uint4*>(pw + r4 * IDEAL_TC);
+                    dot[0][0] = __dp4a(x0, wv.x, dot[0][0]);
+                    dot[0][1] = __dp4a(x0, wv.y, dot[0][1]);
+                    dot[0][2] = __dp4a(x0, wv.z, dot[0][2]);
+                    dot[0][3] = __dp4a(x0, wv.w, dot[0][3]);
+                    dot[1][0] = __dp4a(x1, wv.x, dot[1][0]);
+                    dot[1][1] = __dp4a(x1, wv.y, dot[1][1]);
+                    dot[1][2] = __dp4a(x1, wv.z, dot[1][2]);
+                    dot[1][3] = __dp4a(x1, wv.w, dot[1][3]);
+                }
+                const uint32_t maxw = (uint32_t)L.adc_max[sw];
+                const TotT factor = (TotT)(L.in_factor[sa] * L.w_factor[sw]);
+#pragma unroll
+                for (int e = 0; e < 2; ++e)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        total[e][j] += (TotT)(dot[e][j] < maxw ? dot[e][j] : maxw) * factor;
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const long long vec = v0 + ty + 16 * e;
+            if (vec >= a.n) continue;
+            const ScaleT xs = xscale[vec * MR + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const long long col = col0 + 4 * tx + j;
+                if (col >= col_end) continue;
+                const long long t = col / L.C, cc = col % L.C;
+                const ScaleT ws = wscale[((long long)i * a.p + t) * L.C + cc];
+                cascade_push(acc[e][j], scaled_partial<OutT, ScaleT, TotT>(total[e][j], xs, ws), i, power, full);
+            }
+        }
+    }
+    OutT* out = static_cast<OutT*>(a.out);
+    const ScaleT* bias = static_cast<const ScaleT*>(a.bias);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        const long long vec = v0 + ty + 16 * e;
+        if (vec >= a.n) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const long long col = col0 + 4 * tx + j;
+            if (col >= col_end || col >= a.out_features) continue;
+            OutT value = cascade_finish(acc[e][j]);
+            if (bias) value = add_rn(value, (OutT)bias[col]);
+            out[vec * a.ldo + col] = value;
+        }
+    }
+}
+
+// ---------------------------------------------------------- restore kernel --
+template <typename CurT>
+__global__ void restore_kernel(Layout L, Physics P, const void* packed_raw, int wide_codes, int m,
+                               int p, int begin, int width, uint32_t seed, uint64_t event, CurT* g) {
+    const long long cells = (long long)m * width * L.n_w * L.R * L.C;
+    const uint64_t read_seed = event_seed(seed, event);
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < cells;
+         idx += (long long)gridDim.x * blockDim.x) {
+        long long rest = idx;
+        const int c = rest % L.C; rest /= L.C;
+        const int r = rest % L.R; rest /= L.R;
+        const int w = rest % L.n_w; rest /= L.n_w;
+        const int tw = rest % width;
+        const int arr = (int)(rest / width);
+        const int tile = begin + tw;
+        const long long address = ((((long long)arr * p + tile) * L.n_w + w) * L.R + r) * L.C + c;
+        const long long pi = (((long long)arr * p + tile) * L.R + r) * L.C + c;
+        const long long code = wide_codes ? static_cast<const long long*>(packed_raw)[pi]
+                                          : (long long)static_cast<const uint8_t*>(packed_raw)[pi];
+        const long long state = (code >> L.w_shift[w]) & L.w_mask[w];
+        CurT raw;
+        if (sizeof(CurT) == 4) {
+            const float high = (float)P.high, low = (float)P.low, span = (float)P.span;
+            float f;
+            if (L.w_mask[w] == 1) f = state ? high : low;
+            else f = __fadd_rn(low, __fmul_rn(span, __fdiv_rn((float)state, (float)L.w_mask[w])));
+            if (P.write_var != 0) f = __fmul_rn(f, expf(__fmul_rn((float)P.write_var, rng_normal(address, seed, 10))));
+            f = __fmul_rn(f, (float)P.drift);
+            if (P.saf_cut != 0) {
+                const float u = rng_uniform(address, seed, 30);
+                const float lo = (float)P.saf_low, hi = (float)P.saf_cut;
+                if (u < lo) f = low;
+                if (u >= lo && u < hi) f = high;
+            }
+            if (P.read_mode == 0 && P.read_var != 0)
+                f = __fmul_rn(f, expf(__fmul_rn((float)P.read_var, rng_normal(address, read_seed, 20))));
+            raw = (CurT)f;
+        } else {
+            double d;
+            if (L.w_mask[w] == 1) d = state ? P.high : P.low;
+            else d = __dadd_rn(P.low, __dmul_rn(P.span, __ddiv_rn((double)state, (double)L.w_mask[w])));
+            if (P.write_var != 0)
+                d = __dmul_rn(d, (double)expf(__fmul_rn((float)P.write_var, rng_normal(address, seed, 10))));
+            d = __dmul_rn(d, P.drift);
+            if (P.saf_cut != 0) {
+                const float u = rng_uniform(address, seed, 30);
+                const float lo = (float)P.saf_low, hi = (float)P.saf_cut;
+                if (u < lo) d = P.low;
+                if (u >= lo && u < hi) d = P.high;
+            }
+            if (P.read_mode == 0 && P.read_var != 0)
+                d = __dmul_rn(d, (double)expf(__fmul_rn((float)P.read_var, rng_normal(address, read_seed, 20))));
+            raw = (CurT)d;
+        }
+        g[idx] = raw;
+    }
+}
+
+// ------------------------------------------------------------ ADC counts --
+__device__ __forceinline__ long long adc_count(float current, int maxw, float amw, const Physics& P) {
+    float value = __fmul_rn(__fmul_rn(current, amw), (float)P.inv_unit);
+    if (P.nonlinear != 0) {
+        const float slope = (float)(P.nonlinear / maxw);
+        value = __fdiv_rn(value, __fadd_rn(1.0f, fabsf(__fmul_rn(slope, value))));
+    }
+    value = value < 0.0f ? 0.0f : value;
+    value = value > (float)maxw ? (float)maxw : value;
+    return (long long)rintf(value);
+}
+
+__device__ __forceinline__ long long adc_count(double current, int maxw, double amw, const Physics& P) {
+    double value = __dmul_rn(__dmul_rn(current, amw), P.inv_unit);
+    if (P.nonlinear != 0) {
+        const double slope = P.nonlinear / maxw;
+        value = __ddiv_rn(value, __dadd_rn(1.0, fabs(__dmul_rn(slope, value))));
+    }
+    value = value < 0.0 ? 0.0 : value;
+    value = value > (double)maxw ? (double)maxw : value;
+    return (long long)rint(value);
+}
+
+template <typename T> __device__ __forceinline__ T mul_rn(T a, T b);
+template <> __device__ __forceinline__ float mul_rn<float>(float a, float b) { return __fmul_rn(a, b); }
+template <> __device__ __forceinline__ double mul_rn<double>(double a, double b) { return __dmul_rn(a, b); }
+
+// ---------------------------------------------------------- physical kernel --
+template <typename CodeT, typename CurT, typename OutT, typename ScaleT>
+__global__ void __launch_bounds__(THREADS) physical_kernel(Layout L, Physics P, MMArgs a, const CurT* G,
+                                                           int group_begin, int group_width, int power,
+                                                           long long full) {
+    __shared__ CurT sV[PHYS_RCH][PHYS_TV];
+    __shared__ CurT sG[PHYS_RCH][PHYS_TC];
+    const CodeT* codes = static_cast<const CodeT*>(a.codes);
+    const ScaleT* xscale = static_cast<const ScaleT*>(a.xscale);
+    const ScaleT* wscale = static_cast<const ScaleT*>(a.wscale);
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const long long v0 = (long long)blockIdx.x * PHYS_TV;
+    const long long col0 = (long long)group_begin * L.C + (long long)blockIdx.y * PHYS_TC;
+    const long long col_end = (long long)(group_begin + group_width) * L.C;
+    const int MR = a.m * L.reads;
+    const long long row_stride = (long long)a.m * L.R;
+    const uint64_t read_seed = event_seed(a.seed, a.event);
+    const bool output_mode = P.read_mode == 2 && P.read_var != 0;
+    const bool pair_mode = P.read_mode == 1 && P.read_var != 0;
+    const CurT low = (CurT)P.low;
+
+    Cascade<OutT> acc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j].init();
+
+    for (int i = 0; i < MR; ++i) {
+        const int arr = i / L.reads, g = i % L.reads;
+        const int r0 = g * L.rows;
+        const int len = L.rows < L.R - r0 ? L.rows : L.R - r0;
+        long long total[4] = {0, 0, 0, 0};
+        for (int sa = 0; sa < L.n_in; ++sa) {
+            const int amask = L.in_mask[sa];
+            for (int sw = 0; sw < L.n_w; ++sw) {
+                CurT cur[4] = {0, 0, 0, 0}, mean[4] = {0, 0, 0, 0}, var[4] = {0, 0, 0, 0};
+                for (int cb = 0; cb < len; cb += PHYS_RCH) {
+                    const int clen = PHYS_RCH < len - cb ? PHYS_RCH : len - cb;
+                    __syncthreads();
+                    for (int idx = tid; idx < PHYS_TV * PHYS_RCH; idx += THREADS) {
+                        const int rr = idx % PHYS_RCH, v = idx / PHYS_RCH;
+                        const long long vec = v0 + v;
+                        CurT value = 0;
+                        if (vec < a.n && rr < clen) {
+                            const int r = r0 + cb + rr;
+                            const long long code = (long long)codes[vec * row_stride + (long long)arr * L.R + r];
+                            const long long d = (code >> L.in_shift[sa]) & amask;
+                            if (sizeof(CurT) == 4) {
+                                float x = __fmul_rn(__fdiv_rn((float)d, (float)amask), (float)P.voltage);
+                                if (P.volt_var != 0) {
+                                    const long long address =
+                                        (((vec + a.vector_offset) * a.m + arr) * L.n_in + sa) * L.R + r;
+                                    float f = __fmul_rn((float)P.volt_var, rng_normal(address, read_seed, 40));
+                                    x = __fmul_rn(x, __fadd_rn(1.0f, f));
+                                }
+                                value = (CurT)x;
+                            } else {
+                                double x = __dmul_rn(__ddiv_rn((double)d, (double)amask), P.voltage);
+                                if (P.volt_var != 0) {
+                                    const long long address =
+                                        (((vec + a.vector_offset) * a.m + arr) * L.n_in + sa) * L.R + r;
+                                    float f = __fmul_rn((float)P.volt_var, rng_normal(address, read_seed, 40));
+                                    x = __dmul_rn(x, (double)__fadd_rn(1.0f, f));
+                                }
+                                value = (CurT)x;
+                            }
+                        }
+                        sV[rr][v] = value;
+                    }
+                    for (int idx = tid; idx < PHYS_RCH * PHYS_TC; idx += THREADS) {
+                        const int c = idx % PHYS_TC, rr = idx / PHYS_TC;
+                        const long long col = col0 + c;
+                        CurT value = 0;
+                        if (col < col_end && rr < clen) {
+                            const int r = r0 + cb + rr;
+                            const long long t = col / L.C, cc = col % L.C;
+                            value = G[((((long long)arr * group_width + (t - group_begin)) * L.n_w + sw) * L.R + r) * L.C + cc];
+                            if (pair_mode) {
+                                const long long cell = ((((long long)arr * a.p + t) * L.n_w + sw) * L.R + r) * L.C + cc;
+                                const float e = expf(__fmul_rn((float)P.read_var,
+                                                               rng_normal(cell * L.n_in + sa, read_seed, 20)));
+                                value = sizeof(CurT) == 4 ? (CurT)__fmul_rn((float)value, e)
+                                                          : (CurT)__dmul_rn((double)value, (double)e);
+                            }
+                        }
+                        sG[rr][c] = value;
+                    }
+                    __syncthreads();
+                    for (int rr = 0; rr < clen; ++rr) {
+                        const CurT vr = sV[rr][ty];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const CurT gv = sG[rr][4 * tx + j];
+                            cur[j] = add_rn(cur[j], mul_rn(vr, add_rn(gv, -low)));
+                            if (output_mode) {
+                                mean[j] = add_rn(mean[j], mul_rn(vr, gv));
+                                var[j] = add_rn(var[j], mul_rn(mul_rn(vr, vr), mul_rn(gv, gv)));
+                            }
+                        }
+                    }
+                }
+                const long long factor = L.in_factor[sa] * L.w_factor[sw];
+                const int maxw = L.adc_max[sw];
+                const long long vec = v0 + ty;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    CurT current = cur[j];
+                    if (output_mode) {
+                        const long long col = col0 + 4 * tx + j;
+                        const long long t = col / L.C, cc = col % L.C;
+                        const long long address =
+                            (((((vec + a.vector_offset) * MR + i) * a.p + t) * L.n_in + sa) * L.n_w + sw) * L.C + cc;
+                        const float z = rng_normal(address, read_seed, 60);
+                        if (sizeof(CurT) == 4) {
+                            const float mu = __fmul_rn((float)mean[j], (float)P.mean_factor);
+                            const float sig = __fmul_rn((float)var[j], (float)P.var_factor);
+                            current = (CurT)__fadd_rn((float)current, __fadd_rn(mu, __fmul_rn(sqrtf(sig), z)));
+                        } else {
+                            const double mu = __dmul_rn((double)mean[j], P.mean_factor);
+                            const double sig = __dmul_rn((double)var[j], P.var_factor);
+                            current = (CurT)__dadd_rn((double)current, __dadd_rn(mu, __dmul_rn(sqrt(sig), (double)z)));
+                        }
+                    }
+                    const CurT amw = (CurT)((long long)amask * L.w_mask[sw]);
+                    total[j] += adc_count(current, maxw, amw, P) * factor;
+                }
+            }
+        }
+        const long long vec = v0 + ty;
+        if (vec < a.n) {
+            const ScaleT xs = xscale[vec * MR + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const long long col = col0 + 4 * tx + j;
+                if (col >= col_end) continue;
+                const long long t = col / L.C, cc = col % L.C;
+                const ScaleT ws = wscale[((long long)i * a.p + t) * L.C + cc];
+                cascade_push(acc[j], scaled_partial<OutT, ScaleT, long long>(total[j], xs, ws), i, power, full);
+            }
+        }
+    }
+    OutT* out = static_cast<OutT*>(a.out);
+    const ScaleT* bias = static_cast<const ScaleT*>(a.bias);
+    const long long vec = v0 + ty;
+    if (vec >= a.n) return;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const long long col = col0 + 4 * tx + j;
+        if (col >= col_end || col >= a.out_features) continue;
+        OutT value = cascade_finish(acc[j]);
+        if (bias) value = add_rn(value, (OutT)bias[col]);
+        out[vec * a.ldo + col] = value;
+    }
+}
+
+size_t ideal_smem(const mf_config& c) {
+    const size_t r4 = (size_t)(c.read_rows + 3) / 4;
+    return ((size_t)c.n_in * IDEAL_TV + (size_t)c.n_w * IDEAL_TC) * r4 * 4;
+}
+
+Physics make_physics(const mf_config& c) {
+    Physics P{};
+    P.precise = c.precise_currents;
+    P.read_mode = c.read_mode;
+    P.high = c.high;
+    P.low = c.low;
+    P.span = c.high - c.low;
+    P.voltage = c.voltage;
+    P.inv_unit = 1.0 / c.unit;
+    P.write_var = c.write_var;
+    P.read_var = c.read_var;
+    P.volt_var = c.volt_var;
+    P.nonlinear = c.nonlinear;
+    P.saf_low = c.saf_low;
+    P.saf_cut = c.saf_low + c.saf_high;
+    P.drift = c.drift;
+    const double s2 = c.read_var * c.read_var;
+    P.mean_factor = expm1(0.5 * s2);
+    P.var_factor = exp(s2) * expm1(s2);
+    return P;
+}
+
+template <typename OutT, typename ScaleT>
+mf_status launch_ideal_t(const mf_config& c, const MMArgs& a, cudaStream_t st) {
+    Layout L = make_layout(c);
+    const int MR = a.m * c.reads;
+    const int power = cascade_power(MR);
+    const long long full = (long long)MR - MR % (1LL << power);
+    const size_t smem = ideal_smem(c);
+    const long long cols = (long long)(a.tile_end - a.tile_begin) * c.cols;
+    dim3 grid((unsigned)((a.n + IDEAL_TV - 1) / IDEAL_TV), (unsigned)((cols + IDEAL_TC - 1) / IDEAL_TC));
+    const bool small_totals = reconstruction_bound(c) < 2147483647.0;
+#define MF_IDEAL(CODE, TOT)                                                                          \
+    do {                                                                                             \
+        auto kern = ideal_kernel<CODE, TOT, OutT, ScaleT>;                                           \
+        MF_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), \
+                      "ideal kernel smem attribute");                                                \
+        kern<<<grid, THREADS, smem, st>>>(L, a, power, full);                                         \
+    } while (0)
+    if (c.wide_codes) {
+        if (small_totals) MF_IDEAL(long long, int); else MF_IDEAL(long long, long long);
+    } else {
+        if (small_totals) MF_IDEAL(uint8_t, int); else MF_IDEAL(uint8_t, long long);
+    }
+#undef MF_IDEAL
+    MF_LAUNCH_CHECK("ideal_kernel");
+    return MF_OK;
+}
+
+template <typename CurT, typename OutT, typename ScaleT>
+mf_status launch_physical_t(const mf_config& c, const mf_schedule& s, const MMArgs& a, void* ws,
+                            size_t ws_bytes, cudaStream_t st) {
+    Layout L = make_layout(c);
+    Physics P = make_physics(c);
+    const int MR = a.m * c.reads;
+    const int power = cascade_power(MR);
+    const long long full = (long long)MR - MR % (1LL << power);
+    const int tiles = a.tile_end - a.tile_begin;
+    int width = s.arrays < 1 ? 1 : s.arrays;
+    width = width > tiles ? tiles : width;
+    const size_t need = physical_workspace_bytes(c, s, a.m, tiles);
+    if (ws_bytes < need) {
+        set_error("physical workspace too small: %zu < %zu bytes", ws_bytes, need);
+        return MF_ERR_RESOURCE;
+    }
+    CurT* G = static_cast<CurT*>(ws);
+    for (int begin = a.tile_begin; begin < a.tile_end; begin += width) {
+        const int gw = begin + width <= a.tile_end ? width : a.tile_end - begin;
+        const long long cells = (long long)a.m * gw * c.n_w * c.rows * c.cols;
+        long long blocks = (cells + 255) / 256;
+        if (blocks > 148 * 64) blocks = 148 * 64;
+        restore_kernel<CurT><<<(unsigned)blocks, 256, 0, st>>>(L, P, a.packed, c.wide_codes, a.m, a.p, begin, gw,
+                                                             a.seed, a.event, G);
+        MF_LAUNCH_CHECK("restore_kernel");
+        const long long cols = (long long)gw * c.cols;
+        dim3 grid((unsigned)((a.n + PHYS_TV - 1) / PHYS_TV), (unsigned)((cols + PHYS_TC - 1) / PHYS_TC));
+        if (c.wide_codes)
+            physical_kernel<long long, CurT, OutT, ScaleT><<<grid, THREADS, 0, st>>>(L, P, a, G, begin, gw, power, full);
+        else
+            physical_kernel<uint8_t, CurT, OutT, ScaleT><<<grid, THREADS, 0, st>>>(L, P, a, G, begin, gw, power, full);
+        MF_LAUNCH_CHECK("physical_kernel");
+    }
+    return MF_OK;
+}
+
+}  // namespace
+
+double reconstruction_bound(const mf_config& c) {
+    double in = 0, wt = 0;
+    for (int i = 0; i < c.n_in; ++i) in += fabs((double)c.in_factor[i]);
+    for (int i = 0; i < c.n_w; ++i) wt += fabs((double)c.w_factor[i]) * c.adc_max[i];
+    return in * wt;
+}
+
+bool exact_integer_counts(const mf_config& c) {
+    int maxadc = 0;
+    for (int i = 0; i < c.n_w; ++i) maxadc = c.adc_max[i] > maxadc ? c.adc_max[i] : maxadc;
+    const double eps = c.precise_currents ? ldexp(1.0, -52) : ldexp(1.0, -23);
+    return (c.read_rows + 16.0) * (maxadc + 1.0) * eps * 4.0 < 0.5;
+}
+
+bool generic_ideal_fits(const mf_config& c, const mf_schedule&) {
+    for (int i = 0; i < c.n_in; ++i)
+        if (c.in_mask[i] > 255) return false;
+    for (int i = 0; i < c.n_w; ++i)
+        if (c.w_mask[i] > 255) return false;
+    return ideal_smem(c) <= 200 * 1024;
+}
+
+mf_status generic_ideal(const mf_config& c, const mf_schedule&, const MMArgs& a, cudaStream_t st) {
+    if (a.stable) {
+        return c.wide ? launch_ideal_t<double, double>(c, a, st) : launch_ideal_t<double, float>(c, a, st);
+    }
+    return c.wide ? launch_ideal_t<double, double>(c, a, st) : launch_ideal_t<float, float>(c, a, st);
+}
+
+size_t physical_workspace_bytes(const mf_config& c, const mf_schedule& s, int32_t m, int32_t tiles) {
+    int width = s.arrays < 1 ? 1 : s.arrays;
+    width = width > tiles ? tiles : width;
+    const size_t elem = c.precise_currents ? 8 : 4;
+    return (size_t)m * width * c.n_w * c.rows * c.cols * elem;
+}
+
+mf_status physical(const mf_config& c, const mf_schedule& s, const MMArgs& a, void* ws, size_t ws_bytes,
+                   cudaStream_t st) {
+    const bool dbl_out = c.wide || a.stable;
+    if (c.precise_currents) {
+        if (!dbl_out) return launch_physical_t<double, float, float>(c, s, a, ws, ws_bytes, st);
+        return c.wide ? launch_physical_t<double, double, double>(c, s, a, ws, ws_bytes, st)
+                      : launch_physical_t<double, double, float>(c, s, a, ws, ws_bytes, st);
+    }
+    if (!dbl_out) return launch_physical_t<float, float, float>(c, s, a, ws, ws_bytes, st);
+    return c.wide ? launch_physical_t<float, double, double>(c, s, a, ws, ws_bytes, st)
+                  : launch_physical_t<float, double, float>(c, s, a, ws, ws_bytes, st);
+}
+
+}  // namespace mf

@@ -1,0 +1,53 @@
+// Internal host-side entry points shared by the C ABI and the kernel files.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace mf {
+
+size_t quantize_workspace_bytes(const mf_config& c, bool weight, int64_t rows, int64_t cols);
+
+mf_status quantize_input(const mf_config& c, const void* x, int dtype, int64_t n, int64_t k,
+                         int64_t ldx, const void* fixed, void* codes, void* xscale,
+                         void* workspace, size_t ws_bytes, cudaStream_t stream);
+
+mf_status program_weights(const mf_config& c, const void* w, int dtype, int64_t o, int64_t k,
+                          int64_t ldw, void* packed, void* wscale, void* workspace,
+                          size_t ws_bytes, cudaStream_t stream);
+
+// Everything one sliced product needs, validated by the ABI layer.
+struct MMArgs {
+    const void* codes;
+    const void* xscale;
+    const void* packed;
+    const void* wscale;
+    const void* bias;
+    void* out;
+    int64_t n;
+    int32_t m, p, out_features;
+    int64_t ldo;
+    int32_t tile_begin, tile_end;
+    uint32_t seed;
+    uint64_t event;
+    int64_t vector_offset;
+    int32_t stable;
+};
+
+// Largest |signed reconstruction| of one read, as in config.py:114-122.
+double reconstruction_bound(const mf_config& c);
+
+// True when ideal ADC counts equal exact integer digit dots for this config: the
+// reference's FP32 (or FP64) current error stays below half a count.
+bool exact_integer_counts(const mf_config& c);
+
+// Generic SIMT engine (all configurations).
+bool generic_ideal_fits(const mf_config& c, const mf_schedule& s);
+mf_status generic_ideal(const mf_config& c, const mf_schedule& s, const MMArgs& a, cudaStream_t st);
+size_t physical_workspace_bytes(const mf_config& c, const mf_schedule& s, int32_t m, int32_t tiles);
+mf_status physical(const mf_config& c, const mf_schedule& s, const MMArgs& a, void* workspace,
+                   size_t ws_bytes, cudaStream_t st);
+
+}  // namespace mf

@@ -1,0 +1,361 @@
+// Group quantisation and bit-slice packing on the device.
+//
+// Restates memfast/quantization.py for device buffers:
+//   grouped_quantize  quantization.py:9-44   (INT: scale = max/upper, clamped to the
+//                     smallest subnormal, codes = rint(x/scale) clamped; BFP: shared
+//                     power-of-two exponent per group)
+//   pack_weight       quantization.py:94-112 (two's-complement mask, [m,p,R,C] tiles,
+//                     per-read scale gather with replicate padding)
+//   input_tiles       quantization.py:115-137
+// Three passes: group |max| (atomic max on the IEEE bit pattern, exact for
+// non-negative values), elementwise codes, and the per-read scale gather.
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <float.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mf {
+
+namespace {
+
+template <typename Acc>
+__device__ __forceinline__ Acc load_as(const void* base, int dtype, int64_t index);
+
+template <>
+__device__ __forceinline__ float load_as<float>(const void* base, int dtype, int64_t index) {
+    switch (dtype) {
+        case MF_F16: return __half2float(static_cast<const __half*>(base)[index]);
+        case MF_BF16: return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[index]);
+        case MF_F64: return __double2float_rn(static_cast<const double*>(base)[index]);
+        default: return static_cast<const float*>(base)[index];
+    }
+}
+
+template <>
+__device__ __forceinline__ double load_as<double>(const void* base, int dtype, int64_t index) {
+    switch (dtype) {
+        case MF_F16: return (double)__half2float(static_cast<const __half*>(base)[index]);
+        case MF_BF16: return (double)__bfloat162float(static_cast<const __nv_bfloat16*>(base)[index]);
+        case MF_F64: return static_cast<const double*>(base)[index];
+        default: return (double)static_cast<const float*>(base)[index];
+    }
+}
+
+__device__ __forceinline__ void atomic_max_nonneg(float* slot, float value) {
+    atomicMax(reinterpret_cast<unsigned int*>(slot), __float_as_uint(value));
+}
+__device__ __forceinline__ void atomic_max_nonneg(double* slot, double value) {
+    atomicMax(reinterpret_cast<unsigned long long*>(slot), (unsigned long long)__double_as_longlong(value));
+}
+
+// Logical element (row, col) of the quantised matrix.  Inputs are stored as
+// [rows, cols]; weights are quantised as W^T, so logical (k, o) lives at w[o, k].
+struct View {
+    const void* data;
+    int dtype;
+    int64_t rows, cols, ld;
+    int transposed;
+    __device__ __forceinline__ int64_t offset(int64_t r, int64_t c) const {
+        return transposed ? c * ld + r : r * ld + c;
+    }
+};
+
+struct GroupGrid {
+    int64_t gr, gc, nc;  // group extents and number of group columns
+};
+
+// Each thread scans a run of consecutive stored elements, keeps a running |max|
+// while they stay in one group, and publishes it with one atomic per group run.
+template <typename Acc>
+__global__ void group_amax_kernel(View v, GroupGrid g, Acc* maxima) {
+    constexpr int64_t RUN = 8;
+    const int64_t inner = v.transposed ? v.rows : v.cols;
+    const int64_t total = v.rows * v.cols;
+    const int64_t runs = (total + RUN - 1) / RUN;
+    for (int64_t run = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; run < runs;
+         run += (int64_t)gridDim.x * blockDim.x) {
+        int64_t begin = run * RUN, end = begin + RUN < total ? begin + RUN : total;
+        int64_t current = -1;
+        Acc best = Acc(0);
+        for (int64_t i = begin; i < end; ++i) {
+            int64_t outer = i / inner, in = i % inner;
+            int64_t r = v.transposed ? in : outer;
+            int64_t c = v.transposed ? outer : in;
+            Acc x = load_as<Acc>(v.data, v.dtype, outer * v.ld + in);
+            Acc a = x < Acc(0) ? -x : x;
+            int64_t group = (r / g.gr) * g.nc + c / g.gc;
+            if (group != current) {
+                if (current >= 0) atomic_max_nonneg(&maxima[current], best);
+                current = group;
+                best = a;
+            } else if (a > best) {
+                best = a;
+            }
+        }
+        if (current >= 0) atomic_max_nonneg(&maxima[current], best);
+    }
+}
+
+struct QuantSpec {
+    int bits, signed_codes, bfp, bw_e;
+    int64_t lower, upper, mask;
+};
+
+// Scale of a group from its |max| (quantization.py:27-39).
+template <typename Acc>
+__device__ __forceinline__ Acc group_scale(Acc maximum, const QuantSpec& s);
+
+template <>
+__device__ __forceinline__ float group_scale<float>(float maximum, const QuantSpec& s) {
+    float base = maximum > 0.0f ? maximum : 1.0f;
+    float scale = __fdiv_rn(base, (float)s.upper);
+    const float smallest = 1.40129846e-45f;
+    return scale < smallest ? smallest : scale;
+}
+
+template <>
+__device__ __forceinline__ double group_scale<double>(double maximum, const QuantSpec& s) {
+    if (!s.bfp) {
+        double base = maximum > 0.0 ? maximum : 1.0;
+        double scale = __ddiv_rn(base, (double)s.upper);
+        const double smallest = 4.9406564584124654e-324;
+        return scale < smallest ? smallest : scale;
+    }
+    // floor(log2(max(m, DBL_MIN))) is the frexp exponent minus one, exactly.
+    int e;
+    frexp(maximum > DBL_MIN ? maximum : DBL_MIN, &e);
+    int exponent = e - 1;
+    int limit = (1 << (s.bw_e - 1)) - 1;
+    exponent = exponent < 1 - limit ? 1 - limit : (exponent > limit ? limit : exponent);
+    return ldexp(1.0, exponent + 2 - s.bits);
+}
+
+template <typename Acc>
+__device__ __forceinline__ int64_t quantise(Acc x, Acc scale, const QuantSpec& s) {
+    Acc q = rint(x / scale);
+    if (q < (Acc)s.lower) q = (Acc)s.lower;
+    if (q > (Acc)s.upper) q = (Acc)s.upper;
+    return (int64_t)q & s.mask;
+}
+
+// Input codes: [n, m*R] (zero beyond k).
+template <typename Acc, typename CodeT>
+__global__ void input_code_kernel(View v, GroupGrid g, const Acc* maxima, const Acc* fixed,
+                                  QuantSpec s, int64_t padded_cols, CodeT* codes) {
+    const int64_t total = v.rows * padded_cols;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t r = i / padded_cols, c = i % padded_cols;
+        int64_t code = 0;
+        if (c < v.cols) {
+            Acc x = load_as<Acc>(v.data, v.dtype, v.offset(r, c));
+            Acc scale = fixed ? fixed[c] : group_scale<Acc>(maxima[(r / g.gr) * g.nc + c / g.gc], s);
+            code = quantise<Acc>(x, scale, s);
+        }
+        codes[i] = (CodeT)code;
+    }
+}
+
+// Input per-read scales: xscale[r, i] for read starts i (replicate padding).
+template <typename Acc, typename ScaleT>
+__global__ void input_scale_kernel(View v, GroupGrid g, const Acc* maxima, const Acc* fixed,
+                                   QuantSpec s, int R, int read_rows, int reads, int64_t m,
+                                   ScaleT* xscale) {
+    const int64_t per_row = m * reads;
+    const int64_t total = v.rows * per_row;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t r = i / per_row, idx = i % per_row;
+        int64_t start = (idx / reads) * R + (idx % reads) * read_rows;
+        int64_t c = start < v.cols ? start : v.cols - 1;
+        xscale[i] = (ScaleT)(fixed ? fixed[c] : group_scale<Acc>(maxima[(r / g.gr) * g.nc + c / g.gc], s));
+    }
+}
+
+// Packed weights [m, p, R, C] from logical W^T[k, o]; a 32x32 tile is staged in
+// shared memory so reads (along k in w[o, k]) and writes (along c) both coalesce.
+template <typename Acc, typename CodeT>
+__global__ void weight_code_kernel(View v, GroupGrid g, const Acc* maxima, QuantSpec s, int R,
+                                   int C, int64_t m, int64_t p, CodeT* packed) {
+    __shared__ int64_t tile[32][33];
+    const int64_t k0 = (int64_t)blockIdx.x * 32, o0 = (int64_t)blockIdx.y * 32;
+    const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+    for (int j = ty; j < 32; j += 8) {
+        int64_t k = k0 + tx, o = o0 + j;
+        int64_t code = 0;
+        if (k < v.rows && o < v.cols) {
+            Acc x = load_as<Acc>(v.data, v.dtype, v.offset(k, o));
+            code = quantise<Acc>(x, group_scale<Acc>(maxima[(k / g.gr) * g.nc + o / g.gc], s), s);
+        }
+        tile[tx][j] = code;
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += 8) {
+        int64_t k = k0 + j, o = o0 + tx;
+        if (k < m * R && o < p * C) {
+            int64_t arr = k / R, r = k % R, t = o / C, c = o % C;
+            packed[((arr * p + t) * R + r) * C + c] = (CodeT)tile[j][tx];
+        }
+    }
+}
+
+// wscale[i, t, c] = scale at (read start row, column) with replicate padding.
+template <typename Acc, typename ScaleT>
+__global__ void weight_scale_kernel(View v, GroupGrid g, const Acc* maxima, QuantSpec s, int R,
+                                    int C, int read_rows, int reads, int64_t m, int64_t p,
+                                    ScaleT* wscale) {
+    const int64_t total = m * reads * p * C;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t col = i % (p * C), idx = i / (p * C);
+        int64_t start = (idx / reads) * R + (idx % reads) * read_rows;
+        int64_t k = start < v.rows ? start : v.rows - 1;
+        int64_t o = col < v.cols ? col : v.cols - 1;
+        wscale[i] = (ScaleT)group_scale<Acc>(maxima[(k / g.gr) * g.nc + o / g.gc], s);
+    }
+}
+
+int grid_for(int64_t work, int threads) {
+    int64_t blocks = (work + threads - 1) / threads;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    return blocks < 1 ? 1 : (int)blocks;
+}
+
+GroupGrid groups_of(int64_t rows, int64_t cols, int32_t gr, int32_t gc) {
+    GroupGrid g;
+    g.gr = gr <= 0 ? rows : (gr < rows ? gr : rows);
+    g.gc = gc <= 0 ? cols : (gc < cols ? gc : cols);
+    if (g.gr < 1) g.gr = 1;
+    if (g.gc < 1) g.gc = 1;
+    g.nc = (cols + g.gc - 1) / g.gc;
+    return g;
+}
+
+QuantSpec spec_of(int bits, int signed_codes, int bw_e) {
+    QuantSpec s;
+    s.bits = bits;
+    s.signed_codes = signed_codes;
+    s.bfp = bw_e > 0;
+    s.bw_e = bw_e;
+    s.upper = (int64_t(1) << (bits - (signed_codes ? 1 : 0))) - 1;
+    if (s.bfp) {
+        s.lower = -(int64_t(1) << (bits - 1));
+        s.upper = (int64_t(1) << (bits - 1)) - 1;
+    } else {
+        s.lower = signed_codes ? -s.upper : 0;
+    }
+    s.mask = bits >= 63 ? -1 : ((int64_t(1) << bits) - 1);
+    return s;
+}
+
+bool uses_double(const mf_config& c, int bits) { return bits > 8 || c.bw_e > 0; }
+
+}  // namespace
+
+size_t quantize_workspace_bytes(const mf_config& c, bool weight, int64_t rows, int64_t cols) {
+    // Logical matrix: inputs [n, k]; weights W^T = [k, o] for w of shape [o, k].
+    int64_t lr = weight ? cols : rows, lc = weight ? rows : cols;
+    GroupGrid g = weight ? groups_of(lr, lc, c.w_group_rows, c.w_group_cols)
+                         : groups_of(lr, lc, c.in_group_rows, c.in_group_cols);
+    int64_t nr = (lr + g.gr - 1) / g.gr;
+    int bits = weight ? c.weight_bits : c.activation_bits;
+    size_t elem = uses_double(c, bits) ? 8 : 4;
+    return (size_t)(nr * g.nc) * elem + 256;
+}
+
+template <typename Acc, typename ScaleT>
+static mf_status run_input(const mf_config& c, const View& v, const GroupGrid& g, const QuantSpec& s,
+                           const void* fixed, void* codes, void* xscale, void* workspace,
+                           size_t need, cudaStream_t stream) {
+    const int threads = 256;
+    const int64_t n = v.rows, k = v.cols, m = (k + c.rows - 1) / c.rows;
+    Acc* maxima = static_cast<Acc*>(workspace);
+    const Acc* fx = static_cast<const Acc*>(fixed);
+    if (!fx) {
+        MF_CHECK_CUDA(cudaMemsetAsync(maxima, 0, need, stream), "memset group maxima");
+        group_amax_kernel<Acc><<<grid_for((n * k + 7) / 8, threads), threads, 0, stream>>>(v, g, maxima);
+        MF_LAUNCH_CHECK("group_amax_kernel");
+    }
+    if (c.wide_codes)
+        input_code_kernel<Acc, int64_t><<<grid_for(n * m * c.rows, threads), threads, 0, stream>>>(
+            v, g, maxima, fx, s, m * c.rows, static_cast<int64_t*>(codes));
+    else
+        input_code_kernel<Acc, uint8_t><<<grid_for(n * m * c.rows, threads), threads, 0, stream>>>(
+            v, g, maxima, fx, s, m * c.rows, static_cast<uint8_t*>(codes));
+    MF_LAUNCH_CHECK("input_code_kernel");
+    input_scale_kernel<Acc, ScaleT><<<grid_for(n * m * c.reads, threads), threads, 0, stream>>>(
+        v, g, maxima, fx, s, c.rows, c.read_rows, c.reads, m, static_cast<ScaleT*>(xscale));
+    MF_LAUNCH_CHECK("input_scale_kernel");
+    return MF_OK;
+}
+
+mf_status quantize_input(const mf_config& c, const void* x, int dtype, int64_t n, int64_t k,
+                         int64_t ldx, const void* fixed, void* codes, void* xscale,
+                         void* workspace, size_t ws_bytes, cudaStream_t stream) {
+    View v{x, dtype, n, k, ldx, 0};
+    GroupGrid g = groups_of(n, k, c.in_group_rows, c.in_group_cols);
+    QuantSpec s = spec_of(c.activation_bits, 1, c.bw_e);
+    size_t need = quantize_workspace_bytes(c, false, n, k) - 256;
+    if (!fixed && ws_bytes < need) {
+        set_error("quantize workspace too small: %zu < %zu bytes", ws_bytes, need);
+        return MF_ERR_RESOURCE;
+    }
+    // grouped_quantize computes in FP64 iff bits > 8 or BFP; the stored scales are
+    // FP64 iff Config.wide (quantization.py:10,131).  A fixed scale arrives in the
+    // stored dtype and is applied in it (quantization.py:124-130).
+    const bool dbl = uses_double(c, c.activation_bits);
+    if (fixed) {
+        return c.wide ? run_input<double, double>(c, v, g, s, fixed, codes, xscale, workspace, need, stream)
+                      : run_input<float, float>(c, v, g, s, fixed, codes, xscale, workspace, need, stream);
+    }
+    if (dbl) return run_input<double, double>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
+    if (c.wide) return run_input<float, double>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
+    return run_input<float, float>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
+}
+
+template <typename Acc, typename ScaleT>
+static mf_status run_weights(const mf_config& c, const View& v, const GroupGrid& g, const QuantSpec& s,
+                             void* packed, void* wscale, void* workspace, size_t need,
+                             cudaStream_t stream) {
+    const int threads = 256;
+    const int64_t k = v.rows, o = v.cols;
+    const int64_t m = (k + c.rows - 1) / c.rows, p = (o + c.cols - 1) / c.cols;
+    Acc* maxima = static_cast<Acc*>(workspace);
+    MF_CHECK_CUDA(cudaMemsetAsync(maxima, 0, need, stream), "memset group maxima");
+    group_amax_kernel<Acc><<<grid_for((o * k + 7) / 8, threads), threads, 0, stream>>>(v, g, maxima);
+    MF_LAUNCH_CHECK("group_amax_kernel");
+    dim3 tgrid((unsigned)((m * c.rows + 31) / 32), (unsigned)((p * c.cols + 31) / 32));
+    dim3 tblock(32, 8);
+    if (c.wide_codes)
+        weight_code_kernel<Acc, int64_t><<<tgrid, tblock, 0, stream>>>(
+            v, g, maxima, s, c.rows, c.cols, m, p, static_cast<int64_t*>(packed));
+    else
+        weight_code_kernel<Acc, uint8_t><<<tgrid, tblock, 0, stream>>>(
+            v, g, maxima, s, c.rows, c.cols, m, p, static_cast<uint8_t*>(packed));
+    MF_LAUNCH_CHECK("weight_code_kernel");
+    weight_scale_kernel<Acc, ScaleT><<<grid_for(m * c.reads * p * c.cols, threads), threads, 0, stream>>>(
+        v, g, maxima, s, c.rows, c.cols, c.read_rows, c.reads, m, p, static_cast<ScaleT*>(wscale));
+    MF_LAUNCH_CHECK("weight_scale_kernel");
+    return MF_OK;
+}
+
+mf_status program_weights(const mf_config& c, const void* w, int dtype, int64_t o, int64_t k,
+                          int64_t ldw, void* packed, void* wscale, void* workspace,
+                          size_t ws_bytes, cudaStream_t stream) {
+    View v{w, dtype, k, o, ldw, 1};  // logical [k, o] = w^T
+    GroupGrid g = groups_of(k, o, c.w_group_rows, c.w_group_cols);
+    QuantSpec s = spec_of(c.weight_bits, c.weight_signed, c.bw_e);
+    size_t need = quantize_workspace_bytes(c, true, o, k) - 256;
+    if (ws_bytes < need) {
+        set_error("weight workspace too small: %zu < %zu bytes", ws_bytes, need);
+        return MF_ERR_RESOURCE;
+    }
+    const bool dbl = uses_double(c, c.weight_bits);
+    if (dbl) return run_weights<double, double>(c, v, g, s, packed, wscale, workspace, need, stream);
+    if (c.wide) return run_weights<float, double>(c, v, g, s, packed, wscale, workspace, need, stream);
+    return run_weights<float, float>(c, v, g, s, packed, wscale, workspace, need, stream);
+}
+
+}  // namespace mf

@@ -1,0 +1,173 @@
+"""Device quantisation and packing (memfast/quantization.py behaviour, on CUDA).
+
+* ``input_tiles``   -> ``mf_quantize_input``  (quantization.py:115-137 + :9-44)
+* ``weight_tiles``  -> ``mf_program_weights`` (quantization.py:82-112 + :9-44)
+* ``pack_weight``   packs already-integer codes for ``Simulator.map_quantized``
+  (quantization.py:94-112) with device tensor ops; it runs once per programming.
+* ``read_starts`` / ``check_read_scales`` / ``expanded_parameter`` keep the
+  reference's semantics (quantization.py:47-79).
+
+Every buffer keeps the reference layout: codes [n,m,R], per-read input scales
+[n,m*reads], packed weights [m,p,R,C] and per-read weight scales [m*reads,p,C],
+uint8 codes (int64 beyond 8 bits) and FP32 scales (FP64 when ``Config.wide``).
+"""
+
+import math
+
+import torch
+from torch.nn import functional as F
+
+from . import _lib
+
+
+def _code_dtype(config):
+    return torch.int64 if config.wide_codes else torch.uint8
+
+
+def _scale_dtype(config):
+    return torch.float64 if config.wide else torch.float32
+
+
+def _require_cuda(tensor, name):
+    if not tensor.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (memfast_b200 runs on the GPU only)")
+
+
+def _workspace(config, is_weight, rows, cols, device):
+    need = ct_size(config, is_weight, rows, cols)
+    return torch.empty(max(need, 1), dtype=torch.uint8, device=device), need
+
+
+def ct_size(config, is_weight, rows, cols):
+    import ctypes as ct
+
+    size = ct.c_size_t()
+    _lib.check(
+        _lib.load().mf_quantize_workspace(
+            ct.byref(_lib.native_config(config)), int(is_weight), rows, cols, ct.byref(size)
+        ),
+        "mf_quantize_workspace",
+    )
+    return size.value
+
+
+def read_starts(partitions, config, device):
+    physical = torch.arange(partitions, device=device)[:, None] * config.array_size[0]
+    reads = torch.arange(config.reads_per_array, device=device)[None] * config.read_rows
+    return (physical + reads).flatten()
+
+
+def check_read_scales(value, config, name):
+    """Each column has a single scale or zero point within one analog read."""
+    indices = torch.arange(value.shape[0], device=value.device)
+    physical_start = indices // config.array_size[0] * config.array_size[0]
+    read_offset = (indices % config.array_size[0]) // config.read_rows * config.read_rows
+    if not torch.equal(value, value[physical_start + read_offset]):
+        raise ValueError(f"{name} changes inside an ADC read; reduce rows_per_read")
+
+
+def expanded_parameter(value, shape, device, dtype, name, *, positive=False):
+    original = (
+        torch.as_tensor(value, device=device)
+        if torch.is_tensor(value)
+        else torch.as_tensor(value, device=device, dtype=torch.float64)
+    )
+    if original.is_complex() or not torch.isfinite(original).all():
+        raise ValueError(f"{name} must be real and finite")
+    if positive and (original < 0).any():
+        raise ValueError(f"{name} must be finite and nonnegative")
+    value = original.to(dtype)
+    try:
+        value = torch.broadcast_to(value, shape)
+    except RuntimeError:
+        raise ValueError(f"{name} must broadcast to {tuple(shape)}") from None
+    if not torch.isfinite(value).all() or (positive and (value < 0).any()):
+        raise ValueError(f"{name} must be finite" + (" and nonnegative" if positive else ""))
+    return value
+
+
+def _as_native_float(value, config, bits):
+    """The float operand the kernels read (FP16/BF16/FP32/FP64), checked finite in the
+    dtype grouped_quantize computes in (quantization.py:10-13)."""
+    if value.dtype not in _lib.DTYPES:
+        value = value.float()
+    compute = torch.float64 if bits > 8 or config.bw_e is not None else torch.float32
+    narrowed = value.dtype == torch.float64 and compute == torch.float32
+    if not torch.isfinite(value.to(compute) if narrowed else value).all():
+        raise ValueError(f"quantized values must be finite in {compute}")
+    return value
+
+
+def input_tiles(value, config, fixed_scale=None):
+    """[n, K] activations -> (codes [n, m, R], per-read scales [n, m*reads])."""
+    _require_cuda(value, "input")
+    n, k = value.shape
+    r = config.array_size[0]
+    m = math.ceil(k / r)
+    codes = torch.empty((n, m, r), dtype=_code_dtype(config), device=value.device)
+    xscale = torch.empty((n, m * config.reads_per_array), dtype=_scale_dtype(config), device=value.device)
+    if n == 0:
+        return codes, xscale
+    if fixed_scale is None:
+        value = _as_native_float(value, config, config.activation_bits)
+    else:
+        if not torch.isfinite(value).all():
+            raise ValueError("quantized values must be finite")
+        if value.dtype not in _lib.DTYPES:
+            value = value.float()
+        fixed_scale = fixed_scale.to(_scale_dtype(config)).reshape(-1).contiguous()
+        if fixed_scale.numel() != k:
+            fixed_scale = fixed_scale.expand(k).contiguous()
+    if value.stride(-1) != 1:
+        value = value.contiguous()
+    workspace, need = _workspace(config, False, n, k, value.device)
+    _lib.check(
+        _lib.load().mf_quantize_input(
+            _lib.native_config(config), _lib.ptr(value), _lib.DTYPES[value.dtype], n, k, value.stride(0),
+            _lib.ptr(fixed_scale), _lib.ptr(codes), _lib.ptr(xscale), _lib.ptr(workspace), need,
+            _lib.stream_of(value.device),
+        ),
+        "mf_quantize_input",
+    )
+    return codes, xscale
+
+
+def weight_tiles(weight, config):
+    """PyTorch-layout [O, K] floating weights -> (packed [m,p,R,C], weight_scale [m*reads,p,C])."""
+    _require_cuda(weight, "weight")
+    o, k = weight.shape
+    if not config.weight_signed and (weight < 0).any():
+        raise ValueError(
+            "unsigned floating weights must be nonnegative INT values; "
+            "use map_quantized with zero_points for affine weights"
+        )
+    weight = _as_native_float(weight, config, config.weight_bits)
+    if weight.stride(-1) != 1:
+        weight = weight.contiguous()
+    r, c = config.array_size
+    m, p = math.ceil(k / r), math.ceil(o / c)
+    packed = torch.empty((m, p, r, c), dtype=_code_dtype(config), device=weight.device)
+    wscale = torch.empty((m * config.reads_per_array, p, c), dtype=_scale_dtype(config), device=weight.device)
+    workspace, need = _workspace(config, True, o, k, weight.device)
+    _lib.check(
+        _lib.load().mf_program_weights(
+            _lib.native_config(config), _lib.ptr(weight), _lib.DTYPES[weight.dtype], o, k, weight.stride(0),
+            _lib.ptr(packed), _lib.ptr(wscale), _lib.ptr(workspace), need, _lib.stream_of(weight.device),
+        ),
+        "mf_program_weights",
+    )
+    return packed, wscale
+
+
+def pack_weight(code, scale, config):
+    """Pack logical [K,O] integer codes without estimating or changing their scales."""
+    k, o = code.shape
+    r, c = config.array_size
+    m, p = math.ceil(k / r), math.ceil(o / c)
+    scale = scale.to(_scale_dtype(config))
+    padded = F.pad(code, (0, p * c - o, 0, m * r - k))
+    packed = (padded & ((1 << config.weight_bits) - 1)).to(_code_dtype(config))
+    packed = packed.reshape(m, r, p, c).permute(0, 2, 1, 3).contiguous()
+    scales = F.pad(scale[None, None], (0, p * c - o, 0, m * r - k), mode="replicate")[0, 0]
+    scales = scales[read_starts(m, config, code.device)].reshape(m * config.reads_per_array, p, c)
+    return packed, scales.contiguous()
