@@ -38,12 +38,20 @@ def mm_cases():
 
 # Nonideal currents are real-valued FP32 dot products.  Summing them in another
 # order than the reference's CPU bmm flips an ADC rounding where a current sits
-# within an ulp of a count boundary.  Tolerance for such cases (stated once, used
-# by every parity test): at most 0.5% of output elements differ, by at most 1% of
-# the output range, and the mean signed error stays below 1e-4 of the range.
+# within an ulp of a count boundary, and one flip of the most significant slice
+# pair moves an output by |s_a s_w| * xs * ws (about 1% of the output range for
+# INT8 (1,1,2,2,2)).  Tolerance for such cases, stated once and used by every
+# parity test:
+#   - at most 0.5% of output elements differ;
+#   - no element differs by more than 5% of the output range (a few flips);
+#   - the RMS difference stays below 0.2% and the mean difference below 0.01%
+#     of the range;
+#   - the output distribution matches: mean within 0.1% of the std, std within 0.1%.
 MISMATCH_FRACTION = 5e-3
-MAX_ERROR_OF_RANGE = 1e-2
+MAX_ERROR_OF_RANGE = 5e-2
+RMS_ERROR_OF_RANGE = 2e-3
 MEAN_ERROR_OF_RANGE = 1e-4
+DISTRIBUTION_TOLERANCE = 1e-3
 
 
 def assert_close_nonideal(got, want, label=""):
@@ -52,9 +60,13 @@ def assert_close_nonideal(got, want, label=""):
     assert got.shape == want.shape, label
     scale = max(np.abs(want).max(), 1e-30)
     diff = got - want
-    assert np.mean(diff != 0) <= MISMATCH_FRACTION, (label, np.mean(diff != 0))
-    assert np.abs(diff).max() <= MAX_ERROR_OF_RANGE * scale, (label, np.abs(diff).max() / scale)
-    assert abs(diff.mean()) <= MEAN_ERROR_OF_RANGE * scale, (label, diff.mean() / scale)
+    assert np.mean(diff != 0) <= MISMATCH_FRACTION, (label, "mismatch fraction", np.mean(diff != 0))
+    assert np.abs(diff).max() <= MAX_ERROR_OF_RANGE * scale, (label, "max error", np.abs(diff).max() / scale)
+    assert np.sqrt(np.mean(diff**2)) <= RMS_ERROR_OF_RANGE * scale, (label, "rms", np.sqrt(np.mean(diff**2)) / scale)
+    assert abs(diff.mean()) <= MEAN_ERROR_OF_RANGE * scale, (label, "mean error", diff.mean() / scale)
+    std = max(want.std(), 1e-30)
+    assert abs(got.mean() - want.mean()) <= DISTRIBUTION_TOLERANCE * std, (label, "distribution mean")
+    assert abs(got.std() / std - 1) <= DISTRIBUTION_TOLERANCE, (label, "distribution std")
 
 
 def assert_parity(got, want, config, label=""):

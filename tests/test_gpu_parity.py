@@ -105,9 +105,14 @@ def test_nonideal_all_effects_vs_oracle(mf):
     g = torch.Generator().manual_seed(5)
     a, b = torch.randn(64, 512, generator=g), torch.randn(512, 384, generator=g)
     sim = mf.Simulator(config)
+    a_dev, b_dev = a.cuda(), b.cuda()
+    # The same RHS tensor keeps its program (name matrix.0) and advances its read event.
     for event in range(2):
-        got = sim.mm(a.cuda(), b.cuda()).cpu().numpy()
+        got = sim.mm(a_dev, b_dev).cpu().numpy()
         assert_parity(got, O.mm(a.numpy(), b.numpy(), config, event=event), config, f"event {event}")
+    # A new RHS tensor is a new program: next automatic name, read event 0 (simulator.py:111-171).
+    got = sim.mm(a_dev, b.cuda()).cpu().numpy()
+    assert_parity(got, O.mm(a.numpy(), b.numpy(), config, name="matrix.1"), config, "new rhs")
 
 
 def test_prefix_rows_are_exact_subsets(mf):
