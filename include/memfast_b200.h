@@ -145,6 +145,12 @@ mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedu
                                  int32_t m, int32_t p, int32_t tile_begin, int32_t tile_end,
                                  size_t* bytes);
 
+/* Reads and clears the library's device error word (a synchronising call).  A
+ * non-zero code means a bounded device-side wait gave up inside a kernel: the
+ * launch recorded the failure, released its resources and returned without
+ * finishing its outputs.  Returns MF_ERR_CUDA in that case, MF_OK otherwise. */
+mf_status mf_take_device_error(uint32_t* code);
+
 /* Resource admission for a schedule (replaces Simulator._admit, simulator.py:216-237,
  * and Program.resources, cuda.py:239-273).  MF_ERR_RESOURCE if it cannot run. */
 mf_status mf_query(const mf_config* cfg, const mf_schedule* schedule, int64_t n, int32_t m,

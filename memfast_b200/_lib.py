@@ -80,6 +80,7 @@ _SIGNATURES = {
     "mf_sliced_mm_workspace": (ct.c_int, [ct.POINTER(MFConfig), ct.POINTER(MFSchedule), ct.c_int64,
                                           ct.c_int32, ct.c_int32, ct.c_int32, ct.c_int32,
                                           ct.POINTER(ct.c_size_t)]),
+    "mf_take_device_error": (ct.c_int, [ct.POINTER(ct.c_uint32)]),
     "mf_query": (ct.c_int, [ct.POINTER(MFConfig), ct.POINTER(MFSchedule), ct.c_int64, ct.c_int32,
                             ct.c_int32, ct.POINTER(MFResources)]),
 }

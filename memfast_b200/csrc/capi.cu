@@ -145,8 +145,12 @@ mf_status mf_program_weights(const mf_config* cfg, const void* w, int32_t w_dtyp
 
 static bool use_ideal(const mf_config& c, const mf_schedule& s) {
     if (!c.ideal || !exact_integer_counts(c)) return false;
-    if (s.kernel == 1 || s.kernel == 0 || s.kernel == 2) return generic_ideal_fits(c, s);
-    return false;
+    return generic_ideal_fits(c, s);
+}
+
+// Kernel 2 (tcgen05) when requested or automatic and the configuration is in its plan.
+static bool use_tc(const mf_config& c, const mf_schedule& s, int32_t m, int32_t stable) {
+    return (s.kernel == 0 || s.kernel == 2) && !stable && tc_eligible(c, m);
 }
 
 static mf_schedule schedule_or_default(const mf_schedule* s) {
@@ -163,7 +167,8 @@ mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedu
         return MF_ERR_INVALID;
     }
     mf_schedule s = schedule_or_default(schedule);
-    *bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, tile_end - tile_begin);
+    if (use_tc(*cfg, s, m, 0)) *bytes = tc_workspace_bytes(*cfg, m, p);
+    else *bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, tile_end - tile_begin);
     return MF_OK;
 }
 
@@ -190,6 +195,7 @@ mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const 
     mf_schedule s = schedule_or_default(schedule);
     MMArgs a{codes, xscale, packed, wscale, bias, out, n, m, p, out_features, ldo, tile_begin, tile_end,
              seed, event, vector_offset, stable};
+    if (use_tc(*cfg, s, m, stable)) return tc_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
     if (use_ideal(*cfg, s)) return generic_ideal(*cfg, s, a, (cudaStream_t)stream);
     return physical(*cfg, s, a, workspace, workspace_bytes, (cudaStream_t)stream);
 }
@@ -204,8 +210,29 @@ mf_status mf_query(const mf_config* cfg, const mf_schedule* schedule, int64_t n,
     }
     mf_schedule s = schedule_or_default(schedule);
     memset(out, 0, sizeof(*out));
-    out->workspace_bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, p);
-    out->threads = 256;
+    if (use_tc(*cfg, s, m, 0)) {
+        out->workspace_bytes = tc_workspace_bytes(*cfg, m, p);
+        out->threads = 384;
+    } else {
+        out->workspace_bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, p);
+        out->threads = 256;
+    }
+    return MF_OK;
+}
+
+mf_status mf_take_device_error(uint32_t* code) {
+    if (!code) {
+        set_error("mf_take_device_error: NULL output");
+        return MF_ERR_INVALID;
+    }
+    unsigned value = 0;
+    mf_status st = tc_take_error(&value);
+    *code = value;
+    if (st) return st;
+    if (value) {
+        set_error("a device-side wait timed out (code %u); results of the affected launch are invalid", value);
+        return MF_ERR_CUDA;
+    }
     return MF_OK;
 }
 

@@ -50,4 +50,10 @@ size_t physical_workspace_bytes(const mf_config& c, const mf_schedule& s, int32_
 mf_status physical(const mf_config& c, const mf_schedule& s, const MMArgs& a, void* workspace,
                    size_t ws_bytes, cudaStream_t st);
 
+// tcgen05 / TMEM fast path (ideal INT8 configurations, tc_ideal.cu).
+bool tc_eligible(const mf_config& c, int32_t m);
+size_t tc_workspace_bytes(const mf_config& c, int32_t m, int32_t p);
+mf_status tc_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st);
+mf_status tc_take_error(unsigned* code);
+
 }  // namespace mf

@@ -45,7 +45,7 @@ from .quantization import (
 ResourceError = _lib.ResourceError
 
 _GRID_ARRAYS = (1, 2, 4, 8, 16, 32, 64)
-_GRID_KERNELS = (1,)
+_GRID_KERNELS = (1, 2)
 
 
 def default_schedule(config):
@@ -105,6 +105,12 @@ def restore_scales(value, input_scale, weight_scale):
     first = exponent.clamp(-1022, 1023)
     restored = torch.ldexp(torch.ldexp(mantissa, first), exponent - first)
     return torch.where(mantissa == 0, 0.0, restored)
+
+
+def check_device_error():
+    """Raise if a bounded device-side wait inside a kernel gave up (synchronises)."""
+    code = ct.c_uint32()
+    _lib.check(_lib.load().mf_take_device_error(ct.byref(code)), "device-side wait")
 
 
 def device_identity(device):
@@ -574,7 +580,9 @@ class AnalogMatrix(nn.Module):
             schedule = self._prepared[key]
         output = self._execute(q, xscale, schedule, event)
         output = output.reshape(*shape[:-1], self.out_features).to(x.dtype)
-        if not torch.isfinite(output).all():
+        finite = bool(torch.isfinite(output).all())
+        check_device_error()
+        if not finite:
             raise FloatingPointError("nonfinite analog output")
         self._event += 1
         return output

@@ -1,0 +1,124 @@
+"""The tcgen05/TMEM fast path against the generic engine and the oracle (needs a B200)."""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_parity
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def mf():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import memfast_b200
+
+    return memfast_b200
+
+
+def int8_config(mf, adc=(6, 7, 7, 8, 8), **kw):
+    base = dict(array_size=(128, 128), rows_per_read=32, weight_quant_gran=(32, 1), input_quant_gran=(1, 32),
+                input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2), adc_bits=adc,
+                nonidealities=mf.Nonidealities(write_variation=0.0))
+    base.update(kw)
+    return mf.Config(**base)
+
+
+def run(mf, config, a, b, kernel):
+    """One sliced product through the engine with an explicit kernel choice."""
+    from memfast_b200.quantization import input_tiles
+    from memfast_b200.simulator import check_device_error
+
+    sim = mf.Simulator(config)
+    matrix = sim.map(b.T.contiguous(), name="matrix.0")
+    q, xscale = input_tiles(a, config)
+    out = matrix._execute(q, xscale, dict(kernel=kernel, tile_n=32, tile_o=64, arrays=2), 0)
+    torch.cuda.synchronize()
+    check_device_error()
+    return out.cpu().numpy()
+
+
+def test_fast_path_is_selected_for_the_benchmark_config(mf):
+    import ctypes as ct
+
+    from memfast_b200 import _lib
+
+    config = int8_config(mf)
+    res = _lib.MFResources()
+    sched = _lib.schedule(kernel=0)
+    _lib.check(_lib.load().mf_query(_lib.native_config(config), ct.byref(sched), 4096, 32, 32, ct.byref(res)), "q")
+    assert res.threads == 384
+
+
+@pytest.mark.parametrize("shape", [(128, 128, 128), (1, 256, 128), (200, 384, 300), (333, 1024, 520),
+                                   (1024, 2048, 1024), (64, 8192, 256)])
+def test_tcgen05_bit_exact_vs_generic_random(mf, shape):
+    n, k, o = shape
+    g = torch.Generator().manual_seed(n * 7 + k + o)
+    a = torch.randn(n, k, generator=g).cuda()
+    b = torch.randn(k, o, generator=g).cuda()
+    config = int8_config(mf)
+    fast, slow = run(mf, config, a, b, 2), run(mf, config, a, b, 1)
+    assert np.array_equal(fast.view(np.uint32), slow.view(np.uint32)), np.mean(fast != slow)
+
+
+@pytest.mark.parametrize("adc", [(6, 7, 7, 8, 8), 7, (4, 5, 6, 7, 8), 8])
+def test_tcgen05_bit_exact_when_adcs_clip(mf, adc):
+    """Saturated inputs drive every digit to 3: every clip-capable pair clips, conditional pairs included."""
+    g = torch.Generator().manual_seed(11)
+    a = (1.0 + 0.02 * torch.rand(256, 512, generator=g)).cuda()
+    a[:, ::3] *= -1
+    b = (1.0 + 0.02 * torch.rand(512, 256, generator=g)).cuda()
+    b[::5] *= -1
+    b[:, 100:] = torch.randn(512, 156, generator=g).cuda()
+    config = int8_config(mf, adc=adc)
+    fast, slow = run(mf, config, a, b, 2), run(mf, config, a, b, 1)
+    assert np.array_equal(fast.view(np.uint32), slow.view(np.uint32)), np.mean(fast != slow)
+
+
+def test_tcgen05_vs_oracle_with_bias_and_unsigned_weights(mf):
+    from oracle import oracle as O
+
+    config = int8_config(mf, weight_signed=False, weight_slice=(2, 2, 2, 2))
+    g = torch.Generator().manual_seed(3)
+    a = torch.randn(96, 384, generator=g)
+    w = torch.rand(160, 384, generator=g) * 3
+    bias = torch.randn(160, generator=g)
+    lin = torch.nn.Linear(384, 160)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+        lin.bias.copy_(bias)
+    layer = mf.AnalogLinear(lin.cuda(), mf.Simulator(config), name="unsigned")
+    got = layer(a.cuda()).cpu().numpy()
+    want = O.linear(a.numpy(), w.numpy(), bias.numpy(), config, name="unsigned")
+    assert_parity(got, want, config, "unsigned linear")
+
+
+def test_tcgen05_column_shards_match_full_output(mf):
+    """Tiles [begin, end) of a sharded call equal the same columns of the full product."""
+    import ctypes as ct
+
+    from memfast_b200 import _lib
+    from memfast_b200.quantization import input_tiles
+
+    config = int8_config(mf)
+    g = torch.Generator().manual_seed(5)
+    a = torch.randn(256, 512, generator=g).cuda()
+    b = torch.randn(512, 640, generator=g).cuda()
+    sim = mf.Simulator(config)
+    matrix = sim.map(b.T.contiguous(), name="matrix.0")
+    q, xs = input_tiles(a, config)
+    full = matrix._execute(q, xs, dict(kernel=2, tile_n=32, tile_o=64, arrays=2), 0)
+    part = torch.zeros_like(full)
+    ws_bytes = matrix._workspace_size(256, dict(kernel=2, tile_n=32, tile_o=64, arrays=2))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    sched = _lib.schedule(kernel=2)
+    for begin, end in ((0, 2), (2, 5)):
+        _lib.check(_lib.load().mf_sliced_mm(
+            _lib.native_config(config), ct.byref(sched), _lib.ptr(q), _lib.ptr(xs), _lib.ptr(matrix.packed),
+            _lib.ptr(matrix.weight_scale), None, _lib.ptr(part), 256, matrix.packed.shape[0], matrix.p, 640, 640,
+            begin, end, matrix.seed, 0, 0, 0, _lib.ptr(ws), ws_bytes, _lib.stream_of(a.device)), "shard")
+    torch.cuda.synchronize()
+    assert torch.equal(full, part)
