@@ -44,15 +44,17 @@ namespace tc {
 constexpr int BM = 128;          // vectors per CTA (TMEM lanes)
 constexpr int BN = 128;          // output columns per CTA
 constexpr int SUB = 32;          // columns per MMA job
-constexpr int NSUB = BN / SUB;   // jobs per read
+constexpr int NSUB = BN / SUB;   // jobs per read; job j runs on TMEM half j & 1
 constexpr int KR = 32;           // rows per read (MMA K for 8-bit operands)
 constexpr int STAGES = 4;
-constexpr int RING = 8;          // per-read scale / flag ring
-constexpr int SLOTS = 16;        // TMEM slots of SUB columns (512 columns)
+constexpr int RING = 8;          // per-read flag ring
+constexpr int SCB = 4;           // reads per scale block
+constexpr int SCRING = 4;        // scale blocks in flight
 constexpr int MAXPA = 3;         // max clip-capable input-slice planes
 constexpr int MAXPB = 4;         // max clip-capable weight-slice planes
 constexpr int THREADS = 384;     // 12 warps
 constexpr int TILE = BM * KR;    // 4096 bytes: one [128 x 32] 8-bit tile
+constexpr int HALF_COLS = 256;   // TMEM columns per half
 
 // Shared memory plan (1024-aligned tiles first).
 struct Smem {
@@ -60,18 +62,18 @@ struct Smem {
     uint8_t w[STAGES][TILE];                        // TMA: weight codes, K-major [128 cols][32 B]
     uint8_t ap[STAGES][MAXPA][TILE];                // A digit planes
     uint8_t bp[STAGES][NSUB][MAXPB][SUB * KR];      // B digit planes [job][plane][32 rows][32 B]
-    float acc1[BN / 2][2][BM];                      // cascade level 1: [column pair][.][row]
-    float xs[RING][BM];
-    float ws[RING][BN];
+    float acc1[BN][BM];                             // cascade level 1, [column][row]
+    float xs[SCRING][BM][SCB];                      // TMA: input scales [row][read]
+    float ws[SCRING][SCB][BN];                      // TMA: weight scales [read][column]
     uint32_t flags[RING][2];                        // one word per transform warp
     uint64_t full[STAGES], ready[STAGES], empty[STAGES];
-    uint64_t ring_full[RING], ring_empty[RING];
-    uint64_t slot_full[SLOTS], slot_empty[SLOTS];
+    uint64_t flag_full[RING], flag_empty[RING];
+    uint64_t sc_full[SCRING], sc_empty[SCRING];
+    uint64_t unit_full[2], unit_empty[2];
     uint64_t drained;
     uint32_t tmem_base;
     int abort;
 };
-
 static_assert(sizeof(Smem) + 1024 <= 232448, "tcgen05 kernel exceeds the 227 KB shared-memory limit");
 
 struct Plan {
@@ -88,12 +90,10 @@ struct Plan {
 
 struct Args {
     Plan plan;
-    const float* xscale;    // [n, MR]
-    const float* wscale;    // [MR, p*C]
     const float* bias;      // [out_features] or null
     float* out;
     long long n, ldo;
-    int out_features, total_cols, MR;
+    int out_features, MR;
     long long full;         // reads in complete 16-read cascade blocks
     int col_begin;          // first output column of this call (tile_begin * C)
     int col_end;            // one past the last column (tile_end * C)
@@ -131,10 +131,9 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: ~2 s of clock64 at most, or until another role aborts the CTA.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Smem& s, unsigned* error,
-                                          unsigned code) {
-    if (mbar_try(bar, parity)) return true;
+// Bounded wait: about 2 s of clock64, or until another role aborted the CTA.
+__device__ __forceinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, Smem& s, unsigned* error,
+                                            unsigned code) {
     const long long start = clock64();
     while (true) {
         if (mbar_try(bar, parity)) return true;
@@ -144,7 +143,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Smem& 
             *(volatile int*)&s.abort = 1;
             return false;
         }
-        __nanosleep(64);
+        __nanosleep(32);
+    }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Smem& s, unsigned* error,
+                                          unsigned code) {
+    if (mbar_try(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, s, error, code);
+}
+
+// Bounded wait that ignores the abort flag (drains own work before exit).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    const long long start = clock64();
+    while (!mbar_try(bar, parity)) {
+        if (clock64() - start > 4000000000LL) return;
+        __nanosleep(256);
     }
 }
 
@@ -186,24 +200,45 @@ __host__ __device__ constexpr uint32_t idesc_e4m3(int n) {
            | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_i8(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+__device__ __forceinline__ void mma_i8(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc) {
+    asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, 0;" ::"r"(tmem), "l"(a), "l"(b), "r"(idesc));
 }
 
-__device__ __forceinline__ void mma_f8(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+__device__ __forceinline__ void mma_f8(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc) {
+    asm volatile("tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, 0;" ::"r"(tmem), "l"(a), "l"(b),
+                 "r"(idesc));
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      smem_u32(bar))
                  : "memory");
+}
+
+// 32 consecutive TMEM columns of this thread's lane.  The values are only valid
+// after tmem_wait(), which takes the registers as operands so that no use can be
+// scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(addr));
+}
+
+__device__ __forceinline__ void tmem_wait(uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.wait::ld.sync.aligned;"
+        : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+          "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+          "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+          "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+        :
+        : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&r)[16]) {
@@ -215,7 +250,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&r)[16]) {
         : "r"(addr));
 }
 
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait(uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.wait::ld.sync.aligned;"
+        : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+          "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+        :
+        : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -225,60 +268,50 @@ __device__ __forceinline__ float fma_sat(float a, float b, float c) {
     return d;
 }
 
-// d = a*b + c on two lanes at once.
-__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0, float c1) {
-    uint64_t a, b, c, d;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(c0), "f"(c1));
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
-}
+template <int N>
+__device__ __forceinline__ void set_maxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void set_maxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
 
-__device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-    uint64_t a, b, d;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
-}
-
-__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-    uint64_t a, b, d;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
-}
-
-// ------------------------------------------------------------- job geometry
-// A job is one (read, 32-column block).  Its TMEM groups, in order: the base
-// x.w accumulator (1 slot), one always-pair group per A plane (nwa slots), and
-// when the job is flagged one conditional group per A plane (nwc slots).  The
-// MMA issuer and the epilogue walk the same sequence, so TMEM slots are
-// assigned identically without communication.  A group that would wrap the
-// 16-slot ring starts at slot 0 instead; the skipped slots are passed through
-// (produced and consumed empty) so every slot completes one phase per lap.
-__device__ __forceinline__ uint32_t lap_parity(uint32_t pos) { return (pos / SLOTS) & 1u; }
-
-__device__ __forceinline__ bool job_flagged(const Plan& P, uint32_t f0, uint32_t f1, int j) {
+__device__ __forceinline__ bool job_flagged(int nwc, uint32_t f0, uint32_t f1, int j) {
     const uint32_t f = f0 | f1;
-    return P.nwc > 0 && (f & 1u) && (f & (2u << j));
+    return nwc > 0 && (f & 1u) && (f & (2u << j));
 }
 
-// Bounded wait that ignores the abort flag (drains own work before exit).
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-    const long long start = clock64();
-    while (!mbar_try(bar, parity)) {
-        if (clock64() - start > 4000000000LL) return;
-        __nanosleep(256);
+// T (32 columns) from the x.w accumulator: |x.w| < 2^22, so 1.5*2^23 + x.w holds the
+// integer exactly in its mantissa.
+__device__ __forceinline__ void base_to_float(const uint32_t (&v)[16], float2 (&T)[8]) {
+    const float2 magic = make_float2(-12582912.0f, -12582912.0f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+        T[e] = __fadd2_rn(make_float2(__int_as_float((int)v[2 * e] + 0x4B400000),
+                                      __int_as_float((int)v[2 * e + 1] + 0x4B400000)),
+                          magic);
+}
+
+// T -= s_a s_w relu(D - m) for one pair plane; D arrives as D * 2^-18.
+__device__ __forceinline__ void relu_correct(const uint32_t (&v)[16], float2 (&T)[8], float ds, float off, float cf) {
+    const float2 c2 = make_float2(cf, cf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const float y0 = fma_sat(__uint_as_float(v[2 * e]), ds, off);
+        const float y1 = fma_sat(__uint_as_float(v[2 * e + 1]), ds, off);
+        T[e] = __ffma2_rn(make_float2(y0, y1), c2, T[e]);
     }
 }
 
 // ------------------------------------------------------------------- kernel
+// NA / NWA / NWC: plan sizes (clip-capable input planes, always and conditional
+// weight planes).  A job's TMEM unit on its half: base x.w at column 0 (32 cols),
+// always group a at 32 + 64a (NWA x 32 cols); a conditional unit (flagged jobs
+// only) reuses the half with group a at 64a.
+template <int NA, int NWA, int NWC>
 __global__ void __launch_bounds__(THREADS, 1)
     tc_ideal_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                    const __grid_constant__ CUtensorMap map_xs, const __grid_constant__ CUtensorMap map_ws,
                     const Args args) {
+    static_assert(NA <= MAXPA && NWA + NWC <= MAXPB, "plan exceeds shared-memory planes");
+    static_assert(32 + NA * NWA * SUB <= HALF_COLS && NA * NWC * SUB <= HALF_COLS, "unit exceeds a TMEM half");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const Plan& P = args.plan;
@@ -295,21 +328,27 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&s.empty[i], 1);
         }
         for (int i = 0; i < RING; ++i) {
-            mbar_init(&s.ring_full[i], 2);
-            mbar_init(&s.ring_empty[i], 8);
+            mbar_init(&s.flag_full[i], 2);
+            mbar_init(&s.flag_empty[i], 8);
         }
-        for (int i = 0; i < SLOTS; ++i) {
-            mbar_init(&s.slot_full[i], 1);
-            mbar_init(&s.slot_empty[i], 8);
+        for (int i = 0; i < SCRING; ++i) {
+            mbar_init(&s.sc_full[i], 1);
+            mbar_init(&s.sc_empty[i], 8);
+        }
+        for (int h = 0; h < 2; ++h) {
+            mbar_init(&s.unit_full[h], 1);
+            mbar_init(&s.unit_empty[h], 4);
         }
         mbar_init(&s.drained, 1);
         s.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    for (int idx = threadIdx.x; idx < (BN / 2) * 2 * BM; idx += THREADS) (&s.acc1[0][0][0])[idx] = 0.0f;
+    for (int idx = threadIdx.x; idx < BN * BM; idx += THREADS) (&s.acc1[0][0])[idx] = 0.0f;
     if (warp == 0 && lane == 0) {
         prefetch_map(&map_x);
         prefetch_map(&map_w);
+        prefetch_map(&map_xs);
+        prefetch_map(&map_ws);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s.tmem_base)),
@@ -321,252 +360,264 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ producer
-        if (lane == 0) {
-            int issued = 0;
-            for (int i = 0; i < MR; ++i) {
-                const int st = i % STAGES;
-                if (!mbar_wait(&s.empty[st], ((i / STAGES) & 1) ^ 1, s, err, 1)) break;
-                mbar_expect_tx(&s.full[st], 2 * TILE);
-                tma_load_2d(s.x[st], &map_x, i * KR, (int)n0, &s.full[st]);
-                tma_load_2d(s.w[st], &map_w, i * KR, c0, &s.full[st]);
-                issued = i + 1;
-            }
-            // Every issued load lands before the CTA may exit.
-            for (int i = issued - STAGES > 0 ? issued - STAGES : 0; i < issued; ++i)
-                mbar_drain(&s.full[i % STAGES], (i / STAGES) & 1);
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            uint32_t pos = 0;
-            const uint32_t id_base = idesc_i8(SUB, P.b_signed != 0);
-            const uint32_t id_always = idesc_e4m3(SUB * (P.nwa > 0 ? P.nwa : 1));
-            const uint32_t id_cond = idesc_e4m3(SUB * (P.nwc > 0 ? P.nwc : 1));
-            bool ok = true;
-            for (int i = 0; i < MR && ok; ++i) {
-                const int st = i % STAGES;
-                if (!mbar_wait(&s.ready[st], (i / STAGES) & 1, s, err, 2)) break;
-                tc_fence_after();
-                const uint32_t f0 = *(volatile uint32_t*)&s.flags[i % RING][0];
-                const uint32_t f1 = *(volatile uint32_t*)&s.flags[i % RING][1];
-                const uint64_t dx = desc_sw32(s.x[st]);
-                for (int j = 0; j < NSUB && ok; ++j) {
-                    const int groups = 1 + P.na + (job_flagged(P, f0, f1, j) ? P.na : 0);
-                    for (int g = 0; g < groups && ok; ++g) {
-                        const int size = g == 0 ? 1 : (g <= P.na ? P.nwa : P.nwc);
-                        if ((pos % SLOTS) + size > SLOTS) {
-                            while (pos % SLOTS) {   // pass the lap's tail slots through
-                                const uint32_t q = pos % SLOTS;
-                                if (!mbar_wait(&s.slot_empty[q], lap_parity(pos) ^ 1, s, err, 3)) { ok = false; break; }
-                                mbar_arrive(&s.slot_full[q]);
-                                ++pos;
-                            }
-                            if (!ok) break;
-                        }
-                        const uint32_t first = pos % SLOTS;
-                        for (int k = 0; k < size && ok; ++k)
-                            if (!mbar_wait(&s.slot_empty[first + k], lap_parity(pos + k) ^ 1, s, err, 4)) ok = false;
-                        if (!ok) break;
-                        tc_fence_after();
-                        const uint32_t dst = tmem + first * SUB;
-                        if (g == 0) {
-                            mma_i8(dst, dx, desc_sw32(s.w[st] + j * SUB * KR), id_base, 0);
-                        } else if (g <= P.na) {
-                            mma_f8(dst, desc_sw32(s.ap[st][g - 1]), desc_sw32(s.bp[st][j][0]), id_always, 0);
-                        } else {
-                            mma_f8(dst, desc_sw32(s.ap[st][g - 1 - P.na]), desc_sw32(s.bp[st][j][P.nwa]), id_cond, 0);
-                        }
-                        mma_commit(&s.slot_full[first]);
-                        for (int k = 1; k < size; ++k) mbar_arrive(&s.slot_full[first + k]);
-                        pos += size;
-                    }
-                }
-                if (ok) mma_commit(&s.empty[st]);
-            }
-            // All issued MMAs complete before TMEM is released.
-            mma_commit(&s.drained);
-            mbar_drain(&s.drained, 0);
-        }
-    } else if (warp < 4) {
-        // ------------------------------------------------------------ transform
-        const int tw = warp - 2;                  // 0 or 1
-        for (int i = 0; i < MR; ++i) {
-            const int st = i % STAGES, rs = i % RING;
-            bool ok = mbar_wait(&s.full[st], (i / STAGES) & 1, s, err, 5);
-            ok = ok && mbar_wait(&s.ring_empty[rs], ((i / RING) & 1) ^ 1, s, err, 6);
-            if (!__all_sync(0xFFFFFFFFu, ok)) break;
-            uint32_t word = 0;
-            for (int h = 0; h < 2; ++h) {
-                const int t = tw * 32 + lane + 64 * h;    // A row t and B column t (0..127)
-                // Row t of a [128 x 32] SW32 tile: its two 16-byte chunks stay inside the row,
-                // so an elementwise transform keeps the swizzle when written at the same offsets.
-                const uint4* xrow = reinterpret_cast<const uint4*>(s.x[st] + t * KR);
-                const uint4 xa = xrow[0], xb = xrow[1];
-                const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-                uint32_t rowmax = 0;
-                for (int a = 0; a < P.na; ++a) {
-                    const uint32_t m4 = (uint32_t)P.a_mask[a] * 0x01010101u;
-                    uint32_t d[8], sum = 0;
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        d[k] = (xw[k] >> P.a_shift[a]) & m4;
-                        sum = __dp4a(d[k], 0x01010101u, sum);
-                    }
-                    uint4* dst = reinterpret_cast<uint4*>(s.ap[st][a] + t * KR);
-                    dst[0] = make_uint4(d[0], d[1], d[2], d[3]);
-                    dst[1] = make_uint4(d[4], d[5], d[6], d[7]);
-                    rowmax = sum > rowmax ? sum : rowmax;
-                }
-                const uint4* wrow = reinterpret_cast<const uint4*>(s.w[st] + t * KR);
-                const uint4 wa = wrow[0], wb = wrow[1];
-                const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-                bool colflag = false;
-                for (int q = 0; q < P.nwa + P.nwc; ++q) {
-                    const uint32_t m4 = (uint32_t)P.w_mask[q] * 0x01010101u;
-                    uint32_t d[8], sum = 0;
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        d[k] = (ww[k] >> P.w_shift[q]) & m4;
-                        sum = __dp4a(d[k], 0x01010101u, sum);
-                    }
-                    uint4* dst = reinterpret_cast<uint4*>(s.bp[st][t >> 5][q] + (t & 31) * KR);
-                    dst[0] = make_uint4(d[0], d[1], d[2], d[3]);
-                    dst[1] = make_uint4(d[4], d[5], d[6], d[7]);
-                    if (q >= P.nwa && (int)sum > P.col_limit[q]) colflag = true;
-                }
-                const long long row = n0 + t;
-                s.xs[rs][t] = row < args.n ? args.xscale[row * MR + i] : 0.0f;
-                const int col = c0 + t;
-                s.ws[rs][t] = col < args.col_end ? args.wscale[(long long)i * args.total_cols + col] : 0.0f;
-                const bool rowflag = P.nwc > 0 && (int)rowmax > P.row_limit && row < args.n;
-                if (__any_sync(0xFFFFFFFFu, rowflag)) word |= 1u;
-                if (__any_sync(0xFFFFFFFFu, colflag)) word |= 2u << (t >> 5);
-            }
-            if (lane == 0) s.flags[rs][tw] = word;
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
+    if (warp < 4) {
+        set_maxnreg_dec<96>();
+        if (warp == 0) {
+            // -------------------------------------------------------- producer
             if (lane == 0) {
-                mbar_arrive(&s.ready[st]);
-                mbar_arrive(&s.ring_full[rs]);
+                int issued = 0, scissued = 0;
+                for (int i = 0; i < MR; ++i) {
+                    if (i % SCB == 0) {
+                        const int b = i / SCB, sb = b % SCRING;
+                        if (!mbar_wait(&s.sc_empty[sb], ((b / SCRING) & 1) ^ 1, s, err, 12)) break;
+                        mbar_expect_tx(&s.sc_full[sb], (BM + BN) * SCB * 4);
+                        tma_load_2d(s.xs[sb], &map_xs, i, (int)n0, &s.sc_full[sb]);
+                        tma_load_2d(s.ws[sb], &map_ws, c0, i, &s.sc_full[sb]);
+                        scissued = b + 1;
+                    }
+                    const int st = i % STAGES;
+                    if (!mbar_wait(&s.empty[st], ((i / STAGES) & 1) ^ 1, s, err, 1)) break;
+                    mbar_expect_tx(&s.full[st], 2 * TILE);
+                    tma_load_2d(s.x[st], &map_x, i * KR, (int)n0, &s.full[st]);
+                    tma_load_2d(s.w[st], &map_w, i * KR, c0, &s.full[st]);
+                    issued = i + 1;
+                }
+                // Every issued load lands before the CTA may exit.
+                for (int i = issued - STAGES > 0 ? issued - STAGES : 0; i < issued; ++i)
+                    mbar_drain(&s.full[i % STAGES], (i / STAGES) & 1);
+                for (int b = scissued - SCRING > 0 ? scissued - SCRING : 0; b < scissued; ++b)
+                    mbar_drain(&s.sc_full[b % SCRING], (b / SCRING) & 1);
+            }
+        } else if (warp == 1) {
+            // -------------------------------------------------------- MMA issuer
+            if (lane == 0) {
+                const uint32_t id_base = idesc_i8(SUB, P.b_signed != 0);
+                const uint32_t id_always = idesc_e4m3(SUB * (NWA > 0 ? NWA : 1));
+                const uint32_t id_cond = idesc_e4m3(SUB * (NWC > 0 ? NWC : 1));
+                uint32_t units[2] = {0, 0};
+                bool ok = true;
+                for (int i = 0; i < MR && ok; ++i) {
+                    const int st = i % STAGES;
+                    if (!mbar_wait(&s.ready[st], (i / STAGES) & 1, s, err, 2)) break;
+                    tc_fence_after();
+                    const uint32_t f0 = *(volatile uint32_t*)&s.flags[i % RING][0];
+                    const uint32_t f1 = *(volatile uint32_t*)&s.flags[i % RING][1];
+                    const uint64_t dx = desc_sw32(s.x[st]);
+#pragma unroll
+                    for (int j = 0; j < NSUB; ++j) {
+                        const int h = j & 1;
+                        const uint32_t half = tmem + h * HALF_COLS;
+                        if (!mbar_wait(&s.unit_empty[h], (units[h] & 1) ^ 1, s, err, 3)) { ok = false; break; }
+                        tc_fence_after();
+                        mma_i8(half, dx, desc_sw32(s.w[st] + j * SUB * KR), id_base);
+#pragma unroll
+                        for (int a = 0; a < NA; ++a)
+                            mma_f8(half + 32 + a * NWA * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][0]),
+                                   id_always);
+                        mma_commit(&s.unit_full[h]);
+                        ++units[h];
+                        if (NWC > 0 && job_flagged(NWC, f0, f1, j)) {
+                            if (!mbar_wait(&s.unit_empty[h], (units[h] & 1) ^ 1, s, err, 4)) { ok = false; break; }
+                            tc_fence_after();
+#pragma unroll
+                            for (int a = 0; a < NA; ++a)
+                                mma_f8(half + a * NWC * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][NWA]),
+                                       id_cond);
+                            mma_commit(&s.unit_full[h]);
+                            ++units[h];
+                        }
+                    }
+                    if (ok) mma_commit(&s.empty[st]);
+                }
+                // All issued MMAs complete before TMEM is released.
+                mma_commit(&s.drained);
+                mbar_drain(&s.drained, 0);
+            }
+        } else {
+            // -------------------------------------------------------- transform
+            const int tw = warp - 2;              // 0 or 1
+            for (int i = 0; i < MR; ++i) {
+                const int st = i % STAGES, rs = i % RING;
+                bool ok = mbar_wait(&s.full[st], (i / STAGES) & 1, s, err, 5);
+                ok = ok && mbar_wait(&s.flag_empty[rs], ((i / RING) & 1) ^ 1, s, err, 6);
+                if (!__all_sync(0xFFFFFFFFu, ok)) break;
+                uint32_t word = 0;
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int t = tw * 32 + lane + 64 * hh;   // A row t and B column t (0..127)
+                    // Row t of a [128 x 32] SW32 tile keeps both 16-byte chunks inside the
+                    // row, so an elementwise transform written at the same offsets stays swizzled.
+                    const uint4* xrow = reinterpret_cast<const uint4*>(s.x[st] + t * KR);
+                    const uint4 xa = xrow[0], xb = xrow[1];
+                    const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+                    uint32_t rowmax = 0;
+#pragma unroll
+                    for (int a = 0; a < NA; ++a) {
+                        const uint32_t m4 = (uint32_t)P.a_mask[a] * 0x01010101u;
+                        uint32_t d[8], sum = 0;
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            d[k] = (xw[k] >> P.a_shift[a]) & m4;
+                            if (NWC > 0) sum = __dp4a(d[k], 0x01010101u, sum);
+                        }
+                        uint4* dst = reinterpret_cast<uint4*>(s.ap[st][a] + t * KR);
+                        dst[0] = make_uint4(d[0], d[1], d[2], d[3]);
+                        dst[1] = make_uint4(d[4], d[5], d[6], d[7]);
+                        rowmax = sum > rowmax ? sum : rowmax;
+                    }
+                    const uint4* wrow = reinterpret_cast<const uint4*>(s.w[st] + t * KR);
+                    const uint4 wa = wrow[0], wb = wrow[1];
+                    const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                    bool colflag = false;
+#pragma unroll
+                    for (int q = 0; q < NWA + NWC; ++q) {
+                        const uint32_t m4 = (uint32_t)P.w_mask[q] * 0x01010101u;
+                        uint32_t d[8], sum = 0;
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            d[k] = (ww[k] >> P.w_shift[q]) & m4;
+                            if (q >= NWA) sum = __dp4a(d[k], 0x01010101u, sum);
+                        }
+                        uint4* dst = reinterpret_cast<uint4*>(s.bp[st][t >> 5][q] + (t & 31) * KR);
+                        dst[0] = make_uint4(d[0], d[1], d[2], d[3]);
+                        dst[1] = make_uint4(d[4], d[5], d[6], d[7]);
+                        if (q >= NWA && (int)sum > P.col_limit[q]) colflag = true;
+                    }
+                    const bool rowflag = NWC > 0 && (int)rowmax > P.row_limit && n0 + t < args.n;
+                    if (__any_sync(0xFFFFFFFFu, rowflag)) word |= 1u;
+                    if (__any_sync(0xFFFFFFFFu, colflag)) word |= 2u << (t >> 5);
+                }
+                if (lane == 0) s.flags[rs][tw] = word;
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&s.ready[st]);
+                    mbar_arrive(&s.flag_full[rs]);
+                }
             }
         }
     } else {
+        set_maxnreg_inc<208>();
         // ------------------------------------------------------------ epilogue
+        const int h = (warp - 4) >> 2;              // TMEM half = job parity owned by this warpgroup
         const int quad = warp & 3;                  // TMEM lane quadrant of this warp
-        const int half = (warp - 4) >> 2;           // columns [16*half, 16*half+16) of each job
         const int r = quad * 32 + lane;             // CTA row = TMEM lane
         const long long row = n0 + r;
-        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-        float acc0[NSUB][16];
+        const uint32_t half = tmem + ((uint32_t)(quad * 32) << 16) + h * HALF_COLS;
+        float2 acc0[2][16];                         // jobs h and h + 2, 32 columns each
 #pragma unroll
-        for (int j = 0; j < NSUB; ++j)
+        for (int jj = 0; jj < 2; ++jj)
 #pragma unroll
-            for (int e = 0; e < 16; ++e) acc0[j][e] = 0.0f;
-        uint32_t pos = 0;
+            for (int e = 0; e < 16; ++e) acc0[jj][e] = make_float2(0.0f, 0.0f);
+        uint32_t units = 0;
         bool ok = true;
         for (int i = 0; i < MR && ok; ++i) {
-            const int rs = i % RING;
-            ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.ring_full[rs], (i / RING) & 1, s, err, 7));
+            const int rs = i % RING, b = i / SCB, sb = b % SCRING;
+            if (i % SCB == 0) {
+                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.sc_full[sb], (b / SCRING) & 1, s, err, 13));
+                if (!ok) break;
+            }
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.flag_full[rs], (i / RING) & 1, s, err, 7));
             if (!ok) break;
-            const float xs = s.xs[rs][r];
+            const float xs = s.xs[sb][r][i % SCB];
+            const float2 xs2 = make_float2(xs, xs);
             const uint32_t f0 = *(volatile uint32_t*)&s.flags[rs][0];
             const uint32_t f1 = *(volatile uint32_t*)&s.flags[rs][1];
 #pragma unroll
-            for (int j = 0; j < NSUB; ++j) {
-                const int groups = 1 + P.na + (job_flagged(P, f0, f1, j) ? P.na : 0);
-                float T[16];
-                for (int g = 0; g < groups && ok; ++g) {
-                    const int size = g == 0 ? 1 : (g <= P.na ? P.nwa : P.nwc);
-                    if ((pos % SLOTS) + size > SLOTS) {
-                        while (pos % SLOTS) {
-                            const uint32_t q = pos % SLOTS;
-                            ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.slot_full[q], lap_parity(pos), s, err, 8));
-                            if (!ok) break;
-                            if (lane == 0) mbar_arrive(&s.slot_empty[q]);
-                            ++pos;
+            for (int jj = 0; jj < 2; ++jj) {
+                const int j = h + 2 * jj;
+                const bool flagged = NWC > 0 && job_flagged(NWC, f0, f1, j);
+                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[h], units & 1, s, err, 9));
+                if (!ok) break;
+                tc_fence_after();
+                float2 T[2][8];
+                // Two 16-column halves; TMEM loads double-buffered behind the math.
+#pragma unroll
+                for (int ch = 0; ch < 2; ++ch) {
+                    uint32_t va[16], vb[16];
+                    const uint32_t col = half + ch * 16;
+                    tmem_ld16(col, va);
+                    tmem_wait(va);
+                    if (NA * NWA > 0) tmem_ld16(col + 32, vb);
+                    base_to_float(va, T[ch]);
+#pragma unroll
+                    for (int k = 0; k < NA * NWA; ++k) {
+                        const int a = k / (NWA > 0 ? NWA : 1), q = k % (NWA > 0 ? NWA : 1);
+                        if (k & 1) {
+                            tmem_wait(va);
+                            if (k + 1 < NA * NWA) tmem_ld16(col + 32 + (k + 1) * SUB, vb);
+                            relu_correct(va, T[ch], P.dscale[q], P.offset[q], P.coef[a][q]);
+                        } else {
+                            tmem_wait(vb);
+                            if (k + 1 < NA * NWA) tmem_ld16(col + 32 + (k + 1) * SUB, va);
+                            relu_correct(vb, T[ch], P.dscale[q], P.offset[q], P.coef[a][q]);
                         }
-                        if (!ok) break;
                     }
-                    const uint32_t first = pos % SLOTS;
-                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.slot_full[first], lap_parity(pos), s, err, 9));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s.unit_empty[h]);
+                ++units;
+                if (flagged) {
+                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[h], units & 1, s, err, 10));
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t base = tmem + lane_addr + first * SUB + half * 16;
-                    if (g == 0) {
-                        uint32_t v[16];
-                        tmem_ld16(base, v);
-                        tmem_wait_ld();
-                        // |x.w| < 2^22: the integer is exact in the mantissa of 1.5*2^23 + x.w.
 #pragma unroll
-                        for (int e = 0; e < 16; e += 2)
-                            add2(T[e], T[e + 1], __int_as_float((int)v[e] + 0x4B400000),
-                                 __int_as_float((int)v[e + 1] + 0x4B400000), -12582912.0f, -12582912.0f);
-                    } else {
-                        const int a = g <= P.na ? g - 1 : g - 1 - P.na;
-                        const int wbase = g <= P.na ? 0 : P.nwa;
-                        for (int k = 0; k < size; ++k) {
-                            const int q = wbase + k;
-                            uint32_t v[16];
-                            tmem_ld16(base + k * SUB, v);
-                            tmem_wait_ld();
-                            const float ds = P.dscale[q], off = P.offset[q], cf = P.coef[a][q];
+                    for (int ch = 0; ch < 2; ++ch)
 #pragma unroll
-                            for (int e = 0; e < 16; e += 2) {
-                                const float y0 = fma_sat(__uint_as_float(v[e]), ds, off);
-                                const float y1 = fma_sat(__uint_as_float(v[e + 1]), ds, off);
-                                fma2(T[e], T[e + 1], y0, y1, cf, cf, T[e], T[e + 1]);
-                            }
+                        for (int k = 0; k < NA * NWC; ++k) {
+                            const int a = k / (NWC > 0 ? NWC : 1), q = NWA + k % (NWC > 0 ? NWC : 1);
+                            uint32_t va[16];
+                            tmem_ld16(half + ch * 16 + k * SUB, va);
+                            tmem_wait(va);
+                            relu_correct(va, T[ch], P.dscale[q], P.offset[q], P.coef[a][q]);
                         }
-                    }
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0)
-                        for (int k = 0; k < size; ++k) mbar_arrive(&s.slot_empty[first + k]);
-                    pos += size;
+                    if (lane == 0) mbar_arrive(&s.unit_empty[h]);
+                    ++units;
                 }
-                if (!ok) break;
                 // fl(fl(T * xs) * ws) pushed into cascade level 0 for read i.
-                const float* wsr = &s.ws[rs][j * SUB + half * 16];
+                const float2* wsr = reinterpret_cast<const float2*>(&s.ws[sb][i % SCB][j * SUB]);
 #pragma unroll
-                for (int e = 0; e < 16; e += 2) {
-                    float v0, v1;
-                    mul2(v0, v1, T[e], T[e + 1], xs, xs);
-                    mul2(v0, v1, v0, v1, wsr[e], wsr[e + 1]);
-                    add2(acc0[j][e], acc0[j][e + 1], acc0[j][e], acc0[j][e + 1], v0, v1);
-                }
+                for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        acc0[jj][ch * 8 + e] =
+                            __fadd2_rn(acc0[jj][ch * 8 + e], __fmul2_rn(__fmul2_rn(T[ch][e], xs2), wsr[ch * 8 + e]));
             }
             if (!ok) break;
             __syncwarp();
-            if (lane == 0) mbar_arrive(&s.ring_empty[rs]);
-            // Block boundary of the 16-read cascade: level 1 += level 0 (MR <= 256 needs two levels).
+            if (lane == 0) {
+                mbar_arrive(&s.flag_empty[rs]);
+                if (i % SCB == SCB - 1 || i == MR - 1) mbar_arrive(&s.sc_empty[sb]);
+            }
+            // Block boundary of the 16-read cascade: level 1 += level 0 (MR <= 256 keeps two levels).
             const int done = i + 1;
             if (done <= args.full && (done & 15) == 0) {
 #pragma unroll
-                for (int j = 0; j < NSUB; ++j)
+                for (int jj = 0; jj < 2; ++jj)
 #pragma unroll
-                    for (int e = 0; e < 16; e += 2) {
-                        const int cp = (j * SUB + half * 16 + e) >> 1;
-                        float a0 = s.acc1[cp][0][r], a1 = s.acc1[cp][1][r];
-                        add2(a0, a1, a0, a1, acc0[j][e], acc0[j][e + 1]);
-                        s.acc1[cp][0][r] = a0;
-                        s.acc1[cp][1][r] = a1;
-                        acc0[j][e] = acc0[j][e + 1] = 0.0f;
+                    for (int e = 0; e < 16; ++e) {
+                        const int cl = (h + 2 * jj) * SUB + 2 * e;
+                        s.acc1[cl][r] = __fadd_rn(s.acc1[cl][r], acc0[jj][e].x);
+                        s.acc1[cl + 1][r] = __fadd_rn(s.acc1[cl + 1][r], acc0[jj][e].y);
+                        acc0[jj][e] = make_float2(0.0f, 0.0f);
                     }
             }
         }
         if (ok && row < args.n) {
 #pragma unroll
-            for (int j = 0; j < NSUB; ++j)
+            for (int jj = 0; jj < 2; ++jj)
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int cl = j * SUB + half * 16 + e;
+                for (int e = 0; e < 32; ++e) {
+                    const int cl = (h + 2 * jj) * SUB + e;
                     const int col = c0 + cl;
                     if (col >= args.col_end || col >= args.out_features) continue;
-                    // acc0 + acc1 + acc2 + acc3 (the upper levels are zero), then the
-                    // reference's store into a zero-filled output.
-                    float value = __fadd_rn(acc0[j][e], s.acc1[cl >> 1][cl & 1][r]);
+                    const float a0 = (e & 1) ? acc0[jj][e >> 1].y : acc0[jj][e >> 1].x;
+                    // acc0 + acc1 + acc2 + acc3 (upper levels zero), then the reference's
+                    // store into a zero-filled output.
+                    float value = __fadd_rn(a0, s.acc1[cl][r]);
                     value = __fadd_rn(value, 0.0f);
                     value = __fadd_rn(value, 0.0f);
                     value = __fadd_rn(0.0f, value);
@@ -625,19 +676,26 @@ EncodeTiled encoder() {
     return fn;
 }
 
-mf_status make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer) {
+// 2D tiled tensor map: `inner` x `outer` elements of `bytes` each, row stride
+// `stride` elements, box `box_inner` x `box_outer`.
+mf_status make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int bytes, uint64_t inner,
+                   uint64_t outer, uint64_t stride, uint32_t box_inner, uint32_t box_outer,
+                   CUtensorMapSwizzle swizzle) {
     EncodeTiled fn = encoder();
     if (!fn) {
         set_error("cuTensorMapEncodeTiled unavailable");
         return MF_ERR_CUDA;
     }
+    if (((uintptr_t)base & 15) || (stride * bytes) % 16) {
+        set_error("tensor map needs 16-byte aligned base and row stride");
+        return MF_ERR_INVALID;
+    }
     const cuuint64_t dims[2] = {inner, outer};
-    const cuuint64_t strides[1] = {inner};
-    const cuuint32_t box[2] = {tc::KR, tc::BM};
+    const cuuint64_t strides[1] = {stride * bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
     const cuuint32_t elem[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
         return MF_ERR_CUDA;
@@ -721,6 +779,13 @@ bool tc_plan(const mf_config& c, tc::Plan& P) {
     return true;
 }
 
+// Plan shapes with a compiled kernel: (NA, NWA, NWC).
+static bool tc_shape_supported(int na, int nwa, int nwc) {
+    return (na == 3 && nwa == 2 && nwc == 2) ||
+           (na == 3 && nwa == 2 && nwc == 0) || (na == 3 && nwa == 1 && nwc == 0) ||
+           (na == 3 && nwa == 1 && nwc == 2) || (na == 0 && nwa == 0 && nwc == 0);
+}
+
 bool tc_eligible(const mf_config& c, int32_t m) {
     if (!c.ideal || !exact_integer_counts(c) || c.wide || c.wide_codes) return false;
     if (c.activation_bits != 8 || c.weight_bits != 8) return false;
@@ -729,14 +794,28 @@ bool tc_eligible(const mf_config& c, int32_t m) {
         if (c.in_mask[i] > 7) return false;
     for (int i = 0; i < c.n_w; ++i)
         if (c.w_mask[i] > 7) return false;
-    if ((long long)m * c.reads > 256) return false;
+    const long long MR = (long long)m * c.reads;
+    if (MR > 256 || MR % tc::SCB) return false;
     if (reconstruction_bound(c) >= 16777216.0) return false;
     tc::Plan P;
-    return tc_plan(c, P);
+    if (!tc_plan(c, P)) return false;
+    return tc_shape_supported(P.na, P.nwa, P.nwc);
 }
 
 size_t tc_workspace_bytes(const mf_config& c, int32_t m, int32_t p) {
     return (size_t)p * c.cols * m * c.rows + 256;
+}
+
+template <int NA, int NWA, int NWC>
+static mf_status launch_tc(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mxs,
+                           const CUtensorMap& mws, const tc::Args& args, dim3 grid, cudaStream_t st) {
+    const size_t smem = sizeof(tc::Smem) + 1024;
+    auto kern = tc::tc_ideal_kernel<NA, NWA, NWC>;
+    MF_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                  "tc smem attribute");
+    kern<<<grid, tc::THREADS, smem, st>>>(mx, mw, mxs, mws, args);
+    MF_LAUNCH_CHECK("tc_ideal_kernel");
+    return MF_OK;
 }
 
 mf_status tc_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st) {
@@ -754,46 +833,55 @@ mf_status tc_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, siz
         return MF_ERR_RESOURCE;
     }
     tc::Args args{};
-    if (!tc_plan(c, args.plan)) {
+    if (!tc_plan(c, args.plan) || !tc_shape_supported(args.plan.na, args.plan.nwa, args.plan.nwc)) {
         set_error("configuration outside the tcgen05 plan");
         return MF_ERR_UNSUPPORTED;
     }
     args.plan.b_signed = c.weight_signed;
     const long long K = (long long)a.m * c.rows;
     const long long O = (long long)a.p * c.cols;
+    const int MR = a.m * c.reads;
     uint8_t* wk = static_cast<uint8_t*>(workspace);
     dim3 tgrid((unsigned)((K + 31) / 32), (unsigned)((O + 31) / 32));
     weights_kmajor_kernel<<<tgrid, dim3(32, 8), 0, st>>>(static_cast<const uint8_t*>(a.packed), wk, a.m, a.p,
                                                           c.rows, c.cols);
     MF_LAUNCH_CHECK("weights_kmajor_kernel");
-    CUtensorMap mx, mw;
-    mf_status s1 = make_map(&mx, a.codes, (uint64_t)K, (uint64_t)a.n);
-    if (s1) return s1;
-    s1 = make_map(&mw, wk, (uint64_t)K, (uint64_t)O);
-    if (s1) return s1;
+    CUtensorMap mx, mw, mxs, mws;
+    mf_status r = make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n, (uint64_t)K,
+                           tc::KR, tc::BM, CU_TENSOR_MAP_SWIZZLE_32B);
+    if (!r) r = make_map(&mw, wk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)O, (uint64_t)K, tc::KR,
+                         tc::BN, CU_TENSOR_MAP_SWIZZLE_32B);
+    // Scales: xscale [n, MR] -> boxes [128 rows][4 reads]; wscale [MR, O] -> [4 reads][128 cols].
+    if (!r) r = make_map(&mxs, a.xscale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)MR, (uint64_t)a.n,
+                         (uint64_t)MR, tc::SCB, tc::BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!r) r = make_map(&mws, a.wscale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)O, (uint64_t)MR, (uint64_t)O,
+                         tc::BN, tc::SCB, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (r) return r;
     unsigned* err = nullptr;
     MF_CHECK_CUDA(cudaGetSymbolAddress((void**)&err, g_tc_error), "error symbol");
-    args.xscale = static_cast<const float*>(a.xscale);
-    args.wscale = static_cast<const float*>(a.wscale);
     args.bias = static_cast<const float*>(a.bias);
     args.out = static_cast<float*>(a.out);
     args.n = a.n;
     args.ldo = a.ldo;
     args.out_features = a.out_features;
-    args.total_cols = (int)O;
-    args.MR = a.m * c.reads;
-    args.full = (long long)args.MR - args.MR % 16;
+    args.MR = MR;
+    args.full = (long long)MR - MR % 16;
     args.col_begin = a.tile_begin * c.cols;
     args.col_end = a.tile_end * c.cols;
     args.error = err;
-    const size_t smem = sizeof(tc::Smem) + 1024;
-    MF_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_ideal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                  "tc smem attribute");
     const long long cols = (long long)(a.tile_end - a.tile_begin) * c.cols;
     dim3 grid((unsigned)((a.n + tc::BM - 1) / tc::BM), (unsigned)((cols + tc::BN - 1) / tc::BN));
-    tc::tc_ideal_kernel<<<grid, tc::THREADS, smem, st>>>(mx, mw, args);
-    MF_LAUNCH_CHECK("tc_ideal_kernel");
-    return MF_OK;
+    const tc::Plan& P = args.plan;
+#define MF_TC(NA_, NWA_, NWC_) \
+    if (P.na == NA_ && P.nwa == NWA_ && P.nwc == NWC_) return launch_tc<NA_, NWA_, NWC_>(mx, mw, mxs, mws, args, grid, st)
+    MF_TC(3, 2, 2);
+    MF_TC(3, 2, 0);
+    MF_TC(3, 1, 0);
+    MF_TC(3, 1, 2);
+    MF_TC(0, 0, 0);
+#undef MF_TC
+    set_error("no compiled tcgen05 kernel for plan (%d, %d, %d)", P.na, P.nwa, P.nwc);
+    return MF_ERR_UNSUPPORTED;
 }
 
 mf_status tc_take_error(unsigned* code) {

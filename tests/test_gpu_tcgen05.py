@@ -81,7 +81,7 @@ def test_tcgen05_bit_exact_when_adcs_clip(mf, adc):
 def test_tcgen05_vs_oracle_with_bias_and_unsigned_weights(mf):
     from oracle import oracle as O
 
-    config = int8_config(mf, weight_signed=False, weight_slice=(2, 2, 2, 2))
+    config = int8_config(mf, weight_signed=False, weight_slice=(2, 2, 2, 2), adc=(6, 7, 7, 8))
     g = torch.Generator().manual_seed(3)
     a = torch.randn(96, 384, generator=g)
     w = torch.rand(160, 384, generator=g) * 3
