@@ -55,6 +55,14 @@ constexpr int MAXPB = 4;         // max clip-capable weight-slice planes
 constexpr int THREADS = 384;     // 12 warps
 constexpr int TILE = BM * KR;    // 4096 bytes: one [128 x 32] 8-bit tile
 constexpr int HALF_COLS = 256;   // TMEM columns per half
+// Register split between warpgroup 0 (producer, MMA, transform) and the two
+// epilogue warpgroups.  setmaxnreg.inc draws on the registers the block was
+// launched with, so 128 * REG_LOW + 256 * REG_HIGH must not exceed
+// THREADS * (registers per thread at launch); the host checks this before
+// every launch (launch_tc), because an increase that cannot be met never returns.
+constexpr int REG_LOW = 88;
+constexpr int REG_HIGH = 208;
+static_assert(128 * REG_LOW + 256 * REG_HIGH <= THREADS * 168, "register split exceeds the launch pool");
 
 // Shared memory plan (1024-aligned tiles first).
 struct Smem {
@@ -361,7 +369,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tmem = s.tmem_base;
 
     if (warp < 4) {
-        set_maxnreg_dec<96>();
+        set_maxnreg_dec<REG_LOW>();
         if (warp == 0) {
             // -------------------------------------------------------- producer
             if (lane == 0) {
@@ -497,7 +505,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     } else {
-        set_maxnreg_inc<208>();
+        set_maxnreg_inc<REG_HIGH>();
         // ------------------------------------------------------------ epilogue
         const int h = (warp - 4) >> 2;              // TMEM half = job parity owned by this warpgroup
         const int quad = warp & 3;                  // TMEM lane quadrant of this warp
@@ -811,6 +819,16 @@ static mf_status launch_tc(const CUtensorMap& mx, const CUtensorMap& mw, const C
                            const CUtensorMap& mws, const tc::Args& args, dim3 grid, cudaStream_t st) {
     const size_t smem = sizeof(tc::Smem) + 1024;
     auto kern = tc::tc_ideal_kernel<NA, NWA, NWC>;
+    cudaFuncAttributes attr;
+    MF_CHECK_CUDA(cudaFuncGetAttributes(&attr, kern), "tc kernel attributes");
+    // Registers are allocated per thread in multiples of 8.
+    const long long pool = (long long)((attr.numRegs + 7) / 8 * 8) * tc::THREADS;
+    const long long split = 128LL * tc::REG_LOW + 256LL * tc::REG_HIGH;
+    if (split > pool) {
+        set_error("tcgen05 kernel launched with %d registers/thread cannot host the %d/%d register split",
+                  attr.numRegs, tc::REG_LOW, tc::REG_HIGH);
+        return MF_ERR_RESOURCE;
+    }
     MF_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                   "tc smem attribute");
     kern<<<grid, tc::THREADS, smem, st>>>(mx, mw, mxs, mws, args);
