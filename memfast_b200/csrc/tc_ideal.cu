@@ -528,7 +528,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.flag_full[rs], (i / RING) & 1, s, err, 7));
             if (!ok) break;
             const float xs = s.xs[sb][r][i % SCB];
-            const float2 xs2 = make_float2(xs, xs);
             const uint32_t f0 = *(volatile uint32_t*)&s.flags[rs][0];
             const uint32_t f1 = *(volatile uint32_t*)&s.flags[rs][1];
 #pragma unroll
@@ -585,14 +584,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (lane == 0) mbar_arrive(&s.unit_empty[h]);
                     ++units;
                 }
-                // fl(fl(T * xs) * ws) pushed into cascade level 0 for read i.
+                // fl(fl(T * xs) * ws) pushed into cascade level 0 for read i.  Scalar
+                // round-to-nearest intrinsics: packed f32x2 multiplies followed by an add
+                // were observed to round once (as an FMA), which the reference does not.
                 const float2* wsr = reinterpret_cast<const float2*>(&s.ws[sb][i % SCB][j * SUB]);
 #pragma unroll
                 for (int ch = 0; ch < 2; ++ch)
 #pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        acc0[jj][ch * 8 + e] =
-                            __fadd2_rn(acc0[jj][ch * 8 + e], __fmul2_rn(__fmul2_rn(T[ch][e], xs2), wsr[ch * 8 + e]));
+                    for (int e = 0; e < 8; ++e) {
+                        const float2 w2 = wsr[ch * 8 + e];
+                        float2& a2 = acc0[jj][ch * 8 + e];
+                        a2.x = __fadd_rn(a2.x, __fmul_rn(__fmul_rn(T[ch][e].x, xs), w2.x));
+                        a2.y = __fadd_rn(a2.y, __fmul_rn(__fmul_rn(T[ch][e].y, xs), w2.y));
+                    }
             }
             if (!ok) break;
             __syncwarp();
