@@ -74,6 +74,7 @@ struct Smem {
     float xs[SCRING][BM][SCB];                      // TMA: input scales [row][read]
     float ws[SCRING][SCB][BN];                      // TMA: weight scales [read][column]
     uint32_t flags[RING][2];                        // one word per transform warp
+    uint32_t pbits[RING][2];                        // always-plane clip bounds (see transform)
     uint64_t full[STAGES], ready[STAGES], empty[STAGES];
     uint64_t flag_full[RING], flag_empty[RING];
     uint64_t sc_full[SCRING], sc_empty[SCRING];
@@ -92,7 +93,8 @@ struct Plan {
     float dscale[MAXPB];               // 2^(18 - k_w)
     float offset[MAXPB];               // -m_w * 2^-k_w
     int row_limit;                     // conditional: flag a row when S_a(n) > row_limit
-    int col_limit[MAXPB];              // conditional: flag a column when S_w(o) > col_limit[q]
+    int col_limit[MAXPB];              // plane q can clip in column o only if S_wq(o) > col_limit[q]
+    int prow_limit[MAXPB];             // plane q can clip in row n only if max_a S_a(n) > prow_limit[q]
     int b_signed;                      // weight codes signed (s8) or unsigned (u8)
 };
 
@@ -286,25 +288,71 @@ __device__ __forceinline__ bool job_flagged(int nwc, uint32_t f0, uint32_t f1, i
     return nwc > 0 && (f & 1u) && (f & (2u << j));
 }
 
-// T (32 columns) from the x.w accumulator: |x.w| < 2^22, so 1.5*2^23 + x.w holds the
-// integer exactly in its mantissa.
-__device__ __forceinline__ void base_to_float(const uint32_t (&v)[16], float2 (&T)[8]) {
-    const float2 magic = make_float2(-12582912.0f, -12582912.0f);
+// T is kept as packed FP32 pairs (b64) so the f32x2 instructions need no moves.
+// T from the x.w accumulator: |x.w| < 2^22, so 1.5*2^23 + x.w holds the integer
+// exactly in its mantissa and subtracting 1.5*2^23 recovers it.
+__device__ __forceinline__ void base_to_float(const uint32_t (&v)[16], uint64_t (&T)[8]) {
+    const uint64_t magic = 0xCB400000CB400000ull;    // (-1.5*2^23, -1.5*2^23)
 #pragma unroll
     for (int e = 0; e < 8; ++e)
-        T[e] = __fadd2_rn(make_float2(__int_as_float((int)v[2 * e] + 0x4B400000),
-                                      __int_as_float((int)v[2 * e + 1] + 0x4B400000)),
-                          magic);
+        asm("{\n\t.reg .b32 a, b;\n\t.reg .b64 p;\n\t"
+            "add.s32 a, %1, 0x4B400000;\n\t"
+            "add.s32 b, %2, 0x4B400000;\n\t"
+            "mov.b64 p, {a, b};\n\t"
+            "add.rn.f32x2 %0, p, %3;\n\t}"
+            : "=l"(T[e])
+            : "r"(v[2 * e]), "r"(v[2 * e + 1]), "l"(magic));
 }
 
-// T -= s_a s_w relu(D - m) for one pair plane; D arrives as D * 2^-18.
-__device__ __forceinline__ void relu_correct(const uint32_t (&v)[16], float2 (&T)[8], float ds, float off, float cf) {
-    const float2 c2 = make_float2(cf, cf);
+// T -= s_a s_w relu(D - m) for one pair plane; D arrives as D * 2^-18, and
+// fma.sat gives relu(D - m) * 2^-k exactly (k chosen on the host).
+__device__ __forceinline__ void relu_correct(const uint32_t (&v)[16], uint64_t (&T)[8], float ds, float off, float cf) {
+    uint64_t c2;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(c2) : "f"(cf));
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        const float y0 = fma_sat(__uint_as_float(v[2 * e]), ds, off);
-        const float y1 = fma_sat(__uint_as_float(v[2 * e + 1]), ds, off);
-        T[e] = __ffma2_rn(make_float2(y0, y1), c2, T[e]);
+    for (int e = 0; e < 8; ++e)
+        asm("{\n\t.reg .f32 y0, y1;\n\t.reg .b64 y;\n\t"
+            "fma.rn.sat.f32 y0, %1, %3, %4;\n\t"
+            "fma.rn.sat.f32 y1, %2, %3, %4;\n\t"
+            "mov.b64 y, {y0, y1};\n\t"
+            "fma.rn.f32x2 %0, y, %5, %0;\n\t}"
+            : "+l"(T[e])
+            : "f"(__uint_as_float(v[2 * e])), "f"(__uint_as_float(v[2 * e + 1])), "f"(ds), "f"(off), "l"(c2));
+}
+
+__device__ __forceinline__ float2 unpack(uint64_t t) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(t));
+    return r;
+}
+
+// Corrections for the planes in `mask` (bit k = plane k of the unit at `base`),
+// loads double-buffered behind the math.  `planes_per_a` maps k to (a, q).
+__device__ __forceinline__ void correct_planes(uint32_t mask, uint32_t base, int planes_per_a, int qbase,
+                                               const Plan& P, uint64_t (&T)[8]) {
+    uint32_t va[16], vb[16];
+    int k0 = mask ? __ffs(mask) - 1 : -1;
+    mask &= mask - 1;
+    if (k0 >= 0) tmem_ld16(base + k0 * SUB, vb);
+    while (k0 >= 0) {
+        const int k1 = mask ? __ffs(mask) - 1 : -1;
+        mask &= mask - 1;
+        tmem_wait(vb);
+        if (k1 >= 0) tmem_ld16(base + k1 * SUB, va);
+        {
+            const int a = k0 / planes_per_a, q = qbase + k0 % planes_per_a;
+            relu_correct(vb, T, P.dscale[q], P.offset[q], P.coef[a][q]);
+        }
+        if (k1 < 0) break;
+        const int k2 = mask ? __ffs(mask) - 1 : -1;
+        mask &= mask - 1;
+        tmem_wait(va);
+        if (k2 >= 0) tmem_ld16(base + k2 * SUB, vb);
+        {
+            const int a = k1 / planes_per_a, q = qbase + k1 % planes_per_a;
+            relu_correct(va, T, P.dscale[q], P.offset[q], P.coef[a][q]);
+        }
+        k0 = k2;
     }
 }
 
@@ -449,7 +497,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 bool ok = mbar_wait(&s.full[st], (i / STAGES) & 1, s, err, 5);
                 ok = ok && mbar_wait(&s.flag_empty[rs], ((i / RING) & 1) ^ 1, s, err, 6);
                 if (!__all_sync(0xFFFFFFFFu, ok)) break;
-                uint32_t word = 0;
+                uint32_t word = 0, bits = 0;
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
                     const int t = tw * 32 + lane + 64 * hh;   // A row t and B column t (0..127)
@@ -458,7 +506,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint4* xrow = reinterpret_cast<const uint4*>(s.x[st] + t * KR);
                     const uint4 xa = xrow[0], xb = xrow[1];
                     const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-                    uint32_t rowmax = 0;
+                    uint32_t rowmax = 0;   // max over clip-capable A slices of the read's digit sum
 #pragma unroll
                     for (int a = 0; a < NA; ++a) {
                         const uint32_t m4 = (uint32_t)P.a_mask[a] * 0x01010101u;
@@ -466,17 +514,19 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                         for (int k = 0; k < 8; ++k) {
                             d[k] = (xw[k] >> P.a_shift[a]) & m4;
-                            if (NWC > 0) sum = __dp4a(d[k], 0x01010101u, sum);
+                            sum = __dp4a(d[k], 0x01010101u, sum);
                         }
                         uint4* dst = reinterpret_cast<uint4*>(s.ap[st][a] + t * KR);
                         dst[0] = make_uint4(d[0], d[1], d[2], d[3]);
                         dst[1] = make_uint4(d[4], d[5], d[6], d[7]);
                         rowmax = sum > rowmax ? sum : rowmax;
                     }
+                    if (n0 + t >= args.n) rowmax = 0;
                     const uint4* wrow = reinterpret_cast<const uint4*>(s.w[st] + t * KR);
                     const uint4 wa = wrow[0], wb = wrow[1];
                     const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
                     bool colflag = false;
+                    const int job = t >> 5, quad = t >> 5;   // this warp's rows form quadrant t>>5
 #pragma unroll
                     for (int q = 0; q < NWA + NWC; ++q) {
                         const uint32_t m4 = (uint32_t)P.w_mask[q] * 0x01010101u;
@@ -484,18 +534,29 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                         for (int k = 0; k < 8; ++k) {
                             d[k] = (ww[k] >> P.w_shift[q]) & m4;
-                            if (q >= NWA) sum = __dp4a(d[k], 0x01010101u, sum);
+                            sum = __dp4a(d[k], 0x01010101u, sum);
                         }
-                        uint4* dst = reinterpret_cast<uint4*>(s.bp[st][t >> 5][q] + (t & 31) * KR);
+                        uint4* dst = reinterpret_cast<uint4*>(s.bp[st][job][q] + (t & 31) * KR);
                         dst[0] = make_uint4(d[0], d[1], d[2], d[3]);
                         dst[1] = make_uint4(d[4], d[5], d[6], d[7]);
-                        if (q >= NWA && (int)sum > P.col_limit[q]) colflag = true;
+                        const bool cbig = (int)sum > P.col_limit[q];
+                        if (q >= NWA) {
+                            colflag |= cbig;
+                        } else {
+                            // Plane q can clip in this (row quadrant, column job) only if some row
+                            // and some column both exceed their digit-sum limits.
+                            if (__any_sync(0xFFFFFFFFu, cbig)) bits |= 1u << (16 + job * 4 + q);
+                            if (__any_sync(0xFFFFFFFFu, (int)rowmax > P.prow_limit[q])) bits |= 1u << (quad * 4 + q);
+                        }
                     }
-                    const bool rowflag = NWC > 0 && (int)rowmax > P.row_limit && n0 + t < args.n;
+                    const bool rowflag = NWC > 0 && (int)rowmax > P.row_limit;
                     if (__any_sync(0xFFFFFFFFu, rowflag)) word |= 1u;
-                    if (__any_sync(0xFFFFFFFFu, colflag)) word |= 2u << (t >> 5);
+                    if (__any_sync(0xFFFFFFFFu, colflag)) word |= 2u << job;
                 }
-                if (lane == 0) s.flags[rs][tw] = word;
+                if (lane == 0) {
+                    s.flags[rs][tw] = word;
+                    s.pbits[rs][tw] = bits;
+                }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {
@@ -530,6 +591,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const float xs = s.xs[sb][r][i % SCB];
             const uint32_t f0 = *(volatile uint32_t*)&s.flags[rs][0];
             const uint32_t f1 = *(volatile uint32_t*)&s.flags[rs][1];
+            const uint32_t pb = *(volatile uint32_t*)&s.pbits[rs][0] | *(volatile uint32_t*)&s.pbits[rs][1];
 #pragma unroll
             for (int jj = 0; jj < 2; ++jj) {
                 const int j = h + 2 * jj;
@@ -537,29 +599,21 @@ __global__ void __launch_bounds__(THREADS, 1)
                 ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[h], units & 1, s, err, 9));
                 if (!ok) break;
                 tc_fence_after();
-                float2 T[2][8];
-                // Two 16-column halves; TMEM loads double-buffered behind the math.
+                // Planes this warp must correct: plane k = a*NWA + q of the always unit.
+                uint32_t todo = 0;
+#pragma unroll
+                for (int q = 0; q < NWA; ++q)
+                    if (((pb >> (quad * 4 + q)) & 1u) && ((pb >> (16 + j * 4 + q)) & 1u))
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) todo |= 1u << (a * NWA + q);
+                uint64_t T[2][8];
 #pragma unroll
                 for (int ch = 0; ch < 2; ++ch) {
-                    uint32_t va[16], vb[16];
-                    const uint32_t col = half + ch * 16;
-                    tmem_ld16(col, va);
-                    tmem_wait(va);
-                    if (NA * NWA > 0) tmem_ld16(col + 32, vb);
-                    base_to_float(va, T[ch]);
-#pragma unroll
-                    for (int k = 0; k < NA * NWA; ++k) {
-                        const int a = k / (NWA > 0 ? NWA : 1), q = k % (NWA > 0 ? NWA : 1);
-                        if (k & 1) {
-                            tmem_wait(va);
-                            if (k + 1 < NA * NWA) tmem_ld16(col + 32 + (k + 1) * SUB, vb);
-                            relu_correct(va, T[ch], P.dscale[q], P.offset[q], P.coef[a][q]);
-                        } else {
-                            tmem_wait(vb);
-                            if (k + 1 < NA * NWA) tmem_ld16(col + 32 + (k + 1) * SUB, va);
-                            relu_correct(vb, T[ch], P.dscale[q], P.offset[q], P.coef[a][q]);
-                        }
-                    }
+                    uint32_t vt[16];
+                    tmem_ld16(half + ch * 16, vt);
+                    tmem_wait(vt);
+                    base_to_float(vt, T[ch]);
+                    correct_planes(todo, half + 32 + ch * 16, NWA > 0 ? NWA : 1, 0, P, T[ch]);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -569,16 +623,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                     ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[h], units & 1, s, err, 10));
                     if (!ok) break;
                     tc_fence_after();
+                    const uint32_t all = (1u << (NA * NWC)) - 1u;
 #pragma unroll
                     for (int ch = 0; ch < 2; ++ch)
-#pragma unroll
-                        for (int k = 0; k < NA * NWC; ++k) {
-                            const int a = k / (NWC > 0 ? NWC : 1), q = NWA + k % (NWC > 0 ? NWC : 1);
-                            uint32_t va[16];
-                            tmem_ld16(half + ch * 16 + k * SUB, va);
-                            tmem_wait(va);
-                            relu_correct(va, T[ch], P.dscale[q], P.offset[q], P.coef[a][q]);
-                        }
+                        correct_planes(all, half + ch * 16, NWC > 0 ? NWC : 1, NWA, P, T[ch]);
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&s.unit_empty[h]);
@@ -593,9 +641,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         const float2 w2 = wsr[ch * 8 + e];
+                        const float2 t2 = unpack(T[ch][e]);
                         float2& a2 = acc0[jj][ch * 8 + e];
-                        a2.x = __fadd_rn(a2.x, __fmul_rn(__fmul_rn(T[ch][e].x, xs), w2.x));
-                        a2.y = __fadd_rn(a2.y, __fmul_rn(__fmul_rn(T[ch][e].y, xs), w2.y));
+                        a2.x = __fadd_rn(a2.x, __fmul_rn(__fmul_rn(t2.x, xs), w2.x));
+                        a2.y = __fadd_rn(a2.y, __fmul_rn(__fmul_rn(t2.y, xs), w2.y));
                     }
             }
             if (!ok) break;
@@ -781,12 +830,10 @@ bool tc_plan(const mf_config& c, tc::Plan& P) {
         P.offset[q] = -ldexpf((float)c.adc_max[w], -k);
         for (int i = 0; i < na; ++i)
             P.coef[i][q] = -(float)(c.in_factor[clip_a[i]] * c.w_factor[w]) * ldexpf(1.0f, k);
-        if (q >= nwa) {
-            // D <= Mw * S_a(n) and D <= Ma * S_w(o): below these limits no pair of the group can clip.
-            const int rl = c.adc_max[w] / c.w_mask[w];
-            P.row_limit = rl < P.row_limit ? rl : P.row_limit;
-            P.col_limit[q] = c.adc_max[w] / amask;
-        }
+        // D <= Mw * S_a(n) and D <= Ma * S_w(o): below these limits plane q cannot clip.
+        P.prow_limit[q] = c.adc_max[w] / c.w_mask[w];
+        P.col_limit[q] = c.adc_max[w] / amask;
+        if (q >= nwa) P.row_limit = P.prow_limit[q] < P.row_limit ? P.prow_limit[q] : P.row_limit;
     }
     return true;
 }
