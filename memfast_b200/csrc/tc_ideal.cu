@@ -326,36 +326,6 @@ __device__ __forceinline__ float2 unpack(uint64_t t) {
     return r;
 }
 
-// Corrections for the planes in `mask` (bit k = plane k of the unit at `base`),
-// loads double-buffered behind the math.  `planes_per_a` maps k to (a, q).
-__device__ __forceinline__ void correct_planes(uint32_t mask, uint32_t base, int planes_per_a, int qbase,
-                                               const Plan& P, uint64_t (&T)[8]) {
-    uint32_t va[16], vb[16];
-    int k0 = mask ? __ffs(mask) - 1 : -1;
-    mask &= mask - 1;
-    if (k0 >= 0) tmem_ld16(base + k0 * SUB, vb);
-    while (k0 >= 0) {
-        const int k1 = mask ? __ffs(mask) - 1 : -1;
-        mask &= mask - 1;
-        tmem_wait(vb);
-        if (k1 >= 0) tmem_ld16(base + k1 * SUB, va);
-        {
-            const int a = k0 / planes_per_a, q = qbase + k0 % planes_per_a;
-            relu_correct(vb, T, P.dscale[q], P.offset[q], P.coef[a][q]);
-        }
-        if (k1 < 0) break;
-        const int k2 = mask ? __ffs(mask) - 1 : -1;
-        mask &= mask - 1;
-        tmem_wait(va);
-        if (k2 >= 0) tmem_ld16(base + k2 * SUB, vb);
-        {
-            const int a = k1 / planes_per_a, q = qbase + k1 % planes_per_a;
-            relu_correct(va, T, P.dscale[q], P.offset[q], P.coef[a][q]);
-        }
-        k0 = k2;
-    }
-}
-
 // ------------------------------------------------------------------- kernel
 // NA / NWA / NWC: plan sizes (clip-capable input planes, always and conditional
 // weight planes).  A job's TMEM unit on its half: base x.w at column 0 (32 cols),
@@ -393,7 +363,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int h = 0; h < 2; ++h) {
             mbar_init(&s.unit_full[h], 1);
-            mbar_init(&s.unit_empty[h], 4);
+            mbar_init(&s.unit_empty[h], 8);
         }
         mbar_init(&s.drained, 1);
         s.abort = 0;
@@ -450,7 +420,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t id_base = idesc_i8(SUB, P.b_signed != 0);
                 const uint32_t id_always = idesc_e4m3(SUB * (NWA > 0 ? NWA : 1));
                 const uint32_t id_cond = idesc_e4m3(SUB * (NWC > 0 ? NWC : 1));
-                uint32_t units[2] = {0, 0};
+                uint32_t units = 0;   // units issued; unit u uses buffer u & 1
                 bool ok = true;
                 for (int i = 0; i < MR && ok; ++i) {
                     const int st = i % STAGES;
@@ -461,26 +431,28 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint64_t dx = desc_sw32(s.x[st]);
 #pragma unroll
                     for (int j = 0; j < NSUB; ++j) {
-                        const int h = j & 1;
-                        const uint32_t half = tmem + h * HALF_COLS;
-                        if (!mbar_wait(&s.unit_empty[h], (units[h] & 1) ^ 1, s, err, 3)) { ok = false; break; }
+                        uint32_t b = units & 1;
+                        if (!mbar_wait(&s.unit_empty[b], ((units >> 1) & 1) ^ 1, s, err, 3)) { ok = false; break; }
                         tc_fence_after();
-                        mma_i8(half, dx, desc_sw32(s.w[st] + j * SUB * KR), id_base);
+                        uint32_t buf = tmem + b * HALF_COLS;
+                        mma_i8(buf, dx, desc_sw32(s.w[st] + j * SUB * KR), id_base);
 #pragma unroll
                         for (int a = 0; a < NA; ++a)
-                            mma_f8(half + 32 + a * NWA * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][0]),
+                            mma_f8(buf + 32 + a * NWA * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][0]),
                                    id_always);
-                        mma_commit(&s.unit_full[h]);
-                        ++units[h];
+                        mma_commit(&s.unit_full[b]);
+                        ++units;
                         if (NWC > 0 && job_flagged(NWC, f0, f1, j)) {
-                            if (!mbar_wait(&s.unit_empty[h], (units[h] & 1) ^ 1, s, err, 4)) { ok = false; break; }
+                            b = units & 1;
+                            if (!mbar_wait(&s.unit_empty[b], ((units >> 1) & 1) ^ 1, s, err, 4)) { ok = false; break; }
                             tc_fence_after();
+                            buf = tmem + b * HALF_COLS;
 #pragma unroll
                             for (int a = 0; a < NA; ++a)
-                                mma_f8(half + a * NWC * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][NWA]),
+                                mma_f8(buf + a * NWC * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][NWA]),
                                        id_cond);
-                            mma_commit(&s.unit_full[h]);
-                            ++units[h];
+                            mma_commit(&s.unit_full[b]);
+                            ++units;
                         }
                     }
                     if (ok) mma_commit(&s.empty[st]);
@@ -568,16 +540,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else {
         set_maxnreg_inc<REG_HIGH>();
         // ------------------------------------------------------------ epilogue
-        const int h = (warp - 4) >> 2;              // TMEM half = job parity owned by this warpgroup
-        const int quad = warp & 3;                  // TMEM lane quadrant of this warp
+        // All 8 warps consume every unit: warp w reads TMEM lane quadrant w & 3 and the
+        // 16-column half hc of each 32-column job.  Two TMEM buffers alternate, so the
+        // MMA fills one while the epilogue drains the other.
+        const int quad = warp & 3;
+        const int hc = (warp - 4) >> 2;
         const int r = quad * 32 + lane;             // CTA row = TMEM lane
         const long long row = n0 + r;
-        const uint32_t half = tmem + ((uint32_t)(quad * 32) << 16) + h * HALF_COLS;
-        float2 acc0[2][16];                         // jobs h and h + 2, 32 columns each
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + hc * 16;
+        float acc0[NSUB][16];
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj)
+        for (int j = 0; j < NSUB; ++j)
 #pragma unroll
-            for (int e = 0; e < 16; ++e) acc0[jj][e] = make_float2(0.0f, 0.0f);
+            for (int e = 0; e < 16; ++e) acc0[j][e] = 0.0f;
         uint32_t units = 0;
         bool ok = true;
         for (int i = 0; i < MR && ok; ++i) {
@@ -593,59 +568,80 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t f1 = *(volatile uint32_t*)&s.flags[rs][1];
             const uint32_t pb = *(volatile uint32_t*)&s.pbits[rs][0] | *(volatile uint32_t*)&s.pbits[rs][1];
 #pragma unroll
-            for (int jj = 0; jj < 2; ++jj) {
-                const int j = h + 2 * jj;
+            for (int j = 0; j < NSUB; ++j) {
                 const bool flagged = NWC > 0 && job_flagged(NWC, f0, f1, j);
-                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[h], units & 1, s, err, 9));
+                uint32_t bsel = units & 1;
+                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[bsel], (units >> 1) & 1, s, err, 9));
                 if (!ok) break;
                 tc_fence_after();
-                // Planes this warp must correct: plane k = a*NWA + q of the always unit.
-                uint32_t todo = 0;
+                uint32_t buf = lane_base + bsel * HALF_COLS;
+                uint64_t T[8];
+                {
+                    // Base x.w and the first always plane of every input slice in one batch.
+                    uint32_t vt[16], v0[NA > 0 ? NA : 1][16];
+                    tmem_ld16(buf, vt);
 #pragma unroll
-                for (int q = 0; q < NWA; ++q)
-                    if (((pb >> (quad * 4 + q)) & 1u) && ((pb >> (16 + j * 4 + q)) & 1u))
-#pragma unroll
-                        for (int a = 0; a < NA; ++a) todo |= 1u << (a * NWA + q);
-                uint64_t T[2][8];
-#pragma unroll
-                for (int ch = 0; ch < 2; ++ch) {
-                    uint32_t vt[16];
-                    tmem_ld16(half + ch * 16, vt);
+                    for (int a = 0; a < NA; ++a) tmem_ld16(buf + 32 + a * NWA * SUB, v0[a]);
                     tmem_wait(vt);
-                    base_to_float(vt, T[ch]);
-                    correct_planes(todo, half + 32 + ch * 16, NWA > 0 ? NWA : 1, 0, P, T[ch]);
+#pragma unroll
+                    for (int a = 0; a < NA; ++a) tmem_wait(v0[a]);
+                    base_to_float(vt, T);
+                    if (NWA > 0 && ((pb >> (quad * 4)) & 1u) && ((pb >> (16 + j * 4)) & 1u)) {
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) relu_correct(v0[a], T, P.dscale[0], P.offset[0], P.coef[a][0]);
+                    }
+                }
+#pragma unroll
+                for (int q = 1; q < NWA; ++q) {
+                    // Further always planes: skipped when no row of this quadrant and no column of
+                    // this job can exceed the plane's ADC limit.
+                    if (((pb >> (quad * 4 + q)) & 1u) && ((pb >> (16 + j * 4 + q)) & 1u)) {
+                        uint32_t v1[NA > 0 ? NA : 1][16];
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) tmem_ld16(buf + 32 + (a * NWA + q) * SUB, v1[a]);
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) tmem_wait(v1[a]);
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) relu_correct(v1[a], T, P.dscale[q], P.offset[q], P.coef[a][q]);
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&s.unit_empty[h]);
+                if (lane == 0) mbar_arrive(&s.unit_empty[bsel]);
                 ++units;
                 if (flagged) {
-                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[h], units & 1, s, err, 10));
+                    bsel = units & 1;
+                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[bsel], (units >> 1) & 1, s, err, 10));
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t all = (1u << (NA * NWC)) - 1u;
+                    buf = lane_base + bsel * HALF_COLS;
 #pragma unroll
-                    for (int ch = 0; ch < 2; ++ch)
-                        correct_planes(all, half + ch * 16, NWC > 0 ? NWC : 1, NWA, P, T[ch]);
+                    for (int q = 0; q < NWC; ++q) {
+                        uint32_t v1[NA > 0 ? NA : 1][16];
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) tmem_ld16(buf + (a * NWC + q) * SUB, v1[a]);
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) tmem_wait(v1[a]);
+#pragma unroll
+                        for (int a = 0; a < NA; ++a)
+                            relu_correct(v1[a], T, P.dscale[NWA + q], P.offset[NWA + q], P.coef[a][NWA + q]);
+                    }
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&s.unit_empty[h]);
+                    if (lane == 0) mbar_arrive(&s.unit_empty[bsel]);
                     ++units;
                 }
                 // fl(fl(T * xs) * ws) pushed into cascade level 0 for read i.  Scalar
                 // round-to-nearest intrinsics: packed f32x2 multiplies followed by an add
                 // were observed to round once (as an FMA), which the reference does not.
-                const float2* wsr = reinterpret_cast<const float2*>(&s.ws[sb][i % SCB][j * SUB]);
+                const float2* wsr = reinterpret_cast<const float2*>(&s.ws[sb][i % SCB][j * SUB + hc * 16]);
 #pragma unroll
-                for (int ch = 0; ch < 2; ++ch)
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float2 w2 = wsr[ch * 8 + e];
-                        const float2 t2 = unpack(T[ch][e]);
-                        float2& a2 = acc0[jj][ch * 8 + e];
-                        a2.x = __fadd_rn(a2.x, __fmul_rn(__fmul_rn(t2.x, xs), w2.x));
-                        a2.y = __fadd_rn(a2.y, __fmul_rn(__fmul_rn(t2.y, xs), w2.y));
-                    }
+                for (int e = 0; e < 8; ++e) {
+                    const float2 w2 = wsr[e];
+                    const float2 t2 = unpack(T[e]);
+                    acc0[j][2 * e] = __fadd_rn(acc0[j][2 * e], __fmul_rn(__fmul_rn(t2.x, xs), w2.x));
+                    acc0[j][2 * e + 1] = __fadd_rn(acc0[j][2 * e + 1], __fmul_rn(__fmul_rn(t2.y, xs), w2.y));
+                }
             }
             if (!ok) break;
             __syncwarp();
@@ -657,28 +653,26 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int done = i + 1;
             if (done <= args.full && (done & 15) == 0) {
 #pragma unroll
-                for (int jj = 0; jj < 2; ++jj)
+                for (int j = 0; j < NSUB; ++j)
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
-                        const int cl = (h + 2 * jj) * SUB + 2 * e;
-                        s.acc1[cl][r] = __fadd_rn(s.acc1[cl][r], acc0[jj][e].x);
-                        s.acc1[cl + 1][r] = __fadd_rn(s.acc1[cl + 1][r], acc0[jj][e].y);
-                        acc0[jj][e] = make_float2(0.0f, 0.0f);
+                        const int cl = j * SUB + hc * 16 + e;
+                        s.acc1[cl][r] = __fadd_rn(s.acc1[cl][r], acc0[j][e]);
+                        acc0[j][e] = 0.0f;
                     }
             }
         }
         if (ok && row < args.n) {
 #pragma unroll
-            for (int jj = 0; jj < 2; ++jj)
+            for (int j = 0; j < NSUB; ++j)
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int cl = (h + 2 * jj) * SUB + e;
+                for (int e = 0; e < 16; ++e) {
+                    const int cl = j * SUB + hc * 16 + e;
                     const int col = c0 + cl;
                     if (col >= args.col_end || col >= args.out_features) continue;
-                    const float a0 = (e & 1) ? acc0[jj][e >> 1].y : acc0[jj][e >> 1].x;
                     // acc0 + acc1 + acc2 + acc3 (upper levels zero), then the reference's
                     // store into a zero-filled output.
-                    float value = __fadd_rn(a0, s.acc1[cl][r]);
+                    float value = __fadd_rn(acc0[j][e], s.acc1[cl][r]);
                     value = __fadd_rn(value, 0.0f);
                     value = __fadd_rn(value, 0.0f);
                     value = __fadd_rn(0.0f, value);
