@@ -470,7 +470,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 ok = ok && mbar_wait(&s.flag_empty[rs], ((i / RING) & 1) ^ 1, s, err, 6);
                 if (!__all_sync(0xFFFFFFFFu, ok)) break;
                 uint32_t word = 0, bits = 0;
-#pragma unroll
+#pragma unroll 1
                 for (int hh = 0; hh < 2; ++hh) {
                     const int t = tw * 32 + lane + 64 * hh;   // A row t and B column t (0..127)
                     // Row t of a [128 x 32] SW32 tile keeps both 16-byte chunks inside the
@@ -567,7 +567,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t f0 = *(volatile uint32_t*)&s.flags[rs][0];
             const uint32_t f1 = *(volatile uint32_t*)&s.flags[rs][1];
             const uint32_t pb = *(volatile uint32_t*)&s.pbits[rs][0] | *(volatile uint32_t*)&s.pbits[rs][1];
-#pragma unroll
+            // Jobs share one copy of the TMEM/correction code (a runtime loop keeps the hot
+            // code small enough for the instruction cache); only the register-resident
+            // scale-and-accumulate step is specialised per job.
+#pragma unroll 1
             for (int j = 0; j < NSUB; ++j) {
                 const bool flagged = NWC > 0 && job_flagged(NWC, f0, f1, j);
                 uint32_t bsel = units & 1;
@@ -635,12 +638,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // round-to-nearest intrinsics: packed f32x2 multiplies followed by an add
                 // were observed to round once (as an FMA), which the reference does not.
                 const float2* wsr = reinterpret_cast<const float2*>(&s.ws[sb][i % SCB][j * SUB + hc * 16]);
+                float v[16];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     const float2 w2 = wsr[e];
                     const float2 t2 = unpack(T[e]);
-                    acc0[j][2 * e] = __fadd_rn(acc0[j][2 * e], __fmul_rn(__fmul_rn(t2.x, xs), w2.x));
-                    acc0[j][2 * e + 1] = __fadd_rn(acc0[j][2 * e + 1], __fmul_rn(__fmul_rn(t2.y, xs), w2.y));
+                    v[2 * e] = __fmul_rn(__fmul_rn(t2.x, xs), w2.x);
+                    v[2 * e + 1] = __fmul_rn(__fmul_rn(t2.y, xs), w2.y);
+                }
+                switch (j) {
+#define MF_ACC(J)                                                         \
+    case J:                                                               \
+        _Pragma("unroll") for (int e = 0; e < 16; ++e) acc0[J][e] = __fadd_rn(acc0[J][e], v[e]); \
+        break;
+                    MF_ACC(0)
+                    MF_ACC(1)
+                    MF_ACC(2)
+                    MF_ACC(3)
+#undef MF_ACC
                 }
             }
             if (!ok) break;
