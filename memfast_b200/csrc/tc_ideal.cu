@@ -54,8 +54,7 @@ constexpr int MAXPA = 3;         // max clip-capable input-slice planes
 constexpr int MAXPB = 4;         // max clip-capable weight-slice planes
 constexpr int THREADS = 384;     // 12 warps
 constexpr int TILE = BM * KR;    // 4096 bytes: one [128 x 32] 8-bit tile
-constexpr int HALF_COLS = 256;   // TMEM columns per epilogue warpgroup
-constexpr int UNIT_COLS = 128;   // TMEM columns per unit (two units per warpgroup)
+constexpr int HALF_COLS = 256;   // TMEM columns per half
 // Register split between warpgroup 0 (producer, MMA, transform) and the two
 // epilogue warpgroups.  setmaxnreg.inc draws on the registers the block was
 // launched with, so 128 * REG_LOW + 256 * REG_HIGH must not exceed
@@ -74,11 +73,12 @@ struct Smem {
     float acc1[BN][BM];                             // cascade level 1, [column][row]
     float xs[SCRING][BM][SCB];                      // TMA: input scales [row][read]
     float ws[SCRING][SCB][BN];                      // TMA: weight scales [read][column]
+    uint32_t flags[RING][2];                        // one word per transform warp
     uint32_t pbits[RING][2];                        // always-plane clip bounds (see transform)
     uint64_t full[STAGES], ready[STAGES], empty[STAGES];
     uint64_t flag_full[RING], flag_empty[RING];
     uint64_t sc_full[SCRING], sc_empty[SCRING];
-    uint64_t unit_full[2][2], unit_empty[2][2];     // [warpgroup][buffer]
+    uint64_t unit_full[2], unit_empty[2];
     uint64_t drained;
     uint32_t tmem_base;
     int abort;
@@ -92,6 +92,7 @@ struct Plan {
     float coef[MAXPA][MAXPB];          // -(s_a s_w) * 2^k_w
     float dscale[MAXPB];               // 2^(18 - k_w)
     float offset[MAXPB];               // -m_w * 2^-k_w
+    int row_limit;                     // conditional: flag a row when S_a(n) > row_limit
     int col_limit[MAXPB];              // plane q can clip in column o only if S_wq(o) > col_limit[q]
     int prow_limit[MAXPB];             // plane q can clip in row n only if max_a S_a(n) > prow_limit[q]
     int b_signed;                      // weight codes signed (s8) or unsigned (u8)
@@ -140,33 +141,19 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// try_wait with a suspend-time hint: the thread sleeps in hardware until the
-// phase completes or about `ns` nanoseconds pass, so waiting warps do not spend
-// issue slots polling.
-__device__ __forceinline__ bool mbar_try_suspend(uint64_t* bar, uint32_t parity, uint32_t ns) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
-        : "memory");
-    return ok != 0;
-}
-
 // Bounded wait: about 2 s of clock64, or until another role aborted the CTA.
 __device__ __forceinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, Smem& s, unsigned* error,
-                                               unsigned code) {
+                                            unsigned code) {
     const long long start = clock64();
     while (true) {
-        if (mbar_try_suspend(bar, parity, 20000)) return true;
+        if (mbar_try(bar, parity)) return true;
         if (*(volatile int*)&s.abort) return false;
         if (clock64() - start > 4000000000LL) {
             atomicCAS(error, 0u, code);
             *(volatile int*)&s.abort = 1;
             return false;
         }
+        __nanosleep(32);
     }
 }
 
@@ -296,13 +283,10 @@ __device__ __forceinline__ void set_maxnreg_inc() { asm volatile("setmaxnreg.inc
 template <int N>
 __device__ __forceinline__ void set_maxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
 
-// Plane q can clip somewhere in job j: some row of the CTA (bits q, 4+q, 8+q, 12+q:
-// one per lane quadrant) and some column of the job (bit 16 + 4j + q) exceed their
-// digit-sum limits.
-__device__ __forceinline__ bool cond_job_flag(uint32_t pb, int q, int j) {
-    return (pb & (0x1111u << q)) && ((pb >> (16 + 4 * j + q)) & 1u);
+__device__ __forceinline__ bool job_flagged(int nwc, uint32_t f0, uint32_t f1, int j) {
+    const uint32_t f = f0 | f1;
+    return nwc > 0 && (f & 1u) && (f & (2u << j));
 }
-
 
 // T is kept as packed FP32 pairs (b64) so the f32x2 instructions need no moves.
 // T from the x.w accumulator: |x.w| < 2^22, so 1.5*2^23 + x.w holds the integer
@@ -353,7 +337,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const __grid_constant__ CUtensorMap map_xs, const __grid_constant__ CUtensorMap map_ws,
                     const Args args) {
     static_assert(NA <= MAXPA && NWA + NWC <= MAXPB, "plan exceeds shared-memory planes");
-    static_assert(32 + NA * NWA * SUB <= UNIT_COLS && NA * SUB <= UNIT_COLS, "unit exceeds its TMEM buffer");
+    static_assert(32 + NA * NWA * SUB <= HALF_COLS && NA * NWC * SUB <= HALF_COLS, "unit exceeds a TMEM half");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const Plan& P = args.plan;
@@ -377,11 +361,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&s.sc_full[i], 1);
             mbar_init(&s.sc_empty[i], 8);
         }
-        for (int h = 0; h < 2; ++h)
-            for (int b = 0; b < 2; ++b) {
-                mbar_init(&s.unit_full[h][b], 1);
-                mbar_init(&s.unit_empty[h][b], 4);
-            }
+        for (int h = 0; h < 2; ++h) {
+            mbar_init(&s.unit_full[h], 1);
+            mbar_init(&s.unit_empty[h], 8);
+        }
         mbar_init(&s.drained, 1);
         s.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -436,41 +419,40 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (lane == 0) {
                 const uint32_t id_base = idesc_i8(SUB, P.b_signed != 0);
                 const uint32_t id_always = idesc_e4m3(SUB * (NWA > 0 ? NWA : 1));
-                const uint32_t id_cond = idesc_e4m3(SUB);
-                uint32_t units[2] = {0, 0};   // per warpgroup; unit u uses buffer u & 1
+                const uint32_t id_cond = idesc_e4m3(SUB * (NWC > 0 ? NWC : 1));
+                uint32_t units = 0;   // units issued; unit u uses buffer u & 1
                 bool ok = true;
                 for (int i = 0; i < MR && ok; ++i) {
                     const int st = i % STAGES;
                     if (!mbar_wait(&s.ready[st], (i / STAGES) & 1, s, err, 2)) break;
                     tc_fence_after();
-                    const uint32_t pb = *(volatile uint32_t*)&s.pbits[i % RING][0] | *(volatile uint32_t*)&s.pbits[i % RING][1];
+                    const uint32_t f0 = *(volatile uint32_t*)&s.flags[i % RING][0];
+                    const uint32_t f1 = *(volatile uint32_t*)&s.flags[i % RING][1];
                     const uint64_t dx = desc_sw32(s.x[st]);
 #pragma unroll
-                    for (int j = 0; j < NSUB && ok; ++j) {
-                        const int h = j & 1;
+                    for (int j = 0; j < NSUB; ++j) {
+                        uint32_t b = units & 1;
+                        if (!mbar_wait(&s.unit_empty[b], ((units >> 1) & 1) ^ 1, s, err, 3)) { ok = false; break; }
+                        tc_fence_after();
+                        uint32_t buf = tmem + b * HALF_COLS;
+                        mma_i8(buf, dx, desc_sw32(s.w[st] + j * SUB * KR), id_base);
 #pragma unroll
-                        for (int u = 0; u < 1 + NWC; ++u) {
-                            // Unit 0: base + always planes.  Unit 1 + c: conditional plane NWA + c,
-                            // issued only when some row and some column of the job can clip it.
-                            if (u > 0 && !cond_job_flag(pb, NWA + u - 1, j)) continue;
-                            const uint32_t b = units[h] & 1;
-                            if (!mbar_wait(&s.unit_empty[h][b], ((units[h] >> 1) & 1) ^ 1, s, err, 3)) { ok = false; break; }
+                        for (int a = 0; a < NA; ++a)
+                            mma_f8(buf + 32 + a * NWA * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][0]),
+                                   id_always);
+                        mma_commit(&s.unit_full[b]);
+                        ++units;
+                        if (NWC > 0 && job_flagged(NWC, f0, f1, j)) {
+                            b = units & 1;
+                            if (!mbar_wait(&s.unit_empty[b], ((units >> 1) & 1) ^ 1, s, err, 4)) { ok = false; break; }
                             tc_fence_after();
-                            const uint32_t buf = tmem + h * HALF_COLS + b * UNIT_COLS;
-                            if (u == 0) {
-                                mma_i8(buf, dx, desc_sw32(s.w[st] + j * SUB * KR), id_base);
+                            buf = tmem + b * HALF_COLS;
 #pragma unroll
-                                for (int a = 0; a < NA; ++a)
-                                    mma_f8(buf + 32 + a * NWA * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][0]),
-                                           id_always);
-                            } else {
-#pragma unroll
-                                for (int a = 0; a < NA; ++a)
-                                    mma_f8(buf + a * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][NWA + u - 1]),
-                                           id_cond);
-                            }
-                            mma_commit(&s.unit_full[h][b]);
-                            ++units[h];
+                            for (int a = 0; a < NA; ++a)
+                                mma_f8(buf + a * NWC * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][NWA]),
+                                       id_cond);
+                            mma_commit(&s.unit_full[b]);
+                            ++units;
                         }
                     }
                     if (ok) mma_commit(&s.empty[st]);
@@ -487,7 +469,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 bool ok = mbar_wait(&s.full[st], (i / STAGES) & 1, s, err, 5);
                 ok = ok && mbar_wait(&s.flag_empty[rs], ((i / RING) & 1) ^ 1, s, err, 6);
                 if (!__all_sync(0xFFFFFFFFu, ok)) break;
-                uint32_t bits = 0;
+                uint32_t word = 0, bits = 0;
 #pragma unroll 1
                 for (int hh = 0; hh < 2; ++hh) {
                     const int t = tw * 32 + lane + 64 * hh;   // A row t and B column t (0..127)
@@ -515,6 +497,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint4* wrow = reinterpret_cast<const uint4*>(s.w[st] + t * KR);
                     const uint4 wa = wrow[0], wb = wrow[1];
                     const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                    bool colflag = false;
                     const int job = t >> 5, quad = t >> 5;   // this warp's rows form quadrant t>>5
 #pragma unroll
                     for (int q = 0; q < NWA + NWC; ++q) {
@@ -528,14 +511,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                         uint4* dst = reinterpret_cast<uint4*>(s.bp[st][job][q] + (t & 31) * KR);
                         dst[0] = make_uint4(d[0], d[1], d[2], d[3]);
                         dst[1] = make_uint4(d[4], d[5], d[6], d[7]);
-                        // D_aq <= Mq * S_a(n) and D_aq <= Ma * S_q(o): plane q can clip in a
-                        // (row quadrant, column job) only if some row and some column of it
-                        // exceed their digit-sum limits.
-                        if (__any_sync(0xFFFFFFFFu, (int)sum > P.col_limit[q])) bits |= 1u << (16 + job * 4 + q);
-                        if (__any_sync(0xFFFFFFFFu, (int)rowmax > P.prow_limit[q])) bits |= 1u << (quad * 4 + q);
+                        const bool cbig = (int)sum > P.col_limit[q];
+                        if (q >= NWA) {
+                            colflag |= cbig;
+                        } else {
+                            // Plane q can clip in this (row quadrant, column job) only if some row
+                            // and some column both exceed their digit-sum limits.
+                            if (__any_sync(0xFFFFFFFFu, cbig)) bits |= 1u << (16 + job * 4 + q);
+                            if (__any_sync(0xFFFFFFFFu, (int)rowmax > P.prow_limit[q])) bits |= 1u << (quad * 4 + q);
+                        }
                     }
+                    const bool rowflag = NWC > 0 && (int)rowmax > P.row_limit;
+                    if (__any_sync(0xFFFFFFFFu, rowflag)) word |= 1u;
+                    if (__any_sync(0xFFFFFFFFu, colflag)) word |= 2u << job;
                 }
-                if (lane == 0) s.pbits[rs][tw] = bits;
+                if (lane == 0) {
+                    s.flags[rs][tw] = word;
+                    s.pbits[rs][tw] = bits;
+                }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {
@@ -547,20 +540,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else {
         set_maxnreg_inc<REG_HIGH>();
         // ------------------------------------------------------------ epilogue
-        // Warpgroup h owns jobs h and h + 2 of every read and two private TMEM buffers,
-        // so the MMA refills one buffer while this warpgroup drains the other, and the
-        // two warpgroups run out of phase.  Warp w reads lane quadrant w & 3; a job's 32
-        // columns are processed as two 16-column halves.
-        const int h = (warp - 4) >> 2;
+        // All 8 warps consume every unit: warp w reads TMEM lane quadrant w & 3 and the
+        // 16-column half hc of each 32-column job.  Two TMEM buffers alternate, so the
+        // MMA fills one while the epilogue drains the other.
         const int quad = warp & 3;
+        const int hc = (warp - 4) >> 2;
         const int r = quad * 32 + lane;             // CTA row = TMEM lane
         const long long row = n0 + r;
-        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + h * HALF_COLS;
-        float acc0[2][32];                          // jobs h and h + 2
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + hc * 16;
+        float acc0[NSUB][16];
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj)
+        for (int j = 0; j < NSUB; ++j)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) acc0[jj][e] = 0.0f;
+            for (int e = 0; e < 16; ++e) acc0[j][e] = 0.0f;
         uint32_t units = 0;
         bool ok = true;
         for (int i = 0; i < MR && ok; ++i) {
@@ -572,86 +564,98 @@ __global__ void __launch_bounds__(THREADS, 1)
             ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.flag_full[rs], (i / RING) & 1, s, err, 7));
             if (!ok) break;
             const float xs = s.xs[sb][r][i % SCB];
+            const uint32_t f0 = *(volatile uint32_t*)&s.flags[rs][0];
+            const uint32_t f1 = *(volatile uint32_t*)&s.flags[rs][1];
             const uint32_t pb = *(volatile uint32_t*)&s.pbits[rs][0] | *(volatile uint32_t*)&s.pbits[rs][1];
+            // Jobs share one copy of the TMEM/correction code (a runtime loop keeps the hot
+            // code small enough for the instruction cache); only the register-resident
+            // scale-and-accumulate step is specialised per job.
 #pragma unroll 1
-            for (int jj = 0; jj < 2; ++jj) {
-                const int j = h + 2 * jj;
-                uint64_t T[2][8];
-                {   // Unit 0: base x.w and the always planes.
-                    const uint32_t bsel = units & 1;
-                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[h][bsel], (units >> 1) & 1, s, err, 9));
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t buf = lane_base + bsel * UNIT_COLS;
-#pragma unroll
-                    for (int ch = 0; ch < 2; ++ch) {
-                        uint32_t vt[16], vp[NA * NWA > 0 ? NA * NWA : 1][16];
-                        tmem_ld16(buf + ch * 16, vt);
-#pragma unroll
-                        for (int k = 0; k < NA * NWA; ++k) tmem_ld16(buf + 32 + k * SUB + ch * 16, vp[k]);
-                        tmem_wait(vt);
-#pragma unroll
-                        for (int k = 0; k < NA * NWA; ++k) tmem_wait(vp[k]);
-                        base_to_float(vt, T[ch]);
-#pragma unroll
-                        for (int k = 0; k < NA * NWA; ++k) {
-                            const int a = k / (NWA > 0 ? NWA : 1), q = k % (NWA > 0 ? NWA : 1);
-                            // Skipped when no row of this quadrant or no column of this job can clip.
-                            if (((pb >> (quad * 4 + q)) & 1u) && ((pb >> (16 + j * 4 + q)) & 1u))
-                                relu_correct(vp[k], T[ch], P.dscale[q], P.offset[q], P.coef[a][q]);
-                        }
-                    }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&s.unit_empty[h][bsel]);
-                    ++units;
-                }
-#pragma unroll
-                for (int c = 0; c < NWC; ++c) {
-                    const int q = NWA + c;
-                    if (!cond_job_flag(pb, q, j)) continue;
-                    const uint32_t bsel = units & 1;
-                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[h][bsel], (units >> 1) & 1, s, err, 10));
-                    if (!ok) break;
-                    tc_fence_after();
-                    if (((pb >> (quad * 4 + q)) & 1u) && ((pb >> (16 + j * 4 + q)) & 1u)) {
-                        const uint32_t buf = lane_base + bsel * UNIT_COLS;
-#pragma unroll
-                        for (int ch = 0; ch < 2; ++ch) {
-                            uint32_t vp[NA > 0 ? NA : 1][16];
-#pragma unroll
-                            for (int a = 0; a < NA; ++a) tmem_ld16(buf + a * SUB + ch * 16, vp[a]);
-#pragma unroll
-                            for (int a = 0; a < NA; ++a) tmem_wait(vp[a]);
-#pragma unroll
-                            for (int a = 0; a < NA; ++a) relu_correct(vp[a], T[ch], P.dscale[q], P.offset[q], P.coef[a][q]);
-                        }
-                    }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&s.unit_empty[h][bsel]);
-                    ++units;
-                }
+            for (int j = 0; j < NSUB; ++j) {
+                const bool flagged = NWC > 0 && job_flagged(NWC, f0, f1, j);
+                uint32_t bsel = units & 1;
+                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[bsel], (units >> 1) & 1, s, err, 9));
                 if (!ok) break;
-                // fl(fl(T * xs) * ws) pushed into cascade level 0 for read i.  The products may
-                // be packed; the accumulation stays scalar (a packed multiply feeding a packed
-                // add was observed to round once, as an FMA, which the reference does not).
-                const float2* wsr = reinterpret_cast<const float2*>(&s.ws[sb][i % SCB][j * SUB]);
-                float v[32];
+                tc_fence_after();
+                uint32_t buf = lane_base + bsel * HALF_COLS;
+                uint64_t T[8];
+                {
+                    // Base x.w and the first always plane of every input slice in one batch.
+                    uint32_t vt[16], v0[NA > 0 ? NA : 1][16];
+                    tmem_ld16(buf, vt);
 #pragma unroll
-                for (int ch = 0; ch < 2; ++ch)
+                    for (int a = 0; a < NA; ++a) tmem_ld16(buf + 32 + a * NWA * SUB, v0[a]);
+                    tmem_wait(vt);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float2 pr = __fmul2_rn(__fmul2_rn(unpack(T[ch][e]), make_float2(xs, xs)), wsr[ch * 8 + e]);
-                        v[ch * 16 + 2 * e] = pr.x;
-                        v[ch * 16 + 2 * e + 1] = pr.y;
+                    for (int a = 0; a < NA; ++a) tmem_wait(v0[a]);
+                    base_to_float(vt, T);
+                    if (NWA > 0 && ((pb >> (quad * 4)) & 1u) && ((pb >> (16 + j * 4)) & 1u)) {
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) relu_correct(v0[a], T, P.dscale[0], P.offset[0], P.coef[a][0]);
                     }
-                if (jj == 0) {
+                }
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) acc0[0][e] = __fadd_rn(acc0[0][e], v[e]);
-                } else {
+                for (int q = 1; q < NWA; ++q) {
+                    // Further always planes: skipped when no row of this quadrant and no column of
+                    // this job can exceed the plane's ADC limit.
+                    if (((pb >> (quad * 4 + q)) & 1u) && ((pb >> (16 + j * 4 + q)) & 1u)) {
+                        uint32_t v1[NA > 0 ? NA : 1][16];
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) acc0[1][e] = __fadd_rn(acc0[1][e], v[e]);
+                        for (int a = 0; a < NA; ++a) tmem_ld16(buf + 32 + (a * NWA + q) * SUB, v1[a]);
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) tmem_wait(v1[a]);
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) relu_correct(v1[a], T, P.dscale[q], P.offset[q], P.coef[a][q]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s.unit_empty[bsel]);
+                ++units;
+                if (flagged) {
+                    bsel = units & 1;
+                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[bsel], (units >> 1) & 1, s, err, 10));
+                    if (!ok) break;
+                    tc_fence_after();
+                    buf = lane_base + bsel * HALF_COLS;
+#pragma unroll
+                    for (int q = 0; q < NWC; ++q) {
+                        uint32_t v1[NA > 0 ? NA : 1][16];
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) tmem_ld16(buf + (a * NWC + q) * SUB, v1[a]);
+#pragma unroll
+                        for (int a = 0; a < NA; ++a) tmem_wait(v1[a]);
+#pragma unroll
+                        for (int a = 0; a < NA; ++a)
+                            relu_correct(v1[a], T, P.dscale[NWA + q], P.offset[NWA + q], P.coef[a][NWA + q]);
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s.unit_empty[bsel]);
+                    ++units;
+                }
+                // fl(fl(T * xs) * ws) pushed into cascade level 0 for read i.  Scalar
+                // round-to-nearest intrinsics: packed f32x2 multiplies followed by an add
+                // were observed to round once (as an FMA), which the reference does not.
+                const float2* wsr = reinterpret_cast<const float2*>(&s.ws[sb][i % SCB][j * SUB + hc * 16]);
+                float v[16];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float2 w2 = wsr[e];
+                    const float2 t2 = unpack(T[e]);
+                    v[2 * e] = __fmul_rn(__fmul_rn(t2.x, xs), w2.x);
+                    v[2 * e + 1] = __fmul_rn(__fmul_rn(t2.y, xs), w2.y);
+                }
+                switch (j) {
+#define MF_ACC(J)                                                         \
+    case J:                                                               \
+        _Pragma("unroll") for (int e = 0; e < 16; ++e) acc0[J][e] = __fadd_rn(acc0[J][e], v[e]); \
+        break;
+                    MF_ACC(0)
+                    MF_ACC(1)
+                    MF_ACC(2)
+                    MF_ACC(3)
+#undef MF_ACC
                 }
             }
             if (!ok) break;
@@ -664,26 +668,26 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int done = i + 1;
             if (done <= args.full && (done & 15) == 0) {
 #pragma unroll
-                for (int jj = 0; jj < 2; ++jj)
+                for (int j = 0; j < NSUB; ++j)
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        const int cl = (h + 2 * jj) * SUB + e;
-                        s.acc1[cl][r] = __fadd_rn(s.acc1[cl][r], acc0[jj][e]);
-                        acc0[jj][e] = 0.0f;
+                    for (int e = 0; e < 16; ++e) {
+                        const int cl = j * SUB + hc * 16 + e;
+                        s.acc1[cl][r] = __fadd_rn(s.acc1[cl][r], acc0[j][e]);
+                        acc0[j][e] = 0.0f;
                     }
             }
         }
         if (ok && row < args.n) {
 #pragma unroll
-            for (int jj = 0; jj < 2; ++jj)
+            for (int j = 0; j < NSUB; ++j)
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int cl = (h + 2 * jj) * SUB + e;
+                for (int e = 0; e < 16; ++e) {
+                    const int cl = j * SUB + hc * 16 + e;
                     const int col = c0 + cl;
                     if (col >= args.col_end || col >= args.out_features) continue;
                     // acc0 + acc1 + acc2 + acc3 (upper levels zero), then the reference's
                     // store into a zero-filled output.
-                    float value = __fadd_rn(acc0[jj][e], s.acc1[cl][r]);
+                    float value = __fadd_rn(acc0[j][e], s.acc1[cl][r]);
                     value = __fadd_rn(value, 0.0f);
                     value = __fadd_rn(value, 0.0f);
                     value = __fadd_rn(0.0f, value);
@@ -799,13 +803,9 @@ bool tc_plan(const mf_config& c, tc::Plan& P) {
         for (int i = 1; i < na; ++i)
             if (pair_clip[clip_a[i]][w] != first) return false;
         if (!first) continue;
-        // Planes that clip often (limit below half the largest dot) are corrected in
-        // every job; the rest only where a digit-sum bound admits a clip.  Base plus
-        // always planes share one 128-column TMEM unit.
         const long long dmax = (long long)rows * amask * c.w_mask[w];
-        const bool often = c.adc_max[w] * 2 < dmax;
-        if (often && (nwa + 1) * na <= 3) always[nwa++] = w;
-        else cond[nwc++] = w;
+        if (c.adc_max[w] * 4 >= dmax * 3) cond[nwc++] = w;
+        else always[nwa++] = w;
     }
     for (int a = 0; a < c.n_in; ++a) {
         bool listed = false;
@@ -815,6 +815,7 @@ bool tc_plan(const mf_config& c, tc::Plan& P) {
     }
     if (na == 0) nwa = nwc = 0;
     if (nwa + nwc > tc::MAXPB || (na > 0 && nwa == 0 && nwc == 0)) return false;
+    if (na > 0 && nwa == 0) return false;   // keep at least one always group (simplifies the slot walk)
     P.na = na;
     P.nwa = nwa;
     P.nwc = nwc;
@@ -825,6 +826,7 @@ bool tc_plan(const mf_config& c, tc::Plan& P) {
     int order[tc::MAXPB];
     for (int i = 0; i < nwa; ++i) order[i] = always[i];
     for (int i = 0; i < nwc; ++i) order[nwa + i] = cond[i];
+    P.row_limit = 1 << 30;
     for (int q = 0; q < nwa + nwc; ++q) {
         const int w = order[q];
         P.w_shift[q] = c.w_shift[w];
@@ -840,15 +842,16 @@ bool tc_plan(const mf_config& c, tc::Plan& P) {
         // D <= Mw * S_a(n) and D <= Ma * S_w(o): below these limits plane q cannot clip.
         P.prow_limit[q] = c.adc_max[w] / c.w_mask[w];
         P.col_limit[q] = c.adc_max[w] / amask;
+        if (q >= nwa) P.row_limit = P.prow_limit[q] < P.row_limit ? P.prow_limit[q] : P.row_limit;
     }
     return true;
 }
 
 // Plan shapes with a compiled kernel: (NA, NWA, NWC).
 static bool tc_shape_supported(int na, int nwa, int nwc) {
-    return (na == 3 && nwa == 1 && nwc == 3) || (na == 3 && nwa == 1 && nwc == 2) ||
-           (na == 3 && nwa == 1 && nwc == 0) || (na == 3 && nwa == 0 && nwc == 3) ||
-           (na == 0 && nwa == 0 && nwc == 0);
+    return (na == 3 && nwa == 2 && nwc == 2) ||
+           (na == 3 && nwa == 2 && nwc == 0) || (na == 3 && nwa == 1 && nwc == 0) ||
+           (na == 3 && nwa == 1 && nwc == 2) || (na == 0 && nwa == 0 && nwc == 0);
 }
 
 bool tc_eligible(const mf_config& c, int32_t m) {
@@ -949,10 +952,10 @@ mf_status tc_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, siz
     const tc::Plan& P = args.plan;
 #define MF_TC(NA_, NWA_, NWC_) \
     if (P.na == NA_ && P.nwa == NWA_ && P.nwc == NWC_) return launch_tc<NA_, NWA_, NWC_>(mx, mw, mxs, mws, args, grid, st)
-    MF_TC(3, 1, 3);
-    MF_TC(3, 1, 2);
+    MF_TC(3, 2, 2);
+    MF_TC(3, 2, 0);
     MF_TC(3, 1, 0);
-    MF_TC(3, 0, 3);
+    MF_TC(3, 1, 2);
     MF_TC(0, 0, 0);
 #undef MF_TC
     set_error("no compiled tcgen05 kernel for plan (%d, %d, %d)", P.na, P.nwa, P.nwc);
