@@ -14,7 +14,8 @@ problem, i.e. strong scaling.
 
 ``--impl reference`` times the reference algorithm's CPU restatement (the
 oracle: restored conductances, FP32 currents, ADC, signed reconstruction,
-scale epilogue) on the host cores, on a bounded prefix of the same rows.
+scale epilogue) on the host cores, on bounded row prefixes of the same
+workload; the full-batch time is extrapolated linearly in rows.
 """
 
 import argparse
@@ -30,8 +31,11 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-METRIC = "simulated MAC/s on 4096^3 sliced INT8 Simulator.mm"
 UNIT = "MAC/s"
+
+
+def metric_name(size):
+    return f"simulated MAC/s on {size}^3 sliced INT8 Simulator.mm"
 
 
 def parse():
@@ -68,34 +72,62 @@ def workload(args):
     return dict(workload=f"Simulator.mm {n}x{k}x{o} INT8 (1,1,2,2,2) ideal", n=n, k=k, o=o,
                 array=[128, 128], rows_per_read=32, adc_bits=[6, 7, 7, 8, 8],
                 input_groups=[1, 32], weight_groups=[32, 1], operands="seeded N(0,1) fp32",
-                l2="inputs 2x64 MiB fp32 exceed the 126 MB L2; L2 also flushed between timed steps")
+                l2=f"inputs 2x{4 * n * k / 2**20:.0f} MiB fp32; L2 (126 MB) flushed by a 256 MiB write "
+                   f"before every timed step")
 
 
 # ------------------------------------------------------------------ CPU leg --
+class OracleSample:
+    """The oracle (the reference CPU algorithm restated in C) on a row prefix.
+
+    One call programs B (restores every conductance) and then runs the rows, so
+    time = fixed + rows * per_row.  Both terms are measured from two prefixes and
+    the full-batch time is extrapolated linearly (work is exactly linear in the
+    rows: every vector is independent).
+    """
+
+    def __init__(self, size, config, budget_s):
+        from oracle import oracle as O
+
+        self.O = O
+        self.size, self.config = size, config
+        self.threads = os.cpu_count() or 1
+        O.set_threads(self.threads)
+        O.lib()
+        a, b = operands(size)
+        self.a, self.b = a.numpy(), b.numpy()
+        t1 = self.time(1)
+        t9 = self.time(9)
+        per_row = max((t9 - t1) / 8, 1e-6)
+        fixed = max(t1 - per_row, 0.0)
+        self.rows = int(max(9, min(size, (budget_s - fixed) / per_row)))
+        self.t1 = t1
+
+    def time(self, rows):
+        start = time.perf_counter()
+        self.O.mm(self.a[:rows], self.b, self.config, physical=True)
+        return time.perf_counter() - start
+
+    def rate(self, t_rows):
+        """Extrapolated full-batch MAC/s from one timing of self.rows rows."""
+        per_row = max((t_rows - self.t1) / (self.rows - 1), 1e-9)
+        fixed = max(self.t1 - per_row, 0.0)
+        full = fixed + per_row * self.size
+        return float(self.size) ** 3 / full, full
+
+    def describe(self, elapsed):
+        return (f"oracle C restatement of the reference CPU algorithm (physical FP32 currents, ADC, "
+                f"reconstruction, scale epilogue) on {self.threads} threads; prefixes of 1 and {self.rows} of "
+                f"{self.size} rows timed ({elapsed:.1f} s), B programmed once per call, full-batch time "
+                f"extrapolated linearly in rows")
+
+
 def cpu_sample(size, budget_s, config):
-    """Time the oracle (reference algorithm restated in C, all host threads) on a row prefix."""
-    import numpy as np
-
-    from oracle import oracle as O
-
-    threads = os.cpu_count() or 1
-    O.set_threads(threads)
-    O.lib()
-    a, b = operands(size)
-    a, b = a.numpy(), b.numpy()
-    rows = 1
-    start = time.perf_counter()
-    O.mm(a[:rows], b, config, physical=True)
-    first = time.perf_counter() - start
-    rows = int(max(1, min(size, budget_s / max(first, 1e-3))))
-    start = time.perf_counter()
-    O.mm(a[:rows], b, config, physical=True)
-    elapsed = time.perf_counter() - start
-    value = rows * size * size / elapsed
-    return dict(value=value, unit=UNIT, cores=threads, kind="port",
-                sample=f"oracle C restatement, physical FP32 path, first {rows} of {size} rows "
-                       f"(B programmed once per sample), {elapsed:.1f} s wall",
-                seconds=elapsed, rows=rows)
+    sample = OracleSample(size, config, budget_s)
+    elapsed = sample.time(sample.rows)
+    value, full = sample.rate(elapsed)
+    return dict(value=value, unit=UNIT, cores=sample.threads, kind="port", sample=sample.describe(elapsed),
+                extrapolated_full_batch_s=full, rows=sample.rows)
 
 
 def reference_arm(args):
@@ -105,34 +137,21 @@ def reference_arm(args):
     if rank != 0:
         return
     config = bench_config(mf)
-    import numpy as np
-
-    from oracle import oracle as O
-
-    threads = os.cpu_count() or 1
-    O.set_threads(threads)
-    size = args.size
-    a, b = operands(size)
-    a, b = a.numpy(), b.numpy()
-    start = time.perf_counter()
-    O.mm(a[:1], b, config, physical=True)
-    one = time.perf_counter() - start
-    budget = max(1.0, 150.0 / max(1, args.steps + args.warmup))
-    rows = int(max(1, min(size, budget / max(one, 1e-3))))
-    times = []
+    budget = max(2.0, 150.0 / max(1, args.steps + args.warmup))
+    sample = OracleSample(args.size, config, budget)
+    rates, times = [], []
     for step in range(args.warmup + args.steps):
-        start = time.perf_counter()
-        O.mm(a[:rows], b, config, physical=True)
+        elapsed = sample.time(sample.rows)
         if step >= args.warmup:
-            times.append(time.perf_counter() - start)
-    per_step = statistics.mean(times)
-    value = rows * size * size / per_step
-    line = dict(metric=METRIC, value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
-                ms_per_step=per_step * 1e3, higher_is_better=True, scaling="strong", vs_baseline=None,
-                dtype="f32 currents / int64 totals", data="synthetic", config=workload(args), impl="reference",
-                cpu_baseline=dict(value=value, unit=UNIT, cores=threads, kind="port",
-                                  sample=f"first {rows} of {size} rows per step (oracle C restatement of the "
-                                         f"reference CPU algorithm, physical FP32 path)"),
+            rates.append(sample.rate(elapsed)[0])
+            times.append(elapsed)
+    value = statistics.mean(rates)
+    line = dict(metric=metric_name(args.size), value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
+                ms_per_step=float(args.size) ** 3 / value * 1e3, higher_is_better=True, scaling="strong",
+                vs_baseline=None, dtype="f32 currents / int64 totals", data="synthetic", config=workload(args),
+                impl="reference",
+                cpu_baseline=dict(value=value, unit=UNIT, cores=sample.threads, kind="port",
+                                  sample=sample.describe(sum(times)) + "; each step one prefix call"),
                 e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
 
@@ -329,7 +348,7 @@ def engine_arm(args):
     achieved_tops = kernel_ops / kernel_s / 1e12
     traffic = profiled_traffic()
     line = dict(
-        metric=METRIC, value=macs / per_step, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+        metric=metric_name(args.size), value=macs / per_step, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
         ms_per_step=per_step * 1e3, higher_is_better=True, scaling="strong", vs_baseline=None,
         dtype="u8 digits / int32 totals / f32 epilogue", data="synthetic", config=workload(args),
         slice_pair_macs_per_s=macs * pairs / per_step,
