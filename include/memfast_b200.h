@@ -115,6 +115,32 @@ mf_status mf_program_weights(const mf_config* cfg, const void* w, int32_t w_dtyp
                              int64_t k, int64_t ldw, void* packed, void* wscale,
                              void* workspace, size_t workspace_bytes, void* stream);
 
+/* Capacity of the library's own scratch for mf_quantize_input_static: 4 MiB,
+ * i.e. 1,048,576 FP32 (or 524,288 FP64) group maxima. */
+#define MF_STATIC_QUANTIZE_SCRATCH_BYTES (4u << 20)
+
+/* mf_quantize_input without a caller workspace (no counterpart in the
+ * reference, which always allocates its temporaries through torch).  Same
+ * arguments, results and errors as mf_quantize_input; the group maxima live in
+ * a fixed device array inside the library instead of `workspace`.
+ *   - For callers that cannot hand out device memory: a plain C host that owns
+ *     only its input and output buffers, or one that must not call cudaMalloc
+ *     between launches because cudaMalloc can wait for the whole device.
+ *   - Neither it nor its set-up allocates device memory.  The first call on
+ *     each device resolves the array's address (cudaGetSymbolAddress); a caller
+ *     that wants no set-up work inside a later phase (for example a stream
+ *     capture) makes one call on that device before the phase begins.
+ *   - Limit: when dynamic scales need more than
+ *     MF_STATIC_QUANTIZE_SCRATCH_BYTES of group maxima (mf_quantize_workspace()
+ *     minus its 256-byte pad), the call fails with MF_ERR_RESOURCE and enqueues
+ *     nothing; use mf_quantize_input with a workspace instead.
+ *   - One array per device: calls that can overlap on a device (other streams,
+ *     other host threads without ordering between them) race on it and give
+ *     wrong codes.  Keep such calls on one stream. */
+mf_status mf_quantize_input_static(const mf_config* cfg, const void* x, int32_t x_dtype, int64_t n,
+                                   int64_t k, int64_t ldx, const void* fixed_scale, void* codes,
+                                   void* xscale, void* stream);
+
 /* Bytes of scratch mf_quantize_input (is_weight=0, shape [n,k]) or
  * mf_program_weights (is_weight=1, shape [o,k]) needs. */
 mf_status mf_quantize_workspace(const mf_config* cfg, int32_t is_weight, int64_t rows,

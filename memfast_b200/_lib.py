@@ -18,6 +18,7 @@ LIBRARY = PACKAGE / "libmemfast_b200.so"
 ABI_VERSION = 1
 MAX_SLICES = 32
 
+STATIC_QUANTIZE_SCRATCH_BYTES = 4 << 20
 MF_OK, MF_ERR_INVALID, MF_ERR_RESOURCE, MF_ERR_CUDA, MF_ERR_UNSUPPORTED = range(5)
 DTYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 3}
 
@@ -71,6 +72,8 @@ _SIGNATURES = {
                                          ct.POINTER(ct.c_size_t)]),
     "mf_quantize_input": (ct.c_int, [ct.POINTER(MFConfig), _VOID, ct.c_int32, ct.c_int64, ct.c_int64,
                                      ct.c_int64, _VOID, _VOID, _VOID, _VOID, ct.c_size_t, _VOID]),
+    "mf_quantize_input_static": (ct.c_int, [ct.POINTER(MFConfig), _VOID, ct.c_int32, ct.c_int64, ct.c_int64,
+                                            ct.c_int64, _VOID, _VOID, _VOID, _VOID]),
     "mf_program_weights": (ct.c_int, [ct.POINTER(MFConfig), _VOID, ct.c_int32, ct.c_int64, ct.c_int64,
                                       ct.c_int64, _VOID, _VOID, _VOID, ct.c_size_t, _VOID]),
     "mf_sliced_mm": (ct.c_int, [ct.POINTER(MFConfig), ct.POINTER(MFSchedule), _VOID, _VOID, _VOID, _VOID,

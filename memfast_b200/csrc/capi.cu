@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -126,6 +127,64 @@ mf_status mf_quantize_input(const mf_config* cfg, const void* x, int32_t x_dtype
     }
     return quantize_input(*cfg, x, x_dtype, n, k, ldx, fixed_scale, codes, xscale, workspace,
                           workspace_bytes, (cudaStream_t)stream);
+}
+
+}  // extern "C"
+
+// Group-maxima scratch of mf_quantize_input_static.  It is a module global so
+// that hosts which own no spare device memory (plain C callers holding only
+// their operands, or loops that must not call cudaMalloc because it can stall
+// the whole device) can still quantise with dynamic scales.  One copy exists
+// per device; its address is looked up once per device and cached.
+namespace {
+constexpr int kStaticDevices = 64;
+__device__ __align__(256) unsigned char g_static_quantize_scratch[MF_STATIC_QUANTIZE_SCRATCH_BYTES];
+std::mutex g_static_mutex;
+void* g_static_scratch[kStaticDevices] = {};
+
+mf_status static_scratch(void** out) {
+    int dev = 0;
+    MF_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev < 0 || dev >= kStaticDevices) {
+        set_error("device %d beyond the %d devices the static scratch table covers", dev, kStaticDevices);
+        return MF_ERR_RESOURCE;
+    }
+    std::lock_guard<std::mutex> lock(g_static_mutex);
+    if (!g_static_scratch[dev]) {
+        void* p = nullptr;
+        MF_CHECK_CUDA(cudaGetSymbolAddress(&p, g_static_quantize_scratch), "static quantize scratch address");
+        g_static_scratch[dev] = p;
+    }
+    *out = g_static_scratch[dev];
+    return MF_OK;
+}
+}  // namespace
+
+extern "C" {
+
+mf_status mf_quantize_input_static(const mf_config* cfg, const void* x, int32_t x_dtype, int64_t n, int64_t k,
+                                   int64_t ldx, const void* fixed_scale, void* codes, void* xscale, void* stream) {
+    mf_status st = check_config(cfg);
+    if (st) return st;
+    if (!x || !codes || !xscale || n < 1 || k < 1 || ldx < k || x_dtype < MF_F32 || x_dtype > MF_F64) {
+        set_error("mf_quantize_input_static: invalid operands (n=%lld k=%lld ldx=%lld dtype=%d)", (long long)n,
+                  (long long)k, (long long)ldx, x_dtype);
+        return MF_ERR_INVALID;
+    }
+    // quantize_workspace_bytes pads by 256 bytes; the maxima themselves need the rest.
+    const size_t need = quantize_workspace_bytes(*cfg, false, n, k) - 256;
+    if (!fixed_scale && need > MF_STATIC_QUANTIZE_SCRATCH_BYTES) {
+        set_error("mf_quantize_input_static: %zu bytes of group maxima exceed the %u-byte static scratch; "
+                  "use mf_quantize_input with a workspace", need, MF_STATIC_QUANTIZE_SCRATCH_BYTES);
+        return MF_ERR_RESOURCE;
+    }
+    void* scratch = nullptr;
+    st = static_scratch(&scratch);
+    if (st) return st;
+    // The shared quantiser clears the maxima it uses (cudaMemsetAsync) before
+    // the max pass, so nothing from an earlier call leaks into this one.
+    return quantize_input(*cfg, x, x_dtype, n, k, ldx, fixed_scale, codes, xscale, scratch,
+                          MF_STATIC_QUANTIZE_SCRATCH_BYTES, (cudaStream_t)stream);
 }
 
 mf_status mf_program_weights(const mf_config* cfg, const void* w, int32_t w_dtype, int64_t o, int64_t k,
