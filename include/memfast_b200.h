@@ -76,7 +76,8 @@ typedef struct {
  * re-declared over this engine's tile shapes).  Every schedule gives
  * bit-identical output. */
 typedef struct {
-    int32_t kernel;     /* 0 auto, 1 generic SIMT, 2 tcgen05 fast path */
+    int32_t kernel;     /* 0 auto, 1 generic SIMT, 2 tcgen05 (packed integer counts when the
+                           configuration fits, else FP8 digit planes), 3 tcgen05 FP8 digit planes */
     int32_t tile_n;     /* vectors per CTA (generic: 8,16,32) */
     int32_t tile_o;     /* output columns per CTA (generic: 32,64,128) */
     int32_t arrays;     /* tiles restored per group in physical mode (>=1) */

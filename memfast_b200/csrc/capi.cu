@@ -207,9 +207,14 @@ static bool use_ideal(const mf_config& c, const mf_schedule& s) {
     return generic_ideal_fits(c, s);
 }
 
-// Kernel 2 (tcgen05) when requested or automatic and the configuration is in its plan.
+// Tensor-core kernels: 2 = packed integer counts when the configuration fits its
+// plan, else FP8 digit planes; 3 = FP8 digit planes; 0 (automatic) = as 2.
+static bool use_packed(const mf_config& c, const mf_schedule& s, int32_t m, int32_t stable) {
+    return (s.kernel == 0 || s.kernel == 2) && !stable && tc_packed_eligible(c, m);
+}
+
 static bool use_tc(const mf_config& c, const mf_schedule& s, int32_t m, int32_t stable) {
-    return (s.kernel == 0 || s.kernel == 2) && !stable && tc_eligible(c, m);
+    return (s.kernel == 0 || s.kernel == 2 || s.kernel == 3) && !stable && tc_eligible(c, m);
 }
 
 static mf_schedule schedule_or_default(const mf_schedule* s) {
@@ -226,7 +231,8 @@ mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedu
         return MF_ERR_INVALID;
     }
     mf_schedule s = schedule_or_default(schedule);
-    if (use_tc(*cfg, s, m, 0)) *bytes = tc_workspace_bytes(*cfg, m, p);
+    if (use_packed(*cfg, s, m, 0)) *bytes = tc_packed_workspace_bytes(*cfg, n, m, p, tile_end - tile_begin);
+    else if (use_tc(*cfg, s, m, 0)) *bytes = tc_workspace_bytes(*cfg, m, p);
     else *bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, tile_end - tile_begin);
     return MF_OK;
 }
@@ -254,6 +260,8 @@ mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const 
     mf_schedule s = schedule_or_default(schedule);
     MMArgs a{codes, xscale, packed, wscale, bias, out, n, m, p, out_features, ldo, tile_begin, tile_end,
              seed, event, vector_offset, stable};
+    if (use_packed(*cfg, s, m, stable))
+        return tc_packed_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
     if (use_tc(*cfg, s, m, stable)) return tc_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
     if (use_ideal(*cfg, s)) return generic_ideal(*cfg, s, a, (cudaStream_t)stream);
     return physical(*cfg, s, a, workspace, workspace_bytes, (cudaStream_t)stream);
@@ -269,9 +277,12 @@ mf_status mf_query(const mf_config* cfg, const mf_schedule* schedule, int64_t n,
     }
     mf_schedule s = schedule_or_default(schedule);
     memset(out, 0, sizeof(*out));
-    if (use_tc(*cfg, s, m, 0)) {
+    if (use_packed(*cfg, s, m, 0)) {
+        out->workspace_bytes = tc_packed_workspace_bytes(*cfg, n, m, p, p);
+        out->threads = tc_packed_threads();
+    } else if (use_tc(*cfg, s, m, 0)) {
         out->workspace_bytes = tc_workspace_bytes(*cfg, m, p);
-        out->threads = 384;
+        out->threads = tc_block_threads();
     } else {
         out->workspace_bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, p);
         out->threads = 256;

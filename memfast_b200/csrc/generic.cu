@@ -61,9 +61,18 @@ __device__ __forceinline__ uint32_t digit_of(CodeT code, int shift, int mask) {
     return (uint32_t)(((long long)code >> shift) & mask);
 }
 
+// Restricts a launch to the output tiles a tensor-core kernel flagged for an
+// exact rerun: flags[(col - tile_begin * C) / cols][row / rows] != 0.  A null
+// `flags` runs every tile.
+struct TileFilter {
+    const unsigned* flags;
+    int rows, cols, row_tiles;
+};
+
 // ------------------------------------------------------------ ideal kernel --
 template <typename CodeT, typename TotT, typename OutT, typename ScaleT>
-__global__ void __launch_bounds__(THREADS) ideal_kernel(Layout L, MMArgs a, int power, long long full) {
+__global__ void __launch_bounds__(THREADS) ideal_kernel(Layout L, MMArgs a, int power, long long full,
+                                                        TileFilter filter) {
     extern __shared__ __align__(16) uint32_t smem[];
     const int R4 = (L.rows + 3) >> 2;
     uint32_t* sA = smem;                               // [n_in][32][R4]
@@ -78,6 +87,10 @@ __global__ void __launch_bounds__(THREADS) ideal_kernel(Layout L, MMArgs a, int 
     const long long col_end = (long long)a.tile_end * L.C;
     const int MR = a.m * L.reads;
     const long long row_stride = (long long)a.m * L.R;
+    if (filter.flags) {
+        const long long tr = v0 / filter.rows, tc = (col0 - (long long)a.tile_begin * L.C) / filter.cols;
+        if (!filter.flags[tc * filter.row_tiles + tr]) return;   // uniform across the CTA
+    }
 
     Cascade<OutT> acc[2][4];
 #pragma unroll
@@ -451,7 +464,7 @@ Physics make_physics(const mf_config& c) {
 }
 
 template <typename OutT, typename ScaleT>
-mf_status launch_ideal_t(const mf_config& c, const MMArgs& a, cudaStream_t st) {
+mf_status launch_ideal_t(const mf_config& c, const MMArgs& a, cudaStream_t st, TileFilter filter = TileFilter{}) {
     Layout L = make_layout(c);
     const int MR = a.m * c.reads;
     const int power = cascade_power(MR);
@@ -465,7 +478,7 @@ mf_status launch_ideal_t(const mf_config& c, const MMArgs& a, cudaStream_t st) {
         auto kern = ideal_kernel<CODE, TOT, OutT, ScaleT>;                                           \
         MF_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), \
                       "ideal kernel smem attribute");                                                \
-        kern<<<grid, THREADS, smem, st>>>(L, a, power, full);                                         \
+        kern<<<grid, THREADS, smem, st>>>(L, a, power, full, filter);                                 \
     } while (0)
     if (c.wide_codes) {
         if (small_totals) MF_IDEAL(long long, int); else MF_IDEAL(long long, long long);
@@ -542,6 +555,16 @@ mf_status generic_ideal(const mf_config& c, const mf_schedule&, const MMArgs& a,
         return c.wide ? launch_ideal_t<double, double>(c, a, st) : launch_ideal_t<double, float>(c, a, st);
     }
     return c.wide ? launch_ideal_t<double, double>(c, a, st) : launch_ideal_t<float, float>(c, a, st);
+}
+
+mf_status generic_ideal_tiles(const mf_config& c, const MMArgs& a, const unsigned* flags, int rows, int cols,
+                              int row_tiles, cudaStream_t st) {
+    if (rows % IDEAL_TV || cols % IDEAL_TC) {
+        set_error("tile filter %dx%d is not a multiple of the generic tile", rows, cols);
+        return MF_ERR_INVALID;
+    }
+    const TileFilter filter{flags, rows, cols, row_tiles};
+    return c.wide ? launch_ideal_t<double, double>(c, a, st, filter) : launch_ideal_t<float, float>(c, a, st, filter);
 }
 
 size_t physical_workspace_bytes(const mf_config& c, const mf_schedule& s, int32_t m, int32_t tiles) {

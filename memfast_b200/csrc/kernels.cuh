@@ -1,6 +1,7 @@
 // Internal host-side entry points shared by the C ABI and the kernel files.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -46,14 +47,33 @@ bool exact_integer_counts(const mf_config& c);
 // Generic SIMT engine (all configurations).
 bool generic_ideal_fits(const mf_config& c, const mf_schedule& s);
 mf_status generic_ideal(const mf_config& c, const mf_schedule& s, const MMArgs& a, cudaStream_t st);
+// The same product restricted to the rows x cols output tiles whose flag is set
+// (flags[col_tile * row_tiles + row_tile], device memory).
+mf_status generic_ideal_tiles(const mf_config& c, const MMArgs& a, const unsigned* flags, int rows, int cols,
+                              int row_tiles, cudaStream_t st);
 size_t physical_workspace_bytes(const mf_config& c, const mf_schedule& s, int32_t m, int32_t tiles);
 mf_status physical(const mf_config& c, const mf_schedule& s, const MMArgs& a, void* workspace,
                    size_t ws_bytes, cudaStream_t st);
 
-// tcgen05 / TMEM fast path (ideal INT8 configurations, tc_ideal.cu).
+// Shared by the tensor-core kernels (tc_common.cu).
+mf_status tc_weights_kmajor(const void* packed, uint8_t* out, int m, int p, int R, int C, cudaStream_t st);
+mf_status tc_make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int bytes, uint64_t inner,
+                      uint64_t outer, uint64_t stride, uint32_t box_inner, uint32_t box_outer,
+                      CUtensorMapSwizzle swizzle);
+mf_status tc_error_word(unsigned** word);
+mf_status tc_take_error(unsigned* code);
+
+// tcgen05 / TMEM fast path with FP8 digit planes (ideal INT8 configurations, tc_ideal.cu).
 bool tc_eligible(const mf_config& c, int32_t m);
 size_t tc_workspace_bytes(const mf_config& c, int32_t m, int32_t p);
+int tc_block_threads();
 mf_status tc_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st);
-mf_status tc_take_error(unsigned* code);
+
+// tcgen05 / TMEM fast path with packed integer counts (tc_packed.cu).
+bool tc_packed_eligible(const mf_config& c, int32_t m);
+size_t tc_packed_workspace_bytes(const mf_config& c, int64_t n, int32_t m, int32_t p, int32_t tiles);
+int tc_packed_threads();
+mf_status tc_packed_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, size_t ws_bytes,
+                              cudaStream_t st);
 
 }  // namespace mf

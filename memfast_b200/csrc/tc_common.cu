@@ -1,0 +1,100 @@
+// Host-side pieces shared by the tensor-core kernels: the K-major weight copy
+// that TMA reads, tensor-map encoding, and the device error word that bounded
+// waits write when they give up.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mf {
+namespace {
+
+// Weight codes [m, p, R, C] -> K-major [p*C, m*R] (8-bit, same bytes).
+__global__ void weights_kmajor_kernel(const uint8_t* packed, uint8_t* out, int m, int p, int R, int C) {
+    __shared__ uint8_t tile[32][33];
+    const long long k0 = (long long)blockIdx.x * 32, o0 = (long long)blockIdx.y * 32;
+    const long long K = (long long)m * R, O = (long long)p * C;
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const long long k = k0 + j, o = o0 + threadIdx.x;
+        uint8_t v = 0;
+        if (k < K && o < O) {
+            const long long arr = k / R, r = k % R, t = o / C, c = o % C;
+            v = packed[((arr * p + t) * R + r) * C + c];
+        }
+        tile[j][threadIdx.x] = v;
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const long long o = o0 + j, k = k0 + threadIdx.x;
+        if (k < K && o < O) out[o * K + k] = tile[threadIdx.x][j];
+    }
+}
+
+typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    }
+    return fn;
+}
+
+__device__ unsigned g_tc_error = 0;
+
+}  // namespace
+
+mf_status tc_weights_kmajor(const void* packed, uint8_t* out, int m, int p, int R, int C, cudaStream_t st) {
+    const long long K = (long long)m * R, O = (long long)p * C;
+    dim3 grid((unsigned)((K + 31) / 32), (unsigned)((O + 31) / 32));
+    weights_kmajor_kernel<<<grid, dim3(32, 8), 0, st>>>(static_cast<const uint8_t*>(packed), out, m, p, R, C);
+    MF_LAUNCH_CHECK("weights_kmajor_kernel");
+    return MF_OK;
+}
+
+mf_status tc_make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int bytes, uint64_t inner,
+                      uint64_t outer, uint64_t stride, uint32_t box_inner, uint32_t box_outer,
+                      CUtensorMapSwizzle swizzle) {
+    EncodeTiled fn = encoder();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled unavailable");
+        return MF_ERR_CUDA;
+    }
+    if (((uintptr_t)base & 15) || (stride * bytes) % 16) {
+        set_error("tensor map needs 16-byte aligned base and row stride");
+        return MF_ERR_INVALID;
+    }
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {stride * bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t elem[2] = {1, 1};
+    CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return MF_ERR_CUDA;
+    }
+    return MF_OK;
+}
+
+mf_status tc_error_word(unsigned** word) {
+    MF_CHECK_CUDA(cudaGetSymbolAddress((void**)word, g_tc_error), "error symbol");
+    return MF_OK;
+}
+
+mf_status tc_take_error(unsigned* code) {
+    unsigned value = 0, zero = 0;
+    MF_CHECK_CUDA(cudaMemcpyFromSymbol(&value, g_tc_error, sizeof(value)), "read device error");
+    if (value) MF_CHECK_CUDA(cudaMemcpyToSymbol(g_tc_error, &zero, sizeof(zero)), "clear device error");
+    *code = value;
+    return MF_OK;
+}
+
+}  // namespace mf

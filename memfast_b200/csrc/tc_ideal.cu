@@ -21,14 +21,14 @@
 // CPU cascade order in registers (simulator.py:578-585), so no partial ever
 // reaches HBM.
 //
-// Warp roles (384 threads, 1 CTA per SM, 128 rows x 128 columns per CTA):
+// Warp roles (128 + 32 * EPI_WARPS threads, 1 CTA per SM, 128 rows x 128 columns per CTA):
 //   warp 0      TMA producer: code tiles of x [128 x 32] and w [128 x 32] per read
 //   warp 1      TMEM owner and MMA issuer (one elected thread)
 //   warps 2-3   transform: digit planes in shared memory (elementwise on the
 //               swizzled tiles), conditional-pair flags, per-read scale rings
-//   warps 4-11  epilogue: 2 warps per TMEM lane quadrant, 16 columns of every
-//               32-column job each; cascade level 0 in registers, level 1 in
-//               shared memory
+//   warps 4..   epilogue: EPI_WARPS / 4 warps per TMEM lane quadrant, EC columns
+//               of every 32-column job each; cascade level 0 in registers,
+//               level 1 in shared memory
 // Every mbarrier wait is bounded; on timeout the CTA records an error code,
 // waits (bounded) for its own TMA loads and MMAs, frees its TMEM and exits.
 #include <cuda.h>
@@ -37,6 +37,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tcgen05.cuh"
 
 namespace mf {
 namespace tc {
@@ -52,17 +53,21 @@ constexpr int SCB = 4;           // reads per scale block
 constexpr int SCRING = 4;        // scale blocks in flight
 constexpr int MAXPA = 3;         // max clip-capable input-slice planes
 constexpr int MAXPB = 4;         // max clip-capable weight-slice planes
-constexpr int THREADS = 384;     // 12 warps
+constexpr int EPI_WARPS = 16;    // epilogue warps: EPI_WARPS / 4 per TMEM lane quadrant
+constexpr int EC = SUB / (EPI_WARPS / 4);   // columns of a job per epilogue thread
+constexpr int THREADS = 128 + 32 * EPI_WARPS;
 constexpr int TILE = BM * KR;    // 4096 bytes: one [128 x 32] 8-bit tile
 constexpr int HALF_COLS = 256;   // TMEM columns per half
 // Register split between warpgroup 0 (producer, MMA, transform) and the two
 // epilogue warpgroups.  setmaxnreg.inc draws on the registers the block was
-// launched with, so 128 * REG_LOW + 256 * REG_HIGH must not exceed
+// launched with, so 128 * REG_LOW + 32 * EPI_WARPS * REG_HIGH must not exceed
 // THREADS * (registers per thread at launch); the host checks this before
 // every launch (launch_tc), because an increase that cannot be met never returns.
-constexpr int REG_LOW = 88;
-constexpr int REG_HIGH = 208;
-static_assert(128 * REG_LOW + 256 * REG_HIGH <= THREADS * 168, "register split exceeds the launch pool");
+constexpr int LAUNCH_REGS = (65536 / THREADS) / 8 * 8;
+constexpr int REG_LOW = EPI_WARPS == 16 ? 56 : 88;
+constexpr int REG_HIGH = EPI_WARPS == 16 ? 104 : 208;
+static_assert(128 * REG_LOW + 32 * EPI_WARPS * REG_HIGH <= THREADS * LAUNCH_REGS,
+              "register split exceeds the launch pool");
 
 // Shared memory plan (1024-aligned tiles first).
 struct Smem {
@@ -92,6 +97,7 @@ struct Plan {
     float coef[MAXPA][MAXPB];          // -(s_a s_w) * 2^k_w
     float dscale[MAXPB];               // 2^(18 - k_w)
     float offset[MAXPB];               // -m_w * 2^-k_w
+    float thresh[MAXPB];               // m_w * 2^-18: D * 2^-18 above it clips
     int row_limit;                     // conditional: flag a row when S_a(n) > row_limit
     int col_limit[MAXPB];              // plane q can clip in column o only if S_wq(o) > col_limit[q]
     int prow_limit[MAXPB];             // plane q can clip in row n only if max_a S_a(n) > prow_limit[q]
@@ -110,167 +116,7 @@ struct Args {
     unsigned* error;        // device error word
 };
 
-// ------------------------------------------------------------------ PTX helpers
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait: about 2 s of clock64, or until another role aborted the CTA.
-__device__ __forceinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, Smem& s, unsigned* error,
-                                            unsigned code) {
-    const long long start = clock64();
-    while (true) {
-        if (mbar_try(bar, parity)) return true;
-        if (*(volatile int*)&s.abort) return false;
-        if (clock64() - start > 4000000000LL) {
-            atomicCAS(error, 0u, code);
-            *(volatile int*)&s.abort = 1;
-            return false;
-        }
-        __nanosleep(32);
-    }
-}
-
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Smem& s, unsigned* error,
-                                          unsigned code) {
-    if (mbar_try(bar, parity)) return true;
-    return mbar_wait_slow(bar, parity, s, error, code);
-}
-
-// Bounded wait that ignores the abort flag (drains own work before exit).
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-    const long long start = clock64();
-    while (!mbar_try(bar, parity)) {
-        if (clock64() - start > 4000000000LL) return;
-        __nanosleep(256);
-    }
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
-}
-
-// K-major, 32-byte swizzle: rows of 32 B, 8-row atoms of 256 B (SBO), version 1.
-__device__ __forceinline__ uint64_t desc_sw32(const void* tile) {
-    const uint64_t addr = smem_u32(tile);
-    uint64_t d = 0;
-    d |= (addr >> 4) & 0x3FFFull;            // start address
-    d |= (uint64_t)1 << 16;                  // leading byte offset (unused when swizzled)
-    d |= (uint64_t)(256 >> 4) << 32;         // stride byte offset: 8 rows x 32 B
-    d |= (uint64_t)1 << 46;                  // descriptor version (sm_100)
-    d |= (uint64_t)6 << 61;                  // SWIZZLE_32B
-    return d;
-}
-
-// Instruction descriptors (M = 128, K-major A and B, dense).
-__host__ __device__ constexpr uint32_t idesc_i8(int n, bool b_signed) {
-    return (2u << 4)                       // D = S32
-           | (1u << 7)                     // A = s8
-           | ((b_signed ? 1u : 0u) << 10)  // B = s8 / u8
-           | ((uint32_t)(n >> 3) << 17)    // N
-           | ((uint32_t)(BM >> 4) << 24);  // M
-}
-__host__ __device__ constexpr uint32_t idesc_e4m3(int n) {
-    return (1u << 4)                       // D = F32
-           | (0u << 7) | (0u << 10)        // A = B = E4M3
-           | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_i8(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc) {
-    asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, 0;" ::"r"(tmem), "l"(a), "l"(b), "r"(idesc));
-}
-
-__device__ __forceinline__ void mma_f8(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc) {
-    asm volatile("tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, 0;" ::"r"(tmem), "l"(a), "l"(b),
-                 "r"(idesc));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-
-// 32 consecutive TMEM columns of this thread's lane.  The values are only valid
-// after tmem_wait(), which takes the registers as operands so that no use can be
-// scheduled ahead of the wait.
-__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(addr));
-}
-
-__device__ __forceinline__ void tmem_wait(uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.wait::ld.sync.aligned;"
-        : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-          "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
-          "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
-          "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
-        :
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(addr));
-}
-
-__device__ __forceinline__ void tmem_wait(uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.wait::ld.sync.aligned;"
-        : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-          "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
-        :
-        : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+using namespace tg;
 
 __device__ __forceinline__ float fma_sat(float a, float b, float c) {
     float d;
@@ -278,10 +124,6 @@ __device__ __forceinline__ float fma_sat(float a, float b, float c) {
     return d;
 }
 
-template <int N>
-__device__ __forceinline__ void set_maxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
-template <int N>
-__device__ __forceinline__ void set_maxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
 
 __device__ __forceinline__ bool job_flagged(int nwc, uint32_t f0, uint32_t f1, int j) {
     const uint32_t f = f0 | f1;
@@ -291,10 +133,11 @@ __device__ __forceinline__ bool job_flagged(int nwc, uint32_t f0, uint32_t f1, i
 // T is kept as packed FP32 pairs (b64) so the f32x2 instructions need no moves.
 // T from the x.w accumulator: |x.w| < 2^22, so 1.5*2^23 + x.w holds the integer
 // exactly in its mantissa and subtracting 1.5*2^23 recovers it.
-__device__ __forceinline__ void base_to_float(const uint32_t (&v)[16], uint64_t (&T)[8]) {
+template <int E>
+__device__ __forceinline__ void base_to_float(const uint32_t (&v)[E], uint64_t (&T)[E / 2]) {
     const uint64_t magic = 0xCB400000CB400000ull;    // (-1.5*2^23, -1.5*2^23)
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
+    for (int e = 0; e < E / 2; ++e)
         asm("{\n\t.reg .b32 a, b;\n\t.reg .b64 p;\n\t"
             "add.s32 a, %1, 0x4B400000;\n\t"
             "add.s32 b, %2, 0x4B400000;\n\t"
@@ -306,11 +149,13 @@ __device__ __forceinline__ void base_to_float(const uint32_t (&v)[16], uint64_t 
 
 // T -= s_a s_w relu(D - m) for one pair plane; D arrives as D * 2^-18, and
 // fma.sat gives relu(D - m) * 2^-k exactly (k chosen on the host).
-__device__ __forceinline__ void relu_correct(const uint32_t (&v)[16], uint64_t (&T)[8], float ds, float off, float cf) {
+template <int E>
+__device__ __forceinline__ void relu_correct(const uint32_t (&v)[E], uint64_t (&T)[E / 2], float ds, float off,
+                                             float cf) {
     uint64_t c2;
     asm("mov.b64 %0, {%1, %1};" : "=l"(c2) : "f"(cf));
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
+    for (int e = 0; e < E / 2; ++e)
         asm("{\n\t.reg .f32 y0, y1;\n\t.reg .b64 y;\n\t"
             "fma.rn.sat.f32 y0, %1, %3, %4;\n\t"
             "fma.rn.sat.f32 y1, %2, %3, %4;\n\t"
@@ -324,6 +169,39 @@ __device__ __forceinline__ float2 unpack(uint64_t t) {
     float2 r;
     asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(t));
     return r;
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Largest D * 2^-18 over this thread's E columns of NA input-slice planes (all
+// values are non-negative and exact, so comparing it with m * 2^-18 tells
+// exactly whether any of them clips).
+template <int NA, int E>
+__device__ __forceinline__ float planes_max(const uint32_t (&v)[NA > 0 ? NA : 1][E]) {
+    float m[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        if (NA >= 3) {
+            m[e] = max3(__uint_as_float(v[0][e]), __uint_as_float(v[1][e]), __uint_as_float(v[2][e]));
+#pragma unroll
+            for (int a = 3; a < NA; ++a) m[e] = fmaxf(m[e], __uint_as_float(v[a][e]));
+        } else {
+            m[e] = __uint_as_float(v[0][e]);
+#pragma unroll
+            for (int a = 1; a < NA; ++a) m[e] = fmaxf(m[e], __uint_as_float(v[a][e]));
+        }
+    }
+    if (E == 16) {
+        const float t0 = max3(m[0], m[1], m[2]), t1 = max3(m[3], m[4], m[5]), t2 = max3(m[6], m[7], m[8]);
+        const float t3 = max3(m[9], m[10], m[11]), t4 = max3(m[12], m[13], m[14]);
+        return fmaxf(max3(t0, t1, t2), max3(t3, t4, m[E - 1]));
+    }
+    const float t0 = max3(m[0], m[1], m[2]), t1 = max3(m[3], m[4], m[5]);
+    return max3(t0, t1, fmaxf(m[6], m[7]));
 }
 
 // ------------------------------------------------------------------- kernel
@@ -355,15 +233,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int i = 0; i < RING; ++i) {
             mbar_init(&s.flag_full[i], 2);
-            mbar_init(&s.flag_empty[i], 8);
+            mbar_init(&s.flag_empty[i], EPI_WARPS);
         }
         for (int i = 0; i < SCRING; ++i) {
             mbar_init(&s.sc_full[i], 1);
-            mbar_init(&s.sc_empty[i], 8);
+            mbar_init(&s.sc_empty[i], EPI_WARPS);
         }
         for (int h = 0; h < 2; ++h) {
             mbar_init(&s.unit_full[h], 1);
-            mbar_init(&s.unit_empty[h], 8);
+            mbar_init(&s.unit_empty[h], EPI_WARPS);
         }
         mbar_init(&s.drained, 1);
         s.abort = 0;
@@ -377,9 +255,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         prefetch_map(&map_ws);
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s.tmem_base)),
-                     "r"(512));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        tmem_alloc(&s.tmem_base, 512);
     }
     tc_fence_before();
     __syncthreads();
@@ -395,14 +271,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int i = 0; i < MR; ++i) {
                     if (i % SCB == 0) {
                         const int b = i / SCB, sb = b % SCRING;
-                        if (!mbar_wait(&s.sc_empty[sb], ((b / SCRING) & 1) ^ 1, s, err, 12)) break;
+                        if (!mbar_wait(&s.sc_empty[sb], ((b / SCRING) & 1) ^ 1, &s.abort, err, 12)) break;
                         mbar_expect_tx(&s.sc_full[sb], (BM + BN) * SCB * 4);
                         tma_load_2d(s.xs[sb], &map_xs, i, (int)n0, &s.sc_full[sb]);
                         tma_load_2d(s.ws[sb], &map_ws, c0, i, &s.sc_full[sb]);
                         scissued = b + 1;
                     }
                     const int st = i % STAGES;
-                    if (!mbar_wait(&s.empty[st], ((i / STAGES) & 1) ^ 1, s, err, 1)) break;
+                    if (!mbar_wait(&s.empty[st], ((i / STAGES) & 1) ^ 1, &s.abort, err, 1)) break;
                     mbar_expect_tx(&s.full[st], 2 * TILE);
                     tma_load_2d(s.x[st], &map_x, i * KR, (int)n0, &s.full[st]);
                     tma_load_2d(s.w[st], &map_w, i * KR, c0, &s.full[st]);
@@ -417,14 +293,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else if (warp == 1) {
             // -------------------------------------------------------- MMA issuer
             if (lane == 0) {
-                const uint32_t id_base = idesc_i8(SUB, P.b_signed != 0);
-                const uint32_t id_always = idesc_e4m3(SUB * (NWA > 0 ? NWA : 1));
-                const uint32_t id_cond = idesc_e4m3(SUB * (NWC > 0 ? NWC : 1));
+                const uint32_t id_base = idesc_i8(BM, SUB, true, P.b_signed != 0);
+                const uint32_t id_always = idesc_e4m3(BM, SUB * (NWA > 0 ? NWA : 1));
+                const uint32_t id_cond = idesc_e4m3(BM, SUB * (NWC > 0 ? NWC : 1));
                 uint32_t units = 0;   // units issued; unit u uses buffer u & 1
                 bool ok = true;
                 for (int i = 0; i < MR && ok; ++i) {
                     const int st = i % STAGES;
-                    if (!mbar_wait(&s.ready[st], (i / STAGES) & 1, s, err, 2)) break;
+                    if (!mbar_wait(&s.ready[st], (i / STAGES) & 1, &s.abort, err, 2)) break;
                     tc_fence_after();
                     const uint32_t f0 = *(volatile uint32_t*)&s.flags[i % RING][0];
                     const uint32_t f1 = *(volatile uint32_t*)&s.flags[i % RING][1];
@@ -432,25 +308,25 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < NSUB; ++j) {
                         uint32_t b = units & 1;
-                        if (!mbar_wait(&s.unit_empty[b], ((units >> 1) & 1) ^ 1, s, err, 3)) { ok = false; break; }
+                        if (!mbar_wait(&s.unit_empty[b], ((units >> 1) & 1) ^ 1, &s.abort, err, 3)) { ok = false; break; }
                         tc_fence_after();
                         uint32_t buf = tmem + b * HALF_COLS;
-                        mma_i8(buf, dx, desc_sw32(s.w[st] + j * SUB * KR), id_base);
+                        mma_i8(buf, dx, desc_sw32(s.w[st] + j * SUB * KR), id_base, 0);
 #pragma unroll
                         for (int a = 0; a < NA; ++a)
                             mma_f8(buf + 32 + a * NWA * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][0]),
-                                   id_always);
+                                   id_always, 0);
                         mma_commit(&s.unit_full[b]);
                         ++units;
                         if (NWC > 0 && job_flagged(NWC, f0, f1, j)) {
                             b = units & 1;
-                            if (!mbar_wait(&s.unit_empty[b], ((units >> 1) & 1) ^ 1, s, err, 4)) { ok = false; break; }
+                            if (!mbar_wait(&s.unit_empty[b], ((units >> 1) & 1) ^ 1, &s.abort, err, 4)) { ok = false; break; }
                             tc_fence_after();
                             buf = tmem + b * HALF_COLS;
 #pragma unroll
                             for (int a = 0; a < NA; ++a)
                                 mma_f8(buf + a * NWC * SUB, desc_sw32(s.ap[st][a]), desc_sw32(s.bp[st][j][NWA]),
-                                       id_cond);
+                                       id_cond, 0);
                             mma_commit(&s.unit_full[b]);
                             ++units;
                         }
@@ -466,8 +342,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int tw = warp - 2;              // 0 or 1
             for (int i = 0; i < MR; ++i) {
                 const int st = i % STAGES, rs = i % RING;
-                bool ok = mbar_wait(&s.full[st], (i / STAGES) & 1, s, err, 5);
-                ok = ok && mbar_wait(&s.flag_empty[rs], ((i / RING) & 1) ^ 1, s, err, 6);
+                bool ok = mbar_wait(&s.full[st], (i / STAGES) & 1, &s.abort, err, 5);
+                ok = ok && mbar_wait(&s.flag_empty[rs], ((i / RING) & 1) ^ 1, &s.abort, err, 6);
                 if (!__all_sync(0xFFFFFFFFu, ok)) break;
                 uint32_t word = 0, bits = 0;
 #pragma unroll 1
@@ -540,28 +416,28 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else {
         set_maxnreg_inc<REG_HIGH>();
         // ------------------------------------------------------------ epilogue
-        // All 8 warps consume every unit: warp w reads TMEM lane quadrant w & 3 and the
-        // 16-column half hc of each 32-column job.  Two TMEM buffers alternate, so the
-        // MMA fills one while the epilogue drains the other.
+        // Every epilogue warp consumes every unit: warp w reads TMEM lane quadrant w & 3
+        // and the EC-column slice hc of each 32-column job.  Two TMEM buffers alternate,
+        // so the MMA fills one while the epilogue drains the other.
         const int quad = warp & 3;
-        const int hc = (warp - 4) >> 2;
+        const int hc = (warp - 4) >> 2;             // which EC-column slice of every job
         const int r = quad * 32 + lane;             // CTA row = TMEM lane
         const long long row = n0 + r;
-        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + hc * 16;
-        float acc0[NSUB][16];
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + hc * EC;
+        float acc0[NSUB][EC];
 #pragma unroll
         for (int j = 0; j < NSUB; ++j)
 #pragma unroll
-            for (int e = 0; e < 16; ++e) acc0[j][e] = 0.0f;
+            for (int e = 0; e < EC; ++e) acc0[j][e] = 0.0f;
         uint32_t units = 0;
         bool ok = true;
         for (int i = 0; i < MR && ok; ++i) {
             const int rs = i % RING, b = i / SCB, sb = b % SCRING;
             if (i % SCB == 0) {
-                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.sc_full[sb], (b / SCRING) & 1, s, err, 13));
+                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.sc_full[sb], (b / SCRING) & 1, &s.abort, err, 13));
                 if (!ok) break;
             }
-            ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.flag_full[rs], (i / RING) & 1, s, err, 7));
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.flag_full[rs], (i / RING) & 1, &s.abort, err, 7));
             if (!ok) break;
             const float xs = s.xs[sb][r][i % SCB];
             const uint32_t f0 = *(volatile uint32_t*)&s.flags[rs][0];
@@ -574,22 +450,25 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int j = 0; j < NSUB; ++j) {
                 const bool flagged = NWC > 0 && job_flagged(NWC, f0, f1, j);
                 uint32_t bsel = units & 1;
-                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[bsel], (units >> 1) & 1, s, err, 9));
+                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[bsel], (units >> 1) & 1, &s.abort, err, 9));
                 if (!ok) break;
                 tc_fence_after();
                 uint32_t buf = lane_base + bsel * HALF_COLS;
-                uint64_t T[8];
+                uint64_t T[EC / 2];
                 {
                     // Base x.w and the first always plane of every input slice in one batch.
-                    uint32_t vt[16], v0[NA > 0 ? NA : 1][16];
-                    tmem_ld16(buf, vt);
+                    uint32_t vt[EC], v0[NA > 0 ? NA : 1][EC];
+                    tmem_ld(buf, vt);
 #pragma unroll
-                    for (int a = 0; a < NA; ++a) tmem_ld16(buf + 32 + a * NWA * SUB, v0[a]);
+                    for (int a = 0; a < NA; ++a) tmem_ld(buf + 32 + a * NWA * SUB, v0[a]);
                     tmem_wait(vt);
 #pragma unroll
                     for (int a = 0; a < NA; ++a) tmem_wait(v0[a]);
                     base_to_float(vt, T);
-                    if (NWA > 0 && ((pb >> (quad * 4)) & 1u) && ((pb >> (16 + j * 4)) & 1u)) {
+                    // Corrections only where some D of the warp exceeds m (the relu is zero
+                    // elsewhere, so skipping it there changes nothing).
+                    if (NWA > 0 && ((pb >> (quad * 4)) & 1u) && ((pb >> (16 + j * 4)) & 1u) &&
+                        __any_sync(0xFFFFFFFFu, planes_max<NA, EC>(v0) > P.thresh[0])) {
 #pragma unroll
                         for (int a = 0; a < NA; ++a) relu_correct(v0[a], T, P.dscale[0], P.offset[0], P.coef[a][0]);
                     }
@@ -599,13 +478,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                     // Further always planes: skipped when no row of this quadrant and no column of
                     // this job can exceed the plane's ADC limit.
                     if (((pb >> (quad * 4 + q)) & 1u) && ((pb >> (16 + j * 4 + q)) & 1u)) {
-                        uint32_t v1[NA > 0 ? NA : 1][16];
+                        uint32_t v1[NA > 0 ? NA : 1][EC];
 #pragma unroll
-                        for (int a = 0; a < NA; ++a) tmem_ld16(buf + 32 + (a * NWA + q) * SUB, v1[a]);
+                        for (int a = 0; a < NA; ++a) tmem_ld(buf + 32 + (a * NWA + q) * SUB, v1[a]);
 #pragma unroll
                         for (int a = 0; a < NA; ++a) tmem_wait(v1[a]);
+                        if (__any_sync(0xFFFFFFFFu, planes_max<NA, EC>(v1) > P.thresh[q])) {
 #pragma unroll
-                        for (int a = 0; a < NA; ++a) relu_correct(v1[a], T, P.dscale[q], P.offset[q], P.coef[a][q]);
+                            for (int a = 0; a < NA; ++a)
+                                relu_correct(v1[a], T, P.dscale[q], P.offset[q], P.coef[a][q]);
+                        }
                     }
                 }
                 tc_fence_before();
@@ -614,15 +496,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                 ++units;
                 if (flagged) {
                     bsel = units & 1;
-                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[bsel], (units >> 1) & 1, s, err, 10));
+                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[bsel], (units >> 1) & 1, &s.abort, err, 10));
                     if (!ok) break;
                     tc_fence_after();
                     buf = lane_base + bsel * HALF_COLS;
 #pragma unroll
                     for (int q = 0; q < NWC; ++q) {
-                        uint32_t v1[NA > 0 ? NA : 1][16];
+                        uint32_t v1[NA > 0 ? NA : 1][EC];
 #pragma unroll
-                        for (int a = 0; a < NA; ++a) tmem_ld16(buf + (a * NWC + q) * SUB, v1[a]);
+                        for (int a = 0; a < NA; ++a) tmem_ld(buf + (a * NWC + q) * SUB, v1[a]);
 #pragma unroll
                         for (int a = 0; a < NA; ++a) tmem_wait(v1[a]);
 #pragma unroll
@@ -634,22 +516,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (lane == 0) mbar_arrive(&s.unit_empty[bsel]);
                     ++units;
                 }
-                // fl(fl(T * xs) * ws) pushed into cascade level 0 for read i.  Scalar
-                // round-to-nearest intrinsics: packed f32x2 multiplies followed by an add
-                // were observed to round once (as an FMA), which the reference does not.
-                const float2* wsr = reinterpret_cast<const float2*>(&s.ws[sb][i % SCB][j * SUB + hc * 16]);
-                float v[16];
+                // fl(fl(T * xs) * ws) pushed into cascade level 0 for read i: packed
+                // round-to-nearest multiplies, then SCALAR adds (a packed multiply
+                // followed by a packed add was observed to round once, as an FMA,
+                // which the reference does not).
+                const float2* wsr = reinterpret_cast<const float2*>(&s.ws[sb][i % SCB][j * SUB + hc * EC]);
+                float v[EC];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
+                for (int e = 0; e < EC / 2; ++e) {
                     const float2 w2 = wsr[e];
                     const float2 t2 = unpack(T[e]);
-                    v[2 * e] = __fmul_rn(__fmul_rn(t2.x, xs), w2.x);
-                    v[2 * e + 1] = __fmul_rn(__fmul_rn(t2.y, xs), w2.y);
+                    const float2 pr = __fmul2_rn(__fmul2_rn(t2, make_float2(xs, xs)), w2);
+                    v[2 * e] = pr.x;
+                    v[2 * e + 1] = pr.y;
                 }
                 switch (j) {
 #define MF_ACC(J)                                                         \
     case J:                                                               \
-        _Pragma("unroll") for (int e = 0; e < 16; ++e) acc0[J][e] = __fadd_rn(acc0[J][e], v[e]); \
+        _Pragma("unroll") for (int e = 0; e < EC; ++e) acc0[J][e] = __fadd_rn(acc0[J][e], v[e]); \
         break;
                     MF_ACC(0)
                     MF_ACC(1)
@@ -670,8 +554,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < NSUB; ++j)
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int cl = j * SUB + hc * 16 + e;
+                    for (int e = 0; e < EC; ++e) {
+                        const int cl = j * SUB + hc * EC + e;
                         s.acc1[cl][r] = __fadd_rn(s.acc1[cl][r], acc0[j][e]);
                         acc0[j][e] = 0.0f;
                     }
@@ -681,8 +565,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j = 0; j < NSUB; ++j)
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int cl = j * SUB + hc * 16 + e;
+                for (int e = 0; e < EC; ++e) {
+                    const int cl = j * SUB + hc * EC + e;
                     const int col = c0 + cl;
                     if (col >= args.col_end || col >= args.out_features) continue;
                     // acc0 + acc1 + acc2 + acc3 (upper levels zero), then the reference's
@@ -700,83 +584,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+        tmem_dealloc(tmem, 512);
     }
 }
 
 }  // namespace tc
 
 // =================================================================== host side
-namespace {
-
-// Weight codes [m, p, R, C] -> K-major [p*C, m*R] (8-bit, same bytes).
-__global__ void weights_kmajor_kernel(const uint8_t* packed, uint8_t* out, int m, int p, int R, int C) {
-    __shared__ uint8_t tile[32][33];
-    const long long k0 = (long long)blockIdx.x * 32, o0 = (long long)blockIdx.y * 32;
-    const long long K = (long long)m * R, O = (long long)p * C;
-    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-        const long long k = k0 + j, o = o0 + threadIdx.x;
-        uint8_t v = 0;
-        if (k < K && o < O) {
-            const long long arr = k / R, r = k % R, t = o / C, c = o % C;
-            v = packed[((arr * p + t) * R + r) * C + c];
-        }
-        tile[j][threadIdx.x] = v;
-    }
-    __syncthreads();
-    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-        const long long o = o0 + j, k = k0 + threadIdx.x;
-        if (k < K && o < O) out[o * K + k] = tile[threadIdx.x][j];
-    }
-}
-
-typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encoder() {
-    static EncodeTiled fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiled>(p);
-    }
-    return fn;
-}
-
-// 2D tiled tensor map: `inner` x `outer` elements of `bytes` each, row stride
-// `stride` elements, box `box_inner` x `box_outer`.
-mf_status make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int bytes, uint64_t inner,
-                   uint64_t outer, uint64_t stride, uint32_t box_inner, uint32_t box_outer,
-                   CUtensorMapSwizzle swizzle) {
-    EncodeTiled fn = encoder();
-    if (!fn) {
-        set_error("cuTensorMapEncodeTiled unavailable");
-        return MF_ERR_CUDA;
-    }
-    if (((uintptr_t)base & 15) || (stride * bytes) % 16) {
-        set_error("tensor map needs 16-byte aligned base and row stride");
-        return MF_ERR_INVALID;
-    }
-    const cuuint64_t dims[2] = {inner, outer};
-    const cuuint64_t strides[1] = {stride * bytes};
-    const cuuint32_t box[2] = {box_inner, box_outer};
-    const cuuint32_t elem[2] = {1, 1};
-    CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-        set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
-        return MF_ERR_CUDA;
-    }
-    return MF_OK;
-}
-
-__device__ unsigned g_tc_error = 0;
-
-}  // namespace
-
 // Host-side plan: which slice pairs can clip and how the epilogue undoes them.
 bool tc_plan(const mf_config& c, tc::Plan& P) {
     memset(&P, 0, sizeof(P));
@@ -837,6 +651,7 @@ bool tc_plan(const mf_config& c, tc::Plan& P) {
         while ((1LL << k) < span) ++k;
         P.dscale[q] = ldexpf(1.0f, 18 - k);
         P.offset[q] = -ldexpf((float)c.adc_max[w], -k);
+        P.thresh[q] = ldexpf((float)c.adc_max[w], -18);
         for (int i = 0; i < na; ++i)
             P.coef[i][q] = -(float)(c.in_factor[clip_a[i]] * c.w_factor[w]) * ldexpf(1.0f, k);
         // D <= Mw * S_a(n) and D <= Ma * S_w(o): below these limits plane q cannot clip.
@@ -870,6 +685,8 @@ bool tc_eligible(const mf_config& c, int32_t m) {
     return tc_shape_supported(P.na, P.nwa, P.nwc);
 }
 
+int tc_block_threads() { return tc::THREADS; }
+
 size_t tc_workspace_bytes(const mf_config& c, int32_t m, int32_t p) {
     return (size_t)p * c.cols * m * c.rows + 256;
 }
@@ -883,7 +700,7 @@ static mf_status launch_tc(const CUtensorMap& mx, const CUtensorMap& mw, const C
     MF_CHECK_CUDA(cudaFuncGetAttributes(&attr, kern), "tc kernel attributes");
     // Registers are allocated per thread in multiples of 8.
     const long long pool = (long long)((attr.numRegs + 7) / 8 * 8) * tc::THREADS;
-    const long long split = 128LL * tc::REG_LOW + 256LL * tc::REG_HIGH;
+    const long long split = 128LL * tc::REG_LOW + 32LL * tc::EPI_WARPS * tc::REG_HIGH;
     if (split > pool) {
         set_error("tcgen05 kernel launched with %d registers/thread cannot host the %d/%d register split",
                   attr.numRegs, tc::REG_LOW, tc::REG_HIGH);
@@ -920,23 +737,22 @@ mf_status tc_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, siz
     const long long O = (long long)a.p * c.cols;
     const int MR = a.m * c.reads;
     uint8_t* wk = static_cast<uint8_t*>(workspace);
-    dim3 tgrid((unsigned)((K + 31) / 32), (unsigned)((O + 31) / 32));
-    weights_kmajor_kernel<<<tgrid, dim3(32, 8), 0, st>>>(static_cast<const uint8_t*>(a.packed), wk, a.m, a.p,
-                                                          c.rows, c.cols);
-    MF_LAUNCH_CHECK("weights_kmajor_kernel");
+    mf_status r = tc_weights_kmajor(a.packed, wk, a.m, a.p, c.rows, c.cols, st);
+    if (r) return r;
     CUtensorMap mx, mw, mxs, mws;
-    mf_status r = make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n, (uint64_t)K,
+    r = tc_make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n, (uint64_t)K,
                            tc::KR, tc::BM, CU_TENSOR_MAP_SWIZZLE_32B);
-    if (!r) r = make_map(&mw, wk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)O, (uint64_t)K, tc::KR,
+    if (!r) r = tc_make_map(&mw, wk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)O, (uint64_t)K, tc::KR,
                          tc::BN, CU_TENSOR_MAP_SWIZZLE_32B);
     // Scales: xscale [n, MR] -> boxes [128 rows][4 reads]; wscale [MR, O] -> [4 reads][128 cols].
-    if (!r) r = make_map(&mxs, a.xscale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)MR, (uint64_t)a.n,
+    if (!r) r = tc_make_map(&mxs, a.xscale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)MR, (uint64_t)a.n,
                          (uint64_t)MR, tc::SCB, tc::BM, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (!r) r = make_map(&mws, a.wscale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)O, (uint64_t)MR, (uint64_t)O,
+    if (!r) r = tc_make_map(&mws, a.wscale, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)O, (uint64_t)MR, (uint64_t)O,
                          tc::BN, tc::SCB, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (r) return r;
     unsigned* err = nullptr;
-    MF_CHECK_CUDA(cudaGetSymbolAddress((void**)&err, g_tc_error), "error symbol");
+    r = tc_error_word(&err);
+    if (r) return r;
     args.bias = static_cast<const float*>(a.bias);
     args.out = static_cast<float*>(a.out);
     args.n = a.n;
@@ -962,12 +778,5 @@ mf_status tc_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, siz
     return MF_ERR_UNSUPPORTED;
 }
 
-mf_status tc_take_error(unsigned* code) {
-    unsigned value = 0, zero = 0;
-    MF_CHECK_CUDA(cudaMemcpyFromSymbol(&value, g_tc_error, sizeof(value)), "read device error");
-    if (value) MF_CHECK_CUDA(cudaMemcpyToSymbol(g_tc_error, &zero, sizeof(zero)), "clear device error");
-    *code = value;
-    return MF_OK;
-}
 
 }  // namespace mf
