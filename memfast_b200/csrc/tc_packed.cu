@@ -71,7 +71,7 @@ constexpr int MAXCOL = 3;        // packed count blocks per job
 constexpr int MAXFIELD = 3;      // counts per count block
 constexpr int MAXMMA = 6;        // plane MMAs per job
 constexpr int MAXRARE = 4;       // weight slices of rare pairs (column bounds)
-constexpr int UNITS = 2;
+constexpr int UNITS = 512 / (JOBN * (1 + MAXCOL));
 constexpr int UNIT_COLS = JOBN * (1 + MAXCOL);
 constexpr int EPI_WARPS = 16;
 constexpr int EC = JOBN / (EPI_WARPS / 4);   // columns of a job per epilogue thread
@@ -81,7 +81,7 @@ constexpr int EPI_WARP0 = 4;
 constexpr int XF_WARP0 = EPI_WARP0 + EPI_WARPS;
 constexpr int THREADS = 32 * (XF_WARP0 + XF_WARPS);
 constexpr int TILE = BM * KR;    // one [128 x 32] 8-bit tile
-constexpr int SLOT = JOBN * KR;  // one [64 x 32] 8-bit weight-plane slot
+constexpr int SLOT = JOBN * KR;  // one [JOBN x 32] 8-bit weight-plane slot
 constexpr int EPI_BARRIER = 1;   // named barrier of the epilogue warps
 
 // Register split.  setmaxnreg draws on the registers the block was launched
@@ -112,6 +112,7 @@ struct Smem {
     uint32_t tmem_base;
     int abort;
     unsigned rare;
+    int4 field[MAXCOL * MAXFIELD];                  // (shift, width mask, m, coef) of every count
 };
 static_assert(sizeof(Smem) + 1024 <= 232448, "packed kernel exceeds the 227 KB shared-memory limit");
 
@@ -194,6 +195,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_init(&s.drained, 1);
         s.abort = 0;
         s.rare = 0;
+        for (int c = 0; c < MAXCOL; ++c)
+            for (int f = 0; f < MAXFIELD; ++f) {
+                const Field F = P.field[c][f];
+                s.field[c * MAXFIELD + f] = make_int4(F.shift, F.width_mask, F.m, F.coef);
+            }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     for (int idx = threadIdx.x; idx < BN * (BM + 1); idx += THREADS) (&s.acc1[0][0])[idx] = 0.0f;
@@ -281,8 +287,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int k = 0; k < MAXMMA; ++k)
                         if (k < nmma) mma_i8(buf + t_off[k], da + a_off[k], db + b_off[k], idesc[k], acc[k]);
                     mma_commit(&s.unit_full[u]);
-                    u ^= 1;
-                    uphase ^= u == 0;
+                    if (++u == UNITS) {
+                        u = 0;
+                        uphase ^= 1;
+                    }
                 }
                 if (ok) mma_commit(&s.empty[st]);
             }
@@ -429,17 +437,26 @@ __global__ void __launch_bounds__(THREADS, 1)
                             hit |= acc & P.colclip[c];
                         }
                         if (__any_sync(0xFFFFFFFFu, hit != 0)) {
+                            // Counts that clip somewhere in the warp, one bit each, then
+                            // T += -s_a s_w * max(D - m, 0) for those counts only (one loop
+                            // body keeps the hot code small).
+                            uint32_t fire = 0;
 #pragma unroll
-                            for (int c = 0; c < NCOL; ++c) {
-                                for (int f = 0; f < P.nfield[c]; ++f) {
-                                    const Field F = P.field[c][f];
-                                    if (!__any_sync(0xFFFFFFFFu, (o[c] & F.clip) != 0)) continue;
+                            for (int c = 0; c < NCOL; ++c)
 #pragma unroll
-                                    for (int e = 0; e < EH; ++e) {
-                                        const int d = (int)((vc[c][e] >> F.shift) & (uint32_t)F.width_mask);
-                                        const int over = d - F.m;
-                                        T[e] += over > 0 ? F.coef * over : 0;
-                                    }
+                                for (int f = 0; f < MAXFIELD; ++f)
+                                    fire |= (uint32_t)((o[c] & P.field[c][f].clip) != 0) << (c * MAXFIELD + f);
+                            fire = __reduce_or_sync(0xFFFFFFFFu, fire);
+                            while (fire) {
+                                const int k = __ffs(fire) - 1;
+                                fire &= fire - 1;
+                                const int c = k / MAXFIELD;
+                                const int4 F = s.field[k];
+#pragma unroll
+                                for (int e = 0; e < EH; ++e) {
+                                    const uint32_t v = c == 0 ? vc[0][e] : c == 1 ? vc[NCOL > 1 ? 1 : 0][e] : vc[NCOL - 1][e];
+                                    const int d = (int)((v >> F.x) & (uint32_t)F.y);
+                                    T[e] += F.w * __viaddmax_s32(d, -F.z, 0);
                                 }
                             }
                         }
@@ -461,8 +478,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                         acc0[j][h * EH + 2 * e + 1] = __fadd_rn(acc0[j][h * EH + 2 * e + 1], pr.y);
                     }
                 }
-                u ^= 1;
-                uphase ^= u == 0;
+                if (++u == UNITS) {
+                    u = 0;
+                    uphase ^= 1;
+                }
             }
             if (!ok) break;
             __syncwarp();
