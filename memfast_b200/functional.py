@@ -15,6 +15,7 @@ from pathlib import Path
 import torch
 
 from .config import Config
+from .quantization import compute_dtype, finite_flags
 from .simulator import Simulator
 
 
@@ -34,9 +35,11 @@ def _operands(a, b):
         raise ValueError("A and B must use the same device")
     if a.device.type != "cuda":
         raise ValueError("memfast_b200 simulates on CUDA operands only")
-    for name, value in (("A", a), ("B", b)):
-        if not torch.isfinite(value).all():
-            raise ValueError(f"{name} must be finite")
+    finite_a, finite_b = finite_flags(a, b)
+    if not finite_a:
+        raise ValueError("A must be finite")
+    if not finite_b:
+        raise ValueError("B must be finite")
 
 
 def _engine(a, simulator, config, mode, cache_dir):
@@ -97,13 +100,22 @@ def _rhs_view(simulator, owner, rhs, index):
     return record[2][index]
 
 
+def _checked(tensor, config, bits):
+    """_operands verified finiteness in the tensor's own dtype; that covers the
+    quantiser's dtype unless FP64 values are narrowed to FP32."""
+    return not (tensor.dtype == torch.float64 and compute_dtype(config, bits) == torch.float32)
+
+
 def _product(a, b, simulator, cached_rhs=None):
     if torch.is_grad_enabled() and (a.requires_grad or b.requires_grad):
         raise NotImplementedError(
             "memfast_b200 simulates the analog forward only; detach operands or use torch.no_grad()"
         )
-    matrix = simulator._matrix_for(b if cached_rhs is None else cached_rhs)
-    return matrix(a.detach())
+    config = simulator.config
+    matrix = simulator._matrix_for(b if cached_rhs is None else cached_rhs,
+                                   checked=_checked(b, config, config.weight_bits))
+    with torch.no_grad():
+        return matrix._forward(a.detach(), checked=_checked(a, config, config.activation_bits))
 
 
 def _matmul(a, b, *, simulator, config, mode, cache_dir, out):

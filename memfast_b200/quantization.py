@@ -86,20 +86,47 @@ def expanded_parameter(value, shape, device, dtype, name, *, positive=False):
     return value
 
 
-def _as_native_float(value, config, bits):
+def finite_flags(*tensors, dtypes=None):
+    """Whether each tensor holds only finite values (in ``dtypes[i]`` when given),
+    with one device synchronisation: NaN propagates through aminmax and an
+    infinity or an overflow on narrowing shows in the extremes."""
+    extremes = []
+    for index, tensor in enumerate(tensors):
+        if tensor.numel() == 0:
+            extremes.append(torch.zeros(2, device=tensor.device, dtype=torch.float64))
+            continue
+        low, high = torch.aminmax(tensor.detach())
+        pair = torch.stack([low, high])
+        if dtypes is not None and dtypes[index] is not None:
+            pair = pair.to(dtypes[index])
+        extremes.append(pair.to(torch.float64))
+    return [bool(flag) for flag in torch.isfinite(torch.stack(extremes)).all(dim=1).tolist()]
+
+
+def compute_dtype(config, bits):
+    """grouped_quantize computes in FP64 for wide codes or BFP, else FP32 (quantization.py:10-13)."""
+    return torch.float64 if bits > 8 or config.bw_e is not None else torch.float32
+
+
+def _as_native_float(value, config, bits, checked=False):
     """The float operand the kernels read (FP16/BF16/FP32/FP64), checked finite in the
-    dtype grouped_quantize computes in (quantization.py:10-13)."""
+    dtype grouped_quantize computes in (quantization.py:10-13).  ``checked`` marks an
+    operand the caller already verified in that dtype."""
     if value.dtype not in _lib.DTYPES:
         value = value.float()
-    compute = torch.float64 if bits > 8 or config.bw_e is not None else torch.float32
+    if checked:
+        return value
+    compute = compute_dtype(config, bits)
     narrowed = value.dtype == torch.float64 and compute == torch.float32
-    if not torch.isfinite(value.to(compute) if narrowed else value).all():
+    if not finite_flags(value, dtypes=[compute if narrowed else None])[0]:
         raise ValueError(f"quantized values must be finite in {compute}")
     return value
 
 
-def input_tiles(value, config, fixed_scale=None):
-    """[n, K] activations -> (codes [n, m, R], per-read scales [n, m*reads])."""
+def input_tiles(value, config, fixed_scale=None, *, checked=False):
+    """[n, K] activations -> (codes [n, m, R], per-read scales [n, m*reads]).
+
+    ``checked``: the caller verified the activations finite in the quantiser's dtype."""
     _require_cuda(value, "input")
     n, k = value.shape
     r = config.array_size[0]
@@ -109,9 +136,9 @@ def input_tiles(value, config, fixed_scale=None):
     if n == 0:
         return codes, xscale
     if fixed_scale is None:
-        value = _as_native_float(value, config, config.activation_bits)
+        value = _as_native_float(value, config, config.activation_bits, checked)
     else:
-        if not torch.isfinite(value).all():
+        if not checked and not finite_flags(value)[0]:
             raise ValueError("quantized values must be finite")
         if value.dtype not in _lib.DTYPES:
             value = value.float()
@@ -132,8 +159,10 @@ def input_tiles(value, config, fixed_scale=None):
     return codes, xscale
 
 
-def weight_tiles(weight, config):
-    """PyTorch-layout [O, K] floating weights -> (packed [m,p,R,C], weight_scale [m*reads,p,C])."""
+def weight_tiles(weight, config, *, checked=False):
+    """PyTorch-layout [O, K] floating weights -> (packed [m,p,R,C], weight_scale [m*reads,p,C]).
+
+    ``checked``: the caller verified the weights finite in the quantiser's dtype."""
     _require_cuda(weight, "weight")
     o, k = weight.shape
     if not config.weight_signed and (weight < 0).any():
@@ -141,7 +170,7 @@ def weight_tiles(weight, config):
             "unsigned floating weights must be nonnegative INT values; "
             "use map_quantized with zero_points for affine weights"
         )
-    weight = _as_native_float(weight, config, config.weight_bits)
+    weight = _as_native_float(weight, config, config.weight_bits, checked)
     if weight.stride(-1) != 1:
         weight = weight.contiguous()
     r, c = config.array_size
