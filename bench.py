@@ -7,10 +7,12 @@ workload (array 128x128, rows_per_read 32, groups
 seeded N(0,1) FP32 operands.  One step = one ``Simulator.mm(A, B)`` call
 (quantise A, reprogram B, sliced product with fused epilogue), operands
 resident in HBM.  ``e2e`` repeats it with pinned host operands copied in and the
-result copied out inside the timed region.  With --gpus N the batch rows are
-sharded across ranks (noise addresses stay global through vector_offset) and
-the output rows are all-gathered over NCCL inside each step: a fixed total
-problem, i.e. strong scaling.
+result copied out inside the timed region.  With --gpus N (one process per GPU
+under torchrun) the batch has 4096 rows per GPU: every rank runs the 4096^3
+product on its own row block of one (4096 N)-row batch with B replicated, its
+vectors keeping their global indices (noise addresses), and keeps its output
+rows (weak scaling; the path has no data exchange).  --gather adds an NCCL
+all-gather of the output rows to every step.
 
 ``--impl reference`` times the reference algorithm's CPU restatement (the
 oracle: restored conductances, FP32 currents, ADC, signed reconstruction,
@@ -47,6 +49,8 @@ def parse():
     p.add_argument("--size", type=int, default=4096, help="N = K = O")
     p.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work budget of the baseline sample")
+    p.add_argument("--gather", action="store_true",
+                   help="with --gpus N > 1, also all-gather every rank's output rows inside each step")
     p.add_argument("--kernel", type=int, default=0, choices=[0, 1, 2, 3],
                    help="schedule kernel of the kernel-only timing (0 automatic, 1 generic SIMT, "
                         "2 tcgen05 packed counts, 3 tcgen05 FP8 digit planes)")
@@ -61,18 +65,26 @@ def bench_config(mf_module):
     )
 
 
-def operands(size, seed=2024):
+def operands(size, seed=2024, rank=0):
+    """Seeded N(0,1) operands: B is the same on every rank; rank 0's A is the 1-GPU A and
+    rank r > 0 draws its own rows from a seed of its own."""
     import torch
 
     g = torch.Generator().manual_seed(seed)
     a = torch.randn(size, size, generator=g)
     b = torch.randn(size, size, generator=g)
+    if rank > 0:
+        a = torch.randn(size, size, generator=torch.Generator().manual_seed(seed + 7919 * rank))
     return a, b
 
 
 def workload(args):
     n = k = o = args.size
-    return dict(workload=f"Simulator.mm {n}x{k}x{o} INT8 (1,1,2,2,2) ideal", n=n, k=k, o=o,
+    gpus = args.gpus
+    return dict(workload=f"Simulator.mm {n}x{k}x{o} INT8 (1,1,2,2,2) ideal per GPU", n=n, k=k, o=o,
+                batch=f"{gpus} row block(s) of {n}: one {n * gpus}-row batch, rows sharded, B replicated"
+                      + (", output rows all-gathered" if getattr(args, "gather", False) and gpus > 1 else
+                         ", each rank keeps its output rows"),
                 array=[128, 128], rows_per_read=32, adc_bits=[6, 7, 7, 8, 8],
                 input_groups=[1, 32], weight_groups=[32, 1], operands="seeded N(0,1) fp32",
                 l2=f"inputs 2x{4 * n * k / 2**20:.0f} MiB fp32; L2 (126 MB) flushed by a 256 MiB write "
@@ -150,7 +162,7 @@ def reference_arm(args):
             times.append(elapsed)
     value = statistics.mean(rates)
     line = dict(metric=metric_name(args.size), value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
-                ms_per_step=float(args.size) ** 3 / value * 1e3, higher_is_better=True, scaling="strong",
+                ms_per_step=float(args.size) ** 3 / value * 1e3, higher_is_better=True, scaling="weak",
                 vs_baseline=None, dtype="f32 currents / int64 totals", data="synthetic", config=workload(args),
                 impl="reference",
                 cpu_baseline=dict(value=value, unit=UNIT, cores=sample.threads, kind="port",
@@ -253,29 +265,31 @@ def engine_arm(args):
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    from memfast_b200.sharding import gather_rows, row_range, sharded_mm
+
     config = bench_config(mf)
     size = args.size
-    a_cpu, b_cpu = operands(size)
-    rows = size // world
-    r0 = rank * rows
-    r1 = size if rank == world - 1 else r0 + rows
-    a_host = a_cpu[r0:r1].contiguous().pin_memory()
+    # Weak scaling: every rank owns `size` rows of a (size * world)-row batch; its rows
+    # carry their global vector indices (noise addresses), so each rank's output rows
+    # equal those rows of a single-device run.
+    a_cpu, b_cpu = operands(size, rank=rank)
+    total_rows = size * world
+    r0, r1 = rank * size, (rank + 1) * size
+    rows = r1 - r0
+    a_host = a_cpu.contiguous().pin_memory()
     b_host = b_cpu.contiguous().pin_memory()
     a = a_host.to(device)
     b = b_host.to(device)
     sim = mf.Simulator(config, device=device)
-    gathered = torch.empty((size, size), device=device) if world > 1 else None
     out_host = torch.empty((r1 - r0, size), pin_memory=True)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
 
     def step(x, y):
-        out = sim.mm(x, y)
-        if world > 1:
-            if r1 - r0 == rows:
-                dist.all_gather_into_tensor(gathered, out)
-            else:
-                raise SystemExit("bench: batch must divide evenly across ranks")
+        # This rank's rows with global vector indices; optionally the rows of every rank.
+        out = sharded_mm(x, y, simulator=sim, row_offset=r0) if world > 1 else sim.mm(x, y)
+        if world > 1 and args.gather:
+            gather_rows(out, total_rows)
         return out
 
     def timed(fn, count):
@@ -367,7 +381,7 @@ def engine_arm(args):
         dist.destroy_process_group()
     if rank != 0:
         return
-    macs = float(size) ** 3
+    macs = float(size) ** 3 * world
     pairs = len(config.input_layout) * len(config.weight_layout)
     bf16, hbm, peak_kind = measured_peaks()
     int8_peak_tops = 2.0 * bf16
@@ -376,7 +390,7 @@ def engine_arm(args):
     traffic = profiled_traffic()
     line = dict(
         metric=metric_name(args.size), value=macs / per_step, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
-        ms_per_step=per_step * 1e3, higher_is_better=True, scaling="strong", vs_baseline=None,
+        ms_per_step=per_step * 1e3, higher_is_better=True, scaling="weak", vs_baseline=None,
         dtype="u8 digits / int32 totals / f32 epilogue", data="synthetic", config=workload(args),
         slice_pair_macs_per_s=macs * pairs / per_step,
         roofline=dict(bound="tensor", achieved=achieved_tops, peak=int8_peak_tops, unit="TFLOP/s",
@@ -387,8 +401,8 @@ def engine_arm(args):
                            f"dense bf16 ({bf16} TFLOP/s), the int8 dense rate of B200",
                       kernel_ms=kernel_s * 1e3),
         e2e=dict(value=macs / e2e_step_s, unit=UNIT,
-                 h2d_bytes_per_step=int((size * size + size * size * world) * 4),
-                 d2h_bytes_per_step=int(size * size * 4), ms_per_step=e2e_step_s * 1e3),
+                 h2d_bytes_per_step=int(2 * size * size * world * 4),
+                 d2h_bytes_per_step=int(size * size * world * 4), ms_per_step=e2e_step_s * 1e3),
         gpu_launches=int(launches),
         clocks=clocks.summary(),
     )

@@ -577,8 +577,9 @@ class AnalogMatrix(nn.Module):
     def forward(self, x):
         return self._forward(x)
 
-    def _forward(self, x, checked=False):
-        """forward(); ``checked``: the caller verified x finite in the quantiser's dtype."""
+    def _forward(self, x, checked=False, vector_offset=0):
+        """forward(); ``checked``: the caller verified x finite in the quantiser's dtype;
+        ``vector_offset``: global index of x's first vector (noise addresses of row shards)."""
         if x.ndim < 1 or x.shape[-1] != self.in_features or not x.is_floating_point():
             raise ValueError("input must be floating with matching in_features")
         if x.device != self.packed.device or x.device != self.simulator.device:
@@ -600,7 +601,7 @@ class AnalogMatrix(nn.Module):
                 with torch.cuda.device(x.device):
                     self._prepared[key] = self.simulator._select(self, x, q, xscale, event)
             schedule = self._prepared[key]
-        output = self._execute(q, xscale, schedule, event)
+        output = self._execute(q, xscale, schedule, event, vector_offset=vector_offset)
         output = output.reshape(*shape[:-1], self.out_features)
         finite = self._finite and (output.dtype == x.dtype or finite_flags(output, dtypes=[x.dtype])[0])
         output = output.to(x.dtype)
