@@ -47,7 +47,7 @@ def _gather_worker(rank, world, port, n, result):
 @pytest.mark.parametrize("n", [5, 8, 1])
 def test_gather_rows_two_ranks_gloo(n):
     """Uneven shards are padded for the collective and trimmed back in rank order."""
-    manager = mp.Manager()
+    manager = mp.get_context("spawn").Manager()
     result = manager.dict()
     mp.spawn(_gather_worker, args=(2, _free_port(), n, result), nprocs=2, join=True)
     assert result[0] and result[1]
