@@ -1,9 +1,9 @@
 """Regenerate the golden vectors in this directory from the reference MemFast.
 
 Run in a container where the reference package is importable (it is not needed
-at test time):
+at test time); name cases after the path to regenerate only those:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /path/to/MemFast
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /path/to/MemFast [case ...]
 
 Every case stores its operands, its Config keyword arguments (JSON) and the
 reference's outputs, plus the reference's quantised buffers where the case is
@@ -33,7 +33,7 @@ def _jsonable(kwargs):
     return out
 
 
-def main(reference_root):
+def main(reference_root, only=()):
     sys.path.insert(0, str(reference_root))
     sys.dont_write_bytecode = True
     import memfast
@@ -56,6 +56,8 @@ def main(reference_root):
                       nonidealities=Nonidealities(**effects))
 
     def save(case, kwargs, arrays, **meta):
+        if only and case not in only:
+            return
         payload = {k: np.asarray(v) for k, v in arrays.items()}
         payload["config_json"] = np.array(json.dumps(_jsonable(kwargs)))
         payload["meta_json"] = np.array(json.dumps(meta))
@@ -64,6 +66,8 @@ def main(reference_root):
         print(f"{case:28s} {size/1024:7.1f} KiB")
 
     def mm_case(name, kwargs, n, k, o, seed, *, a=None, b=None, calls=1, buffers=False):
+        if only and name not in only:
+            return
         cfg = make(kwargs)
         g = torch.Generator().manual_seed(seed)
         a = torch.randn(n, k, generator=g) if a is None else a
@@ -153,6 +157,25 @@ def main(reference_root):
     save("fixed_input_scale", kwargs, dict(W=w.numpy(), x=x.numpy(), scale=np.float32(0.02),
                                            out0=layer(x).numpy()), kind="fixed_scale", name="fixed")
 
+    # Checkpoint of a programmed layer (simulator.py:452-534): the reference's buffers
+    # and extra state after one read event, and the output of the next read.
+    if not only or "checkpoint" in only:
+        kwargs = dict(int8, adc_bits=7, nonidealities=dict(write_variation=0.02, read_variation=0.02))
+        cfg = make(kwargs)
+        g = torch.Generator().manual_seed(21)
+        w = torch.randn(96, 256, generator=g)
+        bias = torch.randn(96, generator=g)
+        x = torch.randn(6, 256, generator=g)
+        layer = Simulator(cfg, device="cpu").map(w, bias=bias, name="ckpt")
+        out0 = layer(x)
+        state = layer.state_dict()
+        extra = state.pop("_extra_state")
+        out1 = layer(x)
+        save("checkpoint", kwargs, dict(W=w.numpy(), bias=bias.numpy(), x=x.numpy(), out0=out0.numpy(),
+                                        out1=out1.numpy(),
+                                        **{f"state::{k}": v.numpy() for k, v in state.items()}),
+             kind="checkpoint", name="ckpt", extra_state=extra)
+
     # convert_model on a small Conv2d + Linear network (nn/conversion.py, nn/convolution.py).
     kwargs = dict(int8, adc_bits=7, nonidealities=dict(write_variation=0.02))
     cfg = make(kwargs)
@@ -172,4 +195,4 @@ def main(reference_root):
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "../MemFast").resolve())
+    main(Path(sys.argv[1] if len(sys.argv) > 1 else "../MemFast").resolve(), tuple(sys.argv[2:]))
