@@ -25,6 +25,9 @@ constexpr int IDEAL_TC = 64;      // output columns per CTA
 constexpr int PHYS_TV = 16;
 constexpr int PHYS_TC = 64;
 constexpr int PHYS_RCH = 32;      // rows staged per chunk
+constexpr int ST_TV = 32;         // staged physical kernel: vectors per CTA (2 per thread)
+constexpr int ST_TC = 64;         // staged physical kernel: output columns per CTA (4 per thread)
+constexpr size_t ST_SMEM_MAX = 200 * 1024;
 constexpr int THREADS = 256;
 
 template <typename OutT, typename ScaleT, typename TotT>
@@ -436,6 +439,184 @@ __global__ void __launch_bounds__(THREADS) physical_kernel(Layout L, Physics P, 
     }
 }
 
+// ------------------------------------------------- staged physical kernel --
+// physical_kernel for reads whose planes fit in shared memory and whose read
+// noise does not depend on the slice pair (shared and output read modes): per
+// read, the input voltages of every input slice (with their voltage noise) and
+// G - LOW of every weight slice are staged once and shared by all slice pairs,
+// and each thread accumulates a 2-vector x 4-column block of currents with FMAs
+// in ascending row order.
+template <typename T> __device__ __forceinline__ T fma_rn(T a, T b, T c);
+template <> __device__ __forceinline__ float fma_rn<float>(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+template <> __device__ __forceinline__ double fma_rn<double>(double a, double b, double c) { return __fma_rn(a, b, c); }
+
+template <typename CodeT, typename CurT, typename OutT, typename ScaleT, bool OUTPUT_NOISE>
+__global__ void __launch_bounds__(THREADS, 2) physical_staged_kernel(Layout L, Physics P, MMArgs a, const CurT* G,
+                                                                  int group_begin, int group_width, int power,
+                                                                  long long full) {
+    extern __shared__ __align__(16) uint8_t staged_raw[];
+    CurT* sV = reinterpret_cast<CurT*>(staged_raw);        // [n_in][rows][ST_TV]
+    CurT* sG = sV + (size_t)L.n_in * L.rows * ST_TV;         // [n_w][rows][ST_TC], G - LOW
+    const CodeT* codes = static_cast<const CodeT*>(a.codes);
+    const ScaleT* xscale = static_cast<const ScaleT*>(a.xscale);
+    const ScaleT* wscale = static_cast<const ScaleT*>(a.wscale);
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const long long v0 = (long long)blockIdx.x * ST_TV;
+    const long long col0 = (long long)group_begin * L.C + (long long)blockIdx.y * ST_TC;
+    const long long col_end = (long long)(group_begin + group_width) * L.C;
+    const int MR = a.m * L.reads;
+    const long long row_stride = (long long)a.m * L.R;
+    const uint64_t read_seed = event_seed(a.seed, a.event);
+    constexpr bool output_mode = OUTPUT_NOISE;
+    const CurT low = (CurT)P.low;
+
+    Cascade<OutT> acc[2][4];
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[e][j].init();
+
+    for (int i = 0; i < MR; ++i) {
+        const int arr = i / L.reads, g = i % L.reads;
+        const int r0 = g * L.rows;
+        const int len = L.rows < L.R - r0 ? L.rows : L.R - r0;
+        __syncthreads();
+        for (int idx = tid; idx < L.n_in * len * ST_TV; idx += THREADS) {
+            const int v = idx % ST_TV, rr = (idx / ST_TV) % len, sa = idx / (ST_TV * len);
+            const long long vec = v0 + v;
+            CurT value = 0;
+            if (vec < a.n) {
+                const int r = r0 + rr;
+                const int amask = L.in_mask[sa];
+                const long long code = (long long)codes[vec * row_stride + (long long)arr * L.R + r];
+                const long long d = (code >> L.in_shift[sa]) & amask;
+                if (sizeof(CurT) == 4) {
+                    float x = __fmul_rn(__fdiv_rn((float)d, (float)amask), (float)P.voltage);
+                    if (P.volt_var != 0) {
+                        const long long address = (((vec + a.vector_offset) * a.m + arr) * L.n_in + sa) * L.R + r;
+                        x = __fmul_rn(x, __fadd_rn(1.0f, __fmul_rn((float)P.volt_var, rng_normal(address, read_seed, 40))));
+                    }
+                    value = (CurT)x;
+                } else {
+                    double x = __dmul_rn(__ddiv_rn((double)d, (double)amask), P.voltage);
+                    if (P.volt_var != 0) {
+                        const long long address = (((vec + a.vector_offset) * a.m + arr) * L.n_in + sa) * L.R + r;
+                        const float f = __fmul_rn((float)P.volt_var, rng_normal(address, read_seed, 40));
+                        x = __dmul_rn(x, (double)__fadd_rn(1.0f, f));
+                    }
+                    value = (CurT)x;
+                }
+            }
+            sV[((size_t)sa * L.rows + rr) * ST_TV + v] = value;
+        }
+        for (int idx = tid; idx < L.n_w * len * ST_TC; idx += THREADS) {
+            const int c = idx % ST_TC, rr = (idx / ST_TC) % len, sw = idx / (ST_TC * len);
+            const long long col = col0 + c;
+            CurT value = 0;
+            if (col < col_end) {
+                const long long t = col / L.C, cc = col % L.C;
+                value = add_rn(G[((((long long)arr * group_width + (t - group_begin)) * L.n_w + sw) * L.R + r0 + rr) *
+                                 L.C + cc], -low);
+            }
+            sG[((size_t)sw * L.rows + rr) * ST_TC + c] = value;
+        }
+        __syncthreads();
+        long long total[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+        for (int sa = 0; sa < L.n_in; ++sa) {
+            const int amask = L.in_mask[sa];
+            const CurT* pv = sV + (size_t)sa * L.rows * ST_TV;
+            for (int sw = 0; sw < L.n_w; ++sw) {
+                const CurT* pg = sG + (size_t)sw * L.rows * ST_TC + 4 * tx;
+                CurT cur[2][4] = {}, mean[2][4] = {}, var[2][4] = {};
+                for (int rr = 0; rr < len; ++rr) {
+                    const CurT va = pv[rr * ST_TV + ty], vb = pv[rr * ST_TV + ty + 16];
+                    CurT gq[4];
+                    if (sizeof(CurT) == 4) {
+                        const float4 q4 = *reinterpret_cast<const float4*>(pg + rr * ST_TC);
+                        gq[0] = (CurT)q4.x, gq[1] = (CurT)q4.y, gq[2] = (CurT)q4.z, gq[3] = (CurT)q4.w;
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) gq[j] = pg[rr * ST_TC + j];
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        cur[0][j] = fma_rn(va, gq[j], cur[0][j]);
+                        cur[1][j] = fma_rn(vb, gq[j], cur[1][j]);
+                        if (output_mode) {
+                            const CurT gv = add_rn(gq[j], low);
+                            mean[0][j] = fma_rn(va, gv, mean[0][j]);
+                            mean[1][j] = fma_rn(vb, gv, mean[1][j]);
+                            var[0][j] = fma_rn(mul_rn(va, va), mul_rn(gv, gv), var[0][j]);
+                            var[1][j] = fma_rn(mul_rn(vb, vb), mul_rn(gv, gv), var[1][j]);
+                        }
+                    }
+                }
+                const long long factor = L.in_factor[sa] * L.w_factor[sw];
+                const int maxw = L.adc_max[sw];
+                const CurT amw = (CurT)((long long)amask * L.w_mask[sw]);
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const long long vec = v0 + ty + 16 * e;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        CurT current = cur[e][j];
+                        if (output_mode) {
+                            const long long col = col0 + 4 * tx + j;
+                            const long long t = col / L.C, cc = col % L.C;
+                            const long long address =
+                                (((((vec + a.vector_offset) * MR + i) * a.p + t) * L.n_in + sa) * L.n_w + sw) * L.C + cc;
+                            const float z = rng_normal(address, read_seed, 60);
+                            if (sizeof(CurT) == 4) {
+                                const float mu = __fmul_rn((float)mean[e][j], (float)P.mean_factor);
+                                const float sig = __fmul_rn((float)var[e][j], (float)P.var_factor);
+                                current = (CurT)__fadd_rn((float)current, __fadd_rn(mu, __fmul_rn(sqrtf(sig), z)));
+                            } else {
+                                const double mu = __dmul_rn((double)mean[e][j], P.mean_factor);
+                                const double sig = __dmul_rn((double)var[e][j], P.var_factor);
+                                current = (CurT)__dadd_rn((double)current, __dadd_rn(mu, __dmul_rn(sqrt(sig), (double)z)));
+                            }
+                        }
+                        total[e][j] += adc_count(current, maxw, amw, P) * factor;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const long long vec = v0 + ty + 16 * e;
+            if (vec >= a.n) continue;
+            const ScaleT xs = xscale[vec * MR + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const long long col = col0 + 4 * tx + j;
+                if (col >= col_end) continue;
+                const long long t = col / L.C, cc = col % L.C;
+                const ScaleT ws = wscale[((long long)i * a.p + t) * L.C + cc];
+                cascade_push(acc[e][j], scaled_partial<OutT, ScaleT, long long>(total[e][j], xs, ws), i, power, full);
+            }
+        }
+    }
+    OutT* out = static_cast<OutT*>(a.out);
+    const ScaleT* bias = static_cast<const ScaleT*>(a.bias);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        const long long vec = v0 + ty + 16 * e;
+        if (vec >= a.n) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const long long col = col0 + 4 * tx + j;
+            if (col >= col_end || col >= a.out_features) continue;
+            OutT value = cascade_finish(acc[e][j]);
+            if (bias) value = add_rn(value, (OutT)bias[col]);
+            out[vec * a.ldo + col] = value;
+        }
+    }
+}
+
+size_t staged_smem(const mf_config& c, size_t elem) {
+    return ((size_t)c.n_in * c.read_rows * ST_TV + (size_t)c.n_w * c.read_rows * ST_TC) * elem;
+}
+
 size_t ideal_smem(const mf_config& c) {
     const size_t r4 = (size_t)(c.read_rows + 3) / 4;
     return ((size_t)c.n_in * IDEAL_TV + (size_t)c.n_w * IDEAL_TC) * r4 * 4;
@@ -516,6 +697,27 @@ mf_status launch_physical_t(const mf_config& c, const mf_schedule& s, const MMAr
                                                              a.seed, a.event, G);
         MF_LAUNCH_CHECK("restore_kernel");
         const long long cols = (long long)gw * c.cols;
+        const bool pair_noise = c.read_mode == 1 && c.read_var != 0;
+        const size_t smem = staged_smem(c, sizeof(CurT));
+        if (!pair_noise && smem <= ST_SMEM_MAX) {
+            dim3 grid((unsigned)((a.n + ST_TV - 1) / ST_TV), (unsigned)((cols + ST_TC - 1) / ST_TC));
+            const bool output_noise = c.read_mode == 2 && c.read_var != 0;
+#define MF_STAGED(CODE, OUTN)                                                                          \
+    do {                                                                                               \
+        auto kern = physical_staged_kernel<CODE, CurT, OutT, ScaleT, OUTN>;                            \
+        MF_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), \
+                      "staged smem attribute");                                                        \
+        kern<<<grid, THREADS, smem, st>>>(L, P, a, G, begin, gw, power, full);                         \
+    } while (0)
+            if (c.wide_codes) {
+                if (output_noise) MF_STAGED(long long, true); else MF_STAGED(long long, false);
+            } else {
+                if (output_noise) MF_STAGED(uint8_t, true); else MF_STAGED(uint8_t, false);
+            }
+#undef MF_STAGED
+            MF_LAUNCH_CHECK("physical_staged_kernel");
+            continue;
+        }
         dim3 grid((unsigned)((a.n + PHYS_TV - 1) / PHYS_TV), (unsigned)((cols + PHYS_TC - 1) / PHYS_TC));
         if (c.wide_codes)
             physical_kernel<long long, CurT, OutT, ScaleT><<<grid, THREADS, 0, st>>>(L, P, a, G, begin, gw, power, full);
