@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define MF_ABI_VERSION 1
+#define MF_ABI_VERSION 2
 #define MF_MAX_SLICES 32
 
 typedef enum {
@@ -81,11 +81,16 @@ typedef struct {
     int32_t tile_n;     /* vectors per CTA (generic: 8,16,32) */
     int32_t tile_o;     /* output columns per CTA (generic: 32,64,128) */
     int32_t arrays;     /* tiles restored per group in physical mode (>=1) */
+    int32_t kmajor_ready; /* 1: the workspace starts with the K-major weight copy that
+                             mf_program_rhs wrote for these packed weights (tensor-core
+                             kernels then skip rebuilding it); 0: rebuilt per call */
 } mf_schedule;
 
 typedef struct {
     size_t workspace_bytes;
     int32_t threads, shared_bytes, registers, local_bytes, blocks_per_sm;
+    size_t kmajor_bytes;  /* > 0: the chosen kernel reads a K-major weight copy of this many
+                             bytes at the start of its workspace (see kmajor_ready) */
 } mf_resources;
 
 int32_t mf_abi_version(void);
@@ -115,6 +120,17 @@ mf_status mf_quantize_input(const mf_config* cfg, const void* x, int32_t x_dtype
 mf_status mf_program_weights(const mf_config* cfg, const void* w, int32_t w_dtype, int64_t o,
                              int64_t k, int64_t ldw, void* packed, void* wscale,
                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* Programs the right-hand matrix of a product, b [k, o] with row stride ldb (the
+ * reference programs it as weight_tiles(b.T), quantization.py:82-112 via
+ * simulator.py:121-171), without materialising the transpose.  packed / wscale as
+ * mf_program_weights.  kmajor: NULL, or [ceil(o/cols)*cols, ceil(k/rows)*rows]
+ * bytes receiving the K-major copy of the 8-bit codes that the tensor-core kernels
+ * read; pass it as the start of mf_sliced_mm's workspace with kmajor_ready = 1.
+ * workspace: mf_quantize_workspace(cfg, 1, o, k) bytes. */
+mf_status mf_program_rhs(const mf_config* cfg, const void* b, int32_t b_dtype, int64_t k, int64_t o,
+                         int64_t ldb, void* packed, void* wscale, void* kmajor, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /* Capacity of the library's own scratch for mf_quantize_input_static: 4 MiB,
  * i.e. 1,048,576 FP32 (or 524,288 FP64) group maxima. */

@@ -15,7 +15,7 @@ import torch
 
 PACKAGE = Path(__file__).resolve().parent
 LIBRARY = PACKAGE / "libmemfast_b200.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 MAX_SLICES = 32
 
 STATIC_QUANTIZE_SCRATCH_BYTES = 4 << 20
@@ -53,13 +53,14 @@ class MFConfig(ct.Structure):
 
 class MFSchedule(ct.Structure):
     _fields_ = [("kernel", ct.c_int32), ("tile_n", ct.c_int32), ("tile_o", ct.c_int32),
-                ("arrays", ct.c_int32)]
+                ("arrays", ct.c_int32), ("kmajor_ready", ct.c_int32)]
 
 
 class MFResources(ct.Structure):
     _fields_ = [("workspace_bytes", ct.c_size_t), ("threads", ct.c_int32),
                 ("shared_bytes", ct.c_int32), ("registers", ct.c_int32),
-                ("local_bytes", ct.c_int32), ("blocks_per_sm", ct.c_int32)]
+                ("local_bytes", ct.c_int32), ("blocks_per_sm", ct.c_int32),
+                ("kmajor_bytes", ct.c_size_t)]
 
 
 _VOID = ct.c_void_p
@@ -74,6 +75,8 @@ _SIGNATURES = {
                                      ct.c_int64, _VOID, _VOID, _VOID, _VOID, ct.c_size_t, _VOID]),
     "mf_quantize_input_static": (ct.c_int, [ct.POINTER(MFConfig), _VOID, ct.c_int32, ct.c_int64, ct.c_int64,
                                             ct.c_int64, _VOID, _VOID, _VOID, _VOID]),
+    "mf_program_rhs": (ct.c_int, [ct.POINTER(MFConfig), _VOID, ct.c_int32, ct.c_int64, ct.c_int64, ct.c_int64,
+                                  _VOID, _VOID, _VOID, _VOID, ct.c_size_t, _VOID]),
     "mf_program_weights": (ct.c_int, [ct.POINTER(MFConfig), _VOID, ct.c_int32, ct.c_int64, ct.c_int64,
                                       ct.c_int64, _VOID, _VOID, _VOID, ct.c_size_t, _VOID]),
     "mf_sliced_mm": (ct.c_int, [ct.POINTER(MFConfig), ct.POINTER(MFSchedule), _VOID, _VOID, _VOID, _VOID,
@@ -174,8 +177,8 @@ def native_config(config):
     return c
 
 
-def schedule(kernel=0, tile_n=32, tile_o=64, arrays=2):
-    return MFSchedule(kernel, tile_n, tile_o, arrays)
+def schedule(kernel=0, tile_n=32, tile_o=64, arrays=2, kmajor_ready=0):
+    return MFSchedule(kernel, tile_n, tile_o, arrays, kmajor_ready)
 
 
 def stream_of(device):

@@ -187,6 +187,21 @@ mf_status mf_quantize_input_static(const mf_config* cfg, const void* x, int32_t 
                           MF_STATIC_QUANTIZE_SCRATCH_BYTES, (cudaStream_t)stream);
 }
 
+mf_status mf_program_rhs(const mf_config* cfg, const void* b, int32_t b_dtype, int64_t k, int64_t o, int64_t ldb,
+                         void* packed, void* wscale, void* kmajor, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+    mf_status st = check_config(cfg);
+    if (st) return st;
+    if (!b || !packed || !wscale || !workspace || o < 1 || k < 1 || ldb < o || b_dtype < MF_F32 ||
+        b_dtype > MF_F64) {
+        set_error("mf_program_rhs: invalid operands (k=%lld o=%lld ldb=%lld dtype=%d)", (long long)k, (long long)o,
+                  (long long)ldb, b_dtype);
+        return MF_ERR_INVALID;
+    }
+    return program_rhs(*cfg, b, b_dtype, k, o, ldb, packed, wscale, kmajor, workspace, workspace_bytes,
+                       (cudaStream_t)stream);
+}
+
 mf_status mf_program_weights(const mf_config* cfg, const void* w, int32_t w_dtype, int64_t o, int64_t k,
                              int64_t ldw, void* packed, void* wscale, void* workspace,
                              size_t workspace_bytes, void* stream) {
@@ -218,7 +233,7 @@ static bool use_tc(const mf_config& c, const mf_schedule& s, int32_t m, int32_t 
 }
 
 static mf_schedule schedule_or_default(const mf_schedule* s) {
-    mf_schedule d{0, 32, 64, 2};
+    mf_schedule d{0, 32, 64, 2, 0};
     return s ? *s : d;
 }
 
@@ -259,7 +274,7 @@ mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const 
     }
     mf_schedule s = schedule_or_default(schedule);
     MMArgs a{codes, xscale, packed, wscale, bias, out, n, m, p, out_features, ldo, tile_begin, tile_end,
-             seed, event, vector_offset, stable};
+             seed, event, vector_offset, stable, s.kmajor_ready != 0};
     if (use_packed(*cfg, s, m, stable))
         return tc_packed_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
     if (use_tc(*cfg, s, m, stable)) return tc_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
@@ -280,9 +295,11 @@ mf_status mf_query(const mf_config* cfg, const mf_schedule* schedule, int64_t n,
     if (use_packed(*cfg, s, m, 0)) {
         out->workspace_bytes = tc_packed_workspace_bytes(*cfg, n, m, p, p);
         out->threads = tc_packed_threads();
+        out->kmajor_bytes = (size_t)p * cfg->cols * m * cfg->rows;
     } else if (use_tc(*cfg, s, m, 0)) {
         out->workspace_bytes = tc_workspace_bytes(*cfg, m, p);
         out->threads = tc_block_threads();
+        out->kmajor_bytes = (size_t)p * cfg->cols * m * cfg->rows;
     } else {
         out->workspace_bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, p);
         out->threads = 256;

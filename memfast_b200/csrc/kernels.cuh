@@ -19,6 +19,12 @@ mf_status program_weights(const mf_config& c, const void* w, int dtype, int64_t 
                           int64_t ldw, void* packed, void* wscale, void* workspace,
                           size_t ws_bytes, cudaStream_t stream);
 
+// Program a right-hand [k, o] matrix b (row stride ldb); optionally also write the
+// K-major [p*C, m*R] copy of the packed codes the tensor-core kernels read.
+mf_status program_rhs(const mf_config& c, const void* b, int dtype, int64_t k, int64_t o, int64_t ldb,
+                      void* packed, void* wscale, void* kmajor, void* workspace, size_t ws_bytes,
+                      cudaStream_t stream);
+
 // Everything one sliced product needs, validated by the ABI layer.
 struct MMArgs {
     const void* codes;
@@ -35,6 +41,7 @@ struct MMArgs {
     uint64_t event;
     int64_t vector_offset;
     int32_t stable;
+    int32_t kmajor_ready;   // the workspace already starts with the K-major weight copy
 };
 
 // Largest |signed reconstruction| of one read, as in config.py:114-122.

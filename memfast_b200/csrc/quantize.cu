@@ -158,6 +158,52 @@ __global__ void input_code_kernel(View v, GroupGrid g, const Acc* maxima, const 
     }
 }
 
+// One pass for per-row input groups of gc = 4 * T consecutive FP32 values (T a
+// power of two <= 32): a team of T lanes loads one group with float4 loads, takes
+// its |max| with shuffles, quantises and stores four 8-bit codes per lane, and
+// publishes the group maximum for the per-read scale gather.  Columns past k
+// (up to m * R) get code 0 and do not enter any maximum.
+template <int T>
+__global__ void input_rowgroup_kernel(const float* x, int64_t n, int64_t k, int64_t ldx, int64_t padded_cols,
+                                      int64_t nc, QuantSpec s, float* maxima, uint8_t* codes) {
+    constexpr int GC = 4 * T;
+    const int64_t groups_per_row = padded_cols / GC;
+    const int64_t teams = n * groups_per_row;
+    const int lane_in_team = threadIdx.x % T;
+    const int64_t stride = ((int64_t)gridDim.x * blockDim.x) / T;
+    // Warp-uniform trip count: every lane of a warp takes part in the shuffles.
+    for (int64_t team = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / T;
+         __any_sync(0xFFFFFFFFu, team < teams); team += stride) {
+        const bool active = team < teams;
+        const int64_t r = active ? team / groups_per_row : 0, j = active ? team % groups_per_row : 0;
+        const int64_t c = j * GC + 4 * lane_in_team;
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const float* row = x + r * ldx;
+        if (!active) {
+        } else if (c + 3 < k) {
+            const float4 q = *reinterpret_cast<const float4*>(row + c);
+            v[0] = q.x, v[1] = q.y, v[2] = q.z, v[3] = q.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (c + e < k) v[e] = row[c + e];
+        }
+        float best = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) best = fmaxf(best, fabsf(v[e]));
+#pragma unroll
+        for (int off = T / 2; off > 0; off >>= 1) best = fmaxf(best, __shfl_xor_sync(0xFFFFFFFFu, best, off, T));
+        const float scale = group_scale<float>(best, s);
+        uint32_t word = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (c + e < k) word |= (uint32_t)(quantise<float>(v[e], scale, s) & 0xFF) << (8 * e);
+        if (!active) continue;
+        *reinterpret_cast<uint32_t*>(codes + r * padded_cols + c) = word;
+        if (lane_in_team == 0 && j < nc) maxima[r * nc + j] = best;
+    }
+}
+
 // Input per-read scales: xscale[r, i] for read starts i (replicate padding).
 template <typename Acc, typename ScaleT>
 __global__ void input_scale_kernel(View v, GroupGrid g, const Acc* maxima, const Acc* fixed,
@@ -197,6 +243,46 @@ __global__ void weight_code_kernel(View v, GroupGrid g, const Acc* maxima, Quant
         if (k < m * R && o < p * C) {
             int64_t arr = k / R, r = k % R, t = o / C, c = o % C;
             packed[((arr * p + t) * R + r) * C + c] = (CodeT)tile[j][tx];
+        }
+    }
+}
+
+// One pass for a right-hand FP32 matrix b [K, O] (row-major) with column groups
+// of GR rows: a thread owns one (group, column), keeps the GR values in
+// registers, takes their |max|, quantises, writes the packed [m, p, R, C] tiles
+// (coalesced across the warp's columns) and, when `kmajor` is set, the K-major
+// [p*C, m*R] copy the tensor-core kernels read; the group maximum is published
+// for the per-read scale gather.  Padding rows and columns are zeroed by the host.
+template <int GR>
+__global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_t ldb, QuantSpec s, int R, int C,
+                                    int64_t m, int64_t p, float* maxima, uint8_t* packed, uint8_t* kmajor) {
+    const int64_t groups = (K + GR - 1) / GR;
+    const int64_t total = groups * O;
+    const int64_t kpad = m * R;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i / O, o = i % O, k0 = j * GR;
+        float v[GR];
+        float best = 0.0f;
+#pragma unroll
+        for (int r = 0; r < GR; ++r) {
+            v[r] = k0 + r < K ? b[(k0 + r) * ldb + o] : 0.0f;
+            best = fmaxf(best, fabsf(v[r]));
+        }
+        maxima[j * O + o] = best;
+        const float scale = group_scale<float>(best, s);
+        const int64_t t = o / C, c = o % C;
+        uint32_t word = 0;
+#pragma unroll
+        for (int r = 0; r < GR; ++r) {
+            const int64_t k = k0 + r;
+            const uint32_t code = k < K ? (uint32_t)(quantise<float>(v[r], scale, s) & 0xFF) : 0u;
+            if (k < kpad) packed[(((k / R) * p + t) * R + k % R) * C + c] = (uint8_t)code;
+            word |= code << (8 * (r & 3));
+            if ((r & 3) == 3) {
+                if (kmajor && k < kpad) *reinterpret_cast<uint32_t*>(kmajor + o * kpad + k - 3) = word;
+                word = 0;
+            }
         }
     }
 }
@@ -265,6 +351,17 @@ size_t quantize_workspace_bytes(const mf_config& c, bool weight, int64_t rows, i
     return (size_t)(nr * g.nc) * elem + 256;
 }
 
+// The one-pass kernel applies to FP32 rows with 16-byte-aligned rows, dynamic
+// per-row groups of 4 * {1,2,...,32} values and 8-bit codes.
+static int rowgroup_team(const mf_config& c, const View& v, const GroupGrid& g, const void* fixed) {
+    if (fixed || c.wide_codes || v.transposed || v.dtype != MF_F32 || g.gr != 1) return 0;
+    if (((uintptr_t)v.data & 15) || (v.ld % 4)) return 0;
+    const int64_t padded = ((v.cols + c.rows - 1) / c.rows) * c.rows;
+    for (int team = 1; team <= 32; team *= 2)
+        if (g.gc == 4 * team && padded % g.gc == 0) return team;
+    return 0;
+}
+
 template <typename Acc, typename ScaleT>
 static mf_status run_input(const mf_config& c, const View& v, const GroupGrid& g, const QuantSpec& s,
                            const void* fixed, void* codes, void* xscale, void* workspace,
@@ -273,6 +370,30 @@ static mf_status run_input(const mf_config& c, const View& v, const GroupGrid& g
     const int64_t n = v.rows, k = v.cols, m = (k + c.rows - 1) / c.rows;
     Acc* maxima = static_cast<Acc*>(workspace);
     const Acc* fx = static_cast<const Acc*>(fixed);
+    const int team = sizeof(Acc) == 4 ? rowgroup_team(c, v, g, fixed) : 0;
+    if (team) {
+        const int64_t padded = m * c.rows;
+        const int64_t lanes = n * (padded / g.gc) * team;
+        const int blocks = grid_for((lanes + threads - 1) / threads * threads, threads);
+#define MF_ROWGROUP(TEAM)                                                                                    \
+    input_rowgroup_kernel<TEAM><<<blocks, threads, 0, stream>>>(static_cast<const float*>(v.data), n, k, v.ld, \
+                                                                padded, g.nc, s, reinterpret_cast<float*>(maxima), \
+                                                                static_cast<uint8_t*>(codes))
+        switch (team) {
+            case 1: MF_ROWGROUP(1); break;
+            case 2: MF_ROWGROUP(2); break;
+            case 4: MF_ROWGROUP(4); break;
+            case 8: MF_ROWGROUP(8); break;
+            case 16: MF_ROWGROUP(16); break;
+            default: MF_ROWGROUP(32); break;
+        }
+#undef MF_ROWGROUP
+        MF_LAUNCH_CHECK("input_rowgroup_kernel");
+        input_scale_kernel<Acc, ScaleT><<<grid_for(n * m * c.reads, threads), threads, 0, stream>>>(
+            v, g, maxima, fx, s, c.rows, c.read_rows, c.reads, m, static_cast<ScaleT*>(xscale));
+        MF_LAUNCH_CHECK("input_scale_kernel");
+        return MF_OK;
+    }
     if (!fx) {
         MF_CHECK_CUDA(cudaMemsetAsync(maxima, 0, need, stream), "memset group maxima");
         group_amax_kernel<Acc><<<grid_for((n * k + 7) / 8, threads), threads, 0, stream>>>(v, g, maxima);
@@ -339,6 +460,59 @@ static mf_status run_weights(const mf_config& c, const View& v, const GroupGrid&
         v, g, maxima, s, c.rows, c.cols, c.read_rows, c.reads, m, p, static_cast<ScaleT*>(wscale));
     MF_LAUNCH_CHECK("weight_scale_kernel");
     return MF_OK;
+}
+
+mf_status program_rhs(const mf_config& c, const void* b, int dtype, int64_t k, int64_t o, int64_t ldb,
+                      void* packed, void* wscale, void* kmajor, void* workspace, size_t ws_bytes,
+                      cudaStream_t stream) {
+    View v{b, dtype, k, o, ldb, 0};  // logical [k, o] = b
+    GroupGrid g = groups_of(k, o, c.w_group_rows, c.w_group_cols);
+    QuantSpec s = spec_of(c.weight_bits, c.weight_signed, c.bw_e);
+    size_t need = quantize_workspace_bytes(c, true, o, k) - 256;
+    if (ws_bytes < need) {
+        set_error("weight workspace too small: %zu < %zu bytes", ws_bytes, need);
+        return MF_ERR_RESOURCE;
+    }
+    const int64_t m = (k + c.rows - 1) / c.rows, p = (o + c.cols - 1) / c.cols;
+    const bool dbl = uses_double(c, c.weight_bits);
+    // The fused pass stores the K-major copy as 32-bit words: rows of m*R bytes
+    // must keep them aligned.
+    const bool words_aligned = !kmajor || ((m * c.rows) % 4 == 0 && (reinterpret_cast<uintptr_t>(kmajor) & 3) == 0);
+    const bool fused = !dbl && !c.wide && !c.wide_codes && dtype == MF_F32 && g.gc == 1 &&
+                       (g.gr == 32 || g.gr == 64) && words_aligned;
+    if (fused) {
+        const size_t packed_bytes = (size_t)m * p * c.rows * c.cols;
+        if (k < m * c.rows || o < p * c.cols) {
+            MF_CHECK_CUDA(cudaMemsetAsync(packed, 0, packed_bytes, stream), "zero packed padding");
+            if (kmajor) MF_CHECK_CUDA(cudaMemsetAsync(kmajor, 0, packed_bytes, stream), "zero K-major padding");
+        }
+        const int threads = 256;
+        const int64_t work = ((k + g.gr - 1) / g.gr) * o;
+        float* maxima = static_cast<float*>(workspace);
+        if (g.gr == 32)
+            rhs_colgroup_kernel<32><<<grid_for(work, threads), threads, 0, stream>>>(
+                static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
+                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor));
+        else
+            rhs_colgroup_kernel<64><<<grid_for(work, threads), threads, 0, stream>>>(
+                static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
+                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor));
+        MF_LAUNCH_CHECK("rhs_colgroup_kernel");
+        weight_scale_kernel<float, float><<<grid_for(m * c.reads * p * c.cols, threads), threads, 0, stream>>>(
+            v, g, maxima, s, c.rows, c.cols, c.read_rows, c.reads, m, p, static_cast<float*>(wscale));
+        MF_LAUNCH_CHECK("weight_scale_kernel");
+        return MF_OK;
+    }
+    mf_status st;
+    if (dbl) st = run_weights<double, double>(c, v, g, s, packed, wscale, workspace, need, stream);
+    else if (c.wide) st = run_weights<float, double>(c, v, g, s, packed, wscale, workspace, need, stream);
+    else st = run_weights<float, float>(c, v, g, s, packed, wscale, workspace, need, stream);
+    if (st || !kmajor) return st;
+    if (c.wide_codes) {
+        set_error("a K-major copy needs 8-bit codes");
+        return MF_ERR_UNSUPPORTED;
+    }
+    return tc_weights_kmajor(packed, static_cast<uint8_t*>(kmajor), (int)m, (int)p, c.rows, c.cols, stream);
 }
 
 mf_status program_weights(const mf_config& c, const void* w, int dtype, int64_t o, int64_t k,

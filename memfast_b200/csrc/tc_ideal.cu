@@ -737,7 +737,7 @@ mf_status tc_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, siz
     const long long O = (long long)a.p * c.cols;
     const int MR = a.m * c.reads;
     uint8_t* wk = static_cast<uint8_t*>(workspace);
-    mf_status r = tc_weights_kmajor(a.packed, wk, a.m, a.p, c.rows, c.cols, st);
+    mf_status r = a.kmajor_ready ? MF_OK : tc_weights_kmajor(a.packed, wk, a.m, a.p, c.rows, c.cols, st);
     if (r) return r;
     CUtensorMap mx, mw, mxs, mws;
     r = tc_make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n, (uint64_t)K,

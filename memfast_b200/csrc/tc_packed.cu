@@ -963,7 +963,7 @@ mf_status tc_packed_sliced_mm(const mf_config& c, const MMArgs& a, void* workspa
     uint8_t* wk = static_cast<uint8_t*>(workspace);
     const size_t kmajor = ((size_t)O * K + 255) / 256 * 256;
     unsigned* flags = reinterpret_cast<unsigned*>(wk + kmajor);
-    mf_status r = tc_weights_kmajor(a.packed, wk, a.m, a.p, c.rows, c.cols, st);
+    mf_status r = a.kmajor_ready ? MF_OK : tc_weights_kmajor(a.packed, wk, a.m, a.p, c.rows, c.cols, st);
     if (r) return r;
     CUtensorMap mx, mw, mxs, mws;
     r = tc_make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n, (uint64_t)K, tp::KR,

@@ -9,6 +9,7 @@ with a clear error instead of silently dropping gradients.
 """
 
 import itertools
+import math
 import weakref
 from pathlib import Path
 
@@ -113,7 +114,8 @@ def _product(a, b, simulator, cached_rhs=None):
         )
     config = simulator.config
     matrix = simulator._matrix_for(b if cached_rhs is None else cached_rhs,
-                                   checked=_checked(b, config, config.weight_bits))
+                                   checked=_checked(b, config, config.weight_bits),
+                                   rows=math.prod(a.shape[:-1]))
     with torch.no_grad():
         return matrix._forward(a.detach(), checked=_checked(a, config, config.activation_bits))
 

@@ -159,10 +159,14 @@ def input_tiles(value, config, fixed_scale=None, *, checked=False):
     return codes, xscale
 
 
-def weight_tiles(weight, config, *, checked=False):
-    """PyTorch-layout [O, K] floating weights -> (packed [m,p,R,C], weight_scale [m*reads,p,C]).
+def weight_tiles(weight, config, *, checked=False, kmajor=None):
+    """PyTorch-layout [O, K] floating weights -> (packed [m,p,R,C], weight_scale [m*reads,p,C], kmajor_written).
 
-    ``checked``: the caller verified the weights finite in the quantiser's dtype."""
+    ``checked``: the caller verified the weights finite in the quantiser's dtype.
+    ``kmajor``: optional uint8 buffer for the K-major code copy of the tensor-core
+    kernels; it is filled (and ``kmajor_written`` is True) when the weights are the
+    transpose of a row-major [K, O] matrix, the right-hand operand of ``mm``, which
+    is then programmed in place through ``mf_program_rhs``."""
     _require_cuda(weight, "weight")
     o, k = weight.shape
     if not config.weight_signed and (weight < 0).any():
@@ -171,13 +175,25 @@ def weight_tiles(weight, config, *, checked=False):
             "use map_quantized with zero_points for affine weights"
         )
     weight = _as_native_float(weight, config, config.weight_bits, checked)
-    if weight.stride(-1) != 1:
-        weight = weight.contiguous()
     r, c = config.array_size
     m, p = math.ceil(k / r), math.ceil(o / c)
     packed = torch.empty((m, p, r, c), dtype=_code_dtype(config), device=weight.device)
     wscale = torch.empty((m * config.reads_per_array, p, c), dtype=_scale_dtype(config), device=weight.device)
     workspace, need = _workspace(config, True, o, k, weight.device)
+    if weight.stride(0) == 1 and weight.stride(1) >= max(o, 1):
+        # The transpose of a row-major [K, O] matrix: program it in place.
+        rhs = weight.T
+        _lib.check(
+            _lib.load().mf_program_rhs(
+                _lib.native_config(config), _lib.ptr(rhs), _lib.DTYPES[rhs.dtype], k, o, rhs.stride(0),
+                _lib.ptr(packed), _lib.ptr(wscale), _lib.ptr(kmajor), _lib.ptr(workspace), need,
+                _lib.stream_of(weight.device),
+            ),
+            "mf_program_rhs",
+        )
+        return packed, wscale, kmajor is not None
+    if weight.stride(-1) != 1:
+        weight = weight.contiguous()
     _lib.check(
         _lib.load().mf_program_weights(
             _lib.native_config(config), _lib.ptr(weight), _lib.DTYPES[weight.dtype], o, k, weight.stride(0),
@@ -185,7 +201,7 @@ def weight_tiles(weight, config, *, checked=False):
         ),
         "mf_program_weights",
     )
-    return packed, wscale
+    return packed, wscale, False
 
 
 def pack_weight(code, scale, config):

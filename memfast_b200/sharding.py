@@ -46,7 +46,7 @@ def sharded_mm(a_local, b, *, simulator, row_offset):
     _operands(a_local, b)
     if a_local.device != simulator.device:
         raise ValueError("operands and simulator must use the same device")
-    matrix = simulator._matrix_for(b, checked=_checked(b, config, config.weight_bits))
+    matrix = simulator._matrix_for(b, checked=_checked(b, config, config.weight_bits), rows=a_local.shape[0])
     with torch.no_grad():
         return matrix._forward(a_local.detach(), checked=_checked(a_local, config, config.activation_bits),
                                vector_offset=row_offset)

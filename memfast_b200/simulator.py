@@ -181,14 +181,15 @@ class Simulator:
 
         return matmul(input, other, simulator=self, out=out)
 
-    def _matrix_for(self, matrix, checked=False):
+    def _matrix_for(self, matrix, checked=False, rows=1):
         """Reprogram the RHS and reuse the cached program if its codes are unchanged.
 
         A reprogrammed RHS keeps the cached program's name (sampling seed) and read
         event, so in default mode the old and new programs give identical results
         and the new one is kept without comparing codes on the host.  Tuned mode
         compares, because the cached program also carries its schedule selections.
-        ``checked``: the caller verified the matrix finite in the quantiser's dtype.
+        ``checked``: the caller verified the matrix finite in the quantiser's dtype;
+        ``rows``: vectors of the coming product (sizes the tensor-core workspace).
         """
         identity = id(matrix)
         record = self._matrix_cache.get(identity)
@@ -203,7 +204,7 @@ class Simulator:
             self._next_id += 1
         else:
             name = previous.name
-        programmed = AnalogMatrix(matrix.T, self, name=name, _checked=checked)
+        programmed = AnalogMatrix(matrix.T, self, name=name, _checked=checked, _rows=rows)
         if (
             self.mode == "tuned"
             and same_tensor
@@ -347,12 +348,15 @@ class AnalogMatrix(nn.Module):
     """Programmed matrix with optional digital zero-point compensation."""
 
     def __init__(self, weight, simulator, *, bias=None, name="matrix", scales=None, zero_points=None,
-                 _checked=False):
+                 _checked=False, _rows=1):
         super().__init__()
         if weight.ndim != 2 or min(weight.shape) < 1:
             raise ValueError("weight must be a nonempty [O,K] matrix")
         if not _checked and not finite_flags(weight)[0]:
             raise ValueError("weights must be finite")
+        # Workspace of the tensor-core kernels, reused across calls: it starts with
+        # the K-major copy of the packed codes (valid while _ws_ready is set).
+        self._ws, self._ws_bytes, self._kmajor_bytes, self._ws_ready, self._ws_stream = None, 0, 0, False, None
         self.simulator, self.config, self.name = simulator, simulator.config, name
         self.out_features, self.in_features = weight.shape
         self.p = math.ceil(self.out_features / self.config.array_size[1])
@@ -363,7 +367,12 @@ class AnalogMatrix(nn.Module):
                 raise ValueError("unquantized weight must be floating")
             if zero_points is not None:
                 raise ValueError("zero_points requires imported integer codes and scales")
-            packed, scale = weight_tiles(weight.detach().to(simulator.device), self.config, checked=_checked)
+            self._prepare_workspace(math.ceil(self.in_features / self.config.array_size[0]), simulator.device,
+                                    _rows)
+            packed, scale, written = weight_tiles(
+                weight.detach().to(simulator.device), self.config, checked=_checked,
+                kmajor=None if self._ws is None else self._ws[: self._kmajor_bytes])
+            self._ws_ready = written
         else:
             if weight.dtype not in (torch.uint8, torch.int8, torch.int16, torch.int32, torch.int64):
                 raise ValueError("imported weight codes must have an integer dtype")
@@ -447,6 +456,7 @@ class AnalogMatrix(nn.Module):
             if key in state_dict and self._buffers[name] is None:
                 self._buffers[name] = torch.empty_like(state_dict[key], device=self.packed.device)
         super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
+        self._drop_workspace()
         if not torch.isfinite(self.weight_scale).all() or (self.weight_scale < 0).any():
             raise ValueError("checkpoint weight scales exceed the reconstruction dtype")
         if self.bias is not None and not torch.isfinite(self.bias).all():
@@ -469,6 +479,7 @@ class AnalogMatrix(nn.Module):
                 self._buffers[name] = original.to(device=transformed.device)
             if transformed.device != original.device:
                 self._prepared.clear()
+                self._drop_workspace()
         return self
 
     def get_extra_state(self):
@@ -508,16 +519,40 @@ class AnalogMatrix(nn.Module):
         replacement = AnalogMatrix(matrix.T, self.simulator, bias=self.bias, name=self.name)
         self.packed.copy_(replacement.packed)
         self.weight_scale.copy_(replacement.weight_scale)
+        self._drop_workspace()
         self.zero_correction = None
         self._prepared.clear()
         self.reset_read()
         return self
 
     # --------------------------------------------------------------- engine
-    def _workspace_size(self, n, schedule):
+    def _kmajor_size(self, m, schedule):
+        """Bytes of the K-major weight copy the schedule's kernel reads (0: none)."""
+        resources = _lib.MFResources()
+        native = _lib.schedule(**schedule)
+        _lib.check(
+            _lib.load().mf_query(_lib.native_config(self.config), ct.byref(native), 1, m, self.p,
+                                 ct.byref(resources)),
+            "mf_query",
+        )
+        return resources.kmajor_bytes
+
+    def _prepare_workspace(self, m, device, rows=1):
+        """Reserve the persistent workspace (sized for ``rows`` vectors) when the default
+        schedule reads a K-major copy, so that programming can write that copy in place."""
+        self._kmajor_bytes = self._kmajor_size(m, default_schedule(self.config))
+        if self._kmajor_bytes:
+            need = self._workspace_size(max(rows, 1), default_schedule(self.config), m)
+            self._ws = torch.empty(need, dtype=torch.uint8, device=device)
+            self._ws_bytes, self._ws_stream = need, _lib.stream_of(device).value
+
+    def _drop_workspace(self):
+        self._ws, self._ws_bytes, self._ws_ready = None, 0, False
+
+    def _workspace_size(self, n, schedule, m=None):
         size = ct.c_size_t()
         native = _lib.schedule(**schedule)
-        m = self.packed.shape[0]
+        m = self.packed.shape[0] if m is None else m
         _lib.check(
             _lib.load().mf_sliced_mm_workspace(_lib.native_config(self.config), ct.byref(native), n, m,
                                                self.p, 0, self.p, ct.byref(size)),
@@ -533,19 +568,39 @@ class AnalogMatrix(nn.Module):
         output = torch.empty((n, self.out_features), device=q.device, dtype=dtype)
         fuse_bias = self.bias is not None and self.zero_correction is None
         workspace_bytes = self._workspace_size(n, schedule)
-        workspace = torch.empty(max(workspace_bytes, 1), dtype=torch.uint8, device=q.device)
-        native = _lib.schedule(**schedule)
         packed = self.packed.contiguous()
+        stream = _lib.stream_of(q.device)
+        kmajor_ready = 0
+        kmajor_bytes = 0 if stable else self._kmajor_size(packed.shape[0], schedule)
+        if kmajor_bytes:
+            # Tensor-core kernels: keep the workspace, whose leading K-major weight copy
+            # stays valid until the codes change.  A call on another stream gets a fresh
+            # one; a larger one keeps the copy.
+            if self._ws is None or self._ws_stream != stream.value:
+                self._ws = torch.empty(workspace_bytes, dtype=torch.uint8, device=q.device)
+                self._ws_bytes, self._ws_stream, self._ws_ready = workspace_bytes, stream.value, False
+            elif self._ws_bytes < workspace_bytes:
+                grown = torch.empty(workspace_bytes, dtype=torch.uint8, device=q.device)
+                if self._ws_ready:
+                    grown[:kmajor_bytes].copy_(self._ws[:kmajor_bytes])
+                self._ws, self._ws_bytes = grown, workspace_bytes
+            self._kmajor_bytes = kmajor_bytes
+            workspace, workspace_bytes, kmajor_ready = self._ws, self._ws_bytes, int(self._ws_ready)
+        else:
+            workspace = torch.empty(max(workspace_bytes, 1), dtype=torch.uint8, device=q.device)
+        native = _lib.schedule(**schedule, kmajor_ready=kmajor_ready)
         _lib.check(
             _lib.load().mf_sliced_mm(
                 _lib.native_config(self.config), ct.byref(native), _lib.ptr(q), _lib.ptr(xscale),
                 _lib.ptr(packed), _lib.ptr(self.weight_scale.contiguous()),
                 _lib.ptr(self.bias) if fuse_bias else None, _lib.ptr(output), n, packed.shape[0], self.p,
                 self.out_features, self.out_features, 0, self.p, self.seed & 0xFFFFFFFF, event,
-                vector_offset, int(stable), _lib.ptr(workspace), workspace_bytes, _lib.stream_of(q.device),
+                vector_offset, int(stable), _lib.ptr(workspace), workspace_bytes, stream,
             ),
             "mf_sliced_mm",
         )
+        if workspace is self._ws:
+            self._ws_ready = True
         if self.zero_correction is not None:
             bits = self.config.activation_bits
             signed = q.to(torch.int64).reshape(n, -1)

@@ -37,7 +37,7 @@ def test_quantisation_buffers_bit_exact(mf, case):
     from memfast_b200.quantization import input_tiles, weight_tiles
 
     config, arrays, _ = load_case(case)
-    packed, wscale = weight_tiles(cuda(arrays["B"]).T, config)
+    packed, wscale, _ = weight_tiles(cuda(arrays["B"]).T, config)
     q, xscale = input_tiles(cuda(arrays["A"]), config)
     torch.cuda.synchronize()
     assert np.array_equal(packed.cpu().numpy(), arrays["packed"])
