@@ -93,6 +93,19 @@ typedef struct {
                              bytes at the start of its workspace (see kmajor_ready) */
 } mf_resources;
 
+/* One channel group of a 2-D convolution over an NCHW input (AnalogConv2d,
+ * memfast/nn/convolution.py:10-62, which lowers it to F.unfold patches times one
+ * programmed matrix per group). */
+typedef struct {
+    int64_t batch, channels, height, width;          /* x: [batch, channels, height, width] */
+    int64_t stride_n, stride_c, stride_h, stride_w;  /* element strides of x (any layout) */
+    int32_t kernel_h, kernel_w;
+    int32_t stride_y, stride_x;                      /* Conv2d.stride */
+    int32_t pad_h, pad_w;                            /* zero padding (Conv2d.padding) */
+    int32_t dilation_h, dilation_w;
+    int32_t channel_begin, group_channels;           /* the group's input channels */
+} mf_conv2d;
+
 int32_t mf_abi_version(void);
 
 /* Message of this thread's last failure ("" if none).  Returns its length. */
@@ -162,6 +175,24 @@ mf_status mf_quantize_input_static(const mf_config* cfg, const void* x, int32_t 
  * mf_program_weights (is_weight=1, shape [o,k]) needs. */
 mf_status mf_quantize_workspace(const mf_config* cfg, int32_t is_weight, int64_t rows,
                                 int64_t cols, size_t* bytes);
+
+/* mf_quantize_input on the patch matrix of one convolution group without
+ * building it (replaces F.unfold + transpose + input_tiles,
+ * memfast/nn/convolution.py:49-55 with quantization.py:115-137).  The patch
+ * matrix has rows v = (b*OH + oh)*OW + ow (mf_conv_output gives OH, OW) and
+ * columns k = (c*kernel_h + i)*kernel_w + j for c < group_channels, holding
+ * x[b, channel_begin + c, oh*stride_y - pad_h + i*dilation_h,
+ *   ow*stride_x - pad_w + j*dilation_w] (0 outside x).  codes / xscale /
+ * fixed_scale as mf_quantize_input for that [rows, cols] matrix.  nonfinite: a
+ * device uint32 set to 1 when a quantised value is not finite (the reference
+ * raises ValueError then; results are invalid), else 0.
+ * workspace: mf_quantize_workspace(cfg, 0, rows, cols) bytes. */
+mf_status mf_quantize_conv_input(const mf_config* cfg, const mf_conv2d* conv, const void* x, int32_t x_dtype,
+                                 const void* fixed_scale, void* codes, void* xscale, uint32_t* nonfinite,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Output height and width of a convolution group; MF_ERR_INVALID for a bad geometry. */
+mf_status mf_conv_output(const mf_conv2d* conv, int64_t* out_height, int64_t* out_width);
 
 /* The analog product for output tiles [tile_begin, tile_end): replaces
  * cuda.partial (cuda.py:322-373) and the scale/sum epilogue of

@@ -63,6 +63,14 @@ class MFResources(ct.Structure):
                 ("kmajor_bytes", ct.c_size_t)]
 
 
+class MFConv2d(ct.Structure):
+    _fields_ = [(name, ct.c_int64) for name in ("batch", "channels", "height", "width",
+                                                "stride_n", "stride_c", "stride_h", "stride_w")] + \
+               [(name, ct.c_int32) for name in ("kernel_h", "kernel_w", "stride_y", "stride_x", "pad_h",
+                                                "pad_w", "dilation_h", "dilation_w", "channel_begin",
+                                                "group_channels")]
+
+
 _VOID = ct.c_void_p
 _SIGNATURES = {
     "mf_abi_version": (ct.c_int32, []),
@@ -77,6 +85,9 @@ _SIGNATURES = {
                                             ct.c_int64, _VOID, _VOID, _VOID, _VOID]),
     "mf_program_rhs": (ct.c_int, [ct.POINTER(MFConfig), _VOID, ct.c_int32, ct.c_int64, ct.c_int64, ct.c_int64,
                                   _VOID, _VOID, _VOID, _VOID, ct.c_size_t, _VOID]),
+    "mf_quantize_conv_input": (ct.c_int, [ct.POINTER(MFConfig), ct.POINTER(MFConv2d), _VOID, ct.c_int32,
+                                          _VOID, _VOID, _VOID, _VOID, _VOID, ct.c_size_t, _VOID]),
+    "mf_conv_output": (ct.c_int, [ct.POINTER(MFConv2d), ct.POINTER(ct.c_int64), ct.POINTER(ct.c_int64)]),
     "mf_program_weights": (ct.c_int, [ct.POINTER(MFConfig), _VOID, ct.c_int32, ct.c_int64, ct.c_int64,
                                       ct.c_int64, _VOID, _VOID, _VOID, ct.c_size_t, _VOID]),
     "mf_sliced_mm": (ct.c_int, [ct.POINTER(MFConfig), ct.POINTER(MFSchedule), _VOID, _VOID, _VOID, _VOID,

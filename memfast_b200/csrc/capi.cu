@@ -129,6 +129,54 @@ mf_status mf_quantize_input(const mf_config* cfg, const void* x, int32_t x_dtype
                           workspace_bytes, (cudaStream_t)stream);
 }
 
+static bool conv_geometry(const mf_conv2d* cv, int64_t* oh, int64_t* ow) {
+    if (!cv || cv->batch < 0 || cv->channels < 1 || cv->height < 1 || cv->width < 1 || cv->kernel_h < 1 ||
+        cv->kernel_w < 1 || cv->stride_y < 1 || cv->stride_x < 1 || cv->pad_h < 0 || cv->pad_w < 0 ||
+        cv->dilation_h < 1 || cv->dilation_w < 1 || cv->channel_begin < 0 || cv->group_channels < 1 ||
+        (int64_t)cv->channel_begin + cv->group_channels > cv->channels || cv->height > INT32_MAX / 2 ||
+        cv->width > INT32_MAX / 2 || cv->stride_n < 0 || cv->stride_c < 0 || cv->stride_h < 0 || cv->stride_w < 0) {
+        set_error("invalid convolution geometry");
+        return false;
+    }
+    *oh = conv_output_extent(cv->height, cv->kernel_h, cv->stride_y, cv->pad_h, cv->dilation_h);
+    *ow = conv_output_extent(cv->width, cv->kernel_w, cv->stride_x, cv->pad_w, cv->dilation_w);
+    if (*oh < 1 || *ow < 1) {
+        set_error("convolution window larger than the padded input");
+        return false;
+    }
+    return true;
+}
+
+mf_status mf_conv_output(const mf_conv2d* conv, int64_t* out_height, int64_t* out_width) {
+    int64_t oh = 0, ow = 0;
+    if (!out_height || !out_width || !conv_geometry(conv, &oh, &ow)) {
+        if (!out_height || !out_width) set_error("mf_conv_output: NULL output");
+        return MF_ERR_INVALID;
+    }
+    *out_height = oh;
+    *out_width = ow;
+    return MF_OK;
+}
+
+mf_status mf_quantize_conv_input(const mf_config* cfg, const mf_conv2d* conv, const void* x, int32_t x_dtype,
+                                 const void* fixed_scale, void* codes, void* xscale, uint32_t* nonfinite,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+    mf_status st = check_config(cfg);
+    if (st) return st;
+    int64_t oh = 0, ow = 0;
+    if (!conv_geometry(conv, &oh, &ow)) return MF_ERR_INVALID;
+    if (!x || !codes || !xscale || !nonfinite || x_dtype < MF_F32 || x_dtype > MF_F64) {
+        set_error("mf_quantize_conv_input: invalid operands (dtype=%d)", x_dtype);
+        return MF_ERR_INVALID;
+    }
+    if (!fixed_scale && !workspace) {
+        set_error("mf_quantize_conv_input: dynamic scales need a workspace");
+        return MF_ERR_INVALID;
+    }
+    return quantize_conv_input(*cfg, *conv, x, x_dtype, fixed_scale, codes, xscale, nonfinite, workspace,
+                               workspace_bytes, (cudaStream_t)stream);
+}
+
 }  // extern "C"
 
 // Group-maxima scratch of mf_quantize_input_static.  It is a module global so

@@ -19,6 +19,15 @@ mf_status program_weights(const mf_config& c, const void* w, int dtype, int64_t 
                           int64_t ldw, void* packed, void* wscale, void* workspace,
                           size_t ws_bytes, cudaStream_t stream);
 
+// Output extent of a convolution along one axis (0 when the window does not fit).
+int64_t conv_output_extent(int64_t size, int32_t kernel, int32_t stride, int32_t pad, int32_t dilation);
+
+// Quantise the patch matrix of one channel group of a 2-D convolution straight
+// from the NCHW input (no unfold); same buffers as quantize_input on the patches.
+mf_status quantize_conv_input(const mf_config& c, const mf_conv2d& cv, const void* x, int dtype,
+                              const void* fixed, void* codes, void* xscale, uint32_t* nonfinite,
+                              void* workspace, size_t ws_bytes, cudaStream_t stream);
+
 // Program a right-hand [k, o] matrix b (row stride ldb); optionally also write the
 // K-major [p*C, m*R] copy of the packed codes the tensor-core kernels read.
 mf_status program_rhs(const mf_config& c, const void* b, int dtype, int64_t k, int64_t o, int64_t ldb,

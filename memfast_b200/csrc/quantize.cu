@@ -303,6 +303,170 @@ __global__ void weight_scale_kernel(View v, GroupGrid g, const Acc* maxima, Quan
     }
 }
 
+// ---- 2-D convolution patches (implicit im2col) --------------------------------
+// The patch matrix of one channel group, in F.unfold order
+// (memfast/nn/convolution.py:49-55): row v = (b * OH + oh) * OW + ow, column
+// k = (c * KH + i) * KW + j for the group's channels c in [0, CG); element
+// x[b, C0 + c, oh * SY - PH + i * DH, ow * SX - PW + j * DW], zero outside x.
+struct ConvGeom {
+    const void* x;
+    int dtype;
+    int64_t sb, sc, sh, sw;  // element strides of x
+    int32_t H, W, C0, KH, KW, SY, SX, PH, PW, DH, DW, OH, OW;
+    int64_t rows, cols;      // batch * OH * OW, CG * KH * KW
+};
+
+struct PatchRow {
+    int64_t base;      // offset of x[b, C0, 0, 0]
+    int32_t ih0, iw0;  // input coordinates of the window's top-left tap
+};
+
+__device__ __forceinline__ PatchRow patch_row(const ConvGeom& g, int64_t v) {
+    const int64_t plane = (int64_t)g.OH * g.OW;
+    const int64_t b = v / plane;
+    const int32_t l = (int32_t)(v - b * plane);
+    const int32_t oh = l / g.OW, ow = l - oh * g.OW;
+    return PatchRow{b * g.sb + (int64_t)g.C0 * g.sc, oh * g.SY - g.PH, ow * g.SX - g.PW};
+}
+
+// Column k as (channel, kernel row, kernel column); callers then step it.
+struct Tap {
+    int32_t c, i, j;
+    __device__ __forceinline__ void at(const ConvGeom& g, int64_t k) {
+        const int32_t taps = g.KH * g.KW;
+        c = (int32_t)(k / taps);
+        const int32_t rem = (int32_t)(k - (int64_t)c * taps);
+        i = rem / g.KW;
+        j = rem - i * g.KW;
+    }
+    __device__ __forceinline__ void next(const ConvGeom& g) {
+        if (++j == g.KW) {
+            j = 0;
+            if (++i == g.KH) {
+                i = 0;
+                ++c;
+            }
+        }
+    }
+};
+
+// Offset of the tap in x, or -1 in the zero padding.
+__device__ __forceinline__ int64_t tap_offset(const ConvGeom& g, const PatchRow& r, const Tap& t) {
+    const int32_t ih = r.ih0 + t.i * g.DH, iw = r.iw0 + t.j * g.DW;
+    if ((unsigned)ih >= (unsigned)g.H || (unsigned)iw >= (unsigned)g.W) return -1;
+    return r.base + (int64_t)t.c * g.sc + (int64_t)ih * g.sh + (int64_t)iw * g.sw;
+}
+
+__device__ __forceinline__ bool finite_as_stored(const void* base, int dtype, int64_t index) {
+    return isfinite(load_as<double>(base, dtype, index));  // exact widening of every stored dtype
+}
+
+// Group maxima of the patch matrix.  A warp owns 32 consecutive rows (one per
+// lane) and one column group; it walks the group's columns with each load
+// coalesced across the lanes' neighbouring output positions and keeps the
+// running |max| in registers.  Per-row groups store the maximum; groups spanning
+// rows combine with an atomic max (the caller zeroes them).  A non-finite value in
+// the compute dtype raises *nonfinite (grouped_quantize's check, quantization.py:14-15).
+template <typename Acc>
+__global__ void conv_amax_kernel(ConvGeom g, GroupGrid gg, Acc* maxima, unsigned* nonfinite) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row_blocks = (g.rows + 31) / 32;
+    const int64_t items = row_blocks * gg.nc;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t item = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; item < items; item += warps) {
+        const int64_t rb = item / gg.nc, group = item - rb * gg.nc;
+        const int64_t v = rb * 32 + lane;
+        const bool active = v < g.rows;
+        const PatchRow r = patch_row(g, active ? v : 0);
+        const int64_t k0 = group * gg.gc, k1 = k0 + gg.gc < g.cols ? k0 + gg.gc : g.cols;
+        Tap t;
+        t.at(g, k0);
+        Acc best = Acc(0);
+        bool bad = false;
+#pragma unroll 4
+        for (int64_t k = k0; k < k1; ++k) {
+            const int64_t off = active ? tap_offset(g, r, t) : -1;
+            const Acc x = off >= 0 ? load_as<Acc>(g.x, g.dtype, off) : Acc(0);
+            bad |= !isfinite(x);
+            const Acc a = x < Acc(0) ? -x : x;
+            best = a > best ? a : best;
+            t.next(g);
+        }
+        if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(nonfinite, 1u);
+        if (active) {
+            Acc* slot = &maxima[(v / gg.gr) * gg.nc + group];
+            if (gg.gr == 1) *slot = best;
+            else atomic_max_nonneg(slot, best);
+        }
+    }
+}
+
+// Codes of the patch matrix, [rows, padded] row-major (zero past cols).  A
+// 256-thread block owns a tile of 32 rows x 128 columns: each warp quantises 16
+// columns for the 32 rows (lanes; loads coalesced along the output positions),
+// the codes are staged in shared memory and leave as whole 128-column row
+// segments.  With a fixed per-column scale the values are checked finite in their
+// stored dtype (input_tiles' check, quantization.py:124-125).
+template <typename Acc, typename CodeT>
+__global__ void __launch_bounds__(256) conv_code_kernel(ConvGeom g, GroupGrid gg, const Acc* maxima,
+                                                        const Acc* fixed, QuantSpec s, int64_t padded,
+                                                        CodeT* codes, unsigned* nonfinite) {
+    constexpr int TR = 32, TC = 128, PITCH = TC + (sizeof(CodeT) == 1 ? 4 : 1);
+    __shared__ __align__(16) CodeT tile[TR][PITCH];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t row_tiles = (g.rows + TR - 1) / TR, col_tiles = (padded + TC - 1) / TC;
+    const bool words = sizeof(CodeT) == 1 && (padded & 3) == 0;
+    for (int64_t tile_id = blockIdx.x; tile_id < row_tiles * col_tiles; tile_id += gridDim.x) {
+        const int64_t rt = tile_id / col_tiles, ct = tile_id - rt * col_tiles;
+        const int64_t v = rt * TR + lane;
+        const bool active = v < g.rows;
+        const PatchRow r = patch_row(g, active ? v : 0);
+        const int64_t kb = ct * TC + warp * 16;
+        Tap t;
+        t.at(g, kb < g.cols ? kb : 0);
+        int64_t cached = -1;
+        Acc scale = Acc(1);
+        bool bad = false;
+#pragma unroll 4
+        for (int e = 0; e < 16; ++e) {
+            const int64_t k = kb + e;
+            int64_t code = 0;
+            if (active && k < g.cols) {
+                const int64_t off = tap_offset(g, r, t);
+                const Acc x = off >= 0 ? load_as<Acc>(g.x, g.dtype, off) : Acc(0);
+                if (fixed) {
+                    scale = fixed[k];
+                    bad |= off >= 0 && !finite_as_stored(g.x, g.dtype, off);
+                } else {
+                    const int64_t group = (v / gg.gr) * gg.nc + k / gg.gc;
+                    if (group != cached) {
+                        scale = group_scale<Acc>(maxima[group], s);
+                        cached = group;
+                    }
+                }
+                code = quantise<Acc>(x, scale, s);
+                t.next(g);
+            }
+            tile[lane][warp * 16 + e] = (CodeT)code;
+        }
+        if (fixed && __any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(nonfinite, 1u);
+        __syncthreads();
+        for (int rr = warp; rr < TR; rr += 8) {
+            const int64_t row = rt * TR + rr;
+            if (row >= g.rows) break;
+            CodeT* dst = codes + row * padded + ct * TC;
+            const int64_t width = padded - ct * TC < TC ? padded - ct * TC : TC;
+            if (words) {
+                if (4 * lane < width)
+                    reinterpret_cast<uint32_t*>(dst)[lane] = *reinterpret_cast<const uint32_t*>(&tile[rr][4 * lane]);
+            } else {
+                for (int e = lane; e < width; e += 32) dst[e] = tile[rr][e];
+            }
+        }
+        __syncthreads();
+    }
+}
+
 int grid_for(int64_t work, int threads) {
     int64_t blocks = (work + threads - 1) / threads;
     if (blocks > 148 * 32) blocks = 148 * 32;
@@ -339,6 +503,12 @@ QuantSpec spec_of(int bits, int signed_codes, int bw_e) {
 bool uses_double(const mf_config& c, int bits) { return bits > 8 || c.bw_e > 0; }
 
 }  // namespace
+
+int64_t conv_output_extent(int64_t size, int32_t kernel, int32_t stride, int32_t pad, int32_t dilation) {
+    const int64_t span = (int64_t)dilation * (kernel - 1) + 1;
+    const int64_t room = size + 2 * (int64_t)pad - span;
+    return room < 0 ? 0 : room / stride + 1;
+}
 
 size_t quantize_workspace_bytes(const mf_config& c, bool weight, int64_t rows, int64_t cols) {
     // Logical matrix: inputs [n, k]; weights W^T = [k, o] for w of shape [o, k].
@@ -434,6 +604,63 @@ mf_status quantize_input(const mf_config& c, const void* x, int dtype, int64_t n
     if (dbl) return run_input<double, double>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
     if (c.wide) return run_input<float, double>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
     return run_input<float, float>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
+}
+
+mf_status quantize_conv_input(const mf_config& c, const mf_conv2d& cv, const void* x, int dtype,
+                              const void* fixed, void* codes, void* xscale, uint32_t* nonfinite,
+                              void* workspace, size_t ws_bytes, cudaStream_t stream) {
+    ConvGeom g{};
+    g.x = x;
+    g.dtype = dtype;
+    g.sb = cv.stride_n, g.sc = cv.stride_c, g.sh = cv.stride_h, g.sw = cv.stride_w;
+    g.H = (int32_t)cv.height, g.W = (int32_t)cv.width, g.C0 = cv.channel_begin;
+    g.KH = cv.kernel_h, g.KW = cv.kernel_w, g.SY = cv.stride_y, g.SX = cv.stride_x;
+    g.PH = cv.pad_h, g.PW = cv.pad_w, g.DH = cv.dilation_h, g.DW = cv.dilation_w;
+    g.OH = (int32_t)conv_output_extent(cv.height, cv.kernel_h, cv.stride_y, cv.pad_h, cv.dilation_h);
+    g.OW = (int32_t)conv_output_extent(cv.width, cv.kernel_w, cv.stride_x, cv.pad_w, cv.dilation_w);
+    g.rows = cv.batch * g.OH * g.OW;
+    g.cols = (int64_t)cv.group_channels * cv.kernel_h * cv.kernel_w;
+    const GroupGrid gg = groups_of(g.rows, g.cols, c.in_group_rows, c.in_group_cols);
+    const QuantSpec s = spec_of(c.activation_bits, 1, c.bw_e);
+    const size_t need = quantize_workspace_bytes(c, false, g.rows, g.cols) - 256;
+    if (!fixed && ws_bytes < need) {
+        set_error("conv quantize workspace too small: %zu < %zu bytes", ws_bytes, need);
+        return MF_ERR_RESOURCE;
+    }
+    MF_CHECK_CUDA(cudaMemsetAsync(nonfinite, 0, sizeof(uint32_t), stream), "clear non-finite flag");
+    if (g.rows == 0) return MF_OK;
+    const int64_t m = (g.cols + c.rows - 1) / c.rows, padded = m * c.rows;
+    const int threads = 256;
+    const bool dbl = fixed ? c.wide != 0 : uses_double(c, c.activation_bits);
+    const View v{x, dtype, g.rows, g.cols, g.cols, 0};
+    const int64_t code_tiles = ((g.rows + 31) / 32) * ((padded + 127) / 128);
+    const int code_blocks = (int)(code_tiles < 148 * 16 ? code_tiles : 148 * 16);
+    auto run = [&](auto acc_tag, auto code_tag, auto scale_tag) -> mf_status {
+        using Acc = decltype(acc_tag);
+        using CodeT = decltype(code_tag);
+        using ScaleT = decltype(scale_tag);
+        Acc* maxima = static_cast<Acc*>(workspace);
+        const Acc* fx = static_cast<const Acc*>(fixed);
+        if (!fx) {
+            MF_CHECK_CUDA(cudaMemsetAsync(maxima, 0, need, stream), "memset group maxima");
+            const int64_t warps = ((g.rows + 31) / 32) * gg.nc;
+            conv_amax_kernel<Acc><<<grid_for(warps * 32, threads), threads, 0, stream>>>(g, gg, maxima, nonfinite);
+            MF_LAUNCH_CHECK("conv_amax_kernel");
+        }
+        conv_code_kernel<Acc, CodeT><<<code_blocks, threads, 0, stream>>>(g, gg, maxima, fx, s, padded,
+                                                                          static_cast<CodeT*>(codes), nonfinite);
+        MF_LAUNCH_CHECK("conv_code_kernel");
+        input_scale_kernel<Acc, ScaleT><<<grid_for(g.rows * m * c.reads, threads), threads, 0, stream>>>(
+            v, gg, maxima, fx, s, c.rows, c.read_rows, c.reads, m, static_cast<ScaleT*>(xscale));
+        MF_LAUNCH_CHECK("input_scale_kernel");
+        return MF_OK;
+    };
+    if (c.wide_codes) {
+        if (dbl) return run(double{}, int64_t{}, double{});
+        return c.wide ? run(float{}, int64_t{}, double{}) : run(float{}, int64_t{}, float{});
+    }
+    if (dbl) return run(double{}, uint8_t{}, double{});
+    return c.wide ? run(float{}, uint8_t{}, double{}) : run(float{}, uint8_t{}, float{});
 }
 
 template <typename Acc, typename ScaleT>

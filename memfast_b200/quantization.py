@@ -12,6 +12,7 @@ Every buffer keeps the reference layout: codes [n,m,R], per-read input scales
 uint8 codes (int64 beyond 8 bits) and FP32 scales (FP64 when ``Config.wide``).
 """
 
+import ctypes
 import math
 
 import torch
@@ -157,6 +158,57 @@ def input_tiles(value, config, fixed_scale=None, *, checked=False):
         "mf_quantize_input",
     )
     return codes, xscale
+
+
+def conv_input_tiles(x, config, geometry, fixed_scale=None):
+    """One convolution group's patches -> (codes [n, m, R], per-read scales [n, m*reads], flag).
+
+    The buffers ``input_tiles`` gives for the group's ``F.unfold`` patches laid
+    out as [batch*OH*OW, Cg*kh*kw] (memfast/nn/convolution.py:49-55), quantised
+    straight from the NCHW input ``x`` (any strides) without building them.
+    ``geometry``: the group's ``_lib.MFConv2d`` (kernel, stride, padding, dilation,
+    channels); ``x``'s shape and strides are filled in here.  ``flag`` is a device
+    int32 that the kernels set to 1 when a quantised value is not finite (the
+    reference raises ValueError then)."""
+    _require_cuda(x, "input")
+    if x.dtype not in _lib.DTYPES:
+        x = x.float()
+    geometry.batch, geometry.channels, geometry.height, geometry.width = x.shape
+    geometry.stride_n, geometry.stride_c, geometry.stride_h, geometry.stride_w = x.stride()
+    oh, ow = conv_output_size(geometry)
+    n = x.shape[0] * oh * ow
+    k = geometry.group_channels * geometry.kernel_h * geometry.kernel_w
+    r = config.array_size[0]
+    m = math.ceil(k / r)
+    codes = torch.empty((n, m, r), dtype=_code_dtype(config), device=x.device)
+    xscale = torch.empty((n, m * config.reads_per_array), dtype=_scale_dtype(config), device=x.device)
+    flag = torch.zeros(1, dtype=torch.int32, device=x.device)
+    if n == 0:
+        return codes, xscale, flag
+    if fixed_scale is not None:
+        fixed_scale = fixed_scale.to(_scale_dtype(config)).reshape(-1).contiguous()
+        if fixed_scale.numel() != k:
+            fixed_scale = fixed_scale.expand(k).contiguous()
+        workspace, need = None, 0
+    else:
+        workspace, need = _workspace(config, False, n, k, x.device)
+    _lib.check(
+        _lib.load().mf_quantize_conv_input(
+            _lib.native_config(config), ctypes.byref(geometry), _lib.ptr(x), _lib.DTYPES[x.dtype],
+            _lib.ptr(fixed_scale), _lib.ptr(codes), _lib.ptr(xscale), _lib.ptr(flag), _lib.ptr(workspace), need,
+            _lib.stream_of(x.device),
+        ),
+        "mf_quantize_conv_input",
+    )
+    return codes, xscale, flag
+
+
+def conv_output_size(geometry):
+    """(OH, OW) of a convolution group; ValueError when the window does not fit."""
+    oh, ow = ctypes.c_int64(), ctypes.c_int64()
+    _lib.check(_lib.load().mf_conv_output(ctypes.byref(geometry), ctypes.byref(oh), ctypes.byref(ow)),
+               "mf_conv_output")
+    return oh.value, ow.value
 
 
 def weight_tiles(weight, config, *, checked=False, kmajor=None):

@@ -24,6 +24,7 @@ import math
 import os
 import tempfile
 import time
+import types
 import weakref
 from dataclasses import asdict
 from pathlib import Path
@@ -560,8 +561,11 @@ class AnalogMatrix(nn.Module):
         )
         return size.value
 
-    def _execute(self, q, xscale, schedule, event, stable=False, *, vector_offset=0):
-        """One fused device call: analog partials, scales, read sums and bias."""
+    def _execute(self, q, xscale, schedule, event, stable=False, *, vector_offset=0, input_flag=None):
+        """One fused device call: analog partials, scales, read sums and bias.
+
+        ``input_flag``: device int32 set by a quantiser that checks finiteness on the
+        device; read in the same synchronisation as the output check."""
         n = q.shape[0]
         wide = self.config.wide or stable
         dtype = torch.float64 if wide else torch.float32
@@ -623,7 +627,15 @@ class AnalogMatrix(nn.Module):
                 output = output + self.bias
         # One host synchronisation decides both the FP64 rerun of a narrow config
         # (simulator.py:614-615) and, in forward, the non-finite error.
-        self._finite = finite_flags(output)[0]
+        if input_flag is None:
+            self._finite = finite_flags(output)[0]
+        else:
+            extremes = torch.aminmax(output) if output.numel() else (output.new_zeros(()), output.new_zeros(()))
+            low, high, bad = torch.stack([extremes[0].double(), extremes[1].double(),
+                                          input_flag.reshape(()).double()]).tolist()
+            if bad:
+                raise ValueError("quantized values must be finite")
+            self._finite = math.isfinite(low) and math.isfinite(high)
         if not self.config.wide and not stable and not self._finite:
             return self._execute(q, xscale, schedule, event, stable=True, vector_offset=vector_offset)
         return output
@@ -648,18 +660,27 @@ class AnalogMatrix(nn.Module):
         if self._event >= 2**63:
             raise OverflowError("read-event counter exhausted")
         q, xscale = input_tiles(x.reshape(-1, self.in_features), self.config, self.input_scale, checked=checked)
+        output = self._product(q, xscale, shape, x.dtype, vector_offset=vector_offset)
+        return output.reshape(*shape[:-1], self.out_features)
+
+    def _product(self, q, xscale, shape, dtype, *, vector_offset=0, input_flag=None):
+        """forward() from quantised codes on (simulator.py:631-646): schedule, product,
+        non-finite checks, ``dtype`` result, read event.  ``shape``/``dtype`` describe
+        the caller's input (tuned-mode key); ``input_flag`` as in ``_execute``."""
         event = self._event
         schedule = default_schedule(self.config)
-        key = tuple(shape), str(x.dtype)
+        key = tuple(shape), str(dtype)
         if self.simulator.mode == "tuned":
             if key not in self._prepared:
-                with torch.cuda.device(x.device):
-                    self._prepared[key] = self.simulator._select(self, x, q, xscale, event)
+                if input_flag is not None and input_flag.item():
+                    raise ValueError("quantized values must be finite")
+                with torch.cuda.device(q.device):
+                    self._prepared[key] = self.simulator._select(
+                        self, types.SimpleNamespace(shape=tuple(shape), dtype=dtype), q, xscale, event)
             schedule = self._prepared[key]
-        output = self._execute(q, xscale, schedule, event, vector_offset=vector_offset)
-        output = output.reshape(*shape[:-1], self.out_features)
-        finite = self._finite and (output.dtype == x.dtype or finite_flags(output, dtypes=[x.dtype])[0])
-        output = output.to(x.dtype)
+        output = self._execute(q, xscale, schedule, event, vector_offset=vector_offset, input_flag=input_flag)
+        finite = self._finite and (output.dtype == dtype or finite_flags(output, dtypes=[dtype])[0])
+        output = output.to(dtype)
         check_device_error()
         if not finite:
             raise FloatingPointError("nonfinite analog output")

@@ -193,6 +193,42 @@ def main(reference_root, only=()):
                                        **{f"param::{k}": v for k, v in state.items()}),
          kind="convert_model")
 
+    # AnalogConv2d (nn/convolution.py) on its own: geometry, groups, padding modes,
+    # input groups spanning vectors, noise addressed by the patch-row index.
+    def conv_case(name, kwargs, conv_kwargs, x_shape, seed, calls=2):
+        if only and name not in only:
+            return
+        cfg = make(kwargs)
+        torch.manual_seed(seed)
+        source = torch.nn.Conv2d(**conv_kwargs)
+        x = torch.randn(*x_shape)
+        layer = memfast.nn.AnalogConv2d(source, Simulator(cfg, device="cpu"), name="conv")
+        arrays = dict(x=x.numpy(), weight=source.weight.detach().numpy())
+        if source.bias is not None:
+            arrays["bias"] = source.bias.detach().numpy()
+        for i in range(calls):
+            arrays[f"out{i}"] = layer(x).numpy()
+        conv = {key: list(value) if isinstance(value, tuple) else value for key, value in conv_kwargs.items()}
+        save(name, kwargs, arrays, kind="conv", calls=calls, name="conv", conv=conv)
+
+    conv_case("conv_int8", dict(int8, nonidealities=ideal),
+              dict(in_channels=16, out_channels=24, kernel_size=3, stride=1, padding=1), (2, 16, 9, 11), 30)
+    conv_case("conv_dilated_reflect", dict(nonidealities=dict(write_variation=0.02, read_variation=0.02,
+                                                              voltage_variation=0.02)),
+              dict(in_channels=8, out_channels=12, kernel_size=(3, 5), stride=(2, 1), padding=(2, 1),
+                   dilation=(2, 1), groups=2, padding_mode="reflect"), (2, 8, 10, 9), 31)
+    conv_case("conv_row_groups", dict(int8, input_quant_gran=(4, 32), nonidealities=dict(write_variation=0.02)),
+              dict(in_channels=12, out_channels=8, kernel_size=3, stride=2, bias=False), (3, 12, 9, 9), 32)
+    conv_case("conv_depthwise_circular", dict(matrix, activation_bits=4, weight_bits=4, input_slice=(1, 1, 2),
+                                              weight_slice=(1, 1, 2), nonidealities=effects3),
+              dict(in_channels=6, out_channels=6, kernel_size=3, padding=1, groups=6, padding_mode="circular"),
+              (2, 6, 7, 7), 33)
+    conv_case("conv_pointwise_strided", dict(base, adc_bits=7, input_quant_gran=(1, None),
+                                             weight_quant_gran=(None, 1), nonidealities=dict(write_variation=0.02,
+                                                                                             read_variation=0.05,
+                                                                                             read_mode="output")),
+              dict(in_channels=40, out_channels=20, kernel_size=1, stride=3), (2, 40, 8, 10), 34)
+
 
 if __name__ == "__main__":
     main(Path(sys.argv[1] if len(sys.argv) > 1 else "../MemFast").resolve(), tuple(sys.argv[2:]))

@@ -36,6 +36,25 @@ def mm_cases():
     return names
 
 
+def cases_of(kind):
+    names = []
+    for path in sorted(GOLDEN.glob("*.npz")):
+        meta = json.loads(str(np.load(path)["meta_json"]))
+        if meta.get("kind") == kind:
+            names.append(path.stem)
+    return names
+
+
+def conv_arguments(conv):
+    """Conv2d keyword arguments of a golden case as (kernel, stride, padding, dilation) pairs + the rest."""
+    def pair(value):
+        return tuple(value) if isinstance(value, (list, tuple)) else (value, value)
+
+    return dict(kernel=pair(conv["kernel_size"]), stride=pair(conv.get("stride", 1)),
+                padding=pair(conv.get("padding", 0)), dilation=pair(conv.get("dilation", 1)),
+                groups=conv.get("groups", 1), padding_mode=conv.get("padding_mode", "zeros"))
+
+
 # Nonideal currents are real-valued FP32 dot products.  Summing them in another
 # order than the reference's CPU bmm flips an ADC rounding where a current sits
 # within an ulp of a count boundary, and one flip of the most significant slice
@@ -71,8 +90,8 @@ def assert_close_nonideal(got, want, label=""):
 
 def assert_parity(got, want, config, label=""):
     """Bit-exact for ideal devices; the nonideal tolerance above otherwise."""
-    got = np.asarray(got)
-    want = np.asarray(want)
+    got = np.ascontiguousarray(got)
+    want = np.ascontiguousarray(want)
     assert got.dtype == want.dtype and got.shape == want.shape, (label, got.dtype, want.dtype)
     if config.nonidealities.ideal:
         assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), (

@@ -3,7 +3,7 @@
 import numpy as np
 import pytest
 
-from helpers import assert_parity, load_case, mm_cases
+from helpers import assert_parity, cases_of, conv_arguments, load_case, mm_cases
 from oracle import oracle as O
 from oracle import quantize as Q
 
@@ -26,6 +26,16 @@ def test_oracle_quantisation_matches_reference(case):
     assert np.array_equal(q, arrays["q"].astype(np.int64))
     assert np.array_equal(xscale.view(np.uint8), arrays["xscale"].view(np.uint8))
 
+
+@pytest.mark.parametrize("case", cases_of("conv"))
+def test_oracle_conv_matches_reference(case):
+    config, arrays, meta = load_case(case)
+    geometry = conv_arguments(meta["conv"])
+    geometry.pop("kernel")
+    for call in range(meta["calls"]):
+        got = O.conv2d(arrays["x"], arrays["weight"], arrays.get("bias"), config, name=meta["name"], event=call,
+                       **geometry)
+        assert_parity(got, arrays[f"out{call}"], config, f"{case} call {call}")
 
 def test_ideal_integer_path_equals_physical_fp32_path():
     """In ideal mode the physical FP32 currents round to the exact integer counts."""
