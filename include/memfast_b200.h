@@ -200,8 +200,13 @@ mf_status mf_conv_output(const mf_conv2d* conv, int64_t* out_height, int64_t* ou
  *   codes/xscale: from mf_quantize_input ([n, m*rows], [n, m*reads]).
  *   packed/wscale: from mf_program_weights ([m, p, rows, cols], [m*reads, p, cols]).
  *   bias: NULL or [out_features] FP32 (FP64 when wide or stable).
- *   out: [n, ldo] FP32 (FP64 when cfg->wide or stable); columns
- *        [tile_begin*cols, min(tile_end*cols, out_features)) are written.
+ *   out: FP32 (FP64 when cfg->wide or stable); output column `col` of vector
+ *        `v` goes to out[v*ldo + col] for the written columns
+ *        [tile_begin*cols, min(tile_end*cols, out_features)).  ldo is at least
+ *        the written width: out_features for a full [n, out_features] buffer, or
+ *        the shard's width for a buffer holding only the shard's columns (then
+ *        `out` is that buffer's address minus tile_begin*cols elements; nothing
+ *        below the written columns is touched).
  *   seed: AnalogMatrix.seed; event: read-event counter (simulator.py:427-429,633).
  *   vector_offset: global index of row 0 (noise addresses stay global when rows
  *        are sharded across calls or GPUs).

@@ -3,6 +3,7 @@
 // Validation mirrors the argument checks the reference performs before it
 // launches (cuda.py:322-373, simulator.py:216-237); failures return a status
 // and leave a message for mf_last_error() instead of raising.
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -309,7 +310,8 @@ mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const 
     mf_status st = check_config(cfg);
     if (st) return st;
     if (!codes || !xscale || !packed || !wscale || !out || n < 0 || m < 1 || p < 1 || out_features < 1 ||
-        out_features > (int64_t)p * cfg->cols || ldo < out_features || tile_begin < 0 || tile_end > p ||
+        out_features > (int64_t)p * cfg->cols || tile_begin < 0 || tile_end > p ||
+        ldo < std::min((int64_t)tile_end * cfg->cols, (int64_t)out_features) - (int64_t)tile_begin * cfg->cols ||
         tile_begin >= tile_end || vector_offset < 0) {
         set_error("mf_sliced_mm: invalid operands (n=%lld m=%d p=%d out=%d ldo=%lld tiles=[%d,%d))",
                   (long long)n, m, p, out_features, (long long)ldo, tile_begin, tile_end);

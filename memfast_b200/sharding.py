@@ -10,13 +10,23 @@ final all-gather of output rows.  Column (tile) sharding is the C ABI's
 
 Input groups that span several vectors (input_quant_gran[0] != 1) would need a
 collective max over ranks; ``sharded_mm`` rejects them.
+
+Tensor parallelism (``shard_columns`` / ``tensor_parallel``) splits a programmed
+layer's output tiles over the ranks instead: every rank holds the same
+programmed matrix and computes tiles ``tile_range(p, world, rank)``; cell and
+noise addresses use the global tile index and the total tile count
+(memfast/kernels.cu:53,118, reference.py:20-31), so each rank's columns equal
+those of the single-device layer.  The column slabs are all-gathered over NCCL,
+or kept sharded for a consumer that takes them.  Whether a non-finite output
+triggers the FP64 rerun (simulator.py:614-615) is agreed over the group, so the
+ranks rerun together exactly when the single-device layer would.
 """
 
 import torch
 import torch.distributed as dist
 
 from .functional import _checked, _operands
-from .simulator import Simulator
+from .simulator import AnalogMatrix, Simulator
 
 
 def row_range(n, world, rank):
@@ -71,4 +81,76 @@ def gather_rows(local, n, group=None):
     return torch.cat(parts)
 
 
-__all__ = ["row_range", "sharded_mm", "gather_rows"]
+def tile_range(p, world, rank):
+    """Output tiles [t0, t1) of rank ``rank`` when p tiles are split over ``world`` ranks."""
+    return row_range(p, world, rank)
+
+
+def gather_columns(local, out_features, cols, group=None):
+    """All-gather column slabs (``tile_range`` partition of the output tiles) into
+    [..., out_features].  Slabs are padded to the widest for the collective."""
+    world = dist.get_world_size(group)
+    p = -(-out_features // cols)
+    widths = []
+    for rank in range(world):
+        t0, t1 = tile_range(p, world, rank)
+        widths.append(max(0, min(t1 * cols, out_features) - t0 * cols))
+    lead = local.shape[:-1]
+    flat = local.reshape(-1, local.shape[-1])
+    padded = flat.new_zeros((max(widths), flat.shape[0]))
+    padded[: flat.shape[1]] = flat.T
+    stacked = flat.new_empty((world * max(widths), flat.shape[0]))
+    dist.all_gather_into_tensor(stacked, padded, group=group)
+    parts = [stacked[r * max(widths): r * max(widths) + widths[r]] for r in range(world)]
+    return torch.cat(parts).T.reshape(*lead, out_features)
+
+
+class ColumnShard:
+    """The tensor-parallel forward of one programmed layer (see module docstring)."""
+
+    def __init__(self, group=None, *, gather=True):
+        self.group, self.gather = group, gather
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def tiles(self, layer):
+        return tile_range(layer.p, self.world, self.rank)
+
+    def agree(self, flag):
+        state = torch.tensor([1 if flag else 0], dtype=torch.int32, device=self.device)
+        dist.all_reduce(state, op=dist.ReduceOp.MIN, group=self.group)
+        return bool(state.item())
+
+    def __call__(self, layer, x):
+        self.device = x.device if dist.get_backend(self.group) == "nccl" else torch.device("cpu")
+        tiles = self.tiles(layer)
+        if tiles[0] >= tiles[1]:
+            raise ValueError("more ranks than output tiles")
+        local = layer._forward(x, tiles=tiles, agree=self.agree)
+        if not self.gather:
+            return local
+        return gather_columns(local, layer.out_features, layer.config.array_size[1], self.group)
+
+
+def shard_columns(layer, group=None, *, gather=True):
+    """Make ``layer`` (an AnalogMatrix / AnalogLinear) compute only this rank's output
+    tiles, all-gathering the full output unless ``gather`` is False.  Every rank of
+    ``group`` must hold the same programmed layer and call it with the same input."""
+    if not isinstance(layer, AnalogMatrix):
+        raise TypeError("shard_columns needs a programmed AnalogMatrix")
+    layer._column_shard = ColumnShard(group, gather=gather)
+    return layer
+
+
+def tensor_parallel(model, group=None, *, gather=True):
+    """Column-shard every AnalogLinear of a converted model over ``group`` (in place)."""
+    from .nn.linear import AnalogLinear
+
+    for module in model.modules():
+        if isinstance(module, AnalogLinear):
+            shard_columns(module, group, gather=gather)
+    return model
+
+
+__all__ = ["row_range", "sharded_mm", "gather_rows", "tile_range", "gather_columns", "shard_columns",
+           "tensor_parallel", "ColumnShard"]

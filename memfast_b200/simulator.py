@@ -358,6 +358,8 @@ class AnalogMatrix(nn.Module):
         # Workspace of the tensor-core kernels, reused across calls: it starts with
         # the K-major copy of the packed codes (valid while _ws_ready is set).
         self._ws, self._ws_bytes, self._kmajor_bytes, self._ws_ready, self._ws_stream = None, 0, 0, False, None
+        # Tensor-parallel column shard (sharding.shard_columns); None = all columns.
+        self._column_shard = None
         self.simulator, self.config, self.name = simulator, simulator.config, name
         self.out_features, self.in_features = weight.shape
         self.p = math.ceil(self.out_features / self.config.array_size[1])
@@ -561,15 +563,26 @@ class AnalogMatrix(nn.Module):
         )
         return size.value
 
-    def _execute(self, q, xscale, schedule, event, stable=False, *, vector_offset=0, input_flag=None):
+    def _execute(self, q, xscale, schedule, event, stable=False, *, vector_offset=0, input_flag=None,
+                 tiles=None, agree=None):
         """One fused device call: analog partials, scales, read sums and bias.
 
         ``input_flag``: device int32 set by a quantiser that checks finiteness on the
-        device; read in the same synchronisation as the output check."""
+        device; read in the same synchronisation as the output check.
+        ``tiles``: output tiles [t0, t1) only (a column shard; noise addresses stay
+        global), giving columns [t0*cols, min(t1*cols, out_features)).
+        ``agree``: combines this shard's finiteness with the other shards' (the FP64
+        rerun is decided for the whole product)."""
         n = q.shape[0]
         wide = self.config.wide or stable
         dtype = torch.float64 if wide else torch.float32
-        output = torch.empty((n, self.out_features), device=q.device, dtype=dtype)
+        t0, t1 = (0, self.p) if tiles is None else tiles
+        cols = self.config.array_size[1]
+        c0, c1 = t0 * cols, min(t1 * cols, self.out_features)
+        output = torch.empty((n, c1 - c0), device=q.device, dtype=dtype)
+        # The kernels address output columns globally: hand them the buffer shifted
+        # back by c0 columns (only columns >= c0 are written).
+        base = ct.c_void_p(output.data_ptr() - c0 * output.element_size())
         fuse_bias = self.bias is not None and self.zero_correction is None
         workspace_bytes = self._workspace_size(n, schedule)
         packed = self.packed.contiguous()
@@ -597,8 +610,8 @@ class AnalogMatrix(nn.Module):
             _lib.load().mf_sliced_mm(
                 _lib.native_config(self.config), ct.byref(native), _lib.ptr(q), _lib.ptr(xscale),
                 _lib.ptr(packed), _lib.ptr(self.weight_scale.contiguous()),
-                _lib.ptr(self.bias) if fuse_bias else None, _lib.ptr(output), n, packed.shape[0], self.p,
-                self.out_features, self.out_features, 0, self.p, self.seed & 0xFFFFFFFF, event,
+                _lib.ptr(self.bias) if fuse_bias else None, base, n, packed.shape[0], self.p,
+                self.out_features, c1 - c0, t0, t1, self.seed & 0xFFFFFFFF, event,
                 vector_offset, int(stable), _lib.ptr(workspace), workspace_bytes, stream,
             ),
             "mf_sliced_mm",
@@ -614,17 +627,17 @@ class AnalogMatrix(nn.Module):
             sums = padded.reshape(n, -1, step).sum(-1)
             c = self.config.array_size[1]
             if wide:
-                for begin in range(0, self.out_features, c):
-                    end = min(begin + c, self.out_features)
+                for begin in range(c0, c1, c):
+                    end = min(begin + c, c1)
                     correction = restore_scales(
                         sums[:, :, None], xscale[:, :, None], self.zero_correction[None, :, begin:end]
                     ).sum(1)
-                    output[:, begin:end] += correction
+                    output[:, begin - c0:end - c0] += correction
             else:
-                correction = (sums.to(dtype) * xscale.to(dtype)) @ self.zero_correction.to(dtype)
+                correction = (sums.to(dtype) * xscale.to(dtype)) @ self.zero_correction[:, c0:c1].to(dtype)
                 output = output + correction
             if self.bias is not None:
-                output = output + self.bias
+                output = output + self.bias[c0:c1]
         # One host synchronisation decides both the FP64 rerun of a narrow config
         # (simulator.py:614-615) and, in forward, the non-finite error.
         if input_flag is None:
@@ -636,17 +649,21 @@ class AnalogMatrix(nn.Module):
             if bad:
                 raise ValueError("quantized values must be finite")
             self._finite = math.isfinite(low) and math.isfinite(high)
+        if agree is not None:
+            self._finite = agree(self._finite)
         if not self.config.wide and not stable and not self._finite:
-            return self._execute(q, xscale, schedule, event, stable=True, vector_offset=vector_offset)
+            return self._execute(q, xscale, schedule, event, stable=True, vector_offset=vector_offset, tiles=tiles)
         return output
 
     @torch.no_grad()
     def forward(self, x):
-        return self._forward(x)
+        shard = self._column_shard
+        return self._forward(x) if shard is None else shard(self, x)
 
-    def _forward(self, x, checked=False, vector_offset=0):
+    def _forward(self, x, checked=False, vector_offset=0, tiles=None, agree=None):
         """forward(); ``checked``: the caller verified x finite in the quantiser's dtype;
-        ``vector_offset``: global index of x's first vector (noise addresses of row shards)."""
+        ``vector_offset``: global index of x's first vector (noise addresses of row shards);
+        ``tiles``/``agree``: a column shard, as in ``_execute``."""
         if x.ndim < 1 or x.shape[-1] != self.in_features or not x.is_floating_point():
             raise ValueError("input must be floating with matching in_features")
         if x.device != self.packed.device or x.device != self.simulator.device:
@@ -655,15 +672,18 @@ class AnalogMatrix(nn.Module):
         if self.weight_scale.dtype != scale_dtype:
             raise RuntimeError("keep simulator scale buffers at their mapped dtype")
         shape = x.shape
+        cols = self.config.array_size[1]
+        t0, t1 = (0, self.p) if tiles is None else tiles
+        width = min(t1 * cols, self.out_features) - t0 * cols
         if x.numel() == 0:
-            return x.new_empty((*shape[:-1], self.out_features))
+            return x.new_empty((*shape[:-1], width))
         if self._event >= 2**63:
             raise OverflowError("read-event counter exhausted")
         q, xscale = input_tiles(x.reshape(-1, self.in_features), self.config, self.input_scale, checked=checked)
-        output = self._product(q, xscale, shape, x.dtype, vector_offset=vector_offset)
-        return output.reshape(*shape[:-1], self.out_features)
+        output = self._product(q, xscale, shape, x.dtype, vector_offset=vector_offset, tiles=tiles, agree=agree)
+        return output.reshape(*shape[:-1], width)
 
-    def _product(self, q, xscale, shape, dtype, *, vector_offset=0, input_flag=None):
+    def _product(self, q, xscale, shape, dtype, *, vector_offset=0, input_flag=None, tiles=None, agree=None):
         """forward() from quantised codes on (simulator.py:631-646): schedule, product,
         non-finite checks, ``dtype`` result, read event.  ``shape``/``dtype`` describe
         the caller's input (tuned-mode key); ``input_flag`` as in ``_execute``."""
@@ -678,8 +698,11 @@ class AnalogMatrix(nn.Module):
                     self._prepared[key] = self.simulator._select(
                         self, types.SimpleNamespace(shape=tuple(shape), dtype=dtype), q, xscale, event)
             schedule = self._prepared[key]
-        output = self._execute(q, xscale, schedule, event, vector_offset=vector_offset, input_flag=input_flag)
+        output = self._execute(q, xscale, schedule, event, vector_offset=vector_offset, input_flag=input_flag,
+                               tiles=tiles, agree=agree)
         finite = self._finite and (output.dtype == dtype or finite_flags(output, dtypes=[dtype])[0])
+        if agree is not None:
+            finite = agree(finite)
         output = output.to(dtype)
         check_device_error()
         if not finite:

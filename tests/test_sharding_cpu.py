@@ -51,3 +51,42 @@ def test_gather_rows_two_ranks_gloo(n):
     result = manager.dict()
     mp.spawn(_gather_worker, args=(2, _free_port(), n, result), nprocs=2, join=True)
     assert result[0] and result[1]
+
+
+@pytest.mark.parametrize("p,world", [(32, 8), (86, 8), (3, 2), (5, 5)])
+def test_tile_range_partitions_every_tile_once(p, world):
+    from memfast_b200.sharding import tile_range
+
+    spans = [tile_range(p, world, rank) for rank in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == p
+    assert all(a1 == b0 for (_, a1), (b0, _) in zip(spans, spans[1:]))
+    assert all(t1 > t0 for t0, t1 in spans)
+
+
+def _column_worker(rank, world, port, out_features, cols, result):
+    from memfast_b200.sharding import ColumnShard, gather_columns, tile_range
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        full = torch.arange(2 * 3 * out_features, dtype=torch.float32).reshape(2, 3, out_features)
+        t0, t1 = tile_range(-(-out_features // cols), world, rank)
+        local = full[..., t0 * cols:min(t1 * cols, out_features)]
+        gathered = gather_columns(local, out_features, cols)
+        shard = ColumnShard()
+        shard.device = torch.device("cpu")
+        # Finiteness is agreed over the group: one rank's False makes everyone rerun.
+        agreed = shard.agree(rank != 1)
+        result[rank] = (bool(torch.equal(gathered, full)), agreed)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("out_features,cols", [(256, 64), (130, 64), (11008, 128)])
+def test_gather_columns_and_agreement_two_ranks_gloo(out_features, cols):
+    """Column slabs of a tensor-parallel layer are gathered in tile order; the FP64-rerun
+    decision is the AND over ranks."""
+    manager = mp.get_context("spawn").Manager()
+    result = manager.dict()
+    mp.spawn(_column_worker, args=(2, _free_port(), out_features, cols, result), nprocs=2, join=True)
+    assert result[0] == (True, False) and result[1] == (True, False)
