@@ -6,8 +6,9 @@ workload (array 128x128, rows_per_read 32, groups
 (32,1)/(1,32), slices (1,1,2,2,2), adc_bits (6,7,7,8,8), ideal device) on
 seeded N(0,1) FP32 operands.  One step = one ``Simulator.mm(A, B)`` call
 (quantise A, reprogram B, sliced product with fused epilogue), operands
-resident in HBM.  ``e2e`` repeats it with pinned host operands copied in and the
-result copied out inside the timed region.  With --gpus N (one process per GPU
+resident in HBM.  ``e2e`` times the host-operand call ``streaming.host_mm`` on
+pinned A and B: both copied in and the product copied out inside the timed
+region, the copies overlapped with the product row chunk by row chunk.  With --gpus N (one process per GPU
 under torchrun) the batch has 4096 rows per GPU: every rank runs the 4096^3
 product on its own row block of one (4096 N)-row batch with B replicated, its
 vectors keeping their global indices (noise addresses), and keeps its output
@@ -321,12 +322,14 @@ def engine_arm(args):
             torch.cuda.synchronize(device)
     per_step = sum(times) / len(times)
 
-    # End to end: pinned host operands in, result out, every step.
+    # End to end through the host-operand API: pinned A and B copied in and the
+    # product copied out every step, overlapped chunk by chunk with the compute.
+    from memfast_b200.streaming import host_mm
+
     def e2e_step():
-        x = a_host.to(device, non_blocking=True)
-        y = b_host.to(device, non_blocking=True)
-        out = step(x, y)
-        out_host.copy_(out, non_blocking=True)
+        host_mm(a_host, b_host, simulator=sim, out=out_host, row_offset=r0)
+        if world > 1 and args.gather:
+            gather_rows(out_host.to(device), total_rows)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()

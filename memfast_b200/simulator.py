@@ -182,7 +182,7 @@ class Simulator:
 
         return matmul(input, other, simulator=self, out=out)
 
-    def _matrix_for(self, matrix, checked=False, rows=1):
+    def _matrix_for(self, matrix, checked=False, rows=1, program=None):
         """Reprogram the RHS and reuse the cached program if its codes are unchanged.
 
         A reprogrammed RHS keeps the cached program's name (sampling seed) and read
@@ -190,7 +190,9 @@ class Simulator:
         and the new one is kept without comparing codes on the host.  Tuned mode
         compares, because the cached program also carries its schedule selections.
         ``checked``: the caller verified the matrix finite in the quantiser's dtype;
-        ``rows``: vectors of the coming product (sizes the tensor-core workspace).
+        ``rows``: vectors of the coming product (sizes the tensor-core workspace);
+        ``program``: a device copy of a host ``matrix`` to program from (the cache
+        follows the host tensor, as the reference's does for its operand).
         """
         identity = id(matrix)
         record = self._matrix_cache.get(identity)
@@ -205,7 +207,8 @@ class Simulator:
             self._next_id += 1
         else:
             name = previous.name
-        programmed = AnalogMatrix(matrix.T, self, name=name, _checked=checked, _rows=rows)
+        source = matrix if program is None else program
+        programmed = AnalogMatrix(source.T, self, name=name, _checked=checked, _rows=rows)
         if (
             self.mode == "tuned"
             and same_tensor
@@ -355,9 +358,9 @@ class AnalogMatrix(nn.Module):
             raise ValueError("weight must be a nonempty [O,K] matrix")
         if not _checked and not finite_flags(weight)[0]:
             raise ValueError("weights must be finite")
-        # Workspace of the tensor-core kernels, reused across calls: it starts with
-        # the K-major copy of the packed codes (valid while _ws_ready is set).
-        self._ws, self._ws_bytes, self._kmajor_bytes, self._ws_ready, self._ws_stream = None, 0, 0, False, None
+        # Workspaces of the tensor-core kernels, one per stream, reused across calls:
+        # each starts with the K-major copy of the packed codes (valid while ready).
+        self._workspaces, self._kmajor_bytes = {}, 0
         # Tensor-parallel column shard (sharding.shard_columns); None = all columns.
         self._column_shard = None
         self.simulator, self.config, self.name = simulator, simulator.config, name
@@ -372,10 +375,12 @@ class AnalogMatrix(nn.Module):
                 raise ValueError("zero_points requires imported integer codes and scales")
             self._prepare_workspace(math.ceil(self.in_features / self.config.array_size[0]), simulator.device,
                                     _rows)
+            entry = self._workspaces.get(_lib.stream_of(simulator.device).value)
             packed, scale, written = weight_tiles(
                 weight.detach().to(simulator.device), self.config, checked=_checked,
-                kmajor=None if self._ws is None else self._ws[: self._kmajor_bytes])
-            self._ws_ready = written
+                kmajor=None if entry is None else entry[0][: self._kmajor_bytes])
+            if entry is not None:
+                entry[1] = written
         else:
             if weight.dtype not in (torch.uint8, torch.int8, torch.int16, torch.int32, torch.int64):
                 raise ValueError("imported weight codes must have an integer dtype")
@@ -546,11 +551,23 @@ class AnalogMatrix(nn.Module):
         self._kmajor_bytes = self._kmajor_size(m, default_schedule(self.config))
         if self._kmajor_bytes:
             need = self._workspace_size(max(rows, 1), default_schedule(self.config), m)
-            self._ws = torch.empty(need, dtype=torch.uint8, device=device)
-            self._ws_bytes, self._ws_stream = need, _lib.stream_of(device).value
+            self._workspaces[_lib.stream_of(device).value] = [torch.empty(need, dtype=torch.uint8, device=device),
+                                                               False]
 
     def _drop_workspace(self):
-        self._ws, self._ws_bytes, self._ws_ready = None, 0, False
+        self._workspaces.clear()
+
+    @property
+    def _ws(self):
+        """The current stream's tensor-core workspace (None before the first call)."""
+        entry = self._workspaces.get(_lib.stream_of(self.packed.device).value)
+        return None if entry is None else entry[0]
+
+    @property
+    def _ws_ready(self):
+        """Whether the current stream's workspace holds the K-major weight copy."""
+        entry = self._workspaces.get(_lib.stream_of(self.packed.device).value)
+        return entry is not None and entry[1]
 
     def _workspace_size(self, n, schedule, m=None):
         size = ct.c_size_t()
@@ -573,13 +590,37 @@ class AnalogMatrix(nn.Module):
         global), giving columns [t0*cols, min(t1*cols, out_features)).
         ``agree``: combines this shard's finiteness with the other shards' (the FP64
         rerun is decided for the whole product)."""
+        output = self._launch(q, xscale, schedule, event, stable=stable, vector_offset=vector_offset, tiles=tiles)
+        # One host synchronisation decides both the FP64 rerun of a narrow config
+        # (simulator.py:614-615) and, in forward, the non-finite error.
+        if input_flag is None:
+            self._finite = finite_flags(output)[0]
+        else:
+            extremes = torch.aminmax(output) if output.numel() else (output.new_zeros(()), output.new_zeros(()))
+            low, high, bad = torch.stack([extremes[0].double(), extremes[1].double(),
+                                          input_flag.reshape(()).double()]).tolist()
+            if bad:
+                raise ValueError("quantized values must be finite")
+            self._finite = math.isfinite(low) and math.isfinite(high)
+        if agree is not None:
+            self._finite = agree(self._finite)
+        if not self.config.wide and not stable and not self._finite:
+            return self._execute(q, xscale, schedule, event, stable=True, vector_offset=vector_offset, tiles=tiles)
+        return output
+
+    def _launch(self, q, xscale, schedule, event, *, stable=False, vector_offset=0, tiles=None, output=None):
+        """Enqueue the product on the current stream (no host synchronisation) into
+        ``output`` ([n, shard width], allocated when None) and return it."""
         n = q.shape[0]
         wide = self.config.wide or stable
         dtype = torch.float64 if wide else torch.float32
         t0, t1 = (0, self.p) if tiles is None else tiles
         cols = self.config.array_size[1]
         c0, c1 = t0 * cols, min(t1 * cols, self.out_features)
-        output = torch.empty((n, c1 - c0), device=q.device, dtype=dtype)
+        if output is None:
+            output = torch.empty((n, c1 - c0), device=q.device, dtype=dtype)
+        elif output.shape != (n, c1 - c0) or output.dtype != dtype or output.stride(-1) != 1:
+            raise ValueError("output buffer does not match the product")
         # The kernels address output columns globally: hand them the buffer shifted
         # back by c0 columns (only columns >= c0 are written).
         base = ct.c_void_p(output.data_ptr() - c0 * output.element_size())
@@ -590,19 +631,22 @@ class AnalogMatrix(nn.Module):
         kmajor_ready = 0
         kmajor_bytes = 0 if stable else self._kmajor_size(packed.shape[0], schedule)
         if kmajor_bytes:
-            # Tensor-core kernels: keep the workspace, whose leading K-major weight copy
-            # stays valid until the codes change.  A call on another stream gets a fresh
-            # one; a larger one keeps the copy.
-            if self._ws is None or self._ws_stream != stream.value:
-                self._ws = torch.empty(workspace_bytes, dtype=torch.uint8, device=q.device)
-                self._ws_bytes, self._ws_stream, self._ws_ready = workspace_bytes, stream.value, False
-            elif self._ws_bytes < workspace_bytes:
+            # Tensor-core kernels: keep a workspace per stream (launches on different
+            # streams may overlap), whose leading K-major weight copy stays valid
+            # until the codes change; a larger one keeps the copy.
+            entry = self._workspaces.get(stream.value)
+            if entry is None:
+                if len(self._workspaces) >= 4:
+                    self._workspaces.pop(next(iter(self._workspaces)))
+                entry = self._workspaces[stream.value] = [
+                    torch.empty(workspace_bytes, dtype=torch.uint8, device=q.device), False]
+            elif entry[0].numel() < workspace_bytes:
                 grown = torch.empty(workspace_bytes, dtype=torch.uint8, device=q.device)
-                if self._ws_ready:
-                    grown[:kmajor_bytes].copy_(self._ws[:kmajor_bytes])
-                self._ws, self._ws_bytes = grown, workspace_bytes
+                if entry[1]:
+                    grown[:kmajor_bytes].copy_(entry[0][:kmajor_bytes])
+                entry[0] = grown
             self._kmajor_bytes = kmajor_bytes
-            workspace, workspace_bytes, kmajor_ready = self._ws, self._ws_bytes, int(self._ws_ready)
+            workspace, workspace_bytes, kmajor_ready = entry[0], entry[0].numel(), int(entry[1])
         else:
             workspace = torch.empty(max(workspace_bytes, 1), dtype=torch.uint8, device=q.device)
         native = _lib.schedule(**schedule, kmajor_ready=kmajor_ready)
@@ -611,13 +655,13 @@ class AnalogMatrix(nn.Module):
                 _lib.native_config(self.config), ct.byref(native), _lib.ptr(q), _lib.ptr(xscale),
                 _lib.ptr(packed), _lib.ptr(self.weight_scale.contiguous()),
                 _lib.ptr(self.bias) if fuse_bias else None, base, n, packed.shape[0], self.p,
-                self.out_features, c1 - c0, t0, t1, self.seed & 0xFFFFFFFF, event,
+                self.out_features, output.stride(0), t0, t1, self.seed & 0xFFFFFFFF, event,
                 vector_offset, int(stable), _lib.ptr(workspace), workspace_bytes, stream,
             ),
             "mf_sliced_mm",
         )
-        if workspace is self._ws:
-            self._ws_ready = True
+        if kmajor_bytes:
+            entry[1] = True
         if self.zero_correction is not None:
             bits = self.config.activation_bits
             signed = q.to(torch.int64).reshape(n, -1)
@@ -635,24 +679,9 @@ class AnalogMatrix(nn.Module):
                     output[:, begin - c0:end - c0] += correction
             else:
                 correction = (sums.to(dtype) * xscale.to(dtype)) @ self.zero_correction[:, c0:c1].to(dtype)
-                output = output + correction
+                output += correction
             if self.bias is not None:
-                output = output + self.bias[c0:c1]
-        # One host synchronisation decides both the FP64 rerun of a narrow config
-        # (simulator.py:614-615) and, in forward, the non-finite error.
-        if input_flag is None:
-            self._finite = finite_flags(output)[0]
-        else:
-            extremes = torch.aminmax(output) if output.numel() else (output.new_zeros(()), output.new_zeros(()))
-            low, high, bad = torch.stack([extremes[0].double(), extremes[1].double(),
-                                          input_flag.reshape(()).double()]).tolist()
-            if bad:
-                raise ValueError("quantized values must be finite")
-            self._finite = math.isfinite(low) and math.isfinite(high)
-        if agree is not None:
-            self._finite = agree(self._finite)
-        if not self.config.wide and not stable and not self._finite:
-            return self._execute(q, xscale, schedule, event, stable=True, vector_offset=vector_offset, tiles=tiles)
+                output += self.bias[c0:c1]
         return output
 
     @torch.no_grad()
