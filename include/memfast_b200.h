@@ -73,11 +73,16 @@ typedef struct {
 } mf_config;
 
 /* Execution schedule (the reference's tuned-mode grid, simulator.py:27-45,
- * re-declared over this engine's tile shapes).  Every schedule gives
- * bit-identical output. */
+ * re-declared over this engine's tile shapes).  For ideal devices every
+ * schedule gives bit-identical output.  For nonideal devices kernel 1 (SIMT)
+ * and the tensor-core currents (0 / 2) sum each read's FP32 currents in
+ * different orders, so a few ADC roundings differ between them (the tuned mode's
+ * bitwise check then keeps the default's kernel). */
 typedef struct {
-    int32_t kernel;     /* 0 auto, 1 generic SIMT, 2 tcgen05 (packed integer counts when the
-                           configuration fits, else FP8 digit planes), 3 tcgen05 FP8 digit planes */
+    int32_t kernel;     /* 0 auto, 1 generic SIMT, 2 tcgen05 (ideal: packed integer counts when
+                           the configuration fits, else FP8 digit planes; nonideal: FP16 digit x
+                           conductance currents when the configuration fits), 3 tcgen05 FP8
+                           digit planes (ideal) */
     int32_t tile_n;     /* vectors per CTA (generic: 8,16,32) */
     int32_t tile_o;     /* output columns per CTA (generic: 32,64,128) */
     int32_t arrays;     /* tiles restored per group in physical mode (>=1) */

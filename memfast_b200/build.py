@@ -16,7 +16,8 @@ PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libmemfast_b200.so"
-SOURCES = ["capi.cu", "quantize.cu", "generic.cu", "tc_common.cu", "tc_ideal.cu", "tc_packed.cu"]
+SOURCES = ["capi.cu", "quantize.cu", "generic.cu", "tc_common.cu", "tc_ideal.cu", "tc_packed.cu",
+           "tc_physical.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -277,6 +277,12 @@ static bool use_packed(const mf_config& c, const mf_schedule& s, int32_t m, int3
     return (s.kernel == 0 || s.kernel == 2) && !stable && tc_packed_eligible(c, m);
 }
 
+// Nonideal tensor-core currents (tc_physical.cu): automatic choice and schedule
+// kernel 2 when the configuration fits its plan; kernel 1 keeps the SIMT kernels.
+static bool use_tc_physical(const mf_config& c, const mf_schedule& s, int32_t m, int32_t stable) {
+    return (s.kernel == 0 || s.kernel == 2) && !stable && tc_physical_eligible(c, m);
+}
+
 static bool use_tc(const mf_config& c, const mf_schedule& s, int32_t m, int32_t stable) {
     return (s.kernel == 0 || s.kernel == 2 || s.kernel == 3) && !stable && tc_eligible(c, m);
 }
@@ -297,6 +303,7 @@ mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedu
     mf_schedule s = schedule_or_default(schedule);
     if (use_packed(*cfg, s, m, 0)) *bytes = tc_packed_workspace_bytes(*cfg, n, m, p, tile_end - tile_begin);
     else if (use_tc(*cfg, s, m, 0)) *bytes = tc_workspace_bytes(*cfg, m, p);
+    else if (use_tc_physical(*cfg, s, m, 0)) *bytes = tc_physical_workspace_bytes(*cfg, m, tile_end - tile_begin);
     else *bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, tile_end - tile_begin);
     return MF_OK;
 }
@@ -328,6 +335,8 @@ mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const 
     if (use_packed(*cfg, s, m, stable))
         return tc_packed_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
     if (use_tc(*cfg, s, m, stable)) return tc_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
+    if (use_tc_physical(*cfg, s, m, stable))
+        return tc_physical_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
     if (use_ideal(*cfg, s)) return generic_ideal(*cfg, s, a, (cudaStream_t)stream);
     return physical(*cfg, s, a, workspace, workspace_bytes, (cudaStream_t)stream);
 }
@@ -349,6 +358,9 @@ mf_status mf_query(const mf_config* cfg, const mf_schedule* schedule, int64_t n,
     } else if (use_tc(*cfg, s, m, 0)) {
         out->workspace_bytes = tc_workspace_bytes(*cfg, m, p);
         out->threads = tc_block_threads();
+    } else if (use_tc_physical(*cfg, s, m, 0)) {
+        out->workspace_bytes = tc_physical_workspace_bytes(*cfg, m, p);
+        out->threads = tc_physical_threads();
         out->kmajor_bytes = (size_t)p * cfg->cols * m * cfg->rows;
     } else {
         out->workspace_bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, p);

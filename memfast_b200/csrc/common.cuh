@@ -103,6 +103,30 @@ __device__ __forceinline__ float rng_normal(int64_t address, uint64_t seed, uint
     return __fmul_rn(radius, cosf(__fmul_rn(6.283185307179586f, second)));
 }
 
+// ------------------------------------------------- restored conductance --
+// FP32 conductance of one cell (reference.py:10-51): nominal level of the weight
+// digit, write variation (stream 10), drift, stuck-at faults (stream 30) and,
+// in shared read mode, the read event's variation (stream 20).  `address` is the
+// global cell address (((array * p + tile) * W + w) * R + row) * C + col.
+__device__ __forceinline__ float restored_conductance_f32(const Physics& P, long long state, int mask,
+                                                          long long address, uint64_t seed, uint64_t read_seed) {
+    const float high = (float)P.high, low = (float)P.low, span = (float)P.span;
+    float f;
+    if (mask == 1) f = state ? high : low;
+    else f = __fadd_rn(low, __fmul_rn(span, __fdiv_rn((float)state, (float)mask)));
+    if (P.write_var != 0) f = __fmul_rn(f, expf(__fmul_rn((float)P.write_var, rng_normal(address, seed, 10))));
+    f = __fmul_rn(f, (float)P.drift);
+    if (P.saf_cut != 0) {
+        const float u = rng_uniform(address, seed, 30);
+        const float lo = (float)P.saf_low, hi = (float)P.saf_cut;
+        if (u < lo) f = low;
+        if (u >= lo && u < hi) f = high;
+    }
+    if (P.read_mode == 0 && P.read_var != 0)
+        f = __fmul_rn(f, expf(__fmul_rn((float)P.read_var, rng_normal(address, read_seed, 20))));
+    return f;
+}
+
 // ------------------------------------------------------------- cascade sum --
 // PyTorch's CPU reduction over a non-innermost dimension (SumKernel.cpp
 // multi_row_sum): values are summed from +0.0 in blocks of 2^power; at every

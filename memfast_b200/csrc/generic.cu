@@ -223,21 +223,7 @@ __global__ void restore_kernel(Layout L, Physics P, const void* packed_raw, int 
         const long long state = (code >> L.w_shift[w]) & L.w_mask[w];
         CurT raw;
         if (sizeof(CurT) == 4) {
-            const float high = (float)P.high, low = (float)P.low, span = (float)P.span;
-            float f;
-            if (L.w_mask[w] == 1) f = state ? high : low;
-            else f = __fadd_rn(low, __fmul_rn(span, __fdiv_rn((float)state, (float)L.w_mask[w])));
-            if (P.write_var != 0) f = __fmul_rn(f, expf(__fmul_rn((float)P.write_var, rng_normal(address, seed, 10))));
-            f = __fmul_rn(f, (float)P.drift);
-            if (P.saf_cut != 0) {
-                const float u = rng_uniform(address, seed, 30);
-                const float lo = (float)P.saf_low, hi = (float)P.saf_cut;
-                if (u < lo) f = low;
-                if (u >= lo && u < hi) f = high;
-            }
-            if (P.read_mode == 0 && P.read_var != 0)
-                f = __fmul_rn(f, expf(__fmul_rn((float)P.read_var, rng_normal(address, read_seed, 20))));
-            raw = (CurT)f;
+            raw = (CurT)restored_conductance_f32(P, state, L.w_mask[w], address, seed, read_seed);
         } else {
             double d;
             if (L.w_mask[w] == 1) d = state ? P.high : P.low;
@@ -622,27 +608,6 @@ size_t ideal_smem(const mf_config& c) {
     return ((size_t)c.n_in * IDEAL_TV + (size_t)c.n_w * IDEAL_TC) * r4 * 4;
 }
 
-Physics make_physics(const mf_config& c) {
-    Physics P{};
-    P.precise = c.precise_currents;
-    P.read_mode = c.read_mode;
-    P.high = c.high;
-    P.low = c.low;
-    P.span = c.high - c.low;
-    P.voltage = c.voltage;
-    P.inv_unit = 1.0 / c.unit;
-    P.write_var = c.write_var;
-    P.read_var = c.read_var;
-    P.volt_var = c.volt_var;
-    P.nonlinear = c.nonlinear;
-    P.saf_low = c.saf_low;
-    P.saf_cut = c.saf_low + c.saf_high;
-    P.drift = c.drift;
-    const double s2 = c.read_var * c.read_var;
-    P.mean_factor = expm1(0.5 * s2);
-    P.var_factor = exp(s2) * expm1(s2);
-    return P;
-}
 
 template <typename OutT, typename ScaleT>
 mf_status launch_ideal_t(const mf_config& c, const MMArgs& a, cudaStream_t st, TileFilter filter = TileFilter{}) {
@@ -729,6 +694,28 @@ mf_status launch_physical_t(const mf_config& c, const mf_schedule& s, const MMAr
 }
 
 }  // namespace
+
+Physics make_physics(const mf_config& c) {
+    Physics P{};
+    P.precise = c.precise_currents;
+    P.read_mode = c.read_mode;
+    P.high = c.high;
+    P.low = c.low;
+    P.span = c.high - c.low;
+    P.voltage = c.voltage;
+    P.inv_unit = 1.0 / c.unit;
+    P.write_var = c.write_var;
+    P.read_var = c.read_var;
+    P.volt_var = c.volt_var;
+    P.nonlinear = c.nonlinear;
+    P.saf_low = c.saf_low;
+    P.saf_cut = c.saf_low + c.saf_high;
+    P.drift = c.drift;
+    const double s2 = c.read_var * c.read_var;
+    P.mean_factor = expm1(0.5 * s2);
+    P.var_factor = exp(s2) * expm1(s2);
+    return P;
+}
 
 double reconstruction_bound(const mf_config& c) {
     double in = 0, wt = 0;

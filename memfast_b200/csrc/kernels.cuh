@@ -19,6 +19,9 @@ mf_status program_weights(const mf_config& c, const void* w, int dtype, int64_t 
                           int64_t ldw, void* packed, void* wscale, void* workspace,
                           size_t ws_bytes, cudaStream_t stream);
 
+// Physical constants of a configuration for device code (reference.py, config.py).
+Physics make_physics(const mf_config& c);
+
 // Output extent of a convolution along one axis (0 when the window does not fit).
 int64_t conv_output_extent(int64_t size, int32_t kernel, int32_t stride, int32_t pad, int32_t dilation);
 
@@ -84,6 +87,13 @@ bool tc_eligible(const mf_config& c, int32_t m);
 size_t tc_workspace_bytes(const mf_config& c, int32_t m, int32_t p);
 int tc_block_threads();
 mf_status tc_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st);
+
+// Nonideal tensor-core path (tc_physical.cu).
+bool tc_physical_eligible(const mf_config& c, int32_t m);
+size_t tc_physical_workspace_bytes(const mf_config& c, int32_t m, int32_t tiles);
+int tc_physical_threads();
+mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, size_t ws_bytes,
+                                cudaStream_t st);
 
 // tcgen05 / TMEM fast path with packed integer counts (tc_packed.cu).
 bool tc_packed_eligible(const mf_config& c, int32_t m);

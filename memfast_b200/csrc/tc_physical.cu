@@ -1,0 +1,634 @@
+// tcgen05 path for nonideal devices (sm_100a): the FP32 currents of every
+// (input slice, weight slice) pair of every read on the tensor cores.
+//
+// The reference computes, per read of rows_per_read rows, the current
+//     I_aw = sum_r V_a(r) (G_w(r) - LOW),    V_a = voltage * d_a / M_a
+// of every slice pair, converts it with the (optionally S-shaped) ADC and
+// reconstructs T = sum_aw s_a s_w count_aw (memfast/reference.py:63-117).  Here
+//     I_aw = (voltage / M_a) * sum_r d_a(r) * G'_w(r),    G' = G - LOW,
+// with the digit d_a exact in FP16.  G' is carried as a 22-bit fixed-point
+// integer X = rint(G' * 2^s) = 2048 H + L with 11-bit halves H and L (FP16
+// integers), whose products with the digits are summed in separate FP32
+// accumulators: every partial sum is an integer below 2^24, so the tensor core
+// accumulates both exactly, whatever its internal rounding, and the epilogue
+// joins them with one round-to-nearest FMA, 2048 S_H + S_L.  (A single FP32
+// accumulator of floating parts would truncate at every MMA and bias the
+// currents low.)  The 1-bit configuration, whose small counts showed no flips
+// either way, keeps one accumulator of two floating FP16 parts, which leaves
+// room for twice the columns.  The currents then differ from the reference's
+// FP32 bmm by rounding only; the ADC scales, rounds half to even and clamps as
+// the reference does.
+//
+// Scope: FP32 currents and epilogue (not Config.wide / precise_currents), no
+// voltage noise, read noise only in the shared mode (it is folded into G' per
+// read event by restore_split_kernel), input digits of at most 3 bits, 32- or
+// 64-row reads, at most 256 reads per output.  Everything else runs on the SIMT
+// kernels in generic.cu.
+//
+// Per CTA: 128 vectors x BC = NJOB * BN output columns.  Per read:
+//   warp 0      TMA: the read's activation codes [128 x KR] and, for every job
+//               and part, the [NPAD x 16] FP16 tiles of G' per 16-row MMA step
+//   warp 1      TMEM owner and MMA issuer: per job and input slice a, one FP32
+//               accumulator of NPAD columns (BN output columns x NW weight
+//               slices, output-column major) fed by 2 * KR / 16 MMAs
+//   warps 2-3   transform: FP16 digit planes of every input slice (byte lookup)
+//   warps 4-19  epilogue: ADC of every pair, signed reconstruction,
+//               fl(fl(T * xs) * ws) and PyTorch's CPU cascade over the reads
+//               (simulator.py:575-586)
+// Every mbarrier wait is bounded; on timeout the CTA records an error code,
+// drains its own asynchronous work, frees its TMEM and exits.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <string.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "tcgen05.cuh"
+
+namespace mf {
+namespace tcp {
+
+using namespace tg;
+
+constexpr int BM = 128;          // vectors per CTA (TMEM lanes)
+constexpr int PARTS = 2;         // FP16 parts of G'
+constexpr int STAGES = 2;        // TMA stages (codes + G' tiles)
+constexpr int EPI_WARPS = 16;
+constexpr int THREADS = 128 + 32 * EPI_WARPS;
+constexpr int LAUNCH_REGS = (65536 / THREADS) / 8 * 8;
+constexpr int REG_LOW = 56;
+constexpr int REG_HIGH = 104;
+static_assert(128 * REG_LOW + 32 * EPI_WARPS * REG_HIGH <= THREADS * LAUNCH_REGS,
+              "register split exceeds the launch pool");
+constexpr int MAXS = 8;          // slices per operand in the tables below
+
+// Shared-memory and TMEM geometry of one instantiation.
+template <int NIN, int NW, int BN, int NJOB, int KR, bool SPLIT>
+struct Geo {
+    static constexpr int KS = KR / 16;                     // MMA K steps per read
+    static constexpr int NPAD = (NW * BN + 15) / 16 * 16;  // MMA N: B rows of a job
+    static constexpr int ACCS = SPLIT ? PARTS : 1;         // accumulators per slice pair
+    static constexpr int UNIT = ACCS * NIN * NPAD;         // TMEM columns of a job
+    static constexpr int BC = NJOB * BN;                   // output columns per CTA
+    static constexpr int EC = BN / 4;                      // columns per epilogue thread per job
+    static constexpr int VALS = NW * EC;                   // TMEM columns a thread reads per input slice
+    static constexpr int AG = 32 / (ACCS * VALS) < 1 ? 1 : (32 / (ACCS * VALS) < NIN ? 32 / (ACCS * VALS) : NIN);
+                                                           // input slices per TMEM load group
+    static constexpr int XB = BM * KR;                     // code tile
+    static constexpr int BT = NPAD * 32;                   // one [NPAD x 16] FP16 tile
+    static constexpr int BB = NJOB * PARTS * KS * BT;
+    static constexpr int STAGE = (XB + BB + 1023) / 1024 * 1024;
+    static constexpr int AT = BM * 32;                     // one [128 x 16] FP16 tile
+    static constexpr int AB = NIN * KS * AT;               // one set of digit planes
+    // Digit planes double-buffered (transform of read i+1 overlaps the MMAs of read i) when they fit.
+    static constexpr int ABUF = STAGES * STAGE + 2 * AB + BC * BM * 4 + 1024 <= 227 * 1024 ? 2 : 1;
+    static constexpr int OFF_A = STAGES * STAGE;
+    static constexpr int OFF_ACC1 = OFF_A + ABUF * AB;
+    static constexpr int OFF_BAR = OFF_ACC1 + BC * BM * 4;
+    static constexpr int NBAR = 2 * STAGES + 2 * ABUF + 2 * NJOB + 1;
+    static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16;
+    static constexpr int TMEM_COLS = NJOB * UNIT <= 256 ? 256 : 512;
+    static_assert(NJOB * UNIT <= 512, "accumulators exceed TMEM");
+    static_assert(BN % 4 == 0 && KR % 16 == 0 && NIN <= MAXS && NW <= MAXS, "unsupported shape");
+    static_assert(BYTES + 1024 <= 232448, "exceeds the 227 KB shared-memory limit");
+};
+
+struct Args {
+    const float* bias;       // [out_features] or null
+    const float* xscale;     // [n, MR]
+    const float* wscale;     // [MR, ldw]
+    float* out;
+    long long n, ldo, ldw;
+    int out_features, MR;
+    long long full;          // reads in complete 16-read cascade blocks
+    int col_begin, col_end;  // output columns of this call
+    unsigned* error;
+    int a_shift[MAXS];
+    uint32_t a_mask4[MAXS];  // digit mask replicated in every byte
+    uint32_t lut_lo, lut_hi; // FP16 high bytes of the digits 0..7 (low bytes are 0)
+    float cw[MAXS];          // voltage * M_w / unit * 2^-s: FP16-part sum -> ADC input
+    float slope[MAXS];       // S-curve: nonlinear / max_w
+    float maxw[MAXS];
+    int factor[MAXS][MAXS];  // s_a * s_w
+};
+
+template <int N>
+__device__ __forceinline__ void tmem_load_cols(uint32_t addr, uint32_t* v) {
+    if constexpr (N >= 8) {
+        tmem_ld(addr, *reinterpret_cast<uint32_t(*)[8]>(v));
+        tmem_load_cols<N - 8>(addr + 8, v + 8);
+    } else if constexpr (N >= 4) {
+        tmem_ld(addr, *reinterpret_cast<uint32_t(*)[4]>(v));
+        tmem_load_cols<N - 4>(addr + 4, v + 4);
+    } else if constexpr (N >= 2) {
+        tmem_ld(addr, *reinterpret_cast<uint32_t(*)[2]>(v));
+        tmem_load_cols<N - 2>(addr + 2, v + 2);
+    } else if constexpr (N == 1) {
+        tmem_ld(addr, *reinterpret_cast<uint32_t(*)[1]>(v));
+    }
+}
+
+// After tcgen05.wait::ld: route every loaded register through an asm statement
+// ordered after the wait, so that no use is scheduled ahead of it.
+template <int N>
+__device__ __forceinline__ void tmem_loaded(uint32_t* v) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int k = 0; k < N; ++k) asm volatile("" : "+r"(v[k]));
+}
+
+template <int NIN, int NW, int BN, int NJOB, int KR, bool SPLIT, bool NONLINEAR>
+__global__ void __launch_bounds__(THREADS, 1)
+    tc_physical_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_g,
+                       const __grid_constant__ Args args) {
+    using G = Geo<NIN, NW, BN, NJOB, KR, SPLIT>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* a_planes = base + G::OFF_A;
+    float* acc1 = reinterpret_cast<float*>(base + G::OFF_ACC1);             // [BC][BM]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + G::OFF_BAR);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* a_ready = bars + 2 * STAGES;      // [ABUF]
+    uint64_t* a_free = a_ready + G::ABUF;       // [ABUF]
+    uint64_t* unit_full = a_free + G::ABUF;
+    uint64_t* unit_empty = unit_full + NJOB;
+    uint64_t* drained = unit_empty + NJOB;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + G::NBAR);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long n0 = (long long)blockIdx.x * BM;
+    const int c0 = args.col_begin + blockIdx.y * G::BC;   // first output column of this CTA
+    const int MR = args.MR;
+    unsigned* err = args.error;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int b = 0; b < G::ABUF; ++b) {
+            mbar_init(&a_ready[b], 2);
+            mbar_init(&a_free[b], 1);
+        }
+        for (int j = 0; j < NJOB; ++j) {
+            mbar_init(&unit_full[j], 1);
+            mbar_init(&unit_empty[j], EPI_WARPS);
+        }
+        mbar_init(drained, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int idx = threadIdx.x; idx < G::BC * BM; idx += THREADS) acc1[idx] = 0.0f;
+    if (warp == 0 && lane == 0) {
+        prefetch_map(&map_x);
+        prefetch_map(&map_g);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, G::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < 4) {
+        set_maxnreg_dec<REG_LOW>();
+        if (warp == 0) {
+            // ------------------------------------------------------------ producer
+            if (lane == 0) {
+                const int cb0 = blockIdx.y * NJOB;        // first BN-column block of this CTA
+                int issued = 0;
+                for (int i = 0; i < MR; ++i) {
+                    const int st = i % STAGES;
+                    if (!mbar_wait(&empty[st], ((i / STAGES) & 1) ^ 1, abort_flag, err, 41)) break;
+                    uint8_t* stage = base + st * G::STAGE;
+                    mbar_expect_tx(&full[st], G::XB + G::BB);
+                    tma_load_2d(stage, &map_x, i * KR, (int)n0, &full[st]);
+#pragma unroll 1
+                    for (int j = 0; j < NJOB; ++j)
+#pragma unroll
+                        for (int part = 0; part < PARTS; ++part)
+#pragma unroll
+                            for (int ks = 0; ks < G::KS; ++ks)
+                                tma_load_2d(stage + G::XB + ((j * PARTS + part) * G::KS + ks) * G::BT, &map_g,
+                                            i * KR + ks * 16, ((cb0 + j) * PARTS + part) * G::NPAD, &full[st]);
+                    issued = i + 1;
+                }
+                // Every issued load lands before the CTA may exit.
+                for (int i = issued - STAGES > 0 ? issued - STAGES : 0; i < issued; ++i)
+                    mbar_drain(&full[i % STAGES], (i / STAGES) & 1);
+            }
+        } else if (warp == 1) {
+            // ------------------------------------------------------------ MMA issuer
+            if (lane == 0) {
+                const uint32_t idesc = idesc_f16(BM, G::NPAD);
+                bool ok = true;
+                for (int i = 0; i < MR && ok; ++i) {
+                    const int st = i % STAGES;
+                    if (!mbar_wait(&full[st], (i / STAGES) & 1, abort_flag, err, 42)) break;
+                    const int ab = i % G::ABUF;
+                    if (!mbar_wait(&a_ready[ab], (i / G::ABUF) & 1, abort_flag, err, 43)) break;
+                    tc_fence_after();
+                    const uint8_t* btiles = base + st * G::STAGE + G::XB;
+                    const uint8_t* planes = a_planes + ab * G::AB;
+#pragma unroll 1
+                    for (int j = 0; j < NJOB; ++j) {
+                        if (!mbar_wait(&unit_empty[j], (i & 1) ^ 1, abort_flag, err, 44)) { ok = false; break; }
+                        tc_fence_after();
+                        // Descriptors advance by (byte offset >> 4) in their address field.
+                        const uint64_t db = desc_sw32(btiles + j * PARTS * G::KS * G::BT);
+#pragma unroll 1
+                        for (int a = 0; a < NIN; ++a) {
+                            const uint64_t da = desc_sw32(planes + a * G::KS * G::AT);
+#pragma unroll
+                            for (int part = 0; part < PARTS; ++part)
+#pragma unroll
+                                for (int ks = 0; ks < G::KS; ++ks)
+                                    mma_f16(tmem + j * G::UNIT + ((SPLIT ? part * NIN : 0) + a) * G::NPAD,
+                                            da + (uint64_t)((ks * G::AT) >> 4),
+                                            db + (uint64_t)(((part * G::KS + ks) * G::BT) >> 4), idesc,
+                                            SPLIT ? ks != 0 : (part | ks) != 0);
+                        }
+                        mma_commit(&unit_full[j]);
+                    }
+                    if (!ok) break;
+                    mma_commit(&a_free[ab]);
+                    mma_commit(&empty[st]);
+                }
+                // All issued MMAs complete before TMEM is released.
+                mma_commit(drained);
+                mbar_drain(drained, 0);
+            }
+        } else {
+            // ------------------------------------------------------------ transform
+            // Row t of the code tile holds the read's KR codes (no swizzle); each
+            // 16-code step becomes one [128 x 16] FP16 plane per input slice in the
+            // 32-byte-swizzled K-major layout (16-byte halves swapped in rows with bit 2 set).
+            const int tw = warp - 2;
+            for (int i = 0; i < MR; ++i) {
+                const int st = i % STAGES;
+                const int ab = i % G::ABUF;
+                bool ok = mbar_wait(&full[st], (i / STAGES) & 1, abort_flag, err, 45);
+                ok = ok && mbar_wait(&a_free[ab], ((i / G::ABUF) & 1) ^ 1, abort_flag, err, 46);
+                if (!__all_sync(0xFFFFFFFFu, ok)) break;
+                const uint8_t* codes = base + st * G::STAGE;
+                uint8_t* planes = a_planes + ab * G::AB;
+#pragma unroll 1
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int t = tw * 32 + lane + 64 * hh;
+                    const uint32_t flip = ((uint32_t)t >> 2) & 1u;
+#pragma unroll 1
+                    for (int ks = 0; ks < G::KS; ++ks) {
+                        const uint4 c16 = *reinterpret_cast<const uint4*>(codes + t * KR + ks * 16);
+                        const uint32_t w4[4] = {c16.x, c16.y, c16.z, c16.w};
+#pragma unroll
+                        for (int a = 0; a < NIN; ++a) {
+                            uint32_t o[8];
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const uint32_t d = (w4[k] >> args.a_shift[a]) & args.a_mask4[a];
+                                // Output bytes [0, hi(d0), 0, hi(d1)] and [0, hi(d2), 0, hi(d3)].
+                                o[2 * k] = __byte_perm(args.lut_lo, args.lut_hi, (d << 4) & 0xF0F0u);
+                                o[2 * k + 1] = __byte_perm(args.lut_lo, args.lut_hi, (d >> 12) & 0xF0F0u);
+                            }
+                            uint8_t* row = planes + (a * G::KS + ks) * G::AT + t * 32;
+                            *reinterpret_cast<uint4*>(row + (flip << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                            *reinterpret_cast<uint4*>(row + ((flip ^ 1u) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+                        }
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_ready[ab]);
+            }
+        }
+    } else {
+        set_maxnreg_inc<REG_HIGH>();
+        // ---------------------------------------------------------------- epilogue
+        // Warp w reads TMEM lane quadrant w & 3 (rows) and the EC-column slice hc of
+        // every job; within a job's accumulator of input slice a, output column jj
+        // and weight slice w sit at column a * NPAD + jj * NW + w.
+        const int quad = warp & 3;
+        const int hc = (warp - 4) >> 2;
+        const int r = quad * 32 + lane;
+        const long long row = n0 + r;
+        const bool live = row < args.n;
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + hc * G::VALS;
+        float acc0[NJOB][G::EC];
+#pragma unroll
+        for (int j = 0; j < NJOB; ++j)
+#pragma unroll
+            for (int e = 0; e < G::EC; ++e) acc0[j][e] = 0.0f;
+        bool ok = true;
+        for (int i = 0; i < MR && ok; ++i) {
+            const float xs = live ? __ldg(args.xscale + row * MR + i) : 0.0f;
+#pragma unroll 1
+            for (int j = 0; j < NJOB; ++j) {
+                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&unit_full[j], i & 1, abort_flag, err, 47));
+                if (!ok) break;
+                tc_fence_after();
+                // Input slices in groups of at most 32 loaded columns; the unit is released
+                // as soon as the last group is in registers.
+                int total[G::EC];
+#pragma unroll
+                for (int e = 0; e < G::EC; ++e) total[e] = 0;
+#pragma unroll
+                for (int a0 = 0; a0 < NIN; a0 += G::AG) {
+                    uint32_t v[G::ACCS][G::AG][G::VALS];
+#pragma unroll
+                    for (int acc = 0; acc < G::ACCS; ++acc)
+#pragma unroll
+                        for (int a = 0; a < G::AG; ++a)
+                            if (a0 + a < NIN)
+                                tmem_load_cols<G::VALS>(lane_base + j * G::UNIT + (acc * NIN + a0 + a) * G::NPAD,
+                                                        v[acc][a]);
+                    tmem_loaded<G::ACCS * G::AG * G::VALS>(&v[0][0][0]);
+                    if (a0 + G::AG >= NIN) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&unit_empty[j]);
+                    }
+#pragma unroll
+                    for (int a = 0; a < G::AG; ++a) {
+                        if (a0 + a >= NIN) break;
+#pragma unroll
+                        for (int e = 0; e < G::EC; ++e)
+#pragma unroll
+                            for (int w = 0; w < NW; ++w) {
+                                // SPLIT: 2048 S_H + S_L, both exact integers, rounded once.
+                                const float x = SPLIT ? __fmaf_rn(__uint_as_float(v[0][a][e * NW + w]), 2048.0f,
+                                                                  __uint_as_float(v[SPLIT ? 1 : 0][a][e * NW + w]))
+                                                      : __uint_as_float(v[0][a][e * NW + w]);
+                                float z = __fmul_rn(x, args.cw[w]);
+                                if (NONLINEAR) z = __fdiv_rn(z, __fadd_rn(1.0f, fabsf(__fmul_rn(args.slope[w], z))));
+                                z = fminf(fmaxf(z, 0.0f), args.maxw[w]);
+                                total[e] += __float2int_rn(z) * args.factor[a0 + a][w];
+                            }
+                    }
+                }
+                const int colj = c0 + j * BN + hc * G::EC;
+#pragma unroll
+                for (int e = 0; e < G::EC; ++e) {
+                    const int col = colj + e;
+                    const float ws = col < args.col_end ? __ldg(args.wscale + (long long)i * args.ldw + col) : 0.0f;
+                    acc0[j][e] = __fadd_rn(acc0[j][e], __fmul_rn(__fmul_rn(__int2float_rn(total[e]), xs), ws));
+                }
+            }
+            if (!ok) break;
+            // Block boundary of the 16-read cascade: level 1 += level 0 (MR <= 256 keeps two levels).
+            const int done = i + 1;
+            if (done <= args.full && (done & 15) == 0) {
+#pragma unroll
+                for (int j = 0; j < NJOB; ++j)
+#pragma unroll
+                    for (int e = 0; e < G::EC; ++e) {
+                        float* slot = acc1 + (j * BN + hc * G::EC + e) * BM + r;
+                        *slot = __fadd_rn(*slot, acc0[j][e]);
+                        acc0[j][e] = 0.0f;
+                    }
+            }
+        }
+        if (ok && live) {
+#pragma unroll
+            for (int j = 0; j < NJOB; ++j)
+#pragma unroll
+                for (int e = 0; e < G::EC; ++e) {
+                    const int cl = j * BN + hc * G::EC + e;
+                    const int col = c0 + cl;
+                    if (col >= args.col_end || col >= args.out_features) continue;
+                    // acc0 + acc1 + acc2 + acc3 (upper levels zero), then the reference's
+                    // store into a zero-filled output.
+                    float value = __fadd_rn(acc0[j][e], acc1[cl * BM + r]);
+                    value = __fadd_rn(value, 0.0f);
+                    value = __fadd_rn(value, 0.0f);
+                    value = __fadd_rn(0.0f, value);
+                    if (args.bias) value = __fadd_rn(value, args.bias[col]);
+                    args.out[row * args.ldo + col] = value;
+                }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, G::TMEM_COLS);
+    }
+}
+
+// G' = G - LOW of the weight slices as the B operand: rows
+// ((block * PARTS + part) * NPAD + jj * NW + w) for output column
+// col_begin + block * BN + jj and weight slice w (zero rows pad NPAD), K
+// contiguous.  fixed: X = rint(G' * scale) (|X| < 2^22) as the FP16 integers
+// H = rint(X / 2048) and L = X - 2048 H; otherwise x = G' * scale (< 2^14) as the
+// FP16 parts hi = fp16(x), lo = fp16(x - hi).  The conductance is the SIMT
+// path's (restored_conductance_f32).
+__global__ void restore_split_kernel(Layout L, Physics P, const uint8_t* packed, int p, int col_begin, int blocks,
+                                     int bn, int npad, long long kpad, uint32_t seed, uint64_t event, float scale,
+                                     int fixed, __half* gs) {
+    const long long total = (long long)blocks * npad * kpad;
+    const uint64_t read_seed = event_seed(seed, event);
+    const float low = (float)P.low;
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const long long k = idx % kpad;
+        const long long rest = idx / kpad;
+        const int prow = (int)(rest % npad);
+        const int block = (int)(rest / npad);
+        __half hi = __float2half_rn(0.0f), lo = hi;
+        if (prow < L.n_w * bn) {
+            const int jj = prow / L.n_w, w = prow % L.n_w;
+            const long long o = (long long)col_begin + (long long)block * bn + jj;
+            const long long tile = o / L.C, c = o % L.C;
+            const long long arr = k / L.R, r = k % L.R;
+            const long long cell = ((arr * p + tile) * L.R + r) * L.C + c;
+            const long long state = ((long long)packed[cell] >> L.w_shift[w]) & L.w_mask[w];
+            const long long address = (((arr * p + tile) * L.n_w + w) * L.R + r) * L.C + c;
+            const float g = restored_conductance_f32(P, state, L.w_mask[w], address, seed, read_seed);
+            const float x = __fmul_rn(__fadd_rn(g, -low), scale);
+            if (fixed) {
+                const float X = rintf(x);
+                const float H = rintf(__fmul_rn(X, 1.0f / 2048.0f));
+                hi = __float2half_rn(H);
+                lo = __float2half_rn(__fsub_rn(X, __fmul_rn(H, 2048.0f)));
+            } else {
+                hi = __float2half_rn(x);
+                lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
+            }
+        }
+        gs[((long long)(block * PARTS + 0) * npad + prow) * kpad + k] = hi;
+        gs[((long long)(block * PARTS + 1) * npad + prow) * kpad + k] = lo;
+    }
+}
+
+// Instantiations: (input slices, weight slices) -> columns per job, jobs per CTA,
+// split accumulators.
+struct Shape {
+    int nin, nw, bn, njob, split;
+};
+constexpr Shape kShapes[] = {{5, 5, 8, 1, 1}, {3, 3, 16, 1, 1}, {8, 8, 4, 2, 0}, {4, 4, 8, 2, 1}};
+
+bool shape_of(const mf_config& c, Shape& s) {
+    for (const Shape& k : kShapes)
+        if (k.nin == c.n_in && k.nw == c.n_w) {
+            s = k;
+            return true;
+        }
+    return false;
+}
+
+int npad_of(const Shape& s) { return (s.nw * s.bn + 15) / 16 * 16; }
+
+// Scale 2^s of G': the largest |G'| (nominal level, drift, an 8-sigma write and
+// read variation) stays below 2^22 (fixed-point halves) or 2^14 (floating parts).
+float split_scale(const mf_config& c, bool fixed) {
+    const double gmax = fmax(fabs(c.high), fabs(c.low)) * fmax(c.drift, 1e-30) * exp(8.0 * (c.write_var + c.read_var));
+    const int s = (int)floor(log2((fixed ? 4194303.0 : 16384.0) / gmax));
+    return (float)ldexp(1.0, s);
+}
+
+}  // namespace tcp
+
+// =================================================================== host side
+bool tc_physical_eligible(const mf_config& c, int32_t m) {
+    if (c.ideal || c.wide || c.wide_codes || c.precise_currents) return false;
+    if (c.volt_var != 0) return false;
+    if (c.read_var != 0 && c.read_mode != 0) return false;
+    if (c.write_var + c.read_var > 1.0) return false;
+    if (c.read_rows != 32 && c.read_rows != 64) return false;
+    if (c.rows % c.read_rows || c.cols % 16) return false;
+    tcp::Shape s;
+    if (!tcp::shape_of(c, s)) return false;
+    for (int i = 0; i < c.n_in; ++i)
+        if (c.in_mask[i] > 7) return false;
+    for (int i = 0; i < c.n_w; ++i)
+        if (c.adc_max[i] < 1 || c.adc_max[i] > (1 << 24)) return false;
+    const long long MR = (long long)m * c.reads;
+    return MR <= 256 && c.high > 0 && c.drift > 0 && reconstruction_bound(c) < 2147483647.0;
+}
+
+int tc_physical_threads() { return tcp::THREADS; }
+
+size_t tc_physical_workspace_bytes(const mf_config& c, int32_t m, int32_t tiles) {
+    tcp::Shape s;
+    if (!tcp::shape_of(c, s)) return 256;
+    const long long blocks = (long long)tiles * c.cols / s.bn;
+    return (size_t)blocks * tcp::PARTS * tcp::npad_of(s) * (size_t)m * c.rows * sizeof(__half) + 256;
+}
+
+template <int NIN, int NW, int BN, int NJOB, bool SPLIT, int KR, bool NL>
+static mf_status launch_tcp(const CUtensorMap& mx, const CUtensorMap& mg, const tcp::Args& args, dim3 grid,
+                            cudaStream_t st) {
+    using G = tcp::Geo<NIN, NW, BN, NJOB, KR, SPLIT>;
+    const size_t smem = G::BYTES + 1024;
+    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJOB, KR, SPLIT, NL>;
+    cudaFuncAttributes attr;
+    MF_CHECK_CUDA(cudaFuncGetAttributes(&attr, kern), "tc physical kernel attributes");
+    const long long pool = (long long)((attr.numRegs + 7) / 8 * 8) * tcp::THREADS;
+    const long long split = 128LL * tcp::REG_LOW + 32LL * tcp::EPI_WARPS * tcp::REG_HIGH;
+    if (split > pool) {
+        set_error("tcgen05 physical kernel launched with %d registers/thread cannot host the %d/%d split",
+                  attr.numRegs, tcp::REG_LOW, tcp::REG_HIGH);
+        return MF_ERR_RESOURCE;
+    }
+    MF_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                  "tc physical smem attribute");
+    kern<<<grid, tcp::THREADS, smem, st>>>(mx, mg, args);
+    MF_LAUNCH_CHECK("tc_physical_kernel");
+    return MF_OK;
+}
+
+template <int NIN, int NW, int BN, int NJOB, bool SPLIT>
+static mf_status dispatch_tcp(const mf_config& c, const CUtensorMap& mx, const CUtensorMap& mg,
+                              const tcp::Args& args, dim3 grid, cudaStream_t st) {
+    const bool nl = c.nonlinear != 0;
+    if (c.read_rows == 32)
+        return nl ? launch_tcp<NIN, NW, BN, NJOB, SPLIT, 32, true>(mx, mg, args, grid, st)
+                  : launch_tcp<NIN, NW, BN, NJOB, SPLIT, 32, false>(mx, mg, args, grid, st);
+    return nl ? launch_tcp<NIN, NW, BN, NJOB, SPLIT, 64, true>(mx, mg, args, grid, st)
+              : launch_tcp<NIN, NW, BN, NJOB, SPLIT, 64, false>(mx, mg, args, grid, st);
+}
+
+mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, size_t ws_bytes,
+                                cudaStream_t st) {
+    int dev = 0, major = 0;
+    MF_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    MF_CHECK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev), "capability");
+    if (major != 10) {
+        set_error("tcgen05 path needs an sm_100 device");
+        return MF_ERR_UNSUPPORTED;
+    }
+    tcp::Shape shape;
+    if (!tc_physical_eligible(c, a.m) || !tcp::shape_of(c, shape)) {
+        set_error("configuration outside the tcgen05 physical plan");
+        return MF_ERR_UNSUPPORTED;
+    }
+    const int tiles = a.tile_end - a.tile_begin;
+    const size_t need = tc_physical_workspace_bytes(c, a.m, tiles);
+    if (!workspace || ws_bytes < need) {
+        set_error("tcgen05 physical workspace too small: %zu < %zu bytes", ws_bytes, need);
+        return MF_ERR_RESOURCE;
+    }
+    const long long K = (long long)a.m * c.rows;
+    const int cols = tiles * c.cols;
+    const int blocks = cols / shape.bn;
+    const int npad = tcp::npad_of(shape);
+    const float scale = tcp::split_scale(c, shape.split != 0);
+    __half* gs = static_cast<__half*>(workspace);
+    {
+        const long long total = (long long)blocks * npad * K;
+        long long grid = (total + 255) / 256;
+        if (grid > 148 * 64) grid = 148 * 64;
+        tcp::restore_split_kernel<<<(unsigned)grid, 256, 0, st>>>(make_layout(c), make_physics(c),
+                                                                 static_cast<const uint8_t*>(a.packed), a.p,
+                                                                 a.tile_begin * c.cols, blocks, shape.bn, npad, K,
+                                                                 a.seed, a.event, scale, shape.split, gs);
+        MF_LAUNCH_CHECK("restore_split_kernel");
+    }
+    CUtensorMap mx, mg;
+    mf_status r = tc_make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n,
+                              (uint64_t)K, (uint32_t)c.read_rows, tcp::BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!r) r = tc_make_map(&mg, gs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K,
+                            (uint64_t)blocks * tcp::PARTS * npad, (uint64_t)K, 16, (uint32_t)npad,
+                            CU_TENSOR_MAP_SWIZZLE_32B);
+    if (r) return r;
+    tcp::Args args{};
+    r = tc_error_word(&args.error);
+    if (r) return r;
+    args.bias = static_cast<const float*>(a.bias);
+    args.xscale = static_cast<const float*>(a.xscale);
+    args.wscale = static_cast<const float*>(a.wscale);
+    args.out = static_cast<float*>(a.out);
+    args.n = a.n;
+    args.ldo = a.ldo;
+    args.ldw = (long long)a.p * c.cols;
+    args.out_features = a.out_features;
+    args.MR = a.m * c.reads;
+    args.full = (long long)args.MR - args.MR % 16;
+    args.col_begin = a.tile_begin * c.cols;
+    args.col_end = a.tile_end * c.cols;
+    // FP16 high bytes of the digits 0..7 (1.0 = 0x3C00, 2.0 = 0x4000, 3.0 = 0x4200, ...).
+    const uint8_t hi[8] = {0x00, 0x3C, 0x40, 0x42, 0x44, 0x45, 0x46, 0x47};
+    args.lut_lo = hi[0] | hi[1] << 8 | hi[2] << 16 | (uint32_t)hi[3] << 24;
+    args.lut_hi = hi[4] | hi[5] << 8 | hi[6] << 16 | (uint32_t)hi[7] << 24;
+    for (int i = 0; i < c.n_in; ++i) {
+        args.a_shift[i] = c.in_shift[i];
+        args.a_mask4[i] = (uint32_t)c.in_mask[i] * 0x01010101u;
+    }
+    const double inv_unit = 1.0 / c.unit;
+    for (int w = 0; w < c.n_w; ++w) {
+        args.cw[w] = (float)(c.voltage * c.w_mask[w] * inv_unit / scale);
+        args.slope[w] = (float)(c.nonlinear / c.adc_max[w]);
+        args.maxw[w] = (float)c.adc_max[w];
+        for (int i = 0; i < c.n_in; ++i) args.factor[i][w] = (int)(c.in_factor[i] * c.w_factor[w]);
+    }
+    const int bc = shape.bn * shape.njob;
+    dim3 grid((unsigned)((a.n + tcp::BM - 1) / tcp::BM), (unsigned)((cols + bc - 1) / bc));
+    if (shape.nin == 5) return dispatch_tcp<5, 5, 8, 1, true>(c, mx, mg, args, grid, st);
+    if (shape.nin == 3) return dispatch_tcp<3, 3, 16, 1, true>(c, mx, mg, args, grid, st);
+    if (shape.nin == 8) return dispatch_tcp<8, 8, 4, 2, false>(c, mx, mg, args, grid, st);
+    return dispatch_tcp<4, 4, 8, 2, true>(c, mx, mg, args, grid, st);
+}
+
+}  // namespace mf

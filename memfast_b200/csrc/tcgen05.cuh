@@ -114,6 +114,11 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n, bool a_signed, boo
            | ((uint32_t)(n >> 3) << 17)    // N
            | ((uint32_t)(m >> 4) << 24);   // M
 }
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+    return (1u << 4)                       // D = F32
+           | (0u << 7) | (0u << 10)        // A = B = F16
+           | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
 __host__ __device__ constexpr uint32_t idesc_e4m3(int m, int n) {
     return (1u << 4)                       // D = F32
            | (0u << 7) | (0u << 10)        // A = B = E4M3
@@ -132,6 +137,13 @@ __device__ __forceinline__ void mma_f8(uint32_t tmem, uint64_t a, uint64_t b, ui
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
@@ -166,6 +178,20 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t tmem, uint32_t columns) {
 // Consecutive TMEM columns of this thread's lane (32x32b shape).  The values are
 // only valid after tmem_wait(), which takes the registers as operands so that no
 // use can be scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_ld(uint32_t addr, uint32_t (&r)[1]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r[0]) : "r"(addr));
+}
+
+__device__ __forceinline__ void tmem_ld(uint32_t addr, uint32_t (&r)[2]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
+}
+
+__device__ __forceinline__ void tmem_ld(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
 __device__ __forceinline__ void tmem_ld(uint32_t addr, uint32_t (&r)[8]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])

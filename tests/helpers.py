@@ -61,26 +61,33 @@ def conv_arguments(conv):
 # pair moves an output by |s_a s_w| * xs * ws (about 1% of the output range for
 # INT8 (1,1,2,2,2)).  Tolerance for such cases, stated once and used by every
 # parity test:
-#   - at most 0.5% of output elements differ;
-#   - no element differs by more than 5% of the output range (a few flips);
+#   - at most 0.5% of output elements differ, and at least two may (one or two
+#     rounding flips in a product of a few hundred elements are the same event
+#     at the same rate);
+#   - no element differs by more than 5% of the output range (a few flips), or,
+#     where the caller knows the operands' scales, by more than four flips of the
+#     most significant slice pair (``flip`` = max |s_a s_w| * max xs * max ws);
 #   - the RMS difference stays below 0.2% and the mean difference below 0.01%
 #     of the range;
 #   - the output distribution matches: mean within 0.1% of the std, std within 0.1%.
 MISMATCH_FRACTION = 5e-3
+MIN_MISMATCHES = 2
 MAX_ERROR_OF_RANGE = 5e-2
 RMS_ERROR_OF_RANGE = 2e-3
 MEAN_ERROR_OF_RANGE = 1e-4
 DISTRIBUTION_TOLERANCE = 1e-3
 
 
-def assert_close_nonideal(got, want, label=""):
+def assert_close_nonideal(got, want, label="", *, flip=None):
     got = np.asarray(got, np.float64)
     want = np.asarray(want, np.float64)
     assert got.shape == want.shape, label
     scale = max(np.abs(want).max(), 1e-30)
     diff = got - want
-    assert np.mean(diff != 0) <= MISMATCH_FRACTION, (label, "mismatch fraction", np.mean(diff != 0))
-    assert np.abs(diff).max() <= MAX_ERROR_OF_RANGE * scale, (label, "max error", np.abs(diff).max() / scale)
+    assert np.sum(diff != 0) <= max(MISMATCH_FRACTION * diff.size, MIN_MISMATCHES), (
+        label, "mismatch fraction", np.mean(diff != 0))
+    bound = MAX_ERROR_OF_RANGE * scale if flip is None else 4 * flip
+    assert np.abs(diff).max() <= bound, (label, "max error", np.abs(diff).max() / scale, bound / scale)
     assert np.sqrt(np.mean(diff**2)) <= RMS_ERROR_OF_RANGE * scale, (label, "rms", np.sqrt(np.mean(diff**2)) / scale)
     assert abs(diff.mean()) <= MEAN_ERROR_OF_RANGE * scale, (label, "mean error", diff.mean() / scale)
     std = max(want.std(), 1e-30)

@@ -48,9 +48,14 @@ def test_workspace_queries_need_no_gpu():
     lib = _lib.load()
     assert lib.mf_sliced_mm_workspace(_lib.native_config(ideal), ct.byref(sched), 64, 2, 3, 0, 3, ct.byref(size)) == 0
     assert size.value == 0
-    assert lib.mf_sliced_mm_workspace(_lib.native_config(noisy), ct.byref(sched), 64, 2, 3, 0, 3, ct.byref(size)) == 0
+    simt = _lib.schedule(kernel=1)
+    assert lib.mf_sliced_mm_workspace(_lib.native_config(noisy), ct.byref(simt), 64, 2, 3, 0, 3, ct.byref(size)) == 0
     # one group of `arrays` tiles of restored FP32 conductances: m * width * W * R * C * 4
     assert size.value == 2 * 2 * 8 * 64 * 64 * 4
+    assert lib.mf_sliced_mm_workspace(_lib.native_config(noisy), ct.byref(sched), 64, 2, 3, 0, 3, ct.byref(size)) == 0
+    # tensor-core currents: two FP16 parts of G - LOW for 8 weight slices x 4-column
+    # blocks of the 3 tiles (NPAD = 32 rows per block and part) over K = 128
+    assert size.value == (3 * 64 // 4) * 2 * 32 * 128 * 2 + 256
     assert lib.mf_quantize_workspace(_lib.native_config(noisy), 0, 10, 300, ct.byref(size)) == 0
     assert size.value >= 10 * 4
 
