@@ -54,15 +54,27 @@ def parse():
                    help="with --gpus N > 1, also all-gather every rank's output rows inside each step")
     p.add_argument("--kernel", type=int, default=0, choices=[0, 1, 2, 3],
                    help="schedule kernel of the kernel-only timing (0 automatic, 1 generic SIMT, "
-                        "2 tcgen05 packed counts, 3 tcgen05 FP8 digit planes)")
+                        "2 tcgen05 (packed counts / nonideal currents), 3 tcgen05 FP8 digit planes)")
+    p.add_argument("--effects", choices=sorted(EFFECTS), default="ideal",
+                   help="device effects of the configs[1] sweep: ideal (the headline), write "
+                        "(write variation 0.02), shared (write + shared read variation 0.02), "
+                        "noisy (write + read + voltage variation 0.02, BASELINE's noisy run)")
     return p.parse_args()
 
 
-def bench_config(mf_module):
+EFFECTS = {
+    "ideal": dict(write_variation=0.0),
+    "write": dict(write_variation=0.02),
+    "shared": dict(write_variation=0.02, read_variation=0.02),
+    "noisy": dict(write_variation=0.02, read_variation=0.02, voltage_variation=0.02),
+}
+
+
+def bench_config(mf_module, effects="ideal"):
     return mf_module.Config(
         array_size=(128, 128), rows_per_read=32, weight_quant_gran=(32, 1), input_quant_gran=(1, 32),
         input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2), adc_bits=(6, 7, 7, 8, 8),
-        nonidealities=mf_module.Nonidealities(write_variation=0.0),
+        nonidealities=mf_module.Nonidealities(**EFFECTS[effects]),
     )
 
 
@@ -82,7 +94,10 @@ def operands(size, seed=2024, rank=0):
 def workload(args):
     n = k = o = args.size
     gpus = args.gpus
-    return dict(workload=f"Simulator.mm {n}x{k}x{o} INT8 (1,1,2,2,2) ideal per GPU", n=n, k=k, o=o,
+    effects = getattr(args, "effects", "ideal")
+    label = "ideal" if effects == "ideal" else "nonideal: " + ", ".join(
+        f"{name.replace('_variation', '')} {value}" for name, value in EFFECTS[effects].items())
+    return dict(workload=f"Simulator.mm {n}x{k}x{o} INT8 (1,1,2,2,2) {label} per GPU", n=n, k=k, o=o,
                 batch=f"{gpus} row block(s) of {n}: one {n * gpus}-row batch, rows sharded, B replicated"
                       + (", output rows all-gathered" if getattr(args, "gather", False) and gpus > 1 else
                          ", each rank keeps its output rows"),
@@ -152,7 +167,7 @@ def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    config = bench_config(mf)
+    config = bench_config(mf, args.effects)
     budget = max(2.0, 150.0 / max(1, args.steps + args.warmup))
     sample = OracleSample(args.size, config, budget)
     rates, times = [], []
@@ -268,7 +283,7 @@ def engine_arm(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     from memfast_b200.sharding import gather_rows, row_range, sharded_mm
 
-    config = bench_config(mf)
+    config = bench_config(mf, args.effects)
     size = args.size
     # Weak scaling: every rank owns `size` rows of a (size * world)-row batch; its rows
     # carry their global vector indices (noise addresses), so each rank's output rows
@@ -387,21 +402,29 @@ def engine_arm(args):
     macs = float(size) ** 3 * world
     pairs = len(config.input_layout) * len(config.weight_layout)
     bf16, hbm, peak_kind = measured_peaks()
-    int8_peak_tops = 2.0 * bf16
+    ideal = args.effects == "ideal"
+    # Ideal: int8 digit MMAs against the int8 dense rate (2 x bf16).  Nonideal: FP16 digit x
+    # conductance MMAs against the f16 dense rate (= bf16); each current's two FP16 halves
+    # double the issued MMA work over this algorithmic count.
+    peak_tops = 2.0 * bf16 if ideal else bf16
     kernel_ops = 2.0 * (rows * size * size) * pairs
     achieved_tops = kernel_ops / kernel_s / 1e12
-    traffic = profiled_traffic()
+    traffic = profiled_traffic() if ideal else None
+    path = ("the tensor-core kernel plus its K-major weight copy and rare-tile filter launch" if ideal else
+            "the conductance restore and the current kernel")
     line = dict(
         metric=metric_name(args.size), value=macs / per_step, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
         ms_per_step=per_step * 1e3, higher_is_better=True, scaling="weak", vs_baseline=None,
-        dtype="u8 digits / int32 totals / f32 epilogue", data="synthetic", config=workload(args),
+        dtype="u8 digits / int32 totals / f32 epilogue" if ideal else
+              "f16 digits x f16 conductance halves / f32 currents, ADC and epilogue",
+        data="synthetic", config=workload(args),
         slice_pair_macs_per_s=macs * pairs / per_step,
-        roofline=dict(bound="tensor", achieved=achieved_tops, peak=int8_peak_tops, unit="TFLOP/s",
-                      frac=achieved_tops / int8_peak_tops, traffic=traffic,
-                      note=f"one mf_sliced_mm call (schedule kernel {args.kernel}: the tensor-core kernel "
-                           f"plus its K-major weight copy and rare-tile filter launch), {rows}x{size}x{size}; "
-                           f"algorithmic {pairs} slice-pair int8 MAC streams x2 ops; peak = 2 x {peak_kind} "
-                           f"dense bf16 ({bf16} TFLOP/s), the int8 dense rate of B200",
+        roofline=dict(bound="tensor", achieved=achieved_tops, peak=peak_tops, unit="TFLOP/s",
+                      frac=achieved_tops / peak_tops, traffic=traffic,
+                      note=f"one mf_sliced_mm call (schedule kernel {args.kernel}: {path}), "
+                           f"{rows}x{size}x{size}; algorithmic {pairs} slice-pair MAC streams x2 ops; peak = "
+                           + (f"2 x {peak_kind} dense bf16 ({bf16} TFLOP/s), the int8 dense rate of B200" if ideal
+                              else f"{peak_kind} dense bf16 ({bf16} TFLOP/s), the f16 dense rate of B200"),
                       kernel_ms=kernel_s * 1e3),
         e2e=dict(value=macs / e2e_step_s, unit=UNIT,
                  h2d_bytes_per_step=int(2 * size * size * world * 4),

@@ -71,14 +71,15 @@ struct Geo {
     static constexpr int NPAD = (NW * BN + 15) / 16 * 16;  // MMA N: B rows of a job
     static constexpr int ACCS = SPLIT ? PARTS : 1;         // accumulators per slice pair
     static constexpr int UNIT = ACCS * NIN * NPAD;         // TMEM columns of a job
+    static constexpr int U = 512 / UNIT < NJOB ? 512 / UNIT : NJOB;   // TMEM units the jobs rotate over
     static constexpr int BC = NJOB * BN;                   // output columns per CTA
     static constexpr int EC = BN / 4;                      // columns per epilogue thread per job
     static constexpr int VALS = NW * EC;                   // TMEM columns a thread reads per input slice
     static constexpr int AG = 32 / (ACCS * VALS) < 1 ? 1 : (32 / (ACCS * VALS) < NIN ? 32 / (ACCS * VALS) : NIN);
                                                            // input slices per TMEM load group
     static constexpr int XB = BM * KR;                     // code tile
-    static constexpr int BT = NPAD * 32;                   // one [NPAD x 16] FP16 tile
-    static constexpr int BB = NJOB * PARTS * KS * BT;
+    static constexpr int BT = PARTS * NPAD * 32;           // one [PARTS*NPAD x 16] FP16 tile (both halves)
+    static constexpr int BB = NJOB * KS * BT;
     static constexpr int STAGE = (XB + BB + 1023) / 1024 * 1024;
     static constexpr int AT = BM * 32;                     // one [128 x 16] FP16 tile
     static constexpr int AB = NIN * KS * AT;               // one set of digit planes
@@ -87,10 +88,11 @@ struct Geo {
     static constexpr int OFF_A = STAGES * STAGE;
     static constexpr int OFF_ACC1 = OFF_A + ABUF * AB;
     static constexpr int OFF_BAR = OFF_ACC1 + BC * BM * 4;
-    static constexpr int NBAR = 2 * STAGES + 2 * ABUF + 2 * NJOB + 1;
+    static constexpr int NG = (NIN + AG - 1) / AG;          // slice groups per unit (own full/empty barriers)
+    static constexpr int NBAR = 2 * STAGES + 2 * ABUF + 2 * U * NG + 1;
     static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16;
-    static constexpr int TMEM_COLS = NJOB * UNIT <= 256 ? 256 : 512;
-    static_assert(NJOB * UNIT <= 512, "accumulators exceed TMEM");
+    static constexpr int TMEM_COLS = U * UNIT <= 256 ? 256 : 512;
+    static_assert(U >= 1 && U * UNIT <= 512, "accumulators exceed TMEM");
     static_assert(BN % 4 == 0 && KR % 16 == 0 && NIN <= MAXS && NW <= MAXS, "unsupported shape");
     static_assert(BYTES + 1024 <= 232448, "exceeds the 227 KB shared-memory limit");
 };
@@ -111,7 +113,7 @@ struct Args {
     float cw[MAXS];          // voltage * M_w / unit * 2^-s: FP16-part sum -> ADC input
     float slope[MAXS];       // S-curve: nonlinear / max_w
     float maxw[MAXS];
-    int factor[MAXS][MAXS];  // s_a * s_w
+    float factor[MAXS][MAXS];  // s_a * s_w (exact in FP32)
 };
 
 template <int N>
@@ -153,9 +155,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* empty = bars + STAGES;
     uint64_t* a_ready = bars + 2 * STAGES;      // [ABUF]
     uint64_t* a_free = a_ready + G::ABUF;       // [ABUF]
-    uint64_t* unit_full = a_free + G::ABUF;
-    uint64_t* unit_empty = unit_full + NJOB;
-    uint64_t* drained = unit_empty + NJOB;
+    // Accumulators of slice group g of job j: MMAs done (grp_full), read out by
+    // every epilogue warp (grp_empty).  Finer than one barrier per job so that the
+    // next read's MMAs start on a group as soon as the epilogue has loaded it.
+    uint64_t* grp_full = a_free + G::ABUF;          // [U][NG]
+    uint64_t* grp_empty = grp_full + G::U * G::NG;  // [U][NG]
+    uint64_t* drained = grp_empty + G::U * G::NG;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + G::NBAR);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -174,9 +179,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&a_ready[b], 2);
             mbar_init(&a_free[b], 1);
         }
-        for (int j = 0; j < NJOB; ++j) {
-            mbar_init(&unit_full[j], 1);
-            mbar_init(&unit_empty[j], EPI_WARPS);
+        for (int g = 0; g < G::U * G::NG; ++g) {
+            mbar_init(&grp_full[g], 1);
+            mbar_init(&grp_empty[g], EPI_WARPS);
         }
         mbar_init(drained, 1);
         *abort_flag = 0;
@@ -209,11 +214,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
                     for (int j = 0; j < NJOB; ++j)
 #pragma unroll
-                        for (int part = 0; part < PARTS; ++part)
-#pragma unroll
-                            for (int ks = 0; ks < G::KS; ++ks)
-                                tma_load_2d(stage + G::XB + ((j * PARTS + part) * G::KS + ks) * G::BT, &map_g,
-                                            i * KR + ks * 16, ((cb0 + j) * PARTS + part) * G::NPAD, &full[st]);
+                        for (int ks = 0; ks < G::KS; ++ks)
+                            tma_load_2d(stage + G::XB + (j * G::KS + ks) * G::BT, &map_g, i * KR + ks * 16,
+                                        (cb0 + j) * PARTS * G::NPAD, &full[st]);
                     issued = i + 1;
                 }
                 // Every issued load lands before the CTA may exit.
@@ -223,7 +226,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else if (warp == 1) {
             // ------------------------------------------------------------ MMA issuer
             if (lane == 0) {
-                const uint32_t idesc = idesc_f16(BM, G::NPAD);
+                // SPLIT: both halves in one MMA (N = 2 NPAD) into adjacent accumulators;
+                // otherwise one MMA per half into the same accumulator.
+                const uint32_t idesc = idesc_f16(BM, SPLIT ? PARTS * G::NPAD : G::NPAD);
                 bool ok = true;
                 for (int i = 0; i < MR && ok; ++i) {
                     const int st = i % STAGES;
@@ -234,24 +239,40 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint8_t* btiles = base + st * G::STAGE + G::XB;
                     const uint8_t* planes = a_planes + ab * G::AB;
 #pragma unroll 1
-                    for (int j = 0; j < NJOB; ++j) {
-                        if (!mbar_wait(&unit_empty[j], (i & 1) ^ 1, abort_flag, err, 44)) { ok = false; break; }
-                        tc_fence_after();
+                    for (int j = 0; j < NJOB && ok; ++j) {
+                        // Jobs rotate over the TMEM units; job sequence number u = i * NJOB + j.
+                        const int u = i * NJOB + j, unit = u % G::U;
+                        const uint32_t ph = (uint32_t)(u / G::U) & 1u;
+                        const uint32_t tbase = tmem + unit * G::UNIT;
                         // Descriptors advance by (byte offset >> 4) in their address field.
-                        const uint64_t db = desc_sw32(btiles + j * PARTS * G::KS * G::BT);
+                        const uint64_t db = desc_sw32(btiles + j * G::KS * G::BT);
 #pragma unroll 1
-                        for (int a = 0; a < NIN; ++a) {
-                            const uint64_t da = desc_sw32(planes + a * G::KS * G::AT);
+                        for (int g = 0; g < G::NG; ++g) {
+                            if (!mbar_wait(&grp_empty[unit * G::NG + g], ph ^ 1u, abort_flag, err, 44)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+#pragma unroll 1
+                            for (int a = g * G::AG; a < NIN && a < (g + 1) * G::AG; ++a) {
+                                const uint64_t da = desc_sw32(planes + a * G::KS * G::AT);
+                                if (SPLIT) {
 #pragma unroll
-                            for (int part = 0; part < PARTS; ++part)
+                                    for (int ks = 0; ks < G::KS; ++ks)
+                                        mma_f16(tbase + a * PARTS * G::NPAD, da + (uint64_t)((ks * G::AT) >> 4),
+                                                db + (uint64_t)((ks * G::BT) >> 4), idesc, ks != 0);
+                                } else {
 #pragma unroll
-                                for (int ks = 0; ks < G::KS; ++ks)
-                                    mma_f16(tmem + j * G::UNIT + ((SPLIT ? part * NIN : 0) + a) * G::NPAD,
-                                            da + (uint64_t)((ks * G::AT) >> 4),
-                                            db + (uint64_t)(((part * G::KS + ks) * G::BT) >> 4), idesc,
-                                            SPLIT ? ks != 0 : (part | ks) != 0);
+                                    for (int part = 0; part < PARTS; ++part)
+#pragma unroll
+                                        for (int ks = 0; ks < G::KS; ++ks)
+                                            mma_f16(tbase + a * G::NPAD, da + (uint64_t)((ks * G::AT) >> 4),
+                                                    db + (uint64_t)((ks * G::BT + part * G::NPAD * 32) >> 4), idesc,
+                                                    (part | ks) != 0);
+                                }
+                            }
+                            mma_commit(&grp_full[unit * G::NG + g]);
                         }
-                        mma_commit(&unit_full[j]);
                     }
                     if (!ok) break;
                     mma_commit(&a_free[ab]);
@@ -321,35 +342,63 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = 0; j < NJOB; ++j)
 #pragma unroll
             for (int e = 0; e < G::EC; ++e) acc0[j][e] = 0.0f;
+        // Per-read scales are loaded one read ahead so their latency hides behind a read's work.
+        const int colbase = c0 + hc * G::EC;
+        float xs_next = live ? __ldg(args.xscale + row * MR) : 0.0f;
+        float ws_next[NJOB][G::EC];
+#pragma unroll
+        for (int j = 0; j < NJOB; ++j)
+#pragma unroll
+            for (int e = 0; e < G::EC; ++e)
+                ws_next[j][e] = colbase + j * BN + e < args.col_end ? __ldg(args.wscale + colbase + j * BN + e) : 0.0f;
         bool ok = true;
         for (int i = 0; i < MR && ok; ++i) {
-            const float xs = live ? __ldg(args.xscale + row * MR + i) : 0.0f;
+            const float xs = xs_next;
+            float ws_now[NJOB][G::EC];
+#pragma unroll
+            for (int j = 0; j < NJOB; ++j)
+#pragma unroll
+                for (int e = 0; e < G::EC; ++e) ws_now[j][e] = ws_next[j][e];
+            if (i + 1 < MR) {
+                xs_next = live ? __ldg(args.xscale + row * MR + i + 1) : 0.0f;
+#pragma unroll
+                for (int j = 0; j < NJOB; ++j)
+#pragma unroll
+                    for (int e = 0; e < G::EC; ++e) {
+                        const int col = colbase + j * BN + e;
+                        ws_next[j][e] = col < args.col_end ? __ldg(args.wscale + (long long)(i + 1) * args.ldw + col) : 0.0f;
+                    }
+            }
 #pragma unroll 1
-            for (int j = 0; j < NJOB; ++j) {
-                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&unit_full[j], i & 1, abort_flag, err, 47));
-                if (!ok) break;
-                tc_fence_after();
-                // Input slices in groups of at most 32 loaded columns; the unit is released
-                // as soon as the last group is in registers.
-                int total[G::EC];
+            for (int j = 0; j < NJOB && ok; ++j) {
+                // Input slices in groups of at most 32 loaded columns; each group's
+                // accumulators are released as soon as they are in registers.  Counts and totals stay in FP32
+                // (integers below 2^24, exact): rint(z) = (z + 1.5 * 2^23) - 1.5 * 2^23 for
+                // 0 <= z < 2^22, clamped in the shifted domain (the bounds are integers).
+                float total[G::EC];
 #pragma unroll
-                for (int e = 0; e < G::EC; ++e) total[e] = 0;
+                for (int e = 0; e < G::EC; ++e) total[e] = 0.0f;
 #pragma unroll
+                const int u = i * NJOB + j, unit = u % G::U;
+                const uint32_t ph = (uint32_t)(u / G::U) & 1u;
                 for (int a0 = 0; a0 < NIN; a0 += G::AG) {
+                    const int g = a0 / G::AG;
+                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&grp_full[unit * G::NG + g], ph, abort_flag, err, 47));
+                    if (!ok) break;
+                    tc_fence_after();
+                    // Accumulator acc of input slice a: column (a * ACCS + acc) * NPAD of the unit.
                     uint32_t v[G::ACCS][G::AG][G::VALS];
 #pragma unroll
                     for (int acc = 0; acc < G::ACCS; ++acc)
 #pragma unroll
                         for (int a = 0; a < G::AG; ++a)
                             if (a0 + a < NIN)
-                                tmem_load_cols<G::VALS>(lane_base + j * G::UNIT + (acc * NIN + a0 + a) * G::NPAD,
-                                                        v[acc][a]);
+                                tmem_load_cols<G::VALS>(
+                                    lane_base + unit * G::UNIT + ((a0 + a) * G::ACCS + acc) * G::NPAD, v[acc][a]);
                     tmem_loaded<G::ACCS * G::AG * G::VALS>(&v[0][0][0]);
-                    if (a0 + G::AG >= NIN) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&unit_empty[j]);
-                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&grp_empty[unit * G::NG + g]);
 #pragma unroll
                     for (int a = 0; a < G::AG; ++a) {
                         if (a0 + a >= NIN) break;
@@ -361,20 +410,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 const float x = SPLIT ? __fmaf_rn(__uint_as_float(v[0][a][e * NW + w]), 2048.0f,
                                                                   __uint_as_float(v[SPLIT ? 1 : 0][a][e * NW + w]))
                                                       : __uint_as_float(v[0][a][e * NW + w]);
+                                constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
                                 float z = __fmul_rn(x, args.cw[w]);
                                 if (NONLINEAR) z = __fdiv_rn(z, __fadd_rn(1.0f, fabsf(__fmul_rn(args.slope[w], z))));
-                                z = fminf(fmaxf(z, 0.0f), args.maxw[w]);
-                                total[e] += __float2int_rn(z) * args.factor[a0 + a][w];
+                                float q = __fadd_rn(z, kMagic);
+                                q = fminf(fmaxf(q, kMagic), __fadd_rn(args.maxw[w], kMagic));
+                                total[e] = __fmaf_rn(__fsub_rn(q, kMagic), args.factor[a0 + a][w], total[e]);
                             }
                     }
                 }
-                const int colj = c0 + j * BN + hc * G::EC;
 #pragma unroll
-                for (int e = 0; e < G::EC; ++e) {
-                    const int col = colj + e;
-                    const float ws = col < args.col_end ? __ldg(args.wscale + (long long)i * args.ldw + col) : 0.0f;
-                    acc0[j][e] = __fadd_rn(acc0[j][e], __fmul_rn(__fmul_rn(__int2float_rn(total[e]), xs), ws));
-                }
+                for (int e = 0; e < G::EC; ++e)
+                    acc0[j][e] = __fadd_rn(acc0[j][e], __fmul_rn(__fmul_rn(total[e], xs), ws_now[j][e]));
             }
             if (!ok) break;
             // Block boundary of the 16-read cascade: level 1 += level 0 (MR <= 256 keeps two levels).
@@ -467,7 +514,7 @@ __global__ void restore_split_kernel(Layout L, Physics P, const uint8_t* packed,
 struct Shape {
     int nin, nw, bn, njob, split;
 };
-constexpr Shape kShapes[] = {{5, 5, 8, 1, 1}, {3, 3, 16, 1, 1}, {8, 8, 4, 2, 0}, {4, 4, 8, 2, 1}};
+constexpr Shape kShapes[] = {{5, 5, 8, 4, 1}, {3, 3, 16, 2, 1}, {8, 8, 4, 4, 0}, {4, 4, 8, 4, 1}};
 
 bool shape_of(const mf_config& c, Shape& s) {
     for (const Shape& k : kShapes)
@@ -503,9 +550,10 @@ bool tc_physical_eligible(const mf_config& c, int32_t m) {
     for (int i = 0; i < c.n_in; ++i)
         if (c.in_mask[i] > 7) return false;
     for (int i = 0; i < c.n_w; ++i)
-        if (c.adc_max[i] < 1 || c.adc_max[i] > (1 << 24)) return false;
+        if (c.adc_max[i] < 1 || c.adc_max[i] >= (1 << 22)) return false;
     const long long MR = (long long)m * c.reads;
-    return MR <= 256 && c.high > 0 && c.drift > 0 && reconstruction_bound(c) < 2147483647.0;
+    // Totals are accumulated exactly in FP32 and adc_max < 2^22 keeps the rounding trick exact.
+    return MR <= 256 && c.high > 0 && c.drift > 0 && reconstruction_bound(c) < 16777216.0;
 }
 
 int tc_physical_threads() { return tcp::THREADS; }
@@ -590,7 +638,7 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     mf_status r = tc_make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n,
                               (uint64_t)K, (uint32_t)c.read_rows, tcp::BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!r) r = tc_make_map(&mg, gs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K,
-                            (uint64_t)blocks * tcp::PARTS * npad, (uint64_t)K, 16, (uint32_t)npad,
+                            (uint64_t)blocks * tcp::PARTS * npad, (uint64_t)K, 16, (uint32_t)(tcp::PARTS * npad),
                             CU_TENSOR_MAP_SWIZZLE_32B);
     if (r) return r;
     tcp::Args args{};
@@ -621,14 +669,14 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
         args.cw[w] = (float)(c.voltage * c.w_mask[w] * inv_unit / scale);
         args.slope[w] = (float)(c.nonlinear / c.adc_max[w]);
         args.maxw[w] = (float)c.adc_max[w];
-        for (int i = 0; i < c.n_in; ++i) args.factor[i][w] = (int)(c.in_factor[i] * c.w_factor[w]);
+        for (int i = 0; i < c.n_in; ++i) args.factor[i][w] = (float)(c.in_factor[i] * c.w_factor[w]);
     }
     const int bc = shape.bn * shape.njob;
     dim3 grid((unsigned)((a.n + tcp::BM - 1) / tcp::BM), (unsigned)((cols + bc - 1) / bc));
-    if (shape.nin == 5) return dispatch_tcp<5, 5, 8, 1, true>(c, mx, mg, args, grid, st);
-    if (shape.nin == 3) return dispatch_tcp<3, 3, 16, 1, true>(c, mx, mg, args, grid, st);
-    if (shape.nin == 8) return dispatch_tcp<8, 8, 4, 2, false>(c, mx, mg, args, grid, st);
-    return dispatch_tcp<4, 4, 8, 2, true>(c, mx, mg, args, grid, st);
+    if (shape.nin == 5) return dispatch_tcp<5, 5, 8, 4, true>(c, mx, mg, args, grid, st);
+    if (shape.nin == 3) return dispatch_tcp<3, 3, 16, 2, true>(c, mx, mg, args, grid, st);
+    if (shape.nin == 8) return dispatch_tcp<8, 8, 4, 4, false>(c, mx, mg, args, grid, st);
+    return dispatch_tcp<4, 4, 8, 4, true>(c, mx, mg, args, grid, st);
 }
 
 }  // namespace mf
