@@ -25,12 +25,13 @@
 // 64-row reads, at most 256 reads per output.  Everything else runs on the SIMT
 // kernels in generic.cu.
 //
-// Per CTA: 128 vectors x BC = NJOB * BN output columns.  Per read:
-//   warp 0      TMA: the read's activation codes [128 x KR] and, for every job
-//               and part, the [NPAD x 16] FP16 tiles of G' per 16-row MMA step
-//   warp 1      TMEM owner and MMA issuer: per job and input slice a, one FP32
-//               accumulator of NPAD columns (BN output columns x NW weight
-//               slices, output-column major) fed by 2 * KR / 16 MMAs
+// Per CTA: 128 vectors x BC = NJB * BN output columns.  Per read:
+//   warp 0      TMA: the read's activation codes [128 x KR] and, for every job,
+//               the FP16 tile of G' (both halves) per 16-row MMA step
+//   warp 1      TMEM owner and MMA issuer: per job and input slice a, FP32
+//               accumulators of NP = BN x NW columns (output-column major) per
+//               half; jobs alternate between TMEM units so that the MMAs of one
+//               job run while the epilogue drains another
 //   warps 2-3   transform: FP16 digit planes of every input slice (byte lookup)
 //   warps 4-19  epilogue: ADC of every pair, signed reconstruction,
 //               fl(fl(T * xs) * ws) and PyTorch's CPU cascade over the reads
@@ -64,22 +65,25 @@ static_assert(128 * REG_LOW + 32 * EPI_WARPS * REG_HIGH <= THREADS * LAUNCH_REGS
               "register split exceeds the launch pool");
 constexpr int MAXS = 8;          // slices per operand in the tables below
 
-// Shared-memory and TMEM geometry of one instantiation.
-template <int NIN, int NW, int BN, int NJOB, int KR, bool SPLIT>
+// Shared-memory and TMEM geometry of one instantiation.  A job is one input
+// slice a of one BN-column block: one accumulator set of NT columns, fed by
+// KS (split halves stacked along N) or 2 KS MMAs; jobs rotate over U units.
+template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT>
 struct Geo {
     static constexpr int KS = KR / 16;                     // MMA K steps per read
-    static constexpr int NPAD = (NW * BN + 15) / 16 * 16;  // MMA N: B rows of a job
+    static constexpr int EC = BN / 4;                      // columns per epilogue thread per block
+    static constexpr int NP = NW * BN;                     // accumulator columns of one half (jj * NW + w)
+    static constexpr int NT = SPLIT ? (PARTS * NP + 15) / 16 * 16 : (NP + 15) / 16 * 16;   // MMA N
+    static constexpr int PSTRIDE = SPLIT ? NP : NT;        // B rows between the halves of a tile
+    static constexpr int BROWS = ((PARTS * PSTRIDE > NT ? PARTS * PSTRIDE : NT) + 7) / 8 * 8;   // B tile rows
     static constexpr int ACCS = SPLIT ? PARTS : 1;         // accumulators per slice pair
-    static constexpr int UNIT = ACCS * NIN * NPAD;         // TMEM columns of a job
-    static constexpr int U = 512 / UNIT < NJOB ? 512 / UNIT : NJOB;   // TMEM units the jobs rotate over
-    static constexpr int BC = NJOB * BN;                   // output columns per CTA
-    static constexpr int EC = BN / 4;                      // columns per epilogue thread per job
-    static constexpr int VALS = NW * EC;                   // TMEM columns a thread reads per input slice
-    static constexpr int AG = 32 / (ACCS * VALS) < 1 ? 1 : (32 / (ACCS * VALS) < NIN ? 32 / (ACCS * VALS) : NIN);
-                                                           // input slices per TMEM load group
+    static constexpr int UNIT = NT;                        // TMEM columns of a job
+    static constexpr int U = 512 / UNIT < NJB * NIN ? 512 / UNIT : NJB * NIN;   // TMEM units
+    static constexpr int BC = NJB * BN;                    // output columns per CTA
+    static constexpr int VALS = NW * EC;                   // TMEM columns a thread reads per accumulator
     static constexpr int XB = BM * KR;                     // code tile
-    static constexpr int BT = PARTS * NPAD * 32;           // one [PARTS*NPAD x 16] FP16 tile (both halves)
-    static constexpr int BB = NJOB * KS * BT;
+    static constexpr int BT = BROWS * 32;                  // one [BROWS x 16] FP16 tile (both halves)
+    static constexpr int BB = NJB * KS * BT;
     static constexpr int STAGE = (XB + BB + 1023) / 1024 * 1024;
     static constexpr int AT = BM * 32;                     // one [128 x 16] FP16 tile
     static constexpr int AB = NIN * KS * AT;               // one set of digit planes
@@ -88,12 +92,12 @@ struct Geo {
     static constexpr int OFF_A = STAGES * STAGE;
     static constexpr int OFF_ACC1 = OFF_A + ABUF * AB;
     static constexpr int OFF_BAR = OFF_ACC1 + BC * BM * 4;
-    static constexpr int NG = (NIN + AG - 1) / AG;          // slice groups per unit (own full/empty barriers)
-    static constexpr int NBAR = 2 * STAGES + 2 * ABUF + 2 * U * NG + 1;
+    static constexpr int NBAR = 2 * STAGES + 2 * ABUF + 2 * U + 1;
     static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16;
     static constexpr int TMEM_COLS = U * UNIT <= 256 ? 256 : 512;
-    static_assert(U >= 1 && U * UNIT <= 512, "accumulators exceed TMEM");
+    static_assert(U >= 1 && U * UNIT <= 512 && NT <= 256, "accumulators exceed TMEM or the MMA's N");
     static_assert(BN % 4 == 0 && KR % 16 == 0 && NIN <= MAXS && NW <= MAXS, "unsupported shape");
+    static_assert(VALS % 2 == 0, "TMEM loads start on even columns");
     static_assert(BYTES + 1024 <= 232448, "exceeds the 227 KB shared-memory limit");
 };
 
@@ -112,8 +116,9 @@ struct Args {
     uint32_t lut_lo, lut_hi; // FP16 high bytes of the digits 0..7 (low bytes are 0)
     float cw[MAXS];          // voltage * M_w / unit * 2^-s: FP16-part sum -> ADC input
     float slope[MAXS];       // S-curve: nonlinear / max_w
-    float maxw[MAXS];
-    float factor[MAXS][MAXS];  // s_a * s_w (exact in FP32)
+    float qmax[MAXS];        // max_w + 1.5 * 2^23: the ADC's upper clamp in the shifted domain
+    int factor[MAXS][MAXS];  // s_a * s_w
+    int offset;              // -0x4B400000 * sum of factor over the slice pairs (mod 2^32)
 };
 
 template <int N>
@@ -141,26 +146,23 @@ __device__ __forceinline__ void tmem_loaded(uint32_t* v) {
     for (int k = 0; k < N; ++k) asm volatile("" : "+r"(v[k]));
 }
 
-template <int NIN, int NW, int BN, int NJOB, int KR, bool SPLIT, bool NONLINEAR>
+template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, bool NONLINEAR>
 __global__ void __launch_bounds__(THREADS, 1)
     tc_physical_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_g,
                        const __grid_constant__ Args args) {
-    using G = Geo<NIN, NW, BN, NJOB, KR, SPLIT>;
+    using G = Geo<NIN, NW, BN, NJB, KR, SPLIT>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* a_planes = base + G::OFF_A;
     float* acc1 = reinterpret_cast<float*>(base + G::OFF_ACC1);             // [BC][BM]
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + G::OFF_BAR);
-    uint64_t* full = bars;
-    uint64_t* empty = bars + STAGES;
-    uint64_t* a_ready = bars + 2 * STAGES;      // [ABUF]
-    uint64_t* a_free = a_ready + G::ABUF;       // [ABUF]
-    // Accumulators of slice group g of job j: MMAs done (grp_full), read out by
-    // every epilogue warp (grp_empty).  Finer than one barrier per job so that the
-    // next read's MMAs start on a group as soon as the epilogue has loaded it.
-    uint64_t* grp_full = a_free + G::ABUF;          // [U][NG]
-    uint64_t* grp_empty = grp_full + G::U * G::NG;  // [U][NG]
-    uint64_t* drained = grp_empty + G::U * G::NG;
+    uint64_t* full = bars;                      // [STAGES] codes and G' tiles landed
+    uint64_t* empty = bars + STAGES;            // [STAGES] the read's MMAs are done with them
+    uint64_t* a_ready = bars + 2 * STAGES;      // [ABUF] digit planes written
+    uint64_t* a_free = a_ready + G::ABUF;       // [ABUF] the read's MMAs are done with them
+    uint64_t* unit_full = a_free + G::ABUF;     // [U] a job's accumulators complete
+    uint64_t* unit_empty = unit_full + G::U;    // [U] ... and read out by every epilogue warp
+    uint64_t* drained = unit_empty + G::U;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + G::NBAR);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -179,9 +181,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&a_ready[b], 2);
             mbar_init(&a_free[b], 1);
         }
-        for (int g = 0; g < G::U * G::NG; ++g) {
-            mbar_init(&grp_full[g], 1);
-            mbar_init(&grp_empty[g], EPI_WARPS);
+        for (int u = 0; u < G::U; ++u) {
+            mbar_init(&unit_full[u], 1);
+            mbar_init(&unit_empty[u], EPI_WARPS);
         }
         mbar_init(drained, 1);
         *abort_flag = 0;
@@ -203,7 +205,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (warp == 0) {
             // ------------------------------------------------------------ producer
             if (lane == 0) {
-                const int cb0 = blockIdx.y * NJOB;        // first BN-column block of this CTA
+                const int cb0 = blockIdx.y * NJB;          // first BN-column block of this CTA
                 int issued = 0;
                 for (int i = 0; i < MR; ++i) {
                     const int st = i % STAGES;
@@ -212,11 +214,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mbar_expect_tx(&full[st], G::XB + G::BB);
                     tma_load_2d(stage, &map_x, i * KR, (int)n0, &full[st]);
 #pragma unroll 1
-                    for (int j = 0; j < NJOB; ++j)
+                    for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
                         for (int ks = 0; ks < G::KS; ++ks)
-                            tma_load_2d(stage + G::XB + (j * G::KS + ks) * G::BT, &map_g, i * KR + ks * 16,
-                                        (cb0 + j) * PARTS * G::NPAD, &full[st]);
+                            tma_load_2d(stage + G::XB + (cb * G::KS + ks) * G::BT, &map_g, i * KR + ks * 16,
+                                        (cb0 + cb) * G::BROWS, &full[st]);
                     issued = i + 1;
                 }
                 // Every issued load lands before the CTA may exit.
@@ -226,10 +228,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else if (warp == 1) {
             // ------------------------------------------------------------ MMA issuer
             if (lane == 0) {
-                // SPLIT: both halves in one MMA (N = 2 NPAD) into adjacent accumulators;
+                // SPLIT: both halves in one MMA (N = NT) into adjacent accumulators;
                 // otherwise one MMA per half into the same accumulator.
-                const uint32_t idesc = idesc_f16(BM, SPLIT ? PARTS * G::NPAD : G::NPAD);
+                const uint32_t idesc = idesc_f16(BM, G::NT);
                 bool ok = true;
+                int job = 0;                               // job sequence number: unit job % U
                 for (int i = 0; i < MR && ok; ++i) {
                     const int st = i % STAGES;
                     if (!mbar_wait(&full[st], (i / STAGES) & 1, abort_flag, err, 42)) break;
@@ -239,39 +242,28 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint8_t* btiles = base + st * G::STAGE + G::XB;
                     const uint8_t* planes = a_planes + ab * G::AB;
 #pragma unroll 1
-                    for (int j = 0; j < NJOB && ok; ++j) {
-                        // Jobs rotate over the TMEM units; job sequence number u = i * NJOB + j.
-                        const int u = i * NJOB + j, unit = u % G::U;
-                        const uint32_t ph = (uint32_t)(u / G::U) & 1u;
-                        const uint32_t tbase = tmem + unit * G::UNIT;
+                    for (int cb = 0; cb < NJB && ok; ++cb) {
                         // Descriptors advance by (byte offset >> 4) in their address field.
-                        const uint64_t db = desc_sw32(btiles + j * G::KS * G::BT);
+                        const uint64_t db = desc_sw32(btiles + cb * G::KS * G::BT);
 #pragma unroll 1
-                        for (int g = 0; g < G::NG; ++g) {
-                            if (!mbar_wait(&grp_empty[unit * G::NG + g], ph ^ 1u, abort_flag, err, 44)) {
+                        for (int a = 0; a < NIN; ++a, ++job) {
+                            const int unit = job % G::U;
+                            if (!mbar_wait(&unit_empty[unit], (uint32_t)((job / G::U) & 1) ^ 1u, abort_flag, err,
+                                           44)) {
                                 ok = false;
                                 break;
                             }
                             tc_fence_after();
-#pragma unroll 1
-                            for (int a = g * G::AG; a < NIN && a < (g + 1) * G::AG; ++a) {
-                                const uint64_t da = desc_sw32(planes + a * G::KS * G::AT);
-                                if (SPLIT) {
+                            const uint32_t d = tmem + unit * G::UNIT;
+                            const uint64_t da = desc_sw32(planes + a * G::KS * G::AT);
 #pragma unroll
-                                    for (int ks = 0; ks < G::KS; ++ks)
-                                        mma_f16(tbase + a * PARTS * G::NPAD, da + (uint64_t)((ks * G::AT) >> 4),
-                                                db + (uint64_t)((ks * G::BT) >> 4), idesc, ks != 0);
-                                } else {
+                            for (int part = 0; part < (SPLIT ? 1 : PARTS); ++part)
 #pragma unroll
-                                    for (int part = 0; part < PARTS; ++part)
-#pragma unroll
-                                        for (int ks = 0; ks < G::KS; ++ks)
-                                            mma_f16(tbase + a * G::NPAD, da + (uint64_t)((ks * G::AT) >> 4),
-                                                    db + (uint64_t)((ks * G::BT + part * G::NPAD * 32) >> 4), idesc,
-                                                    (part | ks) != 0);
-                                }
-                            }
-                            mma_commit(&grp_full[unit * G::NG + g]);
+                                for (int ks = 0; ks < G::KS; ++ks)
+                                    mma_f16(d, da + (uint64_t)((ks * G::AT) >> 4),
+                                            db + (uint64_t)((ks * G::BT + part * G::PSTRIDE * 32) >> 4), idesc,
+                                            (part | ks) != 0);
+                            mma_commit(&unit_full[unit]);
                         }
                     }
                     if (!ok) break;
@@ -329,125 +321,125 @@ __global__ void __launch_bounds__(THREADS, 1)
         set_maxnreg_inc<REG_HIGH>();
         // ---------------------------------------------------------------- epilogue
         // Warp w reads TMEM lane quadrant w & 3 (rows) and the EC-column slice hc of
-        // every job; within a job's accumulator of input slice a, output column jj
-        // and weight slice w sit at column a * NPAD + jj * NW + w.
+        // every block; in a job's accumulators (input slice a of one block), output
+        // column jj and weight slice w of half acc sit at column acc * NP + jj * NW + w.
         const int quad = warp & 3;
         const int hc = (warp - 4) >> 2;
         const int r = quad * 32 + lane;
         const long long row = n0 + r;
         const bool live = row < args.n;
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + hc * G::VALS;
-        float acc0[NJOB][G::EC];
+        float acc0[NJB][G::EC];
 #pragma unroll
-        for (int j = 0; j < NJOB; ++j)
+        for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
-            for (int e = 0; e < G::EC; ++e) acc0[j][e] = 0.0f;
+            for (int e = 0; e < G::EC; ++e) acc0[cb][e] = 0.0f;
         // Per-read scales are loaded one read ahead so their latency hides behind a read's work.
         const int colbase = c0 + hc * G::EC;
         float xs_next = live ? __ldg(args.xscale + row * MR) : 0.0f;
-        float ws_next[NJOB][G::EC];
+        float ws_next[NJB][G::EC];
 #pragma unroll
-        for (int j = 0; j < NJOB; ++j)
+        for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
             for (int e = 0; e < G::EC; ++e)
-                ws_next[j][e] = colbase + j * BN + e < args.col_end ? __ldg(args.wscale + colbase + j * BN + e) : 0.0f;
+                ws_next[cb][e] = colbase + cb * BN + e < args.col_end ? __ldg(args.wscale + colbase + cb * BN + e)
+                                                                      : 0.0f;
         bool ok = true;
+        int job = 0;
         for (int i = 0; i < MR && ok; ++i) {
             const float xs = xs_next;
-            float ws_now[NJOB][G::EC];
+            float ws_now[NJB][G::EC];
 #pragma unroll
-            for (int j = 0; j < NJOB; ++j)
+            for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
-                for (int e = 0; e < G::EC; ++e) ws_now[j][e] = ws_next[j][e];
+                for (int e = 0; e < G::EC; ++e) ws_now[cb][e] = ws_next[cb][e];
             if (i + 1 < MR) {
                 xs_next = live ? __ldg(args.xscale + row * MR + i + 1) : 0.0f;
 #pragma unroll
-                for (int j = 0; j < NJOB; ++j)
+                for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
                     for (int e = 0; e < G::EC; ++e) {
-                        const int col = colbase + j * BN + e;
-                        ws_next[j][e] = col < args.col_end ? __ldg(args.wscale + (long long)(i + 1) * args.ldw + col) : 0.0f;
+                        const int col = colbase + cb * BN + e;
+                        ws_next[cb][e] =
+                            col < args.col_end ? __ldg(args.wscale + (long long)(i + 1) * args.ldw + col) : 0.0f;
                     }
             }
 #pragma unroll 1
-            for (int j = 0; j < NJOB && ok; ++j) {
-                // Input slices in groups of at most 32 loaded columns; each group's
-                // accumulators are released as soon as they are in registers.  Counts and totals stay in FP32
-                // (integers below 2^24, exact): rint(z) = (z + 1.5 * 2^23) - 1.5 * 2^23 for
-                // 0 <= z < 2^22, clamped in the shifted domain (the bounds are integers).
-                float total[G::EC];
+            for (int cb = 0; cb < NJB && ok; ++cb) {
+                // ADC: q = z + 1.5 * 2^23 rounds z half to even into the low mantissa bits
+                // (0 <= z < 2^22), clamped in that shifted domain (the bounds are integers);
+                // the bit pattern of q is 0x4B400000 + count, so the total accumulates
+                // bits * factor in wrapping int32 and the constant part is removed once.
+                int total[G::EC];
 #pragma unroll
-                for (int e = 0; e < G::EC; ++e) total[e] = 0.0f;
-#pragma unroll
-                const int u = i * NJOB + j, unit = u % G::U;
-                const uint32_t ph = (uint32_t)(u / G::U) & 1u;
-                for (int a0 = 0; a0 < NIN; a0 += G::AG) {
-                    const int g = a0 / G::AG;
-                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&grp_full[unit * G::NG + g], ph, abort_flag, err, 47));
+                for (int e = 0; e < G::EC; ++e) total[e] = args.offset;
+#pragma unroll 1
+                for (int a = 0; a < NIN; ++a, ++job) {
+                    const int unit = job % G::U;
+                    ok = __all_sync(0xFFFFFFFFu,
+                                    mbar_wait(&unit_full[unit], (uint32_t)(job / G::U) & 1u, abort_flag, err, 47));
                     if (!ok) break;
                     tc_fence_after();
-                    // Accumulator acc of input slice a: column (a * ACCS + acc) * NPAD of the unit.
-                    uint32_t v[G::ACCS][G::AG][G::VALS];
+                    uint32_t v[G::ACCS][G::VALS];
 #pragma unroll
                     for (int acc = 0; acc < G::ACCS; ++acc)
-#pragma unroll
-                        for (int a = 0; a < G::AG; ++a)
-                            if (a0 + a < NIN)
-                                tmem_load_cols<G::VALS>(
-                                    lane_base + unit * G::UNIT + ((a0 + a) * G::ACCS + acc) * G::NPAD, v[acc][a]);
-                    tmem_loaded<G::ACCS * G::AG * G::VALS>(&v[0][0][0]);
+                        tmem_load_cols<G::VALS>(lane_base + unit * G::UNIT + acc * G::NP, v[acc]);
+                    tmem_loaded<G::ACCS * G::VALS>(&v[0][0]);
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&grp_empty[unit * G::NG + g]);
+                    if (lane == 0) mbar_arrive(&unit_empty[unit]);
 #pragma unroll
-                    for (int a = 0; a < G::AG; ++a) {
-                        if (a0 + a >= NIN) break;
+                    for (int e = 0; e < G::EC; ++e)
 #pragma unroll
-                        for (int e = 0; e < G::EC; ++e)
-#pragma unroll
-                            for (int w = 0; w < NW; ++w) {
-                                // SPLIT: 2048 S_H + S_L, both exact integers, rounded once.
-                                const float x = SPLIT ? __fmaf_rn(__uint_as_float(v[0][a][e * NW + w]), 2048.0f,
-                                                                  __uint_as_float(v[SPLIT ? 1 : 0][a][e * NW + w]))
-                                                      : __uint_as_float(v[0][a][e * NW + w]);
-                                constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+                        for (int w = 0; w < NW; ++w) {
+                            // SPLIT: 2048 S_H + S_L, both exact integers, rounded once.
+                            const float x = SPLIT ? __fmaf_rn(__uint_as_float(v[0][e * NW + w]), 2048.0f,
+                                                              __uint_as_float(v[SPLIT ? 1 : 0][e * NW + w]))
+                                                  : __uint_as_float(v[0][e * NW + w]);
+                            constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+                            float q;
+                            if (NONLINEAR) {
                                 float z = __fmul_rn(x, args.cw[w]);
-                                if (NONLINEAR) z = __fdiv_rn(z, __fadd_rn(1.0f, fabsf(__fmul_rn(args.slope[w], z))));
-                                float q = __fadd_rn(z, kMagic);
-                                q = fminf(fmaxf(q, kMagic), __fadd_rn(args.maxw[w], kMagic));
-                                total[e] = __fmaf_rn(__fsub_rn(q, kMagic), args.factor[a0 + a][w], total[e]);
+                                z = __fdiv_rn(z, __fadd_rn(1.0f, fabsf(__fmul_rn(args.slope[w], z))));
+                                q = __fadd_rn(z, kMagic);
+                            } else {
+                                q = __fmaf_rn(x, args.cw[w], kMagic);
                             }
-                    }
+                            q = fminf(fmaxf(q, kMagic), args.qmax[w]);
+                            total[e] += __float_as_int(q) * args.factor[a][w];
+                        }
                 }
+                if (!ok) break;
 #pragma unroll
                 for (int e = 0; e < G::EC; ++e)
-                    acc0[j][e] = __fadd_rn(acc0[j][e], __fmul_rn(__fmul_rn(total[e], xs), ws_now[j][e]));
+                    acc0[cb][e] =
+                        __fadd_rn(acc0[cb][e], __fmul_rn(__fmul_rn(__int2float_rn(total[e]), xs), ws_now[cb][e]));
             }
             if (!ok) break;
             // Block boundary of the 16-read cascade: level 1 += level 0 (MR <= 256 keeps two levels).
             const int done = i + 1;
             if (done <= args.full && (done & 15) == 0) {
 #pragma unroll
-                for (int j = 0; j < NJOB; ++j)
+                for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
                     for (int e = 0; e < G::EC; ++e) {
-                        float* slot = acc1 + (j * BN + hc * G::EC + e) * BM + r;
-                        *slot = __fadd_rn(*slot, acc0[j][e]);
-                        acc0[j][e] = 0.0f;
+                        float* slot = acc1 + (cb * BN + hc * G::EC + e) * BM + r;
+                        *slot = __fadd_rn(*slot, acc0[cb][e]);
+                        acc0[cb][e] = 0.0f;
                     }
             }
         }
         if (ok && live) {
 #pragma unroll
-            for (int j = 0; j < NJOB; ++j)
+            for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
                 for (int e = 0; e < G::EC; ++e) {
-                    const int cl = j * BN + hc * G::EC + e;
+                    const int cl = cb * BN + hc * G::EC + e;
                     const int col = c0 + cl;
                     if (col >= args.col_end || col >= args.out_features) continue;
                     // acc0 + acc1 + acc2 + acc3 (upper levels zero), then the reference's
                     // store into a zero-filled output.
-                    float value = __fadd_rn(acc0[j][e], acc1[cl * BM + r]);
+                    float value = __fadd_rn(acc0[cb][e], acc1[cl * BM + r]);
                     value = __fadd_rn(value, 0.0f);
                     value = __fadd_rn(value, 0.0f);
                     value = __fadd_rn(0.0f, value);
@@ -465,27 +457,31 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // G' = G - LOW of the weight slices as the B operand: rows
-// ((block * PARTS + part) * NPAD + jj * NW + w) for output column
-// col_begin + block * BN + jj and weight slice w (zero rows pad NPAD), K
+// (block * brows + part * pstride + jj * nwp + w) for output column
+// col_begin + block * BN + jj and weight slice w (other rows zero), K
 // contiguous.  fixed: X = rint(G' * scale) (|X| < 2^22) as the FP16 integers
 // H = rint(X / 2048) and L = X - 2048 H; otherwise x = G' * scale (< 2^14) as the
 // FP16 parts hi = fp16(x), lo = fp16(x - hi).  The conductance is the SIMT
 // path's (restored_conductance_f32).
 __global__ void restore_split_kernel(Layout L, Physics P, const uint8_t* packed, int p, int col_begin, int blocks,
-                                     int bn, int npad, long long kpad, uint32_t seed, uint64_t event, float scale,
+                                     int bn, int nwp, int brows, int pstride, long long kpad, uint32_t seed,
+                                     uint64_t event,
+                                     float scale,
                                      int fixed, __half* gs) {
-    const long long total = (long long)blocks * npad * kpad;
+    const int np = nwp * bn;
+    const long long total = (long long)blocks * brows * kpad;
     const uint64_t read_seed = event_seed(seed, event);
     const float low = (float)P.low;
     for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
          idx += (long long)gridDim.x * blockDim.x) {
         const long long k = idx % kpad;
         const long long rest = idx / kpad;
-        const int prow = (int)(rest % npad);
-        const int block = (int)(rest / npad);
+        const int brow = (int)(rest % brows);
+        const int block = (int)(rest / brows);
+        const int part = brow / pstride, prow = brow % pstride;
         __half hi = __float2half_rn(0.0f), lo = hi;
-        if (prow < L.n_w * bn) {
-            const int jj = prow / L.n_w, w = prow % L.n_w;
+        if (part < PARTS && prow < np && prow % nwp < L.n_w) {
+            const int jj = prow / nwp, w = prow % nwp;
             const long long o = (long long)col_begin + (long long)block * bn + jj;
             const long long tile = o / L.C, c = o % L.C;
             const long long arr = k / L.R, r = k % L.R;
@@ -504,17 +500,17 @@ __global__ void restore_split_kernel(Layout L, Physics P, const uint8_t* packed,
                 lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
             }
         }
-        gs[((long long)(block * PARTS + 0) * npad + prow) * kpad + k] = hi;
-        gs[((long long)(block * PARTS + 1) * npad + prow) * kpad + k] = lo;
+        gs[((long long)block * brows + brow) * kpad + k] = part == 0 ? hi : lo;
     }
 }
 
-// Instantiations: (input slices, weight slices) -> columns per job, jobs per CTA,
-// split accumulators.
+// Instantiations: (input slices, weight slices) -> columns per block, blocks per
+// CTA, split accumulators.  Each MMA is as wide as TMEM and the 256-column limit of
+// N allow (the tensor core's cost here is per instruction rather than per column).
 struct Shape {
-    int nin, nw, bn, njob, split;
+    int nin, nw, bn, njb, split;
 };
-constexpr Shape kShapes[] = {{5, 5, 8, 4, 1}, {3, 3, 16, 2, 1}, {8, 8, 4, 4, 0}, {4, 4, 8, 4, 1}};
+constexpr Shape kShapes[] = {{5, 5, 16, 2, 1}, {3, 3, 32, 1, 1}, {8, 8, 16, 1, 0}, {4, 4, 16, 2, 1}};
 
 bool shape_of(const mf_config& c, Shape& s) {
     for (const Shape& k : kShapes)
@@ -525,7 +521,15 @@ bool shape_of(const mf_config& c, Shape& s) {
     return false;
 }
 
-int npad_of(const Shape& s) { return (s.nw * s.bn + 15) / 16 * 16; }
+// B tile rows per column block (rounded to 8) and the row offset of the second half,
+// as Geo computes them.
+void rows_of(const Shape& s, int& brows8, int& pstride) {
+    const int np = s.nw * s.bn;
+    const int nt = s.split ? (PARTS * np + 15) / 16 * 16 : (np + 15) / 16 * 16;
+    pstride = s.split ? np : nt;
+    const int brows = PARTS * pstride > nt ? PARTS * pstride : nt;
+    brows8 = (brows + 7) / 8 * 8;
+}
 
 // Scale 2^s of G': the largest |G'| (nominal level, drift, an 8-sigma write and
 // read variation) stays below 2^22 (fixed-point halves) or 2^14 (floating parts).
@@ -562,15 +566,17 @@ size_t tc_physical_workspace_bytes(const mf_config& c, int32_t m, int32_t tiles)
     tcp::Shape s;
     if (!tcp::shape_of(c, s)) return 256;
     const long long blocks = (long long)tiles * c.cols / s.bn;
-    return (size_t)blocks * tcp::PARTS * tcp::npad_of(s) * (size_t)m * c.rows * sizeof(__half) + 256;
+    int brows = 0, pstride = 0;
+    tcp::rows_of(s, brows, pstride);
+    return (size_t)blocks * brows * (size_t)m * c.rows * sizeof(__half) + 256;
 }
 
-template <int NIN, int NW, int BN, int NJOB, bool SPLIT, int KR, bool NL>
+template <int NIN, int NW, int BN, int NJB, bool SPLIT, int KR, bool NL>
 static mf_status launch_tcp(const CUtensorMap& mx, const CUtensorMap& mg, const tcp::Args& args, dim3 grid,
                             cudaStream_t st) {
-    using G = tcp::Geo<NIN, NW, BN, NJOB, KR, SPLIT>;
+    using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT>;
     const size_t smem = G::BYTES + 1024;
-    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJOB, KR, SPLIT, NL>;
+    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NL>;
     cudaFuncAttributes attr;
     MF_CHECK_CUDA(cudaFuncGetAttributes(&attr, kern), "tc physical kernel attributes");
     const long long pool = (long long)((attr.numRegs + 7) / 8 * 8) * tcp::THREADS;
@@ -587,15 +593,15 @@ static mf_status launch_tcp(const CUtensorMap& mx, const CUtensorMap& mg, const 
     return MF_OK;
 }
 
-template <int NIN, int NW, int BN, int NJOB, bool SPLIT>
+template <int NIN, int NW, int BN, int NJB, bool SPLIT>
 static mf_status dispatch_tcp(const mf_config& c, const CUtensorMap& mx, const CUtensorMap& mg,
                               const tcp::Args& args, dim3 grid, cudaStream_t st) {
     const bool nl = c.nonlinear != 0;
     if (c.read_rows == 32)
-        return nl ? launch_tcp<NIN, NW, BN, NJOB, SPLIT, 32, true>(mx, mg, args, grid, st)
-                  : launch_tcp<NIN, NW, BN, NJOB, SPLIT, 32, false>(mx, mg, args, grid, st);
-    return nl ? launch_tcp<NIN, NW, BN, NJOB, SPLIT, 64, true>(mx, mg, args, grid, st)
-              : launch_tcp<NIN, NW, BN, NJOB, SPLIT, 64, false>(mx, mg, args, grid, st);
+        return nl ? launch_tcp<NIN, NW, BN, NJB, SPLIT, 32, true>(mx, mg, args, grid, st)
+                  : launch_tcp<NIN, NW, BN, NJB, SPLIT, 32, false>(mx, mg, args, grid, st);
+    return nl ? launch_tcp<NIN, NW, BN, NJB, SPLIT, 64, true>(mx, mg, args, grid, st)
+              : launch_tcp<NIN, NW, BN, NJB, SPLIT, 64, false>(mx, mg, args, grid, st);
 }
 
 mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, size_t ws_bytes,
@@ -621,16 +627,18 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     const long long K = (long long)a.m * c.rows;
     const int cols = tiles * c.cols;
     const int blocks = cols / shape.bn;
-    const int npad = tcp::npad_of(shape);
+    int brows = 0, pstride = 0;
+    tcp::rows_of(shape, brows, pstride);
     const float scale = tcp::split_scale(c, shape.split != 0);
     __half* gs = static_cast<__half*>(workspace);
     {
-        const long long total = (long long)blocks * npad * K;
+        const long long total = (long long)blocks * brows * K;
         long long grid = (total + 255) / 256;
         if (grid > 148 * 64) grid = 148 * 64;
         tcp::restore_split_kernel<<<(unsigned)grid, 256, 0, st>>>(make_layout(c), make_physics(c),
                                                                  static_cast<const uint8_t*>(a.packed), a.p,
-                                                                 a.tile_begin * c.cols, blocks, shape.bn, npad, K,
+                                                                 a.tile_begin * c.cols, blocks, shape.bn,
+                                                                 shape.nw, brows, pstride, K,
                                                                  a.seed, a.event, scale, shape.split, gs);
         MF_LAUNCH_CHECK("restore_split_kernel");
     }
@@ -638,7 +646,7 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     mf_status r = tc_make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n,
                               (uint64_t)K, (uint32_t)c.read_rows, tcp::BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!r) r = tc_make_map(&mg, gs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K,
-                            (uint64_t)blocks * tcp::PARTS * npad, (uint64_t)K, 16, (uint32_t)(tcp::PARTS * npad),
+                            (uint64_t)blocks * brows, (uint64_t)K, 16, (uint32_t)brows,
                             CU_TENSOR_MAP_SWIZZLE_32B);
     if (r) return r;
     tcp::Args args{};
@@ -665,18 +673,23 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
         args.a_mask4[i] = (uint32_t)c.in_mask[i] * 0x01010101u;
     }
     const double inv_unit = 1.0 / c.unit;
+    uint32_t sum = 0;
     for (int w = 0; w < c.n_w; ++w) {
         args.cw[w] = (float)(c.voltage * c.w_mask[w] * inv_unit / scale);
         args.slope[w] = (float)(c.nonlinear / c.adc_max[w]);
-        args.maxw[w] = (float)c.adc_max[w];
-        for (int i = 0; i < c.n_in; ++i) args.factor[i][w] = (float)(c.in_factor[i] * c.w_factor[w]);
+        args.qmax[w] = (float)c.adc_max[w] + 12582912.0f;
+        for (int i = 0; i < c.n_in; ++i) {
+            args.factor[i][w] = (int)(c.in_factor[i] * c.w_factor[w]);
+            sum += (uint32_t)args.factor[i][w];
+        }
     }
-    const int bc = shape.bn * shape.njob;
+    args.offset = (int)(0u - 0x4B400000u * sum);
+    const int bc = shape.bn * shape.njb;
     dim3 grid((unsigned)((a.n + tcp::BM - 1) / tcp::BM), (unsigned)((cols + bc - 1) / bc));
-    if (shape.nin == 5) return dispatch_tcp<5, 5, 8, 4, true>(c, mx, mg, args, grid, st);
-    if (shape.nin == 3) return dispatch_tcp<3, 3, 16, 2, true>(c, mx, mg, args, grid, st);
-    if (shape.nin == 8) return dispatch_tcp<8, 8, 4, 4, false>(c, mx, mg, args, grid, st);
-    return dispatch_tcp<4, 4, 8, 4, true>(c, mx, mg, args, grid, st);
+    if (shape.nin == 5) return dispatch_tcp<5, 5, 16, 2, true>(c, mx, mg, args, grid, st);
+    if (shape.nin == 3) return dispatch_tcp<3, 3, 32, 1, true>(c, mx, mg, args, grid, st);
+    if (shape.nin == 8) return dispatch_tcp<8, 8, 16, 1, false>(c, mx, mg, args, grid, st);
+    return dispatch_tcp<4, 4, 16, 2, true>(c, mx, mg, args, grid, st);
 }
 
 }  // namespace mf
