@@ -28,12 +28,28 @@ advances.
 """
 
 import math
+import threading
 
 import torch
 
 from .functional import _checked
 from .quantization import compute_dtype, input_tiles
 from .simulator import Simulator, check_device_error, default_schedule
+
+
+_STREAMS = {}
+_STREAMS_LOCK = threading.Lock()
+
+
+def _helper_streams(device):
+    """The pipeline's second compute stream and its copy streams, created once per
+    device: the caching allocator keeps freed blocks per stream, so fresh streams on
+    every call would strand memory in pools that later calls cannot reuse."""
+    key = torch.device(device).index
+    with _STREAMS_LOCK:
+        if key not in _STREAMS:
+            _STREAMS[key] = tuple(torch.cuda.Stream(device) for _ in range(3))
+        return _STREAMS[key]
 
 
 def _nonfinite(tensor, dtype=None):
@@ -98,8 +114,7 @@ def host_mm(a, b, *, simulator, out=None, row_offset=0, chunk_rows=None):
         raise ValueError("chunk_rows must be a positive int")
 
     compute = torch.cuda.current_stream(device)
-    second = torch.cuda.Stream(device)
-    copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    second, copy_in, copy_out = _helper_streams(device)
     a_dev = torch.empty(a.shape, dtype=a.dtype, device=device)
     b_dev = torch.empty(b.shape, dtype=b.dtype, device=device)
     out_dev = torch.empty((n, o), dtype=a.dtype, device=device)
