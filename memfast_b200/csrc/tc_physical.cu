@@ -116,10 +116,18 @@ struct Args {
     uint32_t lut_lo, lut_hi; // FP16 high bytes of the digits 0..7 (low bytes are 0)
     float cw[MAXS];          // voltage * M_w / unit * 2^-s: FP16-part sum -> ADC input
     float slope[MAXS];       // S-curve: nonlinear / max_w
-    float qmax[MAXS];        // max_w + 1.5 * 2^23: the ADC's upper clamp in the shifted domain
+    float cws[MAXS];         // cw / max_w: the ADC input as a fraction of full scale
+    float inv_maxw[MAXS];    // 1 / max_w
+    float maxw[MAXS];
     int factor[MAXS][MAXS];  // s_a * s_w
     int offset;              // -0x4B400000 * sum of factor over the slice pairs (mod 2^32)
 };
+
+__device__ __forceinline__ float mul_sat(float a, float b) {
+    float d;
+    asm("mul.rn.sat.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
 
 template <int N>
 __device__ __forceinline__ void tmem_load_cols(uint32_t addr, uint32_t* v) {
@@ -366,10 +374,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
 #pragma unroll 1
             for (int cb = 0; cb < NJB && ok; ++cb) {
-                // ADC: q = z + 1.5 * 2^23 rounds z half to even into the low mantissa bits
-                // (0 <= z < 2^22), clamped in that shifted domain (the bounds are integers);
-                // the bit pattern of q is 0x4B400000 + count, so the total accumulates
-                // bits * factor in wrapping int32 and the constant part is removed once.
+                // ADC: the saturating multiply clamps z / max_w to [0, 1], and
+                // q = (z / max_w) * max_w + 1.5 * 2^23 rounds the clamped z half to even into
+                // the low mantissa bits (max_w < 2^22); the bit pattern of q is
+                // 0x4B400000 + count, so the total accumulates bits * factor in wrapping int32
+                // and the constant part is removed once.
                 int total[G::EC];
 #pragma unroll
                 for (int e = 0; e < G::EC; ++e) total[e] = args.offset;
@@ -397,15 +406,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                                                               __uint_as_float(v[SPLIT ? 1 : 0][e * NW + w]))
                                                   : __uint_as_float(v[0][e * NW + w]);
                             constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
-                            float q;
+                            float s;
                             if (NONLINEAR) {
                                 float z = __fmul_rn(x, args.cw[w]);
                                 z = __fdiv_rn(z, __fadd_rn(1.0f, fabsf(__fmul_rn(args.slope[w], z))));
-                                q = __fadd_rn(z, kMagic);
+                                s = mul_sat(z, args.inv_maxw[w]);
                             } else {
-                                q = __fmaf_rn(x, args.cw[w], kMagic);
+                                s = mul_sat(x, args.cws[w]);
                             }
-                            q = fminf(fmaxf(q, kMagic), args.qmax[w]);
+                            const float q = __fmaf_rn(s, args.maxw[w], kMagic);
                             total[e] += __float_as_int(q) * args.factor[a][w];
                         }
                 }
@@ -677,7 +686,9 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     for (int w = 0; w < c.n_w; ++w) {
         args.cw[w] = (float)(c.voltage * c.w_mask[w] * inv_unit / scale);
         args.slope[w] = (float)(c.nonlinear / c.adc_max[w]);
-        args.qmax[w] = (float)c.adc_max[w] + 12582912.0f;
+        args.cws[w] = (float)(c.voltage * c.w_mask[w] * inv_unit / scale / c.adc_max[w]);
+        args.inv_maxw[w] = (float)(1.0 / c.adc_max[w]);
+        args.maxw[w] = (float)c.adc_max[w];
         for (int i = 0; i < c.n_in; ++i) {
             args.factor[i][w] = (int)(c.in_factor[i] * c.w_factor[w]);
             sum += (uint32_t)args.factor[i][w];
