@@ -196,6 +196,15 @@ mf_status mf_quantize_conv_input(const mf_config* cfg, const mf_conv2d* conv, co
                                  const void* fixed_scale, void* codes, void* xscale, uint32_t* nonfinite,
                                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* Finiteness check on the device without a host synchronisation (the checks of
+ * memfast/functional.py:50-53 and quantization.py:12-15, read later together with
+ * other flags): over n contiguous values of dtype x_dtype, sets the device word
+ * *flag to `code` if it is still 0 and a value is not finite, or to narrow_code
+ * (non-zero: FP64 input only) if a value is finite in FP64 but not in FP32.
+ * Checks enqueued on one stream report the first failing one. */
+mf_status mf_check_finite(const void* x, int32_t x_dtype, int64_t n, uint32_t code, uint32_t narrow_code,
+                          uint32_t* flag, void* stream);
+
 /* Output height and width of a convolution group; MF_ERR_INVALID for a bad geometry. */
 mf_status mf_conv_output(const mf_conv2d* conv, int64_t* out_height, int64_t* out_width);
 

@@ -130,6 +130,15 @@ mf_status mf_quantize_input(const mf_config* cfg, const void* x, int32_t x_dtype
                           workspace_bytes, (cudaStream_t)stream);
 }
 
+mf_status mf_check_finite(const void* x, int32_t x_dtype, int64_t n, uint32_t code, uint32_t narrow_code,
+                          uint32_t* flag, void* stream) {
+    if ((!x && n > 0) || !flag || n < 0 || x_dtype < MF_F32 || x_dtype > MF_F64 || !code) {
+        set_error("mf_check_finite: invalid operands");
+        return MF_ERR_INVALID;
+    }
+    return check_finite(x, x_dtype, n, code, narrow_code, flag, (cudaStream_t)stream);
+}
+
 static bool conv_geometry(const mf_conv2d* cv, int64_t* oh, int64_t* ow) {
     if (!cv || cv->batch < 0 || cv->channels < 1 || cv->height < 1 || cv->width < 1 || cv->kernel_h < 1 ||
         cv->kernel_w < 1 || cv->stride_y < 1 || cv->stride_x < 1 || cv->pad_h < 0 || cv->pad_w < 0 ||

@@ -22,6 +22,11 @@ mf_status program_weights(const mf_config& c, const void* w, int dtype, int64_t 
 // Physical constants of a configuration for device code (reference.py, config.py).
 Physics make_physics(const mf_config& c);
 
+// Sets *flag (if still 0) to code_own when a value is not finite in its dtype, or to
+// code_narrow when an FP64 value is finite but overflows FP32.
+mf_status check_finite(const void* x, int dtype, int64_t n, uint32_t code_own, uint32_t code_narrow,
+                       uint32_t* flag, cudaStream_t stream);
+
 // Output extent of a convolution along one axis (0 when the window does not fit).
 int64_t conv_output_extent(int64_t size, int32_t kernel, int32_t stride, int32_t pad, int32_t dilation);
 

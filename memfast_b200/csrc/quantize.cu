@@ -467,6 +467,29 @@ __global__ void __launch_bounds__(256) conv_code_kernel(ConvGeom g, GroupGrid gg
     }
 }
 
+// Finiteness of n contiguous values: the first failing check of a stream wins
+// the flag word (atomicCAS from 0), so checks launched in the reference's order
+// report its first error.  code_own: a non-finite value in its stored dtype;
+// code_narrow (FP64 only, 0 = unused): finite in FP64 but not once narrowed to FP32.
+__global__ void check_finite_kernel(const void* x, int dtype, int64_t n, uint32_t code_own, uint32_t code_narrow,
+                                    uint32_t* flag) {
+    uint32_t found = 0;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        if (dtype == MF_F64) {
+            const double v = static_cast<const double*>(x)[i];
+            if (!isfinite(v)) found = found ? found : code_own;
+            else if (code_narrow && !isfinite(__double2float_rn(v))) found = found ? found : code_narrow;
+        } else if (!isfinite(load_as<float>(x, dtype, i))) {
+            found = code_own;
+        }
+        if (__any_sync(__activemask(), found != 0)) break;
+    }
+    // Own-dtype failures outrank narrowing ones within one launch.
+    const uint32_t own = __reduce_or_sync(__activemask(), found == code_own && found ? 1u : 0u);
+    const uint32_t any = __reduce_or_sync(__activemask(), found ? 1u : 0u);
+    if ((threadIdx.x & 31) == 0 && any) atomicCAS(flag, 0u, own ? code_own : code_narrow);
+}
+
 int grid_for(int64_t work, int threads) {
     int64_t blocks = (work + threads - 1) / threads;
     if (blocks > 148 * 32) blocks = 148 * 32;
@@ -604,6 +627,15 @@ mf_status quantize_input(const mf_config& c, const void* x, int dtype, int64_t n
     if (dbl) return run_input<double, double>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
     if (c.wide) return run_input<float, double>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
     return run_input<float, float>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
+}
+
+mf_status check_finite(const void* x, int dtype, int64_t n, uint32_t code_own, uint32_t code_narrow,
+                       uint32_t* flag, cudaStream_t stream) {
+    if (n <= 0) return MF_OK;
+    const int threads = 256;
+    check_finite_kernel<<<grid_for(n, threads), threads, 0, stream>>>(x, dtype, n, code_own, code_narrow, flag);
+    MF_LAUNCH_CHECK("check_finite_kernel");
+    return MF_OK;
 }
 
 mf_status quantize_conv_input(const mf_config& c, const mf_conv2d& cv, const void* x, int dtype,

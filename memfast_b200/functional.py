@@ -16,11 +16,11 @@ from pathlib import Path
 import torch
 
 from .config import Config
-from .quantization import compute_dtype, finite_flags
+from .quantization import check_finite, compute_dtype, finite_flags
 from .simulator import Simulator
 
 
-def _operands(a, b):
+def _operand_types(a, b):
     for name, value in (("A", a), ("B", b)):
         if not isinstance(value, torch.Tensor):
             raise TypeError(f"{name} must be a torch.Tensor")
@@ -36,11 +36,37 @@ def _operands(a, b):
         raise ValueError("A and B must use the same device")
     if a.device.type != "cuda":
         raise ValueError("memfast_b200 simulates on CUDA operands only")
+
+
+def _operands(a, b):
+    """Type, device and finiteness checks of an operand pair (one synchronisation)."""
+    _operand_types(a, b)
     finite_a, finite_b = finite_flags(a, b)
     if not finite_a:
         raise ValueError("A must be finite")
     if not finite_b:
         raise ValueError("B must be finite")
+
+
+# Errors of a deferred operand check, in the reference's order: _operands (A, then
+# B, each in its own dtype), then the quantisers (B is programmed before A is
+# quantised) in the dtype they compute in (quantization.py:14-15).
+OPERAND_ERRORS = {1: "A must be finite", 2: "B must be finite",
+                  3: f"quantized values must be finite in {torch.float32}"}
+
+
+def _operand_code(a, b, config):
+    """Device int32 flags [operand error, output]: the first holds 0 when A and B pass
+    the checks above, else the OPERAND_ERRORS key of the first failure, checked in that
+    order on the device (no synchronisation); the second is left for the output check."""
+    flags = torch.zeros(2, dtype=torch.int32, device=a.device)
+    a_narrows = a.dtype == torch.float64 and compute_dtype(config, config.activation_bits) == torch.float32
+    b_narrows = b.dtype == torch.float64 and compute_dtype(config, config.weight_bits) == torch.float32
+    check_finite(a, flags[:1], 1)
+    check_finite(b, flags[:1], 2, 3 if b_narrows else 0)
+    if a_narrows:
+        check_finite(a, flags[:1], 1, 3)
+    return flags
 
 
 def _engine(a, simulator, config, mode, cache_dir):
@@ -107,21 +133,26 @@ def _checked(tensor, config, bits):
     return not (tensor.dtype == torch.float64 and compute_dtype(config, bits) == torch.float32)
 
 
-def _product(a, b, simulator, cached_rhs=None):
+def _product(a, b, simulator, cached_rhs=None, operand_code=None):
+    """One programmed product.  ``operand_code``: the deferred operand check
+    (``_operand_code``), read with the output check in one synchronisation; None when
+    the caller already checked the operands."""
     if torch.is_grad_enabled() and (a.requires_grad or b.requires_grad):
         raise NotImplementedError(
             "memfast_b200 simulates the analog forward only; detach operands or use torch.no_grad()"
         )
     config = simulator.config
+    deferred = operand_code is not None
     matrix = simulator._matrix_for(b if cached_rhs is None else cached_rhs,
-                                   checked=_checked(b, config, config.weight_bits),
+                                   checked=deferred or _checked(b, config, config.weight_bits),
                                    rows=math.prod(a.shape[:-1]))
     with torch.no_grad():
-        return matrix._forward(a.detach(), checked=_checked(a, config, config.activation_bits))
+        return matrix._forward(a.detach(), checked=deferred or _checked(a, config, config.activation_bits),
+                               input_flag=operand_code, input_errors=OPERAND_ERRORS if deferred else None)
 
 
 def _matmul(a, b, *, simulator, config, mode, cache_dir, out):
-    _operands(a, b)
+    _operand_types(a, b)
     left_vector, right_vector = a.ndim == 1, b.ndim == 1
     left = a.unsqueeze(0) if left_vector else a
     right = b.unsqueeze(-1) if right_vector else b
@@ -137,15 +168,18 @@ def _matmul(a, b, *, simulator, config, mode, cache_dir, out):
     engine = _engine(a, simulator, config, mode, cache_dir)
     with torch.autocast(device_type=a.device.type, enabled=False):
         if a.numel() == 0 or b.numel() == 0 or 0 in shape:
+            _operands(a, b)
             result = a.new_zeros(shape)
         else:
             left = left.expand(batch + (rows, reduction))
             rhs_batch = right.shape[:-2]
             if all(size == 1 for size in rhs_batch):
+                # One product: the operand check is read with the output check.
                 rhs = right if right.ndim == 2 else right.reshape(reduction, columns)
                 cached = None if b.ndim == 2 else _rhs_view(engine, b, rhs, ())
-                result = _product(left, rhs, engine, cached)
+                result = _product(left, rhs, engine, cached, operand_code=_operand_code(a, b, engine.config))
             else:
+                _operands(a, b)
                 groups = {}
                 padding = len(batch) - len(rhs_batch)
                 for index in itertools.product(*(range(size) for size in batch)):

@@ -104,6 +104,23 @@ def finite_flags(*tensors, dtypes=None):
     return [bool(flag) for flag in torch.isfinite(torch.stack(extremes)).all(dim=1).tolist()]
 
 
+def check_finite(tensor, flag, code, narrow_code=0):
+    """Enqueue a finiteness check of ``tensor`` (no synchronisation): the device int32
+    ``flag`` (a one-element view) becomes ``code`` if it is still 0 and a value is not
+    finite, or ``narrow_code`` if an FP64 value overflows FP32 (``mf_check_finite``)."""
+    if tensor.numel() == 0:
+        return
+    if tensor.dtype not in _lib.DTYPES:
+        tensor = tensor.float()
+    if not tensor.is_contiguous():
+        tensor = tensor.contiguous()
+    _lib.check(
+        _lib.load().mf_check_finite(_lib.ptr(tensor), _lib.DTYPES[tensor.dtype], tensor.numel(), code, narrow_code,
+                                    _lib.ptr(flag), _lib.stream_of(tensor.device)),
+        "mf_check_finite",
+    )
+
+
 def compute_dtype(config, bits):
     """grouped_quantize computes in FP64 for wide codes or BFP, else FP32 (quantization.py:10-13)."""
     return torch.float64 if bits > 8 or config.bw_e is not None else torch.float32
@@ -168,8 +185,9 @@ def conv_input_tiles(x, config, geometry, fixed_scale=None):
     straight from the NCHW input ``x`` (any strides) without building them.
     ``geometry``: the group's ``_lib.MFConv2d`` (kernel, stride, padding, dilation,
     channels); ``x``'s shape and strides are filled in here.  ``flag`` is a device
-    int32 that the kernels set to 1 when a quantised value is not finite (the
-    reference raises ValueError then)."""
+    int32 pair whose first word the kernels set to 1 when a quantised value is not
+    finite (the reference raises ValueError then); the second is for the output
+    check."""
     _require_cuda(x, "input")
     if x.dtype not in _lib.DTYPES:
         x = x.float()
@@ -182,7 +200,7 @@ def conv_input_tiles(x, config, geometry, fixed_scale=None):
     m = math.ceil(k / r)
     codes = torch.empty((n, m, r), dtype=_code_dtype(config), device=x.device)
     xscale = torch.empty((n, m * config.reads_per_array), dtype=_scale_dtype(config), device=x.device)
-    flag = torch.zeros(1, dtype=torch.int32, device=x.device)
+    flag = torch.zeros(2, dtype=torch.int32, device=x.device)   # [input error, output check]
     if n == 0:
         return codes, xscale, flag
     if fixed_scale is not None:
@@ -211,14 +229,15 @@ def conv_output_size(geometry):
     return oh.value, ow.value
 
 
-def weight_tiles(weight, config, *, checked=False, kmajor=None):
+def weight_tiles(weight, config, *, checked=False, kmajor=None, out=None):
     """PyTorch-layout [O, K] floating weights -> (packed [m,p,R,C], weight_scale [m*reads,p,C], kmajor_written).
 
     ``checked``: the caller verified the weights finite in the quantiser's dtype.
     ``kmajor``: optional uint8 buffer for the K-major code copy of the tensor-core
     kernels; it is filled (and ``kmajor_written`` is True) when the weights are the
     transpose of a row-major [K, O] matrix, the right-hand operand of ``mm``, which
-    is then programmed in place through ``mf_program_rhs``."""
+    is then programmed in place through ``mf_program_rhs``.  ``out``: (packed, weight_scale)
+    buffers of the right shapes to program into instead of new ones."""
     _require_cuda(weight, "weight")
     o, k = weight.shape
     if not config.weight_signed and (weight < 0).any():
@@ -229,8 +248,15 @@ def weight_tiles(weight, config, *, checked=False, kmajor=None):
     weight = _as_native_float(weight, config, config.weight_bits, checked)
     r, c = config.array_size
     m, p = math.ceil(k / r), math.ceil(o / c)
-    packed = torch.empty((m, p, r, c), dtype=_code_dtype(config), device=weight.device)
-    wscale = torch.empty((m * config.reads_per_array, p, c), dtype=_scale_dtype(config), device=weight.device)
+    if out is None:
+        packed = torch.empty((m, p, r, c), dtype=_code_dtype(config), device=weight.device)
+        wscale = torch.empty((m * config.reads_per_array, p, c), dtype=_scale_dtype(config), device=weight.device)
+    else:
+        packed, wscale = out
+        if (packed.shape != (m, p, r, c) or packed.dtype != _code_dtype(config) or not packed.is_contiguous()
+                or wscale.shape != (m * config.reads_per_array, p, c) or wscale.dtype != _scale_dtype(config)
+                or not wscale.is_contiguous()):
+            raise ValueError("programming buffers do not match the matrix")
     workspace, need = _workspace(config, True, o, k, weight.device)
     if weight.stride(0) == 1 and weight.stride(1) >= max(o, 1):
         # The transpose of a row-major [K, O] matrix: program it in place.

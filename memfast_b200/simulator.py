@@ -35,6 +35,7 @@ from torch import nn
 from . import _lib
 from .config import Config
 from .quantization import (
+    check_finite,
     check_read_scales,
     expanded_parameter,
     finite_flags,
@@ -208,6 +209,19 @@ class Simulator:
         else:
             name = previous.name
         source = matrix if program is None else program
+        if (
+            self.mode == "default"
+            and same_tensor
+            and record[1] == metadata
+            and previous.config == self.config
+            and previous.packed.device == self.device
+            and previous.zero_correction is None
+            and previous.input_scale is None
+        ):
+            # Same tensor, same layout: program its current values into the cached
+            # module's buffers (no new module per call; same name and read event).
+            previous._reprogram(source.T, checked, rows)
+            return previous
         programmed = AnalogMatrix(source.T, self, name=name, _checked=checked, _rows=rows)
         if (
             self.mode == "tuned"
@@ -554,6 +568,24 @@ class AnalogMatrix(nn.Module):
             self._workspaces[_lib.stream_of(device).value] = [torch.empty(need, dtype=torch.uint8, device=device),
                                                                False]
 
+    def _reprogram(self, weight, checked, rows):
+        """Program new [O, K] weights of this module's shape into its buffers, as the
+        reference reprograms the right-hand matrix of every mm call (simulator.py:149)."""
+        if not checked and not finite_flags(weight)[0]:
+            raise ValueError("weights must be finite")
+        device = self.packed.device
+        stream = _lib.stream_of(device).value
+        entry = self._workspaces.get(stream)
+        self._workspaces = {} if entry is None else {stream: entry}
+        if entry is None:
+            self._prepare_workspace(self.packed.shape[0], device, rows)
+            entry = self._workspaces.get(stream)
+        _, _, written = weight_tiles(weight.detach(), self.config, checked=checked,
+                                     kmajor=None if entry is None else entry[0][: self._kmajor_bytes],
+                                     out=(self.packed, self.weight_scale))
+        if entry is not None:
+            entry[1] = written
+
     def _drop_workspace(self):
         self._workspaces.clear()
 
@@ -581,11 +613,12 @@ class AnalogMatrix(nn.Module):
         return size.value
 
     def _execute(self, q, xscale, schedule, event, stable=False, *, vector_offset=0, input_flag=None,
-                 tiles=None, agree=None):
+                 input_errors=None, tiles=None, agree=None):
         """One fused device call: analog partials, scales, read sums and bias.
 
         ``input_flag``: device int32 set by a quantiser that checks finiteness on the
-        device; read in the same synchronisation as the output check.
+        device (or a deferred operand check); read in the same synchronisation as the
+        output check, non-zero raising ``ValueError(input_errors[value])``.
         ``tiles``: output tiles [t0, t1) only (a column shard; noise addresses stay
         global), giving columns [t0*cols, min(t1*cols, out_features)).
         ``agree``: combines this shard's finiteness with the other shards' (the FP64
@@ -593,15 +626,13 @@ class AnalogMatrix(nn.Module):
         output = self._launch(q, xscale, schedule, event, stable=stable, vector_offset=vector_offset, tiles=tiles)
         # One host synchronisation decides both the FP64 rerun of a narrow config
         # (simulator.py:614-615) and, in forward, the non-finite error.
-        if input_flag is None:
-            self._finite = finite_flags(output)[0]
-        else:
-            extremes = torch.aminmax(output) if output.numel() else (output.new_zeros(()), output.new_zeros(()))
-            low, high, bad = torch.stack([extremes[0].double(), extremes[1].double(),
-                                          input_flag.reshape(()).double()]).tolist()
-            if bad:
-                raise ValueError("quantized values must be finite")
-            self._finite = math.isfinite(low) and math.isfinite(high)
+        # flags: [input error code, output non-finite]; one device-to-host read.
+        flags = input_flag if input_flag is not None else torch.zeros(2, dtype=torch.int32, device=q.device)
+        check_finite(output, flags[1:2], 1)
+        bad, nonfinite = flags.tolist()
+        if bad:
+            raise ValueError((input_errors or {}).get(bad, "quantized values must be finite"))
+        self._finite = not nonfinite
         if agree is not None:
             self._finite = agree(self._finite)
         if not self.config.wide and not stable and not self._finite:
@@ -689,10 +720,12 @@ class AnalogMatrix(nn.Module):
         shard = self._column_shard
         return self._forward(x) if shard is None else shard(self, x)
 
-    def _forward(self, x, checked=False, vector_offset=0, tiles=None, agree=None):
+    def _forward(self, x, checked=False, vector_offset=0, tiles=None, agree=None, input_flag=None,
+                 input_errors=None):
         """forward(); ``checked``: the caller verified x finite in the quantiser's dtype;
         ``vector_offset``: global index of x's first vector (noise addresses of row shards);
-        ``tiles``/``agree``: a column shard, as in ``_execute``."""
+        ``tiles``/``agree``: a column shard, as in ``_execute``; ``input_flag`` /
+        ``input_errors``: a deferred operand check, as in ``_execute``."""
         if x.ndim < 1 or x.shape[-1] != self.in_features or not x.is_floating_point():
             raise ValueError("input must be floating with matching in_features")
         if x.device != self.packed.device or x.device != self.simulator.device:
@@ -709,10 +742,12 @@ class AnalogMatrix(nn.Module):
         if self._event >= 2**63:
             raise OverflowError("read-event counter exhausted")
         q, xscale = input_tiles(x.reshape(-1, self.in_features), self.config, self.input_scale, checked=checked)
-        output = self._product(q, xscale, shape, x.dtype, vector_offset=vector_offset, tiles=tiles, agree=agree)
+        output = self._product(q, xscale, shape, x.dtype, vector_offset=vector_offset, tiles=tiles, agree=agree,
+                               input_flag=input_flag, input_errors=input_errors)
         return output.reshape(*shape[:-1], width)
 
-    def _product(self, q, xscale, shape, dtype, *, vector_offset=0, input_flag=None, tiles=None, agree=None):
+    def _product(self, q, xscale, shape, dtype, *, vector_offset=0, input_flag=None, input_errors=None,
+                 tiles=None, agree=None):
         """forward() from quantised codes on (simulator.py:631-646): schedule, product,
         non-finite checks, ``dtype`` result, read event.  ``shape``/``dtype`` describe
         the caller's input (tuned-mode key); ``input_flag`` as in ``_execute``."""
@@ -721,14 +756,14 @@ class AnalogMatrix(nn.Module):
         key = tuple(shape), str(dtype)
         if self.simulator.mode == "tuned":
             if key not in self._prepared:
-                if input_flag is not None and input_flag.item():
-                    raise ValueError("quantized values must be finite")
+                if input_flag is not None and input_flag[0].item():
+                    raise ValueError((input_errors or {}).get(input_flag[0].item(), "quantized values must be finite"))
                 with torch.cuda.device(q.device):
                     self._prepared[key] = self.simulator._select(
                         self, types.SimpleNamespace(shape=tuple(shape), dtype=dtype), q, xscale, event)
             schedule = self._prepared[key]
         output = self._execute(q, xscale, schedule, event, vector_offset=vector_offset, input_flag=input_flag,
-                               tiles=tiles, agree=agree)
+                               input_errors=input_errors, tiles=tiles, agree=agree)
         finite = self._finite and (output.dtype == dtype or finite_flags(output, dtypes=[dtype])[0])
         if agree is not None:
             finite = agree(finite)

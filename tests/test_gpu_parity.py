@@ -140,3 +140,23 @@ def test_nonfinite_inputs_rejected(mf):
     a[0, 0] = float("nan")
     with pytest.raises(ValueError):
         sim.mm(a, torch.randn(128, 32, device="cuda"))
+
+
+@pytest.mark.parametrize("where", ["A", "B"])
+def test_nonfinite_operands_raise_without_consuming_a_read_event(mf, where):
+    """mm checks its operands after enqueueing the product (one synchronisation);
+    the reference's errors and read-event behaviour are unchanged."""
+    config, arrays, _ = load_case("shared_read_events")
+    sim = mf.Simulator(config, device="cuda")
+    a, b = cuda(arrays["A"]), cuda(arrays["B"])
+    first = sim.mm(a, b)
+    bad_a, bad_b = a.clone(), b.clone()
+    (bad_a if where == "A" else bad_b)[1, 2] = float("inf")
+    with pytest.raises(ValueError, match=f"{where} must be finite"):
+        sim.mm(bad_a, bad_b)
+    second = sim.mm(a, b).cpu().numpy()
+    assert_parity(second, arrays["out1"], config, "second read after the error")
+    assert not np.array_equal(first.cpu().numpy(), second)
+    huge = b.double() * 1e300
+    with pytest.raises(ValueError, match="finite in torch.float32"):
+        sim.mm(a.double(), huge)
