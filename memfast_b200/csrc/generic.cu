@@ -599,6 +599,176 @@ __global__ void __launch_bounds__(THREADS, 2) physical_staged_kernel(Layout L, P
     }
 }
 
+// ---------------------------------------------------- tiled physical kernel --
+// physical_staged_kernel's computation for FP32 currents without slice-pair or
+// output-mode read noise (voltage noise included), with 4 vectors x 4 columns
+// per thread: per row, one 128-bit load of four voltages and one of four
+// conductances feed 16 FMAs (the staged kernel's 2 x 4 tile needs three loads for
+// 8).  The voltages of every input slice are staged once per read, G - LOW one
+// weight slice at a time; FMAs run in ascending row order from the same staged
+// values, so the currents equal the staged kernel's bit for bit.  Cascade level 1
+// lives in shared memory (at most 256 reads per output).
+constexpr int TT_V = 64;          // vectors per CTA (4 per thread)
+constexpr int TT_C = 64;          // output columns per CTA (4 per thread)
+
+template <typename CodeT>
+__global__ void __launch_bounds__(THREADS, 2) physical_tile_kernel(Layout L, Physics P, MMArgs a, const float* G,
+                                                                  int group_begin, int group_width, long long full) {
+    extern __shared__ __align__(16) uint8_t tile_raw[];
+    float* sV = reinterpret_cast<float*>(tile_raw);             // [n_in][rows][TT_V]
+    float* sG = sV + (size_t)L.n_in * L.rows * TT_V;           // [rows][TT_C], G - LOW of one weight slice
+    float* acc1 = sG + (size_t)L.rows * TT_C;                   // [TT_V][TT_C], cascade level 1
+    const CodeT* codes = static_cast<const CodeT*>(a.codes);
+    const float* xscale = static_cast<const float*>(a.xscale);
+    const float* wscale = static_cast<const float*>(a.wscale);
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const long long v0 = (long long)blockIdx.x * TT_V;
+    const long long col0 = (long long)group_begin * L.C + (long long)blockIdx.y * TT_C;
+    const long long col_end = (long long)(group_begin + group_width) * L.C;
+    const int MR = a.m * L.reads;
+    const long long row_stride = (long long)a.m * L.R;
+    const uint64_t read_seed = event_seed(a.seed, a.event);
+    const float low = (float)P.low;
+
+    float acc0[4][4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            acc0[e][j] = 0.0f;
+            acc1[(4 * ty + e) * TT_C + 4 * tx + j] = 0.0f;   // each thread owns its 16 cells
+        }
+
+    for (int i = 0; i < MR; ++i) {
+        const int arr = i / L.reads, g = i % L.reads;
+        const int r0 = g * L.rows;
+        const int len = L.rows < L.R - r0 ? L.rows : L.R - r0;
+        __syncthreads();
+        for (int idx = tid; idx < L.n_in * len * TT_V; idx += THREADS) {
+            const int v = idx % TT_V, rr = (idx / TT_V) % len, sa = idx / (TT_V * len);
+            const long long vec = v0 + v;
+            float value = 0.0f;
+            if (vec < a.n) {
+                const int r = r0 + rr;
+                const int amask = L.in_mask[sa];
+                const long long code = (long long)codes[vec * row_stride + (long long)arr * L.R + r];
+                const long long d = (code >> L.in_shift[sa]) & amask;
+                value = __fmul_rn(__fdiv_rn((float)d, (float)amask), (float)P.voltage);
+                if (P.volt_var != 0) {
+                    const long long address = (((vec + a.vector_offset) * a.m + arr) * L.n_in + sa) * L.R + r;
+                    value = __fmul_rn(value, __fadd_rn(1.0f, __fmul_rn((float)P.volt_var,
+                                                                      rng_normal(address, read_seed, 40))));
+                }
+            }
+            sV[((size_t)sa * L.rows + rr) * TT_V + v] = value;
+        }
+        // Totals in wrapping int32 (the host checks |T| < 2^31): the ADC's
+        // rint(clamp(value, 0, max_w)) equals the bit pattern of
+        // clamp(value + 1.5 * 2^23, ...) minus 0x4B400000 (integer bounds, 0 <= value < 2^22).
+        int total[4][4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) total[e][j] = 0;
+        for (int sw = 0; sw < L.n_w; ++sw) {
+            __syncthreads();
+            for (int idx = tid; idx < len * TT_C; idx += THREADS) {
+                const int c = idx % TT_C, rr = idx / TT_C;
+                const long long col = col0 + c;
+                float value = 0.0f;
+                if (col < col_end) {
+                    const long long t = col / L.C, cc = col % L.C;
+                    value = __fadd_rn(
+                        G[((((long long)arr * group_width + (t - group_begin)) * L.n_w + sw) * L.R + r0 + rr) * L.C +
+                          cc],
+                        -low);
+                }
+                sG[rr * TT_C + c] = value;
+            }
+            __syncthreads();
+            const int maxw = L.adc_max[sw];
+            for (int sa = 0; sa < L.n_in; ++sa) {
+                const float* pv = sV + (size_t)sa * L.rows * TT_V + 4 * ty;
+                const float* pg = sG + 4 * tx;
+                float cur[4][4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) cur[e][j] = 0.0f;
+#pragma unroll 4
+                for (int rr = 0; rr < len; ++rr) {
+                    const float4 v4 = *reinterpret_cast<const float4*>(pv + rr * TT_V);
+                    const float4 g4 = *reinterpret_cast<const float4*>(pg + rr * TT_C);
+                    const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+                    const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) cur[e][j] = __fmaf_rn(vv[e], gg[j], cur[e][j]);
+                }
+                const int factor = (int)(L.in_factor[sa] * L.w_factor[sw]);
+                const float amw = (float)((long long)L.in_mask[sa] * L.w_mask[sw]);
+                const float inv_unit = (float)P.inv_unit;
+                const float slope = (float)(P.nonlinear / maxw);
+                constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+                const float qmax = __fadd_rn((float)maxw, kMagic);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        float value = __fmul_rn(__fmul_rn(cur[e][j], amw), inv_unit);
+                        if (P.nonlinear != 0) value = __fdiv_rn(value, __fadd_rn(1.0f, fabsf(__fmul_rn(slope, value))));
+                        const float q = fminf(fmaxf(__fadd_rn(value, kMagic), kMagic), qmax);
+                        total[e][j] += (__float_as_int(q) - 0x4B400000) * factor;
+                    }
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const long long vec = v0 + 4 * ty + e;
+            const float xs = vec < a.n ? xscale[vec * MR + i] : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const long long col = col0 + 4 * tx + j;
+                if (col >= col_end) continue;
+                const long long t = col / L.C, cc = col % L.C;
+                const float ws = wscale[((long long)i * a.p + t) * L.C + cc];
+                acc0[e][j] = __fadd_rn(acc0[e][j], scaled_partial<float, float, int>(total[e][j], xs, ws));
+            }
+        }
+        const int done = i + 1;
+        if (done <= full && (done & 15) == 0) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float* slot = acc1 + (4 * ty + e) * TT_C + 4 * tx + j;
+                    *slot = __fadd_rn(*slot, acc0[e][j]);
+                    acc0[e][j] = 0.0f;
+                }
+        }
+    }
+    float* out = static_cast<float*>(a.out);
+    const float* bias = static_cast<const float*>(a.bias);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const long long vec = v0 + 4 * ty + e;
+        if (vec >= a.n) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const long long col = col0 + 4 * tx + j;
+            if (col >= col_end || col >= a.out_features) continue;
+            // acc0 + acc1 + acc2 + acc3 (upper levels zero), then the store into zeros.
+            float value = __fadd_rn(acc0[e][j], acc1[(4 * ty + e) * TT_C + 4 * tx + j]);
+            value = __fadd_rn(value, 0.0f);
+            value = __fadd_rn(value, 0.0f);
+            value = __fadd_rn(0.0f, value);
+            if (bias) value = __fadd_rn(value, bias[col]);
+            out[vec * a.ldo + col] = value;
+        }
+    }
+}
+
 size_t staged_smem(const mf_config& c, size_t elem) {
     return ((size_t)c.n_in * c.read_rows * ST_TV + (size_t)c.n_w * c.read_rows * ST_TC) * elem;
 }
@@ -663,10 +833,27 @@ mf_status launch_physical_t(const mf_config& c, const mf_schedule& s, const MMAr
         MF_LAUNCH_CHECK("restore_kernel");
         const long long cols = (long long)gw * c.cols;
         const bool pair_noise = c.read_mode == 1 && c.read_var != 0;
+        const bool output_noise = c.read_mode == 2 && c.read_var != 0;
+        const size_t tsmem = ((size_t)c.n_in * c.read_rows * TT_V + (size_t)c.read_rows * TT_C + TT_V * TT_C) * 4;
+        if (sizeof(CurT) == 4 && sizeof(OutT) == 4 && !pair_noise && !output_noise && MR <= 256 &&
+            tsmem <= 110 * 1024 && reconstruction_bound(c) < 2147483647.0 && max_adc(c) < (1 << 22)) {
+            dim3 grid((unsigned)((a.n + TT_V - 1) / TT_V), (unsigned)((cols + TT_C - 1) / TT_C));
+            const long long full16 = (long long)MR - MR % 16;
+#define MF_TILED(CODE)                                                                                \
+    do {                                                                                              \
+        auto kern = physical_tile_kernel<CODE>;                                                       \
+        MF_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem), \
+                      "tiled smem attribute");                                                         \
+        kern<<<grid, THREADS, tsmem, st>>>(L, P, a, reinterpret_cast<const float*>(G), begin, gw, full16); \
+    } while (0)
+            if (c.wide_codes) MF_TILED(long long); else MF_TILED(uint8_t);
+#undef MF_TILED
+            MF_LAUNCH_CHECK("physical_tile_kernel");
+            continue;
+        }
         const size_t smem = staged_smem(c, sizeof(CurT));
         if (!pair_noise && smem <= ST_SMEM_MAX) {
             dim3 grid((unsigned)((a.n + ST_TV - 1) / ST_TV), (unsigned)((cols + ST_TC - 1) / ST_TC));
-            const bool output_noise = c.read_mode == 2 && c.read_var != 0;
 #define MF_STAGED(CODE, OUTN)                                                                          \
     do {                                                                                               \
         auto kern = physical_staged_kernel<CODE, CurT, OutT, ScaleT, OUTN>;                            \
@@ -715,6 +902,12 @@ Physics make_physics(const mf_config& c) {
     P.mean_factor = expm1(0.5 * s2);
     P.var_factor = exp(s2) * expm1(s2);
     return P;
+}
+
+int max_adc(const mf_config& c) {
+    int m = 0;
+    for (int i = 0; i < c.n_w; ++i) m = c.adc_max[i] > m ? c.adc_max[i] : m;
+    return m;
 }
 
 double reconstruction_bound(const mf_config& c) {

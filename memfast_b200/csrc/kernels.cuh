@@ -63,6 +63,7 @@ struct MMArgs {
 
 // Largest |signed reconstruction| of one read, as in config.py:114-122.
 double reconstruction_bound(const mf_config& c);
+int max_adc(const mf_config& c);
 
 // True when ideal ADC counts equal exact integer digit dots for this config: the
 // reference's FP32 (or FP64) current error stays below half a count.
