@@ -19,6 +19,13 @@
 // FP32 bmm by rounding only; the ADC scales, rounds half to even and clamps as
 // the reference does.
 //
+// Ideal devices whose counts the packed and FP8 kernels do not take (64-row
+// reads, Config's 1-bit defaults, the 256 x 256 format configurations) use the
+// same kernel with the weight digits as the B operand (one FP16 part): every
+// product and partial sum is then a small integer, so the accumulator holds the
+// exact digit dot D and the epilogue's count is min(D, m), bit-exact wherever
+// exact_integer_counts holds.
+//
 // Scope: FP32 currents and epilogue (not Config.wide / precise_currents), no
 // voltage noise, read noise only in the shared mode (it is folded into G' per
 // read event by restore_split_kernel), input digits of at most 3 bits, 32- or
@@ -68,15 +75,15 @@ constexpr int MAXS = 8;          // slices per operand in the tables below
 // Shared-memory and TMEM geometry of one instantiation.  A job is one input
 // slice a of one BN-column block: one accumulator set of NT columns, fed by
 // KS (split halves stacked along N) or 2 KS MMAs; jobs rotate over U units.
-template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT>
+template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART>
 struct Geo {
     static constexpr int KS = KR / 16;                     // MMA K steps per read
     static constexpr int EC = BN / 4;                      // columns per epilogue thread per block
     static constexpr int NP = NW * BN;                     // accumulator columns of one half (jj * NW + w)
-    static constexpr int NT = SPLIT ? (PARTS * NP + 15) / 16 * 16 : (NP + 15) / 16 * 16;   // MMA N
+    static constexpr int NT = SPLIT ? (NPART * NP + 15) / 16 * 16 : (NP + 15) / 16 * 16;   // MMA N
     static constexpr int PSTRIDE = SPLIT ? NP : NT;        // B rows between the halves of a tile
-    static constexpr int BROWS = ((PARTS * PSTRIDE > NT ? PARTS * PSTRIDE : NT) + 7) / 8 * 8;   // B tile rows
-    static constexpr int ACCS = SPLIT ? PARTS : 1;         // accumulators per slice pair
+    static constexpr int BROWS = ((NPART * PSTRIDE > NT ? NPART * PSTRIDE : NT) + 7) / 8 * 8;   // B tile rows
+    static constexpr int ACCS = SPLIT ? NPART : 1;         // accumulators per slice pair
     static constexpr int UNIT = NT;                        // TMEM columns of a job
     static constexpr int U = 512 / UNIT < NJB * NIN ? 512 / UNIT : NJB * NIN;   // TMEM units
     static constexpr int BC = NJB * BN;                    // output columns per CTA
@@ -154,11 +161,11 @@ __device__ __forceinline__ void tmem_loaded(uint32_t* v) {
     for (int k = 0; k < N; ++k) asm volatile("" : "+r"(v[k]));
 }
 
-template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, bool NONLINEAR>
+template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool NONLINEAR>
 __global__ void __launch_bounds__(THREADS, 1)
     tc_physical_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_g,
                        const __grid_constant__ Args args) {
-    using G = Geo<NIN, NW, BN, NJB, KR, SPLIT>;
+    using G = Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* a_planes = base + G::OFF_A;
@@ -265,7 +272,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             const uint32_t d = tmem + unit * G::UNIT;
                             const uint64_t da = desc_sw32(planes + a * G::KS * G::AT);
 #pragma unroll
-                            for (int part = 0; part < (SPLIT ? 1 : PARTS); ++part)
+                            for (int part = 0; part < (SPLIT ? 1 : NPART); ++part)
 #pragma unroll
                                 for (int ks = 0; ks < G::KS; ++ks)
                                     mma_f16(d, da + (uint64_t)((ks * G::AT) >> 4),
@@ -372,8 +379,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                             col < args.col_end ? __ldg(args.wscale + (long long)(i + 1) * args.ldw + col) : 0.0f;
                     }
             }
-#pragma unroll 1
-            for (int cb = 0; cb < NJB && ok; ++cb) {
+            // Unrolled: acc0 and the scales stay in registers (a dynamic block index would
+            // put them in local memory).
+#pragma unroll
+            for (int cb = 0; cb < NJB; ++cb) {
                 // ADC: the saturating multiply clamps z / max_w to [0, 1], and
                 // q = (z / max_w) * max_w + 1.5 * 2^23 rounds the clamped z half to even into
                 // the low mantissa bits (max_w < 2^22); the bit pattern of q is
@@ -513,6 +522,31 @@ __global__ void restore_split_kernel(Layout L, Physics P, const uint8_t* packed,
     }
 }
 
+// The weight digits as the B operand (ideal devices): rows
+// (block * brows + jj * NW + w) for output column col_begin + block * BN + jj and
+// weight slice w (other rows zero), K contiguous, exact FP16 integers.
+__global__ void weight_digits_kernel(Layout L, const uint8_t* packed, int p, int col_begin, int blocks, int bn,
+                                     int brows, long long kpad, __half* gs) {
+    const long long total = (long long)blocks * brows * kpad;
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const long long k = idx % kpad;
+        const long long rest = idx / kpad;
+        const int brow = (int)(rest % brows);
+        const int block = (int)(rest / brows);
+        float value = 0.0f;
+        if (brow < L.n_w * bn) {
+            const int jj = brow / L.n_w, w = brow % L.n_w;
+            const long long o = (long long)col_begin + (long long)block * bn + jj;
+            const long long tile = o / L.C, c = o % L.C;
+            const long long arr = k / L.R, r = k % L.R;
+            const long long cell = ((arr * p + tile) * L.R + r) * L.C + c;
+            value = (float)(((long long)packed[cell] >> L.w_shift[w]) & L.w_mask[w]);
+        }
+        gs[idx] = __float2half_rn(value);
+    }
+}
+
 // Instantiations: (input slices, weight slices) -> columns per block, blocks per
 // CTA, split accumulators.  Each MMA is as wide as TMEM and the 256-column limit of
 // N allow (the tensor core's cost here is per instruction rather than per column).
@@ -520,9 +554,11 @@ struct Shape {
     int nin, nw, bn, njb, split;
 };
 constexpr Shape kShapes[] = {{5, 5, 16, 2, 1}, {3, 3, 32, 1, 1}, {8, 8, 16, 1, 0}, {4, 4, 16, 2, 1}};
+// Ideal devices: one FP16 part (the digits), so a block can hold twice the columns.
+constexpr Shape kDigitShapes[] = {{5, 5, 32, 1, 0}, {3, 3, 32, 2, 0}, {8, 8, 16, 1, 0}, {4, 4, 32, 1, 0}};
 
 bool shape_of(const mf_config& c, Shape& s) {
-    for (const Shape& k : kShapes)
+    for (const Shape& k : c.ideal ? kDigitShapes : kShapes)
         if (k.nin == c.n_in && k.nw == c.n_w) {
             s = k;
             return true;
@@ -530,13 +566,15 @@ bool shape_of(const mf_config& c, Shape& s) {
     return false;
 }
 
+int parts_of(const mf_config& c) { return c.ideal ? 1 : PARTS; }
+
 // B tile rows per column block (rounded to 8) and the row offset of the second half,
 // as Geo computes them.
-void rows_of(const Shape& s, int& brows8, int& pstride) {
+void rows_of(const Shape& s, int npart, int& brows8, int& pstride) {
     const int np = s.nw * s.bn;
-    const int nt = s.split ? (PARTS * np + 15) / 16 * 16 : (np + 15) / 16 * 16;
+    const int nt = s.split ? (npart * np + 15) / 16 * 16 : (np + 15) / 16 * 16;
     pstride = s.split ? np : nt;
-    const int brows = PARTS * pstride > nt ? PARTS * pstride : nt;
+    const int brows = npart * pstride > nt ? npart * pstride : nt;
     brows8 = (brows + 7) / 8 * 8;
 }
 
@@ -551,15 +589,34 @@ float split_scale(const mf_config& c, bool fixed) {
 }  // namespace tcp
 
 // =================================================================== host side
+// Ideal devices: the accumulator holds the exact digit dot D (FP16 digits, every
+// partial sum an integer below 2^24) and the epilogue's count is min(D, max_w), the
+// reference's count wherever exact_integer_counts holds; the int32 totals are exact
+// below 2^31.
+static bool digits_eligible(const mf_config& c, int32_t m) {
+    if (!exact_integer_counts(c) || c.wide || c.wide_codes || c.precise_currents) return false;
+    if (c.read_rows != 32 && c.read_rows != 64) return false;
+    tcp::Shape s;
+    if (!tcp::shape_of(c, s)) return false;
+    if (c.rows % c.read_rows || c.cols % s.bn) return false;
+    for (int i = 0; i < c.n_in; ++i)
+        if (c.in_mask[i] > 7) return false;
+    for (int i = 0; i < c.n_w; ++i)
+        if (c.w_mask[i] > 2047 || c.adc_max[i] < 1 || c.adc_max[i] >= (1 << 22)) return false;
+    const long long MR = (long long)m * c.reads;
+    return MR <= 256 && reconstruction_bound(c) < 2147483647.0;
+}
+
 bool tc_physical_eligible(const mf_config& c, int32_t m) {
-    if (c.ideal || c.wide || c.wide_codes || c.precise_currents) return false;
+    if (c.ideal) return digits_eligible(c, m);
+    if (c.wide || c.wide_codes || c.precise_currents) return false;
     if (c.volt_var != 0) return false;
     if (c.read_var != 0 && c.read_mode != 0) return false;
     if (c.write_var + c.read_var > 1.0) return false;
     if (c.read_rows != 32 && c.read_rows != 64) return false;
-    if (c.rows % c.read_rows || c.cols % 16) return false;
     tcp::Shape s;
     if (!tcp::shape_of(c, s)) return false;
+    if (c.rows % c.read_rows || c.cols % s.bn) return false;
     for (int i = 0; i < c.n_in; ++i)
         if (c.in_mask[i] > 7) return false;
     for (int i = 0; i < c.n_w; ++i)
@@ -576,16 +633,16 @@ size_t tc_physical_workspace_bytes(const mf_config& c, int32_t m, int32_t tiles)
     if (!tcp::shape_of(c, s)) return 256;
     const long long blocks = (long long)tiles * c.cols / s.bn;
     int brows = 0, pstride = 0;
-    tcp::rows_of(s, brows, pstride);
+    tcp::rows_of(s, tcp::parts_of(c), brows, pstride);
     return (size_t)blocks * brows * (size_t)m * c.rows * sizeof(__half) + 256;
 }
 
-template <int NIN, int NW, int BN, int NJB, bool SPLIT, int KR, bool NL>
+template <int NIN, int NW, int BN, int NJB, bool SPLIT, int NPART, int KR, bool NL>
 static mf_status launch_tcp(const CUtensorMap& mx, const CUtensorMap& mg, const tcp::Args& args, dim3 grid,
                             cudaStream_t st) {
-    using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT>;
+    using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART>;
     const size_t smem = G::BYTES + 1024;
-    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NL>;
+    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL>;
     cudaFuncAttributes attr;
     MF_CHECK_CUDA(cudaFuncGetAttributes(&attr, kern), "tc physical kernel attributes");
     const long long pool = (long long)((attr.numRegs + 7) / 8 * 8) * tcp::THREADS;
@@ -607,10 +664,18 @@ static mf_status dispatch_tcp(const mf_config& c, const CUtensorMap& mx, const C
                               const tcp::Args& args, dim3 grid, cudaStream_t st) {
     const bool nl = c.nonlinear != 0;
     if (c.read_rows == 32)
-        return nl ? launch_tcp<NIN, NW, BN, NJB, SPLIT, 32, true>(mx, mg, args, grid, st)
-                  : launch_tcp<NIN, NW, BN, NJB, SPLIT, 32, false>(mx, mg, args, grid, st);
-    return nl ? launch_tcp<NIN, NW, BN, NJB, SPLIT, 64, true>(mx, mg, args, grid, st)
-              : launch_tcp<NIN, NW, BN, NJB, SPLIT, 64, false>(mx, mg, args, grid, st);
+        return nl ? launch_tcp<NIN, NW, BN, NJB, SPLIT, tcp::PARTS, 32, true>(mx, mg, args, grid, st)
+                  : launch_tcp<NIN, NW, BN, NJB, SPLIT, tcp::PARTS, 32, false>(mx, mg, args, grid, st);
+    return nl ? launch_tcp<NIN, NW, BN, NJB, SPLIT, tcp::PARTS, 64, true>(mx, mg, args, grid, st)
+              : launch_tcp<NIN, NW, BN, NJB, SPLIT, tcp::PARTS, 64, false>(mx, mg, args, grid, st);
+}
+
+// Ideal devices: one part (the digits), linear ADC.
+template <int NIN, int NW, int BN, int NJB>
+static mf_status dispatch_digits(const mf_config& c, const CUtensorMap& mx, const CUtensorMap& mg,
+                                 const tcp::Args& args, dim3 grid, cudaStream_t st) {
+    if (c.read_rows == 32) return launch_tcp<NIN, NW, BN, NJB, false, 1, 32, false>(mx, mg, args, grid, st);
+    return launch_tcp<NIN, NW, BN, NJB, false, 1, 64, false>(mx, mg, args, grid, st);
 }
 
 mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, size_t ws_bytes,
@@ -637,10 +702,19 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     const int cols = tiles * c.cols;
     const int blocks = cols / shape.bn;
     int brows = 0, pstride = 0;
-    tcp::rows_of(shape, brows, pstride);
-    const float scale = tcp::split_scale(c, shape.split != 0);
+    tcp::rows_of(shape, tcp::parts_of(c), brows, pstride);
+    const float scale = c.ideal ? 1.0f : tcp::split_scale(c, shape.split != 0);
     __half* gs = static_cast<__half*>(workspace);
-    {
+    if (c.ideal) {
+        const long long total = (long long)blocks * brows * K;
+        long long grid = (total + 255) / 256;
+        if (grid > 148 * 64) grid = 148 * 64;
+        tcp::weight_digits_kernel<<<(unsigned)grid, 256, 0, st>>>(make_layout(c),
+                                                                 static_cast<const uint8_t*>(a.packed), a.p,
+                                                                 a.tile_begin * c.cols, blocks, shape.bn, brows,
+                                                                 K, gs);
+        MF_LAUNCH_CHECK("weight_digits_kernel");
+    } else {
         const long long total = (long long)blocks * brows * K;
         long long grid = (total + 255) / 256;
         if (grid > 148 * 64) grid = 148 * 64;
@@ -686,7 +760,9 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     for (int w = 0; w < c.n_w; ++w) {
         args.cw[w] = (float)(c.voltage * c.w_mask[w] * inv_unit / scale);
         args.slope[w] = (float)(c.nonlinear / c.adc_max[w]);
-        args.cws[w] = (float)(c.voltage * c.w_mask[w] * inv_unit / scale / c.adc_max[w]);
+        // Ideal devices: the accumulator is the digit dot D and the count min(D, max_w).
+        args.cws[w] = c.ideal ? (float)(1.0 / c.adc_max[w])
+                              : (float)(c.voltage * c.w_mask[w] * inv_unit / scale / c.adc_max[w]);
         args.inv_maxw[w] = (float)(1.0 / c.adc_max[w]);
         args.maxw[w] = (float)c.adc_max[w];
         for (int i = 0; i < c.n_in; ++i) {
@@ -697,6 +773,12 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     args.offset = (int)(0u - 0x4B400000u * sum);
     const int bc = shape.bn * shape.njb;
     dim3 grid((unsigned)((a.n + tcp::BM - 1) / tcp::BM), (unsigned)((cols + bc - 1) / bc));
+    if (c.ideal) {
+        if (shape.nin == 5) return dispatch_digits<5, 5, 32, 1>(c, mx, mg, args, grid, st);
+        if (shape.nin == 3) return dispatch_digits<3, 3, 32, 2>(c, mx, mg, args, grid, st);
+        if (shape.nin == 8) return dispatch_digits<8, 8, 16, 1>(c, mx, mg, args, grid, st);
+        return dispatch_digits<4, 4, 32, 1>(c, mx, mg, args, grid, st);
+    }
     if (shape.nin == 5) return dispatch_tcp<5, 5, 16, 2, true>(c, mx, mg, args, grid, st);
     if (shape.nin == 3) return dispatch_tcp<3, 3, 32, 1, true>(c, mx, mg, args, grid, st);
     if (shape.nin == 8) return dispatch_tcp<8, 8, 16, 1, false>(c, mx, mg, args, grid, st);

@@ -46,9 +46,13 @@ def test_workspace_queries_need_no_gpu():
     size = ct.c_size_t()
     sched = _lib.schedule()
     lib = _lib.load()
-    assert lib.mf_sliced_mm_workspace(_lib.native_config(ideal), ct.byref(sched), 64, 2, 3, 0, 3, ct.byref(size)) == 0
-    assert size.value == 0
     simt = _lib.schedule(kernel=1)
+    assert lib.mf_sliced_mm_workspace(_lib.native_config(ideal), ct.byref(simt), 64, 2, 3, 0, 3, ct.byref(size)) == 0
+    assert size.value == 0
+    assert lib.mf_sliced_mm_workspace(_lib.native_config(ideal), ct.byref(sched), 64, 2, 3, 0, 3, ct.byref(size)) == 0
+    # tensor-core digit dots: FP16 weight digits of 8 slices x 16-column blocks of the
+    # 3 tiles (128 rows per block) over K = 128
+    assert size.value == (3 * 64 // 16) * 128 * 128 * 2 + 256
     assert lib.mf_sliced_mm_workspace(_lib.native_config(noisy), ct.byref(simt), 64, 2, 3, 0, 3, ct.byref(size)) == 0
     # one group of `arrays` tiles of restored FP32 conductances: m * width * W * R * C * 4
     assert size.value == 2 * 2 * 8 * 64 * 64 * 4

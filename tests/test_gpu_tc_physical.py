@@ -47,8 +47,27 @@ CONFIGS = {
 }
 
 
+# Ideal devices the packed and FP8 kernels do not take: the same kernel with the
+# weight digits as the B operand, bit-exact.  ``saturating_adc`` (4-bit ADC, count
+# limit 15 against digit dots up to 32 x 9) clamps most counts of the upper slices.
+IDEAL = {
+    "default_ideal": dict(nonidealities=dict(write_variation=0.0)),
+    "int8_rpr64_ideal": dict(MATRIX, input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2), adc_bits=7,
+                             nonidealities=dict(write_variation=0.0)),
+    "int4_rpr64_ideal": dict(MATRIX, activation_bits=4, weight_bits=4, input_slice=(1, 1, 2), weight_slice=(1, 1, 2),
+                             adc_bits=6, nonidealities=dict(write_variation=0.0)),
+    "int7_ideal": dict(INT8, activation_bits=7, weight_bits=7, input_slice=(1, 2, 2, 2), weight_slice=(1, 2, 2, 2),
+                       adc_bits=8, nonidealities=dict(write_variation=0.0)),
+    "wide_weight_digits": dict(INT8, input_slice=(1, 2, 2, 3), weight_slice=(1, 1, 2, 4), adc_bits=10,
+                               nonidealities=dict(write_variation=0.0)),
+    "saturating_adc": dict(INT8, adc_bits=4, nonidealities=dict(write_variation=0.0)),
+    "rpr64_unsigned": dict(MATRIX, weight_signed=False, input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2),
+                           adc_bits=6, nonidealities=dict(write_variation=0.0)),
+}
+
+
 def config_of(mf, name):
-    kwargs = dict(CONFIGS[name])
+    kwargs = dict(CONFIGS[name] if name in CONFIGS else IDEAL[name])
     effects = kwargs.pop("nonidealities")
     return mf.Config(**kwargs, nonidealities=mf.Nonidealities(**effects))
 
@@ -117,7 +136,29 @@ def test_tensor_core_currents_match_the_oracle(mf, name):
     assert np.mean(fast != simt) <= 2 * MISMATCH_FRACTION
 
 
-@pytest.mark.parametrize("name", ["int8_write", "int8_rpr64_all", "default_1bit"])
+@pytest.mark.parametrize("name", list(IDEAL))
+def test_ideal_digit_dots_are_bit_exact(mf, name):
+    """Against the SIMT integer kernel (schedule kernel 1) and the CPU oracle, bit for bit."""
+    from oracle import oracle as O
+
+    config = config_of(mf, name)
+    assert config.nonidealities.ideal
+    k = 1024 if config.array_size[0] == 256 else 768
+    a, b = operands(200, k, 384, 7, nonnegative_b=not config.weight_signed)
+    m = -(-k // config.array_size[0])
+    p = -(-384 // config.array_size[1])
+    assert threads_of(mf, config, m, p) == 640, "the tensor-core digit kernel is not selected"
+    fast = product(mf, config, a, b, 0)
+    simt = product(mf, config, a, b, 1)
+    assert torch.equal(fast, simt), (name, (fast != simt).float().mean().item())
+    small = slice(0, 24)
+    want = O.mm(a[small].cpu().numpy(), b.cpu().numpy(), config)
+    got = fast[small].cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (name, np.mean(got != want))
+
+
+@pytest.mark.parametrize("name", ["int8_write", "int8_rpr64_all", "default_1bit", "int8_rpr64_ideal",
+                                  "int4_rpr64_ideal"])
 def test_column_shards_and_row_prefixes_are_exact(mf, name):
     config = config_of(mf, name)
     a, b = operands(300, 512, 640, 4)
