@@ -89,7 +89,7 @@ constexpr int EPI_BARRIER = 1;   // named barrier of the epilogue warps
 // checks the launched register count before every launch.
 constexpr int LAUNCH_REGS = (65536 / THREADS) / 8 * 8;
 constexpr int REG_CTRL = 56;
-constexpr int REG_XF = 56;
+constexpr int REG_XF = 40;
 constexpr int REG_EPI = ((THREADS * LAUNCH_REGS - 128 * REG_CTRL - 32 * XF_WARPS * REG_XF) / (32 * EPI_WARPS)) / 8 * 8;
 static_assert(REG_EPI >= 64 && REG_EPI <= 256, "epilogue register share out of range");
 static_assert(128 * REG_CTRL + 32 * XF_WARPS * REG_XF + 32 * EPI_WARPS * REG_EPI <= THREADS * LAUNCH_REGS,
@@ -309,23 +309,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int t = threadIdx.x - 32 * XF_WARP0;
         const int job = t / JOBN;
         const int jrow = t % JOBN;
-        uint32_t a_src[MAXA], a_m4[MAXA], a_sc[MAXA];
-        uint32_t s_src[MAXSLOT], s_m4[MAXSLOT], s_sc[MAXSLOT];
+        // ((x >> src) & m) << sc per byte of a word as one rotate and one mask:
+        // rotating right by src - sc (mod 32) moves each byte's digit to bit sc of
+        // the same byte, and the bits that cross a byte boundary land outside the
+        // mask (src + width <= 8), also in the rotate's wrap-around.
+        uint32_t a_rot[MAXA], a_m4[MAXA];
+        uint32_t s_rot[MAXSLOT], s_m4[MAXSLOT];
         uint32_t r_src[MAXRARE], r_m4[MAXRARE];
         int r_lim[MAXRARE];
         const int na = P.na, nslot = P.nslot, nr = P.nrare;
 #pragma unroll
         for (int a = 0; a < MAXA; ++a) {
-            a_src[a] = P.a_src[a];
-            a_m4[a] = (uint32_t)P.a_mask[a] * 0x01010101u;
-            a_sc[a] = P.a_scale[a];
+            a_rot[a] = (uint32_t)(P.a_src[a] - P.a_scale[a]) & 31u;
+            a_m4[a] = ((uint32_t)P.a_mask[a] << P.a_scale[a]) * 0x01010101u;
         }
 #pragma unroll
         for (int q = 0; q < MAXSLOT; ++q) {
             const int b = P.slot_plane[q];
-            s_src[q] = P.b_src[b];
-            s_m4[q] = (uint32_t)P.b_mask[b] * 0x01010101u;
-            s_sc[q] = P.b_scale[b];
+            s_rot[q] = (uint32_t)(P.b_src[b] - P.b_scale[b]) & 31u;
+            s_m4[q] = ((uint32_t)P.b_mask[b] << P.b_scale[b]) * 0x01010101u;
         }
 #pragma unroll
         for (int q = 0; q < MAXRARE; ++q) {
@@ -345,7 +347,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (a >= na) break;
                 uint32_t d[8];
 #pragma unroll
-                for (int k = 0; k < 8; ++k) d[k] = ((xw[k] >> a_src[a]) & a_m4[a]) << a_sc[a];
+                for (int k = 0; k < 8; ++k) d[k] = __funnelshift_r(xw[k], xw[k], a_rot[a]) & a_m4[a];
                 uint4* dst = reinterpret_cast<uint4*>(s.ap[st][a] + t * KR);
                 dst[0] = make_uint4(d[0], d[1], d[2], d[3]);
                 dst[1] = make_uint4(d[4], d[5], d[6], d[7]);
@@ -358,7 +360,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (q >= nslot) break;
                 uint32_t d[8];
 #pragma unroll
-                for (int k = 0; k < 8; ++k) d[k] = ((ww[k] >> s_src[q]) & s_m4[q]) << s_sc[q];
+                for (int k = 0; k < 8; ++k) d[k] = __funnelshift_r(ww[k], ww[k], s_rot[q]) & s_m4[q];
                 uint4* dst = reinterpret_cast<uint4*>(s.bp[st][job][q] + jrow * KR);
                 dst[0] = make_uint4(d[0], d[1], d[2], d[3]);
                 dst[1] = make_uint4(d[4], d[5], d[6], d[7]);

@@ -41,6 +41,25 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps
+// until the phase completes or about `ns` nanoseconds pass, instead of spinning
+// on issue slots that the compute warps of the CTA need.
+__device__ __forceinline__ bool mbar_try_suspend(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Longest single suspension of a waiting thread; it also bounds how late a role
+// notices that another role has aborted.
+constexpr uint32_t kSuspendNs = 20000;
+
 // Upper bound of every wait, in SM clock cycles (about 2 s at 1.965 GHz).
 constexpr long long kWaitCycles = 4000000000LL;
 
@@ -51,14 +70,13 @@ __device__ __forceinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, i
                                                unsigned code) {
     const long long start = clock64();
     while (true) {
-        if (mbar_try(bar, parity)) return true;
+        if (mbar_try_suspend(bar, parity, kSuspendNs)) return true;
         if (*(volatile int*)abort) return false;
         if (clock64() - start > kWaitCycles) {
             atomicCAS(error, 0u, code);
             *(volatile int*)abort = 1;
             return false;
         }
-        __nanosleep(32);
     }
 }
 
