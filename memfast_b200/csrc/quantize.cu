@@ -272,12 +272,19 @@ __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_
         maxima[j * O + o] = best;
         const float scale = group_scale<float>(best, s);
         const int64_t t = o / C, c = o % C;
+        // Array and row of k, stepped along the group (no division per element).
+        int64_t arr = k0 / R;
+        int rr = (int)(k0 - arr * R);
         uint32_t word = 0;
 #pragma unroll
         for (int r = 0; r < GR; ++r) {
             const int64_t k = k0 + r;
             const uint32_t code = k < K ? (uint32_t)(quantise<float>(v[r], scale, s) & 0xFF) : 0u;
-            if (k < kpad) packed[(((k / R) * p + t) * R + k % R) * C + c] = (uint8_t)code;
+            if (k < kpad) packed[((arr * p + t) * R + rr) * C + c] = (uint8_t)code;
+            if (++rr == R) {
+                rr = 0;
+                ++arr;
+            }
             word |= code << (8 * (r & 3));
             if ((r & 3) == 3) {
                 if (kmajor && k < kpad) *reinterpret_cast<uint32_t*>(kmajor + o * kpad + k - 3) = word;
@@ -490,6 +497,47 @@ __global__ void check_finite_kernel(const void* x, int dtype, int64_t n, uint32_
     if ((threadIdx.x & 31) == 0 && any) atomicCAS(flag, 0u, own ? code_own : code_narrow);
 }
 
+// Fast path of the same check (no narrowing test): 16-byte loads, four in flight
+// per thread, and an exponent test per element (all-ones exponent = Inf or NaN);
+// block 0 also checks the elements after the last whole vector.
+__device__ __forceinline__ bool vector_nonfinite(const uint4 v, int dtype) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    bool bad = false;
+    if (dtype == MF_F32) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) bad |= (w[i] & 0x7F800000u) == 0x7F800000u;
+    } else if (dtype == MF_F64) {
+        bad = ((w[1] & 0x7FF00000u) == 0x7FF00000u) | ((w[3] & 0x7FF00000u) == 0x7FF00000u);
+    } else {
+        const uint32_t e = dtype == MF_F16 ? 0x7C00u : 0x7F80u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) bad |= ((w[i] & e) == e) | ((w[i] & (e << 16)) == (e << 16));
+    }
+    return bad;
+}
+
+__global__ void check_finite_vector_kernel(const void* x, int dtype, int64_t n, int esize, uint32_t code,
+                                           uint32_t* flag) {
+    const uint4* vec = static_cast<const uint4*>(x);
+    const int64_t nvec = n * esize / 16;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    bool bad = false;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec; i += 4 * stride) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = i + u * stride < nvec ? __ldg(vec + i + u * stride) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) bad |= vector_nonfinite(v[u], dtype);
+    }
+    if (blockIdx.x == 0) {
+        for (int64_t i = nvec * 16 / esize + threadIdx.x; i < n; i += blockDim.x) {
+            if (dtype == MF_F64) bad |= !isfinite(static_cast<const double*>(x)[i]);
+            else bad |= !isfinite(load_as<float>(x, dtype, i));
+        }
+    }
+    if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicCAS(flag, 0u, code);
+}
+
 int grid_for(int64_t work, int threads) {
     int64_t blocks = (work + threads - 1) / threads;
     if (blocks > 148 * 32) blocks = 148 * 32;
@@ -633,6 +681,15 @@ mf_status check_finite(const void* x, int dtype, int64_t n, uint32_t code_own, u
                        uint32_t* flag, cudaStream_t stream) {
     if (n <= 0) return MF_OK;
     const int threads = 256;
+    if (!code_narrow && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+        const int esize = dtype == MF_F64 ? 8 : dtype == MF_F32 ? 4 : 2;
+        const int64_t nvec = n * esize / 16;
+        int64_t blocks = (nvec + 4 * threads - 1) / (4 * threads);
+        blocks = blocks < 1 ? 1 : blocks > 148 * 8 ? 148 * 8 : blocks;
+        check_finite_vector_kernel<<<(int)blocks, threads, 0, stream>>>(x, dtype, n, esize, code_own, flag);
+        MF_LAUNCH_CHECK("check_finite_vector_kernel");
+        return MF_OK;
+    }
     check_finite_kernel<<<grid_for(n, threads), threads, 0, stream>>>(x, dtype, n, code_own, code_narrow, flag);
     MF_LAUNCH_CHECK("check_finite_kernel");
     return MF_OK;

@@ -15,19 +15,31 @@ __global__ void weights_kmajor_kernel(const uint8_t* packed, uint8_t* out, int m
     __shared__ uint8_t tile[32][33];
     const long long k0 = (long long)blockIdx.x * 32, o0 = (long long)blockIdx.y * 32;
     const long long K = (long long)m * R, O = (long long)p * C;
+    // Array/row of k0 and tile/column of this thread's o, once per thread; rows step
+    // from there (no division per element).
+    const long long arr0 = k0 / R;
+    const int r0 = (int)(k0 - arr0 * R);
+    const long long o = o0 + threadIdx.x;
+    const long long t = o / C;
+    const int c = (int)(o - t * C);
     for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-        const long long k = k0 + j, o = o0 + threadIdx.x;
+        const long long k = k0 + j;
         uint8_t v = 0;
         if (k < K && o < O) {
-            const long long arr = k / R, r = k % R, t = o / C, c = o % C;
+            long long arr = arr0;
+            int r = r0 + j;
+            while (r >= R) {
+                r -= R;
+                ++arr;
+            }
             v = packed[((arr * p + t) * R + r) * C + c];
         }
         tile[j][threadIdx.x] = v;
     }
     __syncthreads();
     for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-        const long long o = o0 + j, k = k0 + threadIdx.x;
-        if (k < K && o < O) out[o * K + k] = tile[threadIdx.x][j];
+        const long long ot = o0 + j, k = k0 + threadIdx.x;
+        if (k < K && ot < O) out[ot * K + k] = tile[threadIdx.x][j];
     }
 }
 

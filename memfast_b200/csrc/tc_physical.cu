@@ -474,76 +474,74 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-// G' = G - LOW of the weight slices as the B operand: rows
-// (block * brows + part * pstride + jj * nwp + w) for output column
-// col_begin + block * BN + jj and weight slice w (other rows zero), K
-// contiguous.  fixed: X = rint(G' * scale) (|X| < 2^22) as the FP16 integers
-// H = rint(X / 2048) and L = X - 2048 H; otherwise x = G' * scale (< 2^14) as the
-// FP16 parts hi = fp16(x), lo = fp16(x - hi).  The conductance is the SIMT
-// path's (restored_conductance_f32).
-__global__ void restore_split_kernel(Layout L, Physics P, const uint8_t* packed, int p, int col_begin, int blocks,
-                                     int bn, int nwp, int brows, int pstride, long long kpad, uint32_t seed,
-                                     uint64_t event,
-                                     float scale,
-                                     int fixed, __half* gs) {
-    const int np = nwp * bn;
-    const long long total = (long long)blocks * brows * kpad;
-    const uint64_t read_seed = event_seed(seed, event);
-    const float low = (float)P.low;
-    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-         idx += (long long)gridDim.x * blockDim.x) {
-        const long long k = idx % kpad;
-        const long long rest = idx / kpad;
-        const int brow = (int)(rest % brows);
-        const int block = (int)(rest / brows);
-        const int part = brow / pstride, prow = brow % pstride;
-        __half hi = __float2half_rn(0.0f), lo = hi;
-        if (part < PARTS && prow < np && prow % nwp < L.n_w) {
-            const int jj = prow / nwp, w = prow % nwp;
-            const long long o = (long long)col_begin + (long long)block * bn + jj;
-            const long long tile = o / L.C, c = o % L.C;
-            const long long arr = k / L.R, r = k % L.R;
-            const long long cell = ((arr * p + tile) * L.R + r) * L.C + c;
-            const long long state = ((long long)packed[cell] >> L.w_shift[w]) & L.w_mask[w];
-            const long long address = (((arr * p + tile) * L.n_w + w) * L.R + r) * L.C + c;
-            const float g = restored_conductance_f32(P, state, L.w_mask[w], address, seed, read_seed);
-            const float x = __fmul_rn(__fadd_rn(g, -low), scale);
-            if (fixed) {
-                const float X = rintf(x);
-                const float H = rintf(__fmul_rn(X, 1.0f / 2048.0f));
-                hi = __float2half_rn(H);
-                lo = __float2half_rn(__fsub_rn(X, __fmul_rn(H, 2048.0f)));
-            } else {
-                hi = __float2half_rn(x);
-                lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
-            }
-        }
-        gs[((long long)block * brows + brow) * kpad + k] = part == 0 ? hi : lo;
-    }
-}
+// The B operand of one column block: rows (block * brows + part * pstride +
+// jj * nwp + w) for output column col_begin + block * BN + jj and weight slice w
+// (other rows zero), K contiguous.  One CTA per (column block, KC-row chunk of
+// K): the chunk's codes are staged in shared memory (a block lies inside one
+// tile and a chunk inside one array), so no element needs an index division.
+//   parts == 1 (ideal devices): the weight digit, an exact FP16 integer.
+//   parts == 2: G' = G - LOW, computed once per (row, column, slice) and written
+//   as two FP16 parts.  fixed: X = rint(G' * scale) (|X| < 2^22) as the integers
+//   H = rint(X / 2048) and L = X - 2048 H; otherwise x = G' * scale (< 2^14) as
+//   hi = fp16(x), lo = fp16(x - hi).  The conductance is the SIMT path's
+//   (restored_conductance_f32).
+constexpr int KC = 64;           // K rows per CTA of the operand builder
+constexpr int MAXBN = 32;        // columns per block, at most
 
-// The weight digits as the B operand (ideal devices): rows
-// (block * brows + jj * NW + w) for output column col_begin + block * BN + jj and
-// weight slice w (other rows zero), K contiguous, exact FP16 integers.
-__global__ void weight_digits_kernel(Layout L, const uint8_t* packed, int p, int col_begin, int blocks, int bn,
-                                     int brows, long long kpad, __half* gs) {
-    const long long total = (long long)blocks * brows * kpad;
-    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-         idx += (long long)gridDim.x * blockDim.x) {
-        const long long k = idx % kpad;
-        const long long rest = idx / kpad;
-        const int brow = (int)(rest % brows);
-        const int block = (int)(rest / brows);
-        float value = 0.0f;
-        if (brow < L.n_w * bn) {
-            const int jj = brow / L.n_w, w = brow % L.n_w;
-            const long long o = (long long)col_begin + (long long)block * bn + jj;
-            const long long tile = o / L.C, c = o % L.C;
-            const long long arr = k / L.R, r = k % L.R;
-            const long long cell = ((arr * p + tile) * L.R + r) * L.C + c;
-            value = (float)(((long long)packed[cell] >> L.w_shift[w]) & L.w_mask[w]);
+__global__ void __launch_bounds__(256) b_operand_kernel(Layout L, Physics P, const uint8_t* packed, int p,
+                                                        int col_begin, int blocks, int bn, int nwp, int brows,
+                                                        int pstride, int parts, int kc, long long kpad, uint32_t seed,
+                                                        uint64_t event, float scale, int fixed, __half* gs) {
+    __shared__ uint8_t codes[KC][MAXBN];
+    for (int block = blockIdx.y; block < blocks; block += gridDim.y) {
+        const long long k0 = (long long)blockIdx.x * kc;
+        const long long o0 = (long long)col_begin + (long long)block * bn;
+        const long long tile = o0 / L.C;
+        const int c0 = (int)(o0 - tile * L.C);
+        const long long arr = k0 / L.R;
+        const int r0 = (int)(k0 - arr * L.R);
+        const long long tile_base = (arr * p + tile) * L.R;
+        for (int idx = threadIdx.x; idx < kc * bn; idx += blockDim.x) {
+            const int kk = idx / bn, jj = idx - kk * bn;
+            codes[kk][jj] = packed[(tile_base + r0 + kk) * L.C + c0 + jj];
         }
-        gs[idx] = __float2half_rn(value);
+        __syncthreads();
+        const uint64_t read_seed = event_seed(seed, event);
+        const float low = (float)P.low;
+        const int np = nwp * bn;
+        __half* out = gs + (long long)block * brows * kpad + k0;
+        for (int idx = threadIdx.x; idx < pstride * kc; idx += blockDim.x) {
+            const int prow = idx / kc, kk = idx - prow * kc;
+            const int jj = prow / nwp, w = prow - jj * nwp;
+            __half hi = __float2half_rn(0.0f), lo = hi;
+            if (prow < np && w < L.n_w) {
+                const long long state = ((long long)codes[kk][jj] >> L.w_shift[w]) & L.w_mask[w];
+                if (parts == 1) {
+                    hi = __float2half_rn((float)state);
+                } else {
+                    const long long address = (((arr * p + tile) * L.n_w + w) * L.R + r0 + kk) * L.C + c0 + jj;
+                    const float g = restored_conductance_f32(P, state, L.w_mask[w], address, seed, read_seed);
+                    const float x = __fmul_rn(__fadd_rn(g, -low), scale);
+                    if (fixed) {
+                        const float X = rintf(x);
+                        const float H = rintf(__fmul_rn(X, 1.0f / 2048.0f));
+                        hi = __float2half_rn(H);
+                        lo = __float2half_rn(__fsub_rn(X, __fmul_rn(H, 2048.0f)));
+                    } else {
+                        hi = __float2half_rn(x);
+                        lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
+                    }
+                }
+            }
+            out[(long long)prow * kpad + kk] = hi;
+            if (parts == 2) out[(long long)(pstride + prow) * kpad + kk] = lo;
+        }
+        // Rows past the parts (MMA padding) are zero.
+        for (int idx = parts * pstride * kc + threadIdx.x; idx < brows * kc; idx += blockDim.x) {
+            const int row = idx / kc, kk = idx - row * kc;
+            out[(long long)row * kpad + kk] = __float2half_rn(0.0f);
+        }
+        __syncthreads();   // the next block's codes overwrite the staging tile
     }
 }
 
@@ -705,25 +703,15 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     tcp::rows_of(shape, tcp::parts_of(c), brows, pstride);
     const float scale = c.ideal ? 1.0f : tcp::split_scale(c, shape.split != 0);
     __half* gs = static_cast<__half*>(workspace);
-    if (c.ideal) {
-        const long long total = (long long)blocks * brows * K;
-        long long grid = (total + 255) / 256;
-        if (grid > 148 * 64) grid = 148 * 64;
-        tcp::weight_digits_kernel<<<(unsigned)grid, 256, 0, st>>>(make_layout(c),
-                                                                 static_cast<const uint8_t*>(a.packed), a.p,
-                                                                 a.tile_begin * c.cols, blocks, shape.bn, brows,
-                                                                 K, gs);
-        MF_LAUNCH_CHECK("weight_digits_kernel");
-    } else {
-        const long long total = (long long)blocks * brows * K;
-        long long grid = (total + 255) / 256;
-        if (grid > 148 * 64) grid = 148 * 64;
-        tcp::restore_split_kernel<<<(unsigned)grid, 256, 0, st>>>(make_layout(c), make_physics(c),
-                                                                 static_cast<const uint8_t*>(a.packed), a.p,
-                                                                 a.tile_begin * c.cols, blocks, shape.bn,
-                                                                 shape.nw, brows, pstride, K,
-                                                                 a.seed, a.event, scale, shape.split, gs);
-        MF_LAUNCH_CHECK("restore_split_kernel");
+    {
+        const int kc = c.rows % tcp::KC == 0 ? tcp::KC : 32;
+        const dim3 grid((unsigned)(K / kc), (unsigned)(blocks < 65535 ? blocks : 65535));
+        tcp::b_operand_kernel<<<grid, 256, 0, st>>>(make_layout(c), make_physics(c),
+                                                   static_cast<const uint8_t*>(a.packed), a.p,
+                                                   a.tile_begin * c.cols, blocks, shape.bn, shape.nw, brows, pstride,
+                                                   tcp::parts_of(c), kc, K, a.seed, a.event, scale,
+                                                   shape.split, gs);
+        MF_LAUNCH_CHECK("b_operand_kernel");
     }
     CUtensorMap mx, mg;
     mf_status r = tc_make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n,
