@@ -244,6 +244,12 @@ mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedu
  * finishing its outputs.  Returns MF_ERR_CUDA in that case, MF_OK otherwise. */
 mf_status mf_take_device_error(uint32_t* code);
 
+/* Enqueues on `stream` a copy of the device error word into `host_word` (pinned
+ * host memory), without clearing it: after the stream's next synchronisation a
+ * non-zero word means mf_take_device_error will report a failure.  Lets a caller
+ * test for device-side failures in the synchronisation it makes anyway. */
+mf_status mf_stage_device_error(uint32_t* host_word, void* stream);
+
 /* Resource admission for a schedule (replaces Simulator._admit, simulator.py:216-237,
  * and Program.resources, cuda.py:239-273).  MF_ERR_RESOURCE if it cannot run. */
 mf_status mf_query(const mf_config* cfg, const mf_schedule* schedule, int64_t n, int32_t m,

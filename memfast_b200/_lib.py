@@ -99,6 +99,7 @@ _SIGNATURES = {
                                           ct.c_int32, ct.c_int32, ct.c_int32, ct.c_int32,
                                           ct.POINTER(ct.c_size_t)]),
     "mf_take_device_error": (ct.c_int, [ct.POINTER(ct.c_uint32)]),
+    "mf_stage_device_error": (ct.c_int, [ct.c_void_p, ct.c_void_p]),
     "mf_query": (ct.c_int, [ct.POINTER(MFConfig), ct.POINTER(MFSchedule), ct.c_int64, ct.c_int32,
                             ct.c_int32, ct.POINTER(MFResources)]),
 }
@@ -194,7 +195,11 @@ def schedule(kernel=0, tile_n=32, tile_o=64, arrays=2, kmajor_ready=0):
 
 
 def stream_of(device):
-    return ct.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    """The device's current CUDA stream as a handle (without building a Stream object)."""
+    index = device.index if isinstance(device, torch.device) else device
+    if index is None:
+        index = torch.cuda.current_device()
+    return ct.c_void_p(torch._C._cuda_getCurrentRawStream(index))
 
 
 def ptr(tensor):

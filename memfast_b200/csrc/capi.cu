@@ -378,6 +378,14 @@ mf_status mf_query(const mf_config* cfg, const mf_schedule* schedule, int64_t n,
     return MF_OK;
 }
 
+mf_status mf_stage_device_error(uint32_t* host_word, void* stream) {
+    if (!host_word) {
+        set_error("mf_stage_device_error: NULL output");
+        return MF_ERR_INVALID;
+    }
+    return tc_stage_error(host_word, (cudaStream_t)stream);
+}
+
 mf_status mf_take_device_error(uint32_t* code) {
     if (!code) {
         set_error("mf_take_device_error: NULL output");

@@ -69,13 +69,13 @@ __device__ __forceinline__ uint32_t digit_of(CodeT code, int shift, int mask) {
 // `flags` runs every tile.
 struct TileFilter {
     const unsigned* flags;
-    int rows, cols, row_tiles;
+    int rows, cols, row_tiles, col_tiles;
 };
 
 // ------------------------------------------------------------ ideal kernel --
 template <typename CodeT, typename TotT, typename OutT, typename ScaleT>
 __global__ void __launch_bounds__(THREADS) ideal_kernel(Layout L, MMArgs a, int power, long long full,
-                                                        TileFilter filter) {
+                                                        TileFilter filter, int grid_x, int grid_y) {
     extern __shared__ __align__(16) uint32_t smem[];
     const int R4 = (L.rows + 3) >> 2;
     uint32_t* sA = smem;                               // [n_in][32][R4]
@@ -85,118 +85,133 @@ __global__ void __launch_bounds__(THREADS) ideal_kernel(Layout L, MMArgs a, int 
     const ScaleT* xscale = static_cast<const ScaleT*>(a.xscale);
     const ScaleT* wscale = static_cast<const ScaleT*>(a.wscale);
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-    const long long v0 = (long long)blockIdx.x * IDEAL_TV;
-    const long long col0 = (long long)a.tile_begin * L.C + (long long)blockIdx.y * IDEAL_TC;
     const long long col_end = (long long)a.tile_end * L.C;
     const int MR = a.m * L.reads;
     const long long row_stride = (long long)a.m * L.R;
-    if (filter.flags) {
-        const long long tr = v0 / filter.rows, tc = (col0 - (long long)a.tile_begin * L.C) / filter.cols;
-        if (!filter.flags[tc * filter.row_tiles + tr]) return;   // uniform across the CTA
-    }
-
-    Cascade<OutT> acc[2][4];
-#pragma unroll
-    for (int e = 0; e < 2; ++e)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[e][j].init();
-
-    for (int i = 0; i < MR; ++i) {
-        const int arr = i / L.reads, g = i % L.reads;
-        const int r0 = g * L.rows;
-        const int len = L.rows < L.R - r0 ? L.rows : L.R - r0;
-        __syncthreads();
-        for (int idx = tid; idx < L.n_in * IDEAL_TV * R4; idx += THREADS) {
-            const int r4 = idx % R4, v = (idx / R4) % IDEAL_TV, s = idx / (R4 * IDEAL_TV);
-            const long long vec = v0 + v;
-            uint32_t word = 0;
-            if (vec < a.n) {
-                const CodeT* row = codes + vec * row_stride + (long long)arr * L.R + r0;
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const int r = 4 * r4 + b;
-                    if (r < len) word |= digit_of(row[r], L.in_shift[s], L.in_mask[s]) << (8 * b);
-                }
-            }
-            sA[(s * IDEAL_TV + v) * R4 + r4] = word;
+    // Work items: for a full launch the blocks of the (grid_x x grid_y) grid, one per
+    // CTA; for a filtered launch the filter's tiles, over which a few CTAs step, each
+    // running the blocks of a flagged tile and skipping the others after one flag read.
+    const int sub_x = filter.flags ? filter.rows / IDEAL_TV : 1;
+    const int sub_y = filter.flags ? filter.cols / IDEAL_TC : 1;
+    const long long items = filter.flags ? (long long)filter.row_tiles * filter.col_tiles : (long long)grid_x * grid_y;
+    for (long long item = blockIdx.x + (long long)blockIdx.y * gridDim.x; item < items;
+         item += (long long)gridDim.x * gridDim.y) {
+        long long bx0 = item % grid_x, by0 = item / grid_x;
+        if (filter.flags) {
+            if (!filter.flags[item]) continue;   // uniform across the CTA
+            bx0 = (item % filter.row_tiles) * sub_x;
+            by0 = (item / filter.row_tiles) * sub_y;
         }
-        for (int idx = tid; idx < L.n_w * R4 * IDEAL_TC; idx += THREADS) {
-            const int c = idx % IDEAL_TC, r4 = (idx / IDEAL_TC) % R4, s = idx / (IDEAL_TC * R4);
-            const long long col = col0 + c;
-            uint32_t word = 0;
-            if (col < col_end) {
-                const long long t = col / L.C, cc = col % L.C;
-                const CodeT* base = packed + (((long long)arr * a.p + t) * L.R + r0) * L.C + cc;
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const int r = 4 * r4 + b;
-                    if (r < len) word |= digit_of(base[(long long)r * L.C], L.w_shift[s], L.w_mask[s]) << (8 * b);
-                }
-            }
-            sW[(s * R4 + r4) * IDEAL_TC + c] = word;
-        }
-        __syncthreads();
+        for (int sb = 0; sb < sub_x * sub_y; ++sb) {
+            const long long bx = bx0 + sb % sub_x, by = by0 + sb / sub_x;
+            if (bx >= grid_x || by >= grid_y) continue;
+            const long long v0 = bx * IDEAL_TV;
+            const long long col0 = (long long)a.tile_begin * L.C + by * IDEAL_TC;
 
-        TotT total[2][4];
+            Cascade<OutT> acc[2][4];
 #pragma unroll
-        for (int e = 0; e < 2; ++e)
+            for (int e = 0; e < 2; ++e)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) total[e][j] = 0;
-        for (int sa = 0; sa < L.n_in; ++sa) {
-            const uint32_t* pa0 = sA + (sa * IDEAL_TV + ty) * R4;
-            const uint32_t* pa1 = pa0 + 16 * R4;
-            for (int sw = 0; sw < L.n_w; ++sw) {
-                const uint32_t* pw = sW + sw * R4 * IDEAL_TC + 4 * tx;
-                uint32_t dot[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-                for (int r4 = 0; r4 < R4; ++r4) {
-                    const uint32_t x0 = pa0[r4], x1 = pa1[r4];
-                    const uint4 wv = *reinterpret_cast<const uint4*>(pw + r4 * IDEAL_TC);
-                    dot[0][0] = __dp4a(x0, wv.x, dot[0][0]);
-                    dot[0][1] = __dp4a(x0, wv.y, dot[0][1]);
-                    dot[0][2] = __dp4a(x0, wv.z, dot[0][2]);
-                    dot[0][3] = __dp4a(x0, wv.w, dot[0][3]);
-                    dot[1][0] = __dp4a(x1, wv.x, dot[1][0]);
-                    dot[1][1] = __dp4a(x1, wv.y, dot[1][1]);
-                    dot[1][2] = __dp4a(x1, wv.z, dot[1][2]);
-                    dot[1][3] = __dp4a(x1, wv.w, dot[1][3]);
+                for (int j = 0; j < 4; ++j) acc[e][j].init();
+
+            for (int i = 0; i < MR; ++i) {
+                const int arr = i / L.reads, g = i % L.reads;
+                const int r0 = g * L.rows;
+                const int len = L.rows < L.R - r0 ? L.rows : L.R - r0;
+                __syncthreads();
+                for (int idx = tid; idx < L.n_in * IDEAL_TV * R4; idx += THREADS) {
+                    const int r4 = idx % R4, v = (idx / R4) % IDEAL_TV, s = idx / (R4 * IDEAL_TV);
+                    const long long vec = v0 + v;
+                    uint32_t word = 0;
+                    if (vec < a.n) {
+                        const CodeT* row = codes + vec * row_stride + (long long)arr * L.R + r0;
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const int r = 4 * r4 + b;
+                            if (r < len) word |= digit_of(row[r], L.in_shift[s], L.in_mask[s]) << (8 * b);
+                        }
+                    }
+                    sA[(s * IDEAL_TV + v) * R4 + r4] = word;
                 }
-                const uint32_t maxw = (uint32_t)L.adc_max[sw];
-                const TotT factor = (TotT)(L.in_factor[sa] * L.w_factor[sw]);
+                for (int idx = tid; idx < L.n_w * R4 * IDEAL_TC; idx += THREADS) {
+                    const int c = idx % IDEAL_TC, r4 = (idx / IDEAL_TC) % R4, s = idx / (IDEAL_TC * R4);
+                    const long long col = col0 + c;
+                    uint32_t word = 0;
+                    if (col < col_end) {
+                        const long long t = col / L.C, cc = col % L.C;
+                        const CodeT* base = packed + (((long long)arr * a.p + t) * L.R + r0) * L.C + cc;
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const int r = 4 * r4 + b;
+                            if (r < len) word |= digit_of(base[(long long)r * L.C], L.w_shift[s], L.w_mask[s]) << (8 * b);
+                        }
+                    }
+                    sW[(s * R4 + r4) * IDEAL_TC + c] = word;
+                }
+                __syncthreads();
+
+                TotT total[2][4];
 #pragma unroll
                 for (int e = 0; e < 2; ++e)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        total[e][j] += (TotT)(dot[e][j] < maxw ? dot[e][j] : maxw) * factor;
+                    for (int j = 0; j < 4; ++j) total[e][j] = 0;
+                for (int sa = 0; sa < L.n_in; ++sa) {
+                    const uint32_t* pa0 = sA + (sa * IDEAL_TV + ty) * R4;
+                    const uint32_t* pa1 = pa0 + 16 * R4;
+                    for (int sw = 0; sw < L.n_w; ++sw) {
+                        const uint32_t* pw = sW + sw * R4 * IDEAL_TC + 4 * tx;
+                        uint32_t dot[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+                        for (int r4 = 0; r4 < R4; ++r4) {
+                            const uint32_t x0 = pa0[r4], x1 = pa1[r4];
+                            const uint4 wv = *reinterpret_cast<const uint4*>(pw + r4 * IDEAL_TC);
+                            dot[0][0] = __dp4a(x0, wv.x, dot[0][0]);
+                            dot[0][1] = __dp4a(x0, wv.y, dot[0][1]);
+                            dot[0][2] = __dp4a(x0, wv.z, dot[0][2]);
+                            dot[0][3] = __dp4a(x0, wv.w, dot[0][3]);
+                            dot[1][0] = __dp4a(x1, wv.x, dot[1][0]);
+                            dot[1][1] = __dp4a(x1, wv.y, dot[1][1]);
+                            dot[1][2] = __dp4a(x1, wv.z, dot[1][2]);
+                            dot[1][3] = __dp4a(x1, wv.w, dot[1][3]);
+                        }
+                        const uint32_t maxw = (uint32_t)L.adc_max[sw];
+                        const TotT factor = (TotT)(L.in_factor[sa] * L.w_factor[sw]);
+#pragma unroll
+                        for (int e = 0; e < 2; ++e)
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                total[e][j] += (TotT)(dot[e][j] < maxw ? dot[e][j] : maxw) * factor;
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const long long vec = v0 + ty + 16 * e;
+                    if (vec >= a.n) continue;
+                    const ScaleT xs = xscale[vec * MR + i];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const long long col = col0 + 4 * tx + j;
+                        if (col >= col_end) continue;
+                        const long long t = col / L.C, cc = col % L.C;
+                        const ScaleT ws = wscale[((long long)i * a.p + t) * L.C + cc];
+                        cascade_push(acc[e][j], scaled_partial<OutT, ScaleT, TotT>(total[e][j], xs, ws), i, power, full);
+                    }
+                }
             }
-        }
+            OutT* out = static_cast<OutT*>(a.out);
+            const ScaleT* bias = static_cast<const ScaleT*>(a.bias);
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            const long long vec = v0 + ty + 16 * e;
-            if (vec >= a.n) continue;
-            const ScaleT xs = xscale[vec * MR + i];
+            for (int e = 0; e < 2; ++e) {
+                const long long vec = v0 + ty + 16 * e;
+                if (vec >= a.n) continue;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const long long col = col0 + 4 * tx + j;
-                if (col >= col_end) continue;
-                const long long t = col / L.C, cc = col % L.C;
-                const ScaleT ws = wscale[((long long)i * a.p + t) * L.C + cc];
-                cascade_push(acc[e][j], scaled_partial<OutT, ScaleT, TotT>(total[e][j], xs, ws), i, power, full);
+                for (int j = 0; j < 4; ++j) {
+                    const long long col = col0 + 4 * tx + j;
+                    if (col >= col_end || col >= a.out_features) continue;
+                    OutT value = cascade_finish(acc[e][j]);
+                    if (bias) value = add_rn(value, (OutT)bias[col]);
+                    out[vec * a.ldo + col] = value;
+                }
             }
-        }
-    }
-    OutT* out = static_cast<OutT*>(a.out);
-    const ScaleT* bias = static_cast<const ScaleT*>(a.bias);
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-        const long long vec = v0 + ty + 16 * e;
-        if (vec >= a.n) continue;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const long long col = col0 + 4 * tx + j;
-            if (col >= col_end || col >= a.out_features) continue;
-            OutT value = cascade_finish(acc[e][j]);
-            if (bias) value = add_rn(value, (OutT)bias[col]);
-            out[vec * a.ldo + col] = value;
         }
     }
 }
@@ -787,14 +802,19 @@ mf_status launch_ideal_t(const mf_config& c, const MMArgs& a, cudaStream_t st, T
     const long long full = (long long)MR - MR % (1LL << power);
     const size_t smem = ideal_smem(c);
     const long long cols = (long long)(a.tile_end - a.tile_begin) * c.cols;
-    dim3 grid((unsigned)((a.n + IDEAL_TV - 1) / IDEAL_TV), (unsigned)((cols + IDEAL_TC - 1) / IDEAL_TC));
+    const int grid_x = (int)((a.n + IDEAL_TV - 1) / IDEAL_TV), grid_y = (int)((cols + IDEAL_TC - 1) / IDEAL_TC);
+    // A filtered launch (exact rerun of flagged tiles, usually none) uses at most 4 CTAs
+    // per SM stepping over the filter's tiles.
+    const long long filter_tiles = (long long)filter.row_tiles * filter.col_tiles;
+    dim3 grid = filter.flags ? dim3((unsigned)(filter_tiles < 148 * 4 ? filter_tiles : 148 * 4))
+                             : dim3((unsigned)grid_x, (unsigned)grid_y);
     const bool small_totals = reconstruction_bound(c) < 2147483647.0;
 #define MF_IDEAL(CODE, TOT)                                                                          \
     do {                                                                                             \
         auto kern = ideal_kernel<CODE, TOT, OutT, ScaleT>;                                           \
         MF_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), \
                       "ideal kernel smem attribute");                                                \
-        kern<<<grid, THREADS, smem, st>>>(L, a, power, full, filter);                                 \
+        kern<<<grid, THREADS, smem, st>>>(L, a, power, full, filter, grid_x, grid_y);                 \
     } while (0)
     if (c.wide_codes) {
         if (small_totals) MF_IDEAL(long long, int); else MF_IDEAL(long long, long long);
@@ -945,7 +965,8 @@ mf_status generic_ideal_tiles(const mf_config& c, const MMArgs& a, const unsigne
         set_error("tile filter %dx%d is not a multiple of the generic tile", rows, cols);
         return MF_ERR_INVALID;
     }
-    const TileFilter filter{flags, rows, cols, row_tiles};
+    const long long width = (long long)(a.tile_end - a.tile_begin) * c.cols;
+    const TileFilter filter{flags, rows, cols, row_tiles, (int)((width + cols - 1) / cols)};
     return c.wide ? launch_ideal_t<double, double>(c, a, st, filter) : launch_ideal_t<float, float>(c, a, st, filter);
 }
 

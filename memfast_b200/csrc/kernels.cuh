@@ -87,6 +87,10 @@ mf_status tc_make_map(CUtensorMap* map, const void* base, CUtensorMapDataType ty
                       CUtensorMapSwizzle swizzle);
 mf_status tc_error_word(unsigned** word);
 mf_status tc_take_error(unsigned* code);
+mf_status tc_stage_error(unsigned* host_word, cudaStream_t st);
+// Registers per thread of `kernel` as launched, with its dynamic shared memory
+// raised to `smem` bytes (queried and set once per kernel and device).
+mf_status kernel_setup(const void* kernel, size_t smem, int* regs);
 
 // tcgen05 / TMEM fast path with FP8 digit planes (ideal INT8 configurations, tc_ideal.cu).
 bool tc_eligible(const mf_config& c, int32_t m);

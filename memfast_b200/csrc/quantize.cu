@@ -140,6 +140,32 @@ __device__ __forceinline__ int64_t quantise(Acc x, Acc scale, const QuantSpec& s
     return (int64_t)q & s.mask;
 }
 
+// FP32 computes codes of at most 8 bits (wider codes and BFP compute in FP64), so the
+// clamped value converts through int32 (NaN converts to 0 either way).
+template <>
+__device__ __forceinline__ int64_t quantise<float>(float x, float scale, const QuantSpec& s) {
+    float q = rintf(__fdiv_rn(x, scale));
+    if (q < (float)s.lower) q = (float)s.lower;
+    if (q > (float)s.upper) q = (float)s.upper;
+    return (int64_t)(__float2int_rz(q) & (int)s.mask);
+}
+
+// quantise<float> for codes of at most 8 bits without a division per value:
+// q = x * fl(1/scale) is within |q| * 2^-23 of x / scale, and its nearest integer
+// can differ from the reference's rint(fl(x / scale)) only when q lies within that
+// distance of a half-integer (|q| <= 256 here keeps it below 2^-13); those values
+// are divided exactly.  q + 1.5 * 2^23 rounds half to even into the low mantissa
+// bits, whose low byte is the two's-complement code (NaN gives 0, as in quantise).
+__device__ __forceinline__ uint32_t code8(float x, float scale, float inv, const QuantSpec& s) {
+    constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+    float q = __fmul_rn(x, inv);
+    const float f = __fsub_rn(q, __fsub_rn(__fadd_rn(q, kMagic), kMagic));
+    if (fabsf(__fsub_rn(fabsf(f), 0.5f)) < 1.220703125e-4f) q = __fdiv_rn(x, scale);
+    if (q < (float)s.lower) q = (float)s.lower;
+    if (q > (float)s.upper) q = (float)s.upper;
+    return (uint32_t)__float_as_int(__fadd_rn(q, kMagic)) & (uint32_t)s.mask;
+}
+
 // Input codes: [n, m*R] (zero beyond k).
 template <typename Acc, typename CodeT>
 __global__ void input_code_kernel(View v, GroupGrid g, const Acc* maxima, const Acc* fixed,
@@ -175,7 +201,17 @@ __global__ void input_rowgroup_kernel(const float* x, int64_t n, int64_t k, int6
     for (int64_t team = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / T;
          __any_sync(0xFFFFFFFFu, team < teams); team += stride) {
         const bool active = team < teams;
-        const int64_t r = active ? team / groups_per_row : 0, j = active ? team % groups_per_row : 0;
+        int64_t r = 0, j = 0;
+        if (active) {
+            if (teams <= 0xFFFFFFFFll) {   // 32-bit division where the index fits
+                const uint32_t t32 = (uint32_t)team, g32 = (uint32_t)groups_per_row;
+                r = t32 / g32;
+                j = t32 - (uint32_t)r * g32;
+            } else {
+                r = team / groups_per_row;
+                j = team % groups_per_row;
+            }
+        }
         const int64_t c = j * GC + 4 * lane_in_team;
         float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         const float* row = x + r * ldx;
@@ -194,10 +230,11 @@ __global__ void input_rowgroup_kernel(const float* x, int64_t n, int64_t k, int6
 #pragma unroll
         for (int off = T / 2; off > 0; off >>= 1) best = fmaxf(best, __shfl_xor_sync(0xFFFFFFFFu, best, off, T));
         const float scale = group_scale<float>(best, s);
+        const float inv = __frcp_rn(scale);
         uint32_t word = 0;
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-            if (c + e < k) word |= (uint32_t)(quantise<float>(v[e], scale, s) & 0xFF) << (8 * e);
+            if (c + e < k) word |= (code8(v[e], scale, inv, s) & 0xFFu) << (8 * e);
         if (!active) continue;
         *reinterpret_cast<uint32_t*>(codes + r * padded_cols + c) = word;
         if (lane_in_team == 0 && j < nc) maxima[r * nc + j] = best;
@@ -271,24 +308,39 @@ __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_
         }
         maxima[j * O + o] = best;
         const float scale = group_scale<float>(best, s);
+        const float inv = __frcp_rn(scale);
         const int64_t t = o / C, c = o % C;
-        // Array and row of k, stepped along the group (no division per element).
+        // Array and row of k, stepped along the group (no division or 64-bit product
+        // per element): dst points at packed[arr, t, rr, c].
         int64_t arr = k0 / R;
         int rr = (int)(k0 - arr * R);
-        uint32_t word = 0;
+        uint8_t* dst = packed + ((arr * p + t) * R + rr) * C + c;
+        const int64_t next_array = (p - 1) * R * C;   // from row R-1 of one array to row 0 of the next
+        // K-major codes leave in 16-byte stores (4 words) where the 16 bytes are inside
+        // the padded K and aligned, else word by word: a 4-byte store per word would
+        // cost the memory system one partial-sector write per word.
+        uint32_t words[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int r = 0; r < GR; ++r) {
             const int64_t k = k0 + r;
-            const uint32_t code = k < K ? (uint32_t)(quantise<float>(v[r], scale, s) & 0xFF) : 0u;
-            if (k < kpad) packed[((arr * p + t) * R + rr) * C + c] = (uint8_t)code;
+            const uint32_t code = k < K ? (code8(v[r], scale, inv, s) & 0xFFu) : 0u;
+            if (k < kpad) *dst = (uint8_t)code;
+            dst += C;
             if (++rr == R) {
                 rr = 0;
-                ++arr;
+                dst += next_array;
             }
-            word |= code << (8 * (r & 3));
-            if ((r & 3) == 3) {
-                if (kmajor && k < kpad) *reinterpret_cast<uint32_t*>(kmajor + o * kpad + k - 3) = word;
-                word = 0;
+            words[(r >> 2) & 3] |= code << (8 * (r & 3));
+            if ((r & 15) == 15 && kmajor) {
+                uint8_t* dst = kmajor + o * kpad + k - 15;
+                if (k < kpad && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(words[0], words[1], words[2], words[3]);
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        if (k - 15 + 4 * q + 3 < kpad) *reinterpret_cast<uint32_t*>(dst + 4 * q) = words[q];
+                }
+                words[0] = words[1] = words[2] = words[3] = 0;
             }
         }
     }

@@ -4,6 +4,10 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -97,7 +101,51 @@ mf_status tc_make_map(CUtensorMap* map, const void* base, CUtensorMapDataType ty
 }
 
 mf_status tc_error_word(unsigned** word) {
-    MF_CHECK_CUDA(cudaGetSymbolAddress((void**)word, g_tc_error), "error symbol");
+    // The symbol's address per device, looked up once.
+    static unsigned* cached[64] = {};
+    int dev = 0;
+    MF_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev < 0 || dev >= 64) {
+        MF_CHECK_CUDA(cudaGetSymbolAddress((void**)word, g_tc_error), "error symbol");
+        return MF_OK;
+    }
+    if (!cached[dev]) MF_CHECK_CUDA(cudaGetSymbolAddress((void**)&cached[dev], g_tc_error), "error symbol");
+    *word = cached[dev];
+    return MF_OK;
+}
+
+mf_status kernel_setup(const void* kernel, size_t smem, int* regs) {
+    // (kernel, device) -> (registers at launch, dynamic shared memory opted in): the
+    // attribute calls cost microseconds of host time, so each is made once.
+    static std::mutex lock;
+    static std::map<std::pair<const void*, int>, std::pair<int, size_t>> known;
+    int dev = 0;
+    MF_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    const auto key = std::make_pair(kernel, dev);
+    {
+        std::lock_guard<std::mutex> guard(lock);
+        auto it = known.find(key);
+        if (it != known.end() && it->second.second >= smem) {
+            *regs = it->second.first;
+            return MF_OK;
+        }
+    }
+    cudaFuncAttributes attr;
+    MF_CHECK_CUDA(cudaFuncGetAttributes(&attr, kernel), "kernel attributes");
+    MF_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                  "kernel shared-memory attribute");
+    std::lock_guard<std::mutex> guard(lock);
+    known[key] = std::make_pair(attr.numRegs, smem);
+    *regs = attr.numRegs;
+    return MF_OK;
+}
+
+mf_status tc_stage_error(unsigned* host_word, cudaStream_t st) {
+    unsigned* word = nullptr;
+    mf_status r = tc_error_word(&word);
+    if (r) return r;
+    MF_CHECK_CUDA(cudaMemcpyAsync(host_word, word, sizeof(unsigned), cudaMemcpyDeviceToHost, st),
+                  "stage device error");
     return MF_OK;
 }
 

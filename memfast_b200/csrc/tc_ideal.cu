@@ -696,18 +696,19 @@ static mf_status launch_tc(const CUtensorMap& mx, const CUtensorMap& mw, const C
                            const CUtensorMap& mws, const tc::Args& args, dim3 grid, cudaStream_t st) {
     const size_t smem = sizeof(tc::Smem) + 1024;
     auto kern = tc::tc_ideal_kernel<NA, NWA, NWC>;
-    cudaFuncAttributes attr;
-    MF_CHECK_CUDA(cudaFuncGetAttributes(&attr, kern), "tc kernel attributes");
+    int regs = 0;
+    {
+        const mf_status r = kernel_setup(reinterpret_cast<const void*>(kern), smem, &regs);
+        if (r) return r;
+    }
     // Registers are allocated per thread in multiples of 8.
-    const long long pool = (long long)((attr.numRegs + 7) / 8 * 8) * tc::THREADS;
+    const long long pool = (long long)((regs + 7) / 8 * 8) * tc::THREADS;
     const long long split = 128LL * tc::REG_LOW + 32LL * tc::EPI_WARPS * tc::REG_HIGH;
     if (split > pool) {
         set_error("tcgen05 kernel launched with %d registers/thread cannot host the %d/%d register split",
-                  attr.numRegs, tc::REG_LOW, tc::REG_HIGH);
+                  regs, tc::REG_LOW, tc::REG_HIGH);
         return MF_ERR_RESOURCE;
     }
-    MF_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                  "tc smem attribute");
     kern<<<grid, tc::THREADS, smem, st>>>(mx, mw, mxs, mws, args);
     MF_LAUNCH_CHECK("tc_ideal_kernel");
     return MF_OK;

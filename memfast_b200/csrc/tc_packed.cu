@@ -463,18 +463,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                             }
                         }
                     }
-                    // fl(fl(T * xs) * ws) pushed into cascade level 0 for read i: |T| < 2^22,
-                    // so 1.5 * 2^23 + T is exact and subtracting 1.5 * 2^23 gives float(T).
-                    // Packed round-to-nearest multiplies, then SCALAR adds (a packed multiply
-                    // followed by a packed add was observed to round once, as an FMA, which
-                    // the reference does not).
+                    // fl(fl(T * xs) * ws) pushed into cascade level 0 for read i (|T| < 2^22:
+                    // float(T) is exact).  Packed round-to-nearest multiplies, then SCALAR
+                    // adds (a packed multiply followed by a packed add was observed to round
+                    // once, as an FMA, which the reference does not).
                     const float2* wsr =
                         reinterpret_cast<const float2*>(&s.ws[sb][i % SCB][j * JOBN + hc * EC + h * EH]);
 #pragma unroll
                     for (int e = 0; e < EH / 2; ++e) {
-                        float2 tf = make_float2(__int_as_float(T[2 * e] + 0x4B400000),
-                                                __int_as_float(T[2 * e + 1] + 0x4B400000));
-                        tf = __fadd2_rn(tf, make_float2(-12582912.0f, -12582912.0f));
+                        const float2 tf = make_float2(__int2float_rn(T[2 * e]), __int2float_rn(T[2 * e + 1]));
                         const float2 pr = __fmul2_rn(__fmul2_rn(tf, make_float2(xs, xs)), wsr[e]);
                         acc0[j][h * EH + 2 * e] = __fadd_rn(acc0[j][h * EH + 2 * e], pr.x);
                         acc0[j][h * EH + 2 * e + 1] = __fadd_rn(acc0[j][h * EH + 2 * e + 1], pr.y);
@@ -920,18 +917,19 @@ static mf_status launch_packed(const CUtensorMap& mx, const CUtensorMap& mw, con
                                const CUtensorMap& mws, const tp::Args& args, dim3 grid, cudaStream_t st) {
     const size_t smem = sizeof(tp::Smem) + 1024;
     auto kern = tp::packed_kernel<NCOL>;
-    cudaFuncAttributes attr;
-    MF_CHECK_CUDA(cudaFuncGetAttributes(&attr, kern), "packed kernel attributes");
+    int regs = 0;
+    {
+        const mf_status r = kernel_setup(reinterpret_cast<const void*>(kern), smem, &regs);
+        if (r) return r;
+    }
     // Registers are allocated per thread in multiples of 8.
-    const long long pool = (long long)((attr.numRegs + 7) / 8 * 8) * tp::THREADS;
+    const long long pool = (long long)((regs + 7) / 8 * 8) * tp::THREADS;
     const long long split =
         128LL * tp::REG_CTRL + 32LL * tp::XF_WARPS * tp::REG_XF + 32LL * tp::EPI_WARPS * tp::REG_EPI;
     if (split > pool) {
-        set_error("packed kernel launched with %d registers/thread cannot host its register split", attr.numRegs);
+        set_error("packed kernel launched with %d registers/thread cannot host its register split", regs);
         return MF_ERR_RESOURCE;
     }
-    MF_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                  "packed smem attribute");
     kern<<<grid, tp::THREADS, smem, st>>>(mx, mw, mxs, mws, args);
     MF_LAUNCH_CHECK("packed_kernel");
     return MF_OK;

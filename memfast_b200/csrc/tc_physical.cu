@@ -641,17 +641,18 @@ static mf_status launch_tcp(const CUtensorMap& mx, const CUtensorMap& mg, const 
     using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART>;
     const size_t smem = G::BYTES + 1024;
     auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL>;
-    cudaFuncAttributes attr;
-    MF_CHECK_CUDA(cudaFuncGetAttributes(&attr, kern), "tc physical kernel attributes");
-    const long long pool = (long long)((attr.numRegs + 7) / 8 * 8) * tcp::THREADS;
+    int regs = 0;
+    {
+        const mf_status r = kernel_setup(reinterpret_cast<const void*>(kern), smem, &regs);
+        if (r) return r;
+    }
+    const long long pool = (long long)((regs + 7) / 8 * 8) * tcp::THREADS;
     const long long split = 128LL * tcp::REG_LOW + 32LL * tcp::EPI_WARPS * tcp::REG_HIGH;
     if (split > pool) {
         set_error("tcgen05 physical kernel launched with %d registers/thread cannot host the %d/%d split",
-                  attr.numRegs, tcp::REG_LOW, tcp::REG_HIGH);
+                  regs, tcp::REG_LOW, tcp::REG_HIGH);
         return MF_ERR_RESOURCE;
     }
-    MF_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                  "tc physical smem attribute");
     kern<<<grid, tcp::THREADS, smem, st>>>(mx, mg, args);
     MF_LAUNCH_CHECK("tc_physical_kernel");
     return MF_OK;

@@ -13,6 +13,7 @@ uint8 codes (int64 beyond 8 bits) and FP32 scales (FP64 when ``Config.wide``).
 """
 
 import ctypes
+import functools
 import math
 
 import torch
@@ -34,11 +35,23 @@ def _require_cuda(tensor, name):
         raise ValueError(f"{name} must be a CUDA tensor (memfast_b200 runs on the GPU only)")
 
 
+# Quantiser scratch, one growing buffer per (device, stream): calls on one stream
+# run in order, so a buffer is reused only after the previous call's kernels.
+_SCRATCH = {}
+
+
 def _workspace(config, is_weight, rows, cols, device):
     need = ct_size(config, is_weight, rows, cols)
-    return torch.empty(max(need, 1), dtype=torch.uint8, device=device), need
+    key = (device.index, _lib.stream_of(device).value)
+    buffer = _SCRATCH.get(key)
+    if buffer is None or buffer.numel() < need:
+        if len(_SCRATCH) >= 16:
+            _SCRATCH.pop(next(iter(_SCRATCH)))
+        buffer = _SCRATCH[key] = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
+    return buffer, need
 
 
+@functools.lru_cache(maxsize=1024)
 def ct_size(config, is_weight, rows, cols):
     import ctypes as ct
 

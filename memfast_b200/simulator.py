@@ -17,6 +17,7 @@ CUDA device and fails loudly otherwise.
 """
 
 import ctypes as ct
+import functools
 import hashlib
 import itertools
 import json
@@ -49,6 +50,31 @@ ResourceError = _lib.ResourceError
 
 _GRID_ARRAYS = (1, 2, 4, 8, 16, 32, 64)
 _GRID_KERNELS = (1, 2)
+
+
+@functools.lru_cache(maxsize=4096)
+def _workspace_bytes(config, n, m, p, schedule):
+    """mf_sliced_mm_workspace for (config, n, m, p, schedule items), cached."""
+    size = ct.c_size_t()
+    native = _lib.schedule(**dict(schedule))
+    _lib.check(
+        _lib.load().mf_sliced_mm_workspace(_lib.native_config(config), ct.byref(native), n, m, p, 0, p,
+                                           ct.byref(size)),
+        "mf_sliced_mm_workspace",
+    )
+    return size.value
+
+
+@functools.lru_cache(maxsize=1024)
+def _kmajor_bytes(config, m, p, schedule):
+    """K-major weight copy bytes of the schedule's kernel (mf_query), cached."""
+    resources = _lib.MFResources()
+    native = _lib.schedule(**dict(schedule))
+    _lib.check(
+        _lib.load().mf_query(_lib.native_config(config), ct.byref(native), 1, m, p, ct.byref(resources)),
+        "mf_query",
+    )
+    return resources.kmajor_bytes
 
 
 def default_schedule(config):
@@ -114,6 +140,24 @@ def check_device_error():
     """Raise if a bounded device-side wait inside a kernel gave up (synchronises)."""
     code = ct.c_uint32()
     _lib.check(_lib.load().mf_take_device_error(ct.byref(code)), "device-side wait")
+
+
+_STAGED_WORDS = {}
+
+
+def stage_device_error(device):
+    """Enqueue a copy of the device error word into a pinned host word (per device and
+    stream) and return that word: read it after the caller's next synchronisation of
+    the current stream, and call check_device_error() when it is non-zero."""
+    stream = _lib.stream_of(device)
+    key = (device.index, stream.value)
+    word = _STAGED_WORDS.get(key)
+    if word is None:
+        if len(_STAGED_WORDS) >= 64:
+            _STAGED_WORDS.pop(next(iter(_STAGED_WORDS)))
+        word = _STAGED_WORDS[key] = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    _lib.check(_lib.load().mf_stage_device_error(word.data_ptr(), stream), "mf_stage_device_error")
+    return word
 
 
 def device_identity(device):
@@ -213,7 +257,7 @@ class Simulator:
             self.mode == "default"
             and same_tensor
             and record[1] == metadata
-            and previous.config == self.config
+            and (previous.config is self.config or previous.config == self.config)
             and previous.packed.device == self.device
             and previous.zero_correction is None
             and previous.input_scale is None
@@ -227,7 +271,7 @@ class Simulator:
             self.mode == "tuned"
             and same_tensor
             and record[1] == metadata
-            and previous.config == self.config
+            and (previous.config is self.config or previous.config == self.config)
             and previous.packed.device == self.device
             and torch.equal(previous.packed, programmed.packed)
             and torch.equal(previous.weight_scale, programmed.weight_scale)
@@ -550,14 +594,7 @@ class AnalogMatrix(nn.Module):
     # --------------------------------------------------------------- engine
     def _kmajor_size(self, m, schedule):
         """Bytes of the K-major weight copy the schedule's kernel reads (0: none)."""
-        resources = _lib.MFResources()
-        native = _lib.schedule(**schedule)
-        _lib.check(
-            _lib.load().mf_query(_lib.native_config(self.config), ct.byref(native), 1, m, self.p,
-                                 ct.byref(resources)),
-            "mf_query",
-        )
-        return resources.kmajor_bytes
+        return _kmajor_bytes(self.config, m, self.p, tuple(sorted(schedule.items())))
 
     def _prepare_workspace(self, m, device, rows=1):
         """Reserve the persistent workspace (sized for ``rows`` vectors) when the default
@@ -602,15 +639,8 @@ class AnalogMatrix(nn.Module):
         return entry is not None and entry[1]
 
     def _workspace_size(self, n, schedule, m=None):
-        size = ct.c_size_t()
-        native = _lib.schedule(**schedule)
         m = self.packed.shape[0] if m is None else m
-        _lib.check(
-            _lib.load().mf_sliced_mm_workspace(_lib.native_config(self.config), ct.byref(native), n, m,
-                                               self.p, 0, self.p, ct.byref(size)),
-            "mf_sliced_mm_workspace",
-        )
-        return size.value
+        return _workspace_bytes(self.config, n, m, self.p, tuple(sorted(schedule.items())))
 
     def _execute(self, q, xscale, schedule, event, stable=False, *, vector_offset=0, input_flag=None,
                  input_errors=None, tiles=None, agree=None):
@@ -629,9 +659,12 @@ class AnalogMatrix(nn.Module):
         # flags: [input error code, output non-finite]; one device-to-host read.
         flags = input_flag if input_flag is not None else torch.zeros(2, dtype=torch.int32, device=q.device)
         check_finite(output, flags[1:2], 1)
+        staged = stage_device_error(q.device)
         bad, nonfinite = flags.tolist()
         if bad:
             raise ValueError((input_errors or {}).get(bad, "quantized values must be finite"))
+        if staged[0]:
+            check_device_error()
         self._finite = not nonfinite
         if agree is not None:
             self._finite = agree(self._finite)
@@ -768,7 +801,6 @@ class AnalogMatrix(nn.Module):
         if agree is not None:
             finite = agree(finite)
         output = output.to(dtype)
-        check_device_error()
         if not finite:
             raise FloatingPointError("nonfinite analog output")
         self._event += 1

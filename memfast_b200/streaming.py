@@ -34,7 +34,7 @@ import torch
 
 from .functional import _checked
 from .quantization import compute_dtype, input_tiles
-from .simulator import Simulator, check_device_error, default_schedule
+from .simulator import Simulator, check_device_error, default_schedule, stage_device_error
 
 
 _STREAMS = {}
@@ -170,10 +170,12 @@ def host_mm(a, b, *, simulator, out=None, row_offset=0, chunk_rows=None):
             copy_out.wait_event(done)
             out[r0:r1].copy_(out_dev[r0:r1], non_blocking=True)
     # One synchronisation: operands finite, product finite (and finite in A's dtype).
+    staged = stage_device_error(device)
     flags = torch.stack([bad, _nonfinite(product), _nonfinite(out_dev)]).tolist()
     copy_out.synchronize()
     compute.wait_stream(copy_out)
-    check_device_error()
+    if staged[0]:
+        check_device_error()
     if flags[0]:
         raise ValueError("A and B must be finite")
     if flags[1] and not config.wide:
