@@ -113,6 +113,7 @@ struct Smem {
     int abort;
     unsigned rare;
     int4 field[MAXCOL * MAXFIELD];                  // (shift, width mask, m, coef) of every count
+    uint8_t fieldbit[MAXCOL][32];                   // field of count block c holding bit b
 };
 static_assert(sizeof(Smem) + 1024 <= 232448, "packed kernel exceeds the 227 KB shared-memory limit");
 
@@ -203,6 +204,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     for (int idx = threadIdx.x; idx < BN * (BM + 1); idx += THREADS) (&s.acc1[0][0])[idx] = 0.0f;
+    if (threadIdx.x < MAXCOL * 32) {
+        const int c = threadIdx.x / 32, b = threadIdx.x % 32;
+        uint8_t holder = 0;
+        for (int f = 0; f < P.nfield[c]; ++f) {
+            const Field F = P.field[c][f];
+            if (b >= F.shift && b < F.shift + __popc((unsigned)F.width_mask)) holder = (uint8_t)f;
+        }
+        s.fieldbit[c][b] = holder;
+    }
     if (warp == 0 && lane == 0) {
         prefetch_map(&map_x);
         prefetch_map(&map_w);
@@ -435,30 +445,23 @@ __global__ void __launch_bounds__(THREADS, 1)
                             uint32_t acc = 0;
 #pragma unroll
                             for (int e = 0; e + 1 < EH; e += 2) acc = or3(acc, vc[c][e], vc[c][e + 1]);
-                            o[c] = acc;
-                            hit |= acc & P.colclip[c];
+                            o[c] = acc & P.colclip[c];
+                            hit |= o[c];
                         }
                         if (__any_sync(0xFFFFFFFFu, hit != 0)) {
-                            // Counts that clip somewhere in the warp, one bit each, then
-                            // T += -s_a s_w * max(D - m, 0) for those counts only (one loop
-                            // body keeps the hot code small).
-                            uint32_t fire = 0;
+                            // Per count block, the clip bits set anywhere in the warp name the
+                            // counts that clip; T += -s_a s_w * max(D - m, 0) for those only.
 #pragma unroll
-                            for (int c = 0; c < NCOL; ++c)
+                            for (int c = 0; c < NCOL; ++c) {
+                                uint32_t fired = __reduce_or_sync(0xFFFFFFFFu, o[c]);
+                                while (fired) {
+                                    const int4 F = s.field[c * MAXFIELD + s.fieldbit[c][__ffs(fired) - 1]];
+                                    fired &= ~((uint32_t)F.y << F.x);
 #pragma unroll
-                                for (int f = 0; f < MAXFIELD; ++f)
-                                    fire |= (uint32_t)((o[c] & P.field[c][f].clip) != 0) << (c * MAXFIELD + f);
-                            fire = __reduce_or_sync(0xFFFFFFFFu, fire);
-                            while (fire) {
-                                const int k = __ffs(fire) - 1;
-                                fire &= fire - 1;
-                                const int c = k / MAXFIELD;
-                                const int4 F = s.field[k];
-#pragma unroll
-                                for (int e = 0; e < EH; ++e) {
-                                    const uint32_t v = c == 0 ? vc[0][e] : c == 1 ? vc[NCOL > 1 ? 1 : 0][e] : vc[NCOL - 1][e];
-                                    const int d = (int)((v >> F.x) & (uint32_t)F.y);
-                                    T[e] += F.w * __viaddmax_s32(d, -F.z, 0);
+                                    for (int e = 0; e < EH; ++e) {
+                                        const int d = (int)((vc[c][e] >> F.x) & (uint32_t)F.y);
+                                        T[e] += F.w * __viaddmax_s32(d, -F.z, 0);
+                                    }
                                 }
                             }
                         }
