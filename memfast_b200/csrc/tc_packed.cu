@@ -95,7 +95,7 @@ static_assert(REG_EPI >= 64 && REG_EPI <= 256, "epilogue register share out of r
 static_assert(128 * REG_CTRL + 32 * XF_WARPS * REG_XF + 32 * EPI_WARPS * REG_EPI <= THREADS * LAUNCH_REGS,
               "register split exceeds the launch pool");
 static_assert(UNITS * UNIT_COLS <= 512, "TMEM holds 512 columns");
-static_assert(EC % EH == 0, "epilogue slices");
+static_assert(EC % EH == 0 && EH >= 4 && EH % 2 == 0, "epilogue slices");
 
 struct Smem {
     uint8_t x[STAGES][TILE];                        // TMA: activation codes [128 rows][32 B]
@@ -438,22 +438,25 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int e = 0; e < EH; ++e) T[e] = (int)vb[e];
                     if (NCOL > 0) {
                         // Exact clip test: some D of the warp exceeds its m iff a clip bit is set.
+                        // o[c]: OR of block c's columns; hit = OR of (o[c] & clip bits), one
+                        // three-input logic operation per block.
                         uint32_t o[NCOL > 0 ? NCOL : 1];
                         uint32_t hit = 0;
 #pragma unroll
                         for (int c = 0; c < NCOL; ++c) {
-                            uint32_t acc = 0;
+                            uint32_t acc = or3(vc[c][0], vc[c][1], vc[c][2]);
 #pragma unroll
-                            for (int e = 0; e + 1 < EH; e += 2) acc = or3(acc, vc[c][e], vc[c][e + 1]);
-                            o[c] = acc & P.colclip[c];
-                            hit |= o[c];
+                            for (int e = 3; e + 1 < EH; e += 2) acc = or3(acc, vc[c][e], vc[c][e + 1]);
+                            acc |= vc[c][EH - 1];
+                            o[c] = acc;
+                            hit = (acc & P.colclip[c]) | hit;
                         }
                         if (__any_sync(0xFFFFFFFFu, hit != 0)) {
                             // Per count block, the clip bits set anywhere in the warp name the
                             // counts that clip; T += -s_a s_w * max(D - m, 0) for those only.
 #pragma unroll
                             for (int c = 0; c < NCOL; ++c) {
-                                uint32_t fired = __reduce_or_sync(0xFFFFFFFFu, o[c]);
+                                uint32_t fired = __reduce_or_sync(0xFFFFFFFFu, o[c] & P.colclip[c]);
                                 while (fired) {
                                     const int4 F = s.field[c * MAXFIELD + s.fieldbit[c][__ffs(fired) - 1]];
                                     fired &= ~((uint32_t)F.y << F.x);
