@@ -28,7 +28,7 @@
 //
 // Scope: FP32 currents and epilogue (not Config.wide / precise_currents), no
 // voltage noise, read noise only in the shared mode (it is folded into G' per
-// read event by restore_split_kernel), input digits of at most 3 bits, 32- or
+// read event by b_operand_kernel), input digits of at most 3 bits, 32- or
 // 64-row reads, at most 256 reads per output.  Everything else runs on the SIMT
 // kernels in generic.cu.
 //

@@ -33,7 +33,7 @@ import threading
 import torch
 
 from .functional import _checked
-from .quantization import compute_dtype, input_tiles
+from .quantization import check_finite, input_tiles
 from .simulator import Simulator, check_device_error, default_schedule, stage_device_error
 
 
@@ -52,14 +52,10 @@ def _helper_streams(device):
         return _STREAMS[key]
 
 
-def _nonfinite(tensor, dtype=None):
-    """Device bool: ``tensor`` holds a non-finite value (in ``dtype`` when given)."""
-    if tensor.numel() == 0:
-        return torch.zeros((), dtype=torch.bool, device=tensor.device)
-    extremes = torch.stack(torch.aminmax(tensor))
-    if dtype is not None:
-        extremes = extremes.to(dtype)
-    return ~torch.isfinite(extremes).all()
+def _flag_nonfinite(tensor, flag, narrowed):
+    """Enqueue the finiteness check of ``tensor`` into the device word ``flag`` (set to 1
+    if a value is not finite, or, when ``narrowed``, not finite once narrowed to FP32)."""
+    check_finite(tensor, flag, 1, 1 if narrowed else 0)
 
 
 def _check_operands(a, b, simulator, out):
@@ -136,26 +132,27 @@ def host_mm(a, b, *, simulator, out=None, row_offset=0, chunk_rows=None):
             arrived.append(event)
 
     compute.wait_event(b_arrived)
-    narrowed_w = compute_dtype(config, config.weight_bits)
-    bad = _nonfinite(b_dev, None if _checked(b, config, config.weight_bits) else narrowed_w)
+    # Device words: [operand not finite, product not finite, output not finite].
+    flags = torch.zeros(3, dtype=torch.int32, device=device)
+    _flag_nonfinite(b_dev, flags[0:1], not _checked(b, config, config.weight_bits))
     matrix = simulator._matrix_for(b, checked=True, rows=min(chunk_rows, n), program=b_dev)
     schedule = default_schedule(config)
     event_index = matrix._event
     if event_index >= 2**63:
         raise OverflowError("read-event counter exhausted")
-    narrowed_a = None if _checked(a, config, config.activation_bits) else compute_dtype(config, config.activation_bits)
+    narrowed_a = not _checked(a, config, config.activation_bits)
     wide = torch.float64 if config.wide else torch.float32
     product = out_dev if out_dev.dtype == wide else torch.empty((n, o), dtype=wide, device=device)
     programmed = torch.cuda.Event()
     programmed.record(compute)
     second.wait_event(programmed)
-    finished, flags = [], {compute: [bad], second: []}
+    finished = []
     for index, ((r0, r1), event) in enumerate(zip(spans, arrived)):
         stream = compute if index % 2 == 0 else second
         with torch.cuda.stream(stream):
             stream.wait_event(event)
             rows = a_dev[r0:r1]
-            flags[stream].append(_nonfinite(rows, narrowed_a))
+            _flag_nonfinite(rows, flags[0:1], narrowed_a)
             q, xscale = input_tiles(rows, config, matrix.input_scale, checked=True)
             matrix._launch(q, xscale, schedule, event_index, vector_offset=row_offset + r0, output=product[r0:r1])
             if product is not out_dev:
@@ -164,14 +161,16 @@ def host_mm(a, b, *, simulator, out=None, row_offset=0, chunk_rows=None):
             done.record(stream)
             finished.append(done)
     compute.wait_stream(second)
-    bad = torch.stack([flag.reshape(()) for flag in flags[compute] + flags[second]]).any()
     with torch.cuda.stream(copy_out):
         for (r0, r1), done in zip(spans, finished):
             copy_out.wait_event(done)
             out[r0:r1].copy_(out_dev[r0:r1], non_blocking=True)
     # One synchronisation: operands finite, product finite (and finite in A's dtype).
     staged = stage_device_error(device)
-    flags = torch.stack([bad, _nonfinite(product), _nonfinite(out_dev)]).tolist()
+    _flag_nonfinite(product, flags[1:2], False)
+    if product is not out_dev:
+        _flag_nonfinite(out_dev, flags[2:3], False)
+    flags = flags.tolist()
     copy_out.synchronize()
     compute.wait_stream(copy_out)
     if staged[0]:
