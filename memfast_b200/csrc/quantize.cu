@@ -299,13 +299,15 @@ __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t j = i / O, o = i % O, k0 = j * GR;
-        float v[GR];
+        // Two passes over the group: the maximum, then the codes from a second read
+        // of the same lines (still in L1), so that few registers hold values and
+        // more warps hide the memory latency.
+        const float* col = b + k0 * ldb + o;
+        const int rows = K - k0 < GR ? (int)(K - k0) : GR;
         float best = 0.0f;
-#pragma unroll
-        for (int r = 0; r < GR; ++r) {
-            v[r] = k0 + r < K ? b[(k0 + r) * ldb + o] : 0.0f;
-            best = fmaxf(best, fabsf(v[r]));
-        }
+#pragma unroll 8
+        for (int r = 0; r < GR; ++r)
+            if (r < rows) best = fmaxf(best, fabsf(__ldg(col + r * ldb)));
         maxima[j * O + o] = best;
         const float scale = group_scale<float>(best, s);
         const float inv = __frcp_rn(scale);
@@ -320,10 +322,10 @@ __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_
         // the padded K and aligned, else word by word: a 4-byte store per word would
         // cost the memory system one partial-sector write per word.
         uint32_t words[4] = {0, 0, 0, 0};
-#pragma unroll
+#pragma unroll 16
         for (int r = 0; r < GR; ++r) {
             const int64_t k = k0 + r;
-            const uint32_t code = k < K ? (code8(v[r], scale, inv, s) & 0xFFu) : 0u;
+            const uint32_t code = r < rows ? (code8(__ldg(col + r * ldb), scale, inv, s) & 0xFFu) : 0u;
             if (k < kpad) *dst = (uint8_t)code;
             dst += C;
             if (++rr == R) {
