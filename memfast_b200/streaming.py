@@ -20,7 +20,9 @@ noise draws are addressed by its global vector index
 (memfast/reference.py:81-115), so the chunked product equals the one-call
 product bit for bit.  Other input groupings, tuned mode, and a product that
 needs the FP64 rerun (non-finite outputs, simulator.py:614-615) take the plain
-path: one copy in, the device ``mm``, one copy out.  Finiteness of A and B is
+path: one copy in, the device ``mm``, one copy out; so do nonideal devices, whose
+per-launch conductance restore would be repeated for every chunk while their
+product outlasts the copies many times over.  Finiteness of A and B is
 checked on the device and read with the output check in one synchronisation
 at the end; errors are the reference's (``ValueError`` for non-finite operands,
 ``FloatingPointError`` for a non-finite result), raised before the read event
@@ -101,7 +103,11 @@ def host_mm(a, b, *, simulator, out=None, row_offset=0, chunk_rows=None):
         out = torch.empty((n, o), dtype=a.dtype, pin_memory=a.is_pinned())
     if n == 0 or o == 0 or k == 0:
         return _plain(a, b, simulator, out, row_offset)
-    chunkable = config.input_quant_gran[0] == 1 and simulator.mode == "default"
+    # Nonideal products restore every conductance once per launch (noise of the
+    # read event), a cost that does not shrink with the rows of a chunk, and their
+    # compute dwarfs the PCIe copies: they take the plain path.
+    chunkable = (config.input_quant_gran[0] == 1 and simulator.mode == "default"
+                 and config.nonidealities.ideal)
     if not chunkable:
         return _plain(a, b, simulator, out, row_offset)
     if chunk_rows is None:
