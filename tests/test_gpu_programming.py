@@ -193,3 +193,43 @@ def test_workspace_is_reused_and_invalidated(mf):
     stream.synchronize()
     assert torch.equal(other, first)
     check_device_error()
+
+
+def near_half_integers(groups, seed):
+    """[groups, 32] FP32 values whose quotients by their group's scale sit on or next
+    to half-integers: element 0 fixes the group maximum M = 127 s, the others are
+    fl((k + 1/2) * fl(M / 127)) and their FP32 neighbours, so that rounding the
+    quotient to an integer depends on its last bits (the quantisers' exact path)."""
+    rng = np.random.default_rng(seed)
+    s = np.float32(2.0) ** rng.integers(-12, 4, size=groups).astype(np.float32)
+    s = (s * (1 + rng.random(groups, dtype=np.float32))).astype(np.float32)
+    top = (np.float32(127) * s).astype(np.float32)
+    scale = (top / np.float32(127)).astype(np.float32)
+    k = rng.integers(-127, 127, size=(groups, 31)).astype(np.float32)
+    x = ((k + np.float32(0.5)) * scale[:, None]).astype(np.float32)
+    step = rng.integers(-1, 2, size=x.shape)
+    x = np.where(step < 0, np.nextafter(x, np.float32(-np.inf)),
+                 np.where(step > 0, np.nextafter(x, np.float32(np.inf)), x))
+    x = np.clip(x, -top[:, None], top[:, None]).astype(np.float32)
+    return np.concatenate([top[:, None], x], axis=1)
+
+
+def test_quantisers_round_near_half_integers_like_the_oracle(mf):
+    """The one-pass FP32 quantisers multiply by the reciprocal scale and divide exactly
+    only near half-integers; values placed there round as the reference's division."""
+    from memfast_b200.quantization import input_tiles, weight_tiles
+
+    config = make_config(mf, "int8_g32")
+    rows, k = 96, 256
+    a = near_half_integers(rows * k // 32, 21).reshape(rows, k)
+    codes, xscale = input_tiles(torch.from_numpy(a).cuda(), config)
+    want_codes, want_xscale = Q.input_tiles(a, config)
+    assert np.array_equal(codes.cpu().numpy().astype(np.int64), want_codes)
+    assert np.array_equal(xscale.cpu().numpy().view(np.uint32), want_xscale.view(np.uint32))
+    o = 160
+    b = near_half_integers(o * k // 32, 22).reshape(o, k // 32, 32).transpose(1, 2, 0).reshape(k, o)
+    b = np.ascontiguousarray(b)
+    packed, wscale, _ = weight_tiles(torch.from_numpy(b).cuda().T, config)
+    want_packed, want_wscale = Q.weight_tiles(b.T, config)
+    assert np.array_equal(packed.cpu().numpy().astype(np.int64), want_packed)
+    assert np.array_equal(wscale.cpu().numpy(), want_wscale)
