@@ -191,7 +191,7 @@ __global__ void input_code_kernel(View v, GroupGrid g, const Acc* maxima, const 
 // (up to m * R) get code 0 and do not enter any maximum.
 template <int T>
 __global__ void input_rowgroup_kernel(const float* x, int64_t n, int64_t k, int64_t ldx, int64_t padded_cols,
-                                      int64_t nc, QuantSpec s, float* maxima, uint8_t* codes) {
+                                      int64_t nc, QuantSpec s, float* maxima, uint8_t* codes, float* xscale) {
     constexpr int GC = 4 * T;
     const int64_t groups_per_row = padded_cols / GC;
     const int64_t teams = n * groups_per_row;
@@ -237,7 +237,16 @@ __global__ void input_rowgroup_kernel(const float* x, int64_t n, int64_t k, int6
             if (c + e < k) word |= (code8(v[e], scale, inv, s) & 0xFFu) << (8 * e);
         if (!active) continue;
         *reinterpret_cast<uint32_t*>(codes + r * padded_cols + c) = word;
-        if (lane_in_team == 0 && j < nc) maxima[r * nc + j] = best;
+        if (lane_in_team == 0 && j < nc) {
+            maxima[r * nc + j] = best;
+            // Groups as wide as a read (xscale non-null): group j is read j's scale, and
+            // reads past k take the last group's, as input_scale_kernel gives them.
+            if (xscale) {
+                xscale[r * groups_per_row + j] = scale;
+                if (j == nc - 1)
+                    for (int64_t jj = nc; jj < groups_per_row; ++jj) xscale[r * groups_per_row + jj] = scale;
+            }
+        }
     }
 }
 
@@ -292,7 +301,8 @@ __global__ void weight_code_kernel(View v, GroupGrid g, const Acc* maxima, Quant
 // for the per-read scale gather.  Padding rows and columns are zeroed by the host.
 template <int GR>
 __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_t ldb, QuantSpec s, int R, int C,
-                                    int64_t m, int64_t p, float* maxima, uint8_t* packed, uint8_t* kmajor) {
+                                    int64_t m, int64_t p, float* maxima, uint8_t* packed, uint8_t* kmajor,
+                                    float* wscale) {
     const int64_t groups = (K + GR - 1) / GR;
     const int64_t total = groups * O;
     const int64_t kpad = m * R;
@@ -311,6 +321,16 @@ __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_
         maxima[j * O + o] = best;
         const float scale = group_scale<float>(best, s);
         const float inv = __frcp_rn(scale);
+        if (wscale) {
+            // Groups of one read (wscale non-null): wscale[read j, column o]; reads past K
+            // and columns past O replicate the last group and column, as
+            // weight_scale_kernel's clamped indices give them.
+            const int64_t pc = p * C, mr = kpad / GR;
+            const int64_t last_read = j == groups - 1 ? mr : j + 1;
+            const int64_t last_col = o == O - 1 ? pc : o + 1;
+            for (int64_t jr = j; jr < last_read; ++jr)
+                for (int64_t oc = o; oc < last_col; ++oc) wscale[jr * pc + oc] = scale;
+        }
         const int64_t t = o / C, c = o % C;
         // Array and row of k, stepped along the group (no division or 64-bit product
         // per element): dst points at packed[arr, t, rr, c].
@@ -670,10 +690,13 @@ static mf_status run_input(const mf_config& c, const View& v, const GroupGrid& g
         const int64_t padded = m * c.rows;
         const int64_t lanes = n * (padded / g.gc) * team;
         const int blocks = grid_for((lanes + threads - 1) / threads * threads, threads);
+        // Per-read scales in the same pass when a group spans exactly one read.
+        const bool scales_fused = sizeof(ScaleT) == 4 && g.gc == c.read_rows && c.rows % c.read_rows == 0;
+        float* fused_xscale = scales_fused ? reinterpret_cast<float*>(xscale) : nullptr;
 #define MF_ROWGROUP(TEAM)                                                                                    \
     input_rowgroup_kernel<TEAM><<<blocks, threads, 0, stream>>>(static_cast<const float*>(v.data), n, k, v.ld, \
                                                                 padded, g.nc, s, reinterpret_cast<float*>(maxima), \
-                                                                static_cast<uint8_t*>(codes))
+                                                                static_cast<uint8_t*>(codes), fused_xscale)
         switch (team) {
             case 1: MF_ROWGROUP(1); break;
             case 2: MF_ROWGROUP(2); break;
@@ -684,6 +707,7 @@ static mf_status run_input(const mf_config& c, const View& v, const GroupGrid& g
         }
 #undef MF_ROWGROUP
         MF_LAUNCH_CHECK("input_rowgroup_kernel");
+        if (scales_fused) return MF_OK;
         input_scale_kernel<Acc, ScaleT><<<grid_for(n * m * c.reads, threads), threads, 0, stream>>>(
             v, g, maxima, fx, s, c.rows, c.read_rows, c.reads, m, static_cast<ScaleT*>(xscale));
         MF_LAUNCH_CHECK("input_scale_kernel");
@@ -859,15 +883,19 @@ mf_status program_rhs(const mf_config& c, const void* b, int dtype, int64_t k, i
         const int threads = 256;
         const int64_t work = ((k + g.gr - 1) / g.gr) * o;
         float* maxima = static_cast<float*>(workspace);
+        // Per-read weight scales in the same pass when a group spans exactly one read.
+        const bool scales_fused = g.gr == c.read_rows && c.rows % c.read_rows == 0;
+        float* fused_wscale = scales_fused ? static_cast<float*>(wscale) : nullptr;
         if (g.gr == 32)
             rhs_colgroup_kernel<32><<<grid_for(work, threads), threads, 0, stream>>>(
                 static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
-                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor));
+                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale);
         else
             rhs_colgroup_kernel<64><<<grid_for(work, threads), threads, 0, stream>>>(
                 static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
-                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor));
+                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale);
         MF_LAUNCH_CHECK("rhs_colgroup_kernel");
+        if (scales_fused) return MF_OK;
         weight_scale_kernel<float, float><<<grid_for(m * c.reads * p * c.cols, threads), threads, 0, stream>>>(
             v, g, maxima, s, c.rows, c.cols, c.read_rows, c.reads, m, p, static_cast<float*>(wscale));
         MF_LAUNCH_CHECK("weight_scale_kernel");

@@ -166,6 +166,11 @@ def _matmul(a, b, *, simulator, config, mode, cache_dir, out):
     shape = batch + (() if left_vector else (rows,)) + (() if right_vector else (columns,))
     _out(a, b, out, shape)
     engine = _engine(a, simulator, config, mode, cache_dir)
+    if (a.ndim == 2 and b.ndim == 2 and out is None and a.numel() and b.numel()
+            and not torch.is_autocast_enabled(a.device.type)):
+        # Plain rank-two product outside autocast: one programmed product, no batch
+        # bookkeeping (the general path below gives the same result).
+        return _product(a, b, engine, None, operand_code=_operand_code(a, b, engine.config))
     with torch.autocast(device_type=a.device.type, enabled=False):
         if a.numel() == 0 or b.numel() == 0 or 0 in shape:
             _operands(a, b)
