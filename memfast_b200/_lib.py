@@ -154,9 +154,27 @@ def check(status, what):
     raise RuntimeError(message)
 
 
-@functools.lru_cache(maxsize=256)
+# native_config by object identity first: hashing a Config costs about a microsecond
+# and the hot path asks several times per call.  Each entry keeps its Config alive,
+# so an id cannot be reused while its entry exists.
+_NATIVE_BY_ID = {}
+
+
 def native_config(config):
     """mf_config for a (frozen, hashable) Config; derived values as the reference derives them."""
+    entry = _NATIVE_BY_ID.get(id(config))
+    if entry is not None and entry[0] is config:
+        return entry[1]
+    native = _native_config(config)
+    if len(_NATIVE_BY_ID) >= 256:
+        _NATIVE_BY_ID.pop(next(iter(_NATIVE_BY_ID)))
+    _NATIVE_BY_ID[id(config)] = (config, native)
+    return native
+
+
+@functools.lru_cache(maxsize=256)
+def _native_config(config):
+    """Build the mf_config (equal Configs share one)."""
     ni = config.nonidealities
     c = MFConfig()
     c.abi_version = ABI_VERSION
