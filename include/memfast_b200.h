@@ -205,6 +205,15 @@ mf_status mf_quantize_conv_input(const mf_config* cfg, const mf_conv2d* conv, co
 mf_status mf_check_finite(const void* x, int32_t x_dtype, int64_t n, uint32_t code, uint32_t narrow_code,
                           uint32_t* flag, void* stream);
 
+/* The operand checks of one product in one call (memfast/functional.py:50-53 with
+ * quantization.py:12-15): clears flags[0..flag_words) on `stream`, then checks A
+ * (code 1), B (code 2, or b_narrow_code when B's FP64 values overflow FP32) and,
+ * when a_narrow_code is non-zero, A again in FP32, each as mf_check_finite into
+ * flags[0]; the first failure in that order wins. */
+mf_status mf_check_operands(const void* a, int32_t a_dtype, int64_t a_count, uint32_t a_narrow_code,
+                            const void* b, int32_t b_dtype, int64_t b_count, uint32_t b_narrow_code,
+                            uint32_t* flags, int32_t flag_words, void* stream);
+
 /* Output height and width of a convolution group; MF_ERR_INVALID for a bad geometry. */
 mf_status mf_conv_output(const mf_conv2d* conv, int64_t* out_height, int64_t* out_width);
 

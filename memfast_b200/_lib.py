@@ -88,6 +88,8 @@ _SIGNATURES = {
     "mf_quantize_conv_input": (ct.c_int, [ct.POINTER(MFConfig), ct.POINTER(MFConv2d), _VOID, ct.c_int32,
                                           _VOID, _VOID, _VOID, _VOID, _VOID, ct.c_size_t, _VOID]),
     "mf_check_finite": (ct.c_int, [_VOID, ct.c_int32, ct.c_int64, ct.c_uint32, ct.c_uint32, _VOID, _VOID]),
+    "mf_check_operands": (ct.c_int, [_VOID, ct.c_int32, ct.c_int64, ct.c_uint32, _VOID, ct.c_int32, ct.c_int64,
+                                     ct.c_uint32, _VOID, ct.c_int32, _VOID]),
     "mf_conv_output": (ct.c_int, [ct.POINTER(MFConv2d), ct.POINTER(ct.c_int64), ct.POINTER(ct.c_int64)]),
     "mf_program_weights": (ct.c_int, [ct.POINTER(MFConfig), _VOID, ct.c_int32, ct.c_int64, ct.c_int64,
                                       ct.c_int64, _VOID, _VOID, _VOID, ct.c_size_t, _VOID]),

@@ -139,6 +139,22 @@ mf_status mf_check_finite(const void* x, int32_t x_dtype, int64_t n, uint32_t co
     return check_finite(x, x_dtype, n, code, narrow_code, flag, (cudaStream_t)stream);
 }
 
+mf_status mf_check_operands(const void* a, int32_t a_dtype, int64_t a_count, uint32_t a_narrow_code,
+                            const void* b, int32_t b_dtype, int64_t b_count, uint32_t b_narrow_code,
+                            uint32_t* flags, int32_t flag_words, void* stream) {
+    if (!flags || flag_words < 1 || (!a && a_count > 0) || (!b && b_count > 0) || a_count < 0 || b_count < 0 ||
+        a_dtype < MF_F32 || a_dtype > MF_F64 || b_dtype < MF_F32 || b_dtype > MF_F64) {
+        set_error("mf_check_operands: invalid operands");
+        return MF_ERR_INVALID;
+    }
+    const cudaStream_t st = (cudaStream_t)stream;
+    MF_CHECK_CUDA(cudaMemsetAsync(flags, 0, sizeof(uint32_t) * (size_t)flag_words, st), "clear operand flags");
+    mf_status r = check_finite(a, a_dtype, a_count, 1, 0, flags, st);
+    if (!r) r = check_finite(b, b_dtype, b_count, 2, b_narrow_code, flags, st);
+    if (!r && a_narrow_code) r = check_finite(a, a_dtype, a_count, 1, a_narrow_code, flags, st);
+    return r;
+}
+
 static bool conv_geometry(const mf_conv2d* cv, int64_t* oh, int64_t* ow) {
     if (!cv || cv->batch < 0 || cv->channels < 1 || cv->height < 1 || cv->width < 1 || cv->kernel_h < 1 ||
         cv->kernel_w < 1 || cv->stride_y < 1 || cv->stride_x < 1 || cv->pad_h < 0 || cv->pad_w < 0 ||

@@ -15,6 +15,7 @@ from pathlib import Path
 
 import torch
 
+from . import _lib
 from .config import Config
 from .quantization import check_finite, compute_dtype, finite_flags
 from .simulator import Simulator
@@ -59,13 +60,22 @@ def _operand_code(a, b, config):
     """Device int32 flags [operand error, output]: the first holds 0 when A and B pass
     the checks above, else the OPERAND_ERRORS key of the first failure, checked in that
     order on the device (no synchronisation); the second is left for the output check."""
-    flags = torch.zeros(2, dtype=torch.int32, device=a.device)
     a_narrows = a.dtype == torch.float64 and compute_dtype(config, config.activation_bits) == torch.float32
     b_narrows = b.dtype == torch.float64 and compute_dtype(config, config.weight_bits) == torch.float32
-    check_finite(a, flags[:1], 1)
-    check_finite(b, flags[:1], 2, 3 if b_narrows else 0)
-    if a_narrows:
-        check_finite(a, flags[:1], 1, 3)
+    if (a.dtype not in _lib.DTYPES or b.dtype not in _lib.DTYPES or not a.is_contiguous()
+            or not b.is_contiguous()):
+        flags = torch.zeros(2, dtype=torch.int32, device=a.device)
+        check_finite(a, flags[:1], 1)
+        check_finite(b, flags[:1], 2, 3 if b_narrows else 0)
+        if a_narrows:
+            check_finite(a, flags[:1], 1, 3)
+        return flags
+    # One native call clears the flags and runs the checks in the order above.
+    flags = torch.empty(2, dtype=torch.int32, device=a.device)
+    _lib.check(_lib.load().mf_check_operands(
+        _lib.ptr(a), _lib.DTYPES[a.dtype], a.numel(), 3 if a_narrows else 0,
+        _lib.ptr(b), _lib.DTYPES[b.dtype], b.numel(), 3 if b_narrows else 0,
+        _lib.ptr(flags), 2, _lib.stream_of(a.device)), "mf_check_operands")
     return flags
 
 

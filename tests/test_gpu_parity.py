@@ -160,3 +160,9 @@ def test_nonfinite_operands_raise_without_consuming_a_read_event(mf, where):
     huge = b.double() * 1e300
     with pytest.raises(ValueError, match="finite in torch.float32"):
         sim.mm(a.double(), huge)
+    # Both operands bad: A's error, as the reference checks A first.
+    bad_a, bad_b = a.clone(), b.clone()
+    bad_a[0, 0] = float("nan")
+    bad_b[0, 0] = float("-inf")
+    with pytest.raises(ValueError, match="A must be finite"):
+        sim.mm(bad_a, bad_b)
