@@ -70,7 +70,8 @@ constexpr int MAXSLOT = 6;       // weight-plane slots per job (a plane may fill
 constexpr int MAXCOL = 3;        // packed count blocks per job
 constexpr int MAXFIELD = 3;      // counts per count block
 constexpr int MAXMMA = 6;        // plane MMAs per job
-constexpr int MAXRARE = 4;       // weight slices of rare pairs (column bounds)
+constexpr int MAXRARE = 8;       // weight slices of rare pairs (column bounds), 64-row reads
+constexpr int MAXRARE_32 = 4;    // the same for 32-row reads (keeps the transform's registers)
 constexpr int UNITS = 512 / (JOBN * (1 + MAXCOL));
 constexpr int UNIT_COLS = JOBN * (1 + MAXCOL);
 constexpr int EPI_WARPS = 16;
@@ -164,12 +165,15 @@ __device__ __forceinline__ void epilogue_barrier() {
     asm volatile("bar.sync %0, %1;" ::"n"(EPI_BARRIER), "n"(32 * EPI_WARPS) : "memory");
 }
 
-template <int NCOL>
+// H: 32-row stages per read (1 for 32-row reads, 2 for 64-row reads: both
+// stages' MMAs accumulate into the read's TMEM unit before the epilogue sees it).
+template <int NCOL, int H>
 __global__ void __launch_bounds__(THREADS, 1)
     packed_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                   const __grid_constant__ CUtensorMap map_xs, const __grid_constant__ CUtensorMap map_ws,
                   const __grid_constant__ Args args) {
     static_assert(NCOL <= MAXCOL, "too many count blocks");
+    static_assert(H == 1 || H == 2, "reads of 32 or 64 rows");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const Plan& P = args.plan;
@@ -230,8 +234,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (warp == 0 && lane == 0) {
             // ------------------------------------------------------------ producer
             int issued = 0, scissued = 0;
-            for (int i = 0; i < MR; ++i) {
-                if (i % SCB == 0) {
+            for (int stage = 0; stage < MR * H; ++stage) {
+                const int i = stage / H;
+                if (stage % H == 0 && i % SCB == 0) {
                     const int b = i / SCB, sb = b % SCRING;
                     if (!mbar_wait(&s.sc_empty[sb], ((b / SCRING) & 1) ^ 1, &s.abort, err, 21)) break;
                     mbar_expect_tx(&s.sc_full[sb], (BM + BN) * SCB * 4);
@@ -239,12 +244,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tma_load_2d(s.ws[sb], &map_ws, c0, i, &s.sc_full[sb]);
                     scissued = b + 1;
                 }
-                const int st = i % STAGES;
-                if (!mbar_wait(&s.empty[st], ((i / STAGES) & 1) ^ 1, &s.abort, err, 22)) break;
+                const int st = stage % STAGES;
+                if (!mbar_wait(&s.empty[st], ((stage / STAGES) & 1) ^ 1, &s.abort, err, 22)) break;
                 mbar_expect_tx(&s.full[st], 2 * TILE);
-                tma_load_2d(s.x[st], &map_x, i * KR, (int)n0, &s.full[st]);
-                tma_load_2d(s.w[st], &map_w, i * KR, c0, &s.full[st]);
-                issued = i + 1;
+                tma_load_2d(s.x[st], &map_x, stage * KR, (int)n0, &s.full[st]);
+                tma_load_2d(s.w[st], &map_w, stage * KR, c0, &s.full[st]);
+                issued = stage + 1;
             }
             // Every issued load lands before the CTA may exit.
             for (int i = issued - STAGES > 0 ? issued - STAGES : 0; i < issued; ++i)
@@ -277,30 +282,40 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             uint32_t u = 0, uphase = 0;
             bool ok = true;
-            for (int i = 0; i < MR && ok; ++i) {
-                const int st = i % STAGES;
-                if (!mbar_wait(&s.ready[st], (i / STAGES) & 1, &s.abort, err, 23)) break;
+            for (int stage = 0; stage < MR * H && ok; ++stage) {
+                const int st = stage % STAGES;
+                // Stage hh of a read: the first takes the read's units (waiting for the
+                // epilogue to free them) and overwrites them; later stages accumulate,
+                // and the last one hands the units to the epilogue.
+                const uint32_t hh = (uint32_t)(stage % H);
+                if (!mbar_wait(&s.ready[st], (stage / STAGES) & 1, &s.abort, err, 23)) break;
                 tc_fence_after();
                 const uint64_t dx = dx0 + st * kStageX, dw = dw0 + st * kStageX;
                 const uint64_t da = da0 + st * kStageA, dbs = db0 + st * kStageB;
+                uint32_t uj = u, ph = uphase;
 #pragma unroll
                 for (int j = 0; j < NJOB; ++j) {
-                    if (!mbar_wait(&s.unit_empty[u], uphase ^ 1, &s.abort, err, 24)) {
+                    if (hh == 0 && !mbar_wait(&s.unit_empty[uj], ph ^ 1, &s.abort, err, 24)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t buf = tmem + u * UNIT_COLS;
-                    mma_i8(buf, dx, dw + j * kJobW, id_base, 0);
+                    const uint32_t buf = tmem + uj * UNIT_COLS;
+                    mma_i8(buf, dx, dw + j * kJobW, id_base, hh != 0);
                     const uint64_t db = dbs + j * kJobB;
 #pragma unroll
                     for (int k = 0; k < MAXMMA; ++k)
-                        if (k < nmma) mma_i8(buf + t_off[k], da + a_off[k], db + b_off[k], idesc[k], acc[k]);
-                    mma_commit(&s.unit_full[u]);
-                    if (++u == UNITS) {
-                        u = 0;
-                        uphase ^= 1;
+                        if (k < nmma)
+                            mma_i8(buf + t_off[k], da + a_off[k], db + b_off[k], idesc[k], acc[k] | (hh != 0));
+                    if (hh == H - 1) mma_commit(&s.unit_full[uj]);
+                    if (++uj == UNITS) {
+                        uj = 0;
+                        ph ^= 1;
                     }
+                }
+                if (hh == H - 1) {
+                    u = uj;
+                    uphase = ph;
                 }
                 if (ok) mma_commit(&s.empty[st]);
             }
@@ -325,8 +340,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         // mask (src + width <= 8), also in the rotate's wrap-around.
         uint32_t a_rot[MAXA], a_m4[MAXA];
         uint32_t s_rot[MAXSLOT], s_m4[MAXSLOT];
-        uint32_t r_src[MAXRARE], r_m4[MAXRARE];
-        int r_lim[MAXRARE];
+        constexpr int NRARE = H > 1 ? MAXRARE : MAXRARE_32;
+        uint32_t r_src[NRARE], r_m4[NRARE];
+        int r_lim[NRARE];
+        // Rare-pair digit sums run over a whole read (both stages of a 64-row read).
+        uint32_t rsum[H > 1 ? NRARE : 1];
         const int na = P.na, nslot = P.nslot, nr = P.nrare;
 #pragma unroll
         for (int a = 0; a < MAXA; ++a) {
@@ -340,15 +358,18 @@ __global__ void __launch_bounds__(THREADS, 1)
             s_m4[q] = ((uint32_t)P.b_mask[b] << P.b_scale[b]) * 0x01010101u;
         }
 #pragma unroll
-        for (int q = 0; q < MAXRARE; ++q) {
+        for (int q = 0; q < NRARE; ++q) {
             r_src[q] = P.r_src[q];
             r_m4[q] = (uint32_t)P.r_mask[q] * 0x01010101u;
             r_lim[q] = P.r_limit[q];
         }
+#pragma unroll
+        for (int q = 0; q < (H > 1 ? NRARE : 1); ++q) rsum[q] = 0;
         bool rare = false;
-        for (int i = 0; i < MR; ++i) {
-            const int st = i % STAGES;
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s.full[st], (i / STAGES) & 1, &s.abort, err, 25))) break;
+        for (int stage = 0; stage < MR * H; ++stage) {
+            const int st = stage % STAGES;
+            const int hh = stage % H;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s.full[st], (stage / STAGES) & 1, &s.abort, err, 25))) break;
             const uint4* xrow = reinterpret_cast<const uint4*>(s.x[st] + t * KR);
             const uint4 xa = xrow[0], xb = xrow[1];
             const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
@@ -376,12 +397,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 dst[1] = make_uint4(d[4], d[5], d[6], d[7]);
             }
 #pragma unroll
-            for (int q = 0; q < MAXRARE; ++q) {
+            for (int q = 0; q < NRARE; ++q) {
                 if (q >= nr) break;
-                uint32_t sum = 0;
+                uint32_t sum = (H == 1 || hh == 0) ? 0u : rsum[H > 1 ? q : 0];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) sum = __dp4a((ww[k] >> r_src[q]) & r_m4[q], 0x01010101u, sum);
-                rare |= (int)sum > r_lim[q];
+                if (hh == H - 1) rare |= (int)sum > r_lim[q];
+                else rsum[H > 1 ? q : 0] = sum;
             }
             // Plane writes (generic proxy) must be visible to the tensor core (async proxy).
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -707,7 +729,8 @@ bool slot_layout(const Run* runs, int nrun, int nb, int* slots, int* nslot, int*
 bool base_eligible(const mf_config& c, int32_t m) {
     if (!c.ideal || !exact_integer_counts(c) || c.wide || c.wide_codes) return false;
     if (c.activation_bits != 8 || c.weight_bits != 8) return false;
-    if (c.read_rows != tp::KR || c.rows % tp::KR) return false;
+    // 32-row reads, or 64-row reads as two 32-row stages per read.
+    if ((c.read_rows != tp::KR && c.read_rows != 2 * tp::KR) || c.rows % c.read_rows) return false;
     const long long MR = (long long)m * c.reads;
     if (MR > 256 || MR % tp::SCB) return false;
     // |T| < 2^22 keeps the integer-to-float step exact.
@@ -894,7 +917,7 @@ bool tc_packed_plan(const mf_config& c, tp::Plan& P) {
     // its digit sum stays at or below m_w / Ma (Ma = widest input digit paired).
     for (int w = 0; w < c.n_w; ++w) {
         if (!rare_w[w]) continue;
-        if (P.nrare >= tp::MAXRARE) return false;
+        if (P.nrare >= (rows > tp::KR ? tp::MAXRARE : tp::MAXRARE_32)) return false;
         P.r_src[P.nrare] = c.w_shift[w];
         P.r_mask[P.nrare] = c.w_mask[w];
         P.r_limit[P.nrare] = c.adc_max[w] / rare_amask[w];
@@ -918,11 +941,11 @@ size_t tc_packed_workspace_bytes(const mf_config& c, int64_t n, int32_t m, int32
     return kmajor + ctas * sizeof(unsigned) + 256;
 }
 
-template <int NCOL>
+template <int NCOL, int H>
 static mf_status launch_packed(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mxs,
                                const CUtensorMap& mws, const tp::Args& args, dim3 grid, cudaStream_t st) {
     const size_t smem = sizeof(tp::Smem) + 1024;
-    auto kern = tp::packed_kernel<NCOL>;
+    auto kern = tp::packed_kernel<NCOL, H>;
     int regs = 0;
     {
         const mf_status r = kernel_setup(reinterpret_cast<const void*>(kern), smem, &regs);
@@ -998,11 +1021,16 @@ mf_status tc_packed_sliced_mm(const mf_config& c, const MMArgs& a, void* workspa
     args.tile_flags = flags;
     const long long cols = (long long)tiles * c.cols;
     dim3 grid((unsigned)((a.n + tp::BM - 1) / tp::BM), (unsigned)((cols + tp::BN - 1) / tp::BN));
+    const bool two = c.read_rows == 2 * tp::KR;
     switch (args.plan.ncol) {
-        case 0: r = launch_packed<0>(mx, mw, mxs, mws, args, grid, st); break;
-        case 1: r = launch_packed<1>(mx, mw, mxs, mws, args, grid, st); break;
-        case 2: r = launch_packed<2>(mx, mw, mxs, mws, args, grid, st); break;
-        default: r = launch_packed<3>(mx, mw, mxs, mws, args, grid, st); break;
+        case 0: r = two ? launch_packed<0, 2>(mx, mw, mxs, mws, args, grid, st)
+                        : launch_packed<0, 1>(mx, mw, mxs, mws, args, grid, st); break;
+        case 1: r = two ? launch_packed<1, 2>(mx, mw, mxs, mws, args, grid, st)
+                        : launch_packed<1, 1>(mx, mw, mxs, mws, args, grid, st); break;
+        case 2: r = two ? launch_packed<2, 2>(mx, mw, mxs, mws, args, grid, st)
+                        : launch_packed<2, 1>(mx, mw, mxs, mws, args, grid, st); break;
+        default: r = two ? launch_packed<3, 2>(mx, mw, mxs, mws, args, grid, st)
+                         : launch_packed<3, 1>(mx, mw, mxs, mws, args, grid, st); break;
     }
     if (r) return r;
     // Tiles whose rare pairs could clip are recomputed exactly by the generic kernel.

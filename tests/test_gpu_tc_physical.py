@@ -51,7 +51,9 @@ CONFIGS = {
 # weight digits as the B operand, bit-exact.  ``saturating_adc`` (4-bit ADC, count
 # limit 15 against digit dots up to 32 x 9) clamps most counts of the upper slices.
 IDEAL = {
-    "default_ideal": dict(nonidealities=dict(write_variation=0.0)),
+    # 1-bit slices with 7-bit ADCs: the packed kernel's 2^22 reconstruction bound
+    # is exceeded, so the digit mode runs it (Config's 6-bit defaults go packed).
+    "onebit_adc7": dict(adc_bits=7, nonidealities=dict(write_variation=0.0)),
     "int8_rpr64_ideal": dict(MATRIX, input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2), adc_bits=7,
                              nonidealities=dict(write_variation=0.0)),
     "int4_rpr64_ideal": dict(MATRIX, activation_bits=4, weight_bits=4, input_slice=(1, 1, 2), weight_slice=(1, 1, 2),

@@ -133,3 +133,68 @@ def test_tcgen05_column_shards_match_full_output(mf):
             begin, end, matrix.seed, 0, 0, 0, _lib.ptr(ws), ws_bytes, _lib.stream_of(a.device)), "shard")
     torch.cuda.synchronize()
     assert torch.equal(full, part)
+
+
+def _default_ideal(mf):
+    """Config's defaults (64x64 arrays, 1-bit slices, 6-bit ADCs, whole-array
+    64-row reads), ideal devices: the packed kernel with two 32-row stages per read."""
+    return mf.Config(nonidealities=mf.Nonidealities(write_variation=0.0))
+
+
+def test_64_row_reads_take_the_packed_kernel(mf):
+    import ctypes as ct
+
+    from memfast_b200 import _lib
+
+    config = _default_ideal(mf)
+    assert config.read_rows == 64
+    res = _lib.MFResources()
+    sched = _lib.schedule(kernel=0)
+    _lib.check(_lib.load().mf_query(_lib.native_config(config), ct.byref(sched), 4096, 64, 64, ct.byref(res)), "q")
+    assert res.threads == 768
+
+
+@pytest.mark.parametrize("shape", [(128, 128, 128), (200, 384, 300), (333, 1000, 520)])
+def test_64_row_reads_bit_exact_vs_generic_and_oracle(mf, shape):
+    from oracle import oracle as O
+
+    config = _default_ideal(mf)
+    n, k, o = shape
+    g = torch.Generator().manual_seed(n + k + o)
+    a = torch.randn(n, k, generator=g).cuda()
+    b = torch.randn(k, o, generator=g).cuda()
+    fast = run(mf, config, a, b, 2)
+    slow = run(mf, config, a, b, 1)
+    assert np.array_equal(fast.view(np.uint32), slow.view(np.uint32))
+    want = O.mm(a[:16].cpu().numpy(), b.cpu().numpy(), config)
+    assert np.array_equal(fast[:16].view(np.uint32), want.view(np.uint32))
+
+
+def test_64_row_reads_all_ones_reads_clip_exactly(mf):
+    """Codes of -1 (all bits set) over a whole 64-row read make a 1-bit digit dot
+    reach 64, one past the 6-bit ADC: the packed kernel flags those columns and the
+    exact rerun gives the reference's clipped counts."""
+    from oracle import oracle as O
+
+    config = _default_ideal(mf)
+    n, k, o = 96, 256, 192
+    g = torch.Generator().manual_seed(5)
+    a = torch.randn(n, k, generator=g)
+    b = torch.randn(k, o, generator=g)
+    # Column 7 of B and rows 3 and 40 of A: one value 127 times the rest, which then
+    # quantise to -1 (0xFF); the whole column / row is one quantisation group.
+    b[:, 7] = -1.0
+    b[10, 7] = 127.0
+    a[3, :] = -1.0
+    a[3, 70] = 127.0
+    a[40, :] = -1.0
+    a[40, 5] = 127.0
+    a, b = a.cuda(), b.cuda()
+    fast = run(mf, config, a, b, 2)
+    slow = run(mf, config, a, b, 1)
+    assert np.array_equal(fast.view(np.uint32), slow.view(np.uint32))
+    want = O.mm(a.cpu().numpy(), b.cpu().numpy(), config)
+    assert np.array_equal(fast.view(np.uint32), want.view(np.uint32))
+    # The clipped pairs change the product: a 64-row dot without the clip differs.
+    unclipped = mf.Config(adc_bits=7, nonidealities=mf.Nonidealities(write_variation=0.0))
+    assert not np.array_equal(run(mf, unclipped, a, b, 1)[3], fast[3])
