@@ -80,7 +80,8 @@ typedef struct {
  * bitwise check then keeps the default's kernel). */
 typedef struct {
     int32_t kernel;     /* 0 auto, 1 generic SIMT, 2 tcgen05 (ideal: packed integer counts when
-                           the configuration fits, else FP8 digit planes; nonideal: FP16 digit x
+                           the configuration fits (32- or 64-row reads), else FP8 digit planes
+                           (32-row reads), else FP16 digit dots; nonideal: FP16 digit x
                            conductance currents when the configuration fits), 3 tcgen05 FP8
                            digit planes (ideal) */
     int32_t tile_n;     /* vectors per CTA (generic: 8,16,32) */
