@@ -128,6 +128,7 @@ struct Args {
     float maxw[MAXS];
     int factor[MAXS][MAXS];  // s_a * s_w
     int offset;              // -0x4B400000 * sum of factor over the slice pairs (mod 2^32)
+    float ffactor[MAXS][MAXS];  // s_a * s_w as FP32 (float totals of the digit mode)
 };
 
 __device__ __forceinline__ float mul_sat(float a, float b) {
@@ -161,7 +162,9 @@ __device__ __forceinline__ void tmem_loaded(uint32_t* v) {
     for (int k = 0; k < N; ++k) asm volatile("" : "+r"(v[k]));
 }
 
-template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool NONLINEAR>
+// FSUM (digit mode, reconstruction bound below 2^24): the count min(D, max_w) and
+// the total are FP32 integers, summed exactly with one FMNMX and one FFMA per event.
+template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool NONLINEAR, bool FSUM = false>
 __global__ void __launch_bounds__(THREADS, 1)
     tc_physical_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_g,
                        const __grid_constant__ Args args) {
@@ -389,8 +392,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // 0x4B400000 + count, so the total accumulates bits * factor in wrapping int32
                 // and the constant part is removed once.
                 int total[G::EC];
+                float ftotal[G::EC];
 #pragma unroll
-                for (int e = 0; e < G::EC; ++e) total[e] = args.offset;
+                for (int e = 0; e < G::EC; ++e) {
+                    total[e] = args.offset;
+                    ftotal[e] = 0.0f;
+                }
 #pragma unroll 1
                 for (int a = 0; a < NIN; ++a, ++job) {
                     const int unit = job % G::U;
@@ -415,6 +422,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                                                               __uint_as_float(v[SPLIT ? 1 : 0][e * NW + w]))
                                                   : __uint_as_float(v[0][e * NW + w]);
                             constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+                            if (FSUM) {
+                                ftotal[e] = __fmaf_rn(fminf(x, args.maxw[w]), args.ffactor[a][w], ftotal[e]);
+                                continue;
+                            }
                             float s;
                             if (NONLINEAR) {
                                 float z = __fmul_rn(x, args.cw[w]);
@@ -430,8 +441,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (!ok) break;
 #pragma unroll
                 for (int e = 0; e < G::EC; ++e)
-                    acc0[cb][e] =
-                        __fadd_rn(acc0[cb][e], __fmul_rn(__fmul_rn(__int2float_rn(total[e]), xs), ws_now[cb][e]));
+                    acc0[cb][e] = __fadd_rn(acc0[cb][e], __fmul_rn(__fmul_rn(FSUM ? ftotal[e] : __int2float_rn(total[e]), xs),
+                                                                   ws_now[cb][e]));
             }
             if (!ok) break;
             // Block boundary of the 16-read cascade: level 1 += level 0 (MR <= 256 keeps two levels).
@@ -635,12 +646,12 @@ size_t tc_physical_workspace_bytes(const mf_config& c, int32_t m, int32_t tiles)
     return (size_t)blocks * brows * (size_t)m * c.rows * sizeof(__half) + 256;
 }
 
-template <int NIN, int NW, int BN, int NJB, bool SPLIT, int NPART, int KR, bool NL>
+template <int NIN, int NW, int BN, int NJB, bool SPLIT, int NPART, int KR, bool NL, bool FSUM = false>
 static mf_status launch_tcp(const CUtensorMap& mx, const CUtensorMap& mg, const tcp::Args& args, dim3 grid,
                             cudaStream_t st) {
     using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART>;
     const size_t smem = G::BYTES + 1024;
-    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL>;
+    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL, FSUM>;
     int regs = 0;
     {
         const mf_status r = kernel_setup(reinterpret_cast<const void*>(kern), smem, &regs);
@@ -673,6 +684,11 @@ static mf_status dispatch_tcp(const mf_config& c, const CUtensorMap& mx, const C
 template <int NIN, int NW, int BN, int NJB>
 static mf_status dispatch_digits(const mf_config& c, const CUtensorMap& mx, const CUtensorMap& mg,
                                  const tcp::Args& args, dim3 grid, cudaStream_t st) {
+    // Integer totals below 2^24 are exact in FP32.
+    if (reconstruction_bound(c) < 16777216.0) {
+        if (c.read_rows == 32) return launch_tcp<NIN, NW, BN, NJB, false, 1, 32, false, true>(mx, mg, args, grid, st);
+        return launch_tcp<NIN, NW, BN, NJB, false, 1, 64, false, true>(mx, mg, args, grid, st);
+    }
     if (c.read_rows == 32) return launch_tcp<NIN, NW, BN, NJB, false, 1, 32, false>(mx, mg, args, grid, st);
     return launch_tcp<NIN, NW, BN, NJB, false, 1, 64, false>(mx, mg, args, grid, st);
 }
@@ -756,6 +772,7 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
         args.maxw[w] = (float)c.adc_max[w];
         for (int i = 0; i < c.n_in; ++i) {
             args.factor[i][w] = (int)(c.in_factor[i] * c.w_factor[w]);
+            args.ffactor[i][w] = (float)args.factor[i][w];
             sum += (uint32_t)args.factor[i][w];
         }
     }
