@@ -19,6 +19,8 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
+sys.path[:0] = [str(HERE.parent), str(HERE.parents[1])]
+from helpers import digest, seed_operands  # noqa: E402
 
 
 def _jsonable(kwargs):
@@ -65,16 +67,22 @@ def main(reference_root, only=()):
         size = (HERE / f"{case}.npz").stat().st_size
         print(f"{case:28s} {size/1024:7.1f} KiB")
 
-    def mm_case(name, kwargs, n, k, o, seed, *, a=None, b=None, calls=1, buffers=False):
+    def mm_case(name, kwargs, n, k, o, seed, *, a=None, b=None, calls=1, buffers=False, seeded=False):
+        """``seeded``: operands from numpy's generator (seed_operands), stored as the
+        seed and a digest instead of the arrays (large reduction dimensions)."""
         if only and name not in only:
             return
         cfg = make(kwargs)
+        meta = {}
+        if seeded:
+            a, b = (torch.from_numpy(v) for v in seed_operands(n, k, o, seed))
+            meta = dict(seeded=seed, shape=[n, k, o], digest=digest(a.numpy(), b.numpy()))
         g = torch.Generator().manual_seed(seed)
         a = torch.randn(n, k, generator=g) if a is None else a
         b = torch.randn(k, o, generator=g) if b is None else b
         sim = Simulator(cfg, device="cpu")
         outs = [sim.mm(a, b) for _ in range(calls)]
-        arrays = {"A": a.numpy(), "B": b.numpy()}
+        arrays = {} if seeded else {"A": a.numpy(), "B": b.numpy()}
         for i, out in enumerate(outs):
             arrays[f"out{i}"] = out.numpy()
         if buffers:
@@ -84,7 +92,7 @@ def main(reference_root, only=()):
             q, xs = memfast.quantization.input_tiles(a, cfg)
             arrays["q"] = q.numpy()
             arrays["xscale"] = xs.numpy()
-        save(name, kwargs, arrays, kind="mm", calls=calls, name="matrix.0")
+        save(name, kwargs, arrays, kind="mm", calls=calls, name="matrix.0", **meta)
 
     ideal = dict(write_variation=0.0)
     # BASELINE config #1 exactly: CPU Simulator.mm, torch.manual_seed(0), randn(4,128) @ randn(128,32).
@@ -130,6 +138,32 @@ def main(reference_root, only=()):
                                                          read_mode="output")), 4, 256, 128, 16)
     mm_case("shared_read_events", dict(int8, nonidealities=dict(write_variation=0.0, read_variation=0.05)),
             4, 256, 128, 17, calls=3)
+    # More than 256 reads per output (m * reads = 512 and 272): the cascade sum
+    # over reads reaches its second level (16 blocks of 16 reads per level-2 step).
+    mm_case("int8_ideal_deep", dict(int8, nonidealities=ideal), 3, 16384, 128, 40, seeded=True)
+    mm_case("int8_ideal_deep_ragged", dict(int8, nonidealities=ideal), 2, 8700, 160, 41, seeded=True)
+    mm_case("int8_write_deep", dict(int8, nonidealities=dict(write_variation=0.02)), 2, 16384, 128, 42, seeded=True)
+
+    # The benchmark's own 4096 x 4096 x 4096 operands (bench.operands: seeded numpy
+    # N(0,1), reproducible on any host): the first rows of A against the whole B,
+    # for the ideal headline and the nonideal variants of the sweep.  Only the
+    # outputs and a digest of the operands are stored; tests regenerate the
+    # operands from the seed and check the digest first.
+    def headline_case(name, effects, rows=8, size=4096, seed=2024):
+        if only and name not in only:
+            return
+        from bench import EFFECTS, operand_digest, operands
+
+        kwargs = dict(int8, nonidealities=dict(EFFECTS[effects]))
+        a, b = operands(size, seed)
+        out = Simulator(make(kwargs), device="cpu").mm(torch.from_numpy(a[:rows]), torch.from_numpy(b))
+        save(name, kwargs, dict(out0=out.numpy()), kind="headline", name="matrix.0", size=size, seed=seed,
+             rows=rows, effects=effects, digest=operand_digest(a[:rows], b))
+
+    headline_case("headline_ideal", "ideal")
+    headline_case("headline_write", "write")
+    headline_case("headline_shared", "shared")
+    headline_case("headline_noisy", "noisy")
 
     # Unsigned imported weights with zero points (simulator.py:173-185, 587-611).
     kwargs = dict(int8, weight_signed=False, nonidealities=ideal)

@@ -1,0 +1,104 @@
+"""Parity at the benchmark's own shape: 4096 x 4096 x 4096 INT8 (1,1,2,2,2), the
+operands ``bench.py`` times (seeded numpy N(0,1), seed 2024).
+
+Every vector is independent (its input groups span one row and its noise draws
+are addressed by its global index, memfast/reference.py:77-81,103-106), so a
+row prefix of A against the whole 4096 x 4096 B reproduces those rows of the
+full product exactly.  The prefix is checked three ways: its first rows against
+the reference's own outputs (tests/golden/headline_*.npz), all its rows against
+the CPU oracle, and the prefix product against the same rows of the full
+4096-row product.  Ideal devices are bit-exact; nonideal ones meet the
+tolerance of ``helpers.assert_close_nonideal``.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import bench
+from helpers import adc_events, assert_parity, flip_size, load_case
+
+pytestmark = pytest.mark.gpu
+
+SIZE = 4096
+PREFIX = 64
+
+
+@pytest.fixture(scope="module")
+def mf():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import memfast_b200
+
+    return memfast_b200
+
+
+@pytest.fixture(scope="module")
+def operands():
+    a, b = bench.operands(SIZE)
+    return a, b, torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+
+
+@pytest.mark.parametrize("effects", ["ideal", "write", "shared", "noisy"])
+def test_headline_prefix_matches_reference_and_oracle(mf, operands, effects):
+    from oracle import oracle as O
+
+    config, golden, meta = load_case(f"headline_{effects}")
+    a, b, a_dev, b_dev = operands
+    assert bench.operand_digest(a[:meta["rows"]], b) == meta["digest"]
+    assert config == bench.bench_config(mf, effects)
+    got = mf.Simulator(config).mm(a_dev[:PREFIX], b_dev).cpu().numpy()
+    tolerance = dict(events=adc_events(config, SIZE), flip=flip_size(config, a[:PREFIX], b))
+    # The reference's own first rows.
+    assert_parity(got[:meta["rows"]], golden["out0"], config, f"{effects}: reference rows", **tolerance)
+    # Every prefix row against the oracle (the reference's algorithm restated).
+    want = O.mm(a[:PREFIX], b, config)
+    assert_parity(got, want, config, f"{effects}: oracle rows", **tolerance)
+
+
+@pytest.mark.parametrize("effects", ["ideal", "noisy"])
+def test_headline_full_product_rows_equal_prefix_product(mf, operands, effects):
+    """The full 4096-row product (the benchmark's step) holds the prefix product's
+    rows bit for bit, and, ideal, its last row block matches the oracle too."""
+    from oracle import oracle as O
+
+    config = bench.bench_config(mf, effects)
+    a, b, a_dev, b_dev = operands
+    full = mf.Simulator(config).mm(a_dev, b_dev)
+    prefix = mf.Simulator(config).mm(a_dev[:PREFIX], b_dev)
+    assert torch.equal(full[:PREFIX].view(torch.int32), prefix.view(torch.int32))
+    if effects == "ideal":
+        tail = full[SIZE - PREFIX:].cpu().numpy()
+        assert_parity(tail, O.mm(a[SIZE - PREFIX:], b, config), config, "last row block")
+
+
+@pytest.mark.parametrize("kernel", [1, 2, 3])
+def test_headline_prefix_every_ideal_kernel(mf, operands, kernel):
+    """Each ideal schedule kernel (1 dp4a SIMT, 2 packed tcgen05 counts, 3 tcgen05 FP8
+    digit planes) gives the oracle's bits on the headline operands."""
+    from memfast_b200.quantization import input_tiles
+    from memfast_b200.simulator import default_schedule
+    from oracle import oracle as O
+
+    config = bench.bench_config(mf, "ideal")
+    a, b, a_dev, b_dev = operands
+    sim = mf.Simulator(config)
+    matrix = sim._matrix_for(b_dev)
+    q, xscale = input_tiles(a_dev[:PREFIX], config)
+    got = matrix._execute(q, xscale, dict(default_schedule(config), kernel=kernel), 0).cpu().numpy()
+    want = O.mm(a[:PREFIX], b, config)
+    assert_parity(got, want, config, f"kernel {kernel}")
+
+
+def test_headline_rare_tile_rerun_is_exact(mf, operands):
+    """Columns whose weight digits can clip a rare pair flag their tile for the exact
+    rerun: a B whose first columns are all at the top code (every digit 1s) still
+    gives the oracle's bits at the headline shape."""
+    from oracle import oracle as O
+
+    config = bench.bench_config(mf, "ideal")
+    a, b, a_dev, _ = operands
+    b2 = b.copy()
+    b2[:, :96] = np.abs(b2[:, :96]).max()
+    got = mf.Simulator(config).mm(a_dev[:PREFIX], torch.from_numpy(b2).cuda()).cpu().numpy()
+    assert_parity(got, O.mm(a[:PREFIX], b2, config), config, "rare tiles")

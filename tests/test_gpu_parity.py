@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import assert_parity, load_case, mm_cases
+from helpers import adc_events, assert_parity, flip_size, load_case, mm_cases
 
 pytestmark = pytest.mark.gpu
 
@@ -107,12 +107,15 @@ def test_nonideal_all_effects_vs_oracle(mf):
     sim = mf.Simulator(config)
     a_dev, b_dev = a.cuda(), b.cuda()
     # The same RHS tensor keeps its program (name matrix.0) and advances its read event.
+    # One flip of the sign x sign pair moves an output by far more than 5% of the range
+    # here; the bound is four such flips (helpers.py).
+    tolerance = dict(flip=flip_size(config, a.numpy(), b.numpy()), events=adc_events(config, 512))
     for event in range(2):
         got = sim.mm(a_dev, b_dev).cpu().numpy()
-        assert_parity(got, O.mm(a.numpy(), b.numpy(), config, event=event), config, f"event {event}")
+        assert_parity(got, O.mm(a.numpy(), b.numpy(), config, event=event), config, f"event {event}", **tolerance)
     # A new RHS tensor is a new program: next automatic name, read event 0 (simulator.py:111-171).
     got = sim.mm(a_dev, b.cuda()).cpu().numpy()
-    assert_parity(got, O.mm(a.numpy(), b.numpy(), config, name="matrix.1"), config, "new rhs")
+    assert_parity(got, O.mm(a.numpy(), b.numpy(), config, name="matrix.1"), config, "new rhs", **tolerance)
 
 
 def test_prefix_rows_are_exact_subsets(mf):

@@ -85,3 +85,17 @@ def test_cascade_matches_torch_for_aligned_tiles():
                 col = np.ascontiguousarray(v[b, :, c])
                 got[b, c] = np.float32(0) + lib.orc_cascade_f32(col.ctypes.data_as(ct.POINTER(ct.c_float)), rows, 1)
         assert np.array_equal(got.view(np.int32), want.view(np.int32)), rows
+
+
+@pytest.mark.parametrize("case", cases_of("headline"))
+def test_oracle_headline_rows_match_reference(case):
+    """The benchmark's own 4096^3 operands: the reference's first rows, reproduced by
+    the oracle (bit for bit in ideal mode, within the stated tolerance otherwise)."""
+    import bench
+
+    config, arrays, meta = load_case(case)
+    a, b = bench.operands(meta["size"], meta["seed"])
+    rows = meta["rows"]
+    assert bench.operand_digest(a[:rows], b) == meta["digest"], "regenerated operands differ from the reference's"
+    got = O.mm(a[:rows], b, config, name=meta["name"])
+    assert_parity(got, arrays["out0"], config, case)
