@@ -1,14 +1,14 @@
 """Natural-order analog matrix products (memfast/functional.py behaviour).
 
 ``mm(A, B)`` and ``matmul(A, B)`` follow torch.mm / torch.matmul shapes,
-batching and dtype rules (functional.py:32-220).  The RHS is programmed through
-``Simulator._matrix_for``; each independently indexed batched RHS is its own
-program, broadcast copies share one.  Autograd is outside this engine's scope:
-the analog forward is inference-only, so inputs that require grad are rejected
-with a clear error instead of silently dropping gradients.
+batching and dtype rules (functional.py:32-220).  The right-hand matrix is
+programmed through ``Simulator._matrix_for``; each independently indexed
+batched right-hand matrix is its own program, and broadcast copies share one.
+Autograd is outside this engine's scope: the analog forward is inference-only,
+so inputs that require grad are rejected with a clear error instead of
+silently dropping gradients.
 """
 
-import itertools
 import math
 import weakref
 from pathlib import Path
@@ -20,14 +20,15 @@ from .config import Config
 from .quantization import check_finite, compute_dtype, finite_flags
 from .simulator import Simulator
 
+_FLOATING = (torch.float16, torch.bfloat16, torch.float32, torch.float64)
+
 
 def _operand_types(a, b):
+    """Types, layouts, ranks, dtypes and devices of an operand pair (no device work)."""
     for name, value in (("A", a), ("B", b)):
         if not isinstance(value, torch.Tensor):
             raise TypeError(f"{name} must be a torch.Tensor")
-        if value.layout != torch.strided or value.dtype not in (
-            torch.float16, torch.bfloat16, torch.float32, torch.float64
-        ):
+        if value.layout != torch.strided or value.dtype not in _FLOATING:
             raise TypeError(f"{name} must be a real floating dense tensor")
         if value.ndim == 0:
             raise ValueError(f"{name} must have at least one dimension")
@@ -40,13 +41,11 @@ def _operand_types(a, b):
 
 
 def _operands(a, b):
-    """Type, device and finiteness checks of an operand pair (one synchronisation)."""
+    """The checks above plus finiteness of both operands (one synchronisation)."""
     _operand_types(a, b)
-    finite_a, finite_b = finite_flags(a, b)
-    if not finite_a:
-        raise ValueError("A must be finite")
-    if not finite_b:
-        raise ValueError("B must be finite")
+    for name, finite in zip("AB", finite_flags(a, b)):
+        if not finite:
+            raise ValueError(f"{name} must be finite")
 
 
 # Errors of a deferred operand check, in the reference's order: _operands (A, then
@@ -79,7 +78,9 @@ def _operand_code(a, b, config):
     return flags
 
 
-def _engine(a, simulator, config, mode, cache_dir):
+def _resolve_simulator(a, simulator, config, mode, cache_dir):
+    """The simulator a call runs on: the caller's (whose settings the explicit options
+    must agree with) or, without one, a new simulator for this call."""
     if mode not in ("default", "tuned"):
         raise ValueError("mode must be default or tuned")
     if config is not None and not isinstance(config, Config):
@@ -88,18 +89,21 @@ def _engine(a, simulator, config, mode, cache_dir):
         return Simulator(config, mode=mode, device=a.device, cache_dir=cache_dir)
     if not isinstance(simulator, Simulator):
         raise TypeError("simulator must be Simulator")
-    if simulator.device != a.device:
-        raise ValueError("operands and simulator must use the same device")
-    if config is not None and config != simulator.config:
-        raise ValueError("config differs from the supplied simulator")
-    if mode != "default" and mode != simulator.mode:
-        raise ValueError("mode differs from the supplied simulator")
-    if cache_dir is not None and Path(cache_dir) != simulator.cache_dir:
-        raise ValueError("cache_dir differs from the supplied simulator")
+    disagreements = (
+        (simulator.device != a.device, "operands and simulator must use the same device"),
+        (config is not None and config != simulator.config, "config differs from the supplied simulator"),
+        (mode != "default" and mode != simulator.mode, "mode differs from the supplied simulator"),
+        (cache_dir is not None and Path(cache_dir) != simulator.cache_dir,
+         "cache_dir differs from the supplied simulator"),
+    )
+    for disagrees, message in disagreements:
+        if disagrees:
+            raise ValueError(message)
     return simulator
 
 
-def _out(a, b, out, shape):
+def _check_out(a, b, out, shape):
+    """``out=`` must be a dense tensor of the result's shape, dtype and device."""
     if out is None:
         return
     if not isinstance(out, torch.Tensor) or out.layout != torch.strided:
@@ -110,31 +114,38 @@ def _out(a, b, out, shape):
         raise RuntimeError("out= does not support automatic differentiation")
 
 
-def _rhs_view(simulator, owner, rhs, index):
-    """Stable detached cache keys that do not keep the caller's tensor alive."""
-    cache = getattr(simulator, "_functional_rhs_views", None)
-    if cache is None:
-        cache = simulator._functional_rhs_views = {}
-    identity = id(owner)
-    geometry = (tuple(owner.shape), tuple(owner.stride()), owner.storage_offset(), owner.data_ptr(),
-                owner.dtype, owner.device, owner.is_neg())
-    record = cache.get(identity)
-    if record is None or record[0]() is not owner or record[1] != geometry:
-        engine = weakref.ref(simulator)
+class _RhsViews:
+    """Detached views of a batched right-hand operand, one per batch index, stable
+    across calls with the same operand (so each keeps its program and read events)
+    without keeping the caller's tensor alive."""
 
-        def release(reference):
-            instance = engine()
-            if instance is not None:
-                entries = instance._functional_rhs_views
-                previous = entries.get(identity)
-                if previous is not None and previous[0] is reference:
-                    entries.pop(identity, None)
+    def __init__(self):
+        self._owners = {}
 
-        record = (weakref.ref(owner, release), geometry, {})
-        cache[identity] = record
-    if index not in record[2]:
-        record[2][index] = rhs.detach()
-    return record[2][index]
+    @staticmethod
+    def of(simulator):
+        views = getattr(simulator, "_rhs_views", None)
+        if views is None:
+            views = simulator._rhs_views = _RhsViews()
+        return views
+
+    def view(self, owner, rhs, index):
+        geometry = (tuple(owner.shape), tuple(owner.stride()), owner.storage_offset(), owner.data_ptr(),
+                    owner.dtype, owner.device, owner.is_neg())
+        entry = self._owners.get(id(owner))
+        if entry is None or entry["owner"]() is not owner or entry["geometry"] != geometry:
+            token = object()
+            entry = dict(owner=weakref.ref(owner), geometry=geometry, views={}, token=token)
+            self._owners[id(owner)] = entry
+            weakref.finalize(owner, _RhsViews._forget, weakref.ref(self), id(owner), token)
+        # detach() shares storage and version with the caller's tensor, not its identity.
+        return entry["views"].setdefault(index, rhs.detach())
+
+    @staticmethod
+    def _forget(views_ref, key, token):
+        views = views_ref()
+        if views is not None and views._owners.get(key, {}).get("token") is token:
+            del views._owners[key]
 
 
 def _checked(tensor, config, bits):
@@ -161,11 +172,33 @@ def _product(a, b, simulator, cached_rhs=None, operand_code=None):
                                input_flag=operand_code, input_errors=OPERAND_ERRORS if deferred else None)
 
 
+def _batched_products(left, right, b, batch, rows, columns, engine):
+    """Products of a batch whose right-hand matrices differ along some batch dimension.
+
+    Every batch index maps to the right-hand matrix at its index with the broadcast
+    dimensions set to 0.  Indices sharing one matrix form one product (their vectors
+    stacked in batch order); the products run in the order of their matrices' flat
+    index, which is also the order in which each first appears in the batch, so the
+    programs take the same automatic names (and sampling seeds) as the reference's
+    (functional.py:170-185)."""
+    rhs_batch = right.shape[:-2]
+    flat_left = left.reshape(-1, rows, left.shape[-1])
+    rhs_of = torch.arange(math.prod(rhs_batch)).reshape((1,) * (len(batch) - len(rhs_batch)) + rhs_batch)
+    rhs_of = rhs_of.expand(batch).reshape(-1)
+    result = flat_left.new_empty((flat_left.shape[0], rows, columns))
+    for flat in torch.unique(rhs_of).tolist():
+        members = torch.nonzero(rhs_of == flat).flatten()
+        index = tuple(int(i) for i in torch.unravel_index(torch.tensor(flat), rhs_batch))
+        rhs = right[index]
+        cached = _RhsViews.of(engine).view(b, rhs, index)
+        result[members.to(flat_left.device)] = _product(flat_left[members.to(flat_left.device)], rhs, engine, cached)
+    return result.reshape(batch + (rows, columns))
+
+
 def _matmul(a, b, *, simulator, config, mode, cache_dir, out):
     _operand_types(a, b)
-    left_vector, right_vector = a.ndim == 1, b.ndim == 1
-    left = a.unsqueeze(0) if left_vector else a
-    right = b.unsqueeze(-1) if right_vector else b
+    left = a.unsqueeze(0) if a.ndim == 1 else a
+    right = b.unsqueeze(-1) if b.ndim == 1 else b
     if left.shape[-1] != right.shape[-2]:
         raise ValueError("A and B have incompatible reduction dimensions")
     try:
@@ -173,9 +206,9 @@ def _matmul(a, b, *, simulator, config, mode, cache_dir, out):
     except RuntimeError:
         raise ValueError("A and B batch dimensions cannot broadcast") from None
     rows, reduction, columns = left.shape[-2], left.shape[-1], right.shape[-1]
-    shape = batch + (() if left_vector else (rows,)) + (() if right_vector else (columns,))
-    _out(a, b, out, shape)
-    engine = _engine(a, simulator, config, mode, cache_dir)
+    shape = batch + (() if a.ndim == 1 else (rows,)) + (() if b.ndim == 1 else (columns,))
+    _check_out(a, b, out, shape)
+    engine = _resolve_simulator(a, simulator, config, mode, cache_dir)
     if (a.ndim == 2 and b.ndim == 2 and out is None and a.numel() and b.numel()
             and not torch.is_autocast_enabled(a.device.type)):
         # Plain rank-two product outside autocast: one programmed product, no batch
@@ -187,28 +220,14 @@ def _matmul(a, b, *, simulator, config, mode, cache_dir, out):
             result = a.new_zeros(shape)
         else:
             left = left.expand(batch + (rows, reduction))
-            rhs_batch = right.shape[:-2]
-            if all(size == 1 for size in rhs_batch):
-                # One product: the operand check is read with the output check.
+            if all(size == 1 for size in right.shape[:-2]):
+                # One right-hand matrix: the operand check is read with the output check.
                 rhs = right if right.ndim == 2 else right.reshape(reduction, columns)
-                cached = None if b.ndim == 2 else _rhs_view(engine, b, rhs, ())
+                cached = None if b.ndim == 2 else _RhsViews.of(engine).view(b, rhs, ())
                 result = _product(left, rhs, engine, cached, operand_code=_operand_code(a, b, engine.config))
             else:
                 _operands(a, b)
-                groups = {}
-                padding = len(batch) - len(rhs_batch)
-                for index in itertools.product(*(range(size) for size in batch)):
-                    key = tuple(0 if size == 1 else index[padding + axis] for axis, size in enumerate(rhs_batch))
-                    groups.setdefault(key, []).append(index)
-                outputs = {}
-                for key, indices in groups.items():
-                    inputs = torch.stack([left[index] for index in indices])
-                    rhs = right[key]
-                    values = _product(inputs, rhs, engine, _rhs_view(engine, b, rhs, key))
-                    outputs.update((index, values[row]) for row, index in enumerate(indices))
-                result = torch.stack(
-                    [outputs[index] for index in itertools.product(*(range(size) for size in batch))]
-                ).reshape(batch + (rows, columns))
+                result = _batched_products(left, right, b, batch, rows, columns, engine)
             result = result.reshape(shape)
     if out is not None:
         out.copy_(result)

@@ -6,7 +6,8 @@ from ..simulator import AnalogMatrix
 
 
 class AnalogLinear(AnalogMatrix):
-    """Map a PyTorch Linear, preserving its bias and matrix orientation."""
+    """An ``nn.Linear`` programmed once into analog arrays: its [out, in] weight becomes
+    the matrix (same orientation) and its bias is added to every output."""
 
     def __init__(self, source, simulator, *, name="linear"):
         if not isinstance(source, nn.Linear):

@@ -2,9 +2,9 @@
 
 Behavioural mirror of the reference ``memfast/simulator.py``:
 
-* ``Simulator``      simulator.py:69-347  (device selection, RHS programming
-  cache, tuned-mode schedule search with bitwise validation and a persistent
-  JSON cache, ``report``);
+* ``Simulator``      simulator.py:69-347  (device selection, programming of the
+  right-hand matrix of ``mm`` with reuse of the previous program, tuned mode,
+  ``report``);
 * ``AnalogMatrix``   simulator.py:350-646 (buffers, name-derived sampling seed,
   read-event counter, zero-point correction, bias, non-finite FP64 rerun,
   checkpoint state).
@@ -12,19 +12,15 @@ Behavioural mirror of the reference ``memfast/simulator.py``:
 What changes is the execution: ``AnalogMatrix._execute`` makes one
 ``mf_sliced_mm`` call for all output tiles (quantised codes in, finished
 outputs out) instead of looping over tile groups and reducing partials in
-PyTorch (simulator.py:561-586).  There is no CPU path: a Simulator lives on a
-CUDA device and fails loudly otherwise.
+PyTorch (simulator.py:561-586).  Tuned mode searches this engine's own grid
+(``tuning.py``).  There is no CPU path: a Simulator lives on a CUDA device and
+fails loudly otherwise.
 """
 
 import ctypes as ct
 import functools
 import hashlib
-import itertools
-import json
 import math
-import os
-import tempfile
-import time
 import types
 import weakref
 from dataclasses import asdict
@@ -33,7 +29,7 @@ from pathlib import Path
 import torch
 from torch import nn
 
-from . import _lib
+from . import _lib, tuning
 from .config import Config
 from .quantization import (
     check_finite,
@@ -45,11 +41,17 @@ from .quantization import (
     read_starts,
     weight_tiles,
 )
+from .tuning import atomic_write, cache_root, default_schedule, device_identity, schedule_grid, source_hash
 
 ResourceError = _lib.ResourceError
 
-_GRID_ARRAYS = (1, 2, 4, 8, 16, 32, 64)
-_GRID_KERNELS = (1, 2)
+_INTEGER_DTYPES = (torch.uint8, torch.int8, torch.int16, torch.int32, torch.int64)
+
+# A matrix keeps its tensor-core workspace between calls only when the part rewritten
+# by every call (the conductance operand of nonideal currents, beyond the K-major code
+# copy) is at most this large; bigger ones come from the allocator per call, so that
+# a model of many programmed layers holds one such buffer at a time, not one per layer.
+_KEPT_SCRATCH_BYTES = 64 << 20
 
 
 @functools.lru_cache(maxsize=4096)
@@ -68,72 +70,21 @@ def _workspace_bytes(config, n, m, p, schedule):
 @functools.lru_cache(maxsize=1024)
 def _kmajor_bytes(config, m, p, schedule):
     """K-major weight copy bytes of the schedule's kernel (mf_query), cached."""
-    resources = _lib.MFResources()
-    native = _lib.schedule(**dict(schedule))
-    _lib.check(
-        _lib.load().mf_query(_lib.native_config(config), ct.byref(native), 1, m, p, ct.byref(resources)),
-        "mf_query",
-    )
-    return resources.kmajor_bytes
-
-
-def default_schedule(config):
-    """Engine schedule used outside tuned mode (kernel 0 = automatic choice)."""
-    return dict(kernel=0, tile_n=32, tile_o=64, arrays=2)
-
-
-def schedule_grid(config, n, partitions):
-    """The declared tuned-mode domain over this engine's kernels and tile groups."""
-    seen = set()
-    for kernel, arrays in itertools.product(_GRID_KERNELS, _GRID_ARRAYS):
-        effective = (kernel, min(arrays, partitions))
-        if effective in seen:
-            continue
-        seen.add(effective)
-        yield dict(kernel=kernel, tile_n=32, tile_o=64, arrays=arrays)
-
-
-def source_hash():
-    """Fingerprint of the engine: Python sources plus the built native library."""
-    root = Path(__file__).parent
-    digest = hashlib.sha256()
-    paths = sorted([*root.rglob("*.py"), *root.rglob("*.cu"), *root.rglob("*.cuh")])
-    for path in paths:
-        if "_build" in path.parts:
-            continue
-        digest.update(path.relative_to(root).as_posix().encode())
-        digest.update(path.read_bytes())
-    return digest.hexdigest()
-
-
-def cache_root():
-    base = os.environ.get("MEMFAST_CACHE_DIR")
-    if base:
-        return Path(base).expanduser()
-    return Path(os.environ.get("XDG_CACHE_HOME", Path.home() / ".cache")) / "memfast_b200"
-
-
-def atomic_write(path, content):
-    path.parent.mkdir(parents=True, exist_ok=True)
-    with tempfile.NamedTemporaryFile(dir=path.parent, delete=False) as stream:
-        temporary = Path(stream.name)
-        stream.write(content)
-    try:
-        os.replace(temporary, path)
-    finally:
-        temporary.unlink(missing_ok=True)
+    return tuning.resolve(config, dict(schedule), 1, m, p)[1].kmajor_bytes
 
 
 def restore_scales(value, input_scale, weight_scale):
-    """FP64 scale restoration without intermediate overflow (simulator.py:57-66)."""
-    vm, ve = torch.frexp(value.double())
-    xm, xe = torch.frexp(input_scale.double())
-    wm, we = torch.frexp(weight_scale.double())
-    mantissa = vm * xm * wm
-    exponent = ve + xe + we
-    first = exponent.clamp(-1022, 1023)
-    restored = torch.ldexp(torch.ldexp(mantissa, first), exponent - first)
-    return torch.where(mantissa == 0, 0.0, restored)
+    """``value * input_scale * weight_scale`` in FP64 without overflow or underflow of
+    the intermediate products (simulator.py:57-66): the three mantissas are multiplied
+    (a product in [1/8, 1)) and the summed binary exponent is applied in two ldexp
+    steps, each clamped to the normal range.  torch.ldexp scales by 2.0 ** e, so the
+    steps match the reference's rounding."""
+    parts = [torch.frexp(term.double()) for term in (value, input_scale, weight_scale)]
+    mantissa = parts[0][0] * parts[1][0] * parts[2][0]
+    exponent = parts[0][1] + parts[1][1] + parts[2][1]
+    step = exponent.clamp(-1022, 1023)
+    scaled = torch.ldexp(torch.ldexp(mantissa, step), exponent - step)
+    return torch.where(mantissa == 0, 0.0, scaled)
 
 
 def check_device_error():
@@ -160,16 +111,54 @@ def stage_device_error(device):
     return word
 
 
-def device_identity(device):
-    properties = torch.cuda.get_device_properties(device)
-    return dict(
-        name=properties.name,
-        capability=list(torch.cuda.get_device_capability(device)),
-        multiprocessors=properties.multi_processor_count,
-        memory=properties.total_memory,
-        torch=torch.__version__,
-        cuda=torch.version.cuda,
-    )
+def _tensor_layout(tensor):
+    """What must be unchanged for a cached program of ``tensor`` to stay valid: its
+    geometry, storage address, dtype and device (values are checked separately)."""
+    return (tuple(tensor.shape), tuple(tensor.stride()), tensor.storage_offset(), tensor.data_ptr(), tensor.dtype,
+            tensor.device)
+
+
+class _ProgramCache:
+    """Programs of right-hand operands, keyed by the operand tensor object.
+
+    The reference reprograms ``B`` on every ``mm`` call and keeps the previous
+    program when the new codes and scales are the same (simulator.py:133-171).
+    An entry lives while its tensor does: a finalizer removes it, and a token
+    makes sure a finalizer never removes a newer entry of a tensor that reuses
+    the id.
+    """
+
+    def __init__(self):
+        self._entries = {}
+
+    def get(self, tensor):
+        """(program, same_layout) of ``tensor``'s entry, or (None, False)."""
+        entry = self._entries.get(id(tensor))
+        if entry is None or entry["tensor"]() is not tensor:
+            return None, False
+        return entry["program"], entry["layout"] == _tensor_layout(tensor)
+
+    def put(self, tensor, program):
+        key, token = id(tensor), object()
+        self._entries[key] = dict(tensor=weakref.ref(tensor), layout=_tensor_layout(tensor), program=program,
+                                  token=token)
+        weakref.finalize(tensor, _ProgramCache._drop, weakref.ref(self), key, token)
+
+    @staticmethod
+    def _drop(cache_ref, key, token):
+        cache = cache_ref()
+        if cache is not None and cache._entries.get(key, {}).get("token") is token:
+            del cache._entries[key]
+
+    def __len__(self):
+        return len(self._entries)
+
+
+def _budget_bytes(workspace_mb):
+    if isinstance(workspace_mb, bool) or not isinstance(workspace_mb, (int, float)) or \
+            not math.isfinite(workspace_mb) or workspace_mb <= 0:
+        raise ValueError("workspace_mb must be positive and finite")
+    return int(workspace_mb * 1024**2)
 
 
 class Simulator:
@@ -180,40 +169,40 @@ class Simulator:
     """
 
     def __init__(self, config=None, *, mode="default", device=None, cache_dir=None, workspace_mb=1024):
-        self.config = Config() if config is None else config
-        if not isinstance(self.config, Config):
+        config = Config() if config is None else config
+        if not isinstance(config, Config):
             raise TypeError("config must be Config")
         if mode not in ("default", "tuned"):
             raise ValueError("mode must be default or tuned")
-        if isinstance(workspace_mb, bool) or not isinstance(workspace_mb, (int, float)):
-            raise ValueError("workspace_mb must be positive and finite")
-        if not math.isfinite(workspace_mb) or workspace_mb <= 0:
-            raise ValueError("workspace_mb must be positive and finite")
-        self.mode = mode
+        budget = _budget_bytes(workspace_mb)
         device = torch.device(device or "cuda")
         if device.type != "cuda":
-            raise ValueError(
-                "memfast_b200 runs on CUDA devices only; use the reference memfast package for CPU"
-            )
+            raise ValueError("memfast_b200 runs on CUDA devices only; use the reference memfast package for CPU")
         if not torch.cuda.is_available():
             raise RuntimeError("CUDA is unavailable")
-        index = torch.cuda.current_device() if device.index is None else device.index
-        self.device = torch.device("cuda", index)
         _lib.load()
+        self.config, self.mode, self.workspace_bytes = config, mode, budget
+        self.device = torch.device("cuda", torch.cuda.current_device() if device.index is None else device.index)
         self.cache_dir = Path(cache_dir) if cache_dir is not None else cache_root() / "tuning"
-        self.workspace_bytes = int(workspace_mb * 1024**2)
         self.records = []
         self._selections = {}
         self._fingerprint = source_hash()
-        self._next_id = 0
-        self._matrix_cache = {}
+        self._programs = _ProgramCache()
+        self._names = 0
+
+    def _next_name(self):
+        name = f"matrix.{self._names}"
+        self._names += 1
+        return name
 
     def map(self, weight, *, bias=None, name=None):
         """Low-level layer-weight adapter using PyTorch [O,K] weight layout."""
-        if name is None:
-            name = f"matrix.{self._next_id}"
-            self._next_id += 1
-        return AnalogMatrix(weight, self, bias=bias, name=name)
+        return AnalogMatrix(weight, self, bias=bias, name=self._next_name() if name is None else name)
+
+    def map_quantized(self, codes, scales, *, zero_points=None, bias=None, name=None):
+        """Import integer [O,K] weights as ``scales * (codes - zero_points)``."""
+        return AnalogMatrix(codes, self, bias=bias, name=self._next_name() if name is None else name, scales=scales,
+                            zero_points=zero_points)
 
     def mm(self, input, mat2, *, out=None):
         """Simulate a two-dimensional matrix product, following torch.mm."""
@@ -227,183 +216,115 @@ class Simulator:
 
         return matmul(input, other, simulator=self, out=out)
 
-    def _matrix_for(self, matrix, checked=False, rows=1, program=None):
-        """Reprogram the RHS and reuse the cached program if its codes are unchanged.
-
-        A reprogrammed RHS keeps the cached program's name (sampling seed) and read
-        event, so in default mode the old and new programs give identical results
-        and the new one is kept without comparing codes on the host.  Tuned mode
-        compares, because the cached program also carries its schedule selections.
-        ``checked``: the caller verified the matrix finite in the quantiser's dtype;
-        ``rows``: vectors of the coming product (sizes the tensor-core workspace);
-        ``program``: a device copy of a host ``matrix`` to program from (the cache
-        follows the host tensor, as the reference's does for its operand).
-        """
-        identity = id(matrix)
-        record = self._matrix_cache.get(identity)
-        same_tensor = record is not None and record[0]() is matrix
-        metadata = (
-            tuple(matrix.shape), tuple(matrix.stride()), matrix.storage_offset(),
-            matrix.data_ptr(), matrix.dtype, matrix.device,
-        )
-        previous = record[2] if same_tensor else None
-        if previous is None:
-            name = f"matrix.{self._next_id}"
-            self._next_id += 1
-        else:
-            name = previous.name
-        source = matrix if program is None else program
-        if (
-            self.mode == "default"
-            and same_tensor
-            and record[1] == metadata
-            and (previous.config is self.config or previous.config == self.config)
-            and previous.packed.device == self.device
-            and previous.zero_correction is None
-            and previous.input_scale is None
-        ):
-            # Same tensor, same layout: program its current values into the cached
-            # module's buffers (no new module per call; same name and read event).
-            previous._reprogram(source.T, checked, rows)
-            return previous
-        programmed = AnalogMatrix(source.T, self, name=name, _checked=checked, _rows=rows)
-        if (
-            self.mode == "tuned"
-            and same_tensor
-            and record[1] == metadata
-            and (previous.config is self.config or previous.config == self.config)
-            and previous.packed.device == self.device
-            and torch.equal(previous.packed, programmed.packed)
-            and torch.equal(previous.weight_scale, programmed.weight_scale)
-        ):
-            return previous
-        if previous is not None:
-            programmed._event = previous._event
-        owner = weakref.ref(self)
-
-        def release(reference):
-            simulator = owner()
-            if simulator is not None:
-                cached = simulator._matrix_cache.get(identity)
-                if cached is not None and cached[0] is reference:
-                    simulator._matrix_cache.pop(identity, None)
-
-        self._matrix_cache[identity] = (weakref.ref(matrix, release), metadata, programmed)
-        return programmed
-
-    def map_quantized(self, codes, scales, *, zero_points=None, bias=None, name=None):
-        """Import integer [O,K] weights as ``scales * (codes - zero_points)``."""
-        if name is None:
-            name = f"matrix.{self._next_id}"
-            self._next_id += 1
-        return AnalogMatrix(codes, self, bias=bias, name=name, scales=scales, zero_points=zero_points)
-
     def report(self):
-        return dict(mode=self.mode, device=str(self.device), config=asdict(self.config),
-                    selections=self.records)
+        return dict(mode=self.mode, device=str(self.device), config=asdict(self.config), selections=self.records)
 
-    # ------------------------------------------------------------ tuned mode
-    def _key(self, matrix, x):
-        payload = dict(
-            config=asdict(self.config),
-            hardware=device_identity(self.device),
-            shape=list(x.shape),
-            output=matrix.out_features,
-            dtype=str(x.dtype),
-            sources=self._fingerprint,
-            workspace_bytes=self.workspace_bytes,
-            grid=dict(kernels=list(_GRID_KERNELS), arrays=list(_GRID_ARRAYS)),
-        )
-        payload = json.loads(json.dumps(payload))
-        return hashlib.sha256(json.dumps(payload, sort_keys=True).encode()).hexdigest(), payload
+    def _matrix_for(self, matrix, checked=False, rows=1, program=None):
+        """The programmed matrix for right-hand operand ``matrix`` [K, O] of a product.
 
-    def _admit(self, matrix, q, schedule):
-        n, m, _ = q.shape
-        native = _lib.schedule(**schedule)
-        resources = _lib.MFResources()
-        _lib.check(
-            _lib.load().mf_query(_lib.native_config(self.config), ct.byref(native), n, m, matrix.p,
-                                 ct.byref(resources)),
-            "mf_query",
-        )
-        need = matrix._workspace_size(n, schedule)
-        if need > self.workspace_bytes:
-            raise ResourceError("workspace budget")
-        return dict(workspace_bytes=need, threads=resources.threads)
+        As in the reference, every call programs ``matrix``'s current values, and a
+        program of the same tensor object keeps its name (sampling seed) and read
+        event.  In default mode the cached module is reprogrammed in place (the
+        result equals a new program with that name and event, so nothing is
+        compared).  Tuned mode builds a new program and keeps the cached one when
+        the codes and scales are unchanged, since the cached one also holds the
+        schedules selected for it.  ``checked``: the caller verified the matrix
+        finite in the quantiser's dtype; ``rows``: vectors of the coming product
+        (sizes the tensor-core workspace); ``program``: a device copy of a host
+        ``matrix`` to program from (the cache follows the caller's tensor).
+        """
+        cached, same_layout = self._programs.get(matrix)
+        reusable = (cached is not None and same_layout and cached.packed.device == self.device
+                    and (cached.config is self.config or cached.config == self.config))
+        source = matrix if program is None else program
+        if self.mode == "default" and reusable and cached.zero_correction is None and cached.input_scale is None:
+            cached._reprogram(source.T, checked, rows)
+            return cached
+        name = self._next_name() if cached is None else cached.name
+        fresh = AnalogMatrix(source.T, self, name=name, _checked=checked, _rows=rows)
+        if self.mode == "tuned" and reusable and torch.equal(cached.packed, fresh.packed) and \
+                torch.equal(cached.weight_scale, fresh.weight_scale):
+            return cached
+        if cached is not None:
+            fresh._event = cached._event
+        self._programs.put(matrix, fresh)
+        return fresh
 
     def _select(self, matrix, x, q, xscale, event):
-        started = time.perf_counter()
-        key, payload = self._key(matrix, x)
-        population = list(schedule_grid(self.config, q.shape[0], matrix.p))
-        reference_output = None
-        for baseline in [default_schedule(self.config), *population]:
-            try:
-                self._admit(matrix, q, baseline)
-                reference_output = matrix._execute(q, xscale, baseline, event)
-                break
-            except (ResourceError, torch.cuda.OutOfMemoryError):
-                torch.cuda.empty_cache()
-        if reference_output is None:
-            raise RuntimeError("no feasible reference schedule in the declared grid")
-        if not torch.isfinite(reference_output).all():
-            raise FloatingPointError("nonfinite default output during tuning")
-        path = self.cache_dir / f"{key}.json"
-        record = dict(key=key, layer=matrix.name, shape=list(x.shape), cache_hit=False,
-                      candidates=[], selected=None, complete=False)
-        self.records.append(record)
-        bits = reference_output.view(torch.int32 if reference_output.dtype == torch.float32 else torch.int64)
-        cached = self._selections.get(key)
-        if cached is None and path.is_file():
-            try:
-                content = json.loads(path.read_text(encoding="utf-8"))
-                if content["fingerprint"] == payload and content["complete"] and content["selected"] in population:
-                    cached = content["selected"]
-            except (KeyError, ValueError, TypeError):
-                cached = None
-        if cached is not None:
-            try:
-                self._admit(matrix, q, cached)
-                output = matrix._execute(q, xscale, cached, event)
-                if not torch.equal(bits, output.view(bits.dtype)):
-                    raise RuntimeError("cached schedule changes output")
-                record.update(cache_hit=True, selected=cached, complete=True,
-                              preparation_seconds=time.perf_counter() - started)
-                self._selections[key] = cached
-                return cached
-            except (ResourceError, torch.cuda.OutOfMemoryError):
-                torch.cuda.empty_cache()
-                cached = None
-        for schedule in population:
-            candidate = dict(schedule=schedule, status="rejected", timed_samples=0)
-            record["candidates"].append(candidate)
-            try:
-                candidate["resources"] = self._admit(matrix, q, schedule)
-                output = matrix._execute(q, xscale, schedule, event)
-                if not torch.equal(bits, output.view(bits.dtype)):
-                    raise RuntimeError("schedule changes output")
-                del output
-                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                start.record()
-                output = matrix._execute(q, xscale, schedule, event)
-                end.record()
-                end.synchronize()
-                candidate.update(status="accepted", seconds=start.elapsed_time(end) / 1000, timed_samples=1)
-                del output
-            except ResourceError as error:
-                candidate["reason"] = str(error)
-            except torch.cuda.OutOfMemoryError:
-                candidate["reason"] = "CUDA out of memory"
-                torch.cuda.empty_cache()
-        accepted = [item for item in record["candidates"] if item["status"] == "accepted"]
-        if not accepted:
-            raise RuntimeError("no feasible schedule in the declared grid")
-        selected = min(accepted, key=lambda item: item["seconds"])["schedule"]
-        record.update(selected=selected, complete=True, domain_count=len(population),
-                      preparation_seconds=time.perf_counter() - started)
-        atomic_write(path, json.dumps(dict(fingerprint=payload, complete=True, selected=selected,
-                                           candidates=record["candidates"]), sort_keys=True).encode())
-        self._selections[key] = selected
-        return selected
+        """Tuned-mode schedule for ``matrix`` on inputs shaped like ``x`` (tuning.Search)."""
+        return tuning.Search(self, matrix, x.shape, x.dtype, q, xscale, event).select(default_schedule(self.config))
+
+
+# ----------------------------------------------------------- checkpoints --
+def _check_checkpoint_codes(packed, config):
+    if not torch.is_tensor(packed) or packed.dtype not in _INTEGER_DTYPES:
+        raise ValueError("checkpoint packed weights must have an integer dtype")
+    if packed.numel():
+        low, high = torch.aminmax(packed.to(torch.int64))
+        if low.item() < 0 or high.item() > (1 << config.weight_bits) - 1:
+            raise ValueError("checkpoint packed weights exceed the configured bit width")
+
+
+def _finite_nonnegative(tensor):
+    return bool(torch.isfinite(tensor).all()) and not bool((tensor < 0).any())
+
+
+def _check_checkpoint_scales(scales):
+    if not torch.is_tensor(scales) or not scales.is_floating_point() or not _finite_nonnegative(scales):
+        raise ValueError("checkpoint weight scales must be finite and nonnegative")
+
+
+def _saved_configuration(saved):
+    """A checkpoint's Config dictionary in today's form: the removed ``output_noise``
+    effect must be zero and fields added since default (simulator.py:522-530)."""
+    config = dict(saved)
+    effects = dict(config["nonidealities"])
+    if effects.pop("output_noise", 0) != 0:
+        raise ValueError("checkpoint uses a removed noise model")
+    config["nonidealities"] = effects
+    for name in ("rows_per_read", "input_slice", "weight_slice", "bw_e"):
+        config.setdefault(name, None)
+    config.setdefault("weight_signed", True)
+    return config
+
+
+def _import_codes(codes, scales, zero_points, config, device):
+    """Program integer [O, K] weight codes meaning ``scales * (codes - zero_points)``
+    (simulator.py:173-185, 372-412): packed codes, per-read scales and, with zero
+    points, the per-read correction ``-zero * scale`` applied digitally after the
+    analog product."""
+    if codes.dtype not in _INTEGER_DTYPES:
+        raise ValueError("imported weight codes must have an integer dtype")
+    if config.bw_e is not None:
+        raise ValueError("native INT weight import requires bw_e=None")
+    signed = config.weight_signed
+    low = -(1 << (config.weight_bits - 1)) if signed else 0
+    high = (1 << (config.weight_bits - int(signed))) - 1
+    values = codes.detach().to(device=device, dtype=torch.int64)
+    smallest, largest = torch.aminmax(values)
+    if smallest.item() < low or largest.item() > high:
+        raise ValueError("weight codes exceed configured signedness or bit width")
+    dtype = torch.float64 if config.wide else torch.float32
+    shape = codes.shape
+
+    def per_element(value, name, **kwargs):
+        # [K, O]: rows follow the reduction dimension, as the packed codes do.
+        return expanded_parameter(value, shape, device, dtype, name, **kwargs).detach().T.contiguous()
+
+    code_ko = values.T.contiguous()
+    scale_ko = per_element(scales, "scales", positive=True)
+    check_read_scales(scale_ko, config, "weight scale")
+    packed, scale = pack_weight(code_ko, scale_ko, config)
+    correction = None
+    if zero_points is not None:
+        zeros_ko = per_element(zero_points, "zero_points")
+        check_read_scales(zeros_ko, config, "weight zero point")
+        k = shape[1]
+        first_rows = read_starts(math.ceil(k / config.array_size[0]), config, device).clamp_max(k - 1)
+        correction = -(zeros_ko[first_rows] * scale_ko[first_rows])
+        if not torch.isfinite(correction).all():
+            raise ValueError("scaled zero points exceed the reconstruction dtype")
+    return packed, scale, correction
 
 
 class AnalogMatrix(nn.Module):
@@ -416,75 +337,51 @@ class AnalogMatrix(nn.Module):
             raise ValueError("weight must be a nonempty [O,K] matrix")
         if not _checked and not finite_flags(weight)[0]:
             raise ValueError("weights must be finite")
+        config, device = simulator.config, simulator.device
         # Workspaces of the tensor-core kernels, one per stream, reused across calls:
-        # each starts with the K-major copy of the packed codes (valid while ready).
+        # each starts with the K-major copy of the packed codes (valid while flagged).
         self._workspaces, self._kmajor_bytes = {}, 0
         # Tensor-parallel column shard (sharding.shard_columns); None = all columns.
         self._column_shard = None
-        self.simulator, self.config, self.name = simulator, simulator.config, name
+        self.simulator, self.config, self.name = simulator, config, name
         self.out_features, self.in_features = weight.shape
-        self.p = math.ceil(self.out_features / self.config.array_size[1])
-        dtype = torch.float64 if self.config.wide else torch.float32
-        zero_correction = None
+        self.p = math.ceil(self.out_features / config.array_size[1])
+        reconstruction = torch.float64 if config.wide else torch.float32
         if scales is None:
             if not weight.is_floating_point():
                 raise ValueError("unquantized weight must be floating")
             if zero_points is not None:
                 raise ValueError("zero_points requires imported integer codes and scales")
-            self._prepare_workspace(math.ceil(self.in_features / self.config.array_size[0]), simulator.device,
-                                    _rows)
-            entry = self._workspaces.get(_lib.stream_of(simulator.device).value)
-            packed, scale, written = weight_tiles(
-                weight.detach().to(simulator.device), self.config, checked=_checked,
-                kmajor=None if entry is None else entry[0][: self._kmajor_bytes])
-            if entry is not None:
-                entry[1] = written
+            packed, scale = self._program_values(weight.detach().to(device), _checked, _rows)
+            correction = None
         else:
-            if weight.dtype not in (torch.uint8, torch.int8, torch.int16, torch.int32, torch.int64):
-                raise ValueError("imported weight codes must have an integer dtype")
-            if self.config.bw_e is not None:
-                raise ValueError("native INT weight import requires bw_e=None")
-            lower = -(1 << (self.config.weight_bits - 1)) if self.config.weight_signed else 0
-            upper = (1 << (self.config.weight_bits - int(self.config.weight_signed))) - 1
-            imported = weight.detach().to(device=simulator.device, dtype=torch.int64)
-            if (imported < lower).any() or (imported > upper).any():
-                raise ValueError("weight codes exceed configured signedness or bit width")
-            code = imported.T.contiguous()
-            scale_full = (
-                expanded_parameter(scales, weight.shape, simulator.device, dtype, "scales", positive=True)
-                .detach().T.contiguous()
-            )
-            check_read_scales(scale_full, self.config, "weight scale")
-            packed, scale = pack_weight(code, scale_full, self.config)
-            if zero_points is not None:
-                zeros = (
-                    expanded_parameter(zero_points, weight.shape, simulator.device, dtype, "zero_points")
-                    .detach().T.contiguous()
-                )
-                check_read_scales(zeros, self.config, "weight zero point")
-                r = self.config.array_size[0]
-                starts = read_starts(math.ceil(self.in_features / r), self.config, code.device)
-                indices = starts.clamp_max(self.in_features - 1)
-                zero_correction = -(zeros[indices] * scale_full[indices])
-                if not torch.isfinite(zero_correction).all():
-                    raise ValueError("scaled zero points exceed the reconstruction dtype")
+            packed, scale, correction = _import_codes(weight, scales, zero_points, config, device)
         self.register_buffer("packed", packed)
         self.register_buffer("weight_scale", scale)
-        self.register_buffer("zero_correction", zero_correction)
+        self.register_buffer("zero_correction", correction)
         self.register_buffer("input_scale", None)
-        if bias is not None and (
-            not bias.is_floating_point() or bias.shape != (self.out_features,) or not torch.isfinite(bias).all()
-        ):
+        if bias is not None and (not bias.is_floating_point() or bias.shape != (self.out_features,)
+                                 or not torch.isfinite(bias).all()):
             raise ValueError("bias must be finite and match out_features")
-        self.register_buffer(
-            "bias", None if bias is None else bias.detach().to(device=simulator.device, dtype=dtype).clone()
-        )
+        self.register_buffer("bias", None if bias is None else
+                             bias.detach().to(device=device, dtype=reconstruction).clone())
         if self.bias is not None and not torch.isfinite(self.bias).all():
             raise ValueError("bias exceeds the reconstruction dtype")
         self._event = 0
-        tag = int.from_bytes(hashlib.sha256(name.encode()).digest()[:4], "little")
-        self.seed = self.config.seed ^ tag
+        self.seed = config.seed ^ int.from_bytes(hashlib.sha256(name.encode()).digest()[:4], "little")
         self._prepared = {}
+
+    def _program_values(self, weight, checked, rows):
+        """Quantise and pack floating [O, K] weights, writing the tensor-core kernels'
+        K-major copy into this stream's workspace in the same pass when they read one."""
+        device = self.simulator.device
+        self._prepare_workspace(math.ceil(self.in_features / self.config.array_size[0]), device, rows)
+        entry = self._workspaces.get(_lib.stream_of(device).value)
+        packed, scale, written = weight_tiles(weight, self.config, checked=checked,
+                                              kmajor=None if entry is None else entry[0][: self._kmajor_bytes])
+        if entry is not None:
+            entry[1] = written
+        return packed, scale
 
     def set_input_scale(self, scale):
         """Fix symmetric activation scales for subsequent calls; None restores dynamic scales."""
@@ -501,75 +398,66 @@ class AnalogMatrix(nn.Module):
         self._prepared.clear()
         return self
 
+    # ----------------------------------------------------------- checkpoints
     def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
-        packed = state_dict.get(prefix + "packed")
-        if packed is not None:
-            if not torch.is_tensor(packed) or packed.dtype not in (
-                torch.uint8, torch.int8, torch.int16, torch.int32, torch.int64
-            ):
-                raise ValueError("checkpoint packed weights must have an integer dtype")
-            codes = packed.to(torch.int64)
-            if (codes < 0).any() or (codes > (1 << self.config.weight_bits) - 1).any():
-                raise ValueError("checkpoint packed weights exceed the configured bit width")
-        scales = state_dict.get(prefix + "weight_scale")
-        if scales is not None and (
-            not torch.is_tensor(scales) or not scales.is_floating_point()
-            or not torch.isfinite(scales).all() or (scales < 0).any()
-        ):
-            raise ValueError("checkpoint weight scales must be finite and nonnegative")
-        for name in ("input_scale", "zero_correction"):
-            key = prefix + name
-            if key in state_dict and self._buffers[name] is None:
-                self._buffers[name] = torch.empty_like(state_dict[key], device=self.packed.device)
+        """Validate a checkpoint's buffers before loading them (simulator.py:452-493)."""
+        if prefix + "packed" in state_dict:
+            _check_checkpoint_codes(state_dict[prefix + "packed"], self.config)
+        if prefix + "weight_scale" in state_dict:
+            _check_checkpoint_scales(state_dict[prefix + "weight_scale"])
+        # Optional buffers this module does not hold yet take the saved shape first.
+        for optional in ("input_scale", "zero_correction"):
+            saved = state_dict.get(prefix + optional)
+            if saved is not None and self._buffers[optional] is None:
+                self._buffers[optional] = torch.empty_like(saved, device=self.packed.device)
         super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
         self._drop_workspace()
-        if not torch.isfinite(self.weight_scale).all() or (self.weight_scale < 0).any():
+        if not _finite_nonnegative(self.weight_scale):
             raise ValueError("checkpoint weight scales exceed the reconstruction dtype")
         if self.bias is not None and not torch.isfinite(self.bias).all():
             raise ValueError("checkpoint bias exceeds the reconstruction dtype")
         if self.input_scale is not None:
             self.set_input_scale(self.input_scale)
-        if self.zero_correction is not None:
-            expected = (self.weight_scale.shape[0], self.out_features)
-            if tuple(self.zero_correction.shape) != expected:
+        correction = self.zero_correction
+        if correction is not None:
+            if tuple(correction.shape) != (self.weight_scale.shape[0], self.out_features):
                 raise ValueError("checkpoint zero-point correction has an invalid shape")
-            if not torch.isfinite(self.zero_correction).all():
+            if not torch.isfinite(correction).all():
                 raise ValueError("checkpoint zero-point correction must be finite")
 
     def _apply(self, fn, recurse=True):
-        programmed = {name: buffer for name, buffer in self._buffers.items() if buffer is not None}
+        """Device moves apply to the programmed buffers; dtype casts do not (the codes and
+        scales are the device's programmed state).  A cast buffer is replaced by its
+        original values on the new device, so no precision is lost."""
+        originals = {name: tensor for name, tensor in self._buffers.items() if tensor is not None}
         super()._apply(fn, recurse=recurse)
-        for name, original in programmed.items():
-            transformed = self._buffers[name]
-            if transformed.dtype != original.dtype:
-                self._buffers[name] = original.to(device=transformed.device)
-            if transformed.device != original.device:
-                self._prepared.clear()
-                self._drop_workspace()
+        moved = False
+        for name, original in originals.items():
+            current = self._buffers[name]
+            moved |= current.device != original.device
+            if current.dtype != original.dtype:
+                self._buffers[name] = original.to(device=current.device)
+        if moved:
+            self._prepared.clear()
+            self._drop_workspace()
         return self
 
     def get_extra_state(self):
-        return dict(config=asdict(self.config), in_features=self.in_features,
-                    out_features=self.out_features, name=self.name, seed=self.seed, event=self._event)
+        return dict(config=asdict(self.config), in_features=self.in_features, out_features=self.out_features,
+                    name=self.name, seed=self.seed, event=self._event)
 
     def set_extra_state(self, state):
-        for key in ("in_features", "out_features"):
-            if key in state and (type(state[key]) is not int or state[key] != getattr(self, key)):
+        for dimension in ("in_features", "out_features"):
+            saved = state.get(dimension, getattr(self, dimension))
+            if type(saved) is not int or saved != getattr(self, dimension):
                 raise ValueError("checkpoint logical matrix dimensions differ")
-        loaded = dict(state["config"])
-        effects = dict(loaded["nonidealities"])
-        if effects.pop("output_noise", 0) != 0:
-            raise ValueError("checkpoint uses a removed noise model")
-        loaded["nonidealities"] = effects
-        for name in ("rows_per_read", "input_slice", "weight_slice", "bw_e"):
-            loaded.setdefault(name, None)
-        loaded.setdefault("weight_signed", True)
-        if loaded != asdict(self.config):
+        if _saved_configuration(state["config"]) != asdict(self.config):
             raise ValueError("checkpoint physical configuration differs")
-        if type(state["seed"]) is not int or not 0 <= state["seed"] < 2**32:
+        seed = state["seed"]
+        if type(seed) is not int or not 0 <= seed < 2**32:
             raise ValueError("invalid checkpoint sampling seed")
         self.reset_read(state["event"])
-        self.name, self.seed, self._event = state["name"], state["seed"], state["event"]
+        self.name, self.seed = state["name"], seed
         self._prepared.clear()
 
     def reset_read(self, event=0):
@@ -602,6 +490,8 @@ class AnalogMatrix(nn.Module):
         self._kmajor_bytes = self._kmajor_size(m, default_schedule(self.config))
         if self._kmajor_bytes:
             need = self._workspace_size(max(rows, 1), default_schedule(self.config), m)
+            if need - self._kmajor_bytes > _KEPT_SCRATCH_BYTES:
+                return   # a per-call workspace (see _launch): nothing to program in place
             self._workspaces[_lib.stream_of(device).value] = [torch.empty(need, dtype=torch.uint8, device=device),
                                                                False]
 
@@ -643,7 +533,7 @@ class AnalogMatrix(nn.Module):
         return _workspace_bytes(self.config, n, m, self.p, tuple(sorted(schedule.items())))
 
     def _execute(self, q, xscale, schedule, event, stable=False, *, vector_offset=0, input_flag=None,
-                 input_errors=None, tiles=None, agree=None):
+                 input_errors=None, tiles=None, agree=None, output=None):
         """One fused device call: analog partials, scales, read sums and bias.
 
         ``input_flag``: device int32 set by a quantiser that checks finiteness on the
@@ -652,8 +542,10 @@ class AnalogMatrix(nn.Module):
         ``tiles``: output tiles [t0, t1) only (a column shard; noise addresses stay
         global), giving columns [t0*cols, min(t1*cols, out_features)).
         ``agree``: combines this shard's finiteness with the other shards' (the FP64
-        rerun is decided for the whole product)."""
-        output = self._launch(q, xscale, schedule, event, stable=stable, vector_offset=vector_offset, tiles=tiles)
+        rerun is decided for the whole product); ``output``: a buffer of the product's
+        shape and dtype to write into (the FP64 rerun allocates its own)."""
+        output = self._launch(q, xscale, schedule, event, stable=stable, vector_offset=vector_offset, tiles=tiles,
+                              output=output)
         # One host synchronisation decides both the FP64 rerun of a narrow config
         # (simulator.py:614-615) and, in forward, the non-finite error.
         # flags: [input error code, output non-finite]; one device-to-host read.
@@ -671,6 +563,27 @@ class AnalogMatrix(nn.Module):
         if not self.config.wide and not stable and not self._finite:
             return self._execute(q, xscale, schedule, event, stable=True, vector_offset=vector_offset, tiles=tiles)
         return output
+
+    def _zero_point_correction(self, q, xscale, output, c0, c1, wide):
+        """Add the digital zero-point correction of imported codes (simulator.py:587-611):
+        per read, the sum of the signed input codes times the input scale times
+        ``-zero * weight scale``, summed over reads."""
+        n = q.shape[0]
+        half = 1 << (self.config.activation_bits - 1)
+        codes = (q.to(torch.int64).reshape(n, -1) ^ half) - half
+        rows, read = self.config.array_size[0], self.config.read_rows
+        spans = torch.nn.functional.pad(codes.reshape(n, -1, rows), (0, self.config.reads_per_array * read - rows))
+        read_sums = spans.reshape(n, -1, read).sum(-1)
+        if not wide:
+            dtype = output.dtype
+            output += (read_sums.to(dtype) * xscale.to(dtype)) @ self.zero_correction[:, c0:c1].to(dtype)
+            return
+        width = self.config.array_size[1]
+        for begin in range(c0, c1, width):
+            end = min(begin + width, c1)
+            terms = restore_scales(read_sums[:, :, None], xscale[:, :, None],
+                                   self.zero_correction[None, :, begin:end])
+            output[:, begin - c0:end - c0] += terms.sum(1)
 
     def _launch(self, q, xscale, schedule, event, *, stable=False, vector_offset=0, tiles=None, output=None):
         """Enqueue the product on the current stream (no host synchronisation) into
@@ -694,7 +607,12 @@ class AnalogMatrix(nn.Module):
         stream = _lib.stream_of(q.device)
         kmajor_ready = 0
         kmajor_bytes = 0 if stable else self._kmajor_size(packed.shape[0], schedule)
-        if kmajor_bytes:
+        if kmajor_bytes and workspace_bytes - kmajor_bytes > _KEPT_SCRATCH_BYTES:
+            # Per-call workspace; its K-major copy is rebuilt by the call (a pass over the
+            # packed codes, small next to the conductance operand the call writes).
+            workspace = torch.empty(workspace_bytes, dtype=torch.uint8, device=q.device)
+            kmajor_bytes = 0
+        elif kmajor_bytes:
             # Tensor-core kernels: keep a workspace per stream (launches on different
             # streams may overlap), whose leading K-major weight copy stays valid
             # until the codes change; a larger one keeps the copy.
@@ -713,7 +631,7 @@ class AnalogMatrix(nn.Module):
             workspace, workspace_bytes, kmajor_ready = entry[0], entry[0].numel(), int(entry[1])
         else:
             workspace = torch.empty(max(workspace_bytes, 1), dtype=torch.uint8, device=q.device)
-        native = _lib.schedule(**schedule, kmajor_ready=kmajor_ready)
+        native = _lib.schedule(**dict(schedule, kmajor_ready=kmajor_ready))
         _lib.check(
             _lib.load().mf_sliced_mm(
                 _lib.native_config(self.config), ct.byref(native), _lib.ptr(q), _lib.ptr(xscale),
@@ -727,23 +645,7 @@ class AnalogMatrix(nn.Module):
         if kmajor_bytes:
             entry[1] = True
         if self.zero_correction is not None:
-            bits = self.config.activation_bits
-            signed = q.to(torch.int64).reshape(n, -1)
-            signed = (signed ^ (1 << (bits - 1))) - (1 << (bits - 1))
-            r, step = self.config.array_size[0], self.config.read_rows
-            padded = torch.nn.functional.pad(signed.reshape(n, -1, r), (0, self.config.reads_per_array * step - r))
-            sums = padded.reshape(n, -1, step).sum(-1)
-            c = self.config.array_size[1]
-            if wide:
-                for begin in range(c0, c1, c):
-                    end = min(begin + c, c1)
-                    correction = restore_scales(
-                        sums[:, :, None], xscale[:, :, None], self.zero_correction[None, :, begin:end]
-                    ).sum(1)
-                    output[:, begin - c0:end - c0] += correction
-            else:
-                correction = (sums.to(dtype) * xscale.to(dtype)) @ self.zero_correction[:, c0:c1].to(dtype)
-                output += correction
+            self._zero_point_correction(q, xscale, output, c0, c1, wide)
             if self.bias is not None:
                 output += self.bias[c0:c1]
         return output
@@ -754,17 +656,17 @@ class AnalogMatrix(nn.Module):
         return self._forward(x) if shard is None else shard(self, x)
 
     def _forward(self, x, checked=False, vector_offset=0, tiles=None, agree=None, input_flag=None,
-                 input_errors=None):
+                 input_errors=None, out=None):
         """forward(); ``checked``: the caller verified x finite in the quantiser's dtype;
         ``vector_offset``: global index of x's first vector (noise addresses of row shards);
         ``tiles``/``agree``: a column shard, as in ``_execute``; ``input_flag`` /
-        ``input_errors``: a deferred operand check, as in ``_execute``."""
+        ``input_errors``: a deferred operand check, as in ``_execute``; ``out``: a
+        contiguous-rows [vectors, width] buffer of x's dtype receiving the result."""
         if x.ndim < 1 or x.shape[-1] != self.in_features or not x.is_floating_point():
             raise ValueError("input must be floating with matching in_features")
         if x.device != self.packed.device or x.device != self.simulator.device:
             raise ValueError("input and simulator must use the same device")
-        scale_dtype = torch.float64 if self.config.wide else torch.float32
-        if self.weight_scale.dtype != scale_dtype:
+        if self.weight_scale.dtype != (torch.float64 if self.config.wide else torch.float32):
             raise RuntimeError("keep simulator scale buffers at their mapped dtype")
         shape = x.shape
         cols = self.config.array_size[1]
@@ -776,18 +678,18 @@ class AnalogMatrix(nn.Module):
             raise OverflowError("read-event counter exhausted")
         q, xscale = input_tiles(x.reshape(-1, self.in_features), self.config, self.input_scale, checked=checked)
         output = self._product(q, xscale, shape, x.dtype, vector_offset=vector_offset, tiles=tiles, agree=agree,
-                               input_flag=input_flag, input_errors=input_errors)
+                               input_flag=input_flag, input_errors=input_errors, out=out)
         return output.reshape(*shape[:-1], width)
 
     def _product(self, q, xscale, shape, dtype, *, vector_offset=0, input_flag=None, input_errors=None,
-                 tiles=None, agree=None):
+                 tiles=None, agree=None, out=None):
         """forward() from quantised codes on (simulator.py:631-646): schedule, product,
         non-finite checks, ``dtype`` result, read event.  ``shape``/``dtype`` describe
         the caller's input (tuned-mode key); ``input_flag`` as in ``_execute``."""
         event = self._event
         schedule = default_schedule(self.config)
-        key = tuple(shape), str(dtype)
         if self.simulator.mode == "tuned":
+            key = tuple(shape), str(dtype)
             if key not in self._prepared:
                 if input_flag is not None and input_flag[0].item():
                     raise ValueError((input_errors or {}).get(input_flag[0].item(), "quantized values must be finite"))
@@ -795,13 +697,22 @@ class AnalogMatrix(nn.Module):
                     self._prepared[key] = self.simulator._select(
                         self, types.SimpleNamespace(shape=tuple(shape), dtype=dtype), q, xscale, event)
             schedule = self._prepared[key]
+        direct = out if out is not None and out.dtype == (torch.float64 if self.config.wide else torch.float32) \
+            else None
         output = self._execute(q, xscale, schedule, event, vector_offset=vector_offset, input_flag=input_flag,
-                               input_errors=input_errors, tiles=tiles, agree=agree)
+                               input_errors=input_errors, tiles=tiles, agree=agree, output=direct)
         finite = self._finite and (output.dtype == dtype or finite_flags(output, dtypes=[dtype])[0])
         if agree is not None:
             finite = agree(finite)
         output = output.to(dtype)
         if not finite:
             raise FloatingPointError("nonfinite analog output")
+        if out is not None and output.data_ptr() != out.data_ptr():
+            out.copy_(output)
+            output = out
         self._event += 1
         return output
+
+
+__all__ = ["Simulator", "AnalogMatrix", "default_schedule", "schedule_grid", "restore_scales", "atomic_write",
+           "device_identity", "ResourceError"]

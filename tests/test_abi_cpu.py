@@ -82,3 +82,42 @@ def test_simulator_refuses_cpu():
 
     with pytest.raises(ValueError):
         mf.Simulator(device="cpu")
+
+
+def test_debug_stall_hook_validates_its_arguments():
+    """The failure-detection test hook refuses a negative stage or an out-of-range budget
+    (and so arms nothing) without touching a GPU."""
+    from memfast_b200 import _lib
+
+    lib = _lib.load()
+    for stage, cycles in ((-1, 10_000), (0, 10), (0, 5_000_000_000)):
+        assert lib.mf_debug_stall_next_launch(stage, cycles) == _lib.MF_ERR_INVALID
+        assert "mf_debug_stall_next_launch" in _lib.last_error()
+
+
+def test_schedule_grid_lists_each_execution_once():
+    """The tuned-mode domain of the headline configuration covers all three ideal kernel
+    families and both raster orders of the tensor-core ones, each execution once
+    (mf_query resolves schedules on the host)."""
+    from memfast_b200 import Config, Nonidealities
+    from memfast_b200.tuning import _PATH_AXES, resolve, schedule_grid
+
+    config = Config(array_size=(128, 128), rows_per_read=32, weight_quant_gran=(32, 1), input_quant_gran=(1, 32),
+                    input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2), adc_bits=(6, 7, 7, 8, 8),
+                    nonidealities=Nonidealities(write_variation=0.0))
+    domain = list(schedule_grid(config, 4096, 32, 32))
+    identities = []
+    for schedule in domain:
+        path, _ = resolve(config, schedule, 4096, 32, 32)
+        identities.append((path,) + tuple(schedule[axis] for axis in _PATH_AXES[path]))
+    assert len(identities) == len(set(identities))
+    paths = {identity[0] for identity in identities}
+    assert paths == {"generic_ideal", "packed", "fp8_planes"}
+    assert {i[:2] for i in identities if i[0] in ("packed", "fp8_planes")} == {
+        ("packed", 0), ("packed", 1), ("fp8_planes", 0), ("fp8_planes", 1)}
+    # Nonideal: SIMT currents over restore-group sizes, tensor-core currents in both orders.
+    noisy = Config(array_size=(128, 128), rows_per_read=32, weight_quant_gran=(32, 1), input_quant_gran=(1, 32),
+                   input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2), adc_bits=(6, 7, 7, 8, 8),
+                   nonidealities=Nonidealities(write_variation=0.02))
+    paths = [resolve(noisy, s, 64, 4, 4)[0] for s in schedule_grid(noisy, 64, 4, 4)]
+    assert paths.count("tc_currents") == 2 and paths.count("simt_currents") == 3   # arrays 1, 2, 4
