@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define MF_ABI_VERSION 2
+#define MF_ABI_VERSION 3
 #define MF_MAX_SLICES 32
 
 typedef enum {
@@ -84,12 +84,16 @@ typedef struct {
                            (32-row reads), else FP16 digit dots; nonideal: FP16 digit x
                            conductance currents when the configuration fits), 3 tcgen05 FP8
                            digit planes (ideal) */
-    int32_t tile_n;     /* vectors per CTA (generic: 8,16,32) */
-    int32_t tile_o;     /* output columns per CTA (generic: 32,64,128) */
+    int32_t tile_n;     /* reserved: no kernel reads it (the SIMT kernels size their CTAs */
+    int32_t tile_o;     /* from the configuration) */
     int32_t arrays;     /* tiles restored per group in physical mode (>=1) */
     int32_t kmajor_ready; /* 1: the workspace starts with the K-major weight copy that
                              mf_program_rhs wrote for these packed weights (tensor-core
                              kernels then skip rebuilding it); 0: rebuilt per call */
+    int32_t raster;     /* tensor-core kernels, order in which CTAs (128 vectors x one column
+                           block each) are launched: 0 = vector blocks first (the CTAs in
+                           flight share weight tiles in L2), 1 = column blocks first (they
+                           share input-code tiles); the output is the same either way */
 } mf_schedule;
 
 typedef struct {
@@ -97,6 +101,7 @@ typedef struct {
     int32_t threads, shared_bytes, registers, local_bytes, blocks_per_sm;
     size_t kmajor_bytes;  /* > 0: the chosen kernel reads a K-major weight copy of this many
                              bytes at the start of its workspace (see kmajor_ready) */
+    int32_t path;         /* kernel family the schedule resolves to: an mf_path value, below */
 } mf_resources;
 
 /* One channel group of a 2-D convolution over an NCHW input (AnalogConv2d,
@@ -172,7 +177,10 @@ mf_status mf_program_rhs(const mf_config* cfg, const void* b, int32_t b_dtype, i
  *     nothing; use mf_quantize_input with a workspace instead.
  *   - One array per device: calls that can overlap on a device (other streams,
  *     other host threads without ordering between them) race on it and give
- *     wrong codes.  Keep such calls on one stream. */
+ *     wrong codes.  Keep such calls on one stream.
+ *   - The array's address is looked up once per device and kept for the life of
+ *     the process.  cudaDeviceReset unloads the module, so that address does not
+ *     survive it: do not call this entry point on a device after resetting it. */
 mf_status mf_quantize_input_static(const mf_config* cfg, const void* x, int32_t x_dtype, int64_t n,
                                    int64_t k, int64_t ldx, const void* fixed_scale, void* codes,
                                    void* xscale, void* stream);
@@ -247,6 +255,34 @@ mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const 
 mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedule, int64_t n,
                                  int32_t m, int32_t p, int32_t tile_begin, int32_t tile_end,
                                  size_t* bytes);
+
+/* Kernel families behind mf_sliced_mm.  The reference has one pair of SIMT
+ * kernels (memfast/kernels.cu:43-202); this engine picks among these per
+ * configuration and schedule. */
+typedef enum {
+    MF_PATH_NONE = 0,
+    MF_PATH_GENERIC_IDEAL = 1,   /* ideal devices, dp4a digit dots (SIMT) */
+    MF_PATH_PACKED = 2,          /* ideal devices, tcgen05 kind::i8 packed counts */
+    MF_PATH_FP8_PLANES = 3,      /* ideal devices, tcgen05 kind::f8f6f4 digit planes */
+    MF_PATH_TC_CURRENTS = 4,     /* tcgen05 kind::f16 digit x conductance (or digit) currents */
+    MF_PATH_SIMT_CURRENTS = 5    /* restored conductances, FP32/FP64 SIMT currents */
+} mf_path;
+
+/* The mf_path of this thread's last successful mf_sliced_mm call (MF_PATH_NONE
+ * before one).  Tests and tuned-mode reports use it to see which kernel ran. */
+int32_t mf_last_path(void);
+
+/* Test hook for the failure-detection path (no counterpart in the reference,
+ * which has no device-side waits).  Arms a one-shot stall consumed by the next
+ * mf_sliced_mm call in this process: if that call runs the packed tcgen05
+ * kernel, its load producer issues nothing from pipeline stage `stop_stage` on
+ * (a 32-row stage; reads of 64 rows take two), so every wait on a later stage
+ * runs out after `wait_cycles` SM clock cycles instead of about two seconds.
+ * Each CTA then records the wait's code in the device error word, drains its
+ * own loads and MMAs, frees its TMEM and exits, and mf_take_device_error reports
+ * MF_ERR_CUDA; the library stays usable.  Other paths ignore the stall.
+ * MF_ERR_INVALID unless stop_stage >= 0 and 1000 <= wait_cycles <= 4e9. */
+mf_status mf_debug_stall_next_launch(int32_t stop_stage, int64_t wait_cycles);
 
 /* Reads and clears the library's device error word (a synchronising call).  A
  * non-zero code means a bounded device-side wait gave up inside a kernel: the

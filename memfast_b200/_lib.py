@@ -15,11 +15,13 @@ import torch
 
 PACKAGE = Path(__file__).resolve().parent
 LIBRARY = PACKAGE / "libmemfast_b200.so"
-ABI_VERSION = 2
+ABI_VERSION = 3
 MAX_SLICES = 32
 
 STATIC_QUANTIZE_SCRATCH_BYTES = 4 << 20
 MF_OK, MF_ERR_INVALID, MF_ERR_RESOURCE, MF_ERR_CUDA, MF_ERR_UNSUPPORTED = range(5)
+# mf_path: the kernel family of a thread's last mf_sliced_mm call (mf_last_path).
+PATHS = {0: "none", 1: "generic_ideal", 2: "packed", 3: "fp8_planes", 4: "tc_currents", 5: "simt_currents"}
 DTYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 3}
 
 
@@ -53,14 +55,14 @@ class MFConfig(ct.Structure):
 
 class MFSchedule(ct.Structure):
     _fields_ = [("kernel", ct.c_int32), ("tile_n", ct.c_int32), ("tile_o", ct.c_int32),
-                ("arrays", ct.c_int32), ("kmajor_ready", ct.c_int32)]
+                ("arrays", ct.c_int32), ("kmajor_ready", ct.c_int32), ("raster", ct.c_int32)]
 
 
 class MFResources(ct.Structure):
     _fields_ = [("workspace_bytes", ct.c_size_t), ("threads", ct.c_int32),
                 ("shared_bytes", ct.c_int32), ("registers", ct.c_int32),
                 ("local_bytes", ct.c_int32), ("blocks_per_sm", ct.c_int32),
-                ("kmajor_bytes", ct.c_size_t)]
+                ("kmajor_bytes", ct.c_size_t), ("path", ct.c_int32)]
 
 
 class MFConv2d(ct.Structure):
@@ -75,6 +77,8 @@ _VOID = ct.c_void_p
 _SIGNATURES = {
     "mf_abi_version": (ct.c_int32, []),
     "mf_launch_count": (ct.c_uint64, []),
+    "mf_last_path": (ct.c_int32, []),
+    "mf_debug_stall_next_launch": (ct.c_int, [ct.c_int32, ct.c_int64]),
     "mf_last_error": (ct.c_int32, [ct.c_char_p, ct.c_size_t]),
     "mf_device_check": (ct.c_int, [ct.c_int32, ct.POINTER(ct.c_int32)]),
     "mf_quantize_workspace": (ct.c_int, [ct.POINTER(MFConfig), ct.c_int32, ct.c_int64, ct.c_int64,
@@ -210,8 +214,8 @@ def _native_config(config):
     return c
 
 
-def schedule(kernel=0, tile_n=32, tile_o=64, arrays=2, kmajor_ready=0):
-    return MFSchedule(kernel, tile_n, tile_o, arrays, kmajor_ready)
+def schedule(kernel=0, tile_n=32, tile_o=64, arrays=2, kmajor_ready=0, raster=0):
+    return MFSchedule(kernel, tile_n, tile_o, arrays, kmajor_ready, raster)
 
 
 def stream_of(device):

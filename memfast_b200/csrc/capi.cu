@@ -17,6 +17,10 @@
 namespace mf {
 
 static thread_local std::string g_last_error;
+static thread_local int32_t g_last_path = MF_PATH_NONE;
+// mf_debug_stall_next_launch: armed by the test hook, consumed by the next mf_sliced_mm.
+static std::atomic<int32_t> g_stall_stage{-1};
+static std::atomic<int64_t> g_stall_cycles{0};
 static std::atomic<unsigned long long> g_launches{0};
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
@@ -255,8 +259,10 @@ mf_status mf_quantize_input_static(const mf_config* cfg, const void* x, int32_t 
     void* scratch = nullptr;
     st = static_scratch(&scratch);
     if (st) return st;
-    // The shared quantiser clears the maxima it uses (cudaMemsetAsync) before
-    // the max pass, so nothing from an earlier call leaks into this one.
+    // Nothing from an earlier call leaks into this one: each path of the shared
+    // quantiser either clears the maxima before its atomic max pass
+    // (cudaMemsetAsync) or, in the one-pass row-group kernel, writes every maximum
+    // it later reads; a fixed scale reads none.
     return quantize_input(*cfg, x, x_dtype, n, k, ldx, fixed_scale, codes, xscale, scratch,
                           MF_STATIC_QUANTIZE_SCRATCH_BYTES, (cudaStream_t)stream);
 }
@@ -313,7 +319,7 @@ static bool use_tc(const mf_config& c, const mf_schedule& s, int32_t m, int32_t 
 }
 
 static mf_schedule schedule_or_default(const mf_schedule* s) {
-    mf_schedule d{0, 32, 64, 2, 0};
+    mf_schedule d{0, 32, 64, 2, 0, 0};
     return s ? *s : d;
 }
 
@@ -328,7 +334,7 @@ mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedu
     mf_schedule s = schedule_or_default(schedule);
     if (use_packed(*cfg, s, m, 0)) *bytes = tc_packed_workspace_bytes(*cfg, n, m, p, tile_end - tile_begin);
     else if (use_tc(*cfg, s, m, 0)) *bytes = tc_workspace_bytes(*cfg, m, p);
-    else if (use_tc_physical(*cfg, s, m, 0)) *bytes = tc_physical_workspace_bytes(*cfg, m, tile_end - tile_begin);
+    else if (use_tc_physical(*cfg, s, m, 0)) *bytes = tc_physical_workspace_bytes(*cfg, n, m, tile_end - tile_begin);
     else *bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, tile_end - tile_begin);
     return MF_OK;
 }
@@ -355,15 +361,47 @@ mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const 
         return MF_ERR_RESOURCE;
     }
     mf_schedule s = schedule_or_default(schedule);
+    if (s.raster < 0 || s.raster > 1) {
+        set_error("mf_sliced_mm: raster must be 0 or 1");
+        return MF_ERR_INVALID;
+    }
+    // A stall armed by mf_debug_stall_next_launch applies to this call only, whatever path it takes.
+    const int32_t stall_stage = g_stall_stage.exchange(-1);
     MMArgs a{codes, xscale, packed, wscale, bias, out, n, m, p, out_features, ldo, tile_begin, tile_end,
-             seed, event, vector_offset, stable, s.kmajor_ready != 0};
-    if (use_packed(*cfg, s, m, stable))
-        return tc_packed_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
-    if (use_tc(*cfg, s, m, stable)) return tc_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
-    if (use_tc_physical(*cfg, s, m, stable))
-        return tc_physical_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
-    if (use_ideal(*cfg, s)) return generic_ideal(*cfg, s, a, (cudaStream_t)stream);
-    return physical(*cfg, s, a, workspace, workspace_bytes, (cudaStream_t)stream);
+             seed, event, vector_offset, stable, s.kmajor_ready != 0, s.raster, stall_stage,
+             g_stall_cycles.load()};
+    int32_t path;
+    mf_status r;
+    if (use_packed(*cfg, s, m, stable)) {
+        path = MF_PATH_PACKED;
+        r = tc_packed_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
+    } else if (use_tc(*cfg, s, m, stable)) {
+        path = MF_PATH_FP8_PLANES;
+        r = tc_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
+    } else if (use_tc_physical(*cfg, s, m, stable)) {
+        path = MF_PATH_TC_CURRENTS;
+        r = tc_physical_sliced_mm(*cfg, a, workspace, workspace_bytes, (cudaStream_t)stream);
+    } else if (use_ideal(*cfg, s)) {
+        path = MF_PATH_GENERIC_IDEAL;
+        r = generic_ideal(*cfg, s, a, (cudaStream_t)stream);
+    } else {
+        path = MF_PATH_SIMT_CURRENTS;
+        r = physical(*cfg, s, a, workspace, workspace_bytes, (cudaStream_t)stream);
+    }
+    if (r == MF_OK) g_last_path = path;
+    return r;
+}
+
+int32_t mf_last_path(void) { return g_last_path; }
+
+mf_status mf_debug_stall_next_launch(int32_t stop_stage, int64_t wait_cycles) {
+    if (stop_stage < 0 || wait_cycles < 1000 || wait_cycles > 4000000000LL) {
+        set_error("mf_debug_stall_next_launch: stop_stage >= 0 and wait_cycles in [1000, 4e9] required");
+        return MF_ERR_INVALID;
+    }
+    g_stall_cycles.store(wait_cycles);
+    g_stall_stage.store(stop_stage);
+    return MF_OK;
 }
 
 mf_status mf_query(const mf_config* cfg, const mf_schedule* schedule, int64_t n, int32_t m, int32_t p,
@@ -376,20 +414,30 @@ mf_status mf_query(const mf_config* cfg, const mf_schedule* schedule, int64_t n,
     }
     mf_schedule s = schedule_or_default(schedule);
     memset(out, 0, sizeof(*out));
+    if (s.raster < 0 || s.raster > 1) {
+        set_error("mf_query: raster must be 0 or 1");
+        return MF_ERR_INVALID;
+    }
     if (use_packed(*cfg, s, m, 0)) {
         out->workspace_bytes = tc_packed_workspace_bytes(*cfg, n, m, p, p);
         out->threads = tc_packed_threads();
         out->kmajor_bytes = (size_t)p * cfg->cols * m * cfg->rows;
+        out->path = MF_PATH_PACKED;
     } else if (use_tc(*cfg, s, m, 0)) {
         out->workspace_bytes = tc_workspace_bytes(*cfg, m, p);
         out->threads = tc_block_threads();
+        out->path = MF_PATH_FP8_PLANES;
     } else if (use_tc_physical(*cfg, s, m, 0)) {
-        out->workspace_bytes = tc_physical_workspace_bytes(*cfg, m, p);
+        // The conductance (or digit) operand is built from the packed codes each call:
+        // no K-major copy.
+        out->workspace_bytes = tc_physical_workspace_bytes(*cfg, n, m, p);
         out->threads = tc_physical_threads();
-        out->kmajor_bytes = (size_t)p * cfg->cols * m * cfg->rows;
+        out->path = MF_PATH_TC_CURRENTS;
     } else {
-        out->workspace_bytes = use_ideal(*cfg, s) ? 0 : physical_workspace_bytes(*cfg, s, m, p);
+        const bool ideal = use_ideal(*cfg, s);
+        out->workspace_bytes = ideal ? 0 : physical_workspace_bytes(*cfg, s, m, p);
         out->threads = 256;
+        out->path = ideal ? MF_PATH_GENERIC_IDEAL : MF_PATH_SIMT_CURRENTS;
     }
     return MF_OK;
 }

@@ -59,7 +59,16 @@ struct MMArgs {
     int64_t vector_offset;
     int32_t stable;
     int32_t kmajor_ready;   // the workspace already starts with the K-major weight copy
+    int32_t raster;         // tensor-core kernels: 0 = vector blocks first, 1 = column blocks first
+    int32_t stall_stage;    // mf_debug_stall_next_launch: packed kernel stops its loads here (-1 off)
+    int64_t stall_cycles;   // ... and its waits give up after this many SM cycles
 };
+
+// Grid of a tensor-core launch over nb vector blocks x cb column blocks in the
+// schedule's raster order, and a CTA's (vector block, column block) in it.
+inline dim3 raster_grid(long long nb, long long cb, int raster) {
+    return raster ? dim3((unsigned)cb, (unsigned)nb) : dim3((unsigned)nb, (unsigned)cb);
+}
 
 // Largest |signed reconstruction| of one read, as in config.py:114-122.
 double reconstruction_bound(const mf_config& c);
@@ -68,6 +77,12 @@ int max_adc(const mf_config& c);
 // True when ideal ADC counts equal exact integer digit dots for this config: the
 // reference's FP32 (or FP64) current error stays below half a count.
 bool exact_integer_counts(const mf_config& c);
+
+#ifdef __CUDACC__
+__device__ __forceinline__ unsigned raster_vector_block(int raster) { return raster ? blockIdx.y : blockIdx.x; }
+__device__ __forceinline__ unsigned raster_column_block(int raster) { return raster ? blockIdx.x : blockIdx.y; }
+__device__ __forceinline__ unsigned raster_vector_blocks(int raster) { return raster ? gridDim.y : gridDim.x; }
+#endif
 
 // Generic SIMT engine (all configurations).
 bool generic_ideal_fits(const mf_config& c, const mf_schedule& s);
@@ -100,7 +115,7 @@ mf_status tc_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, siz
 
 // Nonideal tensor-core path (tc_physical.cu).
 bool tc_physical_eligible(const mf_config& c, int32_t m);
-size_t tc_physical_workspace_bytes(const mf_config& c, int32_t m, int32_t tiles);
+size_t tc_physical_workspace_bytes(const mf_config& c, int64_t n, int32_t m, int32_t tiles);
 int tc_physical_threads();
 mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, size_t ws_bytes,
                                 cudaStream_t st);

@@ -114,6 +114,7 @@ struct Args {
     int col_begin;          // first output column of this call (tile_begin * C)
     int col_end;            // one past the last column (tile_end * C)
     unsigned* error;        // device error word
+    int raster;             // 0: blockIdx.x walks vector blocks; 1: blockIdx.x walks column blocks
 };
 
 using namespace tg;
@@ -220,8 +221,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const Plan& P = args.plan;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long n0 = (long long)blockIdx.x * BM;
-    const int c0 = args.col_begin + blockIdx.y * BN;     // first output column of this CTA
+    const long long n0 = (long long)raster_vector_block(args.raster) * BM;
+    const int c0 = args.col_begin + raster_column_block(args.raster) * BN;   // first output column of this CTA
     const int MR = args.MR;
     unsigned* err = args.error;
 
@@ -764,8 +765,9 @@ mf_status tc_sliced_mm(const mf_config& c, const MMArgs& a, void* workspace, siz
     args.col_begin = a.tile_begin * c.cols;
     args.col_end = a.tile_end * c.cols;
     args.error = err;
+    args.raster = a.raster;
     const long long cols = (long long)(a.tile_end - a.tile_begin) * c.cols;
-    dim3 grid((unsigned)((a.n + tc::BM - 1) / tc::BM), (unsigned)((cols + tc::BN - 1) / tc::BN));
+    const dim3 grid = raster_grid((a.n + tc::BM - 1) / tc::BM, (cols + tc::BN - 1) / tc::BN, a.raster);
     const tc::Plan& P = args.plan;
 #define MF_TC(NA_, NWA_, NWC_) \
     if (P.na == NA_ && P.nwa == NWA_ && P.nwc == NWC_) return launch_tc<NA_, NWA_, NWC_>(mx, mw, mxs, mws, args, grid, st)

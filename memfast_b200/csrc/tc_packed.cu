@@ -156,7 +156,11 @@ struct Args {
     long long full;         // reads in complete 16-read cascade blocks
     int col_begin, col_end;
     unsigned* error;        // device error word
-    unsigned* tile_flags;   // [gridDim.y][gridDim.x]: 1 = tile needs the generic rerun
+    unsigned* tile_flags;   // [column blocks][vector blocks]: 1 = tile needs the generic rerun
+    int raster;             // 0: blockIdx.x walks vector blocks; 1: blockIdx.x walks column blocks
+    int stop_stage;         // test hook (mf_debug_stall_next_launch): the producer issues no
+                            // load from this pipeline stage on; -1 = off
+    long long wait_cycles;  // budget of every bounded wait of the launch
 };
 
 __device__ __forceinline__ uint32_t or3(uint32_t a, uint32_t b, uint32_t c) { return a | b | c; }
@@ -178,10 +182,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const Plan& P = args.plan;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long n0 = (long long)blockIdx.x * BM;
-    const int c0 = args.col_begin + blockIdx.y * BN;
+    const unsigned vblk = raster_vector_block(args.raster), cblk = raster_column_block(args.raster);
+    const long long n0 = (long long)vblk * BM;
+    const int c0 = args.col_begin + cblk * BN;
     const int MR = args.MR;
     unsigned* err = args.error;
+    const long long budget = args.wait_cycles;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
@@ -235,17 +241,20 @@ __global__ void __launch_bounds__(THREADS, 1)
             // ------------------------------------------------------------ producer
             int issued = 0, scissued = 0;
             for (int stage = 0; stage < MR * H; ++stage) {
+                // Test hook: stop issuing here; the consumers' waits on this stage then
+                // run out of budget and the CTA takes its error exit.
+                if (stage == args.stop_stage) break;
                 const int i = stage / H;
                 if (stage % H == 0 && i % SCB == 0) {
                     const int b = i / SCB, sb = b % SCRING;
-                    if (!mbar_wait(&s.sc_empty[sb], ((b / SCRING) & 1) ^ 1, &s.abort, err, 21)) break;
+                    if (!mbar_wait(&s.sc_empty[sb], ((b / SCRING) & 1) ^ 1, &s.abort, err, 21, budget)) break;
                     mbar_expect_tx(&s.sc_full[sb], (BM + BN) * SCB * 4);
                     tma_load_2d(s.xs[sb], &map_xs, i, (int)n0, &s.sc_full[sb]);
                     tma_load_2d(s.ws[sb], &map_ws, c0, i, &s.sc_full[sb]);
                     scissued = b + 1;
                 }
                 const int st = stage % STAGES;
-                if (!mbar_wait(&s.empty[st], ((stage / STAGES) & 1) ^ 1, &s.abort, err, 22)) break;
+                if (!mbar_wait(&s.empty[st], ((stage / STAGES) & 1) ^ 1, &s.abort, err, 22, budget)) break;
                 mbar_expect_tx(&s.full[st], 2 * TILE);
                 tma_load_2d(s.x[st], &map_x, stage * KR, (int)n0, &s.full[st]);
                 tma_load_2d(s.w[st], &map_w, stage * KR, c0, &s.full[st]);
@@ -288,14 +297,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // epilogue to free them) and overwrites them; later stages accumulate,
                 // and the last one hands the units to the epilogue.
                 const uint32_t hh = (uint32_t)(stage % H);
-                if (!mbar_wait(&s.ready[st], (stage / STAGES) & 1, &s.abort, err, 23)) break;
+                if (!mbar_wait(&s.ready[st], (stage / STAGES) & 1, &s.abort, err, 23, budget)) break;
                 tc_fence_after();
                 const uint64_t dx = dx0 + st * kStageX, dw = dw0 + st * kStageX;
                 const uint64_t da = da0 + st * kStageA, dbs = db0 + st * kStageB;
                 uint32_t uj = u, ph = uphase;
 #pragma unroll
                 for (int j = 0; j < NJOB; ++j) {
-                    if (hh == 0 && !mbar_wait(&s.unit_empty[uj], ph ^ 1, &s.abort, err, 24)) {
+                    if (hh == 0 && !mbar_wait(&s.unit_empty[uj], ph ^ 1, &s.abort, err, 24, budget)) {
                         ok = false;
                         break;
                     }
@@ -369,7 +378,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int stage = 0; stage < MR * H; ++stage) {
             const int st = stage % STAGES;
             const int hh = stage % H;
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s.full[st], (stage / STAGES) & 1, &s.abort, err, 25))) break;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&s.full[st], (stage / STAGES) & 1, &s.abort, err, 25, budget))) break;
             const uint4* xrow = reinterpret_cast<const uint4*>(s.x[st] + t * KR);
             const uint4 xa = xrow[0], xb = xrow[1];
             const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
@@ -431,13 +440,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int i = 0; i < MR && ok; ++i) {
             const int b = i / SCB, sb = b % SCRING;
             if (i % SCB == 0) {
-                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.sc_full[sb], (b / SCRING) & 1, &s.abort, err, 26));
+                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.sc_full[sb], (b / SCRING) & 1, &s.abort, err, 26, budget));
                 if (!ok) break;
             }
             const float xs = s.xs[sb][r][i % SCB];
 #pragma unroll
             for (int j = 0; j < NJOB; ++j) {
-                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[u], uphase, &s.abort, err, 27));
+                ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s.unit_full[u], uphase, &s.abort, err, 27, budget));
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t buf = lane_base + u * UNIT_COLS;
@@ -556,7 +565,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_before();
     __syncthreads();
     if (threadIdx.x == 0)
-        args.tile_flags[(size_t)blockIdx.y * gridDim.x + blockIdx.x] = (s.rare || s.abort) ? 1u : 0u;
+        args.tile_flags[(size_t)cblk * raster_vector_blocks(args.raster) + vblk] = (s.rare || s.abort) ? 1u : 0u;
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);
@@ -1019,8 +1028,12 @@ mf_status tc_packed_sliced_mm(const mf_config& c, const MMArgs& a, void* workspa
     args.col_end = a.tile_end * c.cols;
     args.error = err;
     args.tile_flags = flags;
+    args.raster = a.raster;
+    args.stop_stage = a.stall_stage;
+    args.wait_cycles = a.stall_stage >= 0 ? a.stall_cycles : tg::kWaitCycles;
     const long long cols = (long long)tiles * c.cols;
-    dim3 grid((unsigned)((a.n + tp::BM - 1) / tp::BM), (unsigned)((cols + tp::BN - 1) / tp::BN));
+    const long long vblocks = (a.n + tp::BM - 1) / tp::BM;
+    const dim3 grid = raster_grid(vblocks, (cols + tp::BN - 1) / tp::BN, a.raster);
     const bool two = c.read_rows == 2 * tp::KR;
     switch (args.plan.ncol) {
         case 0: r = two ? launch_packed<0, 2>(mx, mw, mxs, mws, args, grid, st)
@@ -1034,7 +1047,7 @@ mf_status tc_packed_sliced_mm(const mf_config& c, const MMArgs& a, void* workspa
     }
     if (r) return r;
     // Tiles whose rare pairs could clip are recomputed exactly by the generic kernel.
-    return generic_ideal_tiles(c, a, flags, tp::BM, tp::BN, (int)grid.x, st);
+    return generic_ideal_tiles(c, a, flags, tp::BM, tp::BN, (int)vblocks, st);
 }
 
 }  // namespace mf

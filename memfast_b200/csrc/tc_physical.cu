@@ -75,7 +75,14 @@ constexpr int MAXS = 8;          // slices per operand in the tables below
 // Shared-memory and TMEM geometry of one instantiation.  A job is one input
 // slice a of one BN-column block: one accumulator set of NT columns, fed by
 // KS (split halves stacked along N) or 2 KS MMAs; jobs rotate over U units.
-template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART>
+//
+// VOLT (voltage noise): the A operand is no longer a digit but the noisy voltage
+// d * (1 + sigma z) of every (vector, row, input slice), precomputed by
+// a_operand_kernel as two FP16 parts (hi = fp16(v), lo = fp16(v - hi)) in the
+// MMA's tile layout.  A stage then holds those tiles instead of the code tile,
+// no digit planes are built, and each job issues the MMAs of both parts into the
+// same accumulators.
+template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool VOLT = false>
 struct Geo {
     static constexpr int KS = KR / 16;                     // MMA K steps per read
     static constexpr int EC = BN / 4;                      // columns per epilogue thread per block
@@ -88,14 +95,15 @@ struct Geo {
     static constexpr int U = 512 / UNIT < NJB * NIN ? 512 / UNIT : NJB * NIN;   // TMEM units
     static constexpr int BC = NJB * BN;                    // output columns per CTA
     static constexpr int VALS = NW * EC;                   // TMEM columns a thread reads per accumulator
-    static constexpr int XB = BM * KR;                     // code tile
+    static constexpr int AT = BM * 32;                     // one [128 x 16] FP16 tile
+    static constexpr int XB = VOLT ? NIN * 2 * KS * AT : BM * KR;   // voltage tiles, or the code tile
     static constexpr int BT = BROWS * 32;                  // one [BROWS x 16] FP16 tile (both halves)
     static constexpr int BB = NJB * KS * BT;
     static constexpr int STAGE = (XB + BB + 1023) / 1024 * 1024;
-    static constexpr int AT = BM * 32;                     // one [128 x 16] FP16 tile
-    static constexpr int AB = NIN * KS * AT;               // one set of digit planes
+    static constexpr int AB = VOLT ? 0 : NIN * KS * AT;    // one set of digit planes
     // Digit planes double-buffered (transform of read i+1 overlaps the MMAs of read i) when they fit.
-    static constexpr int ABUF = STAGES * STAGE + 2 * AB + BC * BM * 4 + 1024 <= 227 * 1024 ? 2 : 1;
+    static constexpr int ABUF = VOLT ? 0 : STAGES * STAGE + 2 * AB + BC * BM * 4 + 1024 <= 227 * 1024 ? 2 : 1;
+    static constexpr int ABUF1 = ABUF > 0 ? ABUF : 1;      // divisor for the buffer rotation
     static constexpr int OFF_A = STAGES * STAGE;
     static constexpr int OFF_ACC1 = OFF_A + ABUF * AB;
     static constexpr int OFF_BAR = OFF_ACC1 + BC * BM * 4;
@@ -104,6 +112,7 @@ struct Geo {
     static constexpr int TMEM_COLS = U * UNIT <= 256 ? 256 : 512;
     static_assert(U >= 1 && U * UNIT <= 512 && NT <= 256, "accumulators exceed TMEM or the MMA's N");
     static_assert(BN % 4 == 0 && KR % 16 == 0 && NIN <= MAXS && NW <= MAXS, "unsupported shape");
+    static_assert(!VOLT || SPLIT, "voltage tiles pair with split conductance halves");
     static_assert(VALS % 2 == 0, "TMEM loads start on even columns");
     static_assert(BYTES + 1024 <= 232448, "exceeds the 227 KB shared-memory limit");
 };
@@ -129,6 +138,8 @@ struct Args {
     int factor[MAXS][MAXS];  // s_a * s_w
     int offset;              // -0x4B400000 * sum of factor over the slice pairs (mod 2^32)
     float ffactor[MAXS][MAXS];  // s_a * s_w as FP32 (float totals of the digit mode)
+    int raster;              // 0: blockIdx.x walks vector blocks; 1: blockIdx.x walks column blocks
+    int n_pad;               // VOLT: rows of one (slice, part) plane of the voltage operand
 };
 
 __device__ __forceinline__ float mul_sat(float a, float b) {
@@ -164,11 +175,15 @@ __device__ __forceinline__ void tmem_loaded(uint32_t* v) {
 
 // FSUM (digit mode, reconstruction bound below 2^24): the count min(D, max_w) and
 // the total are FP32 integers, summed exactly with one FMNMX and one FFMA per event.
-template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool NONLINEAR, bool FSUM = false>
+template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool NONLINEAR, bool FSUM = false,
+          bool VOLT = false>
 __global__ void __launch_bounds__(THREADS, 1)
     tc_physical_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_g,
                        const __grid_constant__ Args args) {
-    using G = Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART>;
+    using G = Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT>;
+    // The digit mode sums counts in FP32, exact only while every accumulator read from
+    // TMEM is the integer digit dot itself: one FP16 part, no split halves.
+    static_assert(!FSUM || (!SPLIT && NPART == 1), "FSUM needs exact integer digit dots (one FP16 part)");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* a_planes = base + G::OFF_A;
@@ -185,8 +200,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long n0 = (long long)blockIdx.x * BM;
-    const int c0 = args.col_begin + blockIdx.y * G::BC;   // first output column of this CTA
+    const unsigned vblk = raster_vector_block(args.raster), cb_cta = raster_column_block(args.raster);
+    const long long n0 = (long long)vblk * BM;
+    const int c0 = args.col_begin + cb_cta * G::BC;   // first output column of this CTA
     const int MR = args.MR;
     unsigned* err = args.error;
 
@@ -223,14 +239,24 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (warp == 0) {
             // ------------------------------------------------------------ producer
             if (lane == 0) {
-                const int cb0 = blockIdx.y * NJB;          // first BN-column block of this CTA
+                const int cb0 = cb_cta * NJB;              // first BN-column block of this CTA
                 int issued = 0;
                 for (int i = 0; i < MR; ++i) {
                     const int st = i % STAGES;
                     if (!mbar_wait(&empty[st], ((i / STAGES) & 1) ^ 1, abort_flag, err, 41)) break;
                     uint8_t* stage = base + st * G::STAGE;
                     mbar_expect_tx(&full[st], G::XB + G::BB);
-                    tma_load_2d(stage, &map_x, i * KR, (int)n0, &full[st]);
+                    if (VOLT) {
+                        // Tile (a, part, ks): rows (a * 2 + part) * n_pad + n0 of the voltage operand.
+#pragma unroll 1
+                        for (int t = 0; t < NIN * 2; ++t)
+#pragma unroll
+                            for (int ks = 0; ks < G::KS; ++ks)
+                                tma_load_2d(stage + (t * G::KS + ks) * G::AT, &map_x, i * KR + ks * 16,
+                                            (int)(t * args.n_pad + n0), &full[st]);
+                    } else {
+                        tma_load_2d(stage, &map_x, i * KR, (int)n0, &full[st]);
+                    }
 #pragma unroll 1
                     for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
@@ -254,11 +280,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int i = 0; i < MR && ok; ++i) {
                     const int st = i % STAGES;
                     if (!mbar_wait(&full[st], (i / STAGES) & 1, abort_flag, err, 42)) break;
-                    const int ab = i % G::ABUF;
-                    if (!mbar_wait(&a_ready[ab], (i / G::ABUF) & 1, abort_flag, err, 43)) break;
+                    const int ab = i % G::ABUF1;
+                    if (!VOLT && !mbar_wait(&a_ready[ab], (i / G::ABUF1) & 1, abort_flag, err, 43)) break;
                     tc_fence_after();
                     const uint8_t* btiles = base + st * G::STAGE + G::XB;
-                    const uint8_t* planes = a_planes + ab * G::AB;
+                    // VOLT: the stage's voltage tiles (a, part, ks); otherwise the digit planes (a, ks).
+                    const uint8_t* planes = VOLT ? base + st * G::STAGE : a_planes + ab * G::AB;
 #pragma unroll 1
                     for (int cb = 0; cb < NJB && ok; ++cb) {
                         // Descriptors advance by (byte offset >> 4) in their address field.
@@ -273,19 +300,30 @@ __global__ void __launch_bounds__(THREADS, 1)
                             }
                             tc_fence_after();
                             const uint32_t d = tmem + unit * G::UNIT;
-                            const uint64_t da = desc_sw32(planes + a * G::KS * G::AT);
+                            if (VOLT) {
+                                // Both voltage parts into the same accumulators (B halves stacked along N).
+                                const uint64_t da = desc_sw32(planes + a * 2 * G::KS * G::AT);
 #pragma unroll
-                            for (int part = 0; part < (SPLIT ? 1 : NPART); ++part)
+                                for (int vp = 0; vp < 2; ++vp)
 #pragma unroll
-                                for (int ks = 0; ks < G::KS; ++ks)
-                                    mma_f16(d, da + (uint64_t)((ks * G::AT) >> 4),
-                                            db + (uint64_t)((ks * G::BT + part * G::PSTRIDE * 32) >> 4), idesc,
-                                            (part | ks) != 0);
+                                    for (int ks = 0; ks < G::KS; ++ks)
+                                        mma_f16(d, da + (uint64_t)(((vp * G::KS + ks) * G::AT) >> 4),
+                                                db + (uint64_t)((ks * G::BT) >> 4), idesc, (vp | ks) != 0);
+                            } else {
+                                const uint64_t da = desc_sw32(planes + a * G::KS * G::AT);
+#pragma unroll
+                                for (int part = 0; part < (SPLIT ? 1 : NPART); ++part)
+#pragma unroll
+                                    for (int ks = 0; ks < G::KS; ++ks)
+                                        mma_f16(d, da + (uint64_t)((ks * G::AT) >> 4),
+                                                db + (uint64_t)((ks * G::BT + part * G::PSTRIDE * 32) >> 4), idesc,
+                                                (part | ks) != 0);
+                            }
                             mma_commit(&unit_full[unit]);
                         }
                     }
                     if (!ok) break;
-                    mma_commit(&a_free[ab]);
+                    if (!VOLT) mma_commit(&a_free[ab]);
                     mma_commit(&empty[st]);
                 }
                 // All issued MMAs complete before TMEM is released.
@@ -298,11 +336,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             // 16-code step becomes one [128 x 16] FP16 plane per input slice in the
             // 32-byte-swizzled K-major layout (16-byte halves swapped in rows with bit 2 set).
             const int tw = warp - 2;
-            for (int i = 0; i < MR; ++i) {
+            for (int i = 0; i < (VOLT ? 0 : MR); ++i) {
                 const int st = i % STAGES;
-                const int ab = i % G::ABUF;
+                const int ab = i % G::ABUF1;
                 bool ok = mbar_wait(&full[st], (i / STAGES) & 1, abort_flag, err, 45);
-                ok = ok && mbar_wait(&a_free[ab], ((i / G::ABUF) & 1) ^ 1, abort_flag, err, 46);
+                ok = ok && mbar_wait(&a_free[ab], ((i / G::ABUF1) & 1) ^ 1, abort_flag, err, 46);
                 if (!__all_sync(0xFFFFFFFFu, ok)) break;
                 const uint8_t* codes = base + st * G::STAGE;
                 uint8_t* planes = a_planes + ab * G::AB;
@@ -556,6 +594,40 @@ __global__ void __launch_bounds__(256) b_operand_kernel(Layout L, Physics P, con
     }
 }
 
+// The A operand of the voltage-noise path.  For vector v (global index
+// vector_offset + v), reduction index k (array k / R, row k % R) and input slice
+// a, the voltage factor of the reference, d * (1 + sigma * z) with d the slice's
+// digit and z the normal of stream 40 at address ((v * m + array) * NIN + a) * R
+// + row under the read event's seed (memfast/reference.py:83-86), written as two
+// FP16 parts hi = fp16(x), lo = fp16(x - hi) (x to about 22 bits).  Planes
+// [a][part][n_pad][kpad], K contiguous, so that one TMA box of 16 K x 128 rows is
+// an MMA A tile; rows at or beyond n are zero.  One thread per (row, k) draws the
+// noise of every input slice.
+__global__ void __launch_bounds__(256) a_operand_kernel(Layout L, float volt_var, const uint8_t* codes, long long n,
+                                                        long long n_pad, int m, long long kpad,
+                                                        long long vector_offset, uint64_t read_seed, __half* va) {
+    const long long k = (long long)blockIdx.x * 256 + threadIdx.x;
+    if (k >= kpad) return;
+    const long long arr = k / L.R;
+    const int row = (int)(k - arr * L.R);
+    for (long long v = blockIdx.y; v < n_pad; v += gridDim.y) {
+        const long long code = v < n ? (long long)codes[v * kpad + k] : 0;
+        for (int a = 0; a < L.n_in; ++a) {
+            __half hi = __float2half_rn(0.0f), lo = hi;
+            const long long d = (code >> L.in_shift[a]) & L.in_mask[a];
+            if (d != 0) {
+                const long long address = (((vector_offset + v) * m + arr) * L.n_in + a) * L.R + row;
+                const float f = __fadd_rn(1.0f, __fmul_rn(volt_var, rng_normal(address, read_seed, 40)));
+                const float x = __fmul_rn((float)d, f);
+                hi = __float2half_rn(x);
+                lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
+            }
+            va[((long long)(a * 2) * n_pad + v) * kpad + k] = hi;
+            va[((long long)(a * 2 + 1) * n_pad + v) * kpad + k] = lo;
+        }
+    }
+}
+
 // Instantiations: (input slices, weight slices) -> columns per block, blocks per
 // CTA, split accumulators.  Each MMA is as wide as TMEM and the 256-column limit of
 // N allow (the tensor core's cost here is per instruction rather than per column).
@@ -619,12 +691,14 @@ static bool digits_eligible(const mf_config& c, int32_t m) {
 bool tc_physical_eligible(const mf_config& c, int32_t m) {
     if (c.ideal) return digits_eligible(c, m);
     if (c.wide || c.wide_codes || c.precise_currents) return false;
-    if (c.volt_var != 0) return false;
     if (c.read_var != 0 && c.read_mode != 0) return false;
     if (c.write_var + c.read_var > 1.0) return false;
     if (c.read_rows != 32 && c.read_rows != 64) return false;
     tcp::Shape s;
     if (!tcp::shape_of(c, s)) return false;
+    // Voltage noise: the voltage tiles of a stage fit shared memory for 32-row reads of
+    // the split-halves shapes.
+    if (c.volt_var != 0 && (c.read_rows != 32 || !s.split)) return false;
     if (c.rows % c.read_rows || c.cols % s.bn) return false;
     for (int i = 0; i < c.n_in; ++i)
         if (c.in_mask[i] > 7) return false;
@@ -637,21 +711,33 @@ bool tc_physical_eligible(const mf_config& c, int32_t m) {
 
 int tc_physical_threads() { return tcp::THREADS; }
 
-size_t tc_physical_workspace_bytes(const mf_config& c, int32_t m, int32_t tiles) {
-    tcp::Shape s;
-    if (!tcp::shape_of(c, s)) return 256;
+// Bytes of the conductance operand, rounded to 256.
+static size_t b_operand_bytes(const mf_config& c, const tcp::Shape& s, int32_t m, int32_t tiles) {
     const long long blocks = (long long)tiles * c.cols / s.bn;
     int brows = 0, pstride = 0;
     tcp::rows_of(s, tcp::parts_of(c), brows, pstride);
-    return (size_t)blocks * brows * (size_t)m * c.rows * sizeof(__half) + 256;
+    return ((size_t)blocks * brows * (size_t)m * c.rows * sizeof(__half) + 255) / 256 * 256;
 }
 
-template <int NIN, int NW, int BN, int NJB, bool SPLIT, int NPART, int KR, bool NL, bool FSUM = false>
+// Rows of one (slice, part) plane of the voltage operand.
+static long long voltage_rows(int64_t n) { return (n + tcp::BM - 1) / tcp::BM * tcp::BM; }
+
+size_t tc_physical_workspace_bytes(const mf_config& c, int64_t n, int32_t m, int32_t tiles) {
+    tcp::Shape s;
+    if (!tcp::shape_of(c, s)) return 256;
+    size_t bytes = b_operand_bytes(c, s, m, tiles) + 256;
+    if (!c.ideal && c.volt_var != 0)
+        bytes += (size_t)c.n_in * 2 * voltage_rows(n) * (size_t)m * c.rows * sizeof(__half);
+    return bytes;
+}
+
+template <int NIN, int NW, int BN, int NJB, bool SPLIT, int NPART, int KR, bool NL, bool FSUM = false,
+          bool VOLT = false>
 static mf_status launch_tcp(const CUtensorMap& mx, const CUtensorMap& mg, const tcp::Args& args, dim3 grid,
                             cudaStream_t st) {
-    using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART>;
+    using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT>;
     const size_t smem = G::BYTES + 1024;
-    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL, FSUM>;
+    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL, FSUM, VOLT>;
     int regs = 0;
     {
         const mf_status r = kernel_setup(reinterpret_cast<const void*>(kern), smem, &regs);
@@ -673,6 +759,12 @@ template <int NIN, int NW, int BN, int NJB, bool SPLIT>
 static mf_status dispatch_tcp(const mf_config& c, const CUtensorMap& mx, const CUtensorMap& mg,
                               const tcp::Args& args, dim3 grid, cudaStream_t st) {
     const bool nl = c.nonlinear != 0;
+    if constexpr (SPLIT) {
+        // Voltage noise (32-row reads only, tc_physical_eligible): voltage tiles as the A operand.
+        if (c.volt_var != 0)
+            return nl ? launch_tcp<NIN, NW, BN, NJB, true, tcp::PARTS, 32, true, false, true>(mx, mg, args, grid, st)
+                      : launch_tcp<NIN, NW, BN, NJB, true, tcp::PARTS, 32, false, false, true>(mx, mg, args, grid, st);
+    }
     if (c.read_rows == 32)
         return nl ? launch_tcp<NIN, NW, BN, NJB, SPLIT, tcp::PARTS, 32, true>(mx, mg, args, grid, st)
                   : launch_tcp<NIN, NW, BN, NJB, SPLIT, tcp::PARTS, 32, false>(mx, mg, args, grid, st);
@@ -708,7 +800,7 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
         return MF_ERR_UNSUPPORTED;
     }
     const int tiles = a.tile_end - a.tile_begin;
-    const size_t need = tc_physical_workspace_bytes(c, a.m, tiles);
+    const size_t need = tc_physical_workspace_bytes(c, a.n, a.m, tiles);
     if (!workspace || ws_bytes < need) {
         set_error("tcgen05 physical workspace too small: %zu < %zu bytes", ws_bytes, need);
         return MF_ERR_RESOURCE;
@@ -731,8 +823,27 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
         MF_LAUNCH_CHECK("b_operand_kernel");
     }
     CUtensorMap mx, mg;
-    mf_status r = tc_make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n,
-                              (uint64_t)K, (uint32_t)c.read_rows, tcp::BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    const bool volt = !c.ideal && c.volt_var != 0;
+    const long long n_pad = voltage_rows(a.n);
+    mf_status r = MF_OK;
+    if (volt && (long long)c.n_in * 2 * n_pad > 2147483647LL) {
+        set_error("voltage operand of %lld rows exceeds the TMA row coordinate", (long long)c.n_in * 2 * n_pad);
+        return MF_ERR_RESOURCE;
+    }
+    if (volt) {
+        // The voltage operand follows the conductance operand in the workspace.
+        __half* va = reinterpret_cast<__half*>(static_cast<uint8_t*>(workspace) + b_operand_bytes(c, shape, a.m, tiles));
+        const dim3 grid((unsigned)((K + 255) / 256), (unsigned)(n_pad < 65535 ? n_pad : 65535));
+        tcp::a_operand_kernel<<<grid, 256, 0, st>>>(make_layout(c), (float)c.volt_var,
+                                                   static_cast<const uint8_t*>(a.codes), a.n, n_pad, a.m, K,
+                                                   a.vector_offset, event_seed(a.seed, a.event), va);
+        MF_LAUNCH_CHECK("a_operand_kernel");
+        r = tc_make_map(&mx, va, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K, (uint64_t)c.n_in * 2 * n_pad,
+                        (uint64_t)K, 16, tcp::BM, CU_TENSOR_MAP_SWIZZLE_32B);
+    } else {
+        r = tc_make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n,
+                        (uint64_t)K, (uint32_t)c.read_rows, tcp::BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
     if (!r) r = tc_make_map(&mg, gs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K,
                             (uint64_t)blocks * brows, (uint64_t)K, 16, (uint32_t)brows,
                             CU_TENSOR_MAP_SWIZZLE_32B);
@@ -752,6 +863,7 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     args.full = (long long)args.MR - args.MR % 16;
     args.col_begin = a.tile_begin * c.cols;
     args.col_end = a.tile_end * c.cols;
+    args.n_pad = (int)n_pad;
     // FP16 high bytes of the digits 0..7 (1.0 = 0x3C00, 2.0 = 0x4000, 3.0 = 0x4200, ...).
     const uint8_t hi[8] = {0x00, 0x3C, 0x40, 0x42, 0x44, 0x45, 0x46, 0x47};
     args.lut_lo = hi[0] | hi[1] << 8 | hi[2] << 16 | (uint32_t)hi[3] << 24;
@@ -778,7 +890,8 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     }
     args.offset = (int)(0u - 0x4B400000u * sum);
     const int bc = shape.bn * shape.njb;
-    dim3 grid((unsigned)((a.n + tcp::BM - 1) / tcp::BM), (unsigned)((cols + bc - 1) / bc));
+    args.raster = a.raster;
+    const dim3 grid = raster_grid((a.n + tcp::BM - 1) / tcp::BM, (cols + bc - 1) / bc, a.raster);
     if (c.ideal) {
         if (shape.nin == 5) return dispatch_digits<5, 5, 32, 1>(c, mx, mg, args, grid, st);
         if (shape.nin == 3) return dispatch_digits<3, 3, 32, 2>(c, mx, mg, args, grid, st);

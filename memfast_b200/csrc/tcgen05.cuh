@@ -64,15 +64,16 @@ constexpr uint32_t kSuspendNs = 20000;
 constexpr long long kWaitCycles = 4000000000LL;
 
 // Bounded wait for phase `parity`.  Gives up when another role of the CTA has
-// set *abort, or after kWaitCycles; in the latter case it records `code` in the
-// device error word and sets *abort so that every other role stops too.
+// set *abort, or after `budget` cycles (kWaitCycles unless a launch asks for a
+// shorter one); in the latter case it records `code` in the device error word
+// and sets *abort so that every other role stops too.
 __device__ __forceinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* abort, unsigned* error,
-                                               unsigned code) {
+                                               unsigned code, long long budget = kWaitCycles) {
     const long long start = clock64();
     while (true) {
         if (mbar_try_suspend(bar, parity, kSuspendNs)) return true;
         if (*(volatile int*)abort) return false;
-        if (clock64() - start > kWaitCycles) {
+        if (clock64() - start > budget) {
             atomicCAS(error, 0u, code);
             *(volatile int*)abort = 1;
             return false;
@@ -81,9 +82,9 @@ __device__ __forceinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, i
 }
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* abort, unsigned* error,
-                                          unsigned code) {
+                                          unsigned code, long long budget = kWaitCycles) {
     if (mbar_try(bar, parity)) return true;
-    return mbar_wait_slow(bar, parity, abort, error, code);
+    return mbar_wait_slow(bar, parity, abort, error, code, budget);
 }
 
 // Bounded wait that ignores the abort flag: used to drain a role's own

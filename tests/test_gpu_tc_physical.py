@@ -44,6 +44,11 @@ CONFIGS = {
     "int7_4slices": dict(INT8, activation_bits=7, weight_bits=7, input_slice=(1, 2, 2, 2), weight_slice=(1, 2, 2, 2),
                          adc_bits=8, nonidealities=dict(write_variation=0.02, drift_coefficient=0.1, drift_time=10.0)),
     "unsigned_weights": dict(INT8, weight_signed=False, nonidealities=dict(write_variation=0.02)),
+    # Voltage noise: the noisy input voltages as two FP16 parts (a_operand_kernel).
+    "int8_noisy": dict(INT8, nonidealities=dict(write_variation=0.02, read_variation=0.02, voltage_variation=0.02)),
+    "int8_voltage_all": dict(INT8, nonidealities=dict(ALL, voltage_variation=0.05)),
+    "int4_voltage": dict(INT8, activation_bits=4, weight_bits=4, input_slice=(1, 1, 2), weight_slice=(1, 1, 2),
+                         adc_bits=6, nonidealities=dict(write_variation=0.02, voltage_variation=0.03)),
 }
 
 
@@ -160,7 +165,7 @@ def test_ideal_digit_dots_are_bit_exact(mf, name):
 
 
 @pytest.mark.parametrize("name", ["int8_write", "int8_rpr64_all", "default_1bit", "int8_rpr64_ideal",
-                                  "int4_rpr64_ideal"])
+                                  "int4_rpr64_ideal", "int8_noisy"])
 def test_column_shards_and_row_prefixes_are_exact(mf, name):
     config = config_of(mf, name)
     a, b = operands(300, 512, 640, 4)
@@ -195,8 +200,13 @@ def test_read_events_draw_new_noise(mf):
 
 
 def test_ineligible_configs_keep_the_simt_path(mf):
-    voltage = mf.Config(**INT8, nonidealities=mf.Nonidealities(write_variation=0.02, voltage_variation=0.02))
+    # Voltage noise runs on the tensor cores for 32-row reads only (the voltage tiles of a
+    # 64-row read do not fit a pipeline stage); output-mode read noise stays on SIMT.
+    voltage64 = mf.Config(**dict(MATRIX, input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2)),
+                          nonidealities=mf.Nonidealities(write_variation=0.02, voltage_variation=0.02))
     output_mode = mf.Config(**INT8, nonidealities=mf.Nonidealities(write_variation=0.02, read_variation=0.05,
                                                                    read_mode="output"))
-    for config in (voltage, output_mode):
+    for config in (voltage64, output_mode):
         assert threads_of(mf, config, 2, 2) == 256
+    voltage = mf.Config(**INT8, nonidealities=mf.Nonidealities(write_variation=0.02, voltage_variation=0.02))
+    assert threads_of(mf, voltage, 2, 2) == 640

@@ -152,6 +152,22 @@ def test_64_row_reads_take_the_packed_kernel(mf):
     sched = _lib.schedule(kernel=0)
     _lib.check(_lib.load().mf_query(_lib.native_config(config), ct.byref(sched), 4096, 64, 64, ct.byref(res)), "q")
     assert res.threads == 768
+    # And a 64-row forward really launches it: the packed kernel, its K-major weight copy
+    # (first call) and the rare-tile rerun filter, which finds no flagged tile here.
+    g = torch.Generator().manual_seed(64)
+    a, b = torch.randn(256, 512, generator=g).cuda(), torch.randn(512, 192, generator=g).cuda()
+    lib = _lib.load()
+    sim = mf.Simulator(config)
+    sim.mm(a, b)
+    assert _lib.PATHS[lib.mf_last_path()] == "packed"
+    before = lib.mf_launch_count()
+    sim.mm(a, b)
+    assert _lib.PATHS[lib.mf_last_path()] == "packed"
+    # Second call: operand checks, programming B (with its K-major copy), quantising A,
+    # the packed kernel, the rerun filter, the output check: 12 launches; a fallback of
+    # the product to the generic kernel shows in mf_last_path above.
+    launches = lib.mf_launch_count() - before
+    assert launches <= 12, launches
 
 
 @pytest.mark.parametrize("shape", [(128, 128, 128), (200, 384, 300), (333, 1000, 520)])
