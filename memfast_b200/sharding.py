@@ -38,11 +38,14 @@ def row_range(n, world, rank):
     return r0, r0 + base + (1 if rank < extra else 0)
 
 
-def sharded_mm(a_local, b, *, simulator, row_offset):
+def sharded_mm(a_local, b, *, simulator, row_offset, out=None):
     """Rows [row_offset, row_offset + len(a_local)) of ``simulator.mm(A, B)``.
 
     Bit-identical to the same rows of the unsharded product (same simulator
-    state): noise addresses use the global vector index.
+    state): noise addresses use the global vector index.  ``out``: a [rows, O]
+    buffer of A's dtype with unit column stride (for example this rank's rows of
+    the full output, which ``gather_rows`` then fills in place) receiving the
+    result.
     """
     if not isinstance(simulator, Simulator):
         raise TypeError("simulator must be Simulator")
@@ -56,20 +59,31 @@ def sharded_mm(a_local, b, *, simulator, row_offset):
     _operands(a_local, b)
     if a_local.device != simulator.device:
         raise ValueError("operands and simulator must use the same device")
+    if out is not None and (out.shape != (a_local.shape[0], b.shape[1]) or out.dtype != a_local.dtype
+                            or out.device != a_local.device or out.stride(-1) != 1):
+        raise ValueError("out must be a [rows, O] buffer of A's dtype and device with unit column stride")
     matrix = simulator._matrix_for(b, checked=_checked(b, config, config.weight_bits), rows=a_local.shape[0])
     with torch.no_grad():
         return matrix._forward(a_local.detach(), checked=_checked(a_local, config, config.activation_bits),
-                               vector_offset=row_offset)
+                               vector_offset=row_offset, out=out)
 
 
-def gather_rows(local, n, group=None):
+def gather_rows(local, n, group=None, out=None):
     """All-gather row shards (``row_range`` partition of n rows) into one [n, ...] tensor.
 
     Shards may differ by one row; they are padded to the largest shard for the
-    collective and trimmed afterwards.
+    collective and trimmed afterwards.  ``out``: a contiguous [n, ...] result
+    buffer; when the shards are equal this rank's rows may already sit in it
+    (``local`` is ``out[r0:r1]``), and the collective then runs in place.
     """
     world = dist.get_world_size(group)
     largest = row_range(n, world, 0)[1]
+    if out is not None and n % world == 0 and out.is_contiguous() and local.is_contiguous():
+        if (out.shape != (n,) + tuple(local.shape[1:]) or out.dtype != local.dtype
+                or local.shape[0] != n // world):
+            raise ValueError("out must be the [n, ...] gather of the shards")
+        dist.all_gather_into_tensor(out, local, group=group)
+        return out
     padded = local.new_zeros((largest,) + tuple(local.shape[1:]))
     padded[: local.shape[0]] = local
     stacked = local.new_empty((world * largest,) + tuple(local.shape[1:]))
@@ -78,6 +92,8 @@ def gather_rows(local, n, group=None):
     for rank in range(world):
         r0, r1 = row_range(n, world, rank)
         parts.append(stacked[rank * largest: rank * largest + (r1 - r0)])
+    if out is not None:
+        return torch.cat(parts, out=out)
     return torch.cat(parts)
 
 

@@ -32,24 +32,38 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _gather_worker(rank, world, port, n, result):
+def _gather_worker(rank, world, port, n, mode, result):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         r0, r1 = row_range(n, world, rank)
-        local = torch.arange(r0 * 3, r1 * 3, dtype=torch.float32).reshape(-1, 3)
-        out = gather_rows(local, n)
-        result[rank] = bool(torch.equal(out, torch.arange(n * 3, dtype=torch.float32).reshape(n, 3)))
+        want = torch.arange(n * 3, dtype=torch.float32).reshape(n, 3)
+        if mode == "in_place":
+            # The strong-scaling bench: this rank's rows already sit in the full buffer.
+            full = torch.full((n, 3), -1.0)
+            full[r0:r1] = want[r0:r1]
+            out = gather_rows(full[r0:r1], n, out=full)
+            ok = out is full
+        elif mode == "out":
+            full = torch.full((n, 3), -1.0)
+            out = gather_rows(want[r0:r1].clone(), n, out=full)
+            ok = out is full
+        else:
+            out = gather_rows(want[r0:r1].clone(), n)
+            ok = True
+        result[rank] = ok and bool(torch.equal(out, want))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("n", [5, 8, 1])
-def test_gather_rows_two_ranks_gloo(n):
-    """Uneven shards are padded for the collective and trimmed back in rank order."""
+@pytest.mark.parametrize("n,mode", [(5, "new"), (8, "new"), (1, "new"), (8, "in_place"), (4096, "in_place"),
+                                    (5, "out"), (8, "out")])
+def test_gather_rows_two_ranks_gloo(n, mode):
+    """Uneven shards are padded for the collective and trimmed back in rank order; equal
+    shards gather straight into the caller's buffer, also from rows already in it."""
     manager = mp.get_context("spawn").Manager()
     result = manager.dict()
-    mp.spawn(_gather_worker, args=(2, _free_port(), n, result), nprocs=2, join=True)
+    mp.spawn(_gather_worker, args=(2, _free_port(), n, mode, result), nprocs=2, join=True)
     assert result[0] and result[1]
 
 
