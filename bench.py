@@ -94,7 +94,9 @@ def parse(argv=None):
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    p.add_argument("--impl", choices=["engine", "reference", "reference-cuda"], default="engine",
+                   help="reference: the reference algorithm's CPU restatement on the host cores; reference-cuda: "
+                        "the unmodified reference package (installed in baseline/_ref) on its own CUDA path")
     p.add_argument("--workload", choices=WORKLOADS, default="sweep",
                    help="sweep: BASELINE configs[1] at --size (the headline at 4096); matrix-*: configs[2] at "
                         "2048^3; resnet50: configs[3]; llama7b: configs[4]")
@@ -256,7 +258,9 @@ def parity_report(got, want, ideal, label):
     if ideal:
         line["bit_exact"] = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
         if not line["bit_exact"]:
-            line["mismatch_fraction"] = float(np.mean(got != want))
+            scale = float(max(np.abs(want).max(), 1e-30))
+            line.update(mismatch_fraction=float(np.mean(got != want)),
+                        max_err_of_range=float(np.abs(got.astype(np.float64) - want).max() / scale))
         return line
     diff = got.astype(np.float64) - want
     scale = float(max(np.abs(want).max(), 1e-30))
@@ -510,7 +514,8 @@ def engine_arm(args):
     n_rows = q.shape[0]
     ws_bytes = matrix._workspace_size(n_rows, schedule)
     workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
-    out_k = torch.empty((n_rows, size), device=device)
+    # Wide configurations (BFP, more than 8 bits) reconstruct and write FP64 outputs.
+    out_k = torch.empty((n_rows, size), device=device, dtype=torch.float64 if config.wide else torch.float32)
     native = _lib.schedule(**schedule)
     lib = _lib.load()
     cfg = _lib.native_config(config)
@@ -881,10 +886,66 @@ def llama_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def reference_cuda_arm(args):
+    """The reference's own GPU path on the same operands: ``Simulator(cfg, device="cuda").mm``
+    of the unmodified reference package (NVRTC-compiled SIMT kernels, default schedule,
+    memfast/cuda.py:322-373), installed from the reference sources into baseline/_ref.
+    Rank 0 only; prints ``unavailable`` when the package is not installed."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    package = ROOT / "baseline" / "_ref"
+    if not (package / "memfast" / "__init__.py").exists():
+        print(json.dumps(dict(impl="reference-cuda", unavailable="reference package not installed in baseline/_ref")))
+        return
+    import torch
+
+    sys.path.insert(0, str(package))
+    import memfast as ref
+
+    if args.workload != "sweep":
+        raise SystemExit("--impl reference-cuda times the sweep workload")
+    config = bench_config(ref, args.effects)
+    a_np, b_np = operands(args.size)
+    a, b = torch.from_numpy(a_np).cuda(), torch.from_numpy(b_np).cuda()
+    sim = ref.Simulator(config, device="cuda")
+    for _ in range(max(1, args.warmup)):
+        first = sim.mm(a, b)
+    torch.cuda.synchronize()
+    times = []
+    with ClockSampler(0) as clocks:
+        for _ in range(args.steps):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            sim.mm(a, b)
+            end.record()
+            torch.cuda.synchronize()
+            times.append(start.elapsed_time(end) / 1e3)
+    per_step = sum(times) / len(times)
+    size = args.size
+    line = dict(metric=metric_name(size), value=float(size) ** 3 / per_step, unit=UNIT, n_gpus=1, steps=args.steps,
+                warmup=args.warmup, ms_per_step=per_step * 1e3, higher_is_better=True, scaling="strong",
+                vs_baseline=None, dtype="f32 currents / int64 totals (reference SIMT kernels)", data="synthetic",
+                config=workload(args, 1, (config, size, "INT8", effects_label(args.effects))),
+                impl="reference-cuda", clocks=clocks.summary(),
+                note="unmodified reference memfast 0.3.0 from baseline/_ref, Simulator(device='cuda').mm, default "
+                     "mode: B reprogrammed per call, restore + consume NVRTC kernels per tile group, partials "
+                     "scaled and summed in PyTorch")
+    # Its rows against the oracle, as the engine's line does.
+    from oracle import oracle as O
+
+    rows = args.parity_rows
+    line["parity"] = parity_report(first[:rows].cpu().numpy(), O.mm(a_np[:rows], b_np, config),
+                                   args.effects == "ideal", "oracle (reference CPU algorithm)")
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+    elif args.impl == "reference-cuda":
+        reference_cuda_arm(args)
     elif args.workload == "resnet50":
         resnet_arm(args)
     elif args.workload == "llama7b":

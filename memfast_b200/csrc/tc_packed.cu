@@ -482,12 +482,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                             o[c] = acc;
                             hit = (acc & P.colclip[c]) | hit;
                         }
-                        if (__any_sync(0xFFFFFFFFu, hit != 0)) {
-                            // Per count block, the clip bits set anywhere in the warp name the
-                            // counts that clip; T += -s_a s_w * max(D - m, 0) for those only.
+                        if (hit != 0) {
+                            // Only the lanes whose own counts clip (usually one lane of a
+                            // chunk, when any): per count block, the clip bits set in this
+                            // lane's columns name the counts that clip, and
+                            // T += -s_a s_w * max(D - m, 0) for those only.  (A warp-wide
+                            // vote and reduction of the clip bits measured 3% slower.)
 #pragma unroll
                             for (int c = 0; c < NCOL; ++c) {
-                                uint32_t fired = __reduce_or_sync(0xFFFFFFFFu, o[c] & P.colclip[c]);
+                                uint32_t fired = o[c] & P.colclip[c];
                                 while (fired) {
                                     const int4 F = s.field[c * MAXFIELD + s.fieldbit[c][__ffs(fired) - 1]];
                                     fired &= ~((uint32_t)F.y << F.x);
