@@ -12,10 +12,10 @@ region, the copies overlapped with the product row chunk by row chunk.
 
 With --gpus N (one process per GPU under torchrun) the default is strong
 scaling: the one 4096^3 product is split into N row blocks (``row_range``);
-each rank computes its block (``sharding.sharded_mm``: quantise its rows of A,
-program B, the fused product, written straight into its rows of the full
-output) and an NCCL all-gather fills every rank's copy of the full output
-in place.  Both are inside every timed step; ``breakdown`` reports the kernel,
+each rank computes its block (``sharding.row_parallel_mm``: quantise its rows
+of A, program B, the fused product, written straight into its rows of the full
+output) and an NCCL all-gather, enqueued before the step's one host
+synchronisation, fills every rank's copy of the full output in place.  Both are inside every timed step; ``breakdown`` reports the kernel,
 the gather and the rest per step (max over ranks).  ``--scaling weak`` keeps
 the earlier measurement instead: 4096 rows per rank, each rank keeping its
 output rows (``--gather`` adds the all-gather).
@@ -405,7 +405,7 @@ def engine_arm(args):
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    from memfast_b200.sharding import gather_rows, row_range, sharded_mm
+    from memfast_b200.sharding import gather_rows, row_parallel_mm, row_range, sharded_mm
 
     spec = product_spec(mf, args)
     config, size = spec[0], spec[1]
@@ -435,11 +435,14 @@ def engine_arm(args):
     stream = torch.cuda.current_stream(device)
 
     def step():
-        # This rank's rows with global vector indices (written straight into its rows of
-        # the full output when strong scaling); then the rows of every rank.
+        # Strong scaling: this rank's rows with global vector indices, written straight
+        # into its rows of the full output, and the in-place all-gather enqueued before
+        # the call's one host synchronisation.  Weak scaling: each rank's own product.
         if world == 1:
             return sim.mm(a, b)
-        out = sharded_mm(a, b, simulator=sim, row_offset=r0, out=own)
+        if strong:
+            return row_parallel_mm(a, b, simulator=sim, row_offset=r0, rows=total_rows, out=full)
+        out = sharded_mm(a, b, simulator=sim, row_offset=r0)
         if gather:
             return gather_rows(out, total_rows, out=full)
         return out

@@ -303,6 +303,7 @@ template <int GR>
 __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_t ldb, QuantSpec s, int R, int C,
                                     int64_t m, int64_t p, float* maxima, uint8_t* packed, uint8_t* kmajor,
                                     float* wscale) {
+    static_assert(GR % 32 == 0, "K-major stores cover whole 32-row sectors");
     const int64_t groups = (K + GR - 1) / GR;
     const int64_t total = groups * O;
     const int64_t kpad = m * R;
@@ -338,10 +339,11 @@ __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_
         int rr = (int)(k0 - arr * R);
         uint8_t* dst = packed + ((arr * p + t) * R + rr) * C + c;
         const int64_t next_array = (p - 1) * R * C;   // from row R-1 of one array to row 0 of the next
-        // K-major codes leave in 16-byte stores (4 words) where the 16 bytes are inside
-        // the padded K and aligned, else word by word: a 4-byte store per word would
-        // cost the memory system one partial-sector write per word.
-        uint32_t words[4] = {0, 0, 0, 0};
+        // K-major codes leave as whole 32-byte sectors (two 16-byte stores back to back)
+        // where the 32 bytes are inside the padded K and aligned, else word by word: a
+        // 16-byte store now and its neighbour later cost the memory system two
+        // partial-sector writes.
+        uint32_t words[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll 16
         for (int r = 0; r < GR; ++r) {
             const int64_t k = k0 + r;
@@ -352,17 +354,20 @@ __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_
                 rr = 0;
                 dst += next_array;
             }
-            words[(r >> 2) & 3] |= code << (8 * (r & 3));
-            if ((r & 15) == 15 && kmajor) {
-                uint8_t* dst = kmajor + o * kpad + k - 15;
-                if (k < kpad && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                    *reinterpret_cast<uint4*>(dst) = make_uint4(words[0], words[1], words[2], words[3]);
+            words[(r >> 2) & 7] |= code << (8 * (r & 3));
+            if ((r & 31) == 31 && kmajor) {
+                uint8_t* dst = kmajor + o * kpad + k - 31;
+                if (k < kpad && (reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+                    uint4* out = reinterpret_cast<uint4*>(dst);
+                    out[0] = make_uint4(words[0], words[1], words[2], words[3]);
+                    out[1] = make_uint4(words[4], words[5], words[6], words[7]);
                 } else {
 #pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        if (k - 15 + 4 * q + 3 < kpad) *reinterpret_cast<uint32_t*>(dst + 4 * q) = words[q];
+                    for (int q = 0; q < 8; ++q)
+                        if (k - 31 + 4 * q + 3 < kpad) *reinterpret_cast<uint32_t*>(dst + 4 * q) = words[q];
                 }
-                words[0] = words[1] = words[2] = words[3] = 0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) words[q] = 0;
             }
         }
     }

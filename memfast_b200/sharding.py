@@ -25,7 +25,7 @@ ranks rerun together exactly when the single-device layer would.
 import torch
 import torch.distributed as dist
 
-from .functional import _checked, _operands
+from .functional import OPERAND_ERRORS, _operand_code, _operand_types
 from .simulator import AnalogMatrix, Simulator
 
 
@@ -47,25 +47,79 @@ def sharded_mm(a_local, b, *, simulator, row_offset, out=None):
     the full output, which ``gather_rows`` then fills in place) receiving the
     result.
     """
+    _check_row_shard(a_local, b, simulator, row_offset)
+    if out is not None and (out.shape != (a_local.shape[0], b.shape[1]) or out.dtype != a_local.dtype
+                            or out.device != a_local.device or out.stride(-1) != 1):
+        raise ValueError("out must be a [rows, O] buffer of A's dtype and device with unit column stride")
+    return _row_product(a_local, b, simulator, row_offset, out)
+
+
+def _check_row_shard(a_local, b, simulator, row_offset):
     if not isinstance(simulator, Simulator):
         raise TypeError("simulator must be Simulator")
+    _operand_types(a_local, b)
     if a_local.ndim != 2 or b.ndim != 2 or a_local.shape[1] != b.shape[0]:
         raise ValueError("sharded_mm needs [rows, K] and [K, O] operands")
     if type(row_offset) is not int or row_offset < 0:
         raise ValueError("row_offset must be a non-negative int")
-    config = simulator.config
-    if config.input_quant_gran[0] not in (1,):
+    if simulator.config.input_quant_gran[0] not in (1,):
         raise ValueError("row sharding needs per-vector input groups (input_quant_gran[0] == 1)")
-    _operands(a_local, b)
     if a_local.device != simulator.device:
         raise ValueError("operands and simulator must use the same device")
-    if out is not None and (out.shape != (a_local.shape[0], b.shape[1]) or out.dtype != a_local.dtype
-                            or out.device != a_local.device or out.stride(-1) != 1):
-        raise ValueError("out must be a [rows, O] buffer of A's dtype and device with unit column stride")
-    matrix = simulator._matrix_for(b, checked=_checked(b, config, config.weight_bits), rows=a_local.shape[0])
+
+
+def _row_product(a_local, b, simulator, row_offset, out, before_sync=None):
+    """The rows' product with the operand checks read in the call's one synchronisation
+    (functional.mm's deferred check: same errors, same order)."""
+    code = _operand_code(a_local, b, simulator.config)
+    matrix = simulator._matrix_for(b, checked=True, rows=a_local.shape[0])
     with torch.no_grad():
-        return matrix._forward(a_local.detach(), checked=_checked(a_local, config, config.activation_bits),
-                               vector_offset=row_offset, out=out)
+        return matrix._forward(a_local.detach(), checked=True, vector_offset=row_offset, input_flag=code,
+                               input_errors=OPERAND_ERRORS, out=out, before_sync=before_sync)
+
+
+def row_parallel_mm(a_local, b, *, simulator, row_offset, rows, out=None, group=None):
+    """The whole [rows, O] product ``A @ B`` on every rank of ``group``, each rank
+    holding A's row block [row_offset, row_offset + rows / world) (equal blocks in
+    rank order, as ``row_range`` gives when world divides rows).
+
+    Each rank's rows are written straight into its rows of ``out`` (allocated when
+    None).  The in-place NCCL all-gather of every rank's rows and an all-reduce of
+    the ranks' check flags are enqueued on the stream right after the product,
+    before the call's one host synchronisation, so the transfer follows the product
+    on the device with no host round trip in between.  Because the flags are
+    combined, the FP64 rerun of a product with non-finite outputs
+    (simulator.py:614-615) is decided for the whole product, as on one device:
+    every rank reruns its rows and the gather is repeated; operand errors are
+    raised on every rank.  Bit-identical to ``simulator.mm(A, B)`` on one device.
+    """
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    _check_row_shard(a_local, b, simulator, row_offset)
+    share = rows // world if type(rows) is int and rows >= 0 else -1
+    if share < 0 or rows % world or a_local.shape[0] != share or row_offset != rank * share:
+        raise ValueError("row_parallel_mm needs equal row blocks in rank order: rows divisible by the world size")
+    width = b.shape[1]
+    if out is None:
+        out = torch.empty((rows, width), dtype=a_local.dtype, device=a_local.device)
+    elif out.shape != (rows, width) or out.dtype != a_local.dtype or out.device != a_local.device \
+            or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [rows, O] buffer of A's dtype and device")
+    own = out[row_offset: row_offset + share]
+    gathered = []
+
+    def before_sync(output, flags):
+        dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=group)
+        direct = output.data_ptr() == own.data_ptr()
+        if direct:
+            dist.all_gather_into_tensor(out, own, group=group)
+        gathered.append(direct)
+
+    _row_product(a_local, b, simulator, row_offset, own, before_sync)
+    if not gathered[-1]:
+        # The rows reached `out` after the synchronisation (an FP64 rerun, or a result
+        # cast to A's dtype): gather them now; every rank takes this branch together.
+        dist.all_gather_into_tensor(out, own, group=group)
+    return out
 
 
 def gather_rows(local, n, group=None, out=None):
@@ -168,5 +222,5 @@ def tensor_parallel(model, group=None, *, gather=True):
     return model
 
 
-__all__ = ["row_range", "sharded_mm", "gather_rows", "tile_range", "gather_columns", "shard_columns",
-           "tensor_parallel", "ColumnShard"]
+__all__ = ["row_range", "sharded_mm", "row_parallel_mm", "gather_rows", "tile_range", "gather_columns",
+           "shard_columns", "tensor_parallel", "ColumnShard"]

@@ -533,7 +533,7 @@ class AnalogMatrix(nn.Module):
         return _workspace_bytes(self.config, n, m, self.p, tuple(sorted(schedule.items())))
 
     def _execute(self, q, xscale, schedule, event, stable=False, *, vector_offset=0, input_flag=None,
-                 input_errors=None, tiles=None, agree=None, output=None):
+                 input_errors=None, tiles=None, agree=None, output=None, before_sync=None):
         """One fused device call: analog partials, scales, read sums and bias.
 
         ``input_flag``: device int32 set by a quantiser that checks finiteness on the
@@ -543,7 +543,11 @@ class AnalogMatrix(nn.Module):
         global), giving columns [t0*cols, min(t1*cols, out_features)).
         ``agree``: combines this shard's finiteness with the other shards' (the FP64
         rerun is decided for the whole product); ``output``: a buffer of the product's
-        shape and dtype to write into (the FP64 rerun allocates its own)."""
+        shape and dtype to write into (the FP64 rerun allocates its own);
+        ``before_sync(output, flags)``: work to enqueue on the stream after the product
+        and its checks but before the host reads the flags (collectives of a sharded
+        product, which may also combine the flags of every rank); it runs again for
+        the FP64 rerun."""
         output = self._launch(q, xscale, schedule, event, stable=stable, vector_offset=vector_offset, tiles=tiles,
                               output=output)
         # One host synchronisation decides both the FP64 rerun of a narrow config
@@ -552,6 +556,8 @@ class AnalogMatrix(nn.Module):
         flags = input_flag if input_flag is not None else torch.zeros(2, dtype=torch.int32, device=q.device)
         check_finite(output, flags[1:2], 1)
         staged = stage_device_error(q.device)
+        if before_sync is not None:
+            before_sync(output, flags)
         bad, nonfinite = flags.tolist()
         if bad:
             raise ValueError((input_errors or {}).get(bad, "quantized values must be finite"))
@@ -561,7 +567,8 @@ class AnalogMatrix(nn.Module):
         if agree is not None:
             self._finite = agree(self._finite)
         if not self.config.wide and not stable and not self._finite:
-            return self._execute(q, xscale, schedule, event, stable=True, vector_offset=vector_offset, tiles=tiles)
+            return self._execute(q, xscale, schedule, event, stable=True, vector_offset=vector_offset, tiles=tiles,
+                                 before_sync=before_sync)
         return output
 
     def _zero_point_correction(self, q, xscale, output, c0, c1, wide):
@@ -656,12 +663,13 @@ class AnalogMatrix(nn.Module):
         return self._forward(x) if shard is None else shard(self, x)
 
     def _forward(self, x, checked=False, vector_offset=0, tiles=None, agree=None, input_flag=None,
-                 input_errors=None, out=None):
+                 input_errors=None, out=None, before_sync=None):
         """forward(); ``checked``: the caller verified x finite in the quantiser's dtype;
         ``vector_offset``: global index of x's first vector (noise addresses of row shards);
         ``tiles``/``agree``: a column shard, as in ``_execute``; ``input_flag`` /
         ``input_errors``: a deferred operand check, as in ``_execute``; ``out``: a
-        contiguous-rows [vectors, width] buffer of x's dtype receiving the result."""
+        contiguous-rows [vectors, width] buffer of x's dtype receiving the result;
+        ``before_sync``: as in ``_execute``."""
         if x.ndim < 1 or x.shape[-1] != self.in_features or not x.is_floating_point():
             raise ValueError("input must be floating with matching in_features")
         if x.device != self.packed.device or x.device != self.simulator.device:
@@ -678,11 +686,11 @@ class AnalogMatrix(nn.Module):
             raise OverflowError("read-event counter exhausted")
         q, xscale = input_tiles(x.reshape(-1, self.in_features), self.config, self.input_scale, checked=checked)
         output = self._product(q, xscale, shape, x.dtype, vector_offset=vector_offset, tiles=tiles, agree=agree,
-                               input_flag=input_flag, input_errors=input_errors, out=out)
+                               input_flag=input_flag, input_errors=input_errors, out=out, before_sync=before_sync)
         return output.reshape(*shape[:-1], width)
 
     def _product(self, q, xscale, shape, dtype, *, vector_offset=0, input_flag=None, input_errors=None,
-                 tiles=None, agree=None, out=None):
+                 tiles=None, agree=None, out=None, before_sync=None):
         """forward() from quantised codes on (simulator.py:631-646): schedule, product,
         non-finite checks, ``dtype`` result, read event.  ``shape``/``dtype`` describe
         the caller's input (tuned-mode key); ``input_flag`` as in ``_execute``."""
@@ -700,7 +708,8 @@ class AnalogMatrix(nn.Module):
         direct = out if out is not None and out.dtype == (torch.float64 if self.config.wide else torch.float32) \
             else None
         output = self._execute(q, xscale, schedule, event, vector_offset=vector_offset, input_flag=input_flag,
-                               input_errors=input_errors, tiles=tiles, agree=agree, output=direct)
+                               input_errors=input_errors, tiles=tiles, agree=agree, output=direct,
+                               before_sync=before_sync)
         finite = self._finite and (output.dtype == dtype or finite_flags(output, dtypes=[dtype])[0])
         if agree is not None:
             finite = agree(finite)
