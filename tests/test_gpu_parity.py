@@ -84,8 +84,13 @@ def _int8(mf, **effects):
                      adc_bits=(6, 7, 7, 8, 8), nonidealities=mf.Nonidealities(**effects))
 
 
-@pytest.mark.parametrize("shape", [(1, 128, 128), (33, 257, 300), (256, 1024, 512), (7, 2048, 128)])
+@pytest.mark.parametrize("shape", [(1, 128, 128), (33, 257, 300), (256, 1024, 512), (7, 2048, 128),
+                                   (8, 16384, 128), (3, 12320, 200)])
 def test_ideal_int8_vs_oracle(mf, shape):
+    """K = 16384 is 512 reads of 32 rows per output: PyTorch's CPU sum over reads
+    (``value.sum(1)``, memfast/simulator.py:585) then cascades over more than 256
+    elements, which the packed kernel declines (it keeps two 16-read levels), and
+    12320 leaves a ragged last array and a ragged last cascade block."""
     from oracle import oracle as O
 
     n, k, o = shape
@@ -94,6 +99,19 @@ def test_ideal_int8_vs_oracle(mf, shape):
     a, b = torch.randn(n, k, generator=g), torch.randn(k, o, generator=g)
     got = mf.Simulator(config).mm(a.cuda(), b.cuda()).cpu().numpy()
     assert_parity(got, O.mm(a.numpy(), b.numpy(), config), config, str(shape))
+
+
+def test_nonideal_deep_cascade_vs_oracle(mf):
+    """512 reads per output with write variation: the tensor-core current kernel's
+    cascade above 256 reads, against the oracle within the nonideal tolerance."""
+    from oracle import oracle as O
+
+    config = _int8(mf, write_variation=0.02)
+    g = torch.Generator().manual_seed(9)
+    a, b = torch.randn(8, 16384, generator=g), torch.randn(16384, 128, generator=g)
+    got = mf.Simulator(config).mm(a.cuda(), b.cuda()).cpu().numpy()
+    tolerance = dict(flip=flip_size(config, a.numpy(), b.numpy()), events=adc_events(config, 16384))
+    assert_parity(got, O.mm(a.numpy(), b.numpy(), config), config, "deep cascade", **tolerance)
 
 
 def test_nonideal_all_effects_vs_oracle(mf):
