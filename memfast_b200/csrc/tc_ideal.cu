@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     static_assert(NA <= MAXPA && NWA + NWC <= MAXPB, "plan exceeds shared-memory planes");
     static_assert(32 + NA * NWA * SUB <= HALF_COLS && NA * NWC * SUB <= HALF_COLS, "unit exceeds a TMEM half");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem& s = *reinterpret_cast<Smem*>(smem_align1024(smem_raw));
     const Plan& P = args.plan;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long n0 = (long long)raster_vector_block(args.raster) * BM;

@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     static_assert(NCOL <= MAXCOL, "too many count blocks");
     static_assert(H == 1 || H == 2, "reads of 32 or 64 rows");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem& s = *reinterpret_cast<Smem*>(smem_align1024(smem_raw));
     const Plan& P = args.plan;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const unsigned vblk = raster_vector_block(args.raster), cblk = raster_column_block(args.raster);

@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // TMEM is the integer digit dot itself: one FP16 part, no split halves.
     static_assert(!FSUM || (!SPLIT && NPART == 1), "FSUM needs exact integer digit dots (one FP16 part)");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* base = smem_align1024(smem_raw);
     uint8_t* a_planes = base + G::OFF_A;
     float* acc1 = reinterpret_cast<float*>(base + G::OFF_ACC1);             // [BC][BM]
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + G::OFF_BAR);

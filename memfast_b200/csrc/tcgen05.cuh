@@ -14,6 +14,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }
 
+// First 1024-byte-aligned byte of the dynamic shared-memory window (SWIZZLE
+// atoms and UMMA descriptors want that alignment).  It is computed by pointer
+// arithmetic on the __shared__ array itself, so the compiler keeps the state
+// space and every access through the result is a shared-memory load or store;
+// rounding the address as an integer would leave generic loads (4% of the packed
+// kernel's time at 4096^3).
+__device__ __forceinline__ uint8_t* smem_align1024(uint8_t* raw) {
+    return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
+
 // ------------------------------------------------------------------ mbarriers
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
