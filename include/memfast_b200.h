@@ -256,6 +256,45 @@ mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedu
                                  int32_t m, int32_t p, int32_t tile_begin, int32_t tile_end,
                                  size_t* bytes);
 
+/* Caller-owned device buffers of one mf_mm call. */
+typedef struct {
+    void* codes;                 /* [n, m*rows] input codes, as mf_quantize_input writes them */
+    void* xscale;                /* [n, m*reads] per-read input scales */
+    void* packed;                /* [m, p, rows, cols] program of b, rewritten by the call */
+    void* wscale;                /* [m*reads, p, cols] */
+    void* out;                   /* [n, o] contiguous, FP32 (FP64 when cfg->wide) */
+    uint32_t* flags;             /* 2 device words: [operand check, output check] */
+    void* quantize_workspace;    /* mf_quantize_workspace(cfg, 0, n, k) bytes */
+    size_t quantize_workspace_bytes;
+    void* program_workspace;     /* mf_quantize_workspace(cfg, 1, o, k) bytes */
+    size_t program_workspace_bytes;
+    void* mm_workspace;          /* mf_sliced_mm_workspace(cfg, schedule, n, m, p, 0, p) bytes */
+    size_t mm_workspace_bytes;
+} mf_mm_buffers;
+
+/* One default-mode product out = A @ B with B programmed by the call, enqueued on
+ * `stream` with no host synchronisation: the sequence that memfast.mm /
+ * Simulator.mm runs per call (functional.py:50-53, simulator.py:121-171 and
+ * 561-616 of the reference), in one crossing of this ABI instead of one per step.
+ *   a: [n, k] and b: [k, o], contiguous, both of dtype `dtype`.
+ *   Checks (flags cleared first): flags[0] becomes 1 if A is not finite, else 2
+ *   if B is not finite (or b_narrow_code when B's FP64 values overflow FP32),
+ *   else a_narrow_code when that is non-zero and A's FP64 values overflow FP32,
+ *   as mf_check_operands gives them; flags[1] becomes 1 if an output is not
+ *   finite.  For FP32 operands of the one-pass quantisers the operand checks
+ *   ride on the quantisers' reads instead of separate passes.
+ *   Then A is quantised (mf_quantize_input), b programmed into packed/wscale
+ *   (mf_program_rhs) with the K-major copy written at the start of
+ *   mm_workspace when the schedule's kernel reads one, and the fused product
+ *   of all p tiles runs (mf_sliced_mm: seed, event, vector_offset as there).
+ *   error_word: NULL, or pinned host memory receiving the device error word
+ *   (mf_stage_device_error) after the product.
+ * The results equal those of the separate calls bit for bit. */
+mf_status mf_mm(const mf_config* cfg, const mf_schedule* schedule, const void* a, const void* b, int32_t dtype,
+                int64_t n, int64_t k, int64_t o, uint32_t a_narrow_code, uint32_t b_narrow_code,
+                const mf_mm_buffers* buffers, uint32_t seed, uint64_t event, int64_t vector_offset,
+                uint32_t* error_word, void* stream);
+
 /* Kernel families behind mf_sliced_mm.  The reference has one pair of SIMT
  * kernels (memfast/kernels.cu:43-202); this engine picks among these per
  * configuration and schedule. */

@@ -73,6 +73,14 @@ class MFConv2d(ct.Structure):
                                                 "group_channels")]
 
 
+class MFMMBuffers(ct.Structure):
+    _fields_ = [("codes", ct.c_void_p), ("xscale", ct.c_void_p), ("packed", ct.c_void_p), ("wscale", ct.c_void_p),
+                ("out", ct.c_void_p), ("flags", ct.c_void_p),
+                ("quantize_workspace", ct.c_void_p), ("quantize_workspace_bytes", ct.c_size_t),
+                ("program_workspace", ct.c_void_p), ("program_workspace_bytes", ct.c_size_t),
+                ("mm_workspace", ct.c_void_p), ("mm_workspace_bytes", ct.c_size_t)]
+
+
 _VOID = ct.c_void_p
 _SIGNATURES = {
     "mf_abi_version": (ct.c_int32, []),
@@ -101,6 +109,9 @@ _SIGNATURES = {
                                 _VOID, _VOID, ct.c_int64, ct.c_int32, ct.c_int32, ct.c_int32, ct.c_int64,
                                 ct.c_int32, ct.c_int32, ct.c_uint32, ct.c_uint64, ct.c_int64, ct.c_int32,
                                 _VOID, ct.c_size_t, _VOID]),
+    "mf_mm": (ct.c_int, [ct.POINTER(MFConfig), ct.POINTER(MFSchedule), _VOID, _VOID, ct.c_int32, ct.c_int64,
+                         ct.c_int64, ct.c_int64, ct.c_uint32, ct.c_uint32, ct.POINTER(MFMMBuffers), ct.c_uint32,
+                         ct.c_uint64, ct.c_int64, _VOID, _VOID]),
     "mf_sliced_mm_workspace": (ct.c_int, [ct.POINTER(MFConfig), ct.POINTER(MFSchedule), ct.c_int64,
                                           ct.c_int32, ct.c_int32, ct.c_int32, ct.c_int32,
                                           ct.POINTER(ct.c_size_t)]),

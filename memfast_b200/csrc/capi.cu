@@ -392,6 +392,73 @@ mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const 
     return r;
 }
 
+mf_status mf_mm(const mf_config* cfg, const mf_schedule* schedule, const void* a, const void* b, int32_t dtype,
+                int64_t n, int64_t k, int64_t o, uint32_t a_narrow_code, uint32_t b_narrow_code,
+                const mf_mm_buffers* buffers, uint32_t seed, uint64_t event, int64_t vector_offset,
+                uint32_t* error_word, void* stream) {
+    mf_status st = check_config(cfg);
+    if (st) return st;
+    const mf_mm_buffers* B = buffers;
+    if (!a || !b || !B || !B->codes || !B->xscale || !B->packed || !B->wscale || !B->out || !B->flags ||
+        !B->program_workspace || n < 1 || k < 1 || o < 1 || vector_offset < 0 ||
+        dtype < MF_F32 || dtype > MF_F64) {
+        set_error("mf_mm: invalid operands (n=%lld k=%lld o=%lld dtype=%d)", (long long)n, (long long)k,
+                  (long long)o, dtype);
+        return MF_ERR_INVALID;
+    }
+    const mf_config& c = *cfg;
+    const int64_t m64 = (k + c.rows - 1) / c.rows, p64 = (o + c.cols - 1) / c.cols;
+    if (m64 > INT32_MAX || p64 > INT32_MAX || o > INT32_MAX) {
+        set_error("mf_mm: matrix too large for one product");
+        return MF_ERR_RESOURCE;
+    }
+    const int32_t m = (int32_t)m64, p = (int32_t)p64;
+    const mf_schedule s = schedule_or_default(schedule);
+    const size_t quantize_need = quantize_workspace_bytes(c, false, n, k);
+    const size_t program_need = quantize_workspace_bytes(c, true, o, k);
+    size_t mm_need = 0;
+    st = mf_sliced_mm_workspace(cfg, &s, n, m, p, 0, p, &mm_need);
+    if (st) return st;
+    if (B->quantize_workspace_bytes < quantize_need || !B->quantize_workspace ||
+        B->program_workspace_bytes < program_need || B->mm_workspace_bytes < mm_need ||
+        (mm_need && !B->mm_workspace)) {
+        set_error("mf_mm: workspaces too small (%zu/%zu, %zu/%zu, %zu/%zu bytes)", B->quantize_workspace_bytes,
+                  quantize_need, B->program_workspace_bytes, program_need, B->mm_workspace_bytes, mm_need);
+        return MF_ERR_RESOURCE;
+    }
+    const cudaStream_t stream_ = (cudaStream_t)stream;
+    uint32_t* flags = B->flags;
+    MF_CHECK_CUDA(cudaMemsetAsync(flags, 0, 2 * sizeof(uint32_t), stream_), "clear mf_mm flags");
+    // Operand checks in the reference's order (A, then B, then the quantisers' FP32
+    // narrowing): folded into the quantiser passes when nothing narrows, else run
+    // first as mf_check_operands runs them.
+    uint32_t* fold = flags;
+    if (a_narrow_code || b_narrow_code) {
+        st = check_finite(a, dtype, n * k, 1, 0, flags, stream_);
+        if (!st) st = check_finite(b, dtype, k * o, 2, b_narrow_code, flags, stream_);
+        if (!st && a_narrow_code) st = check_finite(a, dtype, n * k, 1, a_narrow_code, flags, stream_);
+        if (st) return st;
+        fold = nullptr;
+    }
+    st = quantize_input(c, a, dtype, n, k, k, nullptr, B->codes, B->xscale, B->quantize_workspace,
+                        B->quantize_workspace_bytes, stream_, fold, 1);
+    if (st) return st;
+    // The tensor-core kernels read a K-major copy of the codes at the start of their
+    // workspace; programming writes it in the same pass.
+    const bool kmajor = !c.wide_codes && (use_packed(c, s, m, 0) || use_tc(c, s, m, 0));
+    st = program_rhs(c, b, dtype, k, o, o, B->packed, B->wscale, kmajor ? B->mm_workspace : nullptr,
+                     B->program_workspace, B->program_workspace_bytes, stream_, fold, 2);
+    if (st) return st;
+    mf_schedule run = s;
+    run.kmajor_ready = kmajor ? 1 : 0;
+    st = mf_sliced_mm(cfg, &run, B->codes, B->xscale, B->packed, B->wscale, nullptr, B->out, n, m, p, (int32_t)o, o,
+                      0, p, seed, event, vector_offset, 0, B->mm_workspace, B->mm_workspace_bytes, stream);
+    if (st) return st;
+    st = check_finite(B->out, c.wide ? MF_F64 : MF_F32, n * o, 1, 0, flags + 1, stream_);
+    if (st) return st;
+    return error_word ? tc_stage_error(error_word, stream_) : MF_OK;
+}
+
 int32_t mf_last_path(void) { return g_last_path; }
 
 mf_status mf_debug_stall_next_launch(int32_t stop_stage, int64_t wait_cycles) {

@@ -11,9 +11,12 @@ namespace mf {
 
 size_t quantize_workspace_bytes(const mf_config& c, bool weight, int64_t rows, int64_t cols);
 
+// check_flag (optional): the finiteness check of x folded into the pass (the
+// device word becomes check_code if still 0 and a value of x is not finite).
 mf_status quantize_input(const mf_config& c, const void* x, int dtype, int64_t n, int64_t k,
                          int64_t ldx, const void* fixed, void* codes, void* xscale,
-                         void* workspace, size_t ws_bytes, cudaStream_t stream);
+                         void* workspace, size_t ws_bytes, cudaStream_t stream, uint32_t* check_flag = nullptr,
+                         uint32_t check_code = 0);
 
 mf_status program_weights(const mf_config& c, const void* w, int dtype, int64_t o, int64_t k,
                           int64_t ldw, void* packed, void* wscale, void* workspace,
@@ -38,9 +41,10 @@ mf_status quantize_conv_input(const mf_config& c, const mf_conv2d& cv, const voi
 
 // Program a right-hand [k, o] matrix b (row stride ldb); optionally also write the
 // K-major [p*C, m*R] copy of the packed codes the tensor-core kernels read.
+// check_flag as quantize_input's, for b.
 mf_status program_rhs(const mf_config& c, const void* b, int dtype, int64_t k, int64_t o, int64_t ldb,
                       void* packed, void* wscale, void* kmajor, void* workspace, size_t ws_bytes,
-                      cudaStream_t stream);
+                      cudaStream_t stream, uint32_t* check_flag = nullptr, uint32_t check_code = 0);
 
 // Everything one sliced product needs, validated by the ABI layer.
 struct MMArgs {

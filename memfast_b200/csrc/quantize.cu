@@ -191,7 +191,8 @@ __global__ void input_code_kernel(View v, GroupGrid g, const Acc* maxima, const 
 // (up to m * R) get code 0 and do not enter any maximum.
 template <int T>
 __global__ void input_rowgroup_kernel(const float* x, int64_t n, int64_t k, int64_t ldx, int64_t padded_cols,
-                                      int64_t nc, QuantSpec s, float* maxima, uint8_t* codes, float* xscale) {
+                                      int64_t nc, QuantSpec s, float* maxima, uint8_t* codes, float* xscale,
+                                      uint32_t* check_flag, uint32_t check_code) {
     constexpr int GC = 4 * T;
     const int64_t groups_per_row = padded_cols / GC;
     const int64_t teams = n * groups_per_row;
@@ -225,8 +226,15 @@ __global__ void input_rowgroup_kernel(const float* x, int64_t n, int64_t k, int6
                 if (c + e < k) v[e] = row[c + e];
         }
         float best = 0.0f;
+        bool bad = false;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) best = fmaxf(best, fabsf(v[e]));
+        for (int e = 0; e < 4; ++e) {
+            best = fmaxf(best, fabsf(v[e]));
+            bad |= !(fabsf(v[e]) <= FLT_MAX);   // NaN or infinity (zero padding passes)
+        }
+        // The operand check of the product, folded into this read of x: the first
+        // failing check of the stream keeps its code (mf_check_finite's rule).
+        if (bad && check_flag && *(volatile uint32_t*)check_flag == 0u) atomicCAS(check_flag, 0u, check_code);
 #pragma unroll
         for (int off = T / 2; off > 0; off >>= 1) best = fmaxf(best, __shfl_xor_sync(0xFFFFFFFFu, best, off, T));
         const float scale = group_scale<float>(best, s);
@@ -302,7 +310,7 @@ __global__ void weight_code_kernel(View v, GroupGrid g, const Acc* maxima, Quant
 template <int GR>
 __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_t ldb, QuantSpec s, int R, int C,
                                     int64_t m, int64_t p, float* maxima, uint8_t* packed, uint8_t* kmajor,
-                                    float* wscale) {
+                                    float* wscale, uint32_t* check_flag, uint32_t check_code) {
     static_assert(GR % 32 == 0, "K-major stores cover whole 32-row sectors");
     const int64_t groups = (K + GR - 1) / GR;
     const int64_t total = groups * O;
@@ -316,9 +324,17 @@ __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_
         const float* col = b + k0 * ldb + o;
         const int rows = K - k0 < GR ? (int)(K - k0) : GR;
         float best = 0.0f;
+        bool bad = false;
 #pragma unroll 8
         for (int r = 0; r < GR; ++r)
-            if (r < rows) best = fmaxf(best, fabsf(__ldg(col + r * ldb)));
+            if (r < rows) {
+                const float value = fabsf(__ldg(col + r * ldb));
+                best = fmaxf(best, value);
+                bad |= !(value <= FLT_MAX);   // NaN or infinity
+            }
+        // The operand check of the product, folded into this read of b (first failing
+        // check of the stream keeps its code).
+        if (bad && check_flag && *(volatile uint32_t*)check_flag == 0u) atomicCAS(check_flag, 0u, check_code);
         maxima[j * O + o] = best;
         const float scale = group_scale<float>(best, s);
         const float inv = __frcp_rn(scale);
@@ -685,7 +701,8 @@ static int rowgroup_team(const mf_config& c, const View& v, const GroupGrid& g, 
 template <typename Acc, typename ScaleT>
 static mf_status run_input(const mf_config& c, const View& v, const GroupGrid& g, const QuantSpec& s,
                            const void* fixed, void* codes, void* xscale, void* workspace,
-                           size_t need, cudaStream_t stream) {
+                           size_t need, cudaStream_t stream, uint32_t* check_flag = nullptr,
+                           uint32_t check_code = 0) {
     const int threads = 256;
     const int64_t n = v.rows, k = v.cols, m = (k + c.rows - 1) / c.rows;
     Acc* maxima = static_cast<Acc*>(workspace);
@@ -701,7 +718,8 @@ static mf_status run_input(const mf_config& c, const View& v, const GroupGrid& g
 #define MF_ROWGROUP(TEAM)                                                                                    \
     input_rowgroup_kernel<TEAM><<<blocks, threads, 0, stream>>>(static_cast<const float*>(v.data), n, k, v.ld, \
                                                                 padded, g.nc, s, reinterpret_cast<float*>(maxima), \
-                                                                static_cast<uint8_t*>(codes), fused_xscale)
+                                                                static_cast<uint8_t*>(codes), fused_xscale,     \
+                                                                check_flag, check_code)
         switch (team) {
             case 1: MF_ROWGROUP(1); break;
             case 2: MF_ROWGROUP(2); break;
@@ -738,7 +756,8 @@ static mf_status run_input(const mf_config& c, const View& v, const GroupGrid& g
 
 mf_status quantize_input(const mf_config& c, const void* x, int dtype, int64_t n, int64_t k,
                          int64_t ldx, const void* fixed, void* codes, void* xscale,
-                         void* workspace, size_t ws_bytes, cudaStream_t stream) {
+                         void* workspace, size_t ws_bytes, cudaStream_t stream, uint32_t* check_flag,
+                         uint32_t check_code) {
     View v{x, dtype, n, k, ldx, 0};
     GroupGrid g = groups_of(n, k, c.in_group_rows, c.in_group_cols);
     QuantSpec s = spec_of(c.activation_bits, 1, c.bw_e);
@@ -751,13 +770,29 @@ mf_status quantize_input(const mf_config& c, const void* x, int dtype, int64_t n
     // FP64 iff Config.wide (quantization.py:10,131).  A fixed scale arrives in the
     // stored dtype and is applied in it (quantization.py:124-130).
     const bool dbl = uses_double(c, c.activation_bits);
+    if (check_flag) {
+        // The one-pass kernel checks x as it reads it; every other path gets the
+        // separate check first (x must then be contiguous).
+        if (dbl || fixed || !rowgroup_team(c, v, g, nullptr)) {
+            if (ldx != k) {
+                set_error("a folded finiteness check needs contiguous inputs");
+                return MF_ERR_INVALID;
+            }
+            mf_status st = check_finite(x, dtype, n * k, check_code, 0, check_flag, stream);
+            if (st) return st;
+            check_flag = nullptr;
+        }
+    }
     if (fixed) {
         return c.wide ? run_input<double, double>(c, v, g, s, fixed, codes, xscale, workspace, need, stream)
                       : run_input<float, float>(c, v, g, s, fixed, codes, xscale, workspace, need, stream);
     }
     if (dbl) return run_input<double, double>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
-    if (c.wide) return run_input<float, double>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
-    return run_input<float, float>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream);
+    if (c.wide)
+        return run_input<float, double>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream, check_flag,
+                                        check_code);
+    return run_input<float, float>(c, v, g, s, nullptr, codes, xscale, workspace, need, stream, check_flag,
+                                   check_code);
 }
 
 mf_status check_finite(const void* x, int dtype, int64_t n, uint32_t code_own, uint32_t code_narrow,
@@ -863,7 +898,7 @@ static mf_status run_weights(const mf_config& c, const View& v, const GroupGrid&
 
 mf_status program_rhs(const mf_config& c, const void* b, int dtype, int64_t k, int64_t o, int64_t ldb,
                       void* packed, void* wscale, void* kmajor, void* workspace, size_t ws_bytes,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, uint32_t* check_flag, uint32_t check_code) {
     View v{b, dtype, k, o, ldb, 0};  // logical [k, o] = b
     GroupGrid g = groups_of(k, o, c.w_group_rows, c.w_group_cols);
     QuantSpec s = spec_of(c.weight_bits, c.weight_signed, c.bw_e);
@@ -879,6 +914,17 @@ mf_status program_rhs(const mf_config& c, const void* b, int dtype, int64_t k, i
     const bool words_aligned = !kmajor || ((m * c.rows) % 4 == 0 && (reinterpret_cast<uintptr_t>(kmajor) & 3) == 0);
     const bool fused = !dbl && !c.wide && !c.wide_codes && dtype == MF_F32 && g.gc == 1 &&
                        (g.gr == 32 || g.gr == 64) && words_aligned;
+    if (check_flag && !fused) {
+        // Only the one-pass kernel checks b as it reads it: the others get the
+        // separate check first (b must then be contiguous).
+        if (ldb != o) {
+            set_error("a folded finiteness check needs a contiguous right-hand matrix");
+            return MF_ERR_INVALID;
+        }
+        mf_status st = check_finite(b, dtype, k * o, check_code, 0, check_flag, stream);
+        if (st) return st;
+        check_flag = nullptr;
+    }
     if (fused) {
         const size_t packed_bytes = (size_t)m * p * c.rows * c.cols;
         if (k < m * c.rows || o < p * c.cols) {
@@ -894,11 +940,11 @@ mf_status program_rhs(const mf_config& c, const void* b, int dtype, int64_t k, i
         if (g.gr == 32)
             rhs_colgroup_kernel<32><<<grid_for(work, threads), threads, 0, stream>>>(
                 static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
-                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale);
+                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale, check_flag, check_code);
         else
             rhs_colgroup_kernel<64><<<grid_for(work, threads), threads, 0, stream>>>(
                 static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
-                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale);
+                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale, check_flag, check_code);
         MF_LAUNCH_CHECK("rhs_colgroup_kernel");
         if (scales_fused) return MF_OK;
         weight_scale_kernel<float, float><<<grid_for(m * c.reads * p * c.cols, threads), threads, 0, stream>>>(

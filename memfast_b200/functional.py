@@ -78,6 +78,32 @@ def _operand_code(a, b, config):
     return flags
 
 
+def _native_product(a, b, simulator, *, vector_offset=0, out=None, before_sync=None):
+    """A rank-two product through the one-call native path (``AnalogMatrix._native_mm``)
+    when ``b`` already has a program that this call would reprogram in place and the
+    operands are contiguous kernel dtypes; None otherwise (the caller then takes the
+    step-by-step path, which gives the same result)."""
+    if torch.is_grad_enabled() and (a.requires_grad or b.requires_grad):
+        raise NotImplementedError(
+            "memfast_b200 simulates the analog forward only; detach operands or use torch.no_grad()"
+        )
+    config = simulator.config
+    if (a.dtype not in _lib.DTYPES or b.dtype != a.dtype or not a.is_contiguous() or not b.is_contiguous()
+            or not config.weight_signed):
+        return None
+    matrix = simulator._in_place_program(b)
+    scale_dtype = torch.float64 if config.wide else torch.float32
+    if (matrix is None or not matrix.packed.is_contiguous() or not matrix.weight_scale.is_contiguous()
+            or matrix.weight_scale.dtype != scale_dtype):
+        return None
+    a_narrows = a.dtype == torch.float64 and compute_dtype(config, config.activation_bits) == torch.float32
+    b_narrows = b.dtype == torch.float64 and compute_dtype(config, config.weight_bits) == torch.float32
+    with torch.no_grad():
+        return matrix._native_mm(a.detach(), b.detach(), a_narrow=3 if a_narrows else 0,
+                                 b_narrow=3 if b_narrows else 0, input_errors=OPERAND_ERRORS,
+                                 vector_offset=vector_offset, out=out, before_sync=before_sync)
+
+
 def _resolve_simulator(a, simulator, config, mode, cache_dir):
     """The simulator a call runs on: the caller's (whose settings the explicit options
     must agree with) or, without one, a new simulator for this call."""
@@ -212,7 +238,11 @@ def _matmul(a, b, *, simulator, config, mode, cache_dir, out):
     if (a.ndim == 2 and b.ndim == 2 and out is None and a.numel() and b.numel()
             and not torch.is_autocast_enabled(a.device.type)):
         # Plain rank-two product outside autocast: one programmed product, no batch
-        # bookkeeping (the general path below gives the same result).
+        # bookkeeping (the general path below gives the same result); a matrix
+        # programmed before goes through the one-call native path.
+        native = _native_product(a, b, engine)
+        if native is not None:
+            return native
         return _product(a, b, engine, None, operand_code=_operand_code(a, b, engine.config))
     with torch.autocast(device_type=a.device.type, enabled=False):
         if a.numel() == 0 or b.numel() == 0 or 0 in shape:

@@ -42,13 +42,18 @@ _SCRATCH = {}
 
 def _workspace(config, is_weight, rows, cols, device):
     need = ct_size(config, is_weight, rows, cols)
+    return scratch(need, device), need
+
+
+def scratch(need, device):
+    """The current stream's quantiser scratch, at least ``need`` bytes."""
     key = (device.index, _lib.stream_of(device).value)
     buffer = _SCRATCH.get(key)
     if buffer is None or buffer.numel() < need:
         if len(_SCRATCH) >= 16:
             _SCRATCH.pop(next(iter(_SCRATCH)))
         buffer = _SCRATCH[key] = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
-    return buffer, need
+    return buffer
 
 
 @functools.lru_cache(maxsize=1024)

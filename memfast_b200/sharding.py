@@ -25,7 +25,7 @@ ranks rerun together exactly when the single-device layer would.
 import torch
 import torch.distributed as dist
 
-from .functional import OPERAND_ERRORS, _operand_code, _operand_types
+from .functional import OPERAND_ERRORS, _native_product, _operand_code, _operand_types
 from .simulator import AnalogMatrix, Simulator
 
 
@@ -70,7 +70,11 @@ def _check_row_shard(a_local, b, simulator, row_offset):
 
 def _row_product(a_local, b, simulator, row_offset, out, before_sync=None):
     """The rows' product with the operand checks read in the call's one synchronisation
-    (functional.mm's deferred check: same errors, same order)."""
+    (functional.mm's deferred check: same errors, same order); after the first call
+    on ``b``, one native call enqueues the whole product (``_native_product``)."""
+    native = _native_product(a_local, b, simulator, vector_offset=row_offset, out=out, before_sync=before_sync)
+    if native is not None:
+        return native
     code = _operand_code(a_local, b, simulator.config)
     matrix = simulator._matrix_for(b, checked=True, rows=a_local.shape[0])
     with torch.no_grad():

@@ -29,7 +29,7 @@ from pathlib import Path
 import torch
 from torch import nn
 
-from . import _lib, tuning
+from . import _lib, quantization, tuning
 from .config import Config
 from .quantization import (
     check_finite,
@@ -96,17 +96,23 @@ def check_device_error():
 _STAGED_WORDS = {}
 
 
-def stage_device_error(device):
-    """Enqueue a copy of the device error word into a pinned host word (per device and
-    stream) and return that word: read it after the caller's next synchronisation of
-    the current stream, and call check_device_error() when it is non-zero."""
-    stream = _lib.stream_of(device)
+def _staged_word(device, stream):
+    """The pinned host word receiving the device error word for (device, stream)."""
     key = (device.index, stream.value)
     word = _STAGED_WORDS.get(key)
     if word is None:
         if len(_STAGED_WORDS) >= 64:
             _STAGED_WORDS.pop(next(iter(_STAGED_WORDS)))
         word = _STAGED_WORDS[key] = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    return word
+
+
+def stage_device_error(device):
+    """Enqueue a copy of the device error word into a pinned host word (per device and
+    stream) and return that word: read it after the caller's next synchronisation of
+    the current stream, and call check_device_error() when it is non-zero."""
+    stream = _lib.stream_of(device)
+    word = _staged_word(device, stream)
     _lib.check(_lib.load().mf_stage_device_error(word.data_ptr(), stream), "mf_stage_device_error")
     return word
 
@@ -234,8 +240,7 @@ class Simulator:
         ``matrix`` to program from (the cache follows the caller's tensor).
         """
         cached, same_layout = self._programs.get(matrix)
-        reusable = (cached is not None and same_layout and cached.packed.device == self.device
-                    and (cached.config is self.config or cached.config == self.config))
+        reusable = self._reusable(cached, same_layout)
         source = matrix if program is None else program
         if self.mode == "default" and reusable and cached.zero_correction is None and cached.input_scale is None:
             cached._reprogram(source.T, checked, rows)
@@ -249,6 +254,20 @@ class Simulator:
             fresh._event = cached._event
         self._programs.put(matrix, fresh)
         return fresh
+
+    def _reusable(self, cached, same_layout):
+        return (cached is not None and same_layout and cached.packed.device == self.device
+                and (cached.config is self.config or cached.config == self.config))
+
+    def _in_place_program(self, matrix):
+        """The cached program that ``_matrix_for(matrix)`` would reprogram in place
+        (default mode, same layout, no imported zero points or fixed input scale), or
+        None when that call would build a new program."""
+        cached, same_layout = self._programs.get(matrix)
+        if (self.mode == "default" and self._reusable(cached, same_layout) and cached.zero_correction is None
+                and cached.input_scale is None):
+            return cached
+        return None
 
     def _select(self, matrix, x, q, xscale, event):
         """Tuned-mode schedule for ``matrix`` on inputs shaped like ``x`` (tuning.Search)."""
@@ -327,6 +346,61 @@ def _import_codes(codes, scales, zero_points, config, device):
     return packed, scale, correction
 
 
+class _NativePlan:
+    """Buffers and ctypes arguments of ``AnalogMatrix._native_mm`` for one (vectors,
+    stream) pair of one program: input codes and scales, check flags, quantiser
+    scratch, the product workspace whose K-major prefix programming writes, and the
+    mf_mm argument structures.  Valid while the program's buffers and this stream's
+    workspace entry are the ones it was made for."""
+
+    def __init__(self, matrix, a, b, stream):
+        config, device = matrix.config, a.device
+        n, k = a.shape
+        o = b.shape[1]
+        schedule = default_schedule(config)
+        m = matrix.packed.shape[0]
+        self.k, self.stream = k, stream.value
+        self.workspace_bytes = matrix._workspace_size(n, schedule)
+        kmajor_bytes = matrix._kmajor_size(m, schedule)
+        entry = matrix._workspaces.get(stream.value)
+        matrix._workspaces = {} if entry is None else {stream.value: entry}
+        if kmajor_bytes and self.workspace_bytes - kmajor_bytes <= _KEPT_SCRATCH_BYTES:
+            if entry is None or entry[0].numel() < self.workspace_bytes:
+                entry = matrix._workspaces[stream.value] = [
+                    torch.empty(self.workspace_bytes, dtype=torch.uint8, device=device), False]
+            self.entry, self.workspace = entry, entry[0]
+        else:
+            self.entry = self.workspace = None
+        matrix._kmajor_bytes = kmajor_bytes
+        rows = config.array_size[0]
+        self.out_dtype = torch.float64 if config.wide else torch.float32
+        self.codes = torch.empty((n, m, rows), dtype=torch.int64 if config.wide_codes else torch.uint8,
+                                 device=device)
+        self.xscale = torch.empty((n, m * config.reads_per_array), dtype=self.out_dtype, device=device)
+        self.flags = torch.empty(2, dtype=torch.int32, device=device)
+        quantize_need = quantization.ct_size(config, False, n, k)
+        program_need = quantization.ct_size(config, True, o, k)
+        # One scratch serves both quantisers: the call runs them one after the other.
+        self.scratch = quantization.scratch(max(quantize_need, program_need), device)
+        self.packed_ptr, self.wscale_ptr = matrix.packed.data_ptr(), matrix.weight_scale.data_ptr()
+        self.buffers = _lib.MFMMBuffers(
+            self.codes.data_ptr(), self.xscale.data_ptr(), self.packed_ptr, self.wscale_ptr, None,
+            self.flags.data_ptr(), self.scratch.data_ptr(), quantize_need, self.scratch.data_ptr(), program_need,
+            None if self.workspace is None else self.workspace.data_ptr(), self.workspace_bytes)
+        self.buffers_ref = ct.byref(self.buffers)
+        self.config = _lib.native_config(config)
+        self._schedule = _lib.schedule(**schedule)
+        self.schedule = ct.byref(self._schedule)
+        self.seed = matrix.seed & 0xFFFFFFFF
+        self.word = _staged_word(device, stream)
+        self.mm = _lib.load().mf_mm
+
+    def valid(self, matrix, stream):
+        return (matrix.packed.data_ptr() == self.packed_ptr and matrix.weight_scale.data_ptr() == self.wscale_ptr
+                and (self.entry is None or (matrix._workspaces.get(stream) is self.entry
+                                            and self.entry[0] is self.workspace)))
+
+
 class AnalogMatrix(nn.Module):
     """Programmed matrix with optional digital zero-point compensation."""
 
@@ -341,6 +415,8 @@ class AnalogMatrix(nn.Module):
         # Workspaces of the tensor-core kernels, one per stream, reused across calls:
         # each starts with the K-major copy of the packed codes (valid while flagged).
         self._workspaces, self._kmajor_bytes = {}, 0
+        # One-call product plans (``_native_mm``), per (vectors, stream).
+        self._native_plans = {}
         # Tensor-parallel column shard (sharding.shard_columns); None = all columns.
         self._column_shard = None
         self.simulator, self.config, self.name = simulator, config, name
@@ -533,7 +609,7 @@ class AnalogMatrix(nn.Module):
         return _workspace_bytes(self.config, n, m, self.p, tuple(sorted(schedule.items())))
 
     def _execute(self, q, xscale, schedule, event, stable=False, *, vector_offset=0, input_flag=None,
-                 input_errors=None, tiles=None, agree=None, output=None, before_sync=None):
+                 input_errors=None, tiles=None, agree=None, output=None, before_sync=None, launched=None):
         """One fused device call: analog partials, scales, read sums and bias.
 
         ``input_flag``: device int32 set by a quantiser that checks finiteness on the
@@ -547,15 +623,20 @@ class AnalogMatrix(nn.Module):
         ``before_sync(output, flags)``: work to enqueue on the stream after the product
         and its checks but before the host reads the flags (collectives of a sharded
         product, which may also combine the flags of every rank); it runs again for
-        the FP64 rerun."""
-        output = self._launch(q, xscale, schedule, event, stable=stable, vector_offset=vector_offset, tiles=tiles,
-                              output=output)
-        # One host synchronisation decides both the FP64 rerun of a narrow config
-        # (simulator.py:614-615) and, in forward, the non-finite error.
-        # flags: [input error code, output non-finite]; one device-to-host read.
-        flags = input_flag if input_flag is not None else torch.zeros(2, dtype=torch.int32, device=q.device)
-        check_finite(output, flags[1:2], 1)
-        staged = stage_device_error(q.device)
+        the FP64 rerun.  ``launched``: (output, flags, staged error word) of a product
+        already enqueued with its checks (``_native_mm``); only the synchronisation and
+        what follows it remain."""
+        if launched is None:
+            output = self._launch(q, xscale, schedule, event, stable=stable, vector_offset=vector_offset,
+                                  tiles=tiles, output=output)
+            # One host synchronisation decides both the FP64 rerun of a narrow config
+            # (simulator.py:614-615) and, in forward, the non-finite error.
+            # flags: [input error code, output non-finite]; one device-to-host read.
+            flags = input_flag if input_flag is not None else torch.zeros(2, dtype=torch.int32, device=q.device)
+            check_finite(output, flags[1:2], 1)
+            staged = stage_device_error(q.device)
+        else:
+            output, flags, staged = launched
         if before_sync is not None:
             before_sync(output, flags)
         bad, nonfinite = flags.tolist()
@@ -657,6 +738,47 @@ class AnalogMatrix(nn.Module):
                 output += self.bias[c0:c1]
         return output
 
+    def _native_mm(self, a, b, *, a_narrow=0, b_narrow=0, input_errors=None, vector_offset=0, out=None,
+                   before_sync=None):
+        """``mm(a, b)`` on this default-mode program of ``b`` in one ``mf_mm`` call: the
+        operand checks, ``b`` reprogrammed in place (with the K-major copy the kernel
+        reads), ``a`` quantised, the fused product and the output check are enqueued
+        together, as ``_matrix_for`` + ``_forward`` enqueue them one by one; the
+        synchronisation, errors, FP64 rerun and read event follow as in ``_product``.
+        ``a``/``b``: contiguous [n, K] / [K, O] of one dtype; ``a_narrow``/``b_narrow``:
+        the narrowing-check codes of ``functional._operand_code``.  The buffers and
+        argument structures of a (vectors, stream) pair are kept in a plan, so a
+        repeated call only fills in the operand and output addresses."""
+        n, o = a.shape[0], b.shape[1]
+        stream = _lib.stream_of(a.device)
+        plan = self._native_plans.get((n, stream.value))
+        if plan is None or not plan.valid(self, stream.value):
+            plan = _NativePlan(self, a, b, stream)
+            if len(self._native_plans) >= 4:
+                self._native_plans.pop(next(iter(self._native_plans)))
+            self._native_plans[(n, stream.value)] = plan
+        elif len(self._workspaces) > 1:
+            # Programming rewrites the codes: K-major copies kept for other streams go stale.
+            self._workspaces = {stream.value: plan.entry}
+        if self._event >= 2**63:
+            raise OverflowError("read-event counter exhausted")
+        direct = out is not None and out.dtype == plan.out_dtype and out.shape == (n, o) and out.is_contiguous()
+        output = out if direct else torch.empty((n, o), dtype=plan.out_dtype, device=a.device)
+        workspace = plan.workspace
+        if workspace is None:
+            # Large per-call scratch (the conductance operand): from the allocator each call.
+            workspace = torch.empty(max(plan.workspace_bytes, 1), dtype=torch.uint8, device=a.device)
+            plan.buffers.mm_workspace = workspace.data_ptr()
+        plan.buffers.out = output.data_ptr()
+        _lib.check(plan.mm(plan.config, plan.schedule, a.data_ptr(), b.data_ptr(), _lib.DTYPES[a.dtype],
+                           n, plan.k, o, a_narrow, b_narrow, plan.buffers_ref, plan.seed, self._event,
+                           vector_offset, plan.word.data_ptr(), stream), "mf_mm")
+        if plan.entry is not None:
+            plan.entry[1] = True
+        return self._product(plan.codes, plan.xscale, a.shape, a.dtype, vector_offset=vector_offset,
+                             input_errors=input_errors, out=out, before_sync=before_sync,
+                             launched=(output, plan.flags, plan.word))
+
     @torch.no_grad()
     def forward(self, x):
         shard = self._column_shard
@@ -690,7 +812,7 @@ class AnalogMatrix(nn.Module):
         return output.reshape(*shape[:-1], width)
 
     def _product(self, q, xscale, shape, dtype, *, vector_offset=0, input_flag=None, input_errors=None,
-                 tiles=None, agree=None, out=None, before_sync=None):
+                 tiles=None, agree=None, out=None, before_sync=None, launched=None):
         """forward() from quantised codes on (simulator.py:631-646): schedule, product,
         non-finite checks, ``dtype`` result, read event.  ``shape``/``dtype`` describe
         the caller's input (tuned-mode key); ``input_flag`` as in ``_execute``."""
@@ -709,7 +831,7 @@ class AnalogMatrix(nn.Module):
             else None
         output = self._execute(q, xscale, schedule, event, vector_offset=vector_offset, input_flag=input_flag,
                                input_errors=input_errors, tiles=tiles, agree=agree, output=direct,
-                               before_sync=before_sync)
+                               before_sync=before_sync, launched=launched)
         finite = self._finite and (output.dtype == dtype or finite_flags(output, dtypes=[dtype])[0])
         if agree is not None:
             finite = agree(finite)

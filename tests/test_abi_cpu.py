@@ -121,3 +121,24 @@ def test_schedule_grid_lists_each_execution_once():
                    nonidealities=Nonidealities(write_variation=0.02))
     paths = [resolve(noisy, s, 64, 4, 4)[0] for s in schedule_grid(noisy, 64, 4, 4)]
     assert paths.count("tc_currents") == 2 and paths.count("simt_currents") == 3   # arrays 1, 2, 4
+
+
+def test_mf_mm_validates_on_the_host():
+    """mf_mm refuses missing buffers and undersized workspaces before enqueuing anything."""
+    from memfast_b200 import Config, Nonidealities, _lib
+
+    config = Config(array_size=(128, 128), rows_per_read=32, weight_quant_gran=(32, 1), input_quant_gran=(1, 32),
+                    input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2), adc_bits=(6, 7, 7, 8, 8),
+                    nonidealities=Nonidealities(write_variation=0.0))
+    lib = _lib.load()
+    cfg = _lib.native_config(config)
+    sched = _lib.schedule()
+    fake = ct.c_void_p(256)
+    buffers = _lib.MFMMBuffers(fake, fake, fake, fake, fake, fake, fake, 1, fake, 1, fake, 1)
+    args = (ct.byref(cfg), ct.byref(sched), fake, fake, 0, 64, 256, 128, 0, 0)
+    assert lib.mf_mm(*args, None, 0, 0, 0, None, None) == _lib.MF_ERR_INVALID
+    missing = _lib.MFMMBuffers.from_buffer_copy(buffers)
+    missing.flags = None
+    assert lib.mf_mm(*args, ct.byref(missing), 0, 0, 0, None, None) == _lib.MF_ERR_INVALID
+    assert lib.mf_mm(*args, ct.byref(buffers), 0, 0, 0, None, None) == _lib.MF_ERR_RESOURCE
+    assert "workspaces too small" in _lib.last_error()
