@@ -51,6 +51,8 @@ EFFECTS = {
     "write": dict(write_variation=0.02),
     "shared": dict(write_variation=0.02, read_variation=0.02),
     "noisy": dict(write_variation=0.02, read_variation=0.02, voltage_variation=0.02),
+    # Read noise drawn per (input slice, weight slice, cell) instead of per cell.
+    "pair": dict(write_variation=0.02, read_variation=0.02, read_mode="slice_pair"),
 }
 
 
@@ -117,7 +119,8 @@ def parse(argv=None):
     p.add_argument("--effects", choices=sorted(EFFECTS), default="ideal",
                    help="device effects of the configs[1] sweep: ideal (the headline), write "
                         "(write variation 0.02), shared (write + shared read variation 0.02), "
-                        "noisy (write + read + voltage variation 0.02, BASELINE's noisy run)")
+                        "noisy (write + read + voltage variation 0.02, BASELINE's noisy run), pair (write + "
+                        "read variation 0.02 drawn per slice pair)")
     return p.parse_args(argv)
 
 
@@ -162,7 +165,8 @@ def effects_label(effects):
     if effects == "ideal":
         return "ideal"
     return "nonideal: " + ", ".join(f"{name.replace('_variation', '')} {value}"
-                                    for name, value in EFFECTS[effects].items())
+                                    for name, value in EFFECTS[effects].items() if name != "read_mode") + \
+        (f", read mode {EFFECTS[effects]['read_mode']}" if "read_mode" in EFFECTS[effects] else "")
 
 
 def workload(args, world, spec=None):

@@ -26,11 +26,13 @@
 // exact digit dot D and the epilogue's count is min(D, m), bit-exact wherever
 // exact_integer_counts holds.
 //
-// Scope: FP32 currents and epilogue (not Config.wide / precise_currents), no
-// voltage noise, read noise only in the shared mode (it is folded into G' per
-// read event by b_operand_kernel), input digits of at most 3 bits, 32- or
-// 64-row reads, at most 256 reads per output.  Everything else runs on the SIMT
-// kernels in generic.cu.
+// Scope: FP32 currents and epilogue (not Config.wide / precise_currents), input
+// digits of at most 3 bits, 32- or 64-row reads, at most 256 reads per output.
+// Read noise of the shared mode is folded into G' per read event by
+// b_operand_kernel; in the slice-pair mode (32-row reads, no voltage noise) it
+// writes one G' operand per input slice (PAIRB instantiations), whose draws are
+// keyed by cell * A + a (reference.py:88-91).  Everything else (the output read
+// mode among it) runs on the SIMT kernels in generic.cu.
 //
 // Per CTA: 128 vectors x BC = NJB * BN output columns.  Per read:
 //   warp 0      TMA: the read's activation codes [128 x KR] and, for every job,
@@ -82,7 +84,9 @@ constexpr int MAXS = 8;          // slices per operand in the tables below
 // MMA's tile layout.  A stage then holds those tiles instead of the code tile,
 // no digit planes are built, and each job issues the MMAs of both parts into the
 // same accumulators.
-template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool VOLT = false>
+// PAIRB (slice-pair read noise): G' differs per input slice, so a stage holds the
+// B tiles of every input slice (NIN sets) and job (a, block) reads set a.
+template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool VOLT = false, bool PAIRB = false>
 struct Geo {
     static constexpr int KS = KR / 16;                     // MMA K steps per read
     static constexpr int EC = BN / 4;                      // columns per epilogue thread per block
@@ -98,7 +102,8 @@ struct Geo {
     static constexpr int AT = BM * 32;                     // one [128 x 16] FP16 tile
     static constexpr int XB = VOLT ? NIN * 2 * KS * AT : BM * KR;   // voltage tiles, or the code tile
     static constexpr int BT = BROWS * 32;                  // one [BROWS x 16] FP16 tile (both halves)
-    static constexpr int BB = NJB * KS * BT;
+    static constexpr int BSETS = PAIRB ? NIN : 1;           // B tile sets per stage
+    static constexpr int BB = BSETS * NJB * KS * BT;
     static constexpr int STAGE = (XB + BB + 1023) / 1024 * 1024;
     static constexpr int AB = VOLT ? 0 : NIN * KS * AT;    // one set of digit planes
     // Digit planes double-buffered (transform of read i+1 overlaps the MMAs of read i) when they fit.
@@ -113,6 +118,7 @@ struct Geo {
     static_assert(U >= 1 && U * UNIT <= 512 && NT <= 256, "accumulators exceed TMEM or the MMA's N");
     static_assert(BN % 4 == 0 && KR % 16 == 0 && NIN <= MAXS && NW <= MAXS, "unsupported shape");
     static_assert(!VOLT || SPLIT, "voltage tiles pair with split conductance halves");
+    static_assert(!PAIRB || (SPLIT && !VOLT), "per-slice conductance tiles: split halves, no voltage tiles");
     static_assert(VALS % 2 == 0, "TMEM loads start on even columns");
     static_assert(BYTES + 1024 <= 232448, "exceeds the 227 KB shared-memory limit");
 };
@@ -140,6 +146,7 @@ struct Args {
     float ffactor[MAXS][MAXS];  // s_a * s_w as FP32 (float totals of the digit mode)
     int raster;              // 0: blockIdx.x walks vector blocks; 1: blockIdx.x walks column blocks
     int n_pad;               // VOLT: rows of one (slice, part) plane of the voltage operand
+    int gblocks;             // PAIRB: column blocks of one input slice's G' operand
 };
 
 __device__ __forceinline__ float mul_sat(float a, float b) {
@@ -176,11 +183,11 @@ __device__ __forceinline__ void tmem_loaded(uint32_t* v) {
 // FSUM (digit mode, reconstruction bound below 2^24): the count min(D, max_w) and
 // the total are FP32 integers, summed exactly with one FMNMX and one FFMA per event.
 template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool NONLINEAR, bool FSUM = false,
-          bool VOLT = false>
+          bool VOLT = false, bool PAIRB = false>
 __global__ void __launch_bounds__(THREADS, 1)
     tc_physical_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_g,
                        const __grid_constant__ Args args) {
-    using G = Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT>;
+    using G = Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT, PAIRB>;
     // The digit mode sums counts in FP32, exact only while every accumulator read from
     // TMEM is the integer digit dot itself: one FP16 part, no split halves.
     static_assert(!FSUM || (!SPLIT && NPART == 1), "FSUM needs exact integer digit dots (one FP16 part)");
@@ -258,11 +265,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                         tma_load_2d(stage, &map_x, i * KR, (int)n0, &full[st]);
                     }
 #pragma unroll 1
-                    for (int cb = 0; cb < NJB; ++cb)
+                    for (int set = 0; set < G::BSETS; ++set)
+#pragma unroll 1
+                        for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
-                        for (int ks = 0; ks < G::KS; ++ks)
-                            tma_load_2d(stage + G::XB + (cb * G::KS + ks) * G::BT, &map_g, i * KR + ks * 16,
-                                        (cb0 + cb) * G::BROWS, &full[st]);
+                            for (int ks = 0; ks < G::KS; ++ks)
+                                tma_load_2d(stage + G::XB + ((set * NJB + cb) * G::KS + ks) * G::BT, &map_g,
+                                            i * KR + ks * 16, (set * args.gblocks + cb0 + cb) * G::BROWS,
+                                            &full[st]);
                     issued = i + 1;
                 }
                 // Every issued load lands before the CTA may exit.
@@ -288,10 +298,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint8_t* planes = VOLT ? base + st * G::STAGE : a_planes + ab * G::AB;
 #pragma unroll 1
                     for (int cb = 0; cb < NJB && ok; ++cb) {
-                        // Descriptors advance by (byte offset >> 4) in their address field.
-                        const uint64_t db = desc_sw32(btiles + cb * G::KS * G::BT);
 #pragma unroll 1
                         for (int a = 0; a < NIN; ++a, ++job) {
+                            // Descriptors advance by (byte offset >> 4) in their address field.
+                            const uint64_t db = desc_sw32(btiles + ((PAIRB ? a * NJB : 0) + cb) * G::KS * G::BT);
                             const int unit = job % G::U;
                             if (!mbar_wait(&unit_empty[unit], (uint32_t)((job / G::U) & 1) ^ 1u, abort_flag, err,
                                            44)) {
@@ -537,10 +547,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 constexpr int KC = 64;           // K rows per CTA of the operand builder
 constexpr int MAXBN = 32;        // columns per block, at most
 
+//   pair_slices > 0 (slice-pair read noise): one operand per input slice a, set a
+//   starting at row a * blocks * brows, its G scaled by exp(sigma_r z) with z the
+//   normal of stream 20 at cell * pair_slices + a (reference.py:88-91).
 __global__ void __launch_bounds__(256) b_operand_kernel(Layout L, Physics P, const uint8_t* packed, int p,
                                                         int col_begin, int blocks, int bn, int nwp, int brows,
                                                         int pstride, int parts, int kc, long long kpad, uint32_t seed,
-                                                        uint64_t event, float scale, int fixed, __half* gs) {
+                                                        uint64_t event, float scale, int fixed, int pair_slices,
+                                                        __half* gs) {
     __shared__ uint8_t codes[KC][MAXBN];
     for (int block = blockIdx.y; block < blocks; block += gridDim.y) {
         const long long k0 = (long long)blockIdx.x * kc;
@@ -558,38 +572,51 @@ __global__ void __launch_bounds__(256) b_operand_kernel(Layout L, Physics P, con
         const uint64_t read_seed = event_seed(seed, event);
         const float low = (float)P.low;
         const int np = nwp * bn;
+        const int sets = pair_slices > 0 ? pair_slices : 1;
+        const long long set_stride = (long long)blocks * brows * kpad;   // elements of one input slice's operand
         __half* out = gs + (long long)block * brows * kpad + k0;
         for (int idx = threadIdx.x; idx < pstride * kc; idx += blockDim.x) {
             const int prow = idx / kc, kk = idx - prow * kc;
             const int jj = prow / nwp, w = prow - jj * nwp;
-            __half hi = __float2half_rn(0.0f), lo = hi;
-            if (prow < np && w < L.n_w) {
-                const long long state = ((long long)codes[kk][jj] >> L.w_shift[w]) & L.w_mask[w];
-                if (parts == 1) {
-                    hi = __float2half_rn((float)state);
-                } else {
-                    const long long address = (((arr * p + tile) * L.n_w + w) * L.R + r0 + kk) * L.C + c0 + jj;
-                    const float g = restored_conductance_f32(P, state, L.w_mask[w], address, seed, read_seed);
-                    const float x = __fmul_rn(__fadd_rn(g, -low), scale);
-                    if (fixed) {
-                        const float X = rintf(x);
-                        const float H = rintf(__fmul_rn(X, 1.0f / 2048.0f));
-                        hi = __float2half_rn(H);
-                        lo = __float2half_rn(__fsub_rn(X, __fmul_rn(H, 2048.0f)));
+            const bool cell = prow < np && w < L.n_w;
+            const long long state = cell ? ((long long)codes[kk][jj] >> L.w_shift[w]) & L.w_mask[w] : 0;
+            const long long address = (((arr * p + tile) * L.n_w + w) * L.R + r0 + kk) * L.C + c0 + jj;
+            const float g = cell && parts != 1 ? restored_conductance_f32(P, state, L.w_mask[w], address, seed,
+                                                                          read_seed)
+                                               : 0.0f;
+            for (int set = 0; set < sets; ++set) {
+                __half hi = __float2half_rn(0.0f), lo = hi;
+                if (cell) {
+                    if (parts == 1) {
+                        hi = __float2half_rn((float)state);
                     } else {
-                        hi = __float2half_rn(x);
-                        lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
+                        float gs_a = g;
+                        if (pair_slices > 0)
+                            gs_a = __fmul_rn(g, expf(__fmul_rn((float)P.read_var,
+                                                               rng_normal(address * pair_slices + set, read_seed, 20))));
+                        const float x = __fmul_rn(__fadd_rn(gs_a, -low), scale);
+                        if (fixed) {
+                            const float X = rintf(x);
+                            const float H = rintf(__fmul_rn(X, 1.0f / 2048.0f));
+                            hi = __float2half_rn(H);
+                            lo = __float2half_rn(__fsub_rn(X, __fmul_rn(H, 2048.0f)));
+                        } else {
+                            hi = __float2half_rn(x);
+                            lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
+                        }
                     }
                 }
+                __half* dst = out + set * set_stride;
+                dst[(long long)prow * kpad + kk] = hi;
+                if (parts == 2) dst[(long long)(pstride + prow) * kpad + kk] = lo;
             }
-            out[(long long)prow * kpad + kk] = hi;
-            if (parts == 2) out[(long long)(pstride + prow) * kpad + kk] = lo;
         }
         // Rows past the parts (MMA padding) are zero.
-        for (int idx = parts * pstride * kc + threadIdx.x; idx < brows * kc; idx += blockDim.x) {
-            const int row = idx / kc, kk = idx - row * kc;
-            out[(long long)row * kpad + kk] = __float2half_rn(0.0f);
-        }
+        for (int set = 0; set < sets; ++set)
+            for (int idx = parts * pstride * kc + threadIdx.x; idx < brows * kc; idx += blockDim.x) {
+                const int row = idx / kc, kk = idx - row * kc;
+                out[set * set_stride + (long long)row * kpad + kk] = __float2half_rn(0.0f);
+            }
         __syncthreads();   // the next block's codes overwrite the staging tile
     }
 }
@@ -638,10 +665,15 @@ constexpr Shape kShapes[] = {{5, 5, 16, 2, 1}, {3, 3, 32, 1, 1}, {8, 8, 16, 1, 0
 // Ideal devices: one FP16 part (the digits), so a block can hold twice the columns.
 constexpr Shape kDigitShapes[] = {{5, 5, 32, 1, 0}, {3, 3, 32, 2, 0}, {8, 8, 16, 1, 0}, {4, 4, 32, 1, 0}};
 
+// Slice-pair read noise: one G' operand per input slice (PAIRB instantiations).
+bool pair_mode(const mf_config& c) { return !c.ideal && c.read_var != 0 && c.read_mode == 1; }
+
 bool shape_of(const mf_config& c, Shape& s) {
     for (const Shape& k : c.ideal ? kDigitShapes : kShapes)
         if (k.nin == c.n_in && k.nw == c.n_w) {
             s = k;
+            // A stage holds every input slice's tiles: one column block per CTA.
+            if (pair_mode(c)) s.njb = 1;
             return true;
         }
     return false;
@@ -691,7 +723,8 @@ static bool digits_eligible(const mf_config& c, int32_t m) {
 bool tc_physical_eligible(const mf_config& c, int32_t m) {
     if (c.ideal) return digits_eligible(c, m);
     if (c.wide || c.wide_codes || c.precise_currents) return false;
-    if (c.read_var != 0 && c.read_mode != 0) return false;
+    // The output read mode draws noise per ADC event from second moments (SIMT only).
+    if (c.read_var != 0 && c.read_mode == 2) return false;
     if (c.write_var + c.read_var > 1.0) return false;
     if (c.read_rows != 32 && c.read_rows != 64) return false;
     tcp::Shape s;
@@ -699,6 +732,9 @@ bool tc_physical_eligible(const mf_config& c, int32_t m) {
     // Voltage noise: the voltage tiles of a stage fit shared memory for 32-row reads of
     // the split-halves shapes.
     if (c.volt_var != 0 && (c.read_rows != 32 || !s.split)) return false;
+    // Slice-pair read noise: every input slice's G' tiles in a stage, which fits for
+    // 32-row reads of the split-halves shapes without voltage tiles.
+    if (tcp::pair_mode(c) && (c.read_rows != 32 || !s.split || c.volt_var != 0)) return false;
     if (c.rows % c.read_rows || c.cols % s.bn) return false;
     for (int i = 0; i < c.n_in; ++i)
         if (c.in_mask[i] > 7) return false;
@@ -716,7 +752,8 @@ static size_t b_operand_bytes(const mf_config& c, const tcp::Shape& s, int32_t m
     const long long blocks = (long long)tiles * c.cols / s.bn;
     int brows = 0, pstride = 0;
     tcp::rows_of(s, tcp::parts_of(c), brows, pstride);
-    return ((size_t)blocks * brows * (size_t)m * c.rows * sizeof(__half) + 255) / 256 * 256;
+    const size_t sets = tcp::pair_mode(c) ? (size_t)c.n_in : 1;
+    return (sets * blocks * brows * (size_t)m * c.rows * sizeof(__half) + 255) / 256 * 256;
 }
 
 // Rows of one (slice, part) plane of the voltage operand.
@@ -732,12 +769,12 @@ size_t tc_physical_workspace_bytes(const mf_config& c, int64_t n, int32_t m, int
 }
 
 template <int NIN, int NW, int BN, int NJB, bool SPLIT, int NPART, int KR, bool NL, bool FSUM = false,
-          bool VOLT = false>
+          bool VOLT = false, bool PAIRB = false>
 static mf_status launch_tcp(const CUtensorMap& mx, const CUtensorMap& mg, const tcp::Args& args, dim3 grid,
                             cudaStream_t st) {
-    using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT>;
+    using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT, PAIRB>;
     const size_t smem = G::BYTES + 1024;
-    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL, FSUM, VOLT>;
+    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL, FSUM, VOLT, PAIRB>;
     int regs = 0;
     {
         const mf_status r = kernel_setup(reinterpret_cast<const void*>(kern), smem, &regs);
@@ -760,6 +797,13 @@ static mf_status dispatch_tcp(const mf_config& c, const CUtensorMap& mx, const C
                               const tcp::Args& args, dim3 grid, cudaStream_t st) {
     const bool nl = c.nonlinear != 0;
     if constexpr (SPLIT) {
+        // Slice-pair read noise (32-row reads, no voltage noise, tc_physical_eligible): one
+        // column block per CTA, every input slice's G' tiles per stage.
+        if (tcp::pair_mode(c))
+            return nl ? launch_tcp<NIN, NW, BN, 1, true, tcp::PARTS, 32, true, false, false, true>(mx, mg, args, grid,
+                                                                                                   st)
+                      : launch_tcp<NIN, NW, BN, 1, true, tcp::PARTS, 32, false, false, false, true>(mx, mg, args,
+                                                                                                    grid, st);
         // Voltage noise (32-row reads only, tc_physical_eligible): voltage tiles as the A operand.
         if (c.volt_var != 0)
             return nl ? launch_tcp<NIN, NW, BN, NJB, true, tcp::PARTS, 32, true, false, true>(mx, mg, args, grid, st)
@@ -819,7 +863,7 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
                                                    static_cast<const uint8_t*>(a.packed), a.p,
                                                    a.tile_begin * c.cols, blocks, shape.bn, shape.nw, brows, pstride,
                                                    tcp::parts_of(c), kc, K, a.seed, a.event, scale,
-                                                   shape.split, gs);
+                                                   shape.split, tcp::pair_mode(c) ? c.n_in : 0, gs);
         MF_LAUNCH_CHECK("b_operand_kernel");
     }
     CUtensorMap mx, mg;
@@ -844,8 +888,9 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
         r = tc_make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n,
                         (uint64_t)K, (uint32_t)c.read_rows, tcp::BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     }
+    const long long sets = tcp::pair_mode(c) ? c.n_in : 1;
     if (!r) r = tc_make_map(&mg, gs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K,
-                            (uint64_t)blocks * brows, (uint64_t)K, 16, (uint32_t)brows,
+                            (uint64_t)(sets * blocks * brows), (uint64_t)K, 16, (uint32_t)brows,
                             CU_TENSOR_MAP_SWIZZLE_32B);
     if (r) return r;
     tcp::Args args{};
@@ -864,6 +909,7 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     args.col_begin = a.tile_begin * c.cols;
     args.col_end = a.tile_end * c.cols;
     args.n_pad = (int)n_pad;
+    args.gblocks = blocks;
     // FP16 high bytes of the digits 0..7 (1.0 = 0x3C00, 2.0 = 0x4000, 3.0 = 0x4200, ...).
     const uint8_t hi[8] = {0x00, 0x3C, 0x40, 0x42, 0x44, 0x45, 0x46, 0x47};
     args.lut_lo = hi[0] | hi[1] << 8 | hi[2] << 16 | (uint32_t)hi[3] << 24;

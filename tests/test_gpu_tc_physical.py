@@ -49,6 +49,14 @@ CONFIGS = {
     "int8_voltage_all": dict(INT8, nonidealities=dict(ALL, voltage_variation=0.05)),
     "int4_voltage": dict(INT8, activation_bits=4, weight_bits=4, input_slice=(1, 1, 2), weight_slice=(1, 1, 2),
                          adc_bits=6, nonidealities=dict(write_variation=0.02, voltage_variation=0.03)),
+    # Slice-pair read noise: one conductance operand per input slice (PAIRB kernels).
+    "int8_read_pair": dict(INT8, nonidealities=dict(write_variation=0.02, read_variation=0.05,
+                                                    read_mode="slice_pair")),
+    "int4_read_pair_all": dict(INT8, activation_bits=4, weight_bits=4, input_slice=(1, 1, 2), weight_slice=(1, 1, 2),
+                               adc_bits=6, nonidealities=dict(ALL, read_variation=0.03, read_mode="slice_pair")),
+    "int7_read_pair": dict(INT8, activation_bits=7, weight_bits=7, input_slice=(1, 2, 2, 2), weight_slice=(1, 2, 2, 2),
+                           adc_bits=8, nonidealities=dict(write_variation=0.02, read_variation=0.04,
+                                                          read_mode="slice_pair")),
 }
 
 
@@ -165,7 +173,7 @@ def test_ideal_digit_dots_are_bit_exact(mf, name):
 
 
 @pytest.mark.parametrize("name", ["int8_write", "int8_rpr64_all", "default_1bit", "int8_rpr64_ideal",
-                                  "int4_rpr64_ideal", "int8_noisy"])
+                                  "int4_rpr64_ideal", "int8_noisy", "int8_read_pair"])
 def test_column_shards_and_row_prefixes_are_exact(mf, name):
     config = config_of(mf, name)
     a, b = operands(300, 512, 640, 4)
@@ -189,8 +197,9 @@ def test_against_the_oracle(mf):
     assert_close_nonideal(got, want, "oracle")
 
 
-def test_read_events_draw_new_noise(mf):
-    config = config_of(mf, "int8_read_shared")
+@pytest.mark.parametrize("name", ["int8_read_shared", "int8_read_pair"])
+def test_read_events_draw_new_noise(mf, name):
+    config = config_of(mf, name)
     a, b = operands(128, 256, 256, 6)
     sim = mf.Simulator(config)
     first, second = sim.mm(a, b), sim.mm(a, b)
@@ -206,7 +215,14 @@ def test_ineligible_configs_keep_the_simt_path(mf):
                           nonidealities=mf.Nonidealities(write_variation=0.02, voltage_variation=0.02))
     output_mode = mf.Config(**INT8, nonidealities=mf.Nonidealities(write_variation=0.02, read_variation=0.05,
                                                                    read_mode="output"))
-    for config in (voltage64, output_mode):
+    # Slice-pair read noise: 32-row reads without voltage noise only (every input slice's
+    # conductance tiles must fit a pipeline stage).
+    pair64 = mf.Config(**dict(MATRIX, input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2)),
+                       nonidealities=mf.Nonidealities(write_variation=0.02, read_variation=0.02,
+                                                      read_mode="slice_pair"))
+    pair_voltage = mf.Config(**INT8, nonidealities=mf.Nonidealities(read_variation=0.02, voltage_variation=0.02,
+                                                                    read_mode="slice_pair"))
+    for config in (voltage64, output_mode, pair64, pair_voltage):
         assert threads_of(mf, config, 2, 2) == 256
     voltage = mf.Config(**INT8, nonidealities=mf.Nonidealities(write_variation=0.02, voltage_variation=0.02))
     assert threads_of(mf, voltage, 2, 2) == 640
