@@ -53,6 +53,8 @@
 #include <math.h>
 #include <string.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "tcgen05.cuh"
@@ -86,8 +88,18 @@ constexpr int MAXS = 8;          // slices per operand in the tables below
 // same accumulators.
 // PAIRB (slice-pair read noise): G' differs per input slice, so a stage holds the
 // B tiles of every input slice (NIN sets) and job (a, block) reads set a.
-template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool VOLT = false, bool PAIRB = false>
+//
+// WIDE (16-bit BFP and other configurations with more than 8 bits, Config.wide):
+// the codes are int64 and the digits reach 4 bits, so digit_operand_kernel writes
+// the FP16 digits of every input slice in the MMA's tile layout once per call and
+// a stage loads them as VOLT loads its voltage tiles (one part); totals are int64,
+// scaled by restore_scales in FP64 and summed in FP64 (simulator.py:57-66,575-586).
+template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool VOLT = false, bool PAIRB = false,
+          bool WIDE = false>
 struct Geo {
+    static constexpr bool AOP = VOLT || WIDE;              // A tiles loaded from a precomputed operand
+    static constexpr int APARTS = VOLT ? 2 : 1;            // FP16 parts of that operand
+    static constexpr int ACCB = WIDE ? 8 : 4;              // bytes of a cascade value
     static constexpr int KS = KR / 16;                     // MMA K steps per read
     static constexpr int EC = BN / 4;                      // columns per epilogue thread per block
     static constexpr int NP = NW * BN;                     // accumulator columns of one half (jj * NW + w)
@@ -100,18 +112,18 @@ struct Geo {
     static constexpr int BC = NJB * BN;                    // output columns per CTA
     static constexpr int VALS = NW * EC;                   // TMEM columns a thread reads per accumulator
     static constexpr int AT = BM * 32;                     // one [128 x 16] FP16 tile
-    static constexpr int XB = VOLT ? NIN * 2 * KS * AT : BM * KR;   // voltage tiles, or the code tile
+    static constexpr int XB = AOP ? NIN * APARTS * KS * AT : BM * KR;   // operand tiles, or the code tile
     static constexpr int BT = BROWS * 32;                  // one [BROWS x 16] FP16 tile (both halves)
     static constexpr int BSETS = PAIRB ? NIN : 1;           // B tile sets per stage
     static constexpr int BB = BSETS * NJB * KS * BT;
     static constexpr int STAGE = (XB + BB + 1023) / 1024 * 1024;
-    static constexpr int AB = VOLT ? 0 : NIN * KS * AT;    // one set of digit planes
+    static constexpr int AB = AOP ? 0 : NIN * KS * AT;     // one set of digit planes
     // Digit planes double-buffered (transform of read i+1 overlaps the MMAs of read i) when they fit.
-    static constexpr int ABUF = VOLT ? 0 : STAGES * STAGE + 2 * AB + BC * BM * 4 + 1024 <= 227 * 1024 ? 2 : 1;
+    static constexpr int ABUF = AOP ? 0 : STAGES * STAGE + 2 * AB + BC * BM * ACCB + 1024 <= 227 * 1024 ? 2 : 1;
     static constexpr int ABUF1 = ABUF > 0 ? ABUF : 1;      // divisor for the buffer rotation
     static constexpr int OFF_A = STAGES * STAGE;
     static constexpr int OFF_ACC1 = OFF_A + ABUF * AB;
-    static constexpr int OFF_BAR = OFF_ACC1 + BC * BM * 4;
+    static constexpr int OFF_BAR = OFF_ACC1 + BC * BM * ACCB;
     static constexpr int NBAR = 2 * STAGES + 2 * ABUF + 2 * U + 1;
     static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16;
     static constexpr int TMEM_COLS = U * UNIT <= 256 ? 256 : 512;
@@ -119,6 +131,7 @@ struct Geo {
     static_assert(BN % 4 == 0 && KR % 16 == 0 && NIN <= MAXS && NW <= MAXS, "unsupported shape");
     static_assert(!VOLT || SPLIT, "voltage tiles pair with split conductance halves");
     static_assert(!PAIRB || (SPLIT && !VOLT), "per-slice conductance tiles: split halves, no voltage tiles");
+    static_assert(!WIDE || (SPLIT && !VOLT && !PAIRB), "wide configurations: split halves, digits as tiles");
     static_assert(VALS % 2 == 0, "TMEM loads start on even columns");
     static_assert(BYTES + 1024 <= 232448, "exceeds the 227 KB shared-memory limit");
 };
@@ -143,6 +156,7 @@ struct Args {
     float maxw[MAXS];
     int factor[MAXS][MAXS];  // s_a * s_w
     int offset;              // -0x4B400000 * sum of factor over the slice pairs (mod 2^32)
+    long long offset64;      // the same mod 2^64 (int64 totals of wide configurations)
     float ffactor[MAXS][MAXS];  // s_a * s_w as FP32 (float totals of the digit mode)
     int raster;              // 0: blockIdx.x walks vector blocks; 1: blockIdx.x walks column blocks
     int n_pad;               // VOLT: rows of one (slice, part) plane of the voltage operand
@@ -183,18 +197,21 @@ __device__ __forceinline__ void tmem_loaded(uint32_t* v) {
 // FSUM (digit mode, reconstruction bound below 2^24): the count min(D, max_w) and
 // the total are FP32 integers, summed exactly with one FMNMX and one FFMA per event.
 template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool NONLINEAR, bool FSUM = false,
-          bool VOLT = false, bool PAIRB = false>
+          bool VOLT = false, bool PAIRB = false, bool WIDE = false>
 __global__ void __launch_bounds__(THREADS, 1)
     tc_physical_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_g,
                        const __grid_constant__ Args args) {
-    using G = Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT, PAIRB>;
+    using G = Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT, PAIRB, WIDE>;
+    // Cascade values, scales and outputs: FP64 for wide configurations (Config.wide).
+    using Real = typename std::conditional<WIDE, double, float>::type;
+    static_assert(!WIDE || !FSUM, "the digit mode's FP32 totals are not wide");
     // The digit mode sums counts in FP32, exact only while every accumulator read from
     // TMEM is the integer digit dot itself: one FP16 part, no split halves.
     static_assert(!FSUM || (!SPLIT && NPART == 1), "FSUM needs exact integer digit dots (one FP16 part)");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = smem_align1024(smem_raw);
     uint8_t* a_planes = base + G::OFF_A;
-    float* acc1 = reinterpret_cast<float*>(base + G::OFF_ACC1);             // [BC][BM]
+    Real* acc1 = reinterpret_cast<Real*>(base + G::OFF_ACC1);               // [BC][BM]
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + G::OFF_BAR);
     uint64_t* full = bars;                      // [STAGES] codes and G' tiles landed
     uint64_t* empty = bars + STAGES;            // [STAGES] the read's MMAs are done with them
@@ -230,7 +247,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    for (int idx = threadIdx.x; idx < G::BC * BM; idx += THREADS) acc1[idx] = 0.0f;
+    for (int idx = threadIdx.x; idx < G::BC * BM; idx += THREADS) acc1[idx] = Real(0);
     if (warp == 0 && lane == 0) {
         prefetch_map(&map_x);
         prefetch_map(&map_g);
@@ -253,10 +270,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (!mbar_wait(&empty[st], ((i / STAGES) & 1) ^ 1, abort_flag, err, 41)) break;
                     uint8_t* stage = base + st * G::STAGE;
                     mbar_expect_tx(&full[st], G::XB + G::BB);
-                    if (VOLT) {
-                        // Tile (a, part, ks): rows (a * 2 + part) * n_pad + n0 of the voltage operand.
+                    if (G::AOP) {
+                        // Tile (a, part, ks): rows (a * APARTS + part) * n_pad + n0 of the operand.
 #pragma unroll 1
-                        for (int t = 0; t < NIN * 2; ++t)
+                        for (int t = 0; t < NIN * G::APARTS; ++t)
 #pragma unroll
                             for (int ks = 0; ks < G::KS; ++ks)
                                 tma_load_2d(stage + (t * G::KS + ks) * G::AT, &map_x, i * KR + ks * 16,
@@ -291,11 +308,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const int st = i % STAGES;
                     if (!mbar_wait(&full[st], (i / STAGES) & 1, abort_flag, err, 42)) break;
                     const int ab = i % G::ABUF1;
-                    if (!VOLT && !mbar_wait(&a_ready[ab], (i / G::ABUF1) & 1, abort_flag, err, 43)) break;
+                    if (!G::AOP && !mbar_wait(&a_ready[ab], (i / G::ABUF1) & 1, abort_flag, err, 43)) break;
                     tc_fence_after();
                     const uint8_t* btiles = base + st * G::STAGE + G::XB;
-                    // VOLT: the stage's voltage tiles (a, part, ks); otherwise the digit planes (a, ks).
-                    const uint8_t* planes = VOLT ? base + st * G::STAGE : a_planes + ab * G::AB;
+                    // VOLT / WIDE: the stage's operand tiles (a, part, ks); otherwise the digit planes (a, ks).
+                    const uint8_t* planes = G::AOP ? base + st * G::STAGE : a_planes + ab * G::AB;
 #pragma unroll 1
                     for (int cb = 0; cb < NJB && ok; ++cb) {
 #pragma unroll 1
@@ -310,11 +327,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                             }
                             tc_fence_after();
                             const uint32_t d = tmem + unit * G::UNIT;
-                            if (VOLT) {
-                                // Both voltage parts into the same accumulators (B halves stacked along N).
-                                const uint64_t da = desc_sw32(planes + a * 2 * G::KS * G::AT);
+                            if (G::AOP) {
+                                // Every part into the same accumulators (B halves stacked along N).
+                                const uint64_t da = desc_sw32(planes + a * G::APARTS * G::KS * G::AT);
 #pragma unroll
-                                for (int vp = 0; vp < 2; ++vp)
+                                for (int vp = 0; vp < G::APARTS; ++vp)
 #pragma unroll
                                     for (int ks = 0; ks < G::KS; ++ks)
                                         mma_f16(d, da + (uint64_t)(((vp * G::KS + ks) * G::AT) >> 4),
@@ -333,7 +350,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                     }
                     if (!ok) break;
-                    if (!VOLT) mma_commit(&a_free[ab]);
+                    if (!G::AOP) mma_commit(&a_free[ab]);
                     mma_commit(&empty[st]);
                 }
                 // All issued MMAs complete before TMEM is released.
@@ -346,7 +363,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             // 16-code step becomes one [128 x 16] FP16 plane per input slice in the
             // 32-byte-swizzled K-major layout (16-byte halves swapped in rows with bit 2 set).
             const int tw = warp - 2;
-            for (int i = 0; i < (VOLT ? 0 : MR); ++i) {
+            for (int i = 0; i < (G::AOP ? 0 : MR); ++i) {
                 const int st = i % STAGES;
                 const int ab = i % G::ABUF1;
                 bool ok = mbar_wait(&full[st], (i / STAGES) & 1, abort_flag, err, 45);
@@ -395,39 +412,42 @@ __global__ void __launch_bounds__(THREADS, 1)
         const long long row = n0 + r;
         const bool live = row < args.n;
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + hc * G::VALS;
-        float acc0[NJB][G::EC];
+        Real acc0[NJB][G::EC];
 #pragma unroll
         for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
-            for (int e = 0; e < G::EC; ++e) acc0[cb][e] = 0.0f;
+            for (int e = 0; e < G::EC; ++e) acc0[cb][e] = Real(0);
+        // FP32 or FP64 (wide) per-read scales.
+        const Real* xscale = reinterpret_cast<const Real*>(args.xscale);
+        const Real* wscale = reinterpret_cast<const Real*>(args.wscale);
         // Per-read scales are loaded one read ahead so their latency hides behind a read's work.
         const int colbase = c0 + hc * G::EC;
-        float xs_next = live ? __ldg(args.xscale + row * MR) : 0.0f;
-        float ws_next[NJB][G::EC];
+        Real xs_next = live ? __ldg(xscale + row * MR) : Real(0);
+        Real ws_next[NJB][G::EC];
 #pragma unroll
         for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
             for (int e = 0; e < G::EC; ++e)
-                ws_next[cb][e] = colbase + cb * BN + e < args.col_end ? __ldg(args.wscale + colbase + cb * BN + e)
-                                                                      : 0.0f;
+                ws_next[cb][e] = colbase + cb * BN + e < args.col_end ? __ldg(wscale + colbase + cb * BN + e)
+                                                                      : Real(0);
         bool ok = true;
         int job = 0;
         for (int i = 0; i < MR && ok; ++i) {
-            const float xs = xs_next;
-            float ws_now[NJB][G::EC];
+            const Real xs = xs_next;
+            Real ws_now[NJB][G::EC];
 #pragma unroll
             for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
                 for (int e = 0; e < G::EC; ++e) ws_now[cb][e] = ws_next[cb][e];
             if (i + 1 < MR) {
-                xs_next = live ? __ldg(args.xscale + row * MR + i + 1) : 0.0f;
+                xs_next = live ? __ldg(xscale + row * MR + i + 1) : Real(0);
 #pragma unroll
                 for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
                     for (int e = 0; e < G::EC; ++e) {
                         const int col = colbase + cb * BN + e;
                         ws_next[cb][e] =
-                            col < args.col_end ? __ldg(args.wscale + (long long)(i + 1) * args.ldw + col) : 0.0f;
+                            col < args.col_end ? __ldg(wscale + (long long)(i + 1) * args.ldw + col) : Real(0);
                     }
             }
             // Unrolled: acc0 and the scales stay in registers (a dynamic block index would
@@ -439,11 +459,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // the low mantissa bits (max_w < 2^22); the bit pattern of q is
                 // 0x4B400000 + count, so the total accumulates bits * factor in wrapping int32
                 // and the constant part is removed once.
-                int total[G::EC];
+                // Wide configurations: 64-bit totals (the reference's int64 totals,
+                // reference.py:115), accumulated modulo 2^64 like the 32-bit ones.
+                using Tot = typename std::conditional<WIDE, unsigned long long, int>::type;
+                Tot total[G::EC];
                 float ftotal[G::EC];
 #pragma unroll
                 for (int e = 0; e < G::EC; ++e) {
-                    total[e] = args.offset;
+                    total[e] = WIDE ? (Tot)args.offset64 : (Tot)args.offset;
                     ftotal[e] = 0.0f;
                 }
 #pragma unroll 1
@@ -483,14 +506,25 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 s = mul_sat(x, args.cws[w]);
                             }
                             const float q = __fmaf_rn(s, args.maxw[w], kMagic);
-                            total[e] += __float_as_int(q) * args.factor[a][w];
+                            if constexpr (WIDE)
+                                total[e] += (Tot)(long long)__float_as_int(q) * (Tot)(long long)args.factor[a][w];
+                            else
+                                total[e] += __float_as_int(q) * args.factor[a][w];
                         }
                 }
                 if (!ok) break;
 #pragma unroll
-                for (int e = 0; e < G::EC; ++e)
-                    acc0[cb][e] = __fadd_rn(acc0[cb][e], __fmul_rn(__fmul_rn(FSUM ? ftotal[e] : __int2float_rn(total[e]), xs),
-                                                                   ws_now[cb][e]));
+                for (int e = 0; e < G::EC; ++e) {
+                    if constexpr (WIDE) {
+                        // restore_scales in FP64 (simulator.py:57-66).
+                        acc0[cb][e] = __dadd_rn(acc0[cb][e], restore_scales(__ll2double_rn((long long)total[e]), xs,
+                                                                           ws_now[cb][e]));
+                    } else {
+                        acc0[cb][e] = __fadd_rn(
+                            acc0[cb][e],
+                            __fmul_rn(__fmul_rn(FSUM ? ftotal[e] : __int2float_rn(total[e]), xs), ws_now[cb][e]));
+                    }
+                }
             }
             if (!ok) break;
             // Block boundary of the 16-read cascade: level 1 += level 0 (MR <= 256 keeps two levels).
@@ -500,9 +534,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
                     for (int e = 0; e < G::EC; ++e) {
-                        float* slot = acc1 + (cb * BN + hc * G::EC + e) * BM + r;
-                        *slot = __fadd_rn(*slot, acc0[cb][e]);
-                        acc0[cb][e] = 0.0f;
+                        Real* slot = acc1 + (cb * BN + hc * G::EC + e) * BM + r;
+                        *slot = add_rn<Real>(*slot, acc0[cb][e]);
+                        acc0[cb][e] = Real(0);
                     }
             }
         }
@@ -516,12 +550,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (col >= args.col_end || col >= args.out_features) continue;
                     // acc0 + acc1 + acc2 + acc3 (upper levels zero), then the reference's
                     // store into a zero-filled output.
-                    float value = __fadd_rn(acc0[cb][e], acc1[cl * BM + r]);
-                    value = __fadd_rn(value, 0.0f);
-                    value = __fadd_rn(value, 0.0f);
-                    value = __fadd_rn(0.0f, value);
-                    if (args.bias) value = __fadd_rn(value, args.bias[col]);
-                    args.out[row * args.ldo + col] = value;
+                    Real value = add_rn<Real>(acc0[cb][e], acc1[cl * BM + r]);
+                    value = add_rn<Real>(value, Real(0));
+                    value = add_rn<Real>(value, Real(0));
+                    value = add_rn<Real>(Real(0), value);
+                    if (args.bias) value = add_rn<Real>(value, reinterpret_cast<const Real*>(args.bias)[col]);
+                    reinterpret_cast<Real*>(args.out)[row * args.ldo + col] = value;
                 }
         }
     }
@@ -550,12 +584,13 @@ constexpr int MAXBN = 32;        // columns per block, at most
 //   pair_slices > 0 (slice-pair read noise): one operand per input slice a, set a
 //   starting at row a * blocks * brows, its G scaled by exp(sigma_r z) with z the
 //   normal of stream 20 at cell * pair_slices + a (reference.py:88-91).
-__global__ void __launch_bounds__(256) b_operand_kernel(Layout L, Physics P, const uint8_t* packed, int p,
+template <typename CodeT>
+__global__ void __launch_bounds__(256) b_operand_kernel(Layout L, Physics P, const CodeT* packed, int p,
                                                         int col_begin, int blocks, int bn, int nwp, int brows,
                                                         int pstride, int parts, int kc, long long kpad, uint32_t seed,
                                                         uint64_t event, float scale, int fixed, int pair_slices,
                                                         __half* gs) {
-    __shared__ uint8_t codes[KC][MAXBN];
+    __shared__ uint16_t codes[KC][MAXBN];   // weight codes have at most 16 bits
     for (int block = blockIdx.y; block < blocks; block += gridDim.y) {
         const long long k0 = (long long)blockIdx.x * kc;
         const long long o0 = (long long)col_begin + (long long)block * bn;
@@ -566,7 +601,7 @@ __global__ void __launch_bounds__(256) b_operand_kernel(Layout L, Physics P, con
         const long long tile_base = (arr * p + tile) * L.R;
         for (int idx = threadIdx.x; idx < kc * bn; idx += blockDim.x) {
             const int kk = idx / bn, jj = idx - kk * bn;
-            codes[kk][jj] = packed[(tile_base + r0 + kk) * L.C + c0 + jj];
+            codes[kk][jj] = (uint16_t)packed[(tile_base + r0 + kk) * L.C + c0 + jj];
         }
         __syncthreads();
         const uint64_t read_seed = event_seed(seed, event);
@@ -655,6 +690,24 @@ __global__ void __launch_bounds__(256) a_operand_kernel(Layout L, float volt_var
     }
 }
 
+// Digit operand of a wide configuration: the FP16 digit of every input slice a of
+// every (vector, row of K) at row a * n_pad + v, K contiguous (the layout of the
+// voltage operand with one part); rows past n are zero.  The current kernel loads
+// its [128 x 16] tiles with TMA as the A operand.
+template <typename CodeT>
+__global__ void __launch_bounds__(256) digit_operand_kernel(Layout L, const CodeT* codes, long long n,
+                                                            long long n_pad, long long kpad, __half* out) {
+    const long long k = (long long)blockIdx.x * 256 + threadIdx.x;
+    if (k >= kpad) return;
+    for (long long v = blockIdx.y; v < n_pad; v += gridDim.y) {
+        const long long code = v < n ? (long long)codes[v * kpad + k] : 0;
+        for (int a = 0; a < L.n_in; ++a) {
+            const long long d = (code >> L.in_shift[a]) & L.in_mask[a];
+            out[((long long)a * n_pad + v) * kpad + k] = __float2half_rn((float)d);
+        }
+    }
+}
+
 // Instantiations: (input slices, weight slices) -> columns per block, blocks per
 // CTA, split accumulators.  Each MMA is as wide as TMEM and the 256-column limit of
 // N allow (the tensor core's cost here is per instruction rather than per column).
@@ -672,8 +725,9 @@ bool shape_of(const mf_config& c, Shape& s) {
     for (const Shape& k : c.ideal ? kDigitShapes : kShapes)
         if (k.nin == c.n_in && k.nw == c.n_w) {
             s = k;
-            // A stage holds every input slice's tiles: one column block per CTA.
-            if (pair_mode(c)) s.njb = 1;
+            // A stage holds every input slice's tiles (slice-pair noise) or the digit
+            // tiles of a wide configuration: one column block per CTA.
+            if (pair_mode(c) || (!c.ideal && (c.wide || c.wide_codes))) s.njb = 1;
             return true;
         }
     return false;
@@ -722,7 +776,10 @@ static bool digits_eligible(const mf_config& c, int32_t m) {
 
 bool tc_physical_eligible(const mf_config& c, int32_t m) {
     if (c.ideal) return digits_eligible(c, m);
-    if (c.wide || c.wide_codes || c.precise_currents) return false;
+    if (c.precise_currents) return false;
+    // Wide configurations (16-bit BFP): five-slice operands, digits as FP16 tiles, int64 totals.
+    const bool wide = c.wide || c.wide_codes;
+    if (wide && (c.n_in != 5 || c.n_w != 5 || c.volt_var != 0 || tcp::pair_mode(c))) return false;
     // The output read mode draws noise per ADC event from second moments (SIMT only).
     if (c.read_var != 0 && c.read_mode == 2) return false;
     if (c.write_var + c.read_var > 1.0) return false;
@@ -736,13 +793,17 @@ bool tc_physical_eligible(const mf_config& c, int32_t m) {
     // 32-row reads of the split-halves shapes without voltage tiles.
     if (tcp::pair_mode(c) && (c.read_rows != 32 || !s.split || c.volt_var != 0)) return false;
     if (c.rows % c.read_rows || c.cols % s.bn) return false;
+    // Digit planes are built by byte lookup for digits up to 7; wide configurations
+    // take their digits as FP16 tiles (exact up to 2048).
     for (int i = 0; i < c.n_in; ++i)
-        if (c.in_mask[i] > 7) return false;
+        if (c.in_mask[i] > (wide ? 2047 : 7)) return false;
     for (int i = 0; i < c.n_w; ++i)
         if (c.adc_max[i] < 1 || c.adc_max[i] >= (1 << 22)) return false;
     const long long MR = (long long)m * c.reads;
-    // Totals are accumulated exactly in FP32 and adc_max < 2^22 keeps the rounding trick exact.
-    return MR <= 256 && c.high > 0 && c.drift > 0 && reconstruction_bound(c) < 16777216.0;
+    // Totals are exact in FP32 below 2^24 (int64 and FP64 below 2^53 when wide), and
+    // adc_max < 2^22 keeps the rounding trick exact.
+    return MR <= 256 && c.high > 0 && c.drift > 0 &&
+           reconstruction_bound(c) < (wide ? 9007199254740992.0 : 16777216.0);
 }
 
 int tc_physical_threads() { return tcp::THREADS; }
@@ -765,16 +826,18 @@ size_t tc_physical_workspace_bytes(const mf_config& c, int64_t n, int32_t m, int
     size_t bytes = b_operand_bytes(c, s, m, tiles) + 256;
     if (!c.ideal && c.volt_var != 0)
         bytes += (size_t)c.n_in * 2 * voltage_rows(n) * (size_t)m * c.rows * sizeof(__half);
+    else if (!c.ideal && (c.wide || c.wide_codes))
+        bytes += (size_t)c.n_in * voltage_rows(n) * (size_t)m * c.rows * sizeof(__half);
     return bytes;
 }
 
 template <int NIN, int NW, int BN, int NJB, bool SPLIT, int NPART, int KR, bool NL, bool FSUM = false,
-          bool VOLT = false, bool PAIRB = false>
+          bool VOLT = false, bool PAIRB = false, bool WIDE = false>
 static mf_status launch_tcp(const CUtensorMap& mx, const CUtensorMap& mg, const tcp::Args& args, dim3 grid,
                             cudaStream_t st) {
-    using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT, PAIRB>;
+    using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT, PAIRB, WIDE>;
     const size_t smem = G::BYTES + 1024;
-    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL, FSUM, VOLT, PAIRB>;
+    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL, FSUM, VOLT, PAIRB, WIDE>;
     int regs = 0;
     {
         const mf_status r = kernel_setup(reinterpret_cast<const void*>(kern), smem, &regs);
@@ -796,6 +859,21 @@ template <int NIN, int NW, int BN, int NJB, bool SPLIT>
 static mf_status dispatch_tcp(const mf_config& c, const CUtensorMap& mx, const CUtensorMap& mg,
                               const tcp::Args& args, dim3 grid, cudaStream_t st) {
     const bool nl = c.nonlinear != 0;
+    if constexpr (SPLIT && NIN == 5 && NW == 5) {
+        // Wide configurations (tc_physical_eligible): the digits as FP16 tiles, one column
+        // block per CTA, int64 totals and the FP64 epilogue.
+        if (c.wide || c.wide_codes) {
+            if (c.read_rows == 32)
+                return nl ? launch_tcp<5, 5, BN, 1, true, tcp::PARTS, 32, true, false, false, false, true>(
+                                mx, mg, args, grid, st)
+                          : launch_tcp<5, 5, BN, 1, true, tcp::PARTS, 32, false, false, false, false, true>(
+                                mx, mg, args, grid, st);
+            return nl ? launch_tcp<5, 5, BN, 1, true, tcp::PARTS, 64, true, false, false, false, true>(mx, mg, args,
+                                                                                                       grid, st)
+                      : launch_tcp<5, 5, BN, 1, true, tcp::PARTS, 64, false, false, false, false, true>(mx, mg, args,
+                                                                                                        grid, st);
+        }
+    }
     if constexpr (SPLIT) {
         // Slice-pair read noise (32-row reads, no voltage noise, tc_physical_eligible): one
         // column block per CTA, every input slice's G' tiles per stage.
@@ -859,15 +937,22 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     {
         const int kc = c.rows % tcp::KC == 0 ? tcp::KC : 32;
         const dim3 grid((unsigned)(K / kc), (unsigned)(blocks < 65535 ? blocks : 65535));
-        tcp::b_operand_kernel<<<grid, 256, 0, st>>>(make_layout(c), make_physics(c),
-                                                   static_cast<const uint8_t*>(a.packed), a.p,
-                                                   a.tile_begin * c.cols, blocks, shape.bn, shape.nw, brows, pstride,
-                                                   tcp::parts_of(c), kc, K, a.seed, a.event, scale,
-                                                   shape.split, tcp::pair_mode(c) ? c.n_in : 0, gs);
+        const int pair = tcp::pair_mode(c) ? c.n_in : 0;
+        if (c.wide_codes)
+            tcp::b_operand_kernel<long long><<<grid, 256, 0, st>>>(
+                make_layout(c), make_physics(c), static_cast<const long long*>(a.packed), a.p, a.tile_begin * c.cols,
+                blocks, shape.bn, shape.nw, brows, pstride, tcp::parts_of(c), kc, K, a.seed, a.event, scale,
+                shape.split, pair, gs);
+        else
+            tcp::b_operand_kernel<uint8_t><<<grid, 256, 0, st>>>(
+                make_layout(c), make_physics(c), static_cast<const uint8_t*>(a.packed), a.p, a.tile_begin * c.cols,
+                blocks, shape.bn, shape.nw, brows, pstride, tcp::parts_of(c), kc, K, a.seed, a.event, scale,
+                shape.split, pair, gs);
         MF_LAUNCH_CHECK("b_operand_kernel");
     }
     CUtensorMap mx, mg;
     const bool volt = !c.ideal && c.volt_var != 0;
+    const bool wide = !c.ideal && (c.wide || c.wide_codes);
     const long long n_pad = voltage_rows(a.n);
     mf_status r = MF_OK;
     if (volt && (long long)c.n_in * 2 * n_pad > 2147483647LL) {
@@ -883,6 +968,23 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
                                                    a.vector_offset, event_seed(a.seed, a.event), va);
         MF_LAUNCH_CHECK("a_operand_kernel");
         r = tc_make_map(&mx, va, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K, (uint64_t)c.n_in * 2 * n_pad,
+                        (uint64_t)K, 16, tcp::BM, CU_TENSOR_MAP_SWIZZLE_32B);
+    } else if (wide) {
+        // The digit operand follows the conductance operand in the workspace.
+        if ((long long)c.n_in * n_pad > 2147483647LL) {
+            set_error("digit operand of %lld rows exceeds the TMA row coordinate", (long long)c.n_in * n_pad);
+            return MF_ERR_RESOURCE;
+        }
+        __half* da = reinterpret_cast<__half*>(static_cast<uint8_t*>(workspace) + b_operand_bytes(c, shape, a.m, tiles));
+        const dim3 grid((unsigned)((K + 255) / 256), (unsigned)(n_pad < 65535 ? n_pad : 65535));
+        if (c.wide_codes)
+            tcp::digit_operand_kernel<long long><<<grid, 256, 0, st>>>(
+                make_layout(c), static_cast<const long long*>(a.codes), a.n, n_pad, K, da);
+        else
+            tcp::digit_operand_kernel<uint8_t><<<grid, 256, 0, st>>>(
+                make_layout(c), static_cast<const uint8_t*>(a.codes), a.n, n_pad, K, da);
+        MF_LAUNCH_CHECK("digit_operand_kernel");
+        r = tc_make_map(&mx, da, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K, (uint64_t)c.n_in * n_pad,
                         (uint64_t)K, 16, tcp::BM, CU_TENSOR_MAP_SWIZZLE_32B);
     } else {
         r = tc_make_map(&mx, a.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)a.n,
@@ -935,6 +1037,13 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
         }
     }
     args.offset = (int)(0u - 0x4B400000u * sum);
+    {
+        // The same constant modulo 2^64 for the int64 totals of wide configurations.
+        uint64_t sum64 = 0;
+        for (int w = 0; w < c.n_w; ++w)
+            for (int i = 0; i < c.n_in; ++i) sum64 += (uint64_t)(int64_t)(c.in_factor[i] * c.w_factor[w]);
+        args.offset64 = (long long)(0ull - 0x4B400000ull * sum64);
+    }
     const int bc = shape.bn * shape.njb;
     args.raster = a.raster;
     const dim3 grid = raster_grid((a.n + tcp::BM - 1) / tcp::BM, (cols + bc - 1) / bc, a.raster);

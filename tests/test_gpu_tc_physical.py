@@ -49,6 +49,13 @@ CONFIGS = {
     "int8_voltage_all": dict(INT8, nonidealities=dict(ALL, voltage_variation=0.05)),
     "int4_voltage": dict(INT8, activation_bits=4, weight_bits=4, input_slice=(1, 1, 2), weight_slice=(1, 1, 2),
                          adc_bits=6, nonidealities=dict(write_variation=0.02, voltage_variation=0.03)),
+    # Wide configurations (16-bit BFP, BASELINE configs[2]'s third format): int64 codes,
+    # 4-bit digits as FP16 tiles, int64 totals and the FP64 restore_scales epilogue.
+    "bfp16_rpr64_all": dict(MATRIX, activation_bits=16, weight_bits=16, bw_e=8, input_slice=(1, 3, 4, 4, 4),
+                            weight_slice=(1, 3, 4, 4, 4), adc_bits=8, nonidealities=ALL),
+    "bfp16_write": dict(INT8, activation_bits=16, weight_bits=16, bw_e=8, input_slice=(1, 3, 4, 4, 4),
+                        weight_slice=(1, 3, 4, 4, 4), adc_bits=8,
+                        nonidealities=dict(write_variation=0.02, read_variation=0.02)),
     # Slice-pair read noise: one conductance operand per input slice (PAIRB kernels).
     "int8_read_pair": dict(INT8, nonidealities=dict(write_variation=0.02, read_variation=0.05,
                                                     read_mode="slice_pair")),
@@ -141,8 +148,10 @@ def test_tensor_core_currents_match_the_oracle(mf, name):
     m = -(-k // config.array_size[0])
     p = -(-256 // config.array_size[1])
     assert threads_of(mf, config, m, p) == 640, "the tensor-core physical kernel is not selected"
-    fast = product(mf, config, a, b, 0).cpu().numpy()
-    simt = product(mf, config, a, b, 1).cpu().numpy()
+    # Wide configurations reconstruct in FP64; the product is returned in the
+    # operands' dtype, as Simulator.mm returns it (simulator.py:616).
+    fast = product(mf, config, a, b, 0).float().cpu().numpy()
+    simt = product(mf, config, a, b, 1).float().cpu().numpy()
     want = O.mm(a.cpu().numpy(), b.cpu().numpy(), config)
     assert np.isfinite(fast).all()
     flip = largest_flip(mf, config, a, b)
@@ -173,7 +182,7 @@ def test_ideal_digit_dots_are_bit_exact(mf, name):
 
 
 @pytest.mark.parametrize("name", ["int8_write", "int8_rpr64_all", "default_1bit", "int8_rpr64_ideal",
-                                  "int4_rpr64_ideal", "int8_noisy", "int8_read_pair"])
+                                  "int4_rpr64_ideal", "int8_noisy", "int8_read_pair", "bfp16_rpr64_all"])
 def test_column_shards_and_row_prefixes_are_exact(mf, name):
     config = config_of(mf, name)
     a, b = operands(300, 512, 640, 4)
