@@ -389,6 +389,112 @@ __global__ void rhs_colgroup_kernel(const float* b, int64_t K, int64_t O, int64_
     }
 }
 
+// Tiled form of rhs_colgroup_kernel for aligned FP32 matrices (row stride a
+// multiple of 4, 16-byte-aligned base, R a multiple of GR, C a multiple of 16): a
+// CTA stages one GR x 128 tile of b in shared memory with 16-byte coalesced loads
+// (one read of every value), a thread per column takes the group maximum and the
+// codes from shared memory and writes its K-major run of GR codes as whole
+// 32-byte sectors, and the CTA then writes the packed [m, p, R, C] rows of the
+// tile as 16-byte chunks.  Same outputs as rhs_colgroup_kernel.
+template <int GR>
+__global__ void __launch_bounds__(256) rhs_tile_kernel(const float* b, int64_t K, int64_t O, int64_t ldb, QuantSpec s,
+                                                       int R, int C, int64_t m, int64_t p, float* maxima,
+                                                       uint8_t* packed, uint8_t* kmajor, float* wscale,
+                                                       uint32_t* check_flag, uint32_t check_code) {
+    constexpr int TC = 128;                         // columns per tile
+    constexpr int LD = TC + 4;                      // padded row of the staged tile
+    __shared__ __align__(16) float tile[GR][LD];
+    __shared__ __align__(16) uint8_t codes[GR][TC];
+    const int64_t j = blockIdx.y;                   // column group (GR rows)
+    const int64_t k0 = j * GR, o0 = (int64_t)blockIdx.x * TC;
+    const int rows = K - k0 < GR ? (int)(K - k0) : GR;
+    const int cols = O - o0 < TC ? (int)(O - o0) : TC;
+    const int tid = threadIdx.x;
+    // Stage: warp w loads rows w, w + 8, ...; lane l the four columns 4l..4l+3.
+    bool bad = false;
+    {
+        const int lane = tid & 31, c4 = 4 * lane;
+        for (int r = tid >> 5; r < GR; r += 8) {
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (r < rows) {
+                const float* src = b + (k0 + r) * ldb + o0 + c4;
+                if (c4 + 3 < cols) {
+                    v = __ldg(reinterpret_cast<const float4*>(src));
+                } else {
+                    if (c4 < cols) v.x = __ldg(src);
+                    if (c4 + 1 < cols) v.y = __ldg(src + 1);
+                    if (c4 + 2 < cols) v.z = __ldg(src + 2);
+                }
+            }
+            bad |= !(fabsf(v.x) <= FLT_MAX) || !(fabsf(v.y) <= FLT_MAX) || !(fabsf(v.z) <= FLT_MAX) ||
+                   !(fabsf(v.w) <= FLT_MAX);
+            *reinterpret_cast<float4*>(&tile[r][c4]) = v;
+        }
+    }
+    // The operand check of the product, folded into this read of b.
+    if (bad && check_flag && *(volatile uint32_t*)check_flag == 0u) atomicCAS(check_flag, 0u, check_code);
+    __syncthreads();
+    const int64_t kpad = m * R;
+    if (tid < TC && tid < cols) {
+        const int c = tid;
+        const int64_t o = o0 + c;
+        float best = 0.0f;
+#pragma unroll 8
+        for (int r = 0; r < GR; ++r) best = fmaxf(best, fabsf(tile[r][c]));
+        maxima[j * O + o] = best;
+        const float scale = group_scale<float>(best, s);
+        const float inv = __frcp_rn(scale);
+        if (wscale) {
+            // As rhs_colgroup_kernel: reads past K and columns past O replicate the last
+            // group and column.
+            const int64_t groups = (K + GR - 1) / GR;
+            const int64_t pc = p * C, mr = kpad / GR;
+            const int64_t last_read = j == groups - 1 ? mr : j + 1;
+            const int64_t last_col = o == O - 1 ? pc : o + 1;
+            for (int64_t jr = j; jr < last_read; ++jr)
+                for (int64_t oc = o; oc < last_col; ++oc) wscale[jr * pc + oc] = scale;
+        }
+#pragma unroll
+        for (int q = 0; q < GR / 32; ++q) {
+            uint32_t words[8];
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int r = 32 * q + 4 * w + e;
+                    const uint32_t code = r < rows ? (code8(tile[r][c], scale, inv, s) & 0xFFu) : 0u;
+                    codes[r][c] = (uint8_t)code;
+                    word |= code << (8 * e);
+                }
+                words[w] = word;
+            }
+            if (kmajor) {
+                uint4* dst = reinterpret_cast<uint4*>(kmajor + o * kpad + k0 + 32 * q);
+                dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
+                dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
+            }
+        }
+    }
+    __syncthreads();
+    // Packed rows: row k0 + r of the tile's columns, 16 columns per chunk (a chunk
+    // stays inside one array tile since C is a multiple of 16).
+    const int64_t arr = k0 / R;
+    const int rr0 = (int)(k0 - arr * R);
+    for (int idx = tid; idx < GR * (TC / 16); idx += blockDim.x) {
+        const int r = idx / (TC / 16), ch = idx % (TC / 16);
+        const int c = 16 * ch;
+        if (c >= cols) continue;
+        const int64_t o = o0 + c, t = o / C, cc = o % C;
+        uint8_t* dst = packed + ((arr * p + t) * R + rr0 + r) * C + cc;
+        if (c + 15 < cols) {
+            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&codes[r][c]);
+        } else {
+            for (int e = 0; c + e < cols; ++e) dst[e] = codes[r][c + e];
+        }
+    }
+}
+
 // wscale[i, t, c] = scale at (read start row, column) with replicate padding.
 template <typename Acc, typename ScaleT>
 __global__ void weight_scale_kernel(View v, GroupGrid g, const Acc* maxima, QuantSpec s, int R,
@@ -937,15 +1043,35 @@ mf_status program_rhs(const mf_config& c, const void* b, int dtype, int64_t k, i
         // Per-read weight scales in the same pass when a group spans exactly one read.
         const bool scales_fused = g.gr == c.read_rows && c.rows % c.read_rows == 0;
         float* fused_wscale = scales_fused ? static_cast<float*>(wscale) : nullptr;
-        if (g.gr == 32)
-            rhs_colgroup_kernel<32><<<grid_for(work, threads), threads, 0, stream>>>(
-                static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
-                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale, check_flag, check_code);
-        else
-            rhs_colgroup_kernel<64><<<grid_for(work, threads), threads, 0, stream>>>(
-                static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
-                static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale, check_flag, check_code);
-        MF_LAUNCH_CHECK("rhs_colgroup_kernel");
+        // The tiled kernel wherever b's rows and the tiles allow 16-byte loads and chunks.
+        const int64_t tile_rows = (k + g.gr - 1) / g.gr;
+        const bool tiled = c.rows % g.gr == 0 && c.cols % 16 == 0 && ldb % 4 == 0 &&
+                           (reinterpret_cast<uintptr_t>(b) & 15) == 0 && tile_rows <= 65535 &&
+                           (!kmajor || (reinterpret_cast<uintptr_t>(kmajor) & 15) == 0);
+        if (tiled) {
+            const dim3 grid((unsigned)((o + 127) / 128), (unsigned)tile_rows);
+            if (g.gr == 32)
+                rhs_tile_kernel<32><<<grid, 256, 0, stream>>>(
+                    static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
+                    static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale, check_flag, check_code);
+            else
+                rhs_tile_kernel<64><<<grid, 256, 0, stream>>>(
+                    static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
+                    static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale, check_flag, check_code);
+            MF_LAUNCH_CHECK("rhs_tile_kernel");
+        } else {
+            if (g.gr == 32)
+                rhs_colgroup_kernel<32><<<grid_for(work, threads), threads, 0, stream>>>(
+                    static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
+                    static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale, check_flag,
+                    check_code);
+            else
+                rhs_colgroup_kernel<64><<<grid_for(work, threads), threads, 0, stream>>>(
+                    static_cast<const float*>(b), k, o, ldb, s, c.rows, c.cols, m, p, maxima,
+                    static_cast<uint8_t*>(packed), static_cast<uint8_t*>(kmajor), fused_wscale, check_flag,
+                    check_code);
+            MF_LAUNCH_CHECK("rhs_colgroup_kernel");
+        }
         if (scales_fused) return MF_OK;
         weight_scale_kernel<float, float><<<grid_for(m * c.reads * p * c.cols, threads), threads, 0, stream>>>(
             v, g, maxima, s, c.rows, c.cols, c.read_rows, c.reads, m, p, static_cast<float*>(wscale));
