@@ -111,6 +111,10 @@ def parse(argv=None):
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work budget of the baseline sample")
     p.add_argument("--parity-rows", type=int, default=16,
                    help="rows checked against the oracle when the cpu_baseline leg does not run")
+    p.add_argument("--exchange", choices=["nccl", "peers"], default="nccl",
+                   help="strong scaling: how every rank's output rows reach the others -- an NCCL all-gather "
+                        "after the product (default; faster at 8 GPUs) or peer stores from the packed kernel's "
+                        "epilogue over NVLink (falls back to NCCL where unavailable)")
     p.add_argument("--gather", action="store_true",
                    help="--scaling weak only: also all-gather every rank's output rows inside each step")
     p.add_argument("--kernel", type=int, default=0, choices=[0, 1, 2, 3],
@@ -409,7 +413,7 @@ def engine_arm(args):
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    from memfast_b200.sharding import gather_rows, row_parallel_mm, row_range, sharded_mm
+    from memfast_b200.sharding import gather_rows, peer_outputs, row_parallel_mm, row_range, sharded_mm
 
     spec = product_spec(mf, args)
     config, size = spec[0], spec[1]
@@ -434,6 +438,9 @@ def engine_arm(args):
     gather = world > 1 and (strong or args.gather)
     full = torch.empty((total_rows, size), device=device) if gather else None
     own = full[r0:r1] if (gather and strong) else None
+    # Strong scaling with --exchange peers: the kernel stores its rows into every rank's
+    # copy of the output over NVLink (peer stores) instead of an all-gather after it.
+    peers = peer_outputs(full) if strong and args.exchange == "peers" else None
     out_host = torch.empty((rows, size), pin_memory=True)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
@@ -445,7 +452,7 @@ def engine_arm(args):
         if world == 1:
             return sim.mm(a, b)
         if strong:
-            return row_parallel_mm(a, b, simulator=sim, row_offset=r0, rows=total_rows, out=full)
+            return row_parallel_mm(a, b, simulator=sim, row_offset=r0, rows=total_rows, out=full, peers=peers)
         out = sharded_mm(a, b, simulator=sim, row_offset=r0)
         if gather:
             return gather_rows(out, total_rows, out=full)
@@ -598,10 +605,12 @@ def engine_arm(args):
     if world > 1:
         line["breakdown"] = dict(
             step_ms=per_step * 1e3, kernel_ms=kernel_s * 1e3, gather_ms=gather_s * 1e3,
-            rest_ms=max(0.0, per_step - kernel_s - gather_s) * 1e3,
-            note="max over ranks of each part timed alone: the rank's mf_sliced_mm launch, the in-place "
-                 "NCCL all-gather of the output rows, and the step's remainder (host work, quantising A, "
-                 "programming B, checks)")
+            rest_ms=max(0.0, per_step - kernel_s - (0.0 if peers is not None and peers.enabled else gather_s)) * 1e3,
+            output_exchange="peer stores from the packed kernel's epilogue over NVLink" if peers is not None
+                            and peers.enabled else "in-place NCCL all-gather",
+            note="max over ranks of each part timed alone: the rank's mf_sliced_mm launch (no peer stores), the "
+                 "in-place NCCL all-gather of the output rows (which the step replaces by peer stores when "
+                 "output_exchange says so), and the step's remainder")
     oracle_rows = None
     if world == 1 and not args.skip_cpu:
         sample, line["cpu_baseline"] = cpu_sample(size, args.cpu_seconds, config)

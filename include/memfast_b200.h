@@ -256,6 +256,9 @@ mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedu
                                  int32_t m, int32_t p, int32_t tile_begin, int32_t tile_end,
                                  size_t* bytes);
 
+/* Most peer output buffers of one mf_mm call (eight GPUs of a node). */
+#define MF_MAX_PEERS 7
+
 /* Caller-owned device buffers of one mf_mm call. */
 typedef struct {
     void* codes;                 /* [n, m*rows] input codes, as mf_quantize_input writes them */
@@ -270,6 +273,17 @@ typedef struct {
     size_t program_workspace_bytes;
     void* mm_workspace;          /* mf_sliced_mm_workspace(cfg, schedule, n, m, p, 0, p) bytes */
     size_t mm_workspace_bytes;
+    /* Row-sharded products on one node: n_peers (at most MF_MAX_PEERS) addresses of
+     * other GPUs' output buffers mapped into this process (CUDA IPC), each at the
+     * element that corresponds to out[0].  The product stores every output into
+     * `out` and into each of them from the kernel's epilogue, which takes the place
+     * of an all-gather of the rows; the kernel ends with a system-scope fence, so
+     * the stores are visible to a peer once it has synchronised with this GPU after
+     * the call (for example through a collective enqueued after it).  Only the
+     * packed tcgen05 path stores to peers: MF_ERR_UNSUPPORTED otherwise, with
+     * nothing enqueued.  n_peers = 0: no peers. */
+    void* peer_out[MF_MAX_PEERS];
+    int32_t n_peers;
 } mf_mm_buffers;
 
 /* One default-mode product out = A @ B with B programmed by the call, enqueued on
@@ -294,6 +308,29 @@ mf_status mf_mm(const mf_config* cfg, const mf_schedule* schedule, const void* a
                 int64_t n, int64_t k, int64_t o, uint32_t a_narrow_code, uint32_t b_narrow_code,
                 const mf_mm_buffers* buffers, uint32_t seed, uint64_t event, int64_t vector_offset,
                 uint32_t* error_word, void* stream);
+
+/* Lets kernels on the current device read and write memory of device
+ * `peer_device` (cudaDeviceEnablePeerAccess; already enabled counts as success).
+ * The peer-store path of mf_mm needs it for every peer buffer's device: a buffer
+ * mapped from another process lives in that device's context.  MF_ERR_UNSUPPORTED
+ * when the two devices cannot reach each other. */
+mf_status mf_enable_peer_access(int32_t peer_device);
+
+/* The CUDA IPC handle (handle_bytes = sizeof(cudaIpcMemHandle_t), 64) of the
+ * device allocation that contains `ptr`, and ptr's byte offset in it, for another
+ * process to map with mf_ipc_open. */
+mf_status mf_ipc_export(const void* ptr, void* handle, size_t handle_bytes, size_t* offset);
+
+/* Maps a device buffer of another process into the current device's address
+ * space (cudaIpcOpenMemHandle with lazy peer access): `handle` holds the
+ * handle_bytes bytes of that process's cudaIpcMemHandle_t for the buffer's
+ * allocation, *base receives the allocation's address here.  Kernels on the
+ * current device may then read and write it (the peer outputs of mf_mm).
+ * MF_ERR_INVALID when handle_bytes is not the size of a CUDA IPC handle. */
+mf_status mf_ipc_open(const void* handle, size_t handle_bytes, void** base);
+
+/* Unmaps an allocation mapped by mf_ipc_open. */
+mf_status mf_ipc_close(void* base);
 
 /* Kernel families behind mf_sliced_mm.  The reference has one pair of SIMT
  * kernels (memfast/kernels.cu:43-202); this engine picks among these per

@@ -17,6 +17,7 @@ PACKAGE = Path(__file__).resolve().parent
 LIBRARY = PACKAGE / "libmemfast_b200.so"
 ABI_VERSION = 3
 MAX_SLICES = 32
+MAX_PEERS = 7
 
 STATIC_QUANTIZE_SCRATCH_BYTES = 4 << 20
 MF_OK, MF_ERR_INVALID, MF_ERR_RESOURCE, MF_ERR_CUDA, MF_ERR_UNSUPPORTED = range(5)
@@ -78,7 +79,8 @@ class MFMMBuffers(ct.Structure):
                 ("out", ct.c_void_p), ("flags", ct.c_void_p),
                 ("quantize_workspace", ct.c_void_p), ("quantize_workspace_bytes", ct.c_size_t),
                 ("program_workspace", ct.c_void_p), ("program_workspace_bytes", ct.c_size_t),
-                ("mm_workspace", ct.c_void_p), ("mm_workspace_bytes", ct.c_size_t)]
+                ("mm_workspace", ct.c_void_p), ("mm_workspace_bytes", ct.c_size_t),
+                ("peer_out", ct.c_void_p * MAX_PEERS), ("n_peers", ct.c_int32)]
 
 
 _VOID = ct.c_void_p
@@ -86,6 +88,10 @@ _SIGNATURES = {
     "mf_abi_version": (ct.c_int32, []),
     "mf_launch_count": (ct.c_uint64, []),
     "mf_last_path": (ct.c_int32, []),
+    "mf_enable_peer_access": (ct.c_int, [ct.c_int32]),
+    "mf_ipc_export": (ct.c_int, [ct.c_void_p, ct.c_void_p, ct.c_size_t, ct.POINTER(ct.c_size_t)]),
+    "mf_ipc_open": (ct.c_int, [ct.c_void_p, ct.c_size_t, ct.POINTER(ct.c_void_p)]),
+    "mf_ipc_close": (ct.c_int, [ct.c_void_p]),
     "mf_debug_stall_next_launch": (ct.c_int, [ct.c_int32, ct.c_int64]),
     "mf_last_error": (ct.c_int32, [ct.c_char_p, ct.c_size_t]),
     "mf_device_check": (ct.c_int, [ct.c_int32, ct.POINTER(ct.c_int32)]),

@@ -11,6 +11,8 @@
 #include <mutex>
 #include <string>
 
+#include <cuda.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -339,12 +341,16 @@ mf_status mf_sliced_mm_workspace(const mf_config* cfg, const mf_schedule* schedu
     return MF_OK;
 }
 
-mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const void* codes,
-                       const void* xscale, const void* packed, const void* wscale, const void* bias,
-                       void* out, int64_t n, int32_t m, int32_t p, int32_t out_features, int64_t ldo,
-                       int32_t tile_begin, int32_t tile_end, uint32_t seed, uint64_t event,
-                       int64_t vector_offset, int32_t stable, void* workspace, size_t workspace_bytes,
-                       void* stream) {
+}  // extern "C"
+
+// mf_sliced_mm with optional peer outputs (mf_mm_buffers.peer_out): the packed
+// path only, checked by the caller before anything is enqueued.
+static mf_status sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const void* codes,
+                           const void* xscale, const void* packed, const void* wscale, const void* bias,
+                           void* out, int64_t n, int32_t m, int32_t p, int32_t out_features, int64_t ldo,
+                           int32_t tile_begin, int32_t tile_end, uint32_t seed, uint64_t event,
+                           int64_t vector_offset, int32_t stable, void* workspace, size_t workspace_bytes,
+                           void* stream, void* const* peers, int32_t n_peers) {
     mf_status st = check_config(cfg);
     if (st) return st;
     if (!codes || !xscale || !packed || !wscale || !out || n < 0 || m < 1 || p < 1 || out_features < 1 ||
@@ -370,6 +376,12 @@ mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const 
     MMArgs a{codes, xscale, packed, wscale, bias, out, n, m, p, out_features, ldo, tile_begin, tile_end,
              seed, event, vector_offset, stable, s.kmajor_ready != 0, s.raster, stall_stage,
              g_stall_cycles.load()};
+    for (int32_t i = 0; i < n_peers; ++i) a.peer_out[i] = peers[i];
+    a.n_peers = n_peers;
+    if (n_peers && !use_packed(*cfg, s, m, stable)) {
+        set_error("peer outputs need the packed tcgen05 path");
+        return MF_ERR_UNSUPPORTED;
+    }
     int32_t path;
     mf_status r;
     if (use_packed(*cfg, s, m, stable)) {
@@ -390,6 +402,18 @@ mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const 
     }
     if (r == MF_OK) g_last_path = path;
     return r;
+}
+
+extern "C" {
+
+mf_status mf_sliced_mm(const mf_config* cfg, const mf_schedule* schedule, const void* codes,
+                       const void* xscale, const void* packed, const void* wscale, const void* bias,
+                       void* out, int64_t n, int32_t m, int32_t p, int32_t out_features, int64_t ldo,
+                       int32_t tile_begin, int32_t tile_end, uint32_t seed, uint64_t event,
+                       int64_t vector_offset, int32_t stable, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+    return sliced_mm(cfg, schedule, codes, xscale, packed, wscale, bias, out, n, m, p, out_features, ldo, tile_begin,
+                     tile_end, seed, event, vector_offset, stable, workspace, workspace_bytes, stream, nullptr, 0);
 }
 
 mf_status mf_mm(const mf_config* cfg, const mf_schedule* schedule, const void* a, const void* b, int32_t dtype,
@@ -414,6 +438,19 @@ mf_status mf_mm(const mf_config* cfg, const mf_schedule* schedule, const void* a
     }
     const int32_t m = (int32_t)m64, p = (int32_t)p64;
     const mf_schedule s = schedule_or_default(schedule);
+    if (B->n_peers < 0 || B->n_peers > MF_MAX_PEERS) {
+        set_error("mf_mm: n_peers %d outside [0, %d]", B->n_peers, MF_MAX_PEERS);
+        return MF_ERR_INVALID;
+    }
+    for (int32_t i = 0; i < B->n_peers; ++i)
+        if (!B->peer_out[i]) {
+            set_error("mf_mm: peer output %d is NULL", i);
+            return MF_ERR_INVALID;
+        }
+    if (B->n_peers && !use_packed(c, s, m, 0)) {
+        set_error("mf_mm: peer outputs need the packed tcgen05 path");
+        return MF_ERR_UNSUPPORTED;
+    }
     const size_t quantize_need = quantize_workspace_bytes(c, false, n, k);
     const size_t program_need = quantize_workspace_bytes(c, true, o, k);
     size_t mm_need = 0;
@@ -451,12 +488,91 @@ mf_status mf_mm(const mf_config* cfg, const mf_schedule* schedule, const void* a
     if (st) return st;
     mf_schedule run = s;
     run.kmajor_ready = kmajor ? 1 : 0;
-    st = mf_sliced_mm(cfg, &run, B->codes, B->xscale, B->packed, B->wscale, nullptr, B->out, n, m, p, (int32_t)o, o,
-                      0, p, seed, event, vector_offset, 0, B->mm_workspace, B->mm_workspace_bytes, stream);
+    st = sliced_mm(cfg, &run, B->codes, B->xscale, B->packed, B->wscale, nullptr, B->out, n, m, p, (int32_t)o, o, 0,
+                   p, seed, event, vector_offset, 0, B->mm_workspace, B->mm_workspace_bytes, stream, B->peer_out,
+                   B->n_peers);
     if (st) return st;
     st = check_finite(B->out, c.wide ? MF_F64 : MF_F32, n * o, 1, 0, flags + 1, stream_);
     if (st) return st;
     return error_word ? tc_stage_error(error_word, stream_) : MF_OK;
+}
+
+mf_status mf_enable_peer_access(int32_t peer_device) {
+    int device = 0, count = 0, can = 0;
+    MF_CHECK_CUDA(cudaGetDevice(&device), "cudaGetDevice");
+    MF_CHECK_CUDA(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (peer_device < 0 || peer_device >= count) {
+        set_error("peer device %d not present (%d visible)", peer_device, count);
+        return MF_ERR_INVALID;
+    }
+    if (peer_device == device) return MF_OK;
+    MF_CHECK_CUDA(cudaDeviceCanAccessPeer(&can, device, peer_device), "cudaDeviceCanAccessPeer");
+    if (!can) {
+        set_error("device %d cannot access device %d", device, peer_device);
+        return MF_ERR_UNSUPPORTED;
+    }
+    const cudaError_t err = cudaDeviceEnablePeerAccess(peer_device, 0);
+    if (err == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();   // clear the sticky-free status this call leaves
+        return MF_OK;
+    }
+    MF_CHECK_CUDA(err, "cudaDeviceEnablePeerAccess");
+    return MF_OK;
+}
+
+mf_status mf_ipc_export(const void* ptr, void* handle, size_t handle_bytes, size_t* offset) {
+    if (!ptr || !handle || !offset || handle_bytes != sizeof(cudaIpcMemHandle_t)) {
+        set_error("mf_ipc_export: a pointer, a %zu-byte handle buffer and an offset output are required",
+                  sizeof(cudaIpcMemHandle_t));
+        return MF_ERR_INVALID;
+    }
+    // The allocation's base (an IPC handle names a whole allocation), from the driver.
+    typedef CUresult (*AddressRange)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static AddressRange range = nullptr;
+    if (!range) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            range = reinterpret_cast<AddressRange>(p);
+    }
+    if (!range) {
+        set_error("cuMemGetAddressRange unavailable");
+        return MF_ERR_CUDA;
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    const CUresult r = range(&base, &size, (CUdeviceptr)(uintptr_t)ptr);
+    if (r != CUDA_SUCCESS || !base) {
+        set_error("cuMemGetAddressRange failed (%d)", (int)r);
+        return MF_ERR_CUDA;
+    }
+    cudaIpcMemHandle_t h;
+    MF_CHECK_CUDA(cudaIpcGetMemHandle(&h, (void*)(uintptr_t)base), "cudaIpcGetMemHandle");
+    memcpy(handle, &h, sizeof(h));
+    *offset = (size_t)((uintptr_t)ptr - (uintptr_t)base);
+    return MF_OK;
+}
+
+mf_status mf_ipc_open(const void* handle, size_t handle_bytes, void** base) {
+    if (!handle || !base || handle_bytes != sizeof(cudaIpcMemHandle_t)) {
+        set_error("mf_ipc_open: a %zu-byte CUDA IPC handle and an output are required", sizeof(cudaIpcMemHandle_t));
+        return MF_ERR_INVALID;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    *base = nullptr;
+    MF_CHECK_CUDA(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    return MF_OK;
+}
+
+mf_status mf_ipc_close(void* base) {
+    if (!base) {
+        set_error("mf_ipc_close: NULL address");
+        return MF_ERR_INVALID;
+    }
+    MF_CHECK_CUDA(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
+    return MF_OK;
 }
 
 int32_t mf_last_path(void) { return g_last_path; }

@@ -210,8 +210,11 @@ __global__ void __launch_bounds__(THREADS) ideal_kernel(Layout L, MMArgs a, int 
                     OutT value = cascade_finish(acc[e][j]);
                     if (bias) value = add_rn(value, (OutT)bias[col]);
                     out[vec * a.ldo + col] = value;
+                    // Peer outputs of a row-sharded product (the packed kernel's exact rerun).
+                    for (int g = 0; g < a.n_peers; ++g) static_cast<OutT*>(a.peer_out[g])[vec * a.ldo + col] = value;
                 }
             }
+            if (a.n_peers) __threadfence_system();
         }
     }
 }

@@ -66,6 +66,11 @@ struct MMArgs {
     int32_t raster;         // tensor-core kernels: 0 = vector blocks first, 1 = column blocks first
     int32_t stall_stage;    // mf_debug_stall_next_launch: packed kernel stops its loads here (-1 off)
     int64_t stall_cycles;   // ... and its waits give up after this many SM cycles
+    // Peer outputs (mf_mm_buffers.peer_out): every finished output is also stored at
+    // the same offset from each of these addresses, other GPUs' buffers mapped into
+    // this process (packed kernel and its exact rerun only).
+    void* peer_out[MF_MAX_PEERS];
+    int32_t n_peers;
 };
 
 // Grid of a tensor-core launch over nb vector blocks x cb column blocks in the

@@ -161,6 +161,8 @@ struct Args {
     int stop_stage;         // test hook (mf_debug_stall_next_launch): the producer issues no
                             // load from this pipeline stage on; -1 = off
     long long wait_cycles;  // budget of every bounded wait of the launch
+    float* peer_out[MF_MAX_PEERS];   // other GPUs' output buffers (same offsets as out), or none
+    int n_peers;
 };
 
 __device__ __forceinline__ uint32_t or3(uint32_t a, uint32_t b, uint32_t c) { return a | b | c; }
@@ -554,15 +556,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                 s.acc1[cl][r] = value;
             }
         epilogue_barrier();
-        // Coalesced store: each warp writes 32 consecutive columns of one row.
         const int q = threadIdx.x - 32 * EPI_WARP0;
         const int cl = q % BN;
         const int col = c0 + cl;
         if (ok && col < args.col_end && col < args.out_features) {
+            // Coalesced store: each warp writes 32 consecutive columns of one row.
             for (int rr = q / BN; rr < BM; rr += (32 * EPI_WARPS) / BN) {
                 const long long row = n0 + rr;
-                if (row < args.n) args.out[row * args.ldo + col] = s.acc1[cl][rr];
+                if (row >= args.n) continue;
+                const float value = s.acc1[cl][rr];
+                args.out[row * args.ldo + col] = value;
+                // Row-sharded products: the same output into every peer's buffer over
+                // NVLink (plain stores), in place of an all-gather after the kernel.
+                for (int g = 0; g < args.n_peers; ++g) args.peer_out[g][row * args.ldo + col] = value;
             }
+            // The peer stores are performed before anything this GPU does after the kernel.
+            if (args.n_peers) __threadfence_system();
         }
     }
     tc_fence_before();
@@ -1034,6 +1043,8 @@ mf_status tc_packed_sliced_mm(const mf_config& c, const MMArgs& a, void* workspa
     args.raster = a.raster;
     args.stop_stage = a.stall_stage;
     args.wait_cycles = a.stall_stage >= 0 ? a.stall_cycles : tg::kWaitCycles;
+    args.n_peers = a.n_peers;
+    for (int i = 0; i < a.n_peers; ++i) args.peer_out[i] = static_cast<float*>(a.peer_out[i]);
     const long long cols = (long long)tiles * c.cols;
     const long long vblocks = (a.n + tp::BM - 1) / tp::BM;
     const dim3 grid = raster_grid(vblocks, (cols + tp::BN - 1) / tp::BN, a.raster);

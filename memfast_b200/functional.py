@@ -78,7 +78,7 @@ def _operand_code(a, b, config):
     return flags
 
 
-def _native_product(a, b, simulator, *, vector_offset=0, out=None, before_sync=None):
+def _native_product(a, b, simulator, *, vector_offset=0, out=None, before_sync=None, peers=()):
     """A rank-two product through the one-call native path (``AnalogMatrix._native_mm``)
     when ``b`` already has a program that this call would reprogram in place and the
     operands are contiguous kernel dtypes; None otherwise (the caller then takes the
@@ -101,7 +101,7 @@ def _native_product(a, b, simulator, *, vector_offset=0, out=None, before_sync=N
     with torch.no_grad():
         return matrix._native_mm(a.detach(), b.detach(), a_narrow=3 if a_narrows else 0,
                                  b_narrow=3 if b_narrows else 0, input_errors=OPERAND_ERRORS,
-                                 vector_offset=vector_offset, out=out, before_sync=before_sync)
+                                 vector_offset=vector_offset, out=out, before_sync=before_sync, peers=peers)
 
 
 def _resolve_simulator(a, simulator, config, mode, cache_dir):

@@ -25,6 +25,7 @@ ranks rerun together exactly when the single-device layer would.
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .functional import OPERAND_ERRORS, _native_product, _operand_code, _operand_types
 from .simulator import AnalogMatrix, Simulator
 
@@ -54,6 +55,10 @@ def sharded_mm(a_local, b, *, simulator, row_offset, out=None):
     return _row_product(a_local, b, simulator, row_offset, out)
 
 
+class _NoPeerStores(Exception):
+    """The product cannot store into peer buffers (it did not take the one-call path)."""
+
+
 def _check_row_shard(a_local, b, simulator, row_offset):
     if not isinstance(simulator, Simulator):
         raise TypeError("simulator must be Simulator")
@@ -68,13 +73,18 @@ def _check_row_shard(a_local, b, simulator, row_offset):
         raise ValueError("operands and simulator must use the same device")
 
 
-def _row_product(a_local, b, simulator, row_offset, out, before_sync=None):
+def _row_product(a_local, b, simulator, row_offset, out, before_sync=None, peers=()):
     """The rows' product with the operand checks read in the call's one synchronisation
     (functional.mm's deferred check: same errors, same order); after the first call
-    on ``b``, one native call enqueues the whole product (``_native_product``)."""
-    native = _native_product(a_local, b, simulator, vector_offset=row_offset, out=out, before_sync=before_sync)
+    on ``b``, one native call enqueues the whole product (``_native_product``), which
+    also stores the rows into ``peers`` (other ranks' output buffers) when given."""
+    native = _native_product(a_local, b, simulator, vector_offset=row_offset, out=out, before_sync=before_sync,
+                             peers=peers)
     if native is not None:
         return native
+    if peers:
+        # The step-by-step path stores no rows into peers: its caller must gather them.
+        raise _NoPeerStores
     code = _operand_code(a_local, b, simulator.config)
     matrix = simulator._matrix_for(b, checked=True, rows=a_local.shape[0])
     with torch.no_grad():
@@ -82,7 +92,99 @@ def _row_product(a_local, b, simulator, row_offset, out, before_sync=None):
                                input_errors=OPERAND_ERRORS, out=out, before_sync=before_sync)
 
 
-def row_parallel_mm(a_local, b, *, simulator, row_offset, rows, out=None, group=None):
+class PeerOutputs:
+    """Every rank's copy of one output buffer, mapped into every other rank's process
+    over CUDA IPC (``mf_ipc_export`` there, ``mf_ipc_open`` on this rank's device),
+    so that a row-sharded product can store its rows straight into all copies from
+    the kernel's epilogue over NVLink instead of all-gathering them after it
+    (``row_parallel_mm(..., peers=...)``).
+
+    Collective: every rank of ``group`` constructs it with its own ``out`` (same
+    shape and dtype, contiguous, on this node's GPUs).  ``enabled`` is False, on
+    every rank alike, when the ranks are not on one node or a GPU cannot reach
+    another's memory; the product then all-gathers as usual.  The buffers stay
+    mapped while this object lives; every rank must keep its ``out`` alive as long."""
+
+    def __init__(self, out, group=None):
+        import ctypes as ct
+        import socket
+
+        self.out, self.group = out, group
+        self._bases = []
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        usable = (out.is_cuda and out.is_contiguous() and out.numel() > 0 and 1 < world <= _lib.MAX_PEERS + 1
+                  and dist.get_backend(group) == "nccl")
+        shared = None
+        lib = _lib.load()
+        if usable:
+            # The IPC handle of the allocation holding out, and out's byte offset in it.
+            handle, offset = (ct.c_char * 64)(), ct.c_size_t()
+            with torch.cuda.device(out.device):
+                if lib.mf_ipc_export(ct.c_void_p(out.data_ptr()), handle, 64, ct.byref(offset)) == _lib.MF_OK:
+                    shared = (bytes(handle), offset.value)
+        infos = [None] * world
+        dist.all_gather_object(infos, (socket.gethostname(), out.device.index if out.is_cuda else -1,
+                                       str(out.dtype), tuple(out.shape), shared), group=group)
+        addresses = []
+        mine = all(info[4] is not None and info[0] == infos[0][0] and info[2:4] == infos[0][2:4] for info in infos)
+        if mine:
+            # Each peer's allocation is mapped into this device's address space, where
+            # this device's kernels can store to it (lazy peer access).
+            with torch.cuda.device(out.device):
+                for q in range(world):
+                    if q == rank:
+                        continue
+                    handle, offset = infos[q][4]
+                    if lib.mf_enable_peer_access(infos[q][1]) != _lib.MF_OK:
+                        mine = False
+                        break
+                    base = ct.c_void_p()
+                    raw = (ct.c_char * len(handle)).from_buffer_copy(handle)
+                    if lib.mf_ipc_open(raw, len(handle), ct.byref(base)) != _lib.MF_OK or not base.value:
+                        mine = False
+                        break
+                    self._bases.append(base.value)
+                    addresses.append(base.value + offset)
+        votes = [None] * world
+        dist.all_gather_object(votes, bool(mine), group=group)
+        self.enabled = all(votes)
+        # Other ranks' copies in rank order, as addresses in this process.
+        self.buffers = tuple(addresses) if self.enabled else ()
+        if self.enabled:
+            self._start = torch.zeros(1, dtype=torch.int32, device=out.device)
+
+    def __del__(self):
+        lib = _lib.load()
+        for base in getattr(self, "_bases", ()):
+            lib.mf_ipc_close(base)
+
+    def addresses(self, first_row):
+        """Addresses of row ``first_row`` in every other rank's buffer."""
+        row_bytes = self.out.stride(0) * self.out.element_size()
+        return tuple(address + first_row * row_bytes for address in self.buffers)
+
+    def enter(self):
+        """Enqueue an all-reduce that completes only once every rank has entered the
+        call: no rank's kernel writes into a buffer whose owner may still be using
+        its previous contents."""
+        dist.all_reduce(self._start, group=self.group)
+
+
+def peer_outputs(out, group=None):
+    """``PeerOutputs`` of ``out`` over ``group`` (collective)."""
+    return PeerOutputs(out, group)
+
+
+def _packed_path(simulator, n, m, p):
+    """Whether products of this simulator run the packed tcgen05 kernel (the one that
+    stores to peers)."""
+    from . import tuning
+    from .simulator import default_schedule
+
+    return tuning.resolve(simulator.config, default_schedule(simulator.config), n, m, p)[0] == "packed"
+
+
+def row_parallel_mm(a_local, b, *, simulator, row_offset, rows, out=None, group=None, peers=None):
     """The whole [rows, O] product ``A @ B`` on every rank of ``group``, each rank
     holding A's row block [row_offset, row_offset + rows / world) (equal blocks in
     rank order, as ``row_range`` gives when world divides rows).
@@ -91,11 +193,14 @@ def row_parallel_mm(a_local, b, *, simulator, row_offset, rows, out=None, group=
     None).  The in-place NCCL all-gather of every rank's rows and an all-reduce of
     the ranks' check flags are enqueued on the stream right after the product,
     before the call's one host synchronisation, so the transfer follows the product
-    on the device with no host round trip in between.  Because the flags are
-    combined, the FP64 rerun of a product with non-finite outputs
-    (simulator.py:614-615) is decided for the whole product, as on one device:
-    every rank reruns its rows and the gather is repeated; operand errors are
-    raised on every rank.  Bit-identical to ``simulator.mm(A, B)`` on one device.
+    on the device with no host round trip in between.  With ``peers`` (a
+    ``PeerOutputs`` of ``out`` on this node) the packed kernel stores the rows into
+    every rank's buffer itself and no all-gather runs; an all-reduce at the start of
+    the call keeps any rank from writing into a buffer its owner is still using.
+    Because the flags are combined, the FP64 rerun of a product with non-finite
+    outputs (simulator.py:614-615) is decided for the whole product, as on one
+    device: every rank reruns its rows and gathers them; operand errors are raised
+    on every rank.  Bit-identical to ``simulator.mm(A, B)`` on one device.
     """
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     _check_row_shard(a_local, b, simulator, row_offset)
@@ -110,15 +215,31 @@ def row_parallel_mm(a_local, b, *, simulator, row_offset, rows, out=None, group=
         raise ValueError("out must be a contiguous [rows, O] buffer of A's dtype and device")
     own = out[row_offset: row_offset + share]
     gathered = []
+    addresses = ()
+    if peers is not None and peers.enabled and peers.out is out and simulator._in_place_program(b) is not None:
+        m = -(-a_local.shape[1] // simulator.config.array_size[0])
+        p = -(-b.shape[1] // simulator.config.array_size[1])
+        if _packed_path(simulator, share, m, p):
+            addresses = peers.addresses(row_offset)
+            peers.enter()
+    # Rows stored into the peers by this call's first product (not by an FP64 rerun).
+    stored = [bool(addresses)]
 
     def before_sync(output, flags):
         dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=group)
         direct = output.data_ptr() == own.data_ptr()
-        if direct:
+        if stored[0]:
+            stored[0] = False
+        elif direct:
             dist.all_gather_into_tensor(out, own, group=group)
         gathered.append(direct)
 
-    _row_product(a_local, b, simulator, row_offset, own, before_sync)
+    try:
+        _row_product(a_local, b, simulator, row_offset, own, before_sync, peers=addresses)
+    except _NoPeerStores:
+        # Nothing was enqueued: the product runs step by step and its rows are gathered.
+        stored[0] = False
+        _row_product(a_local, b, simulator, row_offset, own, before_sync)
     if not gathered[-1]:
         # The rows reached `out` after the synchronisation (an FP64 rerun, or a result
         # cast to A's dtype): gather them now; every rank takes this branch together.
@@ -226,5 +347,5 @@ def tensor_parallel(model, group=None, *, gather=True):
     return model
 
 
-__all__ = ["row_range", "sharded_mm", "row_parallel_mm", "gather_rows", "tile_range", "gather_columns",
+__all__ = ["row_range", "sharded_mm", "row_parallel_mm", "PeerOutputs", "peer_outputs", "gather_rows", "tile_range", "gather_columns",
            "shard_columns", "tensor_parallel", "ColumnShard"]

@@ -739,7 +739,7 @@ class AnalogMatrix(nn.Module):
         return output
 
     def _native_mm(self, a, b, *, a_narrow=0, b_narrow=0, input_errors=None, vector_offset=0, out=None,
-                   before_sync=None):
+                   before_sync=None, peers=()):
         """``mm(a, b)`` on this default-mode program of ``b`` in one ``mf_mm`` call: the
         operand checks, ``b`` reprogrammed in place (with the K-major copy the kernel
         reads), ``a`` quantised, the fused product and the output check are enqueued
@@ -748,7 +748,9 @@ class AnalogMatrix(nn.Module):
         ``a``/``b``: contiguous [n, K] / [K, O] of one dtype; ``a_narrow``/``b_narrow``:
         the narrowing-check codes of ``functional._operand_code``.  The buffers and
         argument structures of a (vectors, stream) pair are kept in a plan, so a
-        repeated call only fills in the operand and output addresses."""
+        repeated call only fills in the operand and output addresses.  ``peers``:
+        addresses in other GPUs' output buffers (``sharding.PeerOutputs``) that the
+        kernel also stores every output to."""
         n, o = a.shape[0], b.shape[1]
         stream = _lib.stream_of(a.device)
         plan = self._native_plans.get((n, stream.value))
@@ -770,6 +772,9 @@ class AnalogMatrix(nn.Module):
             workspace = torch.empty(max(plan.workspace_bytes, 1), dtype=torch.uint8, device=a.device)
             plan.buffers.mm_workspace = workspace.data_ptr()
         plan.buffers.out = output.data_ptr()
+        plan.buffers.n_peers = len(peers)
+        for index, address in enumerate(peers):
+            plan.buffers.peer_out[index] = address
         _lib.check(plan.mm(plan.config, plan.schedule, a.data_ptr(), b.data_ptr(), _lib.DTYPES[a.dtype],
                            n, plan.k, o, a_narrow, b_narrow, plan.buffers_ref, plan.seed, self._event,
                            vector_offset, plan.word.data_ptr(), stream), "mf_mm")
