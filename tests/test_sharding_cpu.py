@@ -104,3 +104,24 @@ def test_gather_columns_and_agreement_two_ranks_gloo(out_features, cols):
     result = manager.dict()
     mp.spawn(_column_worker, args=(2, _free_port(), out_features, cols, result), nprocs=2, join=True)
     assert result[0] == (True, False) and result[1] == (True, False)
+
+
+def _peer_worker(rank, world, port, result):
+    from memfast_b200.sharding import peer_outputs
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # Host buffers over gloo cannot take peer stores: every rank must agree on that,
+        # so that all of them keep the all-gather (the same collectives in the same order).
+        peers = peer_outputs(torch.zeros(8, 4), None)
+        result[rank] = (peers.enabled, peers.buffers)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_outputs_agree_when_unavailable():
+    manager = mp.Manager()
+    result = manager.dict()
+    mp.spawn(_peer_worker, args=(2, _free_port(), result), nprocs=2, join=True)
+    assert dict(result) == {0: (False, ()), 1: (False, ())}
