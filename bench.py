@@ -53,6 +53,8 @@ EFFECTS = {
     "noisy": dict(write_variation=0.02, read_variation=0.02, voltage_variation=0.02),
     # Read noise drawn per (input slice, weight slice, cell) instead of per cell.
     "pair": dict(write_variation=0.02, read_variation=0.02, read_mode="slice_pair"),
+    # Read noise drawn per ADC event from the read's second moments.
+    "output": dict(write_variation=0.02, read_variation=0.02, read_mode="output"),
 }
 
 
@@ -124,7 +126,7 @@ def parse(argv=None):
                    help="device effects of the configs[1] sweep: ideal (the headline), write "
                         "(write variation 0.02), shared (write + shared read variation 0.02), "
                         "noisy (write + read + voltage variation 0.02, BASELINE's noisy run), pair (write + "
-                        "read variation 0.02 drawn per slice pair)")
+                        "read variation 0.02 drawn per slice pair), output (write + read variation 0.02 drawn per ADC event)")
     return p.parse_args(argv)
 
 

@@ -77,13 +77,27 @@ __device__ __forceinline__ uint32_t rng_mix(uint32_t v) {
     return v ^ (v >> 16);
 }
 
-__device__ __forceinline__ float rng_uniform(int64_t address, uint64_t seed, uint32_t stream) {
-    uint32_t key = rng_mix((uint32_t)seed ^ (stream * 0x9E3779B9u));
-    uint32_t high = (uint32_t)((uint64_t)address >> 32);
+// The hash in three parts, so that a loop over many addresses can keep the parts
+// that depend only on the stream (rng_key) and on the address's high word (rng_fold).
+__device__ __forceinline__ uint32_t rng_key(uint64_t seed, uint32_t stream) {
+    return rng_mix((uint32_t)seed ^ (stream * 0x9E3779B9u));
+}
+
+__device__ __forceinline__ uint32_t rng_fold(uint32_t high, uint64_t seed, uint32_t key) {
     uint32_t folded = rng_mix(high ^ rng_mix((uint32_t)(seed >> 32)));
     if (high != 0) folded ^= rng_mix(high ^ key);
-    uint32_t hashed = rng_mix((uint32_t)address ^ folded ^ key);
-    return __fdiv_rn(__fadd_rn((float)(hashed >> 8), 0.5f), 16777216.0f);
+    return folded;
+}
+
+// (hashed >> 8 + 0.5) / 2^24: the quotient is exact, so it is a product by 2^-24.
+__device__ __forceinline__ float rng_unit(uint32_t low, uint32_t folded, uint32_t key) {
+    const uint32_t hashed = rng_mix(low ^ folded ^ key);
+    return __fmul_rn(__fadd_rn((float)(hashed >> 8), 0.5f), 5.9604644775390625e-8f);
+}
+
+__device__ __forceinline__ float rng_uniform(int64_t address, uint64_t seed, uint32_t stream) {
+    const uint32_t key = rng_key(seed, stream);
+    return rng_unit((uint32_t)address, rng_fold((uint32_t)((uint64_t)address >> 32), seed, key), key);
 }
 
 __host__ __device__ __forceinline__ uint64_t event_seed(uint64_t seed, uint64_t event) {
@@ -96,11 +110,13 @@ __host__ __device__ __forceinline__ uint64_t event_seed(uint64_t seed, uint64_t 
 }
 
 // Box-Muller of streams s and s+1 (random.py:29-33), in FP32.
-__device__ __forceinline__ float rng_normal(int64_t address, uint64_t seed, uint32_t stream) {
-    float first = rng_uniform(address, seed, stream);
-    float second = rng_uniform(address, seed, stream + 1);
-    float radius = sqrtf(__fmul_rn(-2.0f, logf(first)));
+__device__ __forceinline__ float box_muller(float first, float second) {
+    const float radius = sqrtf(__fmul_rn(-2.0f, logf(first)));
     return __fmul_rn(radius, cosf(__fmul_rn(6.283185307179586f, second)));
+}
+
+__device__ __forceinline__ float rng_normal(int64_t address, uint64_t seed, uint32_t stream) {
+    return box_muller(rng_uniform(address, seed, stream), rng_uniform(address, seed, stream + 1));
 }
 
 // ------------------------------------------------- restored conductance --

@@ -94,8 +94,14 @@ constexpr int MAXS = 8;          // slices per operand in the tables below
 // the FP16 digits of every input slice in the MMA's tile layout once per call and
 // a stage loads them as VOLT loads its voltage tiles (one part); totals are int64,
 // scaled by restore_scales in FP64 and summed in FP64 (simulator.py:57-66,575-586).
+//
+// OUTM (output-mode read noise, reference.py:107-114): a job also needs the digit
+// sum S_d = sum_r d(r) of its input slice and Q = sum_r d(r)^2 G(r)^2.  The B tile
+// gets a row of ones after the two halves of G' (its MMA column of the current
+// accumulators is S_d) and two floating FP16 parts of G^2, which the digit-square
+// planes multiply into one more accumulator of NP columns.
 template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool VOLT = false, bool PAIRB = false,
-          bool WIDE = false>
+          bool WIDE = false, bool OUTM = false>
 struct Geo {
     static constexpr bool AOP = VOLT || WIDE;              // A tiles loaded from a precomputed operand
     static constexpr int APARTS = VOLT ? 2 : 1;            // FP16 parts of that operand
@@ -105,19 +111,26 @@ struct Geo {
     static constexpr int NP = NW * BN;                     // accumulator columns of one half (jj * NW + w)
     static constexpr int NT = SPLIT ? (NPART * NP + 15) / 16 * 16 : (NP + 15) / 16 * 16;   // MMA N
     static constexpr int PSTRIDE = SPLIT ? NP : NT;        // B rows between the halves of a tile
-    static constexpr int BROWS = ((NPART * PSTRIDE > NT ? NPART * PSTRIDE : NT) + 7) / 8 * 8;   // B tile rows
+    static constexpr int NTC = OUTM ? NT + 16 : NT;        // N of the current MMA (OUTM: + the ones row)
+    static constexpr int NPV = OUTM ? (NP + 15) / 16 * 16 : 0;   // OUTM: columns of the Q accumulator
+    static constexpr int G2ROW = NTC;                      // OUTM: first B row of the G^2 parts
+    static constexpr int BROWS = OUTM ? (NTC + 2 * NP + 7) / 8 * 8
+                                      : ((NPART * PSTRIDE > NT ? NPART * PSTRIDE : NT) + 7) / 8 * 8;   // B tile rows
     static constexpr int ACCS = SPLIT ? NPART : 1;         // accumulators per slice pair
-    static constexpr int UNIT = NT;                        // TMEM columns of a job
+    static constexpr int UNIT = NTC + NPV;                 // TMEM columns of a job
     static constexpr int U = 512 / UNIT < NJB * NIN ? 512 / UNIT : NJB * NIN;   // TMEM units
     static constexpr int BC = NJB * BN;                    // output columns per CTA
     static constexpr int VALS = NW * EC;                   // TMEM columns a thread reads per accumulator
     static constexpr int AT = BM * 32;                     // one [128 x 16] FP16 tile
     static constexpr int XB = AOP ? NIN * APARTS * KS * AT : BM * KR;   // operand tiles, or the code tile
     static constexpr int BT = BROWS * 32;                  // one [BROWS x 16] FP16 tile (both halves)
+    // A TMA box has at most 256 rows: taller B tiles load as two boxes of BBOX rows.
+    static constexpr int BLOADS = BROWS > 256 ? 2 : 1;
+    static constexpr int BBOX = BROWS / BLOADS;
     static constexpr int BSETS = PAIRB ? NIN : 1;           // B tile sets per stage
     static constexpr int BB = BSETS * NJB * KS * BT;
     static constexpr int STAGE = (XB + BB + 1023) / 1024 * 1024;
-    static constexpr int AB = AOP ? 0 : NIN * KS * AT;     // one set of digit planes
+    static constexpr int AB = AOP ? 0 : (OUTM ? 2 : 1) * NIN * KS * AT;   // digit (and OUTM square) planes
     // Digit planes double-buffered (transform of read i+1 overlaps the MMAs of read i) when they fit.
     static constexpr int ABUF = AOP ? 0 : STAGES * STAGE + 2 * AB + BC * BM * ACCB + 1024 <= 227 * 1024 ? 2 : 1;
     static constexpr int ABUF1 = ABUF > 0 ? ABUF : 1;      // divisor for the buffer rotation
@@ -127,12 +140,16 @@ struct Geo {
     static constexpr int NBAR = 2 * STAGES + 2 * ABUF + 2 * U + 1;
     static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16;
     static constexpr int TMEM_COLS = U * UNIT <= 256 ? 256 : 512;
-    static_assert(U >= 1 && U * UNIT <= 512 && NT <= 256, "accumulators exceed TMEM or the MMA's N");
+    static_assert(U >= 1 && U * UNIT <= 512 && NTC <= 256, "accumulators exceed TMEM or the MMA's N");
+    static_assert(!OUTM || (SPLIT && NPART == 2 && !VOLT && !PAIRB && !WIDE && NP % 16 == 0),
+                  "output-mode noise: split halves of G', NP a multiple of 16, no other operand variant");
     static_assert(BN % 4 == 0 && KR % 16 == 0 && NIN <= MAXS && NW <= MAXS, "unsupported shape");
     static_assert(!VOLT || SPLIT, "voltage tiles pair with split conductance halves");
     static_assert(!PAIRB || (SPLIT && !VOLT), "per-slice conductance tiles: split halves, no voltage tiles");
     static_assert(!WIDE || (SPLIT && !VOLT && !PAIRB), "wide configurations: split halves, digits as tiles");
     static_assert(VALS % 2 == 0, "TMEM loads start on even columns");
+    static_assert(BBOX * BLOADS == BROWS && BBOX % 8 == 0 && BBOX <= 256,
+                  "B tile boxes: at most 256 rows, whole 8-row swizzle atoms");
     static_assert(BYTES + 1024 <= 232448, "exceeds the 227 KB shared-memory limit");
 };
 
@@ -161,6 +178,13 @@ struct Args {
     int raster;              // 0: blockIdx.x walks vector blocks; 1: blockIdx.x walks column blocks
     int n_pad;               // VOLT: rows of one (slice, part) plane of the voltage operand
     int gblocks;             // PAIRB: column blocks of one input slice's G' operand
+    // OUTM: current x (FP16-part units) -> noisy x = x + mf (x + l2s S_d) + z sqrt(vf2 Q),
+    // z the normal of stream 60 at (((((v + vector_offset) MR + i) p + tile) A + a) W + w) C + c.
+    float out_mf, out_vf2, out_l2s;
+    long long vector_offset;
+    int p_total, cols_c;
+    unsigned long long read_seed;
+    uint32_t sq_lo_lo, sq_lo_hi, sq_hi_lo, sq_hi_hi;   // FP16 low / high bytes of d^2, d = 0..7
 };
 
 __device__ __forceinline__ float mul_sat(float a, float b) {
@@ -197,11 +221,11 @@ __device__ __forceinline__ void tmem_loaded(uint32_t* v) {
 // FSUM (digit mode, reconstruction bound below 2^24): the count min(D, max_w) and
 // the total are FP32 integers, summed exactly with one FMNMX and one FFMA per event.
 template <int NIN, int NW, int BN, int NJB, int KR, bool SPLIT, int NPART, bool NONLINEAR, bool FSUM = false,
-          bool VOLT = false, bool PAIRB = false, bool WIDE = false>
+          bool VOLT = false, bool PAIRB = false, bool WIDE = false, bool OUTM = false>
 __global__ void __launch_bounds__(THREADS, 1)
     tc_physical_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_g,
                        const __grid_constant__ Args args) {
-    using G = Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT, PAIRB, WIDE>;
+    using G = Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT, PAIRB, WIDE, OUTM>;
     // Cascade values, scales and outputs: FP64 for wide configurations (Config.wide).
     using Real = typename std::conditional<WIDE, double, float>::type;
     static_assert(!WIDE || !FSUM, "the digit mode's FP32 totals are not wide");
@@ -287,9 +311,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                         for (int cb = 0; cb < NJB; ++cb)
 #pragma unroll
                             for (int ks = 0; ks < G::KS; ++ks)
-                                tma_load_2d(stage + G::XB + ((set * NJB + cb) * G::KS + ks) * G::BT, &map_g,
-                                            i * KR + ks * 16, (set * args.gblocks + cb0 + cb) * G::BROWS,
-                                            &full[st]);
+#pragma unroll
+                                for (int h = 0; h < G::BLOADS; ++h)
+                                    tma_load_2d(stage + G::XB + ((set * NJB + cb) * G::KS + ks) * G::BT +
+                                                    h * G::BBOX * 32,
+                                                &map_g, i * KR + ks * 16,
+                                                (set * args.gblocks + cb0 + cb) * G::BROWS + h * G::BBOX, &full[st]);
                     issued = i + 1;
                 }
                 // Every issued load lands before the CTA may exit.
@@ -301,7 +328,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (lane == 0) {
                 // SPLIT: both halves in one MMA (N = NT) into adjacent accumulators;
                 // otherwise one MMA per half into the same accumulator.
-                const uint32_t idesc = idesc_f16(BM, G::NT);
+                const uint32_t idesc = idesc_f16(BM, G::NTC);
+                const uint32_t idesc_q = idesc_f16(BM, OUTM ? G::NPV : 16);   // OUTM: the Q accumulator
                 bool ok = true;
                 int job = 0;                               // job sequence number: unit job % U
                 for (int i = 0; i < MR && ok; ++i) {
@@ -345,6 +373,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                                         mma_f16(d, da + (uint64_t)((ks * G::AT) >> 4),
                                                 db + (uint64_t)((ks * G::BT + part * G::PSTRIDE * 32) >> 4), idesc,
                                                 (part | ks) != 0);
+                                if constexpr (OUTM) {
+                                    // Q = sum d^2 G^2: digit-square planes against both floating
+                                    // parts of G^2, into one accumulator after the current's.
+                                    const uint64_t dq = desc_sw32(planes + (NIN + a) * G::KS * G::AT);
+#pragma unroll
+                                    for (int ks = 0; ks < G::KS; ++ks)
+#pragma unroll
+                                        for (int part = 0; part < 2; ++part)
+                                            mma_f16(d + G::NTC, dq + (uint64_t)((ks * G::AT) >> 4),
+                                                    db + (uint64_t)((ks * G::BT + (G::G2ROW + part * G::NP) * 32) >> 4),
+                                                    idesc_q, (ks | part) != 0);
+                                }
                             }
                             mma_commit(&unit_full[unit]);
                         }
@@ -392,6 +432,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                             uint8_t* row = planes + (a * G::KS + ks) * G::AT + t * 32;
                             *reinterpret_cast<uint4*>(row + (flip << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
                             *reinterpret_cast<uint4*>(row + ((flip ^ 1u) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+                            if constexpr (OUTM) {
+                                // FP16 d^2: low bytes at positions 0 and 2, high bytes at 1 and 3.
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) {
+                                    const uint32_t d = (w4[k] >> args.a_shift[a]) & args.a_mask4[a];
+                                    o[2 * k] = __byte_perm(args.sq_lo_lo, args.sq_lo_hi, d & 0x0F0Fu) |
+                                               __byte_perm(args.sq_hi_lo, args.sq_hi_hi, (d << 4) & 0xF0F0u);
+                                    o[2 * k + 1] = __byte_perm(args.sq_lo_lo, args.sq_lo_hi, (d >> 16) & 0x0F0Fu) |
+                                                   __byte_perm(args.sq_hi_lo, args.sq_hi_hi, (d >> 12) & 0xF0F0u);
+                                }
+                                uint8_t* sq = planes + ((NIN + a) * G::KS + ks) * G::AT + t * 32;
+                                *reinterpret_cast<uint4*>(sq + (flip << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                                *reinterpret_cast<uint4*>(sq + ((flip ^ 1u) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+                            }
                         }
                     }
                 }
@@ -430,6 +484,24 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int e = 0; e < G::EC; ++e)
                 ws_next[cb][e] = colbase + cb * BN + e < args.col_end ? __ldg(wscale + colbase + cb * BN + e)
                                                                       : Real(0);
+        // OUTM: the hash address of an ADC event,
+        // (((((row + vector_offset) MR + i) p + tile) A + a) W + w) C + cc, is
+        // ev_row + i * ev_read + (a W + w) C + e: this thread's columns colbase + e lie in
+        // one tile (NJB = 1 and BN divides C).  The hash's stream keys and its fold of
+        // the address's high word are kept across events (the word rarely changes).
+        long long ev_row = 0, ev_read = 0;
+        uint32_t key0 = 0, key1 = 0, fold0 = 0, fold1 = 0, fold_high = 0;
+        if constexpr (OUTM) {
+            const int tile = colbase / args.cols_c;
+            ev_read = (long long)args.p_total * NIN * NW * args.cols_c;
+            ev_row = (row + args.vector_offset) * MR * ev_read + (long long)tile * NIN * NW * args.cols_c +
+                     (colbase - tile * args.cols_c);
+            key0 = rng_key(args.read_seed, 60);
+            key1 = rng_key(args.read_seed, 61);
+            fold_high = (uint32_t)((uint64_t)ev_row >> 32);
+            fold0 = rng_fold(fold_high, args.read_seed, key0);
+            fold1 = rng_fold(fold_high, args.read_seed, key1);
+        }
         bool ok = true;
         int job = 0;
         for (int i = 0; i < MR && ok; ++i) {
@@ -476,11 +548,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                                     mbar_wait(&unit_full[unit], (uint32_t)(job / G::U) & 1u, abort_flag, err, 47));
                     if (!ok) break;
                     tc_fence_after();
-                    uint32_t v[G::ACCS][G::VALS];
+                    uint32_t v[G::ACCS + (OUTM ? 1 : 0)][G::VALS];
+                    uint32_t sd[1] = {0u};
 #pragma unroll
                     for (int acc = 0; acc < G::ACCS; ++acc)
                         tmem_load_cols<G::VALS>(lane_base + unit * G::UNIT + acc * G::NP, v[acc]);
-                    tmem_loaded<G::ACCS * G::VALS>(&v[0][0]);
+                    if constexpr (OUTM) {
+                        // Q of this thread's columns, and the row's digit sum (the ones column).
+                        tmem_load_cols<G::VALS>(lane_base + unit * G::UNIT + G::NTC, v[G::ACCS]);
+                        tmem_ld(tmem + ((uint32_t)(quad * 32) << 16) + unit * G::UNIT + G::NT, sd);
+                    }
+                    tmem_loaded<(G::ACCS + (OUTM ? 1 : 0)) * G::VALS>(&v[0][0]);
+                    if constexpr (OUTM) tmem_loaded<1>(sd);
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&unit_empty[unit]);
@@ -489,9 +568,27 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                         for (int w = 0; w < NW; ++w) {
                             // SPLIT: 2048 S_H + S_L, both exact integers, rounded once.
-                            const float x = SPLIT ? __fmaf_rn(__uint_as_float(v[0][e * NW + w]), 2048.0f,
-                                                              __uint_as_float(v[SPLIT ? 1 : 0][e * NW + w]))
-                                                  : __uint_as_float(v[0][e * NW + w]);
+                            float x = SPLIT ? __fmaf_rn(__uint_as_float(v[0][e * NW + w]), 2048.0f,
+                                                        __uint_as_float(v[SPLIT ? 1 : 0][e * NW + w]))
+                                            : __uint_as_float(v[0][e * NW + w]);
+                            if constexpr (OUTM) {
+                                // Output-mode read noise (reference.py:107-114) in the units of x:
+                                // mean = mf (x + LOW 2^s S_d), deviation sqrt(vf2 Q) z, z the
+                                // normal of stream 60 at the event's address.
+                                const long long address =
+                                    ev_row + i * ev_read + (long long)((a * NW + w) * args.cols_c + e);
+                                const uint32_t high = (uint32_t)((uint64_t)address >> 32);
+                                if (high != fold_high) {
+                                    fold_high = high;
+                                    fold0 = rng_fold(high, args.read_seed, key0);
+                                    fold1 = rng_fold(high, args.read_seed, key1);
+                                }
+                                const float z = box_muller(rng_unit((uint32_t)address, fold0, key0),
+                                                           rng_unit((uint32_t)address, fold1, key1));
+                                const float q = __uint_as_float(v[G::ACCS][e * NW + w]);
+                                const float mean = __fmul_rn(args.out_mf, __fmaf_rn(args.out_l2s, __uint_as_float(sd[0]), x));
+                                x = __fadd_rn(x, __fadd_rn(mean, __fmul_rn(sqrtf(__fmul_rn(args.out_vf2, q)), z)));
+                            }
                             constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
                             if (FSUM) {
                                 ftotal[e] = __fmaf_rn(fminf(x, args.maxw[w]), args.ffactor[a][w], ftotal[e]);
@@ -589,7 +686,7 @@ __global__ void __launch_bounds__(256) b_operand_kernel(Layout L, Physics P, con
                                                         int col_begin, int blocks, int bn, int nwp, int brows,
                                                         int pstride, int parts, int kc, long long kpad, uint32_t seed,
                                                         uint64_t event, float scale, int fixed, int pair_slices,
-                                                        __half* gs) {
+                                                        int ones_row, int g2row, float scale2, __half* gs) {
     __shared__ uint16_t codes[KC][MAXBN];   // weight codes have at most 16 bits
     for (int block = blockIdx.y; block < blocks; block += gridDim.y) {
         const long long k0 = (long long)blockIdx.x * kc;
@@ -644,13 +741,26 @@ __global__ void __launch_bounds__(256) b_operand_kernel(Layout L, Physics P, con
                 __half* dst = out + set * set_stride;
                 dst[(long long)prow * kpad + kk] = hi;
                 if (parts == 2) dst[(long long)(pstride + prow) * kpad + kk] = lo;
+                if (g2row >= 0) {
+                    // Output-mode noise: G^2 (not G - LOW) as two floating FP16 parts.
+                    __half hi2 = __float2half_rn(0.0f), lo2 = hi2;
+                    if (cell) {
+                        const float x2 = __fmul_rn(__fmul_rn(g, g), scale2);
+                        hi2 = __float2half_rn(x2);
+                        lo2 = __float2half_rn(__fsub_rn(x2, __half2float(hi2)));
+                    }
+                    dst[(long long)(g2row + prow) * kpad + kk] = hi2;
+                    dst[(long long)(g2row + pstride + prow) * kpad + kk] = lo2;
+                }
             }
         }
-        // Rows past the parts (MMA padding) are zero.
+        // Rows past the parts (MMA padding) are zero, except the row of ones that
+        // gives the output mode its digit sums; the G^2 rows were written above.
         for (int set = 0; set < sets; ++set)
             for (int idx = parts * pstride * kc + threadIdx.x; idx < brows * kc; idx += blockDim.x) {
                 const int row = idx / kc, kk = idx - row * kc;
-                out[set * set_stride + (long long)row * kpad + kk] = __float2half_rn(0.0f);
+                if (g2row >= 0 && row >= g2row && row < g2row + 2 * pstride) continue;
+                out[set * set_stride + (long long)row * kpad + kk] = __float2half_rn(row == ones_row ? 1.0f : 0.0f);
             }
         __syncthreads();   // the next block's codes overwrite the staging tile
     }
@@ -721,13 +831,16 @@ constexpr Shape kDigitShapes[] = {{5, 5, 32, 1, 0}, {3, 3, 32, 2, 0}, {8, 8, 16,
 // Slice-pair read noise: one G' operand per input slice (PAIRB instantiations).
 bool pair_mode(const mf_config& c) { return !c.ideal && c.read_var != 0 && c.read_mode == 1; }
 
+// Output-mode read noise: digit sums and second moments per job (OUTM instantiations).
+bool output_mode(const mf_config& c) { return !c.ideal && c.read_var != 0 && c.read_mode == 2; }
+
 bool shape_of(const mf_config& c, Shape& s) {
     for (const Shape& k : c.ideal ? kDigitShapes : kShapes)
         if (k.nin == c.n_in && k.nw == c.n_w) {
             s = k;
             // A stage holds every input slice's tiles (slice-pair noise) or the digit
             // tiles of a wide configuration: one column block per CTA.
-            if (pair_mode(c) || (!c.ideal && (c.wide || c.wide_codes))) s.njb = 1;
+            if (pair_mode(c) || output_mode(c) || (!c.ideal && (c.wide || c.wide_codes))) s.njb = 1;
             return true;
         }
     return false;
@@ -736,13 +849,27 @@ bool shape_of(const mf_config& c, Shape& s) {
 int parts_of(const mf_config& c) { return c.ideal ? 1 : PARTS; }
 
 // B tile rows per column block (rounded to 8) and the row offset of the second half,
-// as Geo computes them.
-void rows_of(const Shape& s, int npart, int& brows8, int& pstride) {
+// as Geo computes them; with outm also the row of ones (after the current's MMA
+// rows) and the first row of the G^2 parts.
+void rows_of(const Shape& s, int npart, int& brows8, int& pstride, bool outm, int* ones_row, int* g2row) {
     const int np = s.nw * s.bn;
     const int nt = s.split ? (npart * np + 15) / 16 * 16 : (np + 15) / 16 * 16;
     pstride = s.split ? np : nt;
-    const int brows = npart * pstride > nt ? npart * pstride : nt;
+    int brows = npart * pstride > nt ? npart * pstride : nt;
+    if (ones_row) *ones_row = outm ? nt : -1;
+    if (g2row) *g2row = outm ? nt + 16 : -1;
+    if (outm) brows = nt + 16 + 2 * np;
     brows8 = (brows + 7) / 8 * 8;
+}
+
+// Rows of one TMA box of a B tile (Geo::BBOX): tiles over 256 rows load as two boxes.
+int box_rows(int brows8) { return brows8 > 256 ? brows8 / 2 : brows8; }
+
+// Scale 2^u of G^2 as two floating FP16 parts (largest value below 2^14).
+float square_scale(const mf_config& c) {
+    const double gmax = fmax(fabs(c.high), fabs(c.low)) * fmax(c.drift, 1e-30) * exp(8.0 * (c.write_var + c.read_var));
+    const int u = (int)floor(log2(16384.0 / (gmax * gmax)));
+    return (float)ldexp(1.0, u);
 }
 
 // Scale 2^s of G': the largest |G'| (nominal level, drift, an 8-sigma write and
@@ -780,8 +907,6 @@ bool tc_physical_eligible(const mf_config& c, int32_t m) {
     // Wide configurations (16-bit BFP): five-slice operands, digits as FP16 tiles, int64 totals.
     const bool wide = c.wide || c.wide_codes;
     if (wide && (c.n_in != 5 || c.n_w != 5 || c.volt_var != 0 || tcp::pair_mode(c))) return false;
-    // The output read mode draws noise per ADC event from second moments (SIMT only).
-    if (c.read_var != 0 && c.read_mode == 2) return false;
     if (c.write_var + c.read_var > 1.0) return false;
     if (c.read_rows != 32 && c.read_rows != 64) return false;
     tcp::Shape s;
@@ -792,6 +917,10 @@ bool tc_physical_eligible(const mf_config& c, int32_t m) {
     // Slice-pair read noise: every input slice's G' tiles in a stage, which fits for
     // 32-row reads of the split-halves shapes without voltage tiles.
     if (tcp::pair_mode(c) && (c.read_rows != 32 || !s.split || c.volt_var != 0)) return false;
+    // Output-mode read noise: 32-row reads of the split-halves shapes, no voltage noise.
+    if (tcp::output_mode(c) && (c.read_rows != 32 || !s.split || c.volt_var != 0 || wide ||
+                                (s.nw * s.bn) % 16 != 0))
+        return false;
     if (c.rows % c.read_rows || c.cols % s.bn) return false;
     // Digit planes are built by byte lookup for digits up to 7; wide configurations
     // take their digits as FP16 tiles (exact up to 2048).
@@ -812,7 +941,7 @@ int tc_physical_threads() { return tcp::THREADS; }
 static size_t b_operand_bytes(const mf_config& c, const tcp::Shape& s, int32_t m, int32_t tiles) {
     const long long blocks = (long long)tiles * c.cols / s.bn;
     int brows = 0, pstride = 0;
-    tcp::rows_of(s, tcp::parts_of(c), brows, pstride);
+    tcp::rows_of(s, tcp::parts_of(c), brows, pstride, tcp::output_mode(c), nullptr, nullptr);
     const size_t sets = tcp::pair_mode(c) ? (size_t)c.n_in : 1;
     return (sets * blocks * brows * (size_t)m * c.rows * sizeof(__half) + 255) / 256 * 256;
 }
@@ -832,12 +961,12 @@ size_t tc_physical_workspace_bytes(const mf_config& c, int64_t n, int32_t m, int
 }
 
 template <int NIN, int NW, int BN, int NJB, bool SPLIT, int NPART, int KR, bool NL, bool FSUM = false,
-          bool VOLT = false, bool PAIRB = false, bool WIDE = false>
+          bool VOLT = false, bool PAIRB = false, bool WIDE = false, bool OUTM = false>
 static mf_status launch_tcp(const CUtensorMap& mx, const CUtensorMap& mg, const tcp::Args& args, dim3 grid,
                             cudaStream_t st) {
-    using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT, PAIRB, WIDE>;
+    using G = tcp::Geo<NIN, NW, BN, NJB, KR, SPLIT, NPART, VOLT, PAIRB, WIDE, OUTM>;
     const size_t smem = G::BYTES + 1024;
-    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL, FSUM, VOLT, PAIRB, WIDE>;
+    auto kern = tcp::tc_physical_kernel<NIN, NW, BN, NJB, KR, SPLIT, NPART, NL, FSUM, VOLT, PAIRB, WIDE, OUTM>;
     int regs = 0;
     {
         const mf_status r = kernel_setup(reinterpret_cast<const void*>(kern), smem, &regs);
@@ -875,6 +1004,13 @@ static mf_status dispatch_tcp(const mf_config& c, const CUtensorMap& mx, const C
         }
     }
     if constexpr (SPLIT) {
+        // Output-mode read noise (32-row reads, no voltage noise, tc_physical_eligible):
+        // digit sums and second moments per job, the normal draw per ADC event.
+        if (tcp::output_mode(c))
+            return nl ? launch_tcp<NIN, NW, BN, 1, true, tcp::PARTS, 32, true, false, false, false, false, true>(
+                            mx, mg, args, grid, st)
+                      : launch_tcp<NIN, NW, BN, 1, true, tcp::PARTS, 32, false, false, false, false, false, true>(
+                            mx, mg, args, grid, st);
         // Slice-pair read noise (32-row reads, no voltage noise, tc_physical_eligible): one
         // column block per CTA, every input slice's G' tiles per stage.
         if (tcp::pair_mode(c))
@@ -930,9 +1066,11 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     const long long K = (long long)a.m * c.rows;
     const int cols = tiles * c.cols;
     const int blocks = cols / shape.bn;
-    int brows = 0, pstride = 0;
-    tcp::rows_of(shape, tcp::parts_of(c), brows, pstride);
+    int brows = 0, pstride = 0, ones_row = -1, g2row = -1;
+    const bool outm = tcp::output_mode(c);
+    tcp::rows_of(shape, tcp::parts_of(c), brows, pstride, outm, &ones_row, &g2row);
     const float scale = c.ideal ? 1.0f : tcp::split_scale(c, shape.split != 0);
+    const float scale2 = outm ? tcp::square_scale(c) : 1.0f;
     __half* gs = static_cast<__half*>(workspace);
     {
         const int kc = c.rows % tcp::KC == 0 ? tcp::KC : 32;
@@ -942,12 +1080,12 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
             tcp::b_operand_kernel<long long><<<grid, 256, 0, st>>>(
                 make_layout(c), make_physics(c), static_cast<const long long*>(a.packed), a.p, a.tile_begin * c.cols,
                 blocks, shape.bn, shape.nw, brows, pstride, tcp::parts_of(c), kc, K, a.seed, a.event, scale,
-                shape.split, pair, gs);
+                shape.split, pair, ones_row, g2row, scale2, gs);
         else
             tcp::b_operand_kernel<uint8_t><<<grid, 256, 0, st>>>(
                 make_layout(c), make_physics(c), static_cast<const uint8_t*>(a.packed), a.p, a.tile_begin * c.cols,
                 blocks, shape.bn, shape.nw, brows, pstride, tcp::parts_of(c), kc, K, a.seed, a.event, scale,
-                shape.split, pair, gs);
+                shape.split, pair, ones_row, g2row, scale2, gs);
         MF_LAUNCH_CHECK("b_operand_kernel");
     }
     CUtensorMap mx, mg;
@@ -992,7 +1130,7 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     }
     const long long sets = tcp::pair_mode(c) ? c.n_in : 1;
     if (!r) r = tc_make_map(&mg, gs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K,
-                            (uint64_t)(sets * blocks * brows), (uint64_t)K, 16, (uint32_t)brows,
+                            (uint64_t)(sets * blocks * brows), (uint64_t)K, 16, (uint32_t)tcp::box_rows(brows),
                             CU_TENSOR_MAP_SWIZZLE_32B);
     if (r) return r;
     tcp::Args args{};
@@ -1012,6 +1150,30 @@ mf_status tc_physical_sliced_mm(const mf_config& c, const MMArgs& a, void* works
     args.col_end = a.tile_end * c.cols;
     args.n_pad = (int)n_pad;
     args.gblocks = blocks;
+    if (outm) {
+        // Output-mode noise in the units of x (FP16-part sums of d * G' * 2^s):
+        // mean factor expm1(s^2/2), variance factor exp(s^2) expm1(s^2) (reference.py:107-114)
+        // carried from (2^u G^2) to x^2 units by 2^(2s) / 2^u, and LOW * 2^s for the digit sums.
+        const double v2 = c.read_var * c.read_var;
+        args.out_mf = (float)expm1(0.5 * v2);
+        args.out_vf2 = (float)(exp(v2) * expm1(v2) * (double)scale * (double)scale / (double)scale2);
+        args.out_l2s = (float)(c.low * (double)scale);
+        args.vector_offset = a.vector_offset;
+        args.p_total = a.p;
+        args.cols_c = c.cols;
+        args.read_seed = event_seed(a.seed, a.event);
+        // FP16 bit patterns of d^2 for d = 0..7: 0, 1, 4, 9, 16, 25, 36, 49.
+        const uint16_t sq[8] = {0x0000, 0x3C00, 0x4400, 0x4880, 0x4C00, 0x4E40, 0x5080, 0x5220};
+        uint8_t lo[8], hi[8];
+        for (int d = 0; d < 8; ++d) {
+            lo[d] = (uint8_t)(sq[d] & 0xFF);
+            hi[d] = (uint8_t)(sq[d] >> 8);
+        }
+        args.sq_lo_lo = lo[0] | lo[1] << 8 | lo[2] << 16 | (uint32_t)lo[3] << 24;
+        args.sq_lo_hi = lo[4] | lo[5] << 8 | lo[6] << 16 | (uint32_t)lo[7] << 24;
+        args.sq_hi_lo = hi[0] | hi[1] << 8 | hi[2] << 16 | (uint32_t)hi[3] << 24;
+        args.sq_hi_hi = hi[4] | hi[5] << 8 | hi[6] << 16 | (uint32_t)hi[7] << 24;
+    }
     // FP16 high bytes of the digits 0..7 (1.0 = 0x3C00, 2.0 = 0x4000, 3.0 = 0x4200, ...).
     const uint8_t hi[8] = {0x00, 0x3C, 0x40, 0x42, 0x44, 0x45, 0x46, 0x47};
     args.lut_lo = hi[0] | hi[1] << 8 | hi[2] << 16 | (uint32_t)hi[3] << 24;

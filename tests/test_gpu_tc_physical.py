@@ -56,6 +56,13 @@ CONFIGS = {
     "bfp16_write": dict(INT8, activation_bits=16, weight_bits=16, bw_e=8, input_slice=(1, 3, 4, 4, 4),
                         weight_slice=(1, 3, 4, 4, 4), adc_bits=8,
                         nonidealities=dict(write_variation=0.02, read_variation=0.02)),
+    # Output-mode read noise: digit sums and second moments per job, a normal draw per
+    # ADC event (OUTM kernels).
+    "int8_read_output": dict(INT8, nonidealities=dict(write_variation=0.02, read_variation=0.05,
+                                                      read_mode="output")),
+    "int4_read_output_all": dict(INT8, activation_bits=4, weight_bits=4, input_slice=(1, 1, 2),
+                                 weight_slice=(1, 1, 2), adc_bits=6,
+                                 nonidealities=dict(ALL, read_variation=0.03, read_mode="output")),
     # Slice-pair read noise: one conductance operand per input slice (PAIRB kernels).
     "int8_read_pair": dict(INT8, nonidealities=dict(write_variation=0.02, read_variation=0.05,
                                                     read_mode="slice_pair")),
@@ -182,7 +189,8 @@ def test_ideal_digit_dots_are_bit_exact(mf, name):
 
 
 @pytest.mark.parametrize("name", ["int8_write", "int8_rpr64_all", "default_1bit", "int8_rpr64_ideal",
-                                  "int4_rpr64_ideal", "int8_noisy", "int8_read_pair", "bfp16_rpr64_all"])
+                                  "int4_rpr64_ideal", "int8_noisy", "int8_read_pair", "bfp16_rpr64_all",
+                                  "int8_read_output"])
 def test_column_shards_and_row_prefixes_are_exact(mf, name):
     config = config_of(mf, name)
     a, b = operands(300, 512, 640, 4)
@@ -206,7 +214,7 @@ def test_against_the_oracle(mf):
     assert_close_nonideal(got, want, "oracle")
 
 
-@pytest.mark.parametrize("name", ["int8_read_shared", "int8_read_pair"])
+@pytest.mark.parametrize("name", ["int8_read_shared", "int8_read_pair", "int8_read_output"])
 def test_read_events_draw_new_noise(mf, name):
     config = config_of(mf, name)
     a, b = operands(128, 256, 256, 6)
@@ -219,11 +227,13 @@ def test_read_events_draw_new_noise(mf, name):
 
 def test_ineligible_configs_keep_the_simt_path(mf):
     # Voltage noise runs on the tensor cores for 32-row reads only (the voltage tiles of a
-    # 64-row read do not fit a pipeline stage); output-mode read noise stays on SIMT.
+    # 64-row read do not fit a pipeline stage); so does output-mode read noise, without
+    # voltage noise.
     voltage64 = mf.Config(**dict(MATRIX, input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2)),
                           nonidealities=mf.Nonidealities(write_variation=0.02, voltage_variation=0.02))
-    output_mode = mf.Config(**INT8, nonidealities=mf.Nonidealities(write_variation=0.02, read_variation=0.05,
-                                                                   read_mode="output"))
+    output_mode = mf.Config(**dict(MATRIX, input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2)),
+                            nonidealities=mf.Nonidealities(write_variation=0.02, read_variation=0.05,
+                                                           read_mode="output"))
     # Slice-pair read noise: 32-row reads without voltage noise only (every input slice's
     # conductance tiles must fit a pipeline stage).
     pair64 = mf.Config(**dict(MATRIX, input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2)),
@@ -235,3 +245,6 @@ def test_ineligible_configs_keep_the_simt_path(mf):
         assert threads_of(mf, config, 2, 2) == 256
     voltage = mf.Config(**INT8, nonidealities=mf.Nonidealities(write_variation=0.02, voltage_variation=0.02))
     assert threads_of(mf, voltage, 2, 2) == 640
+    output32 = mf.Config(**INT8, nonidealities=mf.Nonidealities(write_variation=0.02, read_variation=0.05,
+                                                                read_mode="output"))
+    assert threads_of(mf, output32, 2, 2) == 640
