@@ -71,6 +71,9 @@ CONFIGS = {
     "int7_read_pair": dict(INT8, activation_bits=7, weight_bits=7, input_slice=(1, 2, 2, 2), weight_slice=(1, 2, 2, 2),
                            adc_bits=8, nonidealities=dict(write_variation=0.02, read_variation=0.04,
                                                           read_mode="slice_pair")),
+    "int7_read_output": dict(INT8, activation_bits=7, weight_bits=7, input_slice=(1, 2, 2, 2),
+                             weight_slice=(1, 2, 2, 2), adc_bits=8,
+                             nonidealities=dict(write_variation=0.02, read_variation=0.04, read_mode="output")),
 }
 
 
