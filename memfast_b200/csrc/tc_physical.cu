@@ -563,6 +563,38 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&unit_empty[unit]);
+                    constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+                    if constexpr (SPLIT && !OUTM && !FSUM) {
+                        // The ADC two events at a time (flattened index k = e * NW + w):
+                        // packed FMAs round each lane once, as the scalar ones below do.
+#pragma unroll
+                        for (int k = 0; k < G::VALS; k += 2) {
+                            const int e0 = k / NW, w0 = k % NW, e1 = (k + 1) / NW, w1 = (k + 1) % NW;
+                            const float2 x2 = __ffma2_rn(
+                                make_float2(__uint_as_float(v[0][k]), __uint_as_float(v[0][k + 1])),
+                                make_float2(2048.0f, 2048.0f),
+                                make_float2(__uint_as_float(v[1][k]), __uint_as_float(v[1][k + 1])));
+                            float2 s2;
+                            if constexpr (NONLINEAR) {
+                                // S-curve per lane: z = x c / (1 + |slope z|), clamped to [0, 1] of max_w.
+                                float z0 = __fmul_rn(x2.x, args.cw[w0]), z1 = __fmul_rn(x2.y, args.cw[w1]);
+                                z0 = __fdiv_rn(z0, __fadd_rn(1.0f, fabsf(__fmul_rn(args.slope[w0], z0))));
+                                z1 = __fdiv_rn(z1, __fadd_rn(1.0f, fabsf(__fmul_rn(args.slope[w1], z1))));
+                                s2 = make_float2(mul_sat(z0, args.inv_maxw[w0]), mul_sat(z1, args.inv_maxw[w1]));
+                            } else {
+                                s2 = make_float2(mul_sat(x2.x, args.cws[w0]), mul_sat(x2.y, args.cws[w1]));
+                            }
+                            const float2 q2 =
+                                __ffma2_rn(s2, make_float2(args.maxw[w0], args.maxw[w1]), make_float2(kMagic, kMagic));
+                            if constexpr (WIDE) {
+                                total[e0] += (Tot)(long long)__float_as_int(q2.x) * (Tot)(long long)args.factor[a][w0];
+                                total[e1] += (Tot)(long long)__float_as_int(q2.y) * (Tot)(long long)args.factor[a][w1];
+                            } else {
+                                total[e0] += __float_as_int(q2.x) * args.factor[a][w0];
+                                total[e1] += __float_as_int(q2.y) * args.factor[a][w1];
+                            }
+                        }
+                    } else
 #pragma unroll
                     for (int e = 0; e < G::EC; ++e)
 #pragma unroll
@@ -589,7 +621,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 const float mean = __fmul_rn(args.out_mf, __fmaf_rn(args.out_l2s, __uint_as_float(sd[0]), x));
                                 x = __fadd_rn(x, __fadd_rn(mean, __fmul_rn(sqrtf(__fmul_rn(args.out_vf2, q)), z)));
                             }
-                            constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
                             if (FSUM) {
                                 ftotal[e] = __fmaf_rn(fminf(x, args.maxw[w]), args.ffactor[a][w], ftotal[e]);
                                 continue;
