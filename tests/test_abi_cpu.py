@@ -142,3 +142,40 @@ def test_mf_mm_validates_on_the_host():
     assert lib.mf_mm(*args, ct.byref(missing), 0, 0, 0, None, None) == _lib.MF_ERR_INVALID
     assert lib.mf_mm(*args, ct.byref(buffers), 0, 0, 0, None, None) == _lib.MF_ERR_RESOURCE
     assert "workspaces too small" in _lib.last_error()
+
+
+def test_read_modes_resolve_to_their_current_kernels():
+    """Every read mode of 32-row reads takes the tensor-core current kernel; output-mode
+    read noise with 64-row reads or with voltage noise keeps the SIMT kernels.  The
+    output mode's conductance operand carries, per 16-column block, the two halves of
+    G' (160 rows for five weight slices), a row of ones padded to 16 rows, and two
+    FP16 parts of G^2 (160 rows): 336 rows against the shared mode's 160.  Resolved on
+    the host (mf_query, mf_sliced_mm_workspace), no GPU needed."""
+    from memfast_b200 import Config, Nonidealities, _lib
+    from memfast_b200.tuning import default_schedule, resolve
+
+    int8 = dict(array_size=(128, 128), rows_per_read=32, weight_quant_gran=(32, 1), input_quant_gran=(1, 32),
+                input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2), adc_bits=(6, 7, 7, 8, 8))
+    rpr64 = dict(array_size=(256, 256), rows_per_read=64, weight_quant_gran=(64, 1), input_quant_gran=(1, 64),
+                 input_slice=(1, 1, 2, 2, 2), weight_slice=(1, 1, 2, 2, 2), adc_bits=(6, 7, 7, 8, 8))
+
+    def config(shape, **effects):
+        return Config(**shape, nonidealities=Nonidealities(write_variation=0.02, **effects))
+
+    def path(c):
+        return resolve(c, default_schedule(c), 64, 2, 3)[0]
+
+    shared = config(int8, read_variation=0.02)
+    pair = config(int8, read_variation=0.02, read_mode="slice_pair")
+    output = config(int8, read_variation=0.02, read_mode="output")
+    assert path(shared) == path(pair) == path(output) == "tc_currents"
+    assert path(config(int8, read_variation=0.02, read_mode="output", voltage_variation=0.02)) == "simt_currents"
+    assert path(config(rpr64, read_variation=0.02, read_mode="output")) == "simt_currents"
+
+    lib = _lib.load()
+    size = ct.c_size_t()
+    blocks, k = 3 * 128 // 16, 2 * 128            # 16-column blocks of 3 tiles; K of 2 arrays
+    for c, rows in ((shared, 160), (output, 336)):
+        sched = _lib.schedule(**default_schedule(c))
+        assert lib.mf_sliced_mm_workspace(_lib.native_config(c), ct.byref(sched), 64, 2, 3, 0, 3, ct.byref(size)) == 0
+        assert size.value == blocks * rows * k * 2 + 256
